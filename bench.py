@@ -1,0 +1,316 @@
+#!/usr/bin/env python
+"""Benchmark: fp32 training throughput of ResNet-50 (batch 64 per GPU,
+synthetic 3x224x224 inputs, cross-entropy, SGD momentum 0.9) on the `ocl`
+backend, data-parallel over N GPUs (one process per GPU, launched by torchrun).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0).  `value` is whole-job images/s with inputs
+resident in HBM (device-timed with events on the backend stream, max over
+ranks); `e2e` is the same metric through the public API with each step's
+batch copied from pinned host memory and the loss read back.  The roofline
+object covers the dominant kernel class (the convolutions, fwd+bwd); the CPU
+baseline is the torch-CPU step (the reference's validation path) timed on
+this host on a bounded sample.
+
+`--impl reference` times the reference's CPU path (torch-CPU ATen, as its
+tests/validate_network.py runs it) for the same workload on all host cores;
+under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+MODEL = "resnet50"
+GFLOP_PER_IMAGE = 24.30  # fwd+bwd conv/linear 2*MAC, torch.utils.flop_counter
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--model", default=MODEL)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                if out.returncode == 0 and out.stdout.strip():
+                    self.samples.append([s.strip() for s in out.stdout.strip().split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
+        mx = max((float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for n, v in zip(names, s[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(self.samples)}
+
+
+# --------------------------------------------------------- reference arm
+def run_reference(a):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return
+    from oracle import step as ostep
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = min(a.batch, 16)  # a bounded sample of the per-GPU batch per step
+    steps = max(1, min(a.steps, 8))
+    warm = max(1, min(a.warmup, 2))
+    dt, used = ostep.time_cpu_steps(a.model, sample, steps, warm, threads)
+    v = sample / dt
+    line = {
+        "impl": "reference", "metric": "train images/sec (fp32)", "value": round(v, 3), "unit": "images/s",
+        "n_gpus": a.gpus, "steps": steps, "warmup": warm, "ms_per_step": round(dt * 1000, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{a.model} fp32 train step, batch {a.batch}/GPU, 3x224x224, SGD m0.9",
+                   "sample": f"{sample} images per step", "path": "torch-CPU ATen (reference CPU validation path)"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "images/s", "cores": used, "kind": "port",
+                         "sample": f"{steps} steps x {sample} images of the {a.model} workload on torch-CPU"},
+        "e2e": {"value": round(v, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------- ours arm
+def conv_flops_per_step(model, x):
+    """Algorithmic conv+linear FLOPs (2*MAC) of one fwd+bwd, from the shapes."""
+    from torch.utils.flop_counter import FlopCounterMode
+
+    m = model.to("cpu")
+    with FlopCounterMode(display=False) as fc:
+        m(x[:1].cpu()).sum().backward()
+    m.zero_grad(set_to_none=True)
+    total = fc.get_total_flops()
+    conv = sum(v for k, v in fc.get_flop_counts()["Global"].items() if "convolution" in str(k))
+    return total * x.shape[0], conv * x.shape[0]
+
+
+def run_ours(a):
+    import pytorch_vulkan_b200 as pvb2
+    from pytorch_vulkan_b200 import _C
+    from pytorch_vulkan_b200.distributed import DistributedDataParallel, init_process_group
+
+    from oracle import models as omodels
+
+    rank, world, local, comm = init_process_group()
+    if world == 1:
+        torch.ocl.set_device(0)
+    dev = f"ocl:{local}"
+    torch.manual_seed(0)
+    model = omodels.build(a.model, 0)
+    x_cpu, y_cpu = omodels.make_inputs(a.model, a.batch, 1234 + rank)
+    total_flops, conv_flops = conv_flops_per_step(model, x_cpu) if rank == 0 else (0, 0)
+    model = model.to(dev)
+    model.train()
+    net = DistributedDataParallel(model, comm) if world > 1 else model
+    opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9, fused=True)
+    loss_fn = omodels.loss_fn(a.model)
+    x = x_cpu.to(dev)
+    y = y_cpu.to(dev)
+
+    def step(xb, yb):
+        opt.zero_grad(set_to_none=True)
+        out = net(xb)
+        l = loss_fn(out, yb)
+        l.backward()
+        opt.step()
+        return l
+
+    def barrier():
+        torch.ocl.synchronize(local)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    for _ in range(a.warmup):
+        step(x, y)
+    barrier()
+    # ---------------------------------------------------------- timed region
+    e0, e1 = _C.impl_event_create(True), _C.impl_event_create(True)
+    l0 = _C.impl_launch_count()
+    with ClockSampler(local) as clk:
+        barrier()
+        _C.impl_event_record(e0, local)
+        for _ in range(a.steps):
+            step(x, y)
+        _C.impl_event_record(e1, local)
+        barrier()
+    launches = _C.impl_launch_count() - l0
+    ms = _C.impl_event_elapsed_ms(e0, e1) / a.steps
+    ms = max_over_ranks(ms)
+    value = a.batch * world / (ms / 1000.0)
+
+    # ----------------------------------------------- end to end (public API)
+    e2e = None
+    if not a.no_e2e:
+        xp, yp = x_cpu.pin_memory(), y_cpu.pin_memory()
+        xb = torch.empty_like(x)
+        yb = torch.empty_like(y)
+        for _ in range(2):
+            xb.copy_(xp, non_blocking=True)
+            yb.copy_(yp, non_blocking=True)
+            step(xb, yb).item()
+        barrier()
+        t0 = time.perf_counter()
+        _C.impl_event_record(e0, local)
+        for _ in range(a.steps):
+            xb.copy_(xp, non_blocking=True)
+            yb.copy_(yp, non_blocking=True)
+            step(xb, yb).item()
+        _C.impl_event_record(e1, local)
+        barrier()
+        ems = max_over_ranks(_C.impl_event_elapsed_ms(e0, e1) / a.steps)
+        e2e = {"value": round(a.batch * world / (ems / 1000.0), 2), "unit": "images/s",
+               "h2d_bytes_per_step": int(x.numel() * x.element_size() + y.numel() * y.element_size()),
+               "d2h_bytes_per_step": 4, "ms_per_step": round(ems, 3)}
+
+    # --------------------------------------- dominant kernel class roofline
+    roof = None
+    if rank == 0:
+        import csv
+        import tempfile
+
+        path = os.path.join(tempfile.mkdtemp(), "prof.csv")
+        with torch.ocl.profile(local, path):
+            step(x, y)
+            torch.ocl.synchronize(local)
+        conv_ms = 0.0
+        n_conv = 0
+        per_op = {}
+        with open(path) as f:
+            for r in csv.DictReader(f):
+                d = float(r["duraion(ms)"])
+                top = r["section"] == ""
+                if top:
+                    per_op[r["kernel"]] = per_op.get(r["kernel"], 0.0) + d
+                if top and r["kernel"] in ("convolution", "convolution_backward"):
+                    conv_ms += d
+                    n_conv += 1
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))
+        except Exception:
+            pass
+        bf16 = peaks.get("bf16_tflops", 1590.0)
+        tf32_peak = bf16 / 2.0
+        achieved = conv_flops / (conv_ms / 1000.0) / 1e12 if conv_ms > 0 else 0.0
+        roof = {"bound": "tensor", "kernel": "convolution fwd+bwd (all conv launches of one step)",
+                "achieved": round(achieved, 2), "peak": round(tf32_peak, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / tf32_peak, 4),
+                "peak_note": "TF32 dense = 1/2 of measured bf16 (MEASURED_PEAKS.json)" if peaks else "fallback",
+                "traffic": None, "conv_ms_per_step": round(conv_ms, 3), "conv_launch_groups": n_conv,
+                "conv_gflop_per_step": round(conv_flops / 1e9, 1),
+                "top_ops_ms": dict(sorted(per_op.items(), key=lambda kv: -kv[1])[:8])}
+
+    # ------------------------------------------------------- CPU baseline
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        from oracle import step as ostep
+
+        threads = os.cpu_count() or 1
+        sample = 8
+        dt, used = ostep.time_cpu_steps(a.model, sample, 2, 1, threads)
+        cpu = {"value": round(sample / dt, 3), "unit": "images/s", "cores": used, "kind": "port",
+               "sample": f"2 timed steps x {sample} images of {a.model} on torch-CPU ATen (reference CPU path)"}
+
+    if rank == 0:
+        line = {
+            "metric": "train images/sec (fp32)", "value": round(value, 2), "unit": "images/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{a.model} fp32 train step (fwd+bwd+SGD m0.9), batch {a.batch}/GPU, 3x224x224",
+                       "global_batch": a.batch * world, "parallelism": f"dp{world}",
+                       "math": ["tf32", "fp32", "3xtf32"][torch.ocl.get_math_mode()],
+                       "l2": "inputs/activations larger than L2 (126 MB) every step",
+                       "gflop_per_step": round(total_flops / 1e9, 1)},
+            "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

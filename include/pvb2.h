@@ -1,0 +1,374 @@
+/*
+ * pvb2.h -- C-ABI of the B200 kernel library (libpvb2.so) behind the `ocl`
+ * (PrivateUse1) PyTorch backend.
+ *
+ * Everything here is plain C: raw device pointers, sizes and strides, an
+ * opaque stream handle, an int status.  No torch types cross this boundary,
+ * so the library can be bound from ctypes, cffi or any C++ host.
+ *
+ * Each entry point names the reference interface it replaces.  In the
+ * reference (pytorch_ocl 0.2.0) those are ATen kernels registered with
+ * TORCH_LIBRARY_IMPL(aten, PrivateUse1) that forward to dlprimitives'
+ * OpenCL kernels; the host layer of this project (csrc/host/*.cpp) keeps the
+ * same ATen registrations and forwards to the functions below instead.
+ *
+ * Conventions
+ *   - Every function returns PVB2_OK (0) or an error code; it never aborts.
+ *     pvb2_last_error() returns a thread-local message for the last failure.
+ *   - Launchers validate shapes, dtypes and alignment before launching.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy
+ *     default stream.
+ *   - Strides are in elements, like torch.
+ *   - No launcher allocates device memory.  Scratch space ("workspace") is
+ *     passed in by the caller; *_workspace_size() reports how much is needed.
+ */
+#ifndef PVB2_H
+#define PVB2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PVB2_API __attribute__((visibility("default")))
+#else
+#define PVB2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ */
+/* status, dtypes, tensor descriptor                                    */
+/* ------------------------------------------------------------------ */
+enum {
+  PVB2_OK = 0,
+  PVB2_ERR_INVALID = 1,     /* bad argument (shape, dtype, alignment)    */
+  PVB2_ERR_UNSUPPORTED = 2, /* valid request this library does not do    */
+  PVB2_ERR_CUDA = 3,        /* CUDA runtime error                        */
+  PVB2_ERR_OOM = 4,         /* cudaMalloc / cudaHostAlloc failed         */
+  PVB2_ERR_NCCL = 5,        /* NCCL error                                */
+  PVB2_ERR_TIMEOUT = 6      /* a bounded wait ran out                    */
+};
+
+/* dtype codes follow the reference's dtype map (src/utils.cpp:5-32). */
+enum {
+  PVB2_F32 = 0, PVB2_F64 = 1, PVB2_F16 = 2, PVB2_BF16 = 3,
+  PVB2_I64 = 4, PVB2_I32 = 5, PVB2_I16 = 6, PVB2_I8 = 7,
+  PVB2_U8 = 8, PVB2_BOOL = 9
+};
+
+#define PVB2_MAX_DIMS 8
+
+/* A strided view of device memory.  Replaces the reference's
+ * torch::Tensor -> dlprim::Tensor bridge `todp()` (src/utils.cpp:44-59),
+ * which required contiguous tensors; here strides are carried through. */
+typedef struct pvb2_tensor {
+  void* data;                       /* points at element [0,...,0]      */
+  int64_t sizes[PVB2_MAX_DIMS];
+  int64_t strides[PVB2_MAX_DIMS];   /* in elements                      */
+  int32_t ndim;
+  int32_t dtype;                    /* PVB2_* dtype code                */
+} pvb2_tensor;
+
+typedef void* pvb2_stream;          /* cudaStream_t */
+typedef void* pvb2_event;           /* cudaEvent_t  */
+
+/* ------------------------------------------------------------------ */
+/* runtime: devices, memory, streams, events                           */
+/* Replaces CLContextManager (src/CLTensor.h:87-282) and the OpenCL     */
+/* buffer/queue calls made by CLCache (src/CLTensor.cpp:9-92).          */
+/* ------------------------------------------------------------------ */
+PVB2_API const char* pvb2_last_error(void);
+PVB2_API int pvb2_version(void);
+PVB2_API int pvb2_device_count(int* count);                         /* CLTensor.h:230-258 */
+PVB2_API int pvb2_set_device(int device);
+PVB2_API int pvb2_get_device(int* device);
+PVB2_API int pvb2_device_name(int device, char* buf, int buflen);
+PVB2_API int pvb2_device_synchronize(void);                         /* python_iface.cpp:34-47 */
+PVB2_API int pvb2_mem_get_info(size_t* free_bytes, size_t* total_bytes);
+PVB2_API int pvb2_malloc(void** ptr, size_t bytes);                 /* CLCache::allocate backing store, CLTensor.cpp:81-92 */
+PVB2_API int pvb2_free(void* ptr);
+PVB2_API int pvb2_host_alloc(void** ptr, size_t bytes);             /* pinned host memory */
+PVB2_API int pvb2_host_free(void* ptr);
+PVB2_API int pvb2_pointer_info(const void* ptr, int* is_device, int* is_pinned_host, int* device);
+PVB2_API int pvb2_stream_create(pvb2_stream* stream, int priority); /* the reference's single in-order queue, CLTensor.h:260-276 */
+PVB2_API int pvb2_stream_destroy(pvb2_stream stream);
+PVB2_API int pvb2_stream_synchronize(pvb2_stream stream);           /* queue.finish(), registeration.cpp:71-74 */
+PVB2_API int pvb2_stream_query(pvb2_stream stream, int* done);      /* registeration.cpp:68-70 (was always false) */
+PVB2_API int pvb2_stream_wait_event(pvb2_stream stream, pvb2_event event);
+PVB2_API int pvb2_event_create(pvb2_event* event, int timing);
+PVB2_API int pvb2_event_destroy(pvb2_event event);
+PVB2_API int pvb2_event_record(pvb2_event event, pvb2_stream stream);
+PVB2_API int pvb2_event_synchronize(pvb2_event event);
+PVB2_API int pvb2_event_query(pvb2_event event, int* done);
+PVB2_API int pvb2_event_elapsed_ms(pvb2_event start, pvb2_event end, float* ms);
+/* kind: 0 host->device, 1 device->host, 2 device->device, 3 inferred */
+PVB2_API int pvb2_memcpy_async(void* dst, const void* src, size_t bytes, int kind, pvb2_stream stream);
+PVB2_API int pvb2_memset_async(void* dst, int value, size_t bytes, pvb2_stream stream);
+/* number of kernels this library has launched in this process (all devices) */
+PVB2_API int64_t pvb2_launch_count(void);
+
+/* ------------------------------------------------------------------ */
+/* tensor plumbing (src/tensor_ops.cpp)                                 */
+/* ------------------------------------------------------------------ */
+/* fill_.Scalar / zero_, tensor_ops.cpp:204-225 */
+PVB2_API int pvb2_fill(const pvb2_tensor* out, double value, pvb2_stream stream);
+/* strided copy with dtype conversion: copy_strided in _copy_from,
+ * tensor_ops.cpp:118-186 (same sizes required; any strides, any dtypes) */
+PVB2_API int pvb2_copy(const pvb2_tensor* dst, const pvb2_tensor* src, pvb2_stream stream);
+/* arange.start_out, pointwise_ops.cpp (arange_out): out[i] = start + i*step */
+PVB2_API int pvb2_arange(const pvb2_tensor* out, double start, double step, pvb2_stream stream);
+/* cat.out along `dim`, pointwise_ops.cpp:689-705 (SliceCopy) */
+PVB2_API int pvb2_cat(const pvb2_tensor* out, const pvb2_tensor* inputs, int n_inputs, int dim, pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* pointwise (src/pointwise_ops.cpp)                                    */
+/* All operands are already broadcast to out's sizes (stride 0 on       */
+/* broadcast dims).  `compute_dtype` is the promoted dtype that the     */
+/* arithmetic runs in (PVB2_F32 / PVB2_F64 / PVB2_I64 / PVB2_I32 /      */
+/* PVB2_BOOL); operands are converted on load and out on store.         */
+/* ------------------------------------------------------------------ */
+enum {
+  /* unary: out = f(x; p0, p1) */
+  PVB2_UN_COPY = 0, PVB2_UN_RELU = 1, PVB2_UN_HARDTANH = 2, PVB2_UN_GELU_ERF = 3,
+  PVB2_UN_GELU_TANH = 4, PVB2_UN_NEG = 5, PVB2_UN_EXP = 6, PVB2_UN_LOG = 7,
+  PVB2_UN_SQRT = 8, PVB2_UN_ABS = 9, PVB2_UN_SIGMOID = 10, PVB2_UN_TANH = 11,
+  PVB2_UN_RECIPROCAL = 12, PVB2_UN_SILU = 13, PVB2_UN_AFFINE = 14, /* x*p0+p1 */
+  PVB2_UN_POW = 15, PVB2_UN_CLAMP = 16, PVB2_UN_LEAKY_RELU = 17, PVB2_UN_SGN = 18,
+  PVB2_UN_HARDSIGMOID = 19, PVB2_UN_HARDSWISH = 20, PVB2_UN_CEIL = 21,
+  PVB2_UN_ROUND = 22, PVB2_UN_ATAN = 23, PVB2_UN_RSQRT = 24, PVB2_UN_LOG_SIGMOID = 25,
+  PVB2_UN_BITWISE_NOT = 26, PVB2_UN_CLAMP_MIN = 27, PVB2_UN_FLOOR = 28, PVB2_UN_TRUNC = 29
+};
+enum {
+  /* binary: out = f(a, b; p0, p1) */
+  PVB2_BIN_ADD = 0,        /* a + p0*b                            add_out, pointwise_ops.cpp:133-172 */
+  PVB2_BIN_SUB = 1,        /* a - p0*b                            sub_out, :206-210 */
+  PVB2_BIN_MUL = 2,        /*                                      mul_out, :407-411 */
+  PVB2_BIN_DIV = 3,        /*                                      div_out, :318-344 */
+  PVB2_BIN_MAXIMUM = 4, PVB2_BIN_MINIMUM = 5,
+  PVB2_BIN_EQ = 6, PVB2_BIN_NE = 7, PVB2_BIN_LT = 8, PVB2_BIN_LE = 9, PVB2_BIN_GT = 10, PVB2_BIN_GE = 11,
+  PVB2_BIN_THRESHOLD_BWD = 12, /* b <= p0 ? 0 : a   (a=grad, b=self) threshold_backward, :437-455 */
+  PVB2_BIN_HARDTANH_BWD = 13,  /* (b > p0 && b < p1) ? a : 0          hardtanh_backward, :590-603 */
+  PVB2_BIN_GELU_ERF_BWD = 14,  /* a * gelu'(b)                         gelu_backward, :1360-1393 */
+  PVB2_BIN_GELU_TANH_BWD = 15,
+  PVB2_BIN_SIGMOID_BWD = 16,   /* a * b*(1-b)   (b = sigmoid output) */
+  PVB2_BIN_TANH_BWD = 17,      /* a * (1-b*b)   (b = tanh output)    */
+  PVB2_BIN_SILU_BWD = 18,
+  PVB2_BIN_LEAKY_RELU_BWD = 19,
+  PVB2_BIN_HARDSIGMOID_BWD = 20, PVB2_BIN_HARDSWISH_BWD = 21,
+  PVB2_BIN_BITWISE_AND = 22, PVB2_BIN_BITWISE_OR = 23, PVB2_BIN_BITWISE_XOR = 24,
+  PVB2_BIN_LERP = 25,          /* a + p0*(b-a) */
+  PVB2_BIN_POW = 26, PVB2_BIN_ATAN2 = 27, PVB2_BIN_LOG_SIGMOID_BWD = 28,
+  PVB2_BIN_DIV_TRUNC = 29, PVB2_BIN_DIV_FLOOR = 30, PVB2_BIN_REMAINDER = 31,
+  PVB2_BIN_MSE_BWD = 32        /* p0 * (a - b) */
+};
+enum {
+  /* ternary: out = f(a, b, c; p0) */
+  PVB2_TER_ADDCMUL = 0,  /* a + p0*b*c   addcmul_out, pointwise_ops.cpp:214-234 */
+  PVB2_TER_ADDCDIV = 1,  /* a + p0*b/c   addcdiv_out, :414-434 */
+  PVB2_TER_WHERE = 2     /* a(bool) ? b : c */
+};
+PVB2_API int pvb2_unary(int op, const pvb2_tensor* out, const pvb2_tensor* x, double p0, double p1,
+               int compute_dtype, pvb2_stream stream);
+PVB2_API int pvb2_binary(int op, const pvb2_tensor* out, const pvb2_tensor* a, const pvb2_tensor* b,
+                double p0, double p1, int compute_dtype, pvb2_stream stream);
+/* binary op with one operand a host scalar: scalar_first=0 computes
+ * f(t, scalar), scalar_first=1 computes f(scalar, t).  Used for the wrapped
+ * CPU numbers of add(x, 2), mul_(0.9), rsub, ... (isCPUScalar fast path of
+ * the reference, pointwise_ops.cpp:33-52). */
+PVB2_API int pvb2_binary_scalar(int op, const pvb2_tensor* out, const pvb2_tensor* t, double scalar,
+                                int scalar_first, double p0, double p1, int compute_dtype, pvb2_stream stream);
+PVB2_API int pvb2_ternary(int op, const pvb2_tensor* out, const pvb2_tensor* a, const pvb2_tensor* b,
+                 const pvb2_tensor* c, double p0, int compute_dtype, pvb2_stream stream);
+
+/* reductions: sum/mean/prod/amax/amin/argmax, red_op_out pointwise_ops.cpp:501-555.
+ * `in` has the full shape; `out` has the same ndim with every reduced dim of
+ * size 1.  `scale` multiplies the result (1/count for mean). */
+enum { PVB2_RED_SUM = 0, PVB2_RED_PROD = 1, PVB2_RED_MAX = 2, PVB2_RED_MIN = 3,
+       PVB2_RED_ARGMAX = 4, PVB2_RED_ARGMIN = 5, PVB2_RED_SUMSQ = 6 };
+PVB2_API int pvb2_reduce(int op, const pvb2_tensor* out, const pvb2_tensor* in, double scale,
+                int compute_dtype, pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* normalisation (src/norm_ops.cpp)                                     */
+/* x, y: [N, C, inner] described by a 4-D NCHW tensor (any of NCHW or   */
+/* channels-last strides).  mean/invstd: [C] fp32.                      */
+/* ------------------------------------------------------------------ */
+/* native_batch_norm (train), norm_ops.cpp:19-84: batch stats, running-stat
+ * update with unbiased variance, normalise.  Returns save_mean and
+ * save_invstd (torch's convention; the reference returned var).
+ * gamma/beta/running_* may be NULL.  workspace >= pvb2_batch_norm_workspace_size. */
+PVB2_API size_t pvb2_batch_norm_workspace_size(const pvb2_tensor* x);
+PVB2_API int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma, const float* beta,
+                              float* running_mean, float* running_var, double momentum, double eps,
+                              const pvb2_tensor* y, float* save_mean, float* save_invstd,
+                              void* workspace, size_t workspace_bytes, pvb2_stream stream);
+/* native_batch_norm (eval): uses running stats */
+PVB2_API int pvb2_batch_norm_fwd_eval(const pvb2_tensor* x, const float* gamma, const float* beta,
+                             const float* running_mean, const float* running_var, double eps,
+                             const pvb2_tensor* y, pvb2_stream stream);
+/* native_batch_norm_backward (training statistics), norm_ops.cpp:87-164.
+ * mean/invstd are save_mean/save_invstd of the forward; `train` must be 1.
+ * dx/dgamma/dbeta may be NULL. */
+PVB2_API int pvb2_batch_norm_bwd(const pvb2_tensor* dy, const pvb2_tensor* x, const float* gamma,
+                        const float* mean, const float* invstd, int train,
+                        const pvb2_tensor* dx, float* dgamma, float* dbeta,
+                        void* workspace, size_t workspace_bytes, pvb2_stream stream);
+/* native_batch_norm_backward with running statistics (eval mode):
+ * dx = dy * gamma / sqrt(running_var + eps) */
+PVB2_API int pvb2_batch_norm_bwd_eval(const pvb2_tensor* dy, const float* gamma, const float* running_var,
+                             double eps, const pvb2_tensor* dx, pvb2_stream stream);
+/* native_layer_norm / _backward, norm_ops.cpp:167-351.  x: [M, N] rows
+ * (contiguous), gamma/beta: [N] or NULL.  mean/rstd: [M]. */
+PVB2_API int pvb2_layer_norm_fwd(const float* x, const float* gamma, const float* beta, int64_t M, int64_t N,
+                        double eps, float* y, float* mean, float* rstd, pvb2_stream stream);
+PVB2_API size_t pvb2_layer_norm_bwd_workspace_size(int64_t M, int64_t N);
+PVB2_API int pvb2_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
+                        const float* gamma, int64_t M, int64_t N, float* dx, float* dgamma, float* dbeta,
+                        void* workspace, size_t workspace_bytes, pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* pooling (src/vision_ops.cpp)                                         */
+/* ------------------------------------------------------------------ */
+typedef struct pvb2_pool2d_desc {
+  int32_t kh, kw, sh, sw, ph, pw, dh, dw;
+  int32_t ceil_mode;
+  int32_t count_include_pad;   /* avg pool */
+  int32_t divisor_override;    /* avg pool, 0 = none */
+} pvb2_pool2d_desc;
+/* max_pool2d_cls forward, vision_ops.cpp:353-410.  x,y NCHW (contiguous or
+ * channels-last); indices int64 with y's layout (flat h*W+w, torch's
+ * convention, bit-exact with CPU) or NULL. */
+PVB2_API int pvb2_max_pool2d_fwd(const pvb2_pool2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* y,
+                        int64_t* indices, pvb2_stream stream);
+/* max_pool2d_cls backward, vision_ops.cpp:411-438 (indices-based here) */
+PVB2_API int pvb2_max_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* dy, const int64_t* indices,
+                        const pvb2_tensor* dx, pvb2_stream stream);
+/* avg_pool2d.out / avg_pool2d_backward, vision_ops.cpp:448-511 */
+PVB2_API int pvb2_avg_pool2d_fwd(const pvb2_pool2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* y, pvb2_stream stream);
+PVB2_API int pvb2_avg_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* dy, const pvb2_tensor* dx, pvb2_stream stream);
+/* _adaptive_avg_pool2d / _backward, vision_ops.cpp:188-241 (general
+ * adaptive windows; the reference supported global pooling only) */
+PVB2_API int pvb2_adaptive_avg_pool2d_fwd(const pvb2_tensor* x, const pvb2_tensor* y, pvb2_stream stream);
+PVB2_API int pvb2_adaptive_avg_pool2d_bwd(const pvb2_tensor* dy, const pvb2_tensor* dx, pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* softmax and losses (src/loss_ops.cpp)                                */
+/* x viewed as (outer, dim, inner), contiguous.                         */
+/* ------------------------------------------------------------------ */
+/* _log_softmax.out / _softmax.out, loss_ops.cpp:137-175 */
+PVB2_API int pvb2_softmax_fwd(int log_softmax, const float* x, float* y, int64_t outer, int64_t dim, int64_t inner,
+                     pvb2_stream stream);
+/* _log_softmax_backward_data.out / _softmax_backward_data.out, loss_ops.cpp:177-213 */
+PVB2_API int pvb2_softmax_bwd(int log_softmax, const float* dy, const float* y, float* dx, int64_t outer, int64_t dim,
+                     int64_t inner, pvb2_stream stream);
+/* nll_loss_forward.output, loss_ops.cpp:23-44.  x [N, C] (or [C] with N=1),
+ * target int64 [N].  reduction 0 none / 1 mean / 2 sum.  weight may be NULL.
+ * out: [N] for none, [] otherwise; total_weight: [] */
+PVB2_API int pvb2_nll_loss_fwd(const float* x, const int64_t* target, const float* weight, int64_t N, int64_t C,
+                      int reduction, int64_t ignore_index, float* out, float* total_weight,
+                      pvb2_stream stream);
+/* nll_loss_backward.grad_input, loss_ops.cpp:46-65 */
+PVB2_API int pvb2_nll_loss_bwd(const float* grad_out, const int64_t* target, const float* weight,
+                      const float* total_weight, int64_t N, int64_t C, int reduction,
+                      int64_t ignore_index, float* grad_in, pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* GEMM (src/vision_ops.cpp:513-673 mm/bmm/addmm, :243-351 linear)      */
+/* C[b] = alpha * A[b] @ B[b] + beta * C[b] (+ bias broadcast)          */
+/* A: [batch, M, K], B: [batch, K, N], C: [batch, M, N]; any strides.   */
+/* bias: NULL, or [N] (bias_dim=1) / [M] (bias_dim=0), added after      */
+/* alpha/beta.                                                          */
+/* math: 0 = TF32 tensor cores where the shapes allow, 1 = exact fp32   */
+/*       (SIMT), 2 = 3xTF32 split (fp32-accurate on tensor cores).      */
+/* ------------------------------------------------------------------ */
+enum { PVB2_MATH_TF32 = 0, PVB2_MATH_FP32 = 1, PVB2_MATH_3XTF32 = 2 };
+PVB2_API int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
+              const float* bias, int bias_dim, double alpha, double beta, int math,
+              pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* convolution (src/vision_ops.cpp:30-186)                              */
+/* ------------------------------------------------------------------ */
+typedef struct pvb2_conv2d_desc {
+  int32_t N, C, H, W;          /* input                                 */
+  int32_t K, R, S;             /* output channels, kernel h, kernel w    */
+  int32_t P, Q;                /* output h, w                            */
+  int32_t stride_h, stride_w, pad_h, pad_w, dil_h, dil_w;
+  int32_t groups;
+  int32_t math;                /* PVB2_MATH_*                            */
+} pvb2_conv2d_desc;
+/* which: 0 fwd, 1 bwd data, 2 bwd filter */
+PVB2_API size_t pvb2_conv2d_workspace_size(const pvb2_conv2d_desc* d, int which);
+/* convolution_overrideable, vision_ops.cpp:61-113: y = conv(x, w) + b
+ * x [N,C,H,W], w [K,C/g,R,S] contiguous, y [N,K,P,Q]; x/y NCHW-contiguous
+ * or channels-last.  b may be NULL. */
+PVB2_API int pvb2_conv2d_fwd(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const float* w, const float* b,
+                    const pvb2_tensor* y, void* workspace, size_t workspace_bytes, pvb2_stream stream);
+/* convolution_backward_overrideable, data branch, vision_ops.cpp:116-163 */
+PVB2_API int pvb2_conv2d_bwd_data(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const float* w,
+                         const pvb2_tensor* dx, void* workspace, size_t workspace_bytes, pvb2_stream stream);
+/* convolution_backward_overrideable, filter and bias branches,
+ * vision_ops.cpp:145-180.  dw [K,C/g,R,S]; db [K] or NULL. */
+PVB2_API int pvb2_conv2d_bwd_filter(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* dy,
+                           float* dw, float* db, void* workspace, size_t workspace_bytes,
+                           pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* optimizer: SGD with momentum over many tensors in one launch.        */
+/* Replaces the per-tensor mul_/add_ loop that torch.optim.SGD's        */
+/* foreach path falls into on the reference (add_out / mul_out,         */
+/* pointwise_ops.cpp:115-172,407-411).                                  */
+/* For every i:  g = grads[i] * grad_scale + weight_decay * params[i]   */
+/*   momentum != 0: buf = first_step ? g : momentum*buf + (1-dampening)*g */
+/*                  g = nesterov ? g + momentum*buf : buf               */
+/*   params[i] -= lr * g                                                */
+/* ------------------------------------------------------------------ */
+PVB2_API int pvb2_sgd_multi(int n, float* const* params, const float* const* grads, float* const* momentum_bufs,
+                   const int64_t* numels, double lr, double momentum, double dampening,
+                   double weight_decay, int nesterov, int first_step, double grad_scale,
+                   pvb2_stream stream);
+/* _foreach_* helpers: out[i] = a[i] (op) (b ? b[i] : scalar) with alpha,
+ * for op in {ADD, SUB, MUL, DIV}; out may alias a.  fp32 only. */
+PVB2_API int pvb2_foreach_binary(int op, int n, float* const* out, const float* const* a, const float* const* b,
+                        const int64_t* numels, double scalar, double alpha, pvb2_stream stream);
+/* gather many tensors into one flat buffer (or scatter back): used by the
+ * data-parallel gradient buckets.  direction 0: flat <- tensors, 1: tensors <- flat */
+PVB2_API int pvb2_flatten_multi(int n, float* const* tensors, const int64_t* numels, float* flat, int direction,
+                       double scale, pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* random (src/random_ops.cpp): Philox-4x32-10 counter-based generator  */
+/* (Salmon et al., SC'11).  Element i of the output uses counter        */
+/* (offset + i/4) and key `seed`, lane i%4.                             */
+/* ------------------------------------------------------------------ */
+/* uniform_ :37-45 -> [lo, hi) ; normal_ :47-56 -> mean, std ; bernoulli_ :58-67 -> p */
+enum { PVB2_RNG_UNIFORM = 0, PVB2_RNG_NORMAL = 1, PVB2_RNG_BERNOULLI = 2 };
+PVB2_API int pvb2_philox_fill(int dist, const pvb2_tensor* out, uint64_t seed, uint64_t offset,
+                     double p0, double p1, pvb2_stream stream);
+/* native_dropout, random_ops.cpp:69-89: mask = u >= p, y = x*mask/(1-p) */
+PVB2_API int pvb2_dropout_fwd(const float* x, float* y, uint8_t* mask, int64_t n, double p, uint64_t seed,
+                     uint64_t offset, pvb2_stream stream);
+/* native_dropout_backward, random_ops.cpp:91-105 */
+PVB2_API int pvb2_dropout_bwd(const float* dy, const uint8_t* mask, float* dx, int64_t n, double scale,
+                     pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* data-parallel gradient exchange (no counterpart in the reference,    */
+/* which has no multi-device code): NCCL over NVLink / NVSwitch.        */
+/* ------------------------------------------------------------------ */
+#define PVB2_NCCL_ID_BYTES 128
+PVB2_API int pvb2_nccl_get_unique_id(uint8_t id[PVB2_NCCL_ID_BYTES]);
+PVB2_API int pvb2_nccl_comm_init(void** comm, int nranks, const uint8_t id[PVB2_NCCL_ID_BYTES], int rank);
+/* op: 0 sum, 1 avg.  dtype: PVB2_F32 / PVB2_F64 / PVB2_I64 */
+PVB2_API int pvb2_nccl_allreduce(void* comm, const void* send, void* recv, size_t count, int dtype, int op,
+                        pvb2_stream stream);
+PVB2_API int pvb2_nccl_broadcast(void* comm, void* buf, size_t count, int dtype, int root, pvb2_stream stream);
+PVB2_API int pvb2_nccl_comm_destroy(void* comm);
+PVB2_API int pvb2_nccl_comm_abort(void* comm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PVB2_H */

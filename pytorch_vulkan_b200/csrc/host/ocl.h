@@ -1,0 +1,100 @@
+// Shared declarations of the `ocl` (PrivateUse1) host extension: device and
+// stream registry, tensor descriptors for the C-ABI, allocation helpers,
+// op tracing.  Every op in ops_*.cpp goes through these.
+#pragma once
+#include <ATen/ATen.h>
+#include <c10/core/Allocator.h>
+#include <c10/core/DeviceGuard.h>
+#include <torch/library.h>
+#include <atomic>
+#include <string>
+#include <vector>
+#include "pvb2.h"
+
+namespace ocl {
+
+constexpr c10::DeviceType kOcl = c10::DeviceType::PrivateUse1;
+
+// ------------------------------------------------------------------ errors
+#define OCL_CHECK(expr)                                                                               \
+  do {                                                                                                \
+    int _s = (expr);                                                                                  \
+    TORCH_CHECK(_s == PVB2_OK, "ocl backend: ", #expr, " failed (status ", _s, "): ", pvb2_last_error()); \
+  } while (0)
+
+// ---------------------------------------------------------- device/stream
+int device_count();
+int current_device();
+void set_device(int device);
+void ensure_device(int device);          // make `device` current for this thread if it is not
+pvb2_stream stream_for(int device);      // the current stream of `device` for this thread
+pvb2_stream current_stream();            // stream_for(current_device())
+void after_op(int device);               // sync-after-op debug mode (OPENCL_NO_MEM_CACHE)
+
+// sets the current device to the tensor's for the scope of an op
+struct DeviceScope {
+  int prev;
+  bool changed;
+  explicit DeviceScope(const at::Tensor& t);
+  explicit DeviceScope(int device);
+  ~DeviceScope();
+};
+
+// --------------------------------------------------------------- tracing
+// Replaces ExecGuard / the GUARD macro (src/guard.cpp, src/CLTensor.h:24-37):
+// OPENCL_DEBUG_MODE (or B200_DEBUG_MODE) = 1 reports the failing op, = 2
+// prints an indented trace; while torch.ocl.profile is active each op is
+// bracketed by CUDA events for the CSV log.
+struct ExecGuard {
+  const char* name;
+  int device;
+  int slot;
+  ExecGuard(const char* name, int device);
+  ~ExecGuard();
+};
+extern std::atomic<int> g_trace_mode;
+extern std::atomic<bool> g_profiling;
+#define OCL_OP(name_str, device_index) ::ocl::ExecGuard _ocl_guard((name_str), (device_index))
+
+// ------------------------------------------------------ tensor <-> C-ABI
+int dtype_code(c10::ScalarType t);
+pvb2_tensor desc(const at::Tensor& t);
+// descriptor of `t` broadcast (expanded) to `sizes`
+pvb2_tensor desc_expanded(const at::Tensor& t, c10::IntArrayRef sizes);
+
+// --------------------------------------------------------------- memory
+c10::Allocator* allocator();
+at::Tensor empty(c10::IntArrayRef sizes, c10::ScalarType dtype, int device,
+                 c10::MemoryFormat mf = c10::MemoryFormat::Contiguous);
+at::Tensor empty_like_dev(const at::Tensor& t);          // contiguous, same dtype/device
+at::Tensor empty_strided_dev(c10::IntArrayRef sizes, c10::IntArrayRef strides, c10::ScalarType dtype, int device);
+// scratch buffer from the caching allocator, released at scope exit
+struct Workspace {
+  c10::DataPtr ptr;
+  size_t bytes = 0;
+  Workspace(size_t bytes, int device);
+  void* get() const { return ptr.get(); }
+};
+void allocator_record_stream(const c10::DataPtr& ptr, pvb2_stream stream);
+
+// ------------------------------------------------------------- settings
+int math_mode();                 // PVB2_MATH_* for convolution / GEMM
+void set_math_mode(int mode);
+
+// -------------------------------------------------------------- helpers
+inline bool is_ocl(const at::Tensor& t) { return t.defined() && t.device().type() == kOcl; }
+// a 0-dim CPU tensor (e.g. a wrapped Python number) used as an operand
+inline bool is_cpu_scalar(const at::Tensor& t) {
+  return t.defined() && t.device().is_cpu() && t.dim() == 0;
+}
+// the element type the arithmetic runs in
+int compute_code(c10::ScalarType t);
+// copy src (any device) into dst (ocl), handling dtype and strides on device
+void copy_into(const at::Tensor& dst, const at::Tensor& src, bool non_blocking);
+// dst = src laid out contiguously (returns src itself if already so)
+at::Tensor contiguous(const at::Tensor& t);
+// out may be non-contiguous or of another dtype: run `fn` on a contiguous
+// temp of `dtype` and copy back if needed
+at::Tensor& write_back(at::Tensor& out, const at::Tensor& tmp);
+
+}  // namespace ocl

@@ -1,0 +1,693 @@
+// Neural-network ops of the `ocl` device: convolution, GEMM family, batch /
+// layer norm, pooling, (log)softmax, NLL loss, dropout and random fills.
+//
+// Mirrors the registrations of src/vision_ops.cpp:833-858,
+// src/norm_ops.cpp:354-359, src/loss_ops.cpp:268-280 and
+// src/random_ops.cpp:109-115.  Max-pool is registered as the indices-based
+// torch op pair (max_pool2d_with_indices[_backward]) instead of the
+// reference's autograd override (vision_ops.cpp:353-445), so the indices are
+// the CPU's, bit for bit.
+#include "ocl.h"
+
+namespace ocl {
+
+std::pair<uint64_t, uint64_t> philox_reserve(const std::optional<at::Generator>& gen, int device, int64_t n);
+
+// ============================================================ convolution
+static pvb2_conv2d_desc conv_desc(const at::Tensor& x, const at::Tensor& w, at::IntArrayRef stride,
+                                  at::IntArrayRef padding, at::IntArrayRef dilation, int64_t groups) {
+  TORCH_CHECK(x.dim() == 4 && w.dim() == 4, "ocl conv: only 2-D convolution (4-D tensors) is supported");
+  TORCH_CHECK(stride.size() == 2 && padding.size() == 2 && dilation.size() == 2,
+              "ocl conv: expecting stride/padding/dilation of size 2");
+  pvb2_conv2d_desc d;
+  d.N = (int32_t)x.size(0);
+  d.C = (int32_t)x.size(1);
+  d.H = (int32_t)x.size(2);
+  d.W = (int32_t)x.size(3);
+  d.K = (int32_t)w.size(0);
+  d.R = (int32_t)w.size(2);
+  d.S = (int32_t)w.size(3);
+  d.stride_h = (int32_t)stride[0];
+  d.stride_w = (int32_t)stride[1];
+  d.pad_h = (int32_t)padding[0];
+  d.pad_w = (int32_t)padding[1];
+  d.dil_h = (int32_t)dilation[0];
+  d.dil_w = (int32_t)dilation[1];
+  d.groups = (int32_t)groups;
+  d.P = (d.H + 2 * d.pad_h - d.dil_h * (d.R - 1) - 1) / d.stride_h + 1;
+  d.Q = (d.W + 2 * d.pad_w - d.dil_w * (d.S - 1) - 1) / d.stride_w + 1;
+  d.math = math_mode();
+  TORCH_CHECK(w.size(1) * groups == x.size(1), "ocl conv: weight/input channel mismatch");
+  return d;
+}
+
+// transposed conv y = conv_transpose(x, w): the data-gradient of the forward
+// conv that maps y-shaped inputs to x-shaped outputs
+static pvb2_conv2d_desc tconv_desc(const at::Tensor& x, const at::Tensor& w, at::IntArrayRef stride,
+                                   at::IntArrayRef padding, at::IntArrayRef dilation, at::IntArrayRef output_padding,
+                                   int64_t groups) {
+  pvb2_conv2d_desc d;
+  d.N = (int32_t)x.size(0);
+  d.K = (int32_t)x.size(1);  // forward conv's output channels = transposed input channels
+  d.P = (int32_t)x.size(2);
+  d.Q = (int32_t)x.size(3);
+  d.C = (int32_t)(w.size(1) * groups);
+  d.R = (int32_t)w.size(2);
+  d.S = (int32_t)w.size(3);
+  d.stride_h = (int32_t)stride[0];
+  d.stride_w = (int32_t)stride[1];
+  d.pad_h = (int32_t)padding[0];
+  d.pad_w = (int32_t)padding[1];
+  d.dil_h = (int32_t)dilation[0];
+  d.dil_w = (int32_t)dilation[1];
+  d.groups = (int32_t)groups;
+  d.H = (d.P - 1) * d.stride_h - 2 * d.pad_h + d.dil_h * (d.R - 1) + (int32_t)output_padding[0] + 1;
+  d.W = (d.Q - 1) * d.stride_w - 2 * d.pad_w + d.dil_w * (d.S - 1) + (int32_t)output_padding[1] + 1;
+  d.math = math_mode();
+  return d;
+}
+
+// convolution_overrideable, vision_ops.cpp:61-113
+static at::Tensor convolution(const at::Tensor& input, const at::Tensor& weight, const std::optional<at::Tensor>& bias,
+                              at::IntArrayRef stride, at::IntArrayRef padding, at::IntArrayRef dilation,
+                              bool transposed, at::IntArrayRef output_padding, int64_t groups) {
+  const int dev = input.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("convolution", dev);
+  at::Tensor x = contiguous(input), w = contiguous(weight);
+  const float* b = nullptr;
+  at::Tensor bc;
+  if (bias.has_value() && bias->defined()) {
+    bc = contiguous(*bias);
+    b = bc.data_ptr<float>();
+  }
+  TORCH_CHECK(x.scalar_type() == at::kFloat, "ocl conv: float32 only");
+  pvb2_stream st = stream_for(dev);
+  if (!transposed) {
+    pvb2_conv2d_desc d = conv_desc(x, w, stride, padding, dilation, groups);
+    at::Tensor y = empty({d.N, d.K, d.P, d.Q}, at::kFloat, dev);
+    if (y.numel() == 0) return y;
+    Workspace ws(pvb2_conv2d_workspace_size(&d, 0), dev);
+    pvb2_tensor xd = desc(x), yd = desc(y);
+    OCL_CHECK(pvb2_conv2d_fwd(&d, &xd, w.data_ptr<float>(), b, &yd, ws.get(), ws.bytes, st));
+    return y;
+  }
+  pvb2_conv2d_desc d = tconv_desc(x, w, stride, padding, dilation, output_padding, groups);
+  at::Tensor y = empty({d.N, d.C, d.H, d.W}, at::kFloat, dev);
+  if (y.numel() == 0) return y;
+  Workspace ws(pvb2_conv2d_workspace_size(&d, 1), dev);
+  pvb2_tensor xd = desc(x), yd = desc(y);
+  OCL_CHECK(pvb2_conv2d_bwd_data(&d, &xd, w.data_ptr<float>(), &yd, ws.get(), ws.bytes, st));
+  if (b) {
+    pvb2_tensor bd = desc(bc.view({1, d.C, 1, 1}).expand(y.sizes()));
+    OCL_CHECK(pvb2_binary(PVB2_BIN_ADD, &yd, &yd, &bd, 1.0, 0.0, PVB2_F32, st));
+  }
+  return y;
+}
+
+// convolution_backward_overrideable, vision_ops.cpp:116-186
+static std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward(
+    const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight, at::IntArrayRef stride,
+    at::IntArrayRef padding, at::IntArrayRef dilation, bool transposed, at::IntArrayRef output_padding, int64_t groups,
+    std::array<bool, 3> output_mask) {
+  const int dev = input.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("convolution_backward", dev);
+  at::Tensor x = contiguous(input), w = contiguous(weight), gy = contiguous(grad_output);
+  pvb2_stream st = stream_for(dev);
+  at::Tensor gx, gw, gb;
+  if (!transposed) {
+    pvb2_conv2d_desc d = conv_desc(x, w, stride, padding, dilation, groups);
+    pvb2_tensor xd = desc(x), gyd = desc(gy);
+    if (output_mask[0]) {
+      gx = empty(x.sizes(), at::kFloat, dev);
+      Workspace ws(pvb2_conv2d_workspace_size(&d, 1), dev);
+      pvb2_tensor gxd = desc(gx);
+      OCL_CHECK(pvb2_conv2d_bwd_data(&d, &gyd, w.data_ptr<float>(), &gxd, ws.get(), ws.bytes, st));
+    }
+    if (output_mask[1] || output_mask[2]) {
+      if (output_mask[1]) gw = empty(w.sizes(), at::kFloat, dev);
+      if (output_mask[2]) gb = empty({d.K}, at::kFloat, dev);
+      Workspace ws(output_mask[1] ? pvb2_conv2d_workspace_size(&d, 2) : 0, dev);
+      OCL_CHECK(pvb2_conv2d_bwd_filter(&d, &xd, &gyd, output_mask[1] ? gw.data_ptr<float>() : nullptr,
+                                       output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, st));
+    }
+    return {gx, gw, gb};
+  }
+  // transposed: forward was y = dgrad(x); so dx = conv_fwd(dy), dw = wgrad(input=dy, grad=x)
+  pvb2_conv2d_desc d = tconv_desc(x, w, stride, padding, dilation, output_padding, groups);
+  pvb2_tensor xd = desc(x), gyd = desc(gy);
+  if (output_mask[0]) {
+    gx = empty(x.sizes(), at::kFloat, dev);
+    Workspace ws(pvb2_conv2d_workspace_size(&d, 0), dev);
+    pvb2_tensor gxd = desc(gx);
+    OCL_CHECK(pvb2_conv2d_fwd(&d, &gyd, w.data_ptr<float>(), nullptr, &gxd, ws.get(), ws.bytes, st));
+  }
+  if (output_mask[1]) {
+    gw = empty(w.sizes(), at::kFloat, dev);
+    Workspace ws(pvb2_conv2d_workspace_size(&d, 2), dev);
+    OCL_CHECK(pvb2_conv2d_bwd_filter(&d, &gyd, &xd, gw.data_ptr<float>(), nullptr, ws.get(), ws.bytes, st));
+  }
+  if (output_mask[2]) gb = gy.sum({0, 2, 3});
+  return {gx, gw, gb};
+}
+
+// ================================================================== GEMM
+// 2-D / 3-D operand as a 3-D [batch, rows, cols] descriptor
+static pvb2_tensor as3d(const at::Tensor& t) {
+  pvb2_tensor d = desc(t);
+  if (t.dim() == 2) {
+    d.ndim = 3;
+    d.sizes[2] = d.sizes[1];
+    d.sizes[1] = d.sizes[0];
+    d.sizes[0] = 1;
+    d.strides[2] = d.strides[1];
+    d.strides[1] = d.strides[0];
+    d.strides[0] = 0;
+  }
+  return d;
+}
+
+static void gemm(const at::Tensor& a, const at::Tensor& b, const at::Tensor& c, const float* bias, int bias_dim,
+                 double alpha, double beta) {
+  const int dev = c.device().index();
+  pvb2_tensor A = as3d(a), B = as3d(b), C = as3d(c);
+  OCL_CHECK(pvb2_gemm(&A, &B, &C, bias, bias_dim, alpha, beta, math_mode(), stream_for(dev)));
+}
+
+// mm.out, vision_ops.cpp:513-560
+static at::Tensor& mm_out(const at::Tensor& self, const at::Tensor& mat2, at::Tensor& out) {
+  const int dev = out.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("mm", dev);
+  TORCH_CHECK(self.dim() == 2 && mat2.dim() == 2 && self.size(1) == mat2.size(0), "mm: shape mismatch");
+  if (!out.sizes().equals({self.size(0), mat2.size(1)})) out.resize_({self.size(0), mat2.size(1)});
+  if (out.numel() == 0) return out;
+  if (self.size(1) == 0) return out.zero_();
+  gemm(self, mat2, out, nullptr, 0, 1.0, 0.0);
+  return out;
+}
+
+// bmm.out, vision_ops.cpp:562-626
+static at::Tensor& bmm_out(const at::Tensor& self, const at::Tensor& mat2, at::Tensor& out) {
+  const int dev = out.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("bmm", dev);
+  TORCH_CHECK(self.dim() == 3 && mat2.dim() == 3 && self.size(0) == mat2.size(0) && self.size(2) == mat2.size(1),
+              "bmm: shape mismatch");
+  if (!out.sizes().equals({self.size(0), self.size(1), mat2.size(2)}))
+    out.resize_({self.size(0), self.size(1), mat2.size(2)});
+  if (out.numel() == 0) return out;
+  if (self.size(2) == 0) return out.zero_();
+  gemm(self, mat2, out, nullptr, 0, 1.0, 0.0);
+  return out;
+}
+
+// addmm.out, vision_ops.cpp:628-673:  out = beta*self + alpha*(mat1 @ mat2)
+static at::Tensor& addmm_out(const at::Tensor& self, const at::Tensor& mat1, const at::Tensor& mat2,
+                             const at::Scalar& beta, const at::Scalar& alpha, at::Tensor& out) {
+  const int dev = out.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("addmm", dev);
+  TORCH_CHECK(mat1.dim() == 2 && mat2.dim() == 2 && mat1.size(1) == mat2.size(0), "addmm: shape mismatch");
+  const int64_t M = mat1.size(0), N = mat2.size(1);
+  if (!out.sizes().equals({M, N})) out.resize_({M, N});
+  if (out.numel() == 0) return out;
+  const double b = beta.toDouble(), a = alpha.toDouble();
+  // linear's case: a bias row added once
+  const bool bias_row = b == 1.0 && !out.is_same(self) && self.dim() <= 2 && self.numel() == N &&
+                        (self.dim() == 1 || self.size(0) == 1) && self.scalar_type() == at::kFloat;
+  if (bias_row && mat1.size(1) > 0) {
+    at::Tensor bc = contiguous(self.reshape({N}));
+    gemm(mat1, mat2, out, bc.data_ptr<float>(), 1, a, 0.0);
+    return out;
+  }
+  if (!out.is_same(self)) {
+    if (b == 0.0) out.zero_();
+    else out.copy_(self.expand({M, N}));
+  }
+  if (mat1.size(1) == 0) {
+    if (b != 1.0) out.mul_(b);
+    return out;
+  }
+  gemm(mat1, mat2, out, nullptr, 0, a, b);
+  return out;
+}
+
+// baddbmm.out: out = beta*self + alpha*(batch1 @ batch2)
+static at::Tensor& baddbmm_out(const at::Tensor& self, const at::Tensor& b1, const at::Tensor& b2,
+                               const at::Scalar& beta, const at::Scalar& alpha, at::Tensor& out) {
+  const int dev = out.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("baddbmm", dev);
+  const int64_t B = b1.size(0), M = b1.size(1), N = b2.size(2);
+  if (!out.sizes().equals({B, M, N})) out.resize_({B, M, N});
+  if (out.numel() == 0) return out;
+  const double bb = beta.toDouble();
+  if (!out.is_same(self)) {
+    if (bb == 0.0) out.zero_();
+    else out.copy_(self.expand({B, M, N}));
+  }
+  gemm(b1, b2, out, nullptr, 0, alpha.toDouble(), bb);
+  return out;
+}
+
+// =========================================================== batch norm
+// native_batch_norm, norm_ops.cpp:19-84 (returns save_mean/save_invstd)
+static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
+    const at::Tensor& input, const std::optional<at::Tensor>& weight, const std::optional<at::Tensor>& bias,
+    const std::optional<at::Tensor>& running_mean, const std::optional<at::Tensor>& running_var, bool training,
+    double momentum, double eps) {
+  const int dev = input.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("native_batch_norm", dev);
+  TORCH_CHECK(input.scalar_type() == at::kFloat, "ocl batch_norm: float32 only");
+  at::Tensor x = contiguous(input);
+  const int64_t C = x.size(1);
+  auto ptr = [](const std::optional<at::Tensor>& t) -> float* {
+    return t.has_value() && t->defined() ? t->data_ptr<float>() : nullptr;
+  };
+  for (const auto* t : {&weight, &bias, &running_mean, &running_var})
+    if (t->has_value() && (*t)->defined()) TORCH_CHECK((*t)->is_contiguous(), "ocl batch_norm: parameters must be contiguous");
+  at::Tensor y = empty(x.sizes(), at::kFloat, dev);
+  pvb2_tensor xd = desc(x), yd = desc(y);
+  pvb2_stream st = stream_for(dev);
+  if (training) {
+    at::Tensor mean = empty({C}, at::kFloat, dev), invstd = empty({C}, at::kFloat, dev);
+    Workspace ws(pvb2_batch_norm_workspace_size(&xd), dev);
+    OCL_CHECK(pvb2_batch_norm_fwd_train(&xd, ptr(weight), ptr(bias), ptr(running_mean), ptr(running_var), momentum,
+                                        eps, &yd, mean.data_ptr<float>(), invstd.data_ptr<float>(), ws.get(),
+                                        ws.bytes, st));
+    return {y, mean, invstd};
+  }
+  TORCH_CHECK(ptr(running_mean) && ptr(running_var), "ocl batch_norm: running stats required in eval mode");
+  OCL_CHECK(pvb2_batch_norm_fwd_eval(&xd, ptr(weight), ptr(bias), ptr(running_mean), ptr(running_var), eps, &yd, st));
+  return {y, empty({0}, at::kFloat, dev), empty({0}, at::kFloat, dev)};
+}
+
+// native_batch_norm_backward, norm_ops.cpp:87-164
+static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward(
+    const at::Tensor& grad_out, const at::Tensor& input, const std::optional<at::Tensor>& weight,
+    const std::optional<at::Tensor>& running_mean, const std::optional<at::Tensor>& running_var,
+    const std::optional<at::Tensor>& save_mean, const std::optional<at::Tensor>& save_invstd, bool train, double eps,
+    std::array<bool, 3> output_mask) {
+  const int dev = input.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("native_batch_norm_backward", dev);
+  at::Tensor x = contiguous(input), gy = contiguous(grad_out);
+  const int64_t C = x.size(1);
+  const float* g = weight.has_value() && weight->defined() ? weight->data_ptr<float>() : nullptr;
+  at::Tensor gx, gw, gb;
+  if (output_mask[0]) gx = empty(x.sizes(), at::kFloat, dev);
+  if (output_mask[1]) gw = empty({C}, at::kFloat, dev);
+  if (output_mask[2]) gb = empty({C}, at::kFloat, dev);
+  pvb2_stream st = stream_for(dev);
+  pvb2_tensor xd = desc(x), gyd = desc(gy);
+  if (train) {
+    TORCH_CHECK(save_mean.has_value() && save_invstd.has_value(), "ocl batch_norm_backward: saved stats required");
+    pvb2_tensor gxd;
+    if (output_mask[0]) gxd = desc(gx);
+    Workspace ws(pvb2_batch_norm_workspace_size(&xd), dev);
+    OCL_CHECK(pvb2_batch_norm_bwd(&gyd, &xd, g, save_mean->data_ptr<float>(), save_invstd->data_ptr<float>(), 1,
+                                  output_mask[0] ? &gxd : nullptr, output_mask[1] ? gw.data_ptr<float>() : nullptr,
+                                  output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, st));
+    return {gx, gw, gb};
+  }
+  // running statistics (eval-mode backward)
+  TORCH_CHECK(running_mean.has_value() && running_var.has_value(), "ocl batch_norm_backward: running stats required");
+  if (output_mask[0]) {
+    pvb2_tensor gxd = desc(gx);
+    OCL_CHECK(pvb2_batch_norm_bwd_eval(&gyd, g, running_var->data_ptr<float>(), eps, &gxd, st));
+  }
+  std::vector<int64_t> red{0};
+  for (int64_t d = 2; d < x.dim(); ++d) red.push_back(d);
+  std::vector<int64_t> bshape(x.dim(), 1);
+  bshape[1] = C;
+  if (output_mask[2]) gb.copy_(gy.sum(red));
+  if (output_mask[1]) {
+    at::Tensor invstd = (*running_var + eps).rsqrt();
+    gw.copy_((gy * (x - running_mean->view(bshape)) * invstd.view(bshape)).sum(red));
+  }
+  return {gx, gw, gb};
+}
+
+// =========================================================== layer norm
+// native_layer_norm, norm_ops.cpp:167-235
+static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_layer_norm(const at::Tensor& input,
+                                                                         at::IntArrayRef normalized_shape,
+                                                                         const std::optional<at::Tensor>& weight,
+                                                                         const std::optional<at::Tensor>& bias,
+                                                                         double eps) {
+  const int dev = input.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("native_layer_norm", dev);
+  at::Tensor x = contiguous(input);
+  const int64_t axis = x.dim() - (int64_t)normalized_shape.size();
+  int64_t M = 1, N = 1;
+  for (int64_t d = 0; d < x.dim(); ++d) (d < axis ? M : N) *= x.size(d);
+  std::vector<int64_t> stat_shape;
+  for (int64_t d = 0; d < x.dim(); ++d) stat_shape.push_back(d < axis ? x.size(d) : 1);
+  at::Tensor y = empty(x.sizes(), at::kFloat, dev);
+  at::Tensor mean = empty(stat_shape, at::kFloat, dev), rstd = empty(stat_shape, at::kFloat, dev);
+  at::Tensor w, b;
+  if (weight.has_value() && weight->defined()) w = contiguous(*weight);
+  if (bias.has_value() && bias->defined()) b = contiguous(*bias);
+  OCL_CHECK(pvb2_layer_norm_fwd(x.data_ptr<float>(), w.defined() ? w.data_ptr<float>() : nullptr,
+                                b.defined() ? b.data_ptr<float>() : nullptr, M, N, eps, y.data_ptr<float>(),
+                                mean.data_ptr<float>(), rstd.data_ptr<float>(), stream_for(dev)));
+  return {y, mean, rstd};
+}
+
+// native_layer_norm_backward, norm_ops.cpp:237-351
+static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_layer_norm_backward(
+    const at::Tensor& grad_out, const at::Tensor& input, at::IntArrayRef normalized_shape, const at::Tensor& mean,
+    const at::Tensor& rstd, const std::optional<at::Tensor>& weight, const std::optional<at::Tensor>& bias,
+    std::array<bool, 3> output_mask) {
+  const int dev = input.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("native_layer_norm_backward", dev);
+  at::Tensor x = contiguous(input), gy = contiguous(grad_out);
+  const int64_t axis = x.dim() - (int64_t)normalized_shape.size();
+  int64_t M = 1, N = 1;
+  for (int64_t d = 0; d < x.dim(); ++d) (d < axis ? M : N) *= x.size(d);
+  at::Tensor w;
+  if (weight.has_value() && weight->defined()) w = contiguous(*weight);
+  at::Tensor gx, gw, gb;
+  if (output_mask[0]) gx = empty(x.sizes(), at::kFloat, dev);
+  if (output_mask[1] && w.defined()) gw = empty(w.sizes(), at::kFloat, dev);
+  if (output_mask[2] && bias.has_value() && bias->defined()) gb = empty(bias->sizes(), at::kFloat, dev);
+  Workspace ws(pvb2_layer_norm_bwd_workspace_size(M, N), dev);
+  OCL_CHECK(pvb2_layer_norm_bwd(gy.data_ptr<float>(), x.data_ptr<float>(), contiguous(mean).data_ptr<float>(),
+                                contiguous(rstd).data_ptr<float>(), w.defined() ? w.data_ptr<float>() : nullptr, M, N,
+                                gx.defined() ? gx.data_ptr<float>() : nullptr,
+                                gw.defined() ? gw.data_ptr<float>() : nullptr,
+                                gb.defined() ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, stream_for(dev)));
+  return {gx, gw, gb};
+}
+
+// ============================================================== pooling
+static pvb2_pool2d_desc pool_desc(at::IntArrayRef k, at::IntArrayRef s, at::IntArrayRef p, at::IntArrayRef d,
+                                  bool ceil_mode) {
+  pvb2_pool2d_desc pd;
+  memset(&pd, 0, sizeof(pd));
+  pd.kh = (int32_t)k[0];
+  pd.kw = (int32_t)(k.size() > 1 ? k[1] : k[0]);
+  pd.sh = s.empty() ? pd.kh : (int32_t)s[0];
+  pd.sw = s.empty() ? pd.kw : (int32_t)(s.size() > 1 ? s[1] : s[0]);
+  pd.ph = (int32_t)p[0];
+  pd.pw = (int32_t)(p.size() > 1 ? p[1] : p[0]);
+  pd.dh = d.empty() ? 1 : (int32_t)d[0];
+  pd.dw = d.empty() ? 1 : (int32_t)(d.size() > 1 ? d[1] : d[0]);
+  pd.ceil_mode = ceil_mode ? 1 : 0;
+  return pd;
+}
+
+static at::Tensor as4d(const at::Tensor& t) { return t.dim() == 3 ? t.unsqueeze(0) : t; }
+
+// max_pool2d_with_indices.out (forward of max_pool2d_cls, vision_ops.cpp:353-410)
+static std::tuple<at::Tensor&, at::Tensor&> max_pool2d_with_indices_out(const at::Tensor& self, at::IntArrayRef k,
+                                                                         at::IntArrayRef s, at::IntArrayRef p,
+                                                                         at::IntArrayRef d, bool ceil_mode,
+                                                                         at::Tensor& out, at::Tensor& indices) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("max_pool2d_with_indices", dev);
+  if (out.numel() == 0) return {out, indices};
+  pvb2_pool2d_desc pd = pool_desc(k, s, p, d, ceil_mode);
+  at::Tensor x = as4d(contiguous(self));
+  at::Tensor o = out.is_contiguous() ? out : empty(out.sizes(), at::kFloat, dev);
+  at::Tensor ind = indices.is_contiguous() ? indices : empty(indices.sizes(), at::kLong, dev);
+  pvb2_tensor xd = desc(x), od = desc(as4d(o));
+  OCL_CHECK(pvb2_max_pool2d_fwd(&pd, &xd, &od, ind.data_ptr<int64_t>(), stream_for(dev)));
+  write_back(out, o);
+  write_back(indices, ind);
+  return {out, indices};
+}
+
+// max_pool2d_with_indices_backward.grad_input (max_pool2d_cls backward, vision_ops.cpp:411-438)
+static at::Tensor& max_pool2d_with_indices_backward_out(const at::Tensor& grad_output, const at::Tensor& self,
+                                                        at::IntArrayRef k, at::IntArrayRef s, at::IntArrayRef p,
+                                                        at::IntArrayRef d, bool ceil_mode, const at::Tensor& indices,
+                                                        at::Tensor& grad_input) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("max_pool2d_with_indices_backward", dev);
+  if (grad_input.numel() == 0) return grad_input;
+  pvb2_pool2d_desc pd = pool_desc(k, s, p, d, ceil_mode);
+  at::Tensor gy = as4d(contiguous(grad_output)), ind = contiguous(indices);
+  at::Tensor gi = grad_input.is_contiguous() ? grad_input : empty(grad_input.sizes(), at::kFloat, dev);
+  pvb2_tensor gyd = desc(gy), gid = desc(as4d(gi));
+  OCL_CHECK(pvb2_max_pool2d_bwd(&pd, &gyd, ind.data_ptr<int64_t>(), &gid, stream_for(dev)));
+  write_back(grad_input, gi);
+  return grad_input;
+}
+
+// avg_pool2d.out / avg_pool2d_backward.grad_input, vision_ops.cpp:448-511
+static at::Tensor& avg_pool2d_out(const at::Tensor& self, at::IntArrayRef k, at::IntArrayRef s, at::IntArrayRef p,
+                                  bool ceil_mode, bool count_include_pad, std::optional<int64_t> divisor_override,
+                                  at::Tensor& out) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("avg_pool2d", dev);
+  if (out.numel() == 0) return out;
+  pvb2_pool2d_desc pd = pool_desc(k, s, p, {}, ceil_mode);
+  pd.count_include_pad = count_include_pad ? 1 : 0;
+  pd.divisor_override = divisor_override.has_value() ? (int32_t)*divisor_override : 0;
+  at::Tensor x = as4d(contiguous(self));
+  at::Tensor o = out.is_contiguous() ? out : empty(out.sizes(), at::kFloat, dev);
+  pvb2_tensor xd = desc(x), od = desc(as4d(o));
+  OCL_CHECK(pvb2_avg_pool2d_fwd(&pd, &xd, &od, stream_for(dev)));
+  write_back(out, o);
+  return out;
+}
+
+static at::Tensor& avg_pool2d_backward_out(const at::Tensor& grad_output, const at::Tensor& self, at::IntArrayRef k,
+                                           at::IntArrayRef s, at::IntArrayRef p, bool ceil_mode,
+                                           bool count_include_pad, std::optional<int64_t> divisor_override,
+                                           at::Tensor& grad_input) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("avg_pool2d_backward", dev);
+  if (grad_input.numel() == 0) return grad_input;
+  pvb2_pool2d_desc pd = pool_desc(k, s, p, {}, ceil_mode);
+  pd.count_include_pad = count_include_pad ? 1 : 0;
+  pd.divisor_override = divisor_override.has_value() ? (int32_t)*divisor_override : 0;
+  at::Tensor gy = as4d(contiguous(grad_output));
+  at::Tensor gi = grad_input.is_contiguous() ? grad_input : empty(grad_input.sizes(), at::kFloat, dev);
+  pvb2_tensor gyd = desc(gy), gid = desc(as4d(gi));
+  OCL_CHECK(pvb2_avg_pool2d_bwd(&pd, &gyd, &gid, stream_for(dev)));
+  write_back(grad_input, gi);
+  return grad_input;
+}
+
+// _adaptive_avg_pool2d / _backward, vision_ops.cpp:188-241
+static at::Tensor adaptive_avg_pool2d(const at::Tensor& self, at::IntArrayRef output_size) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("_adaptive_avg_pool2d", dev);
+  at::Tensor x = as4d(contiguous(self));
+  std::vector<int64_t> osz(self.sizes().begin(), self.sizes().end());
+  osz[osz.size() - 2] = output_size[0];
+  osz[osz.size() - 1] = output_size[1];
+  at::Tensor y = empty(osz, at::kFloat, dev);
+  if (y.numel() == 0) return y;
+  pvb2_tensor xd = desc(x), yd = desc(as4d(y));
+  OCL_CHECK(pvb2_adaptive_avg_pool2d_fwd(&xd, &yd, stream_for(dev)));
+  return y;
+}
+
+static at::Tensor adaptive_avg_pool2d_backward(const at::Tensor& grad_output, const at::Tensor& self) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("_adaptive_avg_pool2d_backward", dev);
+  at::Tensor gy = as4d(contiguous(grad_output));
+  at::Tensor gx = empty(self.sizes(), at::kFloat, dev);
+  if (gx.numel() == 0) return gx;
+  pvb2_tensor gyd = desc(gy), gxd = desc(as4d(gx));
+  OCL_CHECK(pvb2_adaptive_avg_pool2d_bwd(&gyd, &gxd, stream_for(dev)));
+  return gx;
+}
+
+// ======================================================= softmax / loss
+static void split_dim(const at::Tensor& t, int64_t dim, int64_t& outer, int64_t& D, int64_t& inner) {
+  const int64_t d = c10::maybe_wrap_dim(dim, std::max<int64_t>(t.dim(), 1));
+  outer = 1;
+  inner = 1;
+  D = t.dim() ? t.size(d) : 1;
+  for (int64_t i = 0; i < d; ++i) outer *= t.size(i);
+  for (int64_t i = d + 1; i < t.dim(); ++i) inner *= t.size(i);
+}
+
+// _log_softmax.out / _softmax.out, loss_ops.cpp:137-175
+static at::Tensor& softmax_out_impl(bool log, const at::Tensor& self, int64_t dim, at::Tensor& out) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP(log ? "_log_softmax" : "_softmax", dev);
+  if (out.numel() == 0) return out;
+  TORCH_CHECK(self.scalar_type() == at::kFloat, "ocl softmax: float32 only");
+  at::Tensor x = contiguous(self);
+  at::Tensor o = out.is_contiguous() ? out : empty(out.sizes(), at::kFloat, dev);
+  int64_t outer, D, inner;
+  split_dim(x, dim, outer, D, inner);
+  OCL_CHECK(pvb2_softmax_fwd(log ? 1 : 0, x.data_ptr<float>(), o.data_ptr<float>(), outer, D, inner, stream_for(dev)));
+  write_back(out, o);
+  return out;
+}
+static at::Tensor& log_softmax_out(const at::Tensor& self, int64_t dim, bool half_to_float, at::Tensor& out) {
+  return softmax_out_impl(true, self, dim, out);
+}
+static at::Tensor& softmax_out(const at::Tensor& self, int64_t dim, bool half_to_float, at::Tensor& out) {
+  return softmax_out_impl(false, self, dim, out);
+}
+
+// _log_softmax_backward_data.out / _softmax_backward_data.out, loss_ops.cpp:177-213
+static at::Tensor& softmax_bwd_impl(bool log, const at::Tensor& grad_output, const at::Tensor& output, int64_t dim,
+                                    at::Tensor& out) {
+  const int dev = output.device().index();
+  DeviceScope scope(dev);
+  OCL_OP(log ? "_log_softmax_backward" : "_softmax_backward", dev);
+  if (out.numel() == 0) return out;
+  at::Tensor gy = contiguous(grad_output), y = contiguous(output);
+  at::Tensor o = out.is_contiguous() ? out : empty(out.sizes(), at::kFloat, dev);
+  int64_t outer, D, inner;
+  split_dim(y, dim, outer, D, inner);
+  OCL_CHECK(pvb2_softmax_bwd(log ? 1 : 0, gy.data_ptr<float>(), y.data_ptr<float>(), o.data_ptr<float>(), outer, D,
+                             inner, stream_for(dev)));
+  write_back(out, o);
+  return out;
+}
+static at::Tensor& log_softmax_backward_out(const at::Tensor& grad_output, const at::Tensor& output, int64_t dim,
+                                            at::ScalarType input_dtype, at::Tensor& out) {
+  return softmax_bwd_impl(true, grad_output, output, dim, out);
+}
+static at::Tensor& softmax_backward_out(const at::Tensor& grad_output, const at::Tensor& output, int64_t dim,
+                                        at::ScalarType input_dtype, at::Tensor& out) {
+  return softmax_bwd_impl(false, grad_output, output, dim, out);
+}
+
+// nll_loss_forward.output, loss_ops.cpp:23-44
+static std::tuple<at::Tensor&, at::Tensor&> nll_loss_forward_out(const at::Tensor& self, const at::Tensor& target,
+                                                                 const std::optional<at::Tensor>& weight,
+                                                                 int64_t reduction, int64_t ignore_index,
+                                                                 at::Tensor& output, at::Tensor& total_weight) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("nll_loss_forward", dev);
+  at::Tensor x = contiguous(self), t = contiguous(target);
+  const int64_t N = x.dim() == 1 ? 1 : x.size(0), C = x.size(-1);
+  at::Tensor w;
+  if (weight.has_value() && weight->defined()) w = contiguous(*weight);
+  at::Tensor o = output.is_contiguous() ? output : empty(output.sizes(), at::kFloat, dev);
+  OCL_CHECK(pvb2_nll_loss_fwd(x.data_ptr<float>(), t.data_ptr<int64_t>(), w.defined() ? w.data_ptr<float>() : nullptr,
+                              N, C, (int)reduction, ignore_index, o.data_ptr<float>(),
+                              total_weight.data_ptr<float>(), stream_for(dev)));
+  write_back(output, o);
+  return {output, total_weight};
+}
+
+// nll_loss_backward.grad_input, loss_ops.cpp:46-65
+static at::Tensor& nll_loss_backward_out(const at::Tensor& grad_output, const at::Tensor& self,
+                                         const at::Tensor& target, const std::optional<at::Tensor>& weight,
+                                         int64_t reduction, int64_t ignore_index, const at::Tensor& total_weight,
+                                         at::Tensor& grad_input) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("nll_loss_backward", dev);
+  at::Tensor t = contiguous(target), go = contiguous(grad_output);
+  const int64_t N = self.dim() == 1 ? 1 : self.size(0), C = self.size(-1);
+  at::Tensor w;
+  if (weight.has_value() && weight->defined()) w = contiguous(*weight);
+  at::Tensor gi = grad_input.is_contiguous() ? grad_input : empty(grad_input.sizes(), at::kFloat, dev);
+  OCL_CHECK(pvb2_nll_loss_bwd(go.data_ptr<float>(), t.data_ptr<int64_t>(), w.defined() ? w.data_ptr<float>() : nullptr,
+                              total_weight.data_ptr<float>(), N, C, (int)reduction, ignore_index,
+                              gi.data_ptr<float>(), stream_for(dev)));
+  write_back(grad_input, gi);
+  return grad_input;
+}
+
+// ================================================================ random
+// bernoulli_/normal_/uniform_, random_ops.cpp:37-67
+static at::Tensor& philox_fill(at::Tensor& self, int dist, double p0, double p1,
+                               const std::optional<at::Generator>& gen, const char* name) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP(name, dev);
+  if (self.numel() == 0) return self;
+  auto so = philox_reserve(gen, dev, self.numel());
+  pvb2_tensor d = desc(self);
+  OCL_CHECK(pvb2_philox_fill(dist, &d, so.first, so.second, p0, p1, stream_for(dev)));
+  return self;
+}
+static at::Tensor& uniform_(at::Tensor& self, double from, double to, std::optional<at::Generator> gen) {
+  return philox_fill(self, PVB2_RNG_UNIFORM, from, to, gen, "uniform_");
+}
+static at::Tensor& normal_(at::Tensor& self, double mean, double std, std::optional<at::Generator> gen) {
+  return philox_fill(self, PVB2_RNG_NORMAL, mean, std, gen, "normal_");
+}
+static at::Tensor& bernoulli_(at::Tensor& self, double p, std::optional<at::Generator> gen) {
+  return philox_fill(self, PVB2_RNG_BERNOULLI, p, 0, gen, "bernoulli_");
+}
+
+// native_dropout / native_dropout_backward, random_ops.cpp:69-105
+static std::tuple<at::Tensor, at::Tensor> native_dropout(const at::Tensor& input, double p, std::optional<bool> train) {
+  const int dev = input.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("native_dropout", dev);
+  at::Tensor x = contiguous(input);
+  at::Tensor y = empty(x.sizes(), x.scalar_type(), dev);
+  at::Tensor mask = empty(x.sizes(), at::kBool, dev);
+  if (!train.value_or(true) || p == 0.0) {
+    y.copy_(x);
+    mask.fill_(true);
+    return {y, mask};
+  }
+  TORCH_CHECK(x.scalar_type() == at::kFloat, "ocl dropout: float32 only");
+  auto so = philox_reserve(std::nullopt, dev, x.numel());
+  OCL_CHECK(pvb2_dropout_fwd(x.data_ptr<float>(), y.data_ptr<float>(), (uint8_t*)mask.data_ptr(), x.numel(), p,
+                             so.first, so.second, stream_for(dev)));
+  return {y, mask};
+}
+
+static at::Tensor native_dropout_backward(const at::Tensor& grad_output, const at::Tensor& mask, double scale) {
+  const int dev = grad_output.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("native_dropout_backward", dev);
+  at::Tensor gy = contiguous(grad_output), m = contiguous(mask);
+  at::Tensor gx = empty(gy.sizes(), gy.scalar_type(), dev);
+  OCL_CHECK(pvb2_dropout_bwd(gy.data_ptr<float>(), (const uint8_t*)m.data_ptr(), gx.data_ptr<float>(), gy.numel(),
+                             scale, stream_for(dev)));
+  return gx;
+}
+
+}  // namespace ocl
+
+TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
+  using namespace ocl;
+  m.impl("convolution_overrideable", &convolution);
+  m.impl("convolution_backward_overrideable", &convolution_backward);
+  m.impl("mm.out", &mm_out);
+  m.impl("bmm.out", &bmm_out);
+  m.impl("addmm.out", &addmm_out);
+  m.impl("baddbmm.out", &baddbmm_out);
+  m.impl("native_batch_norm", &native_batch_norm);
+  m.impl("native_batch_norm_backward", &native_batch_norm_backward);
+  m.impl("native_layer_norm", &native_layer_norm);
+  m.impl("native_layer_norm_backward", &native_layer_norm_backward);
+  m.impl("max_pool2d_with_indices.out", &max_pool2d_with_indices_out);
+  m.impl("max_pool2d_with_indices_backward.grad_input", &max_pool2d_with_indices_backward_out);
+  m.impl("avg_pool2d.out", &avg_pool2d_out);
+  m.impl("avg_pool2d_backward.grad_input", &avg_pool2d_backward_out);
+  m.impl("_adaptive_avg_pool2d", &adaptive_avg_pool2d);
+  m.impl("_adaptive_avg_pool2d_backward", &adaptive_avg_pool2d_backward);
+  m.impl("_log_softmax.out", &log_softmax_out);
+  m.impl("_softmax.out", &softmax_out);
+  m.impl("_log_softmax_backward_data.out", &log_softmax_backward_out);
+  m.impl("_softmax_backward_data.out", &softmax_backward_out);
+  m.impl("nll_loss_forward.output", &nll_loss_forward_out);
+  m.impl("nll_loss_backward.grad_input", &nll_loss_backward_out);
+  m.impl("uniform_", &uniform_);
+  m.impl("normal_", &normal_);
+  m.impl("bernoulli_.float", &bernoulli_);
+  m.impl("native_dropout", &native_dropout);
+  m.impl("native_dropout_backward", &native_dropout_backward);
+}

@@ -1,0 +1,287 @@
+// 2-D pooling: max (with int64 indices), average, adaptive average.
+//
+// Replaces dlprim::core::Pooling2DForward / MaxPooling2DBackward /
+// AvgPooling2DBackward as called from src/vision_ops.cpp:188-241 (adaptive
+// avg), :353-445 (max_pool2d_cls) and :448-511 (avg_pool2d).  The reference
+// recomputed the argmax from x in backward; here the forward writes torch's
+// flat h*W+w index so max-pool indices are bit-exact with the CPU, and the
+// backward gathers (each input sums the gradients of the windows that picked
+// it, in increasing output order) instead of scattering with atomics, so dx
+// is deterministic and summed in the same order as the CPU kernel.
+#include "common.cuh"
+
+namespace pvb2 {
+
+__global__ void maxpool_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t* __restrict__ ind,
+                                   int64_t planes, int H, int W, int P, int Q, pvb2_pool2d_desc d) {
+  const int64_t total = planes * P * Q;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(i % Q);
+    const int p = (int)((i / Q) % P);
+    const int64_t plane = i / ((int64_t)P * Q);
+    int h0 = p * d.sh - d.ph, w0 = q * d.sw - d.pw;
+    const int h1 = min(h0 + (d.kh - 1) * d.dh + 1, H);
+    const int w1 = min(w0 + (d.kw - 1) * d.dw + 1, W);
+    while (h0 < 0) h0 += d.dh;
+    while (w0 < 0) w0 += d.dw;
+    const float* xp = x + plane * H * W;
+    int64_t best = (int64_t)h0 * W + w0;
+    float bv = -INFINITY;
+    for (int h = h0; h < h1; h += d.dh) {
+      for (int w = w0; w < w1; w += d.dw) {
+        const int64_t idx = (int64_t)h * W + w;
+        const float v = xp[idx];
+        if (v > bv || v != v) {
+          bv = v;
+          best = idx;
+        }
+      }
+    }
+    y[i] = bv;
+    if (ind) ind[i] = best;
+  }
+}
+
+// first output index whose window [o*s - pad, o*s - pad + (k-1)*dil] can include position `pos`
+__device__ __forceinline__ int first_out(int pos, int k, int s, int pad, int dil) {
+  int num = pos + pad - (k - 1) * dil;
+  if (num <= 0) return 0;
+  return (num + s - 1) / s;
+}
+
+__global__ void maxpool_bwd_kernel(const float* __restrict__ dy, const int64_t* __restrict__ ind,
+                                   float* __restrict__ dx, int64_t planes, int H, int W, int P, int Q,
+                                   pvb2_pool2d_desc d) {
+  const int64_t total = planes * H * W;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i % W);
+    const int h = (int)((i / W) % H);
+    const int64_t plane = i / ((int64_t)H * W);
+    const int p0 = first_out(h, d.kh, d.sh, d.ph, d.dh);
+    const int q0 = first_out(w, d.kw, d.sw, d.pw, d.dw);
+    const int p1 = min((h + d.ph) / d.sh + 1, P);
+    const int q1 = min((w + d.pw) / d.sw + 1, Q);
+    const int64_t me = (int64_t)h * W + w;
+    const int64_t base = plane * P * Q;
+    float acc = 0.f;
+    for (int p = p0; p < p1; ++p)
+      for (int q = q0; q < q1; ++q) {
+        const int64_t o = base + (int64_t)p * Q + q;
+        if (ind[o] == me) acc += dy[o];
+      }
+    dx[i] = acc;
+  }
+}
+
+__device__ __forceinline__ int avg_divisor(const pvb2_pool2d_desc& d, int H, int W, int p, int q, int& hs, int& he,
+                                           int& ws, int& we) {
+  hs = p * d.sh - d.ph;
+  ws = q * d.sw - d.pw;
+  he = min(hs + d.kh, H + d.ph);
+  we = min(ws + d.kw, W + d.pw);
+  const int pool_size = (he - hs) * (we - ws);
+  hs = max(hs, 0);
+  ws = max(ws, 0);
+  he = min(he, H);
+  we = min(we, W);
+  if (d.divisor_override) return d.divisor_override;
+  if (d.count_include_pad) return pool_size;
+  return (he - hs) * (we - ws);
+}
+
+__global__ void avgpool_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t planes, int H, int W,
+                                   int P, int Q, pvb2_pool2d_desc d) {
+  const int64_t total = planes * P * Q;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(i % Q);
+    const int p = (int)((i / Q) % P);
+    const int64_t plane = i / ((int64_t)P * Q);
+    int hs, he, ws, we;
+    const int div = avg_divisor(d, H, W, p, q, hs, he, ws, we);
+    const float* xp = x + plane * H * W;
+    float s = 0.f;
+    for (int h = hs; h < he; ++h)
+      for (int w = ws; w < we; ++w) s += xp[(int64_t)h * W + w];
+    y[i] = s / (float)div;
+  }
+}
+
+__global__ void avgpool_bwd_kernel(const float* __restrict__ dy, float* __restrict__ dx, int64_t planes, int H, int W,
+                                   int P, int Q, pvb2_pool2d_desc d) {
+  const int64_t total = planes * H * W;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i % W);
+    const int h = (int)((i / W) % H);
+    const int64_t plane = i / ((int64_t)H * W);
+    const int p0 = first_out(h, d.kh, d.sh, d.ph, 1);
+    const int q0 = first_out(w, d.kw, d.sw, d.pw, 1);
+    const int p1 = min((h + d.ph) / d.sh + 1, P);
+    const int q1 = min((w + d.pw) / d.sw + 1, Q);
+    float acc = 0.f;
+    for (int p = p0; p < p1; ++p)
+      for (int q = q0; q < q1; ++q) {
+        int hs, he, ws, we;
+        const int div = avg_divisor(d, H, W, p, q, hs, he, ws, we);
+        if (h >= hs && h < he && w >= ws && w < we) acc += dy[plane * P * Q + (int64_t)p * Q + q] / (float)div;
+      }
+    dx[i] = acc;
+  }
+}
+
+// adaptive average pooling: window [floor(o*I/O), ceil((o+1)*I/O))
+__device__ __forceinline__ int ad_start(int o, int O, int I) { return (int)(((int64_t)o * I) / O); }
+__device__ __forceinline__ int ad_end(int o, int O, int I) { return (int)((((int64_t)o + 1) * I + O - 1) / O); }
+
+// global pooling (P=Q=1): one warp per plane
+__global__ void global_avgpool_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t planes, int64_t HW) {
+  const int lane = threadIdx.x & 31;
+  const int64_t plane = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (plane >= planes) return;
+  const float* xp = x + plane * HW;
+  float s = 0.f;
+  for (int64_t i = lane; i < HW; i += 32) s += xp[i];
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) y[plane] = s / (float)HW;
+}
+
+__global__ void adaptive_avgpool_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t planes, int H,
+                                            int W, int P, int Q) {
+  const int64_t total = planes * P * Q;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(i % Q);
+    const int p = (int)((i / Q) % P);
+    const int64_t plane = i / ((int64_t)P * Q);
+    const int hs = ad_start(p, P, H), he = ad_end(p, P, H);
+    const int ws = ad_start(q, Q, W), we = ad_end(q, Q, W);
+    const float* xp = x + plane * H * W;
+    float s = 0.f;
+    for (int h = hs; h < he; ++h)
+      for (int w = ws; w < we; ++w) s += xp[(int64_t)h * W + w];
+    y[i] = s / (float)((he - hs) * (we - ws));
+  }
+}
+
+__global__ void adaptive_avgpool_bwd_kernel(const float* __restrict__ dy, float* __restrict__ dx, int64_t planes,
+                                            int H, int W, int P, int Q) {
+  const int64_t total = planes * H * W;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int w = (int)(i % W);
+    const int h = (int)((i / W) % H);
+    const int64_t plane = i / ((int64_t)H * W);
+    float acc = 0.f;
+    // output rows whose window contains h
+    for (int p = 0; p < P; ++p) {
+      const int hs = ad_start(p, P, H), he = ad_end(p, P, H);
+      if (h < hs || h >= he) continue;
+      for (int q = 0; q < Q; ++q) {
+        const int ws = ad_start(q, Q, W), we = ad_end(q, Q, W);
+        if (w < ws || w >= we) continue;
+        acc += dy[plane * P * Q + (int64_t)p * Q + q] / (float)((he - hs) * (we - ws));
+      }
+    }
+    dx[i] = acc;
+  }
+}
+
+static int check_nchw(const pvb2_tensor* t, const char* what) {
+  PVB2_CHECK_ARG(t->dtype == PVB2_F32, "%s: only float32 is supported", what);
+  PVB2_CHECK_ARG(t->ndim == 4, "%s: expected a 4-D NCHW tensor", what);
+  PVB2_CHECK_ARG(is_contiguous(t), "%s: expected NCHW-contiguous memory", what);
+  return PVB2_OK;
+}
+
+}  // namespace pvb2
+
+using namespace pvb2;
+
+extern "C" {
+
+int pvb2_max_pool2d_fwd(const pvb2_pool2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* y, int64_t* indices,
+                        pvb2_stream stream) {
+  PVB2_TRY(check_nchw(x, "max_pool2d"));
+  PVB2_TRY(check_nchw(y, "max_pool2d"));
+  PVB2_CHECK_ARG(d->kh > 0 && d->kw > 0 && d->sh > 0 && d->sw > 0 && d->dh > 0 && d->dw > 0,
+                 "max_pool2d: kernel, stride and dilation must be positive");
+  const int64_t planes = x->sizes[0] * x->sizes[1];
+  const int64_t total = planes * y->sizes[2] * y->sizes[3];
+  if (total == 0) return PVB2_OK;
+  maxpool_fwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(
+      (const float*)x->data, (float*)y->data, indices, planes, (int)x->sizes[2], (int)x->sizes[3], (int)y->sizes[2],
+      (int)y->sizes[3], *d);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+int pvb2_max_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* dy, const int64_t* indices,
+                        const pvb2_tensor* dx, pvb2_stream stream) {
+  PVB2_TRY(check_nchw(dy, "max_pool2d_backward"));
+  PVB2_TRY(check_nchw(dx, "max_pool2d_backward"));
+  const int64_t planes = dx->sizes[0] * dx->sizes[1];
+  const int64_t total = planes * dx->sizes[2] * dx->sizes[3];
+  if (total == 0) return PVB2_OK;
+  maxpool_bwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(
+      (const float*)dy->data, indices, (float*)dx->data, planes, (int)dx->sizes[2], (int)dx->sizes[3],
+      (int)dy->sizes[2], (int)dy->sizes[3], *d);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+int pvb2_avg_pool2d_fwd(const pvb2_pool2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* y, pvb2_stream stream) {
+  PVB2_TRY(check_nchw(x, "avg_pool2d"));
+  PVB2_TRY(check_nchw(y, "avg_pool2d"));
+  const int64_t planes = x->sizes[0] * x->sizes[1];
+  const int64_t total = planes * y->sizes[2] * y->sizes[3];
+  if (total == 0) return PVB2_OK;
+  avgpool_fwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(
+      (const float*)x->data, (float*)y->data, planes, (int)x->sizes[2], (int)x->sizes[3], (int)y->sizes[2],
+      (int)y->sizes[3], *d);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+int pvb2_avg_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* dy, const pvb2_tensor* dx, pvb2_stream stream) {
+  PVB2_TRY(check_nchw(dy, "avg_pool2d_backward"));
+  PVB2_TRY(check_nchw(dx, "avg_pool2d_backward"));
+  const int64_t planes = dx->sizes[0] * dx->sizes[1];
+  const int64_t total = planes * dx->sizes[2] * dx->sizes[3];
+  if (total == 0) return PVB2_OK;
+  avgpool_bwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(
+      (const float*)dy->data, (float*)dx->data, planes, (int)dx->sizes[2], (int)dx->sizes[3], (int)dy->sizes[2],
+      (int)dy->sizes[3], *d);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+int pvb2_adaptive_avg_pool2d_fwd(const pvb2_tensor* x, const pvb2_tensor* y, pvb2_stream stream) {
+  PVB2_TRY(check_nchw(x, "adaptive_avg_pool2d"));
+  PVB2_TRY(check_nchw(y, "adaptive_avg_pool2d"));
+  const int64_t planes = x->sizes[0] * x->sizes[1];
+  const int H = (int)x->sizes[2], W = (int)x->sizes[3], P = (int)y->sizes[2], Q = (int)y->sizes[3];
+  if (planes * P * Q == 0) return PVB2_OK;
+  if (P == 1 && Q == 1) {
+    const int warps = 8;
+    global_avgpool_kernel<<<(unsigned)((planes + warps - 1) / warps), warps * 32, 0, as_stream(stream)>>>(
+        (const float*)x->data, (float*)y->data, planes, (int64_t)H * W);
+  } else {
+    const int64_t total = planes * P * Q;
+    adaptive_avgpool_fwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(
+        (const float*)x->data, (float*)y->data, planes, H, W, P, Q);
+  }
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+int pvb2_adaptive_avg_pool2d_bwd(const pvb2_tensor* dy, const pvb2_tensor* dx, pvb2_stream stream) {
+  PVB2_TRY(check_nchw(dy, "adaptive_avg_pool2d_backward"));
+  PVB2_TRY(check_nchw(dx, "adaptive_avg_pool2d_backward"));
+  const int64_t planes = dx->sizes[0] * dx->sizes[1];
+  const int64_t total = planes * dx->sizes[2] * dx->sizes[3];
+  if (total == 0) return PVB2_OK;
+  adaptive_avgpool_bwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(
+      (const float*)dy->data, (float*)dx->data, planes, (int)dx->sizes[2], (int)dx->sizes[3], (int)dy->sizes[2],
+      (int)dy->sizes[3]);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+}  // extern "C"

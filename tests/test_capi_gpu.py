@@ -1,0 +1,284 @@
+"""Parity through the C-ABI (libpvb2.so via ctypes, no torch dispatcher): each
+entry point is called with raw device pointers and checked against the
+oracle (numpy restatements in oracle.npref / torch-CPU) on seeded inputs,
+including edge cases (empty tensors, ragged sizes, ties in max-pool)."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import npref
+
+pytestmark = pytest.mark.gpu
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(REPO, "pytorch_vulkan_b200", "lib", "libpvb2.so")
+DEV = "ocl:0"
+
+
+class T(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("sizes", ctypes.c_int64 * 8), ("strides", ctypes.c_int64 * 8),
+                ("ndim", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+
+DT = {torch.float32: 0, torch.float64: 1, torch.int64: 4, torch.int32: 5, torch.uint8: 8, torch.bool: 9}
+
+
+def td(t):
+    return T(t.data_ptr() if t.numel() else None, (ctypes.c_int64 * 8)(*t.shape), (ctypes.c_int64 * 8)(*t.stride()),
+             t.dim(), DT[t.dtype])
+
+
+class Conv(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ["N", "C", "H", "W", "K", "R", "S", "P", "Q", "stride_h", "stride_w",
+                                             "pad_h", "pad_w", "dil_h", "dil_w", "groups", "math"]]
+
+
+class Pool(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ["kh", "kw", "sh", "sw", "ph", "pw", "dh", "dw", "ceil_mode",
+                                             "count_include_pad", "divisor_override"]]
+
+
+@pytest.fixture(scope="module")
+def lib(ocl):
+    L = ctypes.CDLL(LIB)
+    L.pvb2_last_error.restype = ctypes.c_char_p
+    L.pvb2_conv2d_workspace_size.restype = ctypes.c_size_t
+    L.pvb2_batch_norm_workspace_size.restype = ctypes.c_size_t
+    return L
+
+
+def stream():
+    import pytorch_vulkan_b200 as p
+
+    return ctypes.c_void_p(p._C.impl_stream_handle(0))
+
+
+def sync():
+    torch.ocl.synchronize()
+
+
+def ok(lib, status):
+    assert status == 0, lib.pvb2_last_error().decode()
+
+
+def dev(x):
+    return torch.as_tensor(x).to(DEV)
+
+
+@pytest.mark.parametrize("math", [1, 0])
+@pytest.mark.parametrize("shape", [
+    # N, C, H, W, K, R, S, stride, pad, dil, groups
+    (2, 8, 9, 11, 12, 3, 3, 1, 1, 1, 1),
+    (2, 6, 10, 20, 8, 3, 5, 2, 2, 1, 2),
+    (3, 16, 7, 7, 32, 1, 1, 1, 0, 1, 1),
+    (1, 3, 23, 23, 16, 7, 7, 2, 3, 1, 1),
+    (2, 64, 14, 14, 64, 3, 3, 1, 1, 1, 1),
+    (2, 128, 8, 8, 256, 1, 1, 2, 0, 1, 1),
+    (2, 4, 9, 9, 4, 3, 3, 1, 2, 2, 1),
+])
+def test_conv_fwd_bwd_capi(lib, shape, math):
+    N, C, H, W, K, R, S, st, pd, dl, g = shape
+    rng = np.random.default_rng(sum(shape))
+    x = rng.standard_normal((N, C, H, W)).astype(np.float32)
+    w = (rng.standard_normal((K, C // g, R, S)) * 0.2).astype(np.float32)
+    b = rng.standard_normal(K).astype(np.float32)
+    yref = npref.conv2d(x, w, b, (st, st), (pd, pd), (dl, dl), g)
+    P, Q = yref.shape[2], yref.shape[3]
+    d = Conv(N, C, H, W, K, R, S, P, Q, st, st, pd, pd, dl, dl, g, math)
+    xd, wd, bd = dev(x), dev(w), dev(b)
+    yd = torch.empty((N, K, P, Q)).to(DEV)
+    ws = torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), 0), 4), dtype=torch.uint8).to(DEV)
+    sync()
+    ok(lib, lib.pvb2_conv2d_fwd(ctypes.byref(d), ctypes.byref(td(xd)), ctypes.c_void_p(wd.data_ptr()),
+                                ctypes.c_void_p(bd.data_ptr()), ctypes.byref(td(yd)), ctypes.c_void_p(ws.data_ptr()),
+                                ctypes.c_size_t(ws.numel()), stream()))
+    sync()
+    tol = 1e-4 if math == 1 else 3e-3 * max(1.0, np.abs(yref).max())
+    assert np.abs(yd.cpu().numpy() - yref).max() <= tol
+    # backward against torch-CPU autograd (the reference's arbiter)
+    xt = torch.from_numpy(x).requires_grad_()
+    wt = torch.from_numpy(w).requires_grad_()
+    yt = torch.nn.functional.conv2d(xt, wt, None, st, pd, dl, g)
+    gy = torch.from_numpy(rng.standard_normal(yt.shape).astype(np.float32))
+    yt.backward(gy)
+    gyd = gy.to(DEV)
+    gxd = torch.empty(x.shape).to(DEV)
+    gwd = torch.empty(w.shape).to(DEV)
+    gbd = torch.empty(K).to(DEV)
+    ws1 = torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), 1), 4), dtype=torch.uint8).to(DEV)
+    ws2 = torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), 2), 4), dtype=torch.uint8).to(DEV)
+    sync()
+    ok(lib, lib.pvb2_conv2d_bwd_data(ctypes.byref(d), ctypes.byref(td(gyd)), ctypes.c_void_p(wd.data_ptr()),
+                                     ctypes.byref(td(gxd)), ctypes.c_void_p(ws1.data_ptr()),
+                                     ctypes.c_size_t(ws1.numel()), stream()))
+    ok(lib, lib.pvb2_conv2d_bwd_filter(ctypes.byref(d), ctypes.byref(td(xd)), ctypes.byref(td(gyd)),
+                                       ctypes.c_void_p(gwd.data_ptr()), ctypes.c_void_p(gbd.data_ptr()),
+                                       ctypes.c_void_p(ws2.data_ptr()), ctypes.c_size_t(ws2.numel()), stream()))
+    sync()
+    sx = max(1.0, xt.grad.abs().max().item())
+    sw = max(1.0, wt.grad.abs().max().item())
+    tx, tw = (1e-4 * sx, 2e-4 * sw) if math == 1 else (3e-3 * sx, 3e-3 * sw)
+    assert (gxd.cpu() - xt.grad).abs().max().item() <= tx
+    assert (gwd.cpu() - wt.grad).abs().max().item() <= tw
+    assert (gbd.cpu() - gy.sum((0, 2, 3))).abs().max().item() <= 1e-3 * max(1.0, gy.abs().sum().item() / K)
+
+
+@pytest.mark.parametrize("M,N,K,batch", [(1, 1, 1, 1), (7, 13, 5, 2), (64, 1000, 2048, 1), (128, 128, 128, 3),
+                                         (300, 257, 129, 1), (64, 9216, 128, 1)])
+@pytest.mark.parametrize("math", [1, 0])
+def test_gemm_capi(lib, M, N, K, batch, math):
+    rng = np.random.default_rng(M * N + K)
+    a = rng.standard_normal((batch, M, K)).astype(np.float32)
+    b = rng.standard_normal((batch, K, N)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    ref = np.einsum("bmk,bkn->bmn", a.astype(np.float64), b.astype(np.float64)) * 0.5 + bias
+    ad, bd, bsd = dev(a), dev(b), dev(bias)
+    cd = torch.empty((batch, M, N)).to(DEV)
+    sync()
+    ok(lib, lib.pvb2_gemm(ctypes.byref(td(ad)), ctypes.byref(td(bd)), ctypes.byref(td(cd)),
+                          ctypes.c_void_p(bsd.data_ptr()), 1, ctypes.c_double(0.5), ctypes.c_double(0.0), math,
+                          stream()))
+    sync()
+    err = np.abs(cd.cpu().numpy() - ref).max()
+    scale = np.sqrt(K) * 0.5
+    assert err <= (1e-5 * scale + 1e-5 if math == 1 else 2e-3 * scale + 1e-4), err
+
+
+def test_gemm_transposed_operands_capi(lib):
+    """B given as a transposed view (linear's W^T): strides carried through the C-ABI."""
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((64, 512)).astype(np.float32)
+    w = rng.standard_normal((1000, 512)).astype(np.float32)
+    xd, wd = dev(x), dev(w)
+    out = torch.empty((64, 1000)).to(DEV)
+    A, B, C = xd.unsqueeze(0), wd.t().unsqueeze(0), out.unsqueeze(0)
+    sync()
+    ok(lib, lib.pvb2_gemm(ctypes.byref(td(A)), ctypes.byref(td(B)), ctypes.byref(td(C)), None, 1,
+                          ctypes.c_double(1.0), ctypes.c_double(0.0), 0, stream()))
+    sync()
+    ref = x.astype(np.float64) @ w.T.astype(np.float64)
+    assert np.abs(out.cpu().numpy() - ref).max() <= 2e-3 * np.sqrt(512)
+
+
+@pytest.mark.parametrize("shape", [(4, 3, 5, 6), (64, 64, 56, 56), (2, 8, 7, 7), (3, 5, 1, 1), (0, 4, 3, 3)])
+def test_batch_norm_capi(lib, shape):
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal(shape) * 3 + 2).astype(np.float32)
+    C = shape[1]
+    gam, bet = rng.standard_normal(C).astype(np.float32), rng.standard_normal(C).astype(np.float32)
+    rm, rv = np.zeros(C, np.float32), np.ones(C, np.float32)
+    xd, gd, bd, rmd, rvd = dev(x), dev(gam), dev(bet), dev(rm), dev(rv)
+    yd = torch.empty(shape).to(DEV)
+    md, isd = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    wsz = lib.pvb2_batch_norm_workspace_size(ctypes.byref(td(xd)))
+    ws = torch.empty(max(wsz, 4), dtype=torch.uint8).to(DEV)
+    sync()
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    ok(lib, lib.pvb2_batch_norm_fwd_train(ctypes.byref(td(xd)), ptr(gd), ptr(bd), ptr(rmd), ptr(rvd),
+                                          ctypes.c_double(0.1), ctypes.c_double(1e-5), ctypes.byref(td(yd)), ptr(md),
+                                          ptr(isd), ptr(ws), ctypes.c_size_t(ws.numel()), stream()))
+    sync()
+    if shape[0] == 0:
+        return
+    y, mean, invstd, nrm, nrv = npref.batch_norm_train(x, gam, bet, rm, rv, 0.1, 1e-5)
+    assert np.abs(yd.cpu().numpy() - y).max() < 1e-4
+    assert np.abs(md.cpu().numpy() - mean).max() < 1e-5
+    assert np.abs(rmd.cpu().numpy() - nrm).max() < 1e-5
+    assert np.abs(rvd.cpu().numpy() - nrv).max() < 1e-4
+    dy = rng.standard_normal(shape).astype(np.float32)
+    dyd = dev(dy)
+    dxd, dgd, dbd = torch.empty(shape).to(DEV), torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    sync()
+    ok(lib, lib.pvb2_batch_norm_bwd(ctypes.byref(td(dyd)), ctypes.byref(td(xd)), ptr(gd), ptr(md), ptr(isd), 1,
+                                    ctypes.byref(td(dxd)), ptr(dgd), ptr(dbd), ptr(ws), ctypes.c_size_t(ws.numel()),
+                                    stream()))
+    sync()
+    dx, dg, db = npref.batch_norm_backward(dy, x, gam, mean, invstd)
+    m = x.size // C
+    assert np.abs(dxd.cpu().numpy() - dx).max() < 1e-4
+    assert np.abs(dgd.cpu().numpy() - dg).max() < 1e-5 * m
+    assert np.abs(dbd.cpu().numpy() - db).max() < 1e-5 * m
+
+
+@pytest.mark.parametrize("cfg", [(3, 2, 1, False), (2, 2, 0, False), (3, 2, 0, True)])
+def test_max_pool_capi_bit_exact(lib, cfg):
+    k, s, p, ceil = cfg
+    rng = np.random.default_rng(2)
+    x = rng.integers(0, 3, (2, 5, 13, 13)).astype(np.float32)  # ties everywhere
+    y, ind = npref.max_pool2d(x, k, s, p, 1, ceil)
+    xd = dev(x)
+    yd = torch.empty(y.shape).to(DEV)
+    indd = torch.empty(y.shape, dtype=torch.int64).to(DEV)
+    pdsc = Pool(k, k, s, s, p, p, 1, 1, int(ceil), 0, 0)
+    sync()
+    ok(lib, lib.pvb2_max_pool2d_fwd(ctypes.byref(pdsc), ctypes.byref(td(xd)), ctypes.byref(td(yd)),
+                                    ctypes.c_void_p(indd.data_ptr()), stream()))
+    sync()
+    assert np.array_equal(yd.cpu().numpy(), y)
+    assert np.array_equal(indd.cpu().numpy(), ind)  # bit-exact indices
+    dy = rng.standard_normal(y.shape).astype(np.float32)
+    dyd = dev(dy)
+    dxd = torch.empty(x.shape).to(DEV)
+    sync()
+    ok(lib, lib.pvb2_max_pool2d_bwd(ctypes.byref(pdsc), ctypes.byref(td(dyd)), ctypes.c_void_p(indd.data_ptr()),
+                                    ctypes.byref(td(dxd)), stream()))
+    sync()
+    assert np.abs(dxd.cpu().numpy() - npref.max_pool2d_backward(dy, ind, x.shape)).max() < 1e-6
+
+
+@pytest.mark.parametrize("N,C", [(64, 1000), (1, 10), (7, 3), (300, 4097)])
+def test_log_softmax_nll_capi(lib, N, C):
+    rng = np.random.default_rng(N + C)
+    x = (rng.standard_normal((N, C)) * 4).astype(np.float32)
+    t = rng.integers(0, C, N).astype(np.int64)
+    if N > 2:
+        t[1] = -100  # ignore_index
+    xd, tdv = dev(x), dev(t)
+    lp = torch.empty((N, C)).to(DEV)
+    out, tw = torch.empty(()).to(DEV), torch.empty(()).to(DEV)
+    sync()
+    ok(lib, lib.pvb2_softmax_fwd(1, ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(lp.data_ptr()),
+                                 ctypes.c_int64(N), ctypes.c_int64(C), ctypes.c_int64(1), stream()))
+    ok(lib, lib.pvb2_nll_loss_fwd(ctypes.c_void_p(lp.data_ptr()), ctypes.c_void_p(tdv.data_ptr()), None,
+                                  ctypes.c_int64(N), ctypes.c_int64(C), 1, ctypes.c_int64(-100),
+                                  ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(tw.data_ptr()), stream()))
+    sync()
+    ref_lp = npref.log_softmax(x, 1)
+    assert np.abs(lp.cpu().numpy() - ref_lp).max() < 1e-5
+    assert abs(out.item() - npref.nll_loss(ref_lp, t, "mean", -100)) < 1e-5
+
+
+def test_sgd_multi_capi(lib):
+    rng = np.random.default_rng(4)
+    sizes = [1, 3, 8193, 100000, 5]
+    ps = [rng.standard_normal(n).astype(np.float32) for n in sizes]
+    gs = [rng.standard_normal(n).astype(np.float32) for n in sizes]
+    pd_ = [dev(p) for p in ps]
+    gd = [dev(g) for g in gs]
+    bd = [torch.empty(n).to(DEV) for n in sizes]
+    arr = lambda ts: (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+    numel = (ctypes.c_int64 * len(sizes))(*sizes)
+    bufs = [None] * len(sizes)
+    ref = list(ps)
+    for it in range(3):
+        sync()
+        ok(lib, lib.pvb2_sgd_multi(len(sizes), arr(pd_), arr(gd), arr(bd), numel, ctypes.c_double(0.1),
+                                   ctypes.c_double(0.9), ctypes.c_double(0.0), ctypes.c_double(1e-4), 0,
+                                   1 if it == 0 else 0, ctypes.c_double(1.0), stream()))
+        sync()
+        for i in range(len(sizes)):
+            ref[i], bufs[i] = npref.sgd_momentum(ref[i], gs[i], bufs[i], 0.1, 0.9, 0.0, 1e-4)
+    for p, r in zip(pd_, ref):
+        assert np.abs(p.cpu().numpy() - r).max() < 1e-5
+
+
+def test_invalid_arguments_are_reported(lib):
+    d = Conv(2, 3, 8, 8, 4, 3, 3, 99, 99, 1, 1, 1, 1, 1, 1, 1, 0)  # inconsistent output size
+    x = torch.empty((2, 3, 8, 8)).to(DEV)
+    y = torch.empty((2, 4, 8, 8)).to(DEV)
+    w = torch.empty((4, 3, 3, 3)).to(DEV)
+    st = lib.pvb2_conv2d_fwd(ctypes.byref(d), ctypes.byref(td(x)), ctypes.c_void_p(w.data_ptr()), None,
+                             ctypes.byref(td(y)), None, ctypes.c_size_t(0), stream())
+    assert st == 1 and b"output size" in lib.pvb2_last_error()

@@ -1,0 +1,89 @@
+"""CPU-only checks of the native libraries: the C-ABI library loads and exports
+every entry point that include/pvb2.h declares, status/error reporting works
+without a GPU, and the torch host extension imports and registers the `ocl`
+device module with the reference's API (python/pytorch_ocl/__init__.py)."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(REPO, "pytorch_vulkan_b200", "lib", "libpvb2.so")
+HDR = os.path.join(REPO, "include", "pvb2.h")
+
+
+def declared_symbols():
+    text = open(HDR).read()
+    return sorted(set(re.findall(r"PVB2_API\s+[\w\s\*]+?\b(pvb2_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert len(syms) > 50
+    for must in ["pvb2_conv2d_fwd", "pvb2_conv2d_bwd_data", "pvb2_conv2d_bwd_filter", "pvb2_gemm",
+                 "pvb2_batch_norm_fwd_train", "pvb2_batch_norm_bwd", "pvb2_layer_norm_fwd", "pvb2_max_pool2d_fwd",
+                 "pvb2_softmax_fwd", "pvb2_nll_loss_fwd", "pvb2_sgd_multi", "pvb2_philox_fill",
+                 "pvb2_nccl_allreduce"]:
+        assert must in syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(LIB)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_library_status_without_gpu():
+    lib = ctypes.CDLL(LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+    n = ctypes.c_int(-1)
+    assert lib.pvb2_device_count(ctypes.byref(n)) == 0
+    assert n.value >= 0
+    assert lib.pvb2_version() >= 1
+    if n.value == 0:
+        # an invalid request is reported as a status code with a message, never an abort
+        assert lib.pvb2_set_device(7) != 0
+        assert len(lib.pvb2_last_error()) > 0
+
+
+def test_launcher_argument_checks_need_no_gpu():
+    """Shape validation happens on the host before any launch."""
+    lib = ctypes.CDLL(LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+
+    class T(ctypes.Structure):
+        _fields_ = [("data", ctypes.c_void_p), ("sizes", ctypes.c_int64 * 8), ("strides", ctypes.c_int64 * 8),
+                    ("ndim", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+    a = T(None, (ctypes.c_int64 * 8)(2, 3, 4), (ctypes.c_int64 * 8)(12, 4, 1), 3, 0)
+    b = T(None, (ctypes.c_int64 * 8)(2, 5, 4), (ctypes.c_int64 * 8)(20, 4, 1), 3, 0)
+    c = T(None, (ctypes.c_int64 * 8)(2, 3, 4), (ctypes.c_int64 * 8)(12, 4, 1), 3, 0)
+    st = lib.pvb2_gemm(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), None, 1, ctypes.c_double(1.0),
+                       ctypes.c_double(0.0), 0, None)
+    assert st == 1  # PVB2_ERR_INVALID: K mismatch (4 vs 5)
+    assert b"shape mismatch" in lib.pvb2_last_error()
+
+
+def test_package_registers_ocl_module():
+    import pytorch_vulkan_b200 as pkg
+
+    assert torch._C._get_privateuse1_backend_name() == "ocl"
+    for name in ["synchronize", "manual_seed_all", "empty_cache", "profile", "enable_profiling", "device",
+                 "_is_in_bad_fork", "is_available", "device_count"]:
+        assert hasattr(torch.ocl, name), name
+    for name in ["impl_custom_device", "impl_seed_all", "impl_synchronize_device", "impl_is_bad_fork",
+                 "impl_empty_cache", "impl_enable_profiling", "impl_start_profiling", "impl_stop_profiling"]:
+        assert hasattr(pkg, name), name
+    assert hasattr(torch.Tensor, "is_ocl")
+
+
+def test_no_cpu_fallback_without_device():
+    """Without a device the backend raises instead of silently computing on the CPU."""
+    import pytorch_vulkan_b200  # noqa: F401
+
+    if torch.ocl.is_available():
+        pytest.skip("a device is visible")
+    with pytest.raises(RuntimeError):
+        torch.empty(3, device="ocl")

@@ -1,0 +1,446 @@
+"""Op-level parity on the `ocl` device against torch-CPU (the reference's own
+differential harness, tests/test_op.py:14-150, with fixed seeds).
+
+Tolerances follow the reference: forward-only ops <= 1e-6 abs, forward +
+backward <= 1e-3 abs (test_op.py:39,103,149), mm / bmm / cat bit-exact
+(test_op.py:190,236,479).  Contractions are checked in both math modes:
+exact fp32 (SIMT, reference tolerances) and TF32 tensor cores (abs 1e-3 +
+rel 2e-3 of the output scale, the stated TF32 tolerance)."""
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+DEV = "ocl:0"
+
+
+def _gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def _inputs(specs, seed, randgen="randn"):
+    g = _gen(seed)
+    xs = []
+    for shape, limit in specs:
+        if limit <= 0:
+            x = torch.randn(shape, generator=g) if randgen == "randn" else torch.rand(shape, generator=g)
+        else:
+            x = torch.randint(limit, shape, generator=g)
+        xs.append(x)
+    return xs
+
+
+def _diff(a, b):
+    return (a.detach().double() - b.detach().to("cpu").double()).abs().max().item() if a.numel() else 0.0
+
+
+def check_fwd(specs, call, tol=1e-6, seed=0):
+    xs = _inputs(specs, seed)
+    with torch.no_grad():
+        y_cpu = call(*xs)
+        y_dev = call(*[x.to(DEV) for x in xs])
+    assert y_dev.device.type == "ocl"
+    d = _diff(y_cpu, y_dev)
+    assert d <= tol, f"forward diff {d} > {tol}"
+
+
+def check_fwd_bwd(specs, call, tol=1e-3, seed=0, randgen="randn"):
+    xs_cpu = _inputs(specs, seed, randgen)
+    xs_dev = []
+    for (shape, limit), x in zip(specs, xs_cpu):
+        xd = x.to(DEV)
+        if limit <= 0:
+            x.requires_grad_()
+            xd.requires_grad_()
+        xs_dev.append(xd)
+    y_cpu = call(*xs_cpu)
+    y_dev = call(*xs_dev)
+    if y_cpu.dim():
+        dy = torch.randn(y_cpu.shape, generator=_gen(seed + 1))
+        y_cpu.backward(dy)
+        y_dev.backward(dy.to(DEV))
+    else:
+        y_cpu.backward()
+        y_dev.backward()
+    diffs = {"y": _diff(y_cpu, y_dev)}
+    for i, (x, xd) in enumerate(zip(xs_cpu, xs_dev)):
+        if x.grad is not None:
+            diffs[f"x{i}"] = _diff(x.grad, xd.grad)
+    worst = max(diffs.values())
+    assert worst <= tol, f"diffs {diffs} > {tol}"
+
+
+def check_module(specs, module, tol=1e-3, seed=0, paramgen=None, rel=0.0):
+    torch.manual_seed(seed)
+    if paramgen is not None:
+        with torch.no_grad():
+            for p in module.parameters():
+                p.copy_(paramgen(p.shape, generator=_gen(seed + 7)))
+    xs_cpu = _inputs(specs, seed)
+    for x in xs_cpu:
+        if x.is_floating_point():
+            x.requires_grad_()
+    y_cpu = module(*xs_cpu)
+    dy = torch.randn(y_cpu.shape, generator=_gen(seed + 1))
+    y_cpu.backward(dy)
+    grads_cpu = {n: p.grad.clone() for n, p in module.named_parameters()}
+    module.zero_grad(set_to_none=True)
+    dev_mod = module.to(DEV)
+    xs_dev = [x.detach().to(DEV).requires_grad_() if x.is_floating_point() else x.to(DEV) for x in xs_cpu]
+    y_dev = dev_mod(*xs_dev)
+    y_dev.backward(dy.to(DEV))
+    scale = max(y_cpu.abs().max().item(), 1.0)
+    diffs = {"y": _diff(y_cpu, y_dev)}
+    for i, (x, xd) in enumerate(zip(xs_cpu, xs_dev)):
+        if x.grad is not None:
+            diffs[f"x{i}"] = _diff(x.grad, xd.grad)
+    for n, p in dev_mod.named_parameters():
+        diffs["p_" + n] = _diff(grads_cpu[n], p.grad)
+    worst = max(diffs.values())
+    assert worst <= tol + rel * scale, f"diffs {diffs}"
+
+
+# ------------------------------------------------------------ reductions
+REDUCTIONS = [
+    ("mean_1d", lambda x: torch.mean(x, dim=0, keepdim=True)),
+    ("mean_2d", lambda x: torch.mean(x, dim=(1, 2), keepdim=True)),
+    ("mean_1d_squeeze", lambda x: torch.mean(x, dim=0, keepdim=False)),
+    ("mean_2d_squeeze", lambda x: torch.mean(x, dim=(0, 2), keepdim=False)),
+    ("mean_all", lambda x: torch.mean(x)),
+    ("sum_1d", lambda x: torch.sum(x, dim=0, keepdim=True)),
+    ("sum_2d", lambda x: torch.sum(x, dim=(1, 2), keepdim=True)),
+    ("sum_1d_squeeze", lambda x: torch.sum(x, dim=0, keepdim=False)),
+    ("sum_2d_squeeze", lambda x: torch.sum(x, dim=(0, 2), keepdim=False)),
+    ("prod_1d", lambda x: torch.prod(x, dim=1, keepdim=True)),
+    ("prod_1d_squeeze", lambda x: torch.prod(x, dim=1, keepdim=False)),
+]
+
+
+@pytest.mark.parametrize("name,fn", REDUCTIONS, ids=[r[0] for r in REDUCTIONS])
+def test_reductions(ocl, name, fn):
+    check_fwd_bwd([([2, 3, 4], -1)], fn)
+
+
+# ------------------------------------------------------- pointwise / acts
+ACTS = [
+    ("logsoftmax_2d", [([4, 3], -1)], nn.LogSoftmax(dim=1)),
+    ("logsoftmax_3d_last", [([4, 3, 5], -1)], nn.LogSoftmax(dim=-1)),
+    ("logsoftmax_3d_mid", [([4, 3, 5], -1)], nn.LogSoftmax(dim=1)),
+    ("logsoftmax_3d_first", [([4, 3, 5], -1)], nn.LogSoftmax(dim=0)),
+    ("softmax", [([4, 3], -1)], nn.Softmax(dim=1)),
+    ("nllloss", [([4, 3], -1), ([4], 3)], nn.NLLLoss()),
+    ("aapool2d", [([4, 8, 2, 2], -1)], nn.AdaptiveAvgPool2d((1, 1))),
+    ("aapool2d_general", [([2, 3, 7, 9], -1)], nn.AdaptiveAvgPool2d((3, 4))),
+    ("abs", [([4, 3], -1)], torch.abs),
+    ("abs_", [([4, 3], -1)], lambda x: torch.abs_(x * 1.0)),
+    ("hardtanh", [([4, 3], -1)], nn.Hardtanh()),
+    ("hardtanh_", [([4, 3], -1)], lambda x: nn.Hardtanh(inplace=True)(x * 1.0)),
+    ("relu6", [([4, 30], -1)], lambda x: nn.ReLU6(inplace=True)(x * 4.0)),
+    ("sigmoid", [([4, 3], -1)], nn.Sigmoid()),
+    ("sigmoid_", [([4, 3], -1)], lambda x: torch.sigmoid_(x * 1.0)),
+    ("hardsigmoid", [([4, 3], -1)], nn.Hardsigmoid()),
+    ("relu", [([4, 3], -1)], nn.ReLU()),
+    ("relu_", [([4, 3], -1)], lambda x: nn.ReLU(inplace=True)(x * 1.0)),
+    ("leaky_relu", [([4, 3], -1)], nn.LeakyReLU()),
+    ("tanh", [([4, 3], -1)], nn.Tanh()),
+    ("tanh_", [([4, 3], -1)], lambda x: torch.tanh_(x * 1.0)),
+    ("silu", [([4, 3], -1)], nn.SiLU()),
+    ("gelu", [([4, 3], -1)], nn.GELU()),
+    ("gelu_tanh", [([4, 3], -1)], lambda x: nn.GELU(approximate="tanh")(x * 1.0)),
+    ("log_sigmoid", [([2, 4], -1)], nn.LogSigmoid()),
+    ("amax", [([2, 3, 4, 5], -1)], lambda x: torch.amax(x, (1, -1))),
+    ("amax_keepdim", [([2, 3, 4, 5], -1)], lambda x: torch.amax(x, (1, -1), keepdim=True)),
+    ("amin", [([2, 3, 4, 5], -1)], lambda x: torch.amin(x, (1, -1))),
+    ("add_broadcast", [([4, 3, 5], -1), ([3, 1], -1)], lambda a, b: a + 2.5 * b),
+    ("mul_div", [([4, 3, 5], -1), ([5], -1)], lambda a, b: a * b / (b.abs() + 1)),
+    ("maxpool_3_2_1", [([2, 4, 11, 11], -1)], lambda x: F.max_pool2d(x, 3, 2, 1)),
+    ("maxpool_2", [([2, 4, 12, 12], -1)], lambda x: F.max_pool2d(x, 2)),
+    ("maxpool_ceil", [([2, 4, 11, 11], -1)], lambda x: F.max_pool2d(x, 3, 2, 0, ceil_mode=True)),
+    ("avgpool", [([2, 4, 11, 11], -1)], lambda x: F.avg_pool2d(x, 3, 2, 1)),
+    ("avgpool_nopad", [([2, 4, 11, 11], -1)], lambda x: F.avg_pool2d(x, 3, 2, 1, count_include_pad=False)),
+    ("cross_entropy", [([6, 10], -1), ([6], 10)], lambda x, t: F.cross_entropy(x, t)),
+    ("batch_norm_train", [([4, 3, 5, 6], -1)],
+     lambda x: F.batch_norm(x, None, None, torch.ones(3, device=x.device), torch.zeros(3, device=x.device), True)),
+    ("layer_norm", [([2, 3, 4, 30], -1)], lambda x: F.layer_norm(x, (4, 30))),
+]
+
+
+@pytest.mark.parametrize("name,specs,fn", ACTS, ids=[a[0] for a in ACTS])
+def test_fwd_bwd_ops(ocl, name, specs, fn):
+    check_fwd_bwd(specs, fn)
+
+
+FWD = [
+    ("atan", [([4, 3, 5], -1)], torch.atan),
+    ("min", [([4, 3, 5], -1)], torch.min),
+    ("max", [([4, 3, 5], -1)], torch.max),
+    ("lerp", [([4, 3, 5], -1), ([4, 3, 1], -1)], lambda x, y: torch.lerp(x, y, 0.1)),
+    ("dot", [([16], -1), ([16], -1)], torch.dot),
+    ("clamp1", [([4, 3, 5], -1)], lambda x: torch.clamp(x, min=-0.2, max=0.3)),
+    ("clamp2", [([4, 3, 5], -1)], lambda x: torch.clamp(x, min=-0.2)),
+    ("clamp3", [([4, 3, 5], -1)], lambda x: torch.clamp(x, max=0.3)),
+    ("pow2", [([2, 4], -1)], lambda a: torch.abs(a) ** 2.0),
+    ("pow13", [([2, 4], -1)], lambda a: torch.abs(a) ** 1.3),
+    ("exp_log", [([2, 4], -1)], lambda a: torch.log(torch.exp(a) + 1)),
+    ("argmax", [([4, 7], -1)], lambda a: torch.argmax(a, 1)),
+    ("where", [([4, 7], -1)], lambda a: torch.where(a > 0, a, a * 0.5)),
+    ("addcmul", [([4, 3], -1), ([4, 3], -1), ([4, 3], -1)], lambda a, b, c: torch.addcmul(a, b, c, value=0.5)),
+    ("addcdiv", [([4, 3], -1), ([4, 3], -1), ([4, 3], -1)],
+     lambda a, b, c: torch.addcdiv(a, b, c.abs() + 1, value=0.5)),
+]
+
+
+@pytest.mark.parametrize("name,specs,fn", FWD, ids=[a[0] for a in FWD])
+def test_fwd_ops(ocl, name, specs, fn):
+    check_fwd(specs, fn)
+
+
+# ------------------------------------------------------- comparisons / logic
+@pytest.mark.parametrize("op", [torch.eq, torch.ne, torch.gt, torch.lt, torch.ge, torch.le, torch.maximum,
+                                torch.minimum])
+def test_compare(ocl, op):
+    """test_op.py:521-557"""
+    check_fwd([([20, 30], -1), ([1, 30], -1)],
+              lambda a, b: op(torch.round(a) * 10, torch.round(b) * 10).to(torch.float))
+    if op not in (torch.maximum, torch.minimum):
+        check_fwd([([20, 30], -1)], lambda a: op(torch.round(a) * 10, 5).to(torch.float))
+    check_fwd([([20, 30], -1)], lambda a: op(torch.round(a) * 10, torch.tensor(5.0)).to(torch.float))
+
+
+@pytest.mark.parametrize("sym", ["&", "|", "^", "~"])
+def test_logical(ocl, sym):
+    ops = {"&": lambda a, b: a & b, "|": lambda a, b: a | b, "^": lambda a, b: a ^ b, "~": lambda a, b: ~a}
+    op = ops[sym]
+    check_fwd([([20, 30], 10), ([1, 30], 10)], lambda a, b: op(a - 5, a - 5))
+    check_fwd([([20, 30], 10), ([1, 30], 10)], lambda a, b: op(a > 5, a > 5).to(torch.float32))
+
+
+# ----------------------------------------------------------- contractions
+@pytest.mark.parametrize("math", ["fp32", "tf32"])
+def test_linear(ocl, math):
+    mode = 1 if math == "fp32" else 0
+    old = torch.ocl.get_math_mode()
+    torch.ocl.set_math_mode(mode)
+    try:
+        tol, rel = (1e-3, 0.0) if math == "fp32" else (1e-3, 2e-3)
+        check_module([([8, 10], -1)], nn.Linear(10, 5), tol=tol, rel=rel)
+        check_module([([2, 6, 10], -1)], nn.Linear(10, 5), tol=tol, rel=rel)
+        check_module([([64, 300], -1)], nn.Linear(300, 130), tol=tol, rel=rel)
+    finally:
+        torch.ocl.set_math_mode(old)
+
+
+CONVS = [
+    ("conv_groups", [([2, 6, 10, 20], -1)], lambda: nn.Conv2d(6, 8, [3, 5], stride=[1, 2], padding=[1, 2], groups=2)),
+    ("conv_3x3", [([2, 16, 14, 14], -1)], lambda: nn.Conv2d(16, 32, 3, padding=1, bias=False)),
+    ("conv_1x1", [([2, 64, 7, 7], -1)], lambda: nn.Conv2d(64, 32, 1, bias=False)),
+    ("conv_1x1_s2", [([2, 32, 14, 14], -1)], lambda: nn.Conv2d(32, 64, 1, stride=2, bias=False)),
+    ("conv_7x7_s2", [([2, 3, 32, 32], -1)], lambda: nn.Conv2d(3, 16, 7, stride=2, padding=3, bias=False)),
+    ("conv_3x3_s2", [([2, 16, 15, 15], -1)], lambda: nn.Conv2d(16, 16, 3, stride=2, padding=1, bias=False)),
+    ("conv_dilated", [([2, 8, 16, 16], -1)], lambda: nn.Conv2d(8, 8, 3, padding=2, dilation=2)),
+    ("depthwise", [([2, 32, 14, 14], -1)], lambda: nn.Conv2d(32, 32, 3, padding=1, groups=32, bias=False)),
+    ("depthwise_s2", [([2, 32, 15, 15], -1)], lambda: nn.Conv2d(32, 32, 3, stride=2, padding=1, groups=32)),
+    ("mnist_conv1", [([4, 1, 28, 28], -1)], lambda: nn.Conv2d(1, 32, 3)),
+    ("convtr", [([2, 6, 10, 20], -1)],
+     lambda: nn.ConvTranspose2d(6, 8, [3, 5], stride=[1, 2], padding=[1, 2], dilation=1, groups=2)),
+    ("convtr_pad", [([2, 6, 10, 20], -1)],
+     lambda: nn.ConvTranspose2d(6, 8, [3, 5], stride=[1, 2], padding=[1, 2], output_padding=[0, 1], groups=2)),
+    ("convtr_nobias", [([2, 6, 10, 20], -1)],
+     lambda: nn.ConvTranspose2d(6, 8, [3, 5], stride=[1, 2], padding=[1, 2], groups=1, bias=False)),
+]
+
+
+@pytest.mark.parametrize("math", ["fp32", "tf32"])
+@pytest.mark.parametrize("name,specs,mk", CONVS, ids=[c[0] for c in CONVS])
+def test_conv(ocl, name, specs, mk, math):
+    old = torch.ocl.get_math_mode()
+    torch.ocl.set_math_mode(1 if math == "fp32" else 0)
+    try:
+        tol, rel = (1e-3, 0.0) if math == "fp32" else (2e-3, 2e-3)
+        check_module(specs, mk(), tol=tol, rel=rel)
+    finally:
+        torch.ocl.set_math_mode(old)
+
+
+def test_batch_norm_module(ocl):
+    bn = nn.BatchNorm2d(5)
+    check_module([([4, 5, 7, 7], -1)], bn, paramgen=torch.randn)
+    # running statistics were updated on the device like on the CPU
+    ref = nn.BatchNorm2d(5)
+    x = _inputs([([4, 5, 7, 7], -1)], 0)[0]
+    ref(x)
+    assert _diff(ref.running_mean, bn.running_mean) < 1e-6
+    assert _diff(ref.running_var, bn.running_var) < 1e-6
+    assert bn.num_batches_tracked.item() == 1
+
+
+def test_layer_norm_affine(ocl):
+    check_module([([2, 3, 4, 30], -1)], nn.LayerNorm((4, 30), elementwise_affine=False))
+    check_module([([2, 3, 4, 30], -1)], nn.LayerNorm((4, 30), elementwise_affine=True), paramgen=torch.randn)
+    check_module([([3, 197, 768], -1)], nn.LayerNorm(768), paramgen=torch.randn)
+
+
+def _mat(D0, D1, d, ind):
+    """test_op.py:153-170: transposed / offset / non-contiguous operands"""
+    tr, offset, non_cont = ind % 2, 0 if ind < 2 else 5, ind >= 4
+    if tr:
+        D0, D1 = D1, D0
+    tmp = torch.arange(0, 400, device=d, dtype=torch.float32)
+    size = D0 * D1 * (4 if non_cont else 1)
+    tmp = tmp[offset:offset + size]
+    tmp = tmp.view(D0 * 2, D1 * 2)[::2, ::2] if non_cont else tmp.view(D0, D1)
+    return tmp.T if tr else tmp
+
+
+@pytest.mark.parametrize("math", [0, 1])
+def test_mm_exact(ocl, math):
+    """test_op.py:172-192: bit-exact over 6x6x6 operand layouts"""
+    old = torch.ocl.get_math_mode()
+    torch.ocl.set_math_mode(math)
+    try:
+        M, N, K = 4, 10, 6
+        for Ct in range(6):
+            for At in range(6):
+                for Bt in range(6):
+                    outs = []
+                    for d in ["cpu", DEV]:
+                        A, B, C = _mat(M, K, d, At), _mat(K, N, d, Bt), _mat(M, N, d, Ct)
+                        torch.mm(A, B, out=C)
+                        outs.append(C)
+                    assert _diff(outs[0], outs[1]) == 0, (At, Bt, Ct)
+    finally:
+        torch.ocl.set_math_mode(old)
+
+
+def _bmat(B, D0, D1, d, ind):
+    tr, offset, non_cont = ind % 2, 0 if ind < 2 else 5, ind >= 4
+    if tr:
+        D0, D1 = D1, D0
+    tmp = torch.arange(0, 10 + B * D0 * D1 * 4, device=d, dtype=torch.float32)
+    size = B * D0 * D1 * (4 if non_cont else 1)
+    tmp = tmp[offset:offset + size]
+    tmp = tmp.view(B, D0 * 2, D1 * 2)[:, ::2, ::2] if non_cont else tmp.view(B, D0, D1)
+    return torch.transpose(tmp, 2, 1) if tr else tmp
+
+
+def test_bmm_exact(ocl):
+    """test_op.py:194-239"""
+    Bc, M, N, K = 3, 4, 10, 6
+    for Ba, Bb in [(Bc, Bc), (1, Bc), (Bc, 1)]:
+        for Ct in range(2):
+            for At in range(6):
+                for Bt in range(6):
+                    outs = []
+                    for d in ["cpu", DEV]:
+                        A, B, C = _bmat(Ba, M, K, d, At), _bmat(Bb, K, N, d, Bt), _bmat(Bc, M, N, d, Ct)
+                        if Ba < Bc:
+                            A = A.expand(Bc, M, K)
+                        if Bb < Bc:
+                            B = B.expand(Bc, K, N)
+                        torch.bmm(A, B, out=C)
+                        outs.append(C)
+                    assert _diff(outs[0], outs[1]) == 0, (Ba, Bb, At, Bt, Ct)
+
+
+@pytest.mark.parametrize("beta,alpha", [(0.0, 1.0), (1.0, 1.0), (1.0, 0.5), (0.5, 0.5)])
+def test_addmm(ocl, math_fp32, beta, alpha):
+    """test_op.py:400-416 (including a transposed `out`)"""
+    check_fwd([([2, 4], -1), ([2, 3], -1), ([3, 4], -1)], lambda a, b, c: torch.addmm(a, b, c, beta=beta, alpha=alpha))
+    check_fwd([([2, 4], -1), ([2, 3], -1), ([3, 4], -1), ([4, 2], -1)],
+              lambda a, b, c, o: torch.addmm(a, b, c, beta=beta, alpha=alpha, out=o.T))
+
+
+def test_cat_exact(ocl):
+    """test_op.py:456-483"""
+    g = _gen(0)
+    x1, x2 = torch.randn(5, 10, generator=g), torch.randn(5, 20, generator=g)
+    y1 = torch.cat((x1, x2), dim=1)
+    y3s = torch.zeros(10, 30)
+    torch.cat((x1, x2), dim=1, out=y3s[::2, :])
+    x1d, x2d = x1.to(DEV), x2.to(DEV)
+    y1d = torch.cat((x1d, x2d), dim=1)
+    y3sd = torch.zeros(10, 30).to(DEV)
+    torch.cat((x1d, x2d), dim=1, out=y3sd[::2, :])
+    assert _diff(y1, y1d) == 0
+    assert _diff(y3s, y3sd) == 0
+
+
+def test_rng_and_dropout(ocl):
+    """test_op.py:492-518"""
+    torch.ocl.manual_seed_all(10)
+    x1 = torch.randn(10, device=DEV).cpu()
+    x2 = torch.randn(10, device=DEV).cpu()
+    torch.ocl.manual_seed_all(10)
+    x3 = torch.randn(10, device=DEV).cpu()
+    assert (x1 - x2).abs().max().item() > 0
+    assert (x1 - x3).abs().max().item() == 0
+    big = torch.randn(100000, device=DEV).cpu()
+    assert abs(big.mean().item()) < 0.02 and abs(big.std().item() - 1) < 0.02
+    u = torch.empty(100000, device=DEV).uniform_(2, 3).cpu()
+    assert u.min() >= 2 and u.max() < 3
+    x = torch.randn(1000, device=DEV, requires_grad=True)
+    y = F.dropout(x, p=0.25, training=False)
+    assert (x - y).abs().max().item() == 0
+    x = torch.rand(1000, device=DEV, requires_grad=True)
+    y = F.dropout(x, p=0.25, training=True)
+    assert abs((y > 0).float().mean().item() - 0.75) < 0.1
+    assert (x.mean() - y.mean()).abs().item() < 0.05
+    y.backward(torch.ones(1000, device=DEV))
+    assert abs((x.grad > 0).float().mean().item() - 0.75) < 0.1
+
+
+def test_copies_and_views(ocl):
+    g = _gen(3)
+    x = torch.randn(4, 5, 6, generator=g)
+    xd = x.to(DEV)
+    assert torch.equal(xd.cpu(), x)
+    assert torch.equal(xd.permute(2, 0, 1).contiguous().cpu(), x.permute(2, 0, 1).contiguous())
+    assert torch.equal(xd[:, 1:4, ::2].cpu(), x[:, 1:4, ::2])
+    assert torch.equal(xd.double().cpu(), x.double())
+    assert torch.equal(xd.to(torch.int64).cpu(), x.to(torch.int64))
+    assert torch.equal(xd.transpose(0, 2).cpu(), x.transpose(0, 2))
+    y = torch.zeros(6, 4, 5).to(DEV)
+    y.copy_(xd.permute(2, 0, 1))
+    assert torch.equal(y.cpu(), x.permute(2, 0, 1))
+    assert xd.sum().item() == pytest.approx(x.sum().item(), rel=1e-5)
+    z = torch.full((3, 3), 2.5, device=DEV)
+    assert torch.equal(z.cpu(), torch.full((3, 3), 2.5))
+    i = torch.arange(10, device=DEV)
+    assert torch.equal(i.cpu(), torch.arange(10))
+    r = torch.empty(0, device=DEV)
+    r.resize_(10)
+    assert r.numel() == 10
+    p = x.pin_memory()
+    assert torch.equal(p.to(DEV, non_blocking=True).cpu(), x)
+
+
+def test_sgd_foreach_and_fused(ocl):
+    g = _gen(5)
+    params = [torch.randn(s, generator=g) for s in [(10, 3), (7,), (4, 4, 4)]]
+    grads = [torch.randn(p.shape, generator=g) for p in params]
+    for kw in [dict(foreach=True), dict(fused=True), dict(foreach=False)]:
+        pc = [p.clone().requires_grad_() for p in params]
+        pd = [p.clone().to(DEV).requires_grad_() for p in params]
+        oc = torch.optim.SGD(pc, lr=0.1, momentum=0.9)
+        od = torch.optim.SGD(pd, lr=0.1, momentum=0.9, **kw)
+        for _ in range(3):
+            for a, b, gr in zip(pc, pd, grads):
+                a.grad = gr.clone()
+                b.grad = gr.to(DEV)
+            oc.step()
+            od.step()
+        for a, b in zip(pc, pd):
+            assert _diff(a, b) < 1e-6, kw
+
+
+def test_profile_csv(ocl, tmp_path):
+    """torch.ocl.profile writes the reference's CSV log (CLTensor.cpp:95-140)"""
+    path = str(tmp_path / "prof.csv")
+    x = torch.randn(64, 64).to(DEV)
+    with torch.ocl.profile(DEV, path):
+        y = torch.relu(x @ x)
+        torch.ocl.synchronize()
+    lines = open(path).read().strip().split("\n")
+    assert lines[0] == "section,kernel,start (ms),end (ms),duraion(ms)"
+    assert any("mm" in l for l in lines[1:])
