@@ -119,6 +119,27 @@ PVB2_API int pvb2_fill(const pvb2_tensor* out, double value, pvb2_stream stream)
 PVB2_API int pvb2_copy(const pvb2_tensor* dst, const pvb2_tensor* src, pvb2_stream stream);
 /* arange.start_out, pointwise_ops.cpp (arange_out): out[i] = start + i*step */
 PVB2_API int pvb2_arange(const pvb2_tensor* out, double start, double step, pvb2_stream stream);
+/* masked_select / nonzero, tensor_ops.cpp:303-356 (the reference copied to
+ * the host; here the compaction runs on the device).  `mask` (bool/u8) and
+ * `src` have equal sizes (broadcast by the caller); elements are taken in
+ * row-major order of those sizes.
+ *   1. pvb2_select_count: per-block counts and their prefix into workspace,
+ *      total count into *d_total (device int64).
+ *   2. pvb2_select_gather: out[k] = k-th selected element of src, or, with
+ *      src == NULL, the k-th selected element's coordinates as
+ *      out[k*ndim + d] (int64), which is nonzero(). */
+PVB2_API size_t pvb2_select_workspace_size(int64_t n);
+PVB2_API int pvb2_select_count(const pvb2_tensor* mask, void* workspace, size_t workspace_bytes,
+                               int64_t* d_total, pvb2_stream stream);
+PVB2_API int pvb2_select_gather(const pvb2_tensor* src, const pvb2_tensor* mask, void* out,
+                                const void* workspace, pvb2_stream stream);
+/* index.Tensor_out (advanced indexing): out[i] = src[i + sum_k idx_k[i] *
+ * index_strides[k]] where src (already restrided: indexed dims have stride
+ * 0) and the int64 index tensors are broadcast to out's sizes; negative
+ * indices wrap by index_sizes[k].  At most 4 index tensors. */
+PVB2_API int pvb2_index_gather(const pvb2_tensor* out, const pvb2_tensor* src, int n_index,
+                               const pvb2_tensor* indices, const int64_t* index_sizes,
+                               const int64_t* index_strides, pvb2_stream stream);
 /* cat.out along `dim`, pointwise_ops.cpp:689-705 (SliceCopy) */
 PVB2_API int pvb2_cat(const pvb2_tensor* out, const pvb2_tensor* inputs, int n_inputs, int dim, pvb2_stream stream);
 
@@ -138,7 +159,9 @@ enum {
   PVB2_UN_POW = 15, PVB2_UN_CLAMP = 16, PVB2_UN_LEAKY_RELU = 17, PVB2_UN_SGN = 18,
   PVB2_UN_HARDSIGMOID = 19, PVB2_UN_HARDSWISH = 20, PVB2_UN_CEIL = 21,
   PVB2_UN_ROUND = 22, PVB2_UN_ATAN = 23, PVB2_UN_RSQRT = 24, PVB2_UN_LOG_SIGMOID = 25,
-  PVB2_UN_BITWISE_NOT = 26, PVB2_UN_CLAMP_MIN = 27, PVB2_UN_FLOOR = 28, PVB2_UN_TRUNC = 29
+  PVB2_UN_BITWISE_NOT = 26, PVB2_UN_CLAMP_MIN = 27, PVB2_UN_FLOOR = 28, PVB2_UN_TRUNC = 29,
+  PVB2_UN_LOGICAL_NOT = 30, PVB2_UN_ISNAN = 31, PVB2_UN_ISINF = 32, PVB2_UN_ISPOSINF = 33,
+  PVB2_UN_ISNEGINF = 34, PVB2_UN_ISFINITE = 35, PVB2_UN_LOGIT = 36 /* p0 = eps, <0 for none */
 };
 enum {
   /* binary: out = f(a, b; p0, p1) */

@@ -45,11 +45,14 @@ def snapshot(model, out=None, loss=None, with_state=False):
 
 
 def cpu_reference(name: str, batch: int, steps: int = 1, lr: float = 0.01, momentum: float = 0.9, seed: int = 0,
-                  input_seed: int = 1234, model=None):
-    """Run `steps` SGD steps of workload `name` on CPU; return (model, snapshot of the last step)."""
+                  input_seed: int = 1234, model=None, dtype=torch.float32):
+    """Run `steps` SGD steps of workload `name` on CPU; return (model, snapshot of the last step).
+    dtype=torch.float64 gives the ground truth that fp32 results are measured against."""
     if model is None:
         model = models.build(name, seed)
+    model = model.to(dtype)
     x, y = models.make_inputs(name, batch, input_seed)
+    x = x.to(dtype)
     opt = torch.optim.SGD(model.parameters(), lr=lr, momentum=momentum, foreach=False)
     loss = models.loss_fn(name)
     model.train()
@@ -98,6 +101,16 @@ def time_cpu_steps(name: str, batch: int, steps: int, warmup: int = 1, threads: 
         train_step(model, x, y, loss, opt)
     dt = (time.perf_counter() - t0) / max(steps, 1)
     return dt, torch.get_num_threads()
+
+
+def frob_rel(a: dict, truth: dict):
+    """per-key ||a - truth||_F / ||truth||_F (keys of `truth` present in `a`)."""
+    out = {}
+    for k, t in truth.items():
+        if k in a and t.numel():
+            n = t.norm().item()
+            out[k] = (a[k] - t).norm().item() / max(n, 1e-30)
+    return out
 
 
 def clone_model(model):

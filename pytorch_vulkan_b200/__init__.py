@@ -24,7 +24,7 @@ try:
 except ImportError as e:  # the product path must fail loudly without its native code
     raise ImportError(
         "pytorch_vulkan_b200: native extension not built "
-        "(run `python -m pytorch_vulkan_b200._build`): " + str(e)
+        "(run `python pytorch_vulkan_b200/_build.py`): " + str(e)
     ) from e
 
 from ._C import (  # noqa: F401  (same impl_* names as the reference's pt_ocl module)

@@ -9,7 +9,8 @@
 Both land in-tree so they travel with the source tree.  Objects go to
 ``<repo>/_build``.  Rebuilds are incremental on source/header mtimes.
 
-Usage:  python -m pytorch_vulkan_b200._build [--force] [-j N]
+Usage:  python pytorch_vulkan_b200/_build.py [--force] [-j N]
+(run it as a script: importing the package first would need the libraries)
 """
 from __future__ import annotations
 

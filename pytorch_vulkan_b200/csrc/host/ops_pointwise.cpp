@@ -190,7 +190,29 @@ UNARY_OUT(trunc_out, PVB2_UN_TRUNC)
 UNARY_OUT(round_out, PVB2_UN_ROUND)
 UNARY_OUT(atan_out, PVB2_UN_ATAN)
 UNARY_OUT(sgn_out, PVB2_UN_SGN)
-UNARY_OUT(bitwise_not_out, PVB2_UN_BITWISE_NOT)
+static at::Tensor& bitwise_not_out(const at::Tensor& self, at::Tensor& out) {
+  return unary_out(self.scalar_type() == at::kBool ? PVB2_UN_LOGICAL_NOT : PVB2_UN_BITWISE_NOT, self, out, 0, 0,
+                   "bitwise_not");
+}
+UNARY_OUT(logical_not_out, PVB2_UN_LOGICAL_NOT)
+UNARY_OUT(isposinf_out, PVB2_UN_ISPOSINF)
+UNARY_OUT(isneginf_out, PVB2_UN_ISNEGINF)
+UNARY_OUT(sign_out, PVB2_UN_SGN)
+static at::Tensor isnan(const at::Tensor& self) {
+  at::Tensor out = empty(self.sizes(), at::kBool, self.device().index());
+  return unary_out(PVB2_UN_ISNAN, self, out, 0, 0, "isnan");
+}
+static at::Tensor& logit_out(const at::Tensor& self, std::optional<double> eps, at::Tensor& out) {
+  return unary_out(PVB2_UN_LOGIT, self, out, eps.has_value() ? *eps : -1.0, 0, "logit");
+}
+static at::Tensor logit(const at::Tensor& self, std::optional<double> eps) {
+  at::Tensor out = empty(self.sizes(), self.scalar_type(), self.device().index());
+  return logit_out(self, eps, out);
+}
+static at::Tensor& clamp_max_out(const at::Tensor& self, const at::Scalar& mx, at::Tensor& out) {
+  return unary_out(PVB2_UN_CLAMP, self, out, at::isFloatingType(out.scalar_type()) ? -INFINITY : -9.2e18, sc(mx),
+                   "clamp_max");
+}
 
 static at::Tensor abs_new(const at::Tensor& self) { return unary_new(PVB2_UN_ABS, self, 0, 0, "abs"); }
 static at::Tensor& hardswish_(at::Tensor& self) { return unary_out(PVB2_UN_HARDSWISH, self, self, 0, 0, "hardswish_"); }
@@ -416,6 +438,210 @@ static at::Tensor& arange_out(const at::Scalar& start, const at::Scalar& end, co
   if (n == 0) return out;
   pvb2_tensor o = desc(out);
   OCL_CHECK(pvb2_arange(&o, s, st, stream_for(dev)));
+  return out;
+}
+
+// all / any: min / max over the values taken as booleans
+static at::Tensor& logical_reduce(bool all, const at::Tensor& self, at::OptionalIntArrayRef dims, bool keepdim,
+                                  at::Tensor& out) {
+  at::Tensor b = self;
+  if (self.scalar_type() != at::kBool) {
+    b = empty(self.sizes(), at::kBool, self.device().index());
+    pvb2_tensor bd = desc(b), sd = desc(self);
+    OCL_CHECK(pvb2_copy(&bd, &sd, stream_for(self.device().index())));
+  }
+  if (self.numel() == 0) return out.fill_(all);
+  return reduce_out(all ? PVB2_RED_MIN : PVB2_RED_MAX, b, dims, keepdim, out, false, all ? "all" : "any");
+}
+static at::Tensor& all_dims_out(const at::Tensor& self, at::OptionalIntArrayRef dim, bool keepdim, at::Tensor& out) {
+  return logical_reduce(true, self, dim, keepdim, out);
+}
+static at::Tensor& all_out(const at::Tensor& self, int64_t dim, bool keepdim, at::Tensor& out) {
+  std::vector<int64_t> d{dim};
+  return logical_reduce(true, self, d, keepdim, out);
+}
+static at::Tensor& all_all_out(const at::Tensor& self, at::Tensor& out) {
+  return logical_reduce(true, self, std::nullopt, false, out);
+}
+static at::Tensor& any_dims_out(const at::Tensor& self, at::OptionalIntArrayRef dim, bool keepdim, at::Tensor& out) {
+  return logical_reduce(false, self, dim, keepdim, out);
+}
+static at::Tensor& any_out(const at::Tensor& self, int64_t dim, bool keepdim, at::Tensor& out) {
+  std::vector<int64_t> d{dim};
+  return logical_reduce(false, self, d, keepdim, out);
+}
+static at::Tensor& any_all_out(const at::Tensor& self, at::Tensor& out) {
+  return logical_reduce(false, self, std::nullopt, false, out);
+}
+
+// masked_select / nonzero (tensor_ops.cpp:303-356): compaction on the device;
+// the one host read is the selected count, needed to size the output
+static int64_t select_count(const pvb2_tensor& m, int dev, Workspace& ws, at::Tensor& total) {
+  OCL_CHECK(pvb2_select_count(&m, ws.get(), ws.bytes, total.data_ptr<int64_t>(), stream_for(dev)));
+  return total.item<int64_t>();
+}
+static at::Tensor masked_select(const at::Tensor& self, const at::Tensor& mask) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("masked_select", dev);
+  auto sizes = at::infer_size(self.sizes(), mask.sizes());
+  pvb2_tensor sd = desc_expanded(self, sizes), md = desc_expanded(mask, sizes);
+  int64_t n = 1;
+  for (auto v : sizes) n *= v;
+  Workspace ws(pvb2_select_workspace_size(n), dev);
+  at::Tensor total = empty({}, at::kLong, dev);
+  const int64_t k = select_count(md, dev, ws, total);
+  at::Tensor out = empty({k}, self.scalar_type(), dev);
+  if (k) OCL_CHECK(pvb2_select_gather(&sd, &md, out.data_ptr(), ws.get(), stream_for(dev)));
+  return out;
+}
+static at::Tensor nonzero(const at::Tensor& self) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("nonzero", dev);
+  pvb2_tensor md = desc(self);
+  Workspace ws(pvb2_select_workspace_size(self.numel()), dev);
+  at::Tensor total = empty({}, at::kLong, dev);
+  const int64_t k = select_count(md, dev, ws, total);
+  at::Tensor out = empty({k, self.dim()}, at::kLong, dev);
+  if (k && self.dim()) OCL_CHECK(pvb2_select_gather(nullptr, &md, out.data_ptr(), ws.get(), stream_for(dev)));
+  return out;
+}
+// masked_fill_: self = mask ? value : self
+static at::Tensor& masked_fill_tensor_(at::Tensor& self, const at::Tensor& mask, const at::Tensor& value) {
+  const int dev = self.device().index();
+  at::Tensor v = value;
+  if (!is_ocl(v)) {
+    v = empty({}, self.scalar_type(), dev);
+    copy_into(v, value.to(self.scalar_type()), false);
+  }
+  return ternary_out(PVB2_TER_WHERE, mask, v, self, 0, self, arith_compute(self), "masked_fill_");
+}
+static at::Tensor& masked_fill_scalar_(at::Tensor& self, const at::Tensor& mask, const at::Scalar& value) {
+  return masked_fill_tensor_(self, mask, at::scalar_tensor(value, at::TensorOptions().dtype(self.scalar_type())));
+}
+
+// index.Tensor_out (advanced indexing).  Same result layout as torch's
+// AdvancedIndex: boolean masks become nonzero() coordinates (on the device),
+// all index tensors broadcast to one shape; if the indexed dims are not
+// adjacent they move to the front; the result is
+// [dims before] + index shape + [dims after], read from src with the indexed
+// dims' strides.  The gather runs on the device.
+static at::Tensor& index_out(const at::Tensor& self, const c10::List<std::optional<at::Tensor>>& indices,
+                             at::Tensor& out) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP("index", dev);
+  // 1. expand masks into per-dim long indices
+  std::vector<at::Tensor> idx;  // one entry per dim of self (undefined = not indexed)
+  for (size_t i = 0; i < indices.size(); ++i) {
+    std::optional<at::Tensor> t = indices[i];
+    if (!t.has_value() || !t->defined()) {
+      idx.emplace_back();
+      continue;
+    }
+    at::Tensor ti = *t;
+    if (ti.scalar_type() == at::kBool || ti.scalar_type() == at::kByte) {
+      const int64_t d0 = (int64_t)idx.size();
+      TORCH_CHECK(d0 + ti.dim() <= self.dim(), "index: too many indices");
+      for (int64_t j = 0; j < ti.dim(); ++j)
+        TORCH_CHECK(ti.size(j) == self.size(d0 + j), "index: mask shape does not match the indexed tensor");
+      at::Tensor nz = is_ocl(ti) ? ti.nonzero() : ti.nonzero().to(self.device());
+      for (int64_t j = 0; j < ti.dim(); ++j) idx.push_back(nz.select(1, j));
+    } else {
+      TORCH_CHECK(ti.scalar_type() == at::kLong || ti.scalar_type() == at::kInt, "index: tensors must be long, int or bool");
+      idx.push_back(is_ocl(ti) ? ti.to(at::kLong) : ti.to(self.device(), at::kLong));
+    }
+  }
+  while ((int64_t)idx.size() < self.dim()) idx.emplace_back();
+  // 2. broadcast the defined indices
+  std::vector<int64_t> bshape;
+  bool first = true;
+  for (auto& t : idx)
+    if (t.defined()) {
+      bshape = first ? t.sizes().vec() : at::infer_size(bshape, t.sizes());
+      first = false;
+    }
+  TORCH_CHECK(!first, "index: no index tensors");
+  // 3. adjacency; move indexed dims to the front when they are not adjacent
+  at::Tensor src = self;
+  std::vector<int64_t> dims_idx;
+  for (int64_t d = 0; d < self.dim(); ++d)
+    if (idx[d].defined()) dims_idx.push_back(d);
+  bool adjacent = true;
+  for (size_t i = 1; i < dims_idx.size(); ++i) adjacent &= dims_idx[i] == dims_idx[i - 1] + 1;
+  if (!adjacent) {
+    std::vector<int64_t> perm;
+    std::vector<at::Tensor> nidx;
+    for (int64_t d : dims_idx) {
+      perm.push_back(d);
+      nidx.push_back(idx[d]);
+    }
+    for (int64_t d = 0; d < self.dim(); ++d)
+      if (!idx[d].defined()) {
+        perm.push_back(d);
+        nidx.emplace_back();
+      }
+    src = self.permute(perm);
+    idx = nidx;
+    dims_idx.clear();
+    for (size_t i = 0; i < nidx.size(); ++i)
+      if (nidx[i].defined()) dims_idx.push_back((int64_t)i);
+  }
+  const int64_t d_first = dims_idx.front(), d_last = dims_idx.back();
+  std::vector<int64_t> osz, ost;
+  std::vector<int64_t> isz, istr;
+  for (int64_t d = 0; d < d_first; ++d) {
+    osz.push_back(src.size(d));
+    ost.push_back(src.stride(d));
+  }
+  const int64_t idx_pos = (int64_t)osz.size();
+  for (int64_t v : bshape) {
+    osz.push_back(v);
+    ost.push_back(0);
+  }
+  for (int64_t d = d_last + 1; d < src.dim(); ++d) {
+    osz.push_back(src.size(d));
+    ost.push_back(src.stride(d));
+  }
+  for (int64_t d : dims_idx) {
+    isz.push_back(src.size(d));
+    istr.push_back(src.stride(d));
+  }
+  TORCH_CHECK(dims_idx.size() <= 4, "ocl index: at most 4 indexed dims");
+  if (!out.sizes().equals(osz)) out.resize_(osz);
+  if (out.numel() == 0) return out;
+  at::Tensor o = out.is_contiguous() ? out : empty(out.sizes(), out.scalar_type(), dev);
+  // src and indices as descriptors of the output's shape
+  pvb2_tensor sd;
+  memset(&sd, 0, sizeof(sd));
+  sd.data = src.data_ptr();
+  sd.ndim = (int32_t)osz.size();
+  sd.dtype = dtype_code(src.scalar_type());
+  for (size_t i = 0; i < osz.size(); ++i) {
+    sd.sizes[i] = osz[i];
+    sd.strides[i] = ost[i];
+  }
+  std::vector<pvb2_tensor> ids;
+  std::vector<at::Tensor> keep;
+  for (int64_t d : dims_idx) {
+    at::Tensor e = idx[d].expand(bshape);
+    keep.push_back(e);
+    pvb2_tensor t;
+    memset(&t, 0, sizeof(t));
+    t.data = e.data_ptr();
+    t.ndim = (int32_t)osz.size();
+    t.dtype = PVB2_I64;
+    for (size_t i = 0; i < osz.size(); ++i) {
+      t.sizes[i] = osz[i];
+      const int64_t j = (int64_t)i - idx_pos;
+      t.strides[i] = (j >= 0 && j < (int64_t)bshape.size()) ? e.stride(j) : 0;
+    }
+    ids.push_back(t);
+  }
+  pvb2_tensor od = desc(o);
+  OCL_CHECK(pvb2_index_gather(&od, &sd, (int)ids.size(), ids.data(), isz.data(), istr.data(), stream_for(dev)));
+  write_back(out, o);
   return out;
 }
 
@@ -648,6 +874,25 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   m.impl("min", &min_all);
   m.impl("dot", &dot);
   m.impl("cat.out", &cat_out);
+  m.impl("logical_not.out", &logical_not_out);
+  m.impl("isposinf.out", &isposinf_out);
+  m.impl("isneginf.out", &isneginf_out);
+  m.impl("isnan", &isnan);
+  m.impl("sign.out", &sign_out);
+  m.impl("logit", &logit);
+  m.impl("logit.out", &logit_out);
+  m.impl("clamp_max.out", &clamp_max_out);
+  m.impl("all.dims_out", &all_dims_out);
+  m.impl("all.out", &all_out);
+  m.impl("all.all_out", &all_all_out);
+  m.impl("any.dims_out", &any_dims_out);
+  m.impl("any.out", &any_out);
+  m.impl("any.all_out", &any_all_out);
+  m.impl("masked_select", &masked_select);
+  m.impl("index.Tensor_out", &index_out);
+  m.impl("nonzero", &nonzero);
+  m.impl("masked_fill_.Scalar", &masked_fill_scalar_);
+  m.impl("masked_fill_.Tensor", &masked_fill_tensor_);
   m.impl("arange.start_out", &arange_out);
   m.impl("_foreach_add_.List", &foreach_add_list_);
   m.impl("_foreach_sub_.List", &foreach_sub_list_);

@@ -73,6 +73,7 @@ inline int64_t numel(const pvb2_tensor* t) {
 }
 
 inline bool is_contiguous(const pvb2_tensor* t) {
+  if (numel(t) == 0) return true;  // torch treats empty tensors as contiguous
   int64_t expect = 1;
   for (int i = t->ndim - 1; i >= 0; --i) {
     if (t->sizes[i] != 1 && t->strides[i] != expect) return false;
@@ -146,7 +147,7 @@ __device__ __forceinline__ void store_as(void* base, int64_t off, int dt, T v) {
 // ------------------------------------------------- strided index helper
 // Up to MAX_ARGS operands sharing one iteration shape, dims coalesced on
 // the host.  offsets computed from a linear index by div/mod per dim.
-constexpr int kMaxArgs = 4;
+constexpr int kMaxArgs = 6;
 struct IterShape {
   int ndim;
   int64_t sizes[PVB2_MAX_DIMS];

@@ -29,9 +29,10 @@ struct ConvGeom {
 
 static ConvGeom geom(const pvb2_conv2d_desc* d) {
   ConvGeom g;
+  const int groups = d->groups > 0 ? d->groups : 1;
   g.N = d->N; g.C = d->C; g.H = d->H; g.W = d->W; g.K = d->K; g.R = d->R; g.S = d->S; g.P = d->P; g.Q = d->Q;
   g.sh = d->stride_h; g.sw = d->stride_w; g.ph = d->pad_h; g.pw = d->pad_w; g.dh = d->dil_h; g.dw = d->dil_w;
-  g.G = d->groups; g.Cg = d->C / d->groups; g.Kg = d->K / d->groups;
+  g.G = groups; g.Cg = d->C / groups; g.Kg = d->K / groups;
   return g;
 }
 
@@ -305,6 +306,7 @@ static bool is_depthwise(const ConvGeom& g) { return g.G > 1 && g.G == g.C && g.
 static int wgrad_splits(const ConvGeom& g) {
   const int64_t kdim = (int64_t)g.N * g.P * g.Q;
   const int64_t tiles = (int64_t)((g.Kg + 63) / 64) * (((int64_t)g.Cg * g.R * g.S + 63) / 64) * g.G;
+  if (tiles <= 0) return 1;
   int64_t want = ((int64_t)num_sms() * 2 + tiles - 1) / tiles;
   int64_t max_by_k = (kdim + 255) / 256;
   if (want > max_by_k) want = max_by_k;
@@ -461,7 +463,13 @@ int pvb2_conv2d_bwd_filter(const pvb2_conv2d_desc* d, const pvb2_tensor* x, cons
   pb.x = (const float*)x->data;
   pb.dy = (const float*)dy->data;
   pb.part = part;
-  PVB2_TRY(launch_igemm_simt(pb, s));
+  // the exact path accumulates the long N*P*Q reduction in fp64: weight
+  // gradients sum many cancelling terms
+  if (d->math == PVB2_MATH_FP32) {
+    PVB2_TRY((launch_igemm_simt<ConvBwdFilterProb, double>(pb, s)));
+  } else {
+    PVB2_TRY(launch_igemm_simt(pb, s));
+  }
   if (splits > 1) {
     reduce_splits_kernel<<<grid_for(wnum, 256), 256, 0, s>>>(part, splits, wnum, dw);
     PVB2_LAUNCH_CHECK();

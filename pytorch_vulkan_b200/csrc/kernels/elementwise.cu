@@ -129,6 +129,17 @@ __device__ __forceinline__ T unary_float(int op, T x, T p0, T p1) {
       T mn = x < zero ? x : zero;
       return mn - M::log1p_(M::exp_(-M::fabs_(x)));
     }
+    case PVB2_UN_LOGICAL_NOT: return x == zero ? one : zero;
+    case PVB2_UN_ISNAN: return is_nan(x) ? one : zero;
+    case PVB2_UN_ISINF: return (!is_nan(x) && M::fabs_(x) == (T)INFINITY) ? one : zero;
+    case PVB2_UN_ISPOSINF: return x == (T)INFINITY ? one : zero;
+    case PVB2_UN_ISNEGINF: return x == (T)-INFINITY ? one : zero;
+    case PVB2_UN_ISFINITE: return (!is_nan(x) && M::fabs_(x) != (T)INFINITY) ? one : zero;
+    case PVB2_UN_LOGIT: {
+      T z = x;
+      if (p0 >= zero) z = z < p0 ? p0 : (z > one - p0 ? one - p0 : z);
+      return M::log_(z / (one - z));
+    }
   }
   return x;
 }
@@ -146,6 +157,12 @@ __device__ __forceinline__ T unary_int(int op, T x, T p0, T p1) {
     case PVB2_UN_AFFINE: return x * p0 + p1;
     case PVB2_UN_SGN: return (T)((x > 0) - (x < 0));
     case PVB2_UN_BITWISE_NOT: return ~x;
+    case PVB2_UN_LOGICAL_NOT: return x == 0 ? 1 : 0;
+    case PVB2_UN_ISNAN:
+    case PVB2_UN_ISINF:
+    case PVB2_UN_ISPOSINF:
+    case PVB2_UN_ISNEGINF: return 0;
+    case PVB2_UN_ISFINITE: return 1;
     case PVB2_UN_CEIL:
     case PVB2_UN_FLOOR:
     case PVB2_UN_TRUNC:

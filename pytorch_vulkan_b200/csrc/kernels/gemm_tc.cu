@@ -1,13 +1,343 @@
-// tcgen05 TF32 GEMM.  Until a shape is claimed here the exact SIMT engine
-// in gemm.cu runs it.
-#include "common.cuh"
+// tcgen05 TF32 GEMM for sm_100a:  C[z] = alpha * A[z] @ B[z] + beta * C[z] (+ bias)
+//
+// Persistent, warp-specialised kernel (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: one thread streams 128x32 A and BNx32 B tiles
+//               (128-byte swizzle) into a kStages-deep shared-memory ring;
+//   warp 1      MMA issuer: allocates 2*BN TMEM columns, one thread issues
+//               tcgen05.mma kind::tf32 (M=128, N=BN, K=8) four times per
+//               32-deep K block and releases ring slots with tcgen05.commit;
+//   warps 2-5   epilogue: drain a finished 128xBN fp32 accumulator from TMEM
+//               (tcgen05.ld 32x32b), apply alpha / beta / bias, store with the
+//               output's strides.  Two TMEM accumulators alternate so the
+//               epilogue of one tile overlaps the main loop of the next.
+// Either operand may be K-major (K contiguous) or MN-major (M/N contiguous),
+// chosen from its strides, so transposed views (linear's W^T, dW = dY^T X)
+// need no copies.  Every wait is bounded (tc_common.cuh).
+//
+// Replaces the dlprim gpu::GEMM / IP kernels behind mm / bmm / addmm / linear
+// (src/vision_ops.cpp:243-351, 513-673).
+#include <cudaTypedefs.h>
+#include <mutex>
+#include "tc_common.cuh"
 
 namespace pvb2 {
 
-int gemm_tc(const pvb2_tensor*, const pvb2_tensor*, const pvb2_tensor*, const float*, int, float, float, int,
-            cudaStream_t, bool* handled) {
+constexpr int kBM = 128, kBK = 32, kStages = 4, kThreads = 192;
+
+struct GemmEpi {
+  float* C;
+  int64_t scb, scm, scn;  // C strides (elements)
+  float alpha, beta;
+  const float* bias;
+  int bias_dim;           // 1: bias[n], 0: bias[m]
+  int M, N, K, batch;
+  int a_bcast, b_bcast;   // operand shared by all batches (batch stride 0)
+};
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int A_BYTES = kBM * kBK * 4;
+  static constexpr int B_BYTES = BN * kBK * 4;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = kStages * STAGE_BYTES;
+  // full[kStages], empty[kStages], acc_full[2], acc_empty[2], tmem slot, abort
+  static constexpr int TOTAL = BAR_OFF + (2 * kStages + 4) * 8 + 16;
+};
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmEpi ep) {
+  using L = GemmSmem<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(smem + L::BAR_OFF);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  volatile int* abort = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_m = (ep.M + kBM - 1) / kBM, tiles_n = (ep.N + BN - 1) / BN;
+  const int total_tiles = tiles_m * tiles_n * ep.batch;
+  const int kblocks = (ep.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch(&tmA);
+      tma_prefetch(&tmB);
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x) {
+        const int nb = tile % tiles_n, mb = (tile / tiles_n) % tiles_m, z = tile / (tiles_n * tiles_m);
+        const int za = ep.a_bcast ? 0 : z, zb = ep.b_bcast ? 0 : z;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
+          uint8_t* sa = smem + s * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_3d(sa, &tmA, &full[s], kb * kBK, mb * kBM, za);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 32; ++j) tma_load_3d(sa + j * 32 * kBK * 4, &tmA, &full[s], mb * kBM + 32 * j, kb * kBK, za);
+          }
+          if (!B_MN) {
+            tma_load_3d(sb, &tmB, &full[s], kb * kBK, nb * BN, zb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j) tma_load_3d(sb + j * 32 * kBK * 4, &tmB, &full[s], nb * BN + 32 * j, kb * kBK, zb);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(kBM, BN, A_MN, B_MN);
+      uint32_t it = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&full[s], ph, abort)) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 8; ++kk) {
+            const uint64_t ad = A_MN ? desc_mnmajor(sa, kk, 32 * kBK * 4) : desc_kmajor(sa, kk);
+            const uint64_t bd = B_MN ? desc_mnmajor(sb, kk, 32 * kBK * 4) : desc_kmajor(sb, kk);
+            mma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+          }
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    int local = 0;
+    for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
+      const int nb = tile % tiles_n, mb = (tile / tiles_n) % tiles_m, z = tile / (tiles_n * tiles_m);
+      const int buf = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], aph, abort)) break;
+      tc_fence_after();
+      const int m = mb * kBM + quarter * 32 + lane;
+      float* crow = ep.C + (int64_t)z * ep.scb + (int64_t)m * ep.scm;
+      const bool mrow = m < ep.M;
+      const float bias_m = (ep.bias && ep.bias_dim == 0 && mrow) ? ep.bias[m] : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + c * 32, v);
+        const int n0 = nb * BN + c * 32;
+        if (mrow) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int n = n0 + j;
+            if (n < ep.N) {
+              float* p = crow + (int64_t)n * ep.scn;
+              float r = ep.alpha * v[j];
+              if (ep.beta != 0.f) r = fmaf(ep.beta, *p, r);
+              if (ep.bias) r += ep.bias_dim == 1 ? ep.bias[n] : bias_m;
+              *p = r;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (*abort) {
+      // let any MMA still in flight finish before the columns are released
+      if (lane == 0) {
+        mma_commit(&acc_full[0]);
+      }
+      __syncwarp();
+      const uint64_t t0 = globaltimer();
+      while (globaltimer() - t0 < 10000000ull) {
+      }
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+int encode_tiled(CUtensorMap* map, int rank, const void* base, const uint64_t* dims, const uint64_t* strides_bytes,
+                 const uint32_t* box, CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2) {
+  auto fn = get_encode();
+  if (!fn) return fail(PVB2_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(PVB2_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PVB2_OK;
+}
+
+// A [batch, rows, cols] operand as a rank-3 TMA map whose innermost dim is
+// its unit-stride dim.  For A, rows = M and cols = K; for B, rows = K and
+// cols = N (`k_is_cols` says which).  *mn_major reports whether the unit-stride
+// dim is M/N (true) or K (false).  Returns PVB2_ERR_UNSUPPORTED when TMA's
+// alignment rules (16-byte base and strides) do not hold.
+static int make_operand_map(CUtensorMap* map, const pvb2_tensor* t, bool k_is_cols, int mn_box, bool* mn_major,
+                            int* bcast) {
+  const int64_t Bt = t->sizes[0], R = t->sizes[1], Cc = t->sizes[2];
+  const int64_t s0 = t->strides[0], s1 = t->strides[1], s2 = t->strides[2];
+  int64_t inner, outer, ostride;
+  bool inner_is_cols;
+  if (s2 == 1 || Cc == 1) {
+    inner_is_cols = true;
+    inner = Cc;
+    outer = R;
+    ostride = s1;
+  } else if (s1 == 1 || R == 1) {
+    inner_is_cols = false;
+    inner = R;
+    outer = Cc;
+    ostride = s2;
+  } else {
+    return PVB2_ERR_UNSUPPORTED;
+  }
+  const bool inner_is_k = inner_is_cols == k_is_cols;
+  *mn_major = !inner_is_k;
+  if (outer == 1) ostride = (inner + 3) / 4 * 4;
+  if (ostride <= 0 || (ostride * 4) % 16 != 0) return PVB2_ERR_UNSUPPORTED;
+  *bcast = (Bt > 1 && s0 == 0) ? 1 : 0;
+  const int64_t nb = (*bcast || Bt == 1) ? 1 : Bt;
+  const int64_t bstride = nb == 1 ? ostride * outer : s0;
+  if (bstride <= 0 || (bstride * 4) % 16 != 0) return PVB2_ERR_UNSUPPORTED;
+  if ((uintptr_t)t->data % 16 != 0) return PVB2_ERR_UNSUPPORTED;
+  uint64_t dims[3] = {(uint64_t)inner, (uint64_t)outer, (uint64_t)nb};
+  uint64_t str[2] = {(uint64_t)ostride * 4, (uint64_t)bstride * 4};
+  uint32_t box[3];
+  if (*mn_major) {
+    box[0] = 32;  // 128 bytes along M/N
+    box[1] = kBK;
+  } else {
+    box[0] = kBK;  // 128 bytes along K
+    box[1] = (uint32_t)mn_box;
+  }
+  box[2] = 1;
+  return encode_tiled(map, 3, t->data, dims, str, box,
+                      *mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmEpi& ep, cudaStream_t s) {
+  constexpr int smem = GemmSmem<BN>::TOTAL + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    PVB2_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_kernel<BN, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       smem));
+    attr_set = true;
+  }
+  const int tiles = ((ep.M + kBM - 1) / kBM) * ((ep.N + BN - 1) / BN) * ep.batch;
+  const int grid = std::min(tiles, num_sms());
+  gemm_tf32_kernel<BN, A_MN, B_MN><<<grid, kThreads, smem, s>>>(ma, mb, ep);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+template <int BN>
+static int dispatch_majors(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmEpi& ep,
+                           cudaStream_t s) {
+  if (!amn && !bmn) return launch_gemm<BN, false, false>(ma, mb, ep, s);
+  if (!amn && bmn) return launch_gemm<BN, false, true>(ma, mb, ep, s);
+  if (amn && !bmn) return launch_gemm<BN, true, false>(ma, mb, ep, s);
+  return launch_gemm<BN, true, true>(ma, mb, ep, s);
+}
+
+int gemm_tc(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, const float* bias, int bias_dim,
+            float alpha, float beta, int math, cudaStream_t s, bool* handled) {
   *handled = false;
+  if (math != PVB2_MATH_TF32) return PVB2_OK;
+  if (getenv("PVB2_DISABLE_TC")) return PVB2_OK;
+  const int64_t batch = C->sizes[0], M = C->sizes[1], N = C->sizes[2], K = A->sizes[2];
+  // small problems: the SIMT engine is as fast and exact
+  if ((double)M * N * K * batch < (double)(1 << 22) || K < 8) return PVB2_OK;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2 || batch > 65535) return PVB2_OK;
+  const int BN = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+  CUtensorMap ma, mb;
+  bool amn = false, bmn = false;
+  int abc = 0, bbc = 0;
+  if (make_operand_map(&ma, A, /*k_is_cols=*/true, kBM, &amn, &abc) != PVB2_OK) return PVB2_OK;
+  if (make_operand_map(&mb, B, /*k_is_cols=*/false, BN, &bmn, &bbc) != PVB2_OK) return PVB2_OK;
+  pvb2::set_error("");
+  GemmEpi ep;
+  ep.C = (float*)C->data;
+  ep.scb = C->strides[0];
+  ep.scm = C->strides[1];
+  ep.scn = C->strides[2];
+  ep.alpha = alpha;
+  ep.beta = beta;
+  ep.bias = bias;
+  ep.bias_dim = bias_dim;
+  ep.M = (int)M;
+  ep.N = (int)N;
+  ep.K = (int)K;
+  ep.batch = (int)batch;
+  ep.a_bcast = abc;
+  ep.b_bcast = bbc;
+  int st;
+  if (BN == 64) st = dispatch_majors<64>(amn, bmn, ma, mb, ep, s);
+  else if (BN == 128) st = dispatch_majors<128>(amn, bmn, ma, mb, ep, s);
+  else st = dispatch_majors<256>(amn, bmn, ma, mb, ep, s);
+  if (st != PVB2_OK) return st;
+  *handled = true;
   return PVB2_OK;
 }
 
 }  // namespace pvb2
+
+extern "C" PVB2_API int pvb2_tc_status(int* timed_out, int reset) {
+  return pvb2::tc_timeout_flag_local(timed_out, reset);
+}

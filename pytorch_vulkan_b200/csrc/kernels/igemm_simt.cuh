@@ -18,7 +18,7 @@ constexpr int kSimtBM = 64, kSimtBN = 64, kSimtBK = 16, kSimtThreads = 256;
 //   __device__ float b(int z, int64_t k, int64_t n) const         (thread-fixed n; see bprep)
 //   __device__ void store(int z, int64_t m, int64_t n, float acc) const
 //   k range per z: [k_begin(z), k_end(z))
-template <class Prob>
+template <class Prob, typename Acc = float>
 __global__ void __launch_bounds__(kSimtThreads) igemm_simt_kernel(Prob pb) {
   __shared__ __align__(16) float As[2][kSimtBK][kSimtBM + 4];
   __shared__ __align__(16) float Bs[2][kSimtBK][kSimtBN + 4];
@@ -34,11 +34,11 @@ __global__ void __launch_bounds__(kSimtThreads) igemm_simt_kernel(Prob pb) {
   const int b_n = tid & 63, b_k = tid >> 6;   // + 4*i
   typename Prob::BCol bcol = pb.bcol(z, n0 + b_n);
 
-  float acc[4][4];
+  Acc acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = (Acc)0;
 
   float ra[4], rb[4];
   auto load_regs = [&](int64_t k0) {
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kSimtThreads) igemm_simt_kernel(Prob pb) {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a4[i], b4[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma((Acc)a4[i], (Acc)b4[j], acc[i][j]);
     }
     if (more) {
       store_smem(buf ^ 1);
@@ -93,18 +93,18 @@ __global__ void __launch_bounds__(kSimtThreads) igemm_simt_kernel(Prob pb) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t n = n0 + tn * 4 + j;
-      if (n < pb.N) pb.store(z, m, n, acc[i][j]);
+      if (n < pb.N) pb.store(z, m, n, (float)acc[i][j]);
     }
   }
 }
 
-template <class Prob>
+template <class Prob, typename Acc = float>
 inline int launch_igemm_simt(const Prob& pb, cudaStream_t s) {
   if (pb.M == 0 || pb.N == 0 || pb.zcount == 0) return PVB2_OK;
   dim3 grid((unsigned)((pb.N + kSimtBN - 1) / kSimtBN), (unsigned)((pb.M + kSimtBM - 1) / kSimtBM),
             (unsigned)pb.zcount);
   if (grid.y > 65535 || grid.z > 65535) return fail(PVB2_ERR_UNSUPPORTED, "igemm_simt: grid too large");
-  igemm_simt_kernel<Prob><<<grid, kSimtThreads, 0, s>>>(pb);
+  igemm_simt_kernel<Prob, Acc><<<grid, kSimtThreads, 0, s>>>(pb);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }

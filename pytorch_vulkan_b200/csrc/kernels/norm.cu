@@ -38,6 +38,11 @@ static BnGeom bn_geom(const pvb2_tensor* x) {
   int64_t splits = (target + g.C - 1) / g.C;
   if (splits > g.N) splits = g.N;
   if (splits < 1) splits = 1;
+  if (g.N == 0) {
+    g.planes_per = 1;
+    g.splits = 1;
+    return g;
+  }
   g.planes_per = (g.N + splits - 1) / splits;
   g.splits = (int)((g.N + g.planes_per - 1) / g.planes_per);
   return g;

@@ -264,15 +264,37 @@ def test_conv(ocl, name, specs, mk, math):
 
 
 def test_batch_norm_module(ocl):
-    bn = nn.BatchNorm2d(5)
-    check_module([([4, 5, 7, 7], -1)], bn, paramgen=torch.randn)
-    # running statistics were updated on the device like on the CPU
-    ref = nn.BatchNorm2d(5)
+    check_module([([4, 5, 7, 7], -1)], nn.BatchNorm2d(5), paramgen=torch.randn)
+    # running statistics are updated on the device like on the CPU (unbiased var)
+    ref, bn = nn.BatchNorm2d(5), nn.BatchNorm2d(5).to(DEV)
     x = _inputs([([4, 5, 7, 7], -1)], 0)[0]
-    ref(x)
+    for _ in range(3):
+        ref(x)
+        bn(x.to(DEV))
     assert _diff(ref.running_mean, bn.running_mean) < 1e-6
     assert _diff(ref.running_var, bn.running_var) < 1e-6
-    assert bn.num_batches_tracked.item() == 1
+    assert bn.num_batches_tracked.item() == 3
+    bn.eval()
+    ref.eval()
+    assert _diff(ref(x), bn(x.to(DEV))) < 1e-5
+
+
+def test_masked_select_nonzero_print(ocl):
+    g = _gen(11)
+    x = torch.randn(7, 33, generator=g)
+    m = x > 0.3
+    xd, md = x.to(DEV), m.to(DEV)
+    assert torch.equal(torch.masked_select(xd, md).cpu(), torch.masked_select(x, m))
+    assert torch.equal(xd[md].cpu(), x[m])
+    assert torch.equal(torch.nonzero(md).cpu(), torch.nonzero(m))
+    big = torch.randn(100003, generator=g)
+    assert torch.equal(big.to(DEV)[big.to(DEV) > 1].cpu(), big[big > 1])
+    y = xd.clone()
+    y.masked_fill_(md, -1.0)
+    assert torch.equal(y.cpu(), x.masked_fill(m, -1.0))
+    assert "ocl" in repr(xd) and str(round(x[0, 0].item(), 4))[:5] in repr(xd)
+    assert torch.equal(md.all(1).cpu(), m.all(1)) and torch.equal(md.any(0).cpu(), m.any(0))
+    assert torch.equal(torch.isneginf(torch.tensor([1.0, -float("inf")]).to(DEV)).cpu(), torch.tensor([False, True]))
 
 
 def test_layer_norm_affine(ocl):
