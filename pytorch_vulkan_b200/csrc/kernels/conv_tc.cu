@@ -1,27 +1,773 @@
-// Tensor-core (tcgen05) convolution paths.  Until a shape is claimed here
-// the exact SIMT implicit GEMM in conv.cu runs it.
-#include "common.cuh"
+// Tensor-core (tcgen05, TF32) implicit-GEMM convolution for sm_100a.
+//
+// Replaces dlprim's Conv2DForward / Conv2DBackwardData / Conv2DBackwardFilter
+// (src/vision_ops.cpp:61-186) for groups == 1.  Activations arrive NCHW; the
+// launcher first stages them channels-last (NHWC, channels zero-padded to a
+// multiple of 4) in the caller's workspace, because TMA can shift a tile by a
+// filter tap along W and H only when the contiguous dim is C.
+//
+//   forward  Y[pix, k] = sum_{r,s,c} Xnhwc[n, p*sh-ph+r*dh, q*sw-pw+s*dw, c] * Wp[k, r, s, c]
+//            GEMM M = 128 output pixels (a BW x BH x BNI block), N = BN output
+//            channels, K = R*S*ceil(C/32) blocks of 32 channels.  A: one 4-D
+//            TMA box per K block, shifted by the tap, stride via the tensor
+//            map's element strides (K-major).  B: packed weights (K-major).
+//            The epilogue scatters the 128 x BN accumulator to NCHW.
+//   dgrad    any stride, by sub-pixel phases: the dX rows/columns of one
+//            residue class mod the stride receive a fixed subset of taps, so
+//            each phase is a stride-1 correlation over dY (tap offsets in a
+//            table, weights packed per phase) written to dX with strides.
+//   small C  (the 3-channel stem): the S filter columns fold into channels,
+//            Xf[n, h, q, (s, c)] = X[n, c, h, q*sw + s*dw - pw], so a 7x7/2
+//            conv on 3 channels runs as 7x1 on 21 (padded to 24).
+//   wgrad    dW[k, c, r, s] = sum_pix dYnhwc[pix, k] * Xnhwc[shift_rs(pix), c]
+//            GEMM M = 128 output channels, N = BN input channels, K = 32-pixel
+//            blocks (MN-major A and B), one tap per tile, split-K over pixel
+//            blocks into fp32 partials that a second kernel sums in a fixed
+//            order.
+// Kernel structure (warp roles, TMA ring, TMEM double buffer, bounded waits)
+// is the one of the GEMM in gemm_tc.cu.
+#include <mutex>
+#include "tc_common.cuh"
 
 namespace pvb2 {
 
-size_t conv_tc_workspace(const pvb2_conv2d_desc*, int) { return 0; }
+constexpr int cBM = 128, cBK = 32, cStages = 4, cThreads = 192;
 
-int conv_tc_fwd(const pvb2_conv2d_desc*, const float*, const float*, const float*, float*, void*, size_t,
-                cudaStream_t, bool* handled) {
-  *handled = false;
+constexpr int kMaxTaps = 8;
+
+struct ConvTcArgs {
+  int N, Cin, Cp, Kout, P, Q, R, S;   // the conv computed (for dgrad: the equivalent conv over dY)
+  int sh, sw, ph, pw, dh, dw;
+  // input coordinate of output (p, q) under tap (r, s): (p*sh + tap_h[r], q*sw + tap_w[s])
+  int tap_h[kMaxTaps], tap_w[kMaxTaps];
+  // forward-shaped output element (n, k, p, q) lives at
+  // out[obase + n*on + k*ok + p*op + q*oq]
+  int64_t obase, on, ok, op, oq;
+  int cblocks;                        // ceil(Cp / 32)
+  int bw, bh, bni;                    // pixel block (fwd: 128 pixels = M; wgrad: 32 pixels = K block)
+  int tq, tp, tn;                     // pixel blocks along q, p, n
+  int kt;                             // fwd: output-channel tiles ceil(Kout / BN); wgrad: ceil(Kout / 128)
+  int ct;                             // wgrad: input-channel tiles ceil(Cin / BN)
+  int splits, kb_per_split, total_kb; // wgrad split-K over pixel blocks
+  float* out;
+  const float* bias;
+};
+
+template <int BN>
+struct ConvSmem {
+  static constexpr int A_BYTES = cBM * cBK * 4;
+  static constexpr int B_BYTES = BN * cBK * 4;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = cStages * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + (2 * cStages + 4) * 8 + 16;
+};
+
+// WGRAD = false: forward / dgrad.  WGRAD = true: weight gradient partials.
+template <int BN, bool WGRAD>
+__global__ void __launch_bounds__(cThreads, 1)
+    conv_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, ConvTcArgs a) {
+  using L = ConvSmem<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(smem + L::BAR_OFF);
+  uint64_t* empty = full + cStages;
+  uint64_t* acc_full = empty + cStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+  volatile int* abort = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int RS = a.R * a.S;
+  const int pix_tiles = a.tq * a.tp * a.tn;
+  const int total_tiles = WGRAD ? a.kt * a.ct * RS * a.splits : pix_tiles * a.kt;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < cStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // tile -> coordinates
+  auto fwd_tile = [&](int tile, int& kt, int& q0, int& p0, int& n0) {
+    kt = tile % a.kt;
+    const int pix = tile / a.kt;
+    q0 = (pix % a.tq) * a.bw;
+    p0 = ((pix / a.tq) % a.tp) * a.bh;
+    n0 = (pix / (a.tq * a.tp)) * a.bni;
+  };
+  auto wg_tile = [&](int tile, int& sp, int& km, int& ctile, int& rs) {
+    sp = tile % a.splits;
+    int t = tile / a.splits;
+    km = t % a.kt;
+    t /= a.kt;
+    ctile = t % a.ct;
+    rs = t / a.ct;
+  };
+  auto wg_range = [&](int sp, int& kb0, int& kb1) {
+    kb0 = sp * a.kb_per_split;
+    kb1 = min(a.total_kb, kb0 + a.kb_per_split);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch(&tmA);
+      tma_prefetch(&tmB);
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x) {
+        if (!WGRAD) {
+          int kt, q0, p0, n0;
+          fwd_tile(tile, kt, q0, p0, n0);
+          const int kblocks = RS * a.cblocks;
+          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            const int s_ = it % cStages;
+            const uint32_t ph = (it / cStages) & 1;
+            if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
+            const int rs = kb / a.cblocks, cb = kb % a.cblocks;
+            const int r = rs / a.S, s = rs % a.S;
+            uint8_t* sa = smem + s_ * L::STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
+            tma_load_4d(sa, &tmA, &full[s_], cb * 32, q0 * a.sw + a.tap_w[s], p0 * a.sh + a.tap_h[r], n0);
+            tma_load_2d(sa + L::A_BYTES, &tmB, &full[s_], rs * a.Cp + cb * 32, kt * BN);
+          }
+        } else {
+          int sp, km, ctile, rs;
+          wg_tile(tile, sp, km, ctile, rs);
+          const int r = rs / a.S, s = rs % a.S;
+          int kb0, kb1;
+          wg_range(sp, kb0, kb1);
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s_ = it % cStages;
+            const uint32_t ph = (it / cStages) & 1;
+            if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
+            const int q0 = (kb % a.tq) * a.bw, p0 = ((kb / a.tq) % a.tp) * a.bh, n0 = (kb / (a.tq * a.tp)) * a.bni;
+            uint8_t* sa = smem + s_ * L::STAGE_BYTES;
+            uint8_t* sb = sa + L::A_BYTES;
+            mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
+#pragma unroll
+            for (int j = 0; j < cBM / 32; ++j) tma_load_4d(sa + j * 32 * cBK * 4, &tmA, &full[s_], km * cBM + 32 * j, q0, p0, n0);
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_4d(sb + j * 32 * cBK * 4, &tmB, &full[s_], ctile * BN + 32 * j, q0 * a.sw + a.tap_w[s],
+                          p0 * a.sh + a.tap_h[r], n0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(cBM, BN, WGRAD, WGRAD);
+      uint32_t it = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        int kb0 = 0, kb1 = RS * a.cblocks;
+        if (WGRAD) {
+          int sp, km, ctile, rs;
+          wg_tile(tile, sp, km, ctile, rs);
+          wg_range(sp, kb0, kb1);
+        }
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s_ = it % cStages;
+          const uint32_t ph = (it / cStages) & 1;
+          if (!mbar_wait(&full[s_], ph, abort)) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s_ * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < cBK / 8; ++kk) {
+            const uint64_t ad = WGRAD ? desc_mnmajor(sa, kk, 32 * cBK * 4) : desc_kmajor(sa, kk);
+            const uint64_t bd = WGRAD ? desc_mnmajor(sb, kk, 32 * cBK * 4) : desc_kmajor(sb, kk);
+            mma_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[s_]);
+        }
+        mma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // TMEM lane = accumulator row
+    int local = 0;
+    for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[buf], aph, abort)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
+      if (!WGRAD) {
+        int kt, q0, p0, n0;
+        fwd_tile(tile, kt, q0, p0, n0);
+        const int q = q0 + row % a.bw, p = p0 + (row / a.bw) % a.bh, n = n0 + row / (a.bw * a.bh);
+        const bool valid = q < a.Q && p < a.P && n < a.N;
+        float* obase = a.out + a.obase + (int64_t)n * a.on + (int64_t)p * a.op + (int64_t)q * a.oq;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          const int k0 = kt * BN + c * 32;
+          if (valid) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int k = k0 + j;
+              if (k < a.Kout) obase[(int64_t)k * a.ok] = a.bias ? v[j] + a.bias[k] : v[j];
+            }
+          }
+        }
+      } else {
+        int sp, km, ctile, rs;
+        wg_tile(tile, sp, km, ctile, rs);
+        const int k = km * cBM + row;
+        const int64_t crs = (int64_t)a.Cin * RS;
+        float* pbase = a.out + ((int64_t)sp * a.Kout + k) * crs + rs;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          const int c0 = ctile * BN + c * 32;
+          if (k < a.Kout) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (c0 + j < a.Cin) pbase[(int64_t)(c0 + j) * RS] = v[j];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (*abort) {
+      const uint64_t t0 = globaltimer();
+      while (globaltimer() - t0 < 10000000ull) {
+      }
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ------------------------------------------------------ layout kernels
+// x [N, C, HW] -> y [N, HW, Cp], channels C..Cp-1 zero
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int C, int Cp, int64_t HW) {
+  __shared__ float tile[32][33];
+  const int64_t n = blockIdx.z;
+  const int64_t p0 = (int64_t)blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  const float* xn = x + n * C * HW;
+  float* yn = y + n * HW * Cp;
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int c = c0 + j;
+    const int64_t p = p0 + threadIdx.x;
+    tile[j][threadIdx.x] = (c < C && p < HW) ? xn[(int64_t)c * HW + p] : 0.f;
+  }
+  __syncthreads();
+  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+    const int64_t p = p0 + j;
+    const int c = c0 + threadIdx.x;
+    if (p < HW && c < Cp) yn[p * Cp + c] = tile[threadIdx.x][j];
+  }
+}
+
+// forward: W [K][C][R][S] -> Wp [K][R][S][Cp]
+__global__ void pack_w_fwd_kernel(const float* __restrict__ w, float* __restrict__ wp, int K, int C, int Cp, int RS) {
+  const int64_t total = (int64_t)K * RS * Cp;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % Cp);
+    const int rs = (int)((i / Cp) % RS);
+    const int64_t k = i / ((int64_t)Cp * RS);
+    wp[i] = c < C ? w[(k * C + c) * RS + rs] : 0.f;
+  }
+}
+
+__global__ void sum_partials_kernel(const float* __restrict__ part, int splits, int64_t n, float* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < splits; ++k) s += part[(int64_t)k * n + i];
+    out[i] = s;
+  }
+}
+
+// dgrad phase: Wd[c][t][k] = W[k][c][r_t][s_t] over the phase's tap list
+__global__ void pack_w_phase_kernel(const float* __restrict__ w, float* __restrict__ wd, int K, int Kp, int C, int R,
+                                    int S, int nr, int ns, int4 rl, int4 rh, int4 sl, int4 shi) {
+  const int rr[8] = {rl.x, rl.y, rl.z, rl.w, rh.x, rh.y, rh.z, rh.w};
+  const int ss[8] = {sl.x, sl.y, sl.z, sl.w, shi.x, shi.y, shi.z, shi.w};
+  const int64_t total = (int64_t)C * nr * ns * Kp;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int k = (int)(i % Kp);
+    const int t = (int)((i / Kp) % (nr * ns));
+    const int64_t c = i / ((int64_t)Kp * nr * ns);
+    const int r = rr[t / ns], s_ = ss[t % ns];
+    wd[i] = k < K ? w[(((int64_t)k * C + c) * R + r) * S + s_] : 0.f;
+  }
+}
+
+// small-C fold: Xf[n, h, q, s*C + c] = X[n, c, h, q*sw + s*dw - pw] (0 outside / in pad channels)
+__global__ void fold_cols_kernel(const float* __restrict__ x, float* __restrict__ xf, int N, int C, int H, int W,
+                                 int Q, int S, int Cf, int sw, int dw, int pw) {
+  const int64_t total = (int64_t)N * H * Q * Cf;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int cf = (int)(i % Cf);
+    const int q = (int)((i / Cf) % Q);
+    const int h = (int)((i / ((int64_t)Cf * Q)) % H);
+    const int64_t n = i / ((int64_t)Cf * Q * H);
+    float v = 0.f;
+    if (cf < S * C) {
+      const int s_ = cf / C, c = cf % C;
+      const int w = q * sw + s_ * dw - pw;
+      if (w >= 0 && w < W) v = x[((n * C + c) * H + h) * W + w];
+    }
+    xf[i] = v;
+  }
+}
+
+// fold weights: Wf[k][r][s*C + c] = W[k][c][r][s]
+__global__ void pack_w_fold_kernel(const float* __restrict__ w, float* __restrict__ wf, int K, int C, int R, int S,
+                                   int Cf) {
+  const int64_t total = (int64_t)K * R * Cf;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int cf = (int)(i % Cf);
+    const int r = (int)((i / Cf) % R);
+    const int64_t k = i / ((int64_t)Cf * R);
+    float v = 0.f;
+    if (cf < S * C) {
+      const int s_ = cf / C, c = cf % C;
+      v = w[((k * C + c) * R + r) * S + s_];
+    }
+    wf[i] = v;
+  }
+}
+
+// fold wgrad: dW[k][c][r][s] = sum_sp part[sp][k][s*C + c][r]
+__global__ void unfold_wgrad_kernel(const float* __restrict__ part, int splits, int K, int C, int R, int S, int Cf,
+                                    float* __restrict__ dw) {
+  const int64_t total = (int64_t)K * C * R * S;
+  const int64_t per_split = (int64_t)K * Cf * R;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int s_ = (int)(i % S);
+    const int r = (int)((i / S) % R);
+    const int c = (int)((i / ((int64_t)S * R)) % C);
+    const int64_t k = i / ((int64_t)S * R * C);
+    const int64_t src = (k * Cf + (s_ * C + c)) * R + r;
+    float acc = 0.f;
+    for (int sp = 0; sp < splits; ++sp) acc += part[sp * per_split + src];
+    dw[i] = acc;
+  }
+}
+
+// ------------------------------------------------------------ host side
+static int round4(int c) { return (c + 3) / 4 * 4; }
+static int pow2_at_least(int v, int lo, int hi) {
+  int p = lo;
+  while (p < v && p < hi) p <<= 1;
+  return p;
+}
+static size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+static int bn_for(int n) { return n <= 64 ? 64 : (n <= 128 ? 128 : 256); }
+
+// pixel block of `pixels` (128 or 32) covering a P x Q grid
+static void pixel_block(int P, int Q, int pixels, int& bw, int& bh, int& bni) {
+  bw = pow2_at_least(Q, 8, pixels >= 64 ? 64 : pixels);
+  if (bw > pixels) bw = pixels;
+  bh = pow2_at_least(P, 1, pixels / bw);
+  if (bh > pixels / bw) bh = pixels / bw;
+  bni = pixels / (bw * bh);
+}
+
+static bool tc_conv_enabled() { return getenv("PVB2_DISABLE_TC") == nullptr; }
+
+static bool tc_conv_shape_ok(const pvb2_conv2d_desc* d) {
+  if (d->groups != 1 || d->math != PVB2_MATH_TF32 || !tc_conv_enabled()) return false;
+  const double macs = (double)d->N * d->P * d->Q * d->K * d->C * d->R * d->S;
+  if (macs < (double)(1 << 19)) return false;
+  if (d->stride_w > 4 || d->stride_h > 4) return false;  // TMA boxes: bw*stride <= 256
+  if (d->R > kMaxTaps || d->S > kMaxTaps) return false;
+  if (d->K < 8) return false;
+  return true;
+}
+
+// fold the S filter columns into channels when the input has few channels
+static bool use_fold(const pvb2_conv2d_desc* d) { return d->C <= 8 && d->S * d->C <= 32; }
+static int fold_channels(const pvb2_conv2d_desc* d) { return round4(d->S * d->C); }
+
+struct Taps {
+  int nr, ns;
+  int h[kMaxTaps], w[kMaxTaps];
+};
+
+template <int BN, bool WG>
+static int launch_conv(const CUtensorMap& ma, const CUtensorMap& mb, const ConvTcArgs& a, int tiles, cudaStream_t s) {
+  constexpr int smem = ConvSmem<BN>::TOTAL + 1024;
+  static bool attr = false;
+  if (!attr) {
+    PVB2_CUDA_TRY(cudaFuncSetAttribute(conv_tf32_kernel<BN, WG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr = true;
+  }
+  const int grid = std::min(tiles, num_sms());
+  conv_tf32_kernel<BN, WG><<<grid, cThreads, smem, s>>>(ma, mb, a);
+  PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
 
-int conv_tc_bwd_data(const pvb2_conv2d_desc*, const float*, const float*, float*, void*, size_t, cudaStream_t,
-                     bool* handled) {
-  *handled = false;
+template <bool WG>
+static int launch_bn(int BN, const CUtensorMap& ma, const CUtensorMap& mb, const ConvTcArgs& a, int tiles,
+                     cudaStream_t s) {
+  if (BN == 64) return launch_conv<64, WG>(ma, mb, a, tiles, s);
+  if (BN == 128) return launch_conv<128, WG>(ma, mb, a, tiles, s);
+  return launch_conv<256, WG>(ma, mb, a, tiles, s);
+}
+
+// channels-last activations [N, H, W, Cp] as a 4-D map (Cp, W, H, N)
+static int act_map(CUtensorMap* m, const float* base, int N, int H, int W, int Cp, int bw, int bh, int bni, int sw,
+                   int sh, bool mn_major) {
+  uint64_t dims[4] = {(uint64_t)Cp, (uint64_t)W, (uint64_t)H, (uint64_t)N};
+  uint64_t str[3] = {(uint64_t)Cp * 4, (uint64_t)W * Cp * 4, (uint64_t)H * W * Cp * 4};
+  uint32_t box[4] = {32, (uint32_t)(bw * sw), (uint32_t)(bh * sh), (uint32_t)bni};
+  uint32_t es[4] = {1, (uint32_t)sw, (uint32_t)sh, 1};
+  return encode_tiled(m, 4, base, dims, str, box, mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, es);
+}
+
+static int to_nhwc(const float* x, float* y, int N, int C, int Cp, int64_t HW, cudaStream_t s) {
+  dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((Cp + 31) / 32), (unsigned)N);
+  nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, y, C, Cp, HW);
+  PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
 
-int conv_tc_bwd_filter(const pvb2_conv2d_desc*, const float*, const float*, float*, void*, size_t, cudaStream_t,
-                       bool* handled) {
+// Forward-shaped implicit GEMM.  act: channels-last [N, H, W, Cp]; wpacked:
+// [K][taps][Cp]; output grid P x Q with strides (sh, sw) and tap offsets;
+// out element (n, k, p, q) at out[obase + n*on + k*ok + p*op + q*oq].
+static int run_fwd_like(const float* act, const float* wpacked, const float* bias, float* out, int N, int Cp, int H,
+                        int W, int K, const Taps& t, int P, int Q, int sh, int sw, int64_t obase, int64_t on,
+                        int64_t ok, int64_t op, int64_t oq, cudaStream_t s) {
+  if (P <= 0 || Q <= 0 || N <= 0) return PVB2_OK;
+  int bw, bh, bni;
+  pixel_block(P, Q, cBM, bw, bh, bni);
+  const int BN = bn_for(K);
+  CUtensorMap ma, mb;
+  PVB2_TRY(act_map(&ma, act, N, H, W, Cp, bw, bh, bni, sw, sh, false));
+  const int taps = t.nr * t.ns;
+  uint64_t wd[2] = {(uint64_t)taps * Cp, (uint64_t)K};
+  uint64_t wst[1] = {(uint64_t)taps * Cp * 4};
+  uint32_t wbox[2] = {32, (uint32_t)BN};
+  PVB2_TRY(encode_tiled(&mb, 2, wpacked, wd, wst, wbox, CU_TENSOR_MAP_SWIZZLE_128B));
+  ConvTcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.N = N; a.Cin = Cp; a.Cp = Cp; a.Kout = K; a.P = P; a.Q = Q; a.R = t.nr; a.S = t.ns;
+  a.sh = sh; a.sw = sw;
+  for (int i = 0; i < kMaxTaps; ++i) {
+    a.tap_h[i] = t.h[i];
+    a.tap_w[i] = t.w[i];
+  }
+  a.obase = obase; a.on = on; a.ok = ok; a.op = op; a.oq = oq;
+  a.cblocks = (Cp + 31) / 32;
+  a.bw = bw; a.bh = bh; a.bni = bni;
+  a.tq = (Q + bw - 1) / bw;
+  a.tp = (P + bh - 1) / bh;
+  a.tn = (N + bni - 1) / bni;
+  a.kt = (K + BN - 1) / BN;
+  a.out = out;
+  a.bias = bias;
+  const int tiles = a.tq * a.tp * a.tn * a.kt;
+  return launch_bn<false>(BN, ma, mb, a, tiles, s);
+}
+
+// Weight-gradient implicit GEMM into partials [splits][K][Cin][taps].
+// dy: channels-last [N, P, Q, Kp]; x: channels-last [N, H, W, Cp] (Cin <= Cp real channels)
+struct WgPlan {
+  int bw, bh, bni, BN, splits, kb_per, total_kb, ct, kt;
+};
+
+static WgPlan plan_wg(int N, int K, int Cin, int P, int Q, int taps) {
+  WgPlan w;
+  pixel_block(P, Q, cBK, w.bw, w.bh, w.bni);
+  w.BN = bn_for(Cin);
+  w.ct = (Cin + w.BN - 1) / w.BN;
+  w.kt = (K + cBM - 1) / cBM;
+  const int tq = (Q + w.bw - 1) / w.bw, tp = (P + w.bh - 1) / w.bh, tn = (N + w.bni - 1) / w.bni;
+  w.total_kb = tq * tp * tn;
+  const int base_tiles = w.kt * w.ct * taps;
+  int splits = (2 * num_sms() + base_tiles - 1) / base_tiles;
+  splits = std::min(splits, std::max(1, w.total_kb / 8));
+  splits = std::max(1, std::min(splits, 64));
+  w.kb_per = (w.total_kb + splits - 1) / splits;
+  w.splits = (w.total_kb + w.kb_per - 1) / w.kb_per;
+  return w;
+}
+
+static int run_wgrad(const float* dyn, int Kp, const float* xn, int Cp, int N, int H, int W, int P, int Q, int K,
+                     int Cin, const Taps& t, int sh, int sw, const WgPlan& p, float* part, cudaStream_t s) {
+  CUtensorMap ma, mb;
+  PVB2_TRY(act_map(&ma, dyn, N, P, Q, Kp, p.bw, p.bh, p.bni, 1, 1, true));
+  PVB2_TRY(act_map(&mb, xn, N, H, W, Cp, p.bw, p.bh, p.bni, sw, sh, true));
+  ConvTcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.N = N; a.Cin = Cin; a.Cp = Cp; a.Kout = K; a.P = P; a.Q = Q; a.R = t.nr; a.S = t.ns;
+  a.sh = sh; a.sw = sw;
+  for (int i = 0; i < kMaxTaps; ++i) {
+    a.tap_h[i] = t.h[i];
+    a.tap_w[i] = t.w[i];
+  }
+  a.bw = p.bw; a.bh = p.bh; a.bni = p.bni;
+  a.tq = (Q + p.bw - 1) / p.bw;
+  a.tp = (P + p.bh - 1) / p.bh;
+  a.tn = (N + p.bni - 1) / p.bni;
+  a.kt = p.kt;
+  a.ct = p.ct;
+  a.splits = p.splits;
+  a.kb_per_split = p.kb_per;
+  a.total_kb = p.total_kb;
+  a.out = part;
+  const int tiles = a.kt * a.ct * t.nr * t.ns * a.splits;
+  return launch_bn<true>(p.BN, ma, mb, a, tiles, s);
+}
+
+static Taps fwd_taps(const pvb2_conv2d_desc* d) {
+  Taps t;
+  t.nr = d->R;
+  t.ns = d->S;
+  for (int i = 0; i < kMaxTaps; ++i) {
+    t.h[i] = i * d->dil_h - d->pad_h;
+    t.w[i] = i * d->dil_w - d->pad_w;
+  }
+  return t;
+}
+
+static Taps fold_taps(const pvb2_conv2d_desc* d) {
+  Taps t = fwd_taps(d);
+  t.ns = 1;
+  for (int i = 0; i < kMaxTaps; ++i) t.w[i] = 0;
+  return t;
+}
+
+// -------------------------------------------------------- workspace plans
+struct Layout {
+  size_t a, b, c, total;
+};
+
+static Layout fwd_layout(const pvb2_conv2d_desc* d) {
+  Layout l;
+  if (use_fold(d)) {
+    const int Cf = fold_channels(d);
+    l.a = 0;
+    l.b = align256((size_t)d->N * d->H * d->Q * Cf * 4);
+    l.total = l.b + align256((size_t)d->K * d->R * Cf * 4);
+  } else {
+    const int Cp = round4(d->C);
+    l.a = 0;
+    l.b = align256((size_t)d->N * d->H * d->W * Cp * 4);
+    l.total = l.b + align256((size_t)d->K * d->R * d->S * Cp * 4);
+  }
+  l.c = l.total;
+  return l;
+}
+
+static Layout dgrad_layout(const pvb2_conv2d_desc* d) {
+  Layout l;
+  const int Kp = round4(d->K);
+  l.a = 0;
+  l.b = align256((size_t)d->N * d->P * d->Q * Kp * 4);
+  l.total = l.b + align256((size_t)d->C * d->R * d->S * Kp * 4);  // one phase's packed weights at a time
+  l.c = l.total;
+  return l;
+}
+
+static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
+  Layout l;
+  const int Kp = round4(d->K);
+  const bool fold = use_fold(d);
+  const int Cx = fold ? fold_channels(d) : round4(d->C);
+  const int Wx = fold ? d->Q : d->W;
+  const int taps = fold ? d->R : d->R * d->S;
+  WgPlan p = plan_wg(d->N, d->K, fold ? Cx : d->C, d->P, d->Q, taps);
+  if (plan) *plan = p;
+  l.a = 0;                                                                   // x channels-last (or folded)
+  l.b = align256((size_t)d->N * d->H * Wx * Cx * 4);                         // dy channels-last
+  l.c = l.b + align256((size_t)d->N * d->P * d->Q * Kp * 4);                 // partials
+  l.total = l.c + align256((size_t)p.splits * d->K * (fold ? Cx : d->C) * taps * 4);
+  return l;
+}
+
+size_t conv_tc_workspace(const pvb2_conv2d_desc* d, int which) {
+  if (!tc_conv_shape_ok(d)) return 0;
+  if (which == 0) return fwd_layout(d).total;
+  if (which == 1) return dgrad_layout(d).total;
+  return wgrad_layout(d, nullptr).total;
+}
+
+int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const float* b, float* y, void* ws,
+                size_t ws_bytes, cudaStream_t s, bool* handled) {
   *handled = false;
+  if (!tc_conv_shape_ok(d)) return PVB2_OK;
+  Layout l = fwd_layout(d);
+  if (!ws || ws_bytes < l.total) return PVB2_OK;  // not enough scratch: exact path
+  float* act = (float*)((char*)ws + l.a);
+  float* wp = (float*)((char*)ws + l.b);
+  const int64_t pq = (int64_t)d->P * d->Q;
+  if (use_fold(d)) {
+    const int Cf = fold_channels(d);
+    const int64_t n1 = (int64_t)d->N * d->H * d->Q * Cf;
+    fold_cols_kernel<<<grid_for(n1, 256), 256, 0, s>>>(x, act, d->N, d->C, d->H, d->W, d->Q, d->S, Cf, d->stride_w,
+                                                        d->dil_w, d->pad_w);
+    PVB2_LAUNCH_CHECK();
+    const int64_t n2 = (int64_t)d->K * d->R * Cf;
+    pack_w_fold_kernel<<<grid_for(n2, 256), 256, 0, s>>>(w, wp, d->K, d->C, d->R, d->S, Cf);
+    PVB2_LAUNCH_CHECK();
+    PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, Cf, d->H, d->Q, d->K, fold_taps(d), d->P, d->Q, d->stride_h, 1, 0,
+                          (int64_t)d->K * pq, pq, d->Q, 1, s));
+  } else {
+    const int Cp = round4(d->C);
+    PVB2_TRY(to_nhwc(x, act, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
+    const int64_t wn = (int64_t)d->K * d->R * d->S * Cp;
+    pack_w_fwd_kernel<<<grid_for(wn, 256), 256, 0, s>>>(w, wp, d->K, d->C, Cp, d->R * d->S);
+    PVB2_LAUNCH_CHECK();
+    PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, Cp, d->H, d->W, d->K, fwd_taps(d), d->P, d->Q, d->stride_h,
+                          d->stride_w, 0, (int64_t)d->K * pq, pq, d->Q, 1, s));
+  }
+  *handled = true;
+  return PVB2_OK;
+}
+
+static int pos_mod(int a, int m) { return ((a % m) + m) % m; }
+
+// dX by sub-pixel phases: output rows h = sh*i + ph_a receive only the taps r
+// with (ph_a + pad_h - r*dil_h) divisible by sh, each reading dY row
+// i + (ph_a + pad_h - r*dil_h)/sh; likewise for columns.  Each phase is a
+// stride-1 correlation over dY with its own tap list, written to dX with
+// strides (sh, sw).  Phases without taps are zero.
+int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, void* ws, size_t ws_bytes,
+                     cudaStream_t s, bool* handled) {
+  *handled = false;
+  if (!tc_conv_shape_ok(d)) return PVB2_OK;
+  Layout l = dgrad_layout(d);
+  if (!ws || ws_bytes < l.total) return PVB2_OK;
+  const int Kp = round4(d->K);
+  float* dyn = (float*)((char*)ws + l.a);
+  float* wd = (float*)((char*)ws + l.b);
+  bool empty_phase = false;
+  Taps ph[16];
+  int nph = 0;
+  int pa[16], pb[16];
+  for (int a = 0; a < d->stride_h; ++a)
+    for (int b = 0; b < d->stride_w; ++b) {
+      Taps t;
+      t.nr = t.ns = 0;
+      for (int r = 0; r < d->R; ++r) {
+        const int v = a + d->pad_h - r * d->dil_h;
+        if (pos_mod(v, d->stride_h) == 0) {
+          t.h[t.nr] = r;  // store r; offsets below
+          ++t.nr;
+        }
+      }
+      for (int s_ = 0; s_ < d->S; ++s_) {
+        const int v = b + d->pad_w - s_ * d->dil_w;
+        if (pos_mod(v, d->stride_w) == 0) {
+          t.w[t.ns] = s_;
+          ++t.ns;
+        }
+      }
+      const int Hph = (d->H - a + d->stride_h - 1) / d->stride_h, Wph = (d->W - b + d->stride_w - 1) / d->stride_w;
+      if (Hph <= 0 || Wph <= 0) continue;
+      if (t.nr == 0 || t.ns == 0) {
+        empty_phase = true;
+        continue;
+      }
+      pa[nph] = a;
+      pb[nph] = b;
+      ph[nph++] = t;
+    }
+  if (empty_phase) PVB2_CUDA_TRY(cudaMemsetAsync(dx, 0, (size_t)d->N * d->C * d->H * d->W * sizeof(float), s));
+  PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
+  const int64_t hw = (int64_t)d->H * d->W;
+  for (int i = 0; i < nph; ++i) {
+    const int a = pa[i], b = pb[i];
+    Taps t = ph[i];
+    int rl[8] = {0}, sl[8] = {0};
+    for (int j = 0; j < t.nr; ++j) rl[j] = t.h[j];
+    for (int j = 0; j < t.ns; ++j) sl[j] = t.w[j];
+    const int64_t wn = (int64_t)d->C * t.nr * t.ns * Kp;
+    pack_w_phase_kernel<<<grid_for(wn, 256), 256, 0, s>>>(w, wd, d->K, Kp, d->C, d->R, d->S, t.nr, t.ns,
+                                                          make_int4(rl[0], rl[1], rl[2], rl[3]),
+                                                          make_int4(rl[4], rl[5], rl[6], rl[7]),
+                                                          make_int4(sl[0], sl[1], sl[2], sl[3]),
+                                                          make_int4(sl[4], sl[5], sl[6], sl[7]));
+    PVB2_LAUNCH_CHECK();
+    Taps off;
+    off.nr = t.nr;
+    off.ns = t.ns;
+    for (int j = 0; j < kMaxTaps; ++j) off.h[j] = off.w[j] = 0;
+    for (int j = 0; j < t.nr; ++j) off.h[j] = (a + d->pad_h - t.h[j] * d->dil_h) / d->stride_h;
+    for (int j = 0; j < t.ns; ++j) off.w[j] = (b + d->pad_w - t.w[j] * d->dil_w) / d->stride_w;
+    const int Hph = (d->H - a + d->stride_h - 1) / d->stride_h, Wph = (d->W - b + d->stride_w - 1) / d->stride_w;
+    PVB2_TRY(run_fwd_like(dyn, wd, nullptr, dx, d->N, Kp, d->P, d->Q, d->C, off, Hph, Wph, 1, 1,
+                          (int64_t)a * d->W + b, (int64_t)d->C * hw, hw, (int64_t)d->stride_h * d->W, d->stride_w, s));
+  }
+  *handled = true;
+  return PVB2_OK;
+}
+
+int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* dy, float* dw, void* ws,
+                       size_t ws_bytes, cudaStream_t s, bool* handled) {
+  *handled = false;
+  if (!tc_conv_shape_ok(d)) return PVB2_OK;
+  WgPlan p;
+  Layout l = wgrad_layout(d, &p);
+  if (!ws || ws_bytes < l.total) return PVB2_OK;
+  const int Kp = round4(d->K);
+  float* xn = (float*)((char*)ws + l.a);
+  float* dyn = (float*)((char*)ws + l.b);
+  float* part = (float*)((char*)ws + l.c);
+  PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
+  if (use_fold(d)) {
+    const int Cf = fold_channels(d);
+    const int64_t n1 = (int64_t)d->N * d->H * d->Q * Cf;
+    fold_cols_kernel<<<grid_for(n1, 256), 256, 0, s>>>(x, xn, d->N, d->C, d->H, d->W, d->Q, d->S, Cf, d->stride_w,
+                                                        d->dil_w, d->pad_w);
+    PVB2_LAUNCH_CHECK();
+    PVB2_TRY(run_wgrad(dyn, Kp, xn, Cf, d->N, d->H, d->Q, d->P, d->Q, d->K, Cf, fold_taps(d), d->stride_h, 1, p, part,
+                       s));
+    const int64_t wn = (int64_t)d->K * d->C * d->R * d->S;
+    unfold_wgrad_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, d->K, d->C, d->R, d->S, Cf, dw);
+    PVB2_LAUNCH_CHECK();
+  } else {
+    const int Cp = round4(d->C);
+    PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
+    PVB2_TRY(run_wgrad(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h,
+                       d->stride_w, p, part, s));
+    const int64_t wn = (int64_t)d->K * d->C * d->R * d->S;
+    sum_partials_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, wn, dw);
+    PVB2_LAUNCH_CHECK();
+  }
+  *handled = true;
   return PVB2_OK;
 }
 
 }  // namespace pvb2
+
+extern "C" PVB2_API int pvb2_conv_tc_status(int* timed_out, int reset) {
+  return pvb2::tc_timeout_flag_local(timed_out, reset);
+}

@@ -213,10 +213,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 int encode_tiled(CUtensorMap* map, int rank, const void* base, const uint64_t* dims, const uint64_t* strides_bytes,
-                 const uint32_t* box, CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2) {
+                 const uint32_t* box, CUtensorMapSwizzle swizzle, CUtensorMapL2promotion l2,
+                 const uint32_t* elem_strides) {
   auto fn = get_encode();
   if (!fn) return fail(PVB2_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  if (elem_strides)
+    for (int i = 0; i < rank; ++i) estr[i] = elem_strides[i];
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(PVB2_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);

@@ -82,6 +82,14 @@ __device__ __forceinline__ void tma_prefetch(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
@@ -181,7 +189,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 // CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B for 32-bit MN-major tiles
 int encode_tiled(CUtensorMap* map, int rank, const void* base, const uint64_t* dims, const uint64_t* strides_bytes,
                  const uint32_t* box, CUtensorMapSwizzle swizzle,
-                 CUtensorMapL2promotion l2 = CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+                 CUtensorMapL2promotion l2 = CU_TENSOR_MAP_L2_PROMOTION_L2_256B, const uint32_t* elem_strides = nullptr);
 
 static inline int tc_timeout_flag_local(int* value, int reset) {
   cudaError_t e = cudaMemcpyFromSymbol(value, g_tc_timeout, sizeof(int));
