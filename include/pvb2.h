@@ -227,6 +227,25 @@ PVB2_API int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma,
                               float* running_mean, float* running_var, double momentum, double eps,
                               const pvb2_tensor* y, float* save_mean, float* save_invstd,
                               void* workspace, size_t workspace_bytes, pvb2_stream stream);
+/* Batch-norm training forward that allocates nothing and takes no workspace.
+ * No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory at the point of the call -- code running while a
+ * CUDA stream is being captured into a graph (cudaMalloc is not allowed
+ * there), or hosts whose memory is fully owned by another allocator and that
+ * hand out only their tensors' pointers.  Results equal
+ * pvb2_batch_norm_fwd_train's.  Its scratch (per-CTA partial sums) is a
+ * fixed 1 MiB array inside this library, resident on every GPU that loads
+ * it until the process exits; inputs needing more than
+ * PVB2_BN_NOALLOC_SCRATCH_BYTES of partials (about 130k channels and up)
+ * are rejected with PVB2_ERR_INVALID.  The first call on each device looks
+ * up that device's copy of the array (make it before any stream capture).
+ * All calls share the one array: calls that may overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller. */
+#define PVB2_BN_NOALLOC_SCRATCH_BYTES (1u << 20)
+PVB2_API int pvb2_batch_norm_fwd_train_noalloc(const pvb2_tensor* x, const float* gamma, const float* beta,
+                              float* running_mean, float* running_var, double momentum, double eps,
+                              const pvb2_tensor* y, float* save_mean, float* save_invstd,
+                              pvb2_stream stream);
 /* native_batch_norm (eval): uses running stats */
 PVB2_API int pvb2_batch_norm_fwd_eval(const pvb2_tensor* x, const float* gamma, const float* beta,
                              const float* running_mean, const float* running_var, double eps,

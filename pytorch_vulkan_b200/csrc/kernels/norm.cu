@@ -16,6 +16,7 @@
 //               save_invstd and updates the running statistics.
 // The backward pass has the same shape: a reduction of (sum dy,
 // sum dy*(x-mean)) per channel, then an apply pass for dx.
+#include <mutex>
 #include "common.cuh"
 
 namespace pvb2 {
@@ -433,6 +434,32 @@ static int check_bn_x(const pvb2_tensor* x) {
   return PVB2_OK;
 }
 
+// Fixed scratch of the allocation-free batch-norm forward: a file-scope
+// device array (every GPU that loads the library holds its own copy until the
+// process exits).  In host code the symbol is only a host-side handle, never
+// a device address; the device address comes from cudaGetSymbolAddress,
+// looked up once per device with that device current.
+static __device__ __align__(256) float g_bn_scratch[PVB2_BN_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+static int bn_scratch_address(float** out) {
+  static std::mutex m;
+  static float* addr[64] = {nullptr};
+  int dev = 0;
+  PVB2_CUDA_TRY(cudaGetDevice(&dev));
+  PVB2_CHECK_ARG(dev >= 0 && dev < 64, "batch_norm_noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> g(m);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_bn_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(PVB2_ERR_CUDA, "batch_norm_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    addr[dev] = (float*)p;
+  }
+  *out = addr[dev];
+  return PVB2_OK;
+}
+
 }  // namespace pvb2
 
 using namespace pvb2;
@@ -457,6 +484,41 @@ int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma, const fl
                  workspace_bytes, need);
   cudaStream_t s = as_stream(stream);
   float* part = (float*)workspace;
+  bn_stats_kernel<<<dim3((unsigned)g.C, (unsigned)g.splits), kBnThreads, 0, s>>>(
+      (const float*)x->data, g.N, g.C, g.HW, g.planes_per, g.splits, part);
+  PVB2_LAUNCH_CHECK();
+  int threads = g.HW >= 1024 ? 256 : (g.HW >= 256 ? 128 : 64);
+  bn_apply_kernel<<<(unsigned)(g.N * g.C), threads, 0, s>>>((const float*)x->data, (float*)y->data, g.N, g.C, g.HW,
+                                                            g.splits, part, gamma, beta, running_mean, running_var,
+                                                            (float)momentum, (float)eps, save_mean, save_invstd);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+// Allocation-free variant of pvb2_batch_norm_fwd_train for callers that
+// cannot allocate device memory when they call (inside stream capture, or
+// when every device byte belongs to another allocator).  The per-CTA partial
+// sums live in g_bn_scratch below instead of a caller workspace.  Every
+// partial slot the apply kernel reads is written by the stats kernel of the
+// same call, so nothing in the array has to be cleared between calls; it
+// simply keeps the last call's partials.  Calls that overlap on the GPU
+// share the array and race.
+int pvb2_batch_norm_fwd_train_noalloc(const pvb2_tensor* x, const float* gamma, const float* beta,
+                                      float* running_mean, float* running_var, double momentum, double eps,
+                                      const pvb2_tensor* y, float* save_mean, float* save_invstd,
+                                      pvb2_stream stream) {
+  PVB2_TRY(check_bn_x(x));
+  PVB2_CHECK_ARG(is_contiguous(y) && y->dtype == PVB2_F32, "batch_norm: output must be contiguous float32");
+  BnGeom g = bn_geom(x);
+  if (g.N * g.HW == 0 || g.C == 0) return PVB2_OK;
+  const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
+  PVB2_CHECK_ARG(need <= sizeof(g_bn_scratch),
+                 "batch_norm_noalloc: %lld channels need %zu bytes of partials, more than the %zu-byte scratch; "
+                 "use pvb2_batch_norm_fwd_train with a workspace",
+                 (long long)g.C, need, sizeof(g_bn_scratch));
+  float* part = nullptr;
+  PVB2_TRY(bn_scratch_address(&part));
+  cudaStream_t s = as_stream(stream);
   bn_stats_kernel<<<dim3((unsigned)g.C, (unsigned)g.splits), kBnThreads, 0, s>>>(
       (const float*)x->data, g.N, g.C, g.HW, g.planes_per, g.splits, part);
   PVB2_LAUNCH_CHECK();

@@ -1,0 +1,107 @@
+"""The allocation-free batch-norm forward, pvb2_batch_norm_fwd_train_noalloc.
+
+It serves callers that cannot allocate device memory when they call it:
+code running while a CUDA stream is captured into a graph, or a host whose
+device memory all belongs to another allocator.  Its partial sums live in a
+fixed 1 MiB array inside libpvb2 instead of a caller-provided workspace.
+
+Checked through the C-ABI against pvb2_batch_norm_fwd_train (the entry point
+that takes a workspace) on the same inputs, for two calls in a row with
+different shapes (the second call reuses the array the first one left
+behind), plus the size limit.  This file is named so that pytest collects it
+last; it also passes when run on its own in a fresh process.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(REPO, "pytorch_vulkan_b200", "lib", "libpvb2.so")
+DEV = "ocl:0"
+SCRATCH_BYTES = 1 << 20
+
+
+class T(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("sizes", ctypes.c_int64 * 8), ("strides", ctypes.c_int64 * 8),
+                ("ndim", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+
+def td(t):
+    return T(t.data_ptr() if t.numel() else None, (ctypes.c_int64 * 8)(*t.shape), (ctypes.c_int64 * 8)(*t.stride()),
+             t.dim(), 0)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import pytorch_vulkan_b200  # noqa: F401  (registers the ocl device)
+
+    if not torch.ocl.is_available():
+        pytest.fail("no ocl (CUDA) device visible")
+    L = ctypes.CDLL(LIB)
+    L.pvb2_last_error.restype = ctypes.c_char_p
+    L.pvb2_batch_norm_workspace_size.restype = ctypes.c_size_t
+    return L
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    import pytorch_vulkan_b200 as p
+
+    return ctypes.c_void_p(p._C.impl_stream_handle(0))
+
+
+def _run(lib, x, gamma, beta, noalloc):
+    C = x.shape[1]
+    y = torch.empty(x.shape).to(DEV)
+    rm, rv = torch.zeros(C).to(DEV), torch.ones(C).to(DEV)
+    mean, invstd = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    torch.ocl.synchronize()
+    if noalloc:
+        st = lib.pvb2_batch_norm_fwd_train_noalloc(ctypes.byref(td(x)), _ptr(gamma), _ptr(beta), _ptr(rm), _ptr(rv),
+                                                   ctypes.c_double(0.1), ctypes.c_double(1e-5), ctypes.byref(td(y)),
+                                                   _ptr(mean), _ptr(invstd), _stream())
+    else:
+        n = lib.pvb2_batch_norm_workspace_size(ctypes.byref(td(x)))
+        ws = torch.empty(max(n, 4), dtype=torch.uint8).to(DEV)
+        torch.ocl.synchronize()
+        st = lib.pvb2_batch_norm_fwd_train(ctypes.byref(td(x)), _ptr(gamma), _ptr(beta), _ptr(rm), _ptr(rv),
+                                           ctypes.c_double(0.1), ctypes.c_double(1e-5), ctypes.byref(td(y)),
+                                           _ptr(mean), _ptr(invstd), _ptr(ws), ctypes.c_size_t(ws.numel()), _stream())
+    assert st == 0, lib.pvb2_last_error().decode()
+    torch.ocl.synchronize()
+    return [t.cpu() for t in (y, mean, invstd, rm, rv)]
+
+
+def test_noalloc_matches_workspace_entry_point_twice(lib):
+    rng = np.random.default_rng(0)
+    # two calls in a row with different shapes: the second reads only partials it wrote itself
+    for shape in [(64, 256, 14, 14), (8, 37, 9, 11)]:
+        x = torch.from_numpy((rng.standard_normal(shape) * 2 + 0.5).astype(np.float32)).to(DEV)
+        C = shape[1]
+        gamma = torch.from_numpy(rng.standard_normal(C).astype(np.float32)).to(DEV)
+        beta = torch.from_numpy(rng.standard_normal(C).astype(np.float32)).to(DEV)
+        ref = _run(lib, x, gamma, beta, noalloc=False)
+        got = _run(lib, x, gamma, beta, noalloc=True)
+        for name, a, b in zip(["y", "mean", "invstd", "running_mean", "running_var"], ref, got):
+            # the two entry points run the same kernels in the same order: identical results
+            assert torch.allclose(a, b, rtol=1e-6, atol=1e-6), name
+
+
+def test_noalloc_rejects_inputs_beyond_scratch(lib):
+    # C * splits * 2 floats of partials must fit the 1 MiB array: 1 x 140000 x 1 x 1 needs 1.12 MB
+    C = 140000
+    x = torch.zeros((1, C, 1, 1)).to(DEV)
+    y = torch.empty((1, C, 1, 1)).to(DEV)
+    mean, invstd = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    st = lib.pvb2_batch_norm_fwd_train_noalloc(ctypes.byref(td(x)), None, None, None, None, ctypes.c_double(0.1),
+                                               ctypes.c_double(1e-5), ctypes.byref(td(y)), _ptr(mean), _ptr(invstd),
+                                               _stream())
+    assert st == 1
+    assert b"scratch" in lib.pvb2_last_error()
