@@ -330,6 +330,14 @@ PVB2_API int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_te
               const float* bias, int bias_dim, double alpha, double beta, int math,
               pvb2_stream stream);
 
+/* Tensor-core watchdogs (no counterpart in the reference, whose OpenCL   */
+/* kernels had no internal waits).  Every mbarrier wait in the tcgen05    */
+/* GEMM / convolution kernels gives up after about 2 s and sets a device  */
+/* flag instead of spinning forever; these read it (synchronising the    */
+/* current device) into *timed_out, and clear it when reset != 0.         */
+PVB2_API int pvb2_tc_status(int* timed_out, int reset);
+PVB2_API int pvb2_conv_tc_status(int* timed_out, int reset);
+
 /* ------------------------------------------------------------------ */
 /* convolution (src/vision_ops.cpp:30-186)                              */
 /* ------------------------------------------------------------------ */
