@@ -1,29 +1,46 @@
 // Tensor-core (tcgen05, TF32) implicit-GEMM convolution for sm_100a.
 //
 // Replaces dlprim's Conv2DForward / Conv2DBackwardData / Conv2DBackwardFilter
-// (src/vision_ops.cpp:61-186) for groups == 1.  Activations arrive NCHW; the
-// launcher first stages them channels-last (NHWC, channels zero-padded to a
-// multiple of 4) in the caller's workspace, because TMA can shift a tile by a
-// filter tap along W and H only when the contiguous dim is C.
+// (src/vision_ops.cpp:61-186) for groups == 1.  Activations arrive NCHW.
 //
-//   forward  Y[pix, k] = sum_{r,s,c} Xnhwc[n, p*sh-ph+r*dh, q*sw-pw+s*dw, c] * Wp[k, r, s, c]
-//            GEMM M = 128 output pixels (a BW x BH x BNI block), N = BN output
-//            channels, K = R*S*ceil(C/32) blocks of 32 channels.  A: one 4-D
-//            TMA box per K block, shifted by the tap, stride via the tensor
-//            map's element strides (K-major).  B: packed weights (K-major).
-//            The epilogue scatters the 128 x BN accumulator to NCHW.
-//   dgrad    any stride, by sub-pixel phases: the dX rows/columns of one
-//            residue class mod the stride receive a fixed subset of taps, so
-//            each phase is a stride-1 correlation over dY (tap offsets in a
-//            table, weights packed per phase) written to dX with strides.
-//   small C  (the 3-channel stem): the S filter columns fold into channels,
-//            Xf[n, h, q, (s, c)] = X[n, c, h, q*sw + s*dw - pw], so a 7x7/2
-//            conv on 3 channels runs as 7x1 on 21 (padded to 24).
-//   wgrad    dW[k, c, r, s] = sum_pix dYnhwc[pix, k] * Xnhwc[shift_rs(pix), c]
-//            GEMM M = 128 output channels, N = BN input channels, K = 32-pixel
-//            blocks (MN-major A and B), one tap per tile, split-K over pixel
-//            blocks into fp32 partials that a second kernel sums in a fixed
-//            order.
+//   1x1 stride-1 (pointwise) convolutions read NCHW directly: the pixels of an
+//   image are contiguous, so a 32-pixel x 32-channel TMA box is an MN-major
+//   operand tile.  GEMM rows are four 32-pixel "slots" (n, hw0); an image
+//   whose pixel count is not a multiple of 32 leaves its last slot part-empty
+//   (TMA fills zeros, the store clips).
+//     forward   Y[n, k, hw]  = sum_c W[k, c] X[n, c, hw]     (A = X slots, B = W K-major)
+//     dgrad     dX[n, c, hw] = sum_k W[k, c] dY[n, k, hw]    (A = dY slots, B = W MN-major)
+//     wgrad     dW[k, c]     = sum_{n,hw} dY[n, k, hw] X[n, c, hw]  (both K-major along pixels)
+//   Other convolutions first stage their activations channels-last (NHWC,
+//   channels zero-padded to a multiple of 4) in the caller's workspace,
+//   because TMA can shift a tile by a filter tap along W and H only when the
+//   contiguous dim is C.
+//     forward   Y[pix, k] = sum_{r,s,c} Xnhwc[n, p*sh-ph+r*dh, q*sw-pw+s*dw, c] * Wp[k, r, s, c]
+//               GEMM M = 128 output pixels (a BW x BH x BNI block), N = BN output
+//               channels, K = R*S*ceil(C/32) blocks of 32 channels.  A: one 4-D
+//               TMA box per K block, shifted by the tap, stride via the tensor
+//               map's element strides (K-major).  B: packed weights (K-major).
+//     dgrad     any stride, by sub-pixel phases: the dX rows/columns of one
+//               residue class mod the stride receive a fixed subset of taps, so
+//               each phase is a stride-1 correlation over dY (tap offsets in a
+//               table, weights packed per phase) written to dX with strides.
+//     small C   (the 3-channel stem): the S filter columns fold into channels,
+//               Xf[n, h, q, (s, c)] = X[n, c, h, q*sw + s*dw - pw], so a 7x7/2
+//               conv on 3 channels runs as 7x1 on 21 (padded to 24).
+//     wgrad     dW[k, c, r, s] = sum_pix dYnhwc[pix, k] * Xnhwc[shift_rs(pix), c]
+//               GEMM M = 128 output channels, N = BN input channels, K = 32-pixel
+//               blocks (MN-major A and B), one tap per tile.
+//   Weight gradients split K (pixels) over CTAs into fp32 partials that a
+//   second kernel sums in a fixed order (or go straight to dW with one split).
+//
+// Epilogue of the forward-shaped launches: each epilogue warp owns 32
+// accumulator rows; per 32-channel chunk it loads TMEM into registers, writes
+// the chunk to a shared-memory box (double-buffered per warp) and issues one
+// TMA tensor store, so global writes are full-line bulk transfers that run
+// behind the next chunk.  The box is (32 q) x (32 k) of an NCHW row, or a
+// (q, p) patch of up to 32 pixels, or a run of whole rows of a plane whose
+// row pitch is not 16-byte aligned; outputs with strided pixels (dgrad
+// phases of strided convolutions) use direct stores.
 // Kernel structure (warp roles, TMA ring, TMEM double buffer, bounded waits)
 // is the one of the GEMM in gemm_tc.cu.
 #include <mutex>
@@ -34,6 +51,23 @@ namespace pvb2 {
 constexpr int cBM = 128, cBK = 32, cStages = 4, cThreads = 192;
 
 constexpr int kMaxTaps = 8;
+
+// where the operands of one launch come from
+enum ConvMode : int {
+  kImplicit = 0,  // forward / dgrad phase: A = channels-last tap boxes (K-major), B = packed weights (K-major)
+  kPwFwd = 1,     // 1x1 stride-1 forward: A = NCHW 32-pixel slots (MN-major), B = W[K][C] (K-major)
+  kPwDgrad = 2,   // 1x1 stride-1 dgrad: A = dY NCHW slots (MN-major), B = W[K][C] read along C (MN-major)
+  kWgrad = 3,     // weight gradient over channels-last tap boxes (A and B MN-major)
+  kPwWgrad = 4,   // 1x1 stride-1 weight gradient: A = dY, B = X, both NCHW, K-major along pixels
+};
+
+// how a forward-shaped launch writes its output
+enum EpiMode : int {
+  kEpiScalar = 0,  // direct per-element stores (any output strides)
+  kEpiBox = 1,     // TMA box (ebq q) x (ebp p) x 32 k of an NCHW-shaped output
+  kEpiFlat = 2,    // TMA box of ebp whole rows (ebp * Q pixels) x 32 k, plane viewed flat
+  kEpiSlots = 3,   // TMA box of one 32-pixel slot x 32 k (pointwise modes)
+};
 
 struct ConvTcArgs {
   int N, Cin, Cp, Kout, P, Q, R, S;   // the conv computed (for dgrad: the equivalent conv over dY)
@@ -49,6 +83,9 @@ struct ConvTcArgs {
   int kt;                             // fwd: output-channel tiles ceil(Kout / BN); wgrad: ceil(Kout / 128)
   int ct;                             // wgrad: input-channel tiles ceil(Cin / BN)
   int splits, kb_per_split, total_kb; // wgrad split-K over pixel blocks
+  int hwb, slots;                     // pointwise: 32-pixel slots per image, slots in all images
+  int tiles;                          // tiles of this launch
+  int epi, ebq, ebp;                  // EpiMode and its box extents
   float* out;
   const float* bias;
 };
@@ -58,14 +95,21 @@ struct ConvSmem {
   static constexpr int A_BYTES = cBM * cBK * 4;
   static constexpr int B_BYTES = BN * cBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = cStages * STAGE_BYTES;
+  static constexpr int EPI_OFF = cStages * STAGE_BYTES;  // 4 epilogue warps x 2 boxes of 32 x 32 fp32
+  static constexpr int EPI_BYTES = 4 * 2 * 32 * 32 * 4;
+  static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int TOTAL = BAR_OFF + (2 * cStages + 4) * 8 + 16;
 };
+static_assert(ConvSmem<256>::TOTAL + 1024 <= 232448, "conv tile does not fit in shared memory");
 
-// WGRAD = false: forward / dgrad.  WGRAD = true: weight gradient partials.
-template <int BN, bool WGRAD>
+template <int BN, int MODE>
 __global__ void __launch_bounds__(cThreads, 1)
-    conv_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, ConvTcArgs a) {
+    conv_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, ConvTcArgs a) {
+  constexpr bool WG = MODE == kWgrad || MODE == kPwWgrad;
+  constexpr bool PW = MODE == kPwFwd || MODE == kPwDgrad;
+  constexpr bool A_MN = MODE == kPwFwd || MODE == kPwDgrad || MODE == kWgrad;
+  constexpr bool B_MN = MODE == kPwDgrad || MODE == kWgrad;
   using L = ConvSmem<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -78,8 +122,7 @@ __global__ void __launch_bounds__(cThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int RS = a.R * a.S;
-  const int pix_tiles = a.tq * a.tp * a.tn;
-  const int total_tiles = WGRAD ? a.kt * a.ct * RS * a.splits : pix_tiles * a.kt;
+  const int total_tiles = a.tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < cStages; ++s) {
@@ -127,7 +170,7 @@ __global__ void __launch_bounds__(cThreads, 1)
       tma_prefetch(&tmB);
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x) {
-        if (!WGRAD) {
+        if (MODE == kImplicit) {
           int kt, q0, p0, n0;
           fwd_tile(tile, kt, q0, p0, n0);
           const int kblocks = RS * a.cblocks;
@@ -142,7 +185,30 @@ __global__ void __launch_bounds__(cThreads, 1)
             tma_load_4d(sa, &tmA, &full[s_], cb * 32, q0 * a.sw + a.tap_w[s], p0 * a.sh + a.tap_h[r], n0);
             tma_load_2d(sa + L::A_BYTES, &tmB, &full[s_], rs * a.Cp + cb * 32, kt * BN);
           }
-        } else {
+        } else if (PW) {
+          const int kt = tile % a.kt, g = tile / a.kt;
+          for (int kb = 0; kb < a.cblocks; ++kb, ++it) {
+            const int s_ = it % cStages;
+            const uint32_t ph = (it / cStages) & 1;
+            if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
+            uint8_t* sa = smem + s_ * L::STAGE_BYTES;
+            uint8_t* sb = sa + L::A_BYTES;
+            mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              // slots past the last image read out of range: TMA fills zeros
+              const int slot = g * 4 + j;
+              const int n = slot / a.hwb;
+              tma_load_3d(sa + j * 32 * cBK * 4, &tmA, &full[s_], (slot - n * a.hwb) * 32, kb * 32, n);
+            }
+            if (MODE == kPwFwd) {
+              tma_load_2d(sb, &tmB, &full[s_], kb * 32, kt * BN);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * 32 * cBK * 4, &tmB, &full[s_], kt * BN + 32 * j, kb * 32);
+            }
+          }
+        } else if (MODE == kWgrad) {
           int sp, km, ctile, rs;
           wg_tile(tile, sp, km, ctile, rs);
           const int r = rs / a.S, s = rs % a.S;
@@ -163,13 +229,28 @@ __global__ void __launch_bounds__(cThreads, 1)
               tma_load_4d(sb + j * 32 * cBK * 4, &tmB, &full[s_], ctile * BN + 32 * j, q0 * a.sw + a.tap_w[s],
                           p0 * a.sh + a.tap_h[r], n0);
           }
+        } else {  // kPwWgrad: K blocks are (image, 32-pixel slot) pairs
+          int sp, km, ctile, rs;
+          wg_tile(tile, sp, km, ctile, rs);
+          int kb0, kb1;
+          wg_range(sp, kb0, kb1);
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s_ = it % cStages;
+            const uint32_t ph = (it / cStages) & 1;
+            if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
+            const int n = kb / a.hwb, hw0 = (kb - n * a.hwb) * 32;
+            uint8_t* sa = smem + s_ * L::STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
+            tma_load_3d(sa, &tmA, &full[s_], hw0, km * cBM, n);
+            tma_load_3d(sa + L::A_BYTES, &tmB, &full[s_], hw0, ctile * BN, n);
+          }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(cBM, BN, WGRAD, WGRAD);
+      constexpr uint32_t idesc = idesc_tf32(cBM, BN, A_MN, B_MN);
       uint32_t it = 0;
       int local = 0;
       for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
@@ -179,7 +260,7 @@ __global__ void __launch_bounds__(cThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         int kb0 = 0, kb1 = RS * a.cblocks;
-        if (WGRAD) {
+        if (WG) {
           int sp, km, ctile, rs;
           wg_tile(tile, sp, km, ctile, rs);
           wg_range(sp, kb0, kb1);
@@ -193,8 +274,8 @@ __global__ void __launch_bounds__(cThreads, 1)
           const uint32_t sb = sa + L::A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < cBK / 8; ++kk) {
-            const uint64_t ad = WGRAD ? desc_mnmajor(sa, kk, 32 * cBK * 4) : desc_kmajor(sa, kk);
-            const uint64_t bd = WGRAD ? desc_mnmajor(sb, kk, 32 * cBK * 4) : desc_kmajor(sb, kk);
+            const uint64_t ad = A_MN ? desc_mnmajor(sa, kk, 32 * cBK * 4) : desc_kmajor(sa, kk);
+            const uint64_t bd = B_MN ? desc_mnmajor(sb, kk, 32 * cBK * 4) : desc_kmajor(sb, kk);
             mma_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&empty[s_]);
@@ -206,6 +287,8 @@ __global__ void __launch_bounds__(cThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane = accumulator row
+    float* stage = (float*)(smem + L::EPI_OFF) + quarter * 2 * 1024;
+    uint32_t echunk = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
       const int buf = local & 1;
@@ -213,23 +296,74 @@ __global__ void __launch_bounds__(cThreads, 1)
       if (!mbar_wait(&acc_full[buf], aph, abort)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
-      if (!WGRAD) {
-        int kt, q0, p0, n0;
-        fwd_tile(tile, kt, q0, p0, n0);
-        const int q = q0 + row % a.bw, p = p0 + (row / a.bw) % a.bh, n = n0 + row / (a.bw * a.bh);
-        const bool valid = q < a.Q && p < a.P && n < a.N;
-        float* obase = a.out + a.obase + (int64_t)n * a.on + (int64_t)p * a.op + (int64_t)q * a.oq;
+      if (!WG) {
+        int kt;
+        bool valid = false, bvalid;
+        float* obase = nullptr;
+        int bx, by = 0, bn;  // store-box origin of this warp's 32 rows
+        if (PW) {
+          kt = tile % a.kt;
+          const int slot = (tile / a.kt) * 4 + quarter;
+          bn = slot / a.hwb;
+          bx = (slot - bn * a.hwb) * 32;
+          bvalid = slot < a.slots;
+        } else {
+          int q0, p0, n0;
+          fwd_tile(tile, kt, q0, p0, n0);
+          const int q = q0 + row % a.bw, p = p0 + (row / a.bw) % a.bh, n = n0 + row / (a.bw * a.bh);
+          valid = q < a.Q && p < a.P && n < a.N;
+          obase = a.out + a.obase + (int64_t)n * a.on + (int64_t)p * a.op + (int64_t)q * a.oq;
+          const int r0 = quarter * 32;
+          const int wq = q0 + r0 % a.bw, wp = p0 + (r0 / a.bw) % a.bh;
+          bn = n0 + r0 / (a.bw * a.bh);
+          bvalid = wq < a.Q && wp < a.P && bn < a.N;
+          if (a.epi == kEpiBox) {
+            bx = wq;
+            by = wp;
+          } else {
+            bx = wp * a.Q;
+          }
+        }
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           const int k0 = kt * BN + c * 32;
-          if (valid) {
+          if (a.epi == kEpiScalar) {
+            if (valid) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int k = k0 + j;
-              if (k < a.Kout) obase[(int64_t)k * a.ok] = a.bias ? v[j] + a.bias[k] : v[j];
+              for (int j = 0; j < 32; ++j) {
+                const int k = k0 + j;
+                if (k < a.Kout) obase[(int64_t)k * a.ok] = a.bias ? v[j] + a.bias[k] : v[j];
+              }
             }
+          } else {
+            if (a.bias) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (k0 + j < a.Kout) v[j] += a.bias[k0 + j];
+            }
+            float* st = stage + (echunk & 1) * 1024;
+            if (lane == 0) bulk_wait_read<1>();  // the store that used this box two chunks ago has read it
+            __syncwarp();
+            if (a.epi == kEpiFlat) {
+              const int qq = lane % a.bw, pp = lane / a.bw, pitch = a.ebp * a.Q;
+              if (qq < a.Q) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) st[j * pitch + pp * a.Q + qq] = v[j];
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) st[j * 32 + lane] = v[j];
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && bvalid && k0 < a.Kout) {
+              if (a.epi == kEpiBox) tma_store_4d(&tmC, st, bx, by, k0, bn);
+              else tma_store_3d(&tmC, st, bx, k0, bn);
+              bulk_commit();
+            }
+            ++echunk;
           }
         }
       } else {
@@ -254,6 +388,7 @@ __global__ void __launch_bounds__(cThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) bulk_wait_all();
   }
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
@@ -387,6 +522,7 @@ static int pow2_at_least(int v, int lo, int hi) {
 }
 static size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 static int bn_for(int n) { return n <= 64 ? 64 : (n <= 128 ? 128 : 256); }
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 // pixel block of `pixels` (128 or 32) covering a P x Q grid
 static void pixel_block(int P, int Q, int pixels, int& bw, int& bh, int& bni) {
@@ -409,6 +545,13 @@ static bool tc_conv_shape_ok(const pvb2_conv2d_desc* d) {
   return true;
 }
 
+// 1x1, stride 1, no padding, and every NCHW row pitch a multiple of 16 bytes:
+// the NCHW tensors themselves are the GEMM operands
+static bool pointwise(const pvb2_conv2d_desc* d) {
+  return d->R == 1 && d->S == 1 && d->stride_h == 1 && d->stride_w == 1 && d->pad_h == 0 && d->pad_w == 0 &&
+         ((int64_t)d->H * d->W) % 4 == 0 && d->C % 4 == 0 && d->K % 4 == 0;
+}
+
 // fold the S filter columns into channels when the input has few channels
 static bool use_fold(const pvb2_conv2d_desc* d) { return d->C <= 8 && d->S * d->C <= 32; }
 static int fold_channels(const pvb2_conv2d_desc* d) { return round4(d->S * d->C); }
@@ -418,26 +561,28 @@ struct Taps {
   int h[kMaxTaps], w[kMaxTaps];
 };
 
-template <int BN, bool WG>
-static int launch_conv(const CUtensorMap& ma, const CUtensorMap& mb, const ConvTcArgs& a, int tiles, cudaStream_t s) {
+template <int BN, int MODE>
+static int launch_conv(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const ConvTcArgs& a,
+                       cudaStream_t s) {
   constexpr int smem = ConvSmem<BN>::TOTAL + 1024;
   static bool attr = false;
   if (!attr) {
-    PVB2_CUDA_TRY(cudaFuncSetAttribute(conv_tf32_kernel<BN, WG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    PVB2_CUDA_TRY(cudaFuncSetAttribute(conv_tf32_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr = true;
   }
-  const int grid = std::min(tiles, num_sms());
-  conv_tf32_kernel<BN, WG><<<grid, cThreads, smem, s>>>(ma, mb, a);
+  if (a.tiles <= 0) return PVB2_OK;
+  const int grid = std::min(a.tiles, num_sms());
+  conv_tf32_kernel<BN, MODE><<<grid, cThreads, smem, s>>>(ma, mb, mc, a);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
 
-template <bool WG>
-static int launch_bn(int BN, const CUtensorMap& ma, const CUtensorMap& mb, const ConvTcArgs& a, int tiles,
+template <int MODE>
+static int launch_bn(int BN, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const ConvTcArgs& a,
                      cudaStream_t s) {
-  if (BN == 64) return launch_conv<64, WG>(ma, mb, a, tiles, s);
-  if (BN == 128) return launch_conv<128, WG>(ma, mb, a, tiles, s);
-  return launch_conv<256, WG>(ma, mb, a, tiles, s);
+  if (BN == 64) return launch_conv<64, MODE>(ma, mb, mc, a, s);
+  if (BN == 128) return launch_conv<128, MODE>(ma, mb, mc, a, s);
+  return launch_conv<256, MODE>(ma, mb, mc, a, s);
 }
 
 // channels-last activations [N, H, W, Cp] as a 4-D map (Cp, W, H, N)
@@ -451,10 +596,50 @@ static int act_map(CUtensorMap* m, const float* base, int N, int H, int W, int C
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, es);
 }
 
+// an NCHW tensor [N, C, HW] as a 3-D map (HW, C, N) with box (32, rows, 1)
+static int nchw_map(CUtensorMap* m, const float* base, int N, int C, int64_t hw, int rows, CUtensorMapSwizzle sw) {
+  uint64_t dims[3] = {(uint64_t)hw, (uint64_t)C, (uint64_t)N};
+  uint64_t str[2] = {(uint64_t)hw * 4, (uint64_t)C * hw * 4};
+  uint32_t box[3] = {32, (uint32_t)rows, 1};
+  return encode_tiled(m, 3, base, dims, str, box, sw);
+}
+
 static int to_nhwc(const float* x, float* y, int N, int C, int Cp, int64_t HW, cudaStream_t s) {
   dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((Cp + 31) / 32), (unsigned)N);
   nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, y, C, Cp, HW);
   PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+// Choose the epilogue of a forward-shaped launch over a bw x bh x bni pixel
+// block and build its store map.  TMA needs a 16-byte-aligned base, unit
+// stride along q and 16-byte multiples for every other stride.
+static int plan_epilogue(ConvTcArgs& a, CUtensorMap* mc, float* out, int N, int K, int P, int Q) {
+  a.epi = kEpiScalar;
+  float* base = out + a.obase;
+  const bool ok = aligned16(base) && a.oq == 1 && (a.ok * 4) % 16 == 0 && (a.on * 4) % 16 == 0 &&
+                  a.bw * a.bh >= 32;
+  if (!ok) return PVB2_OK;
+  if ((a.op * 4) % 16 == 0) {
+    a.epi = kEpiBox;
+    a.ebq = std::min(a.bw, 32);
+    a.ebp = 32 / a.ebq;
+    uint64_t dims[4] = {(uint64_t)Q, (uint64_t)P, (uint64_t)K, (uint64_t)N};
+    uint64_t str[3] = {(uint64_t)a.op * 4, (uint64_t)a.ok * 4, (uint64_t)a.on * 4};
+    uint32_t box[4] = {(uint32_t)a.ebq, (uint32_t)a.ebp, 32, 1};
+    return encode_tiled(mc, 4, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  // rows not 16-byte aligned (e.g. 14 x 14 planes): store whole rows of a contiguous plane
+  const int ebp = 32 / std::max(a.bw, 1);
+  if (a.op == Q && a.bw >= Q && a.bw <= 32 && (ebp * Q) % 4 == 0 && (a.bh * Q) % 4 == 0) {
+    a.epi = kEpiFlat;
+    a.ebq = Q;
+    a.ebp = ebp;
+    uint64_t dims[3] = {(uint64_t)P * Q, (uint64_t)K, (uint64_t)N};
+    uint64_t str[2] = {(uint64_t)a.ok * 4, (uint64_t)a.on * 4};
+    uint32_t box[3] = {(uint32_t)(ebp * Q), 32, 1};
+    return encode_tiled(mc, 3, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
   return PVB2_OK;
 }
 
@@ -468,7 +653,8 @@ static int run_fwd_like(const float* act, const float* wpacked, const float* bia
   int bw, bh, bni;
   pixel_block(P, Q, cBM, bw, bh, bni);
   const int BN = bn_for(K);
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mc;
+  memset(&mc, 0, sizeof(mc));
   PVB2_TRY(act_map(&ma, act, N, H, W, Cp, bw, bh, bni, sw, sh, false));
   const int taps = t.nr * t.ns;
   uint64_t wd[2] = {(uint64_t)taps * Cp, (uint64_t)K};
@@ -492,15 +678,61 @@ static int run_fwd_like(const float* act, const float* wpacked, const float* bia
   a.kt = (K + BN - 1) / BN;
   a.out = out;
   a.bias = bias;
-  const int tiles = a.tq * a.tp * a.tn * a.kt;
-  return launch_bn<false>(BN, ma, mb, a, tiles, s);
+  a.tiles = a.tq * a.tp * a.tn * a.kt;
+  PVB2_TRY(plan_epilogue(a, &mc, out, N, K, P, Q));
+  return launch_bn<kImplicit>(BN, ma, mb, mc, a, s);
 }
 
-// Weight-gradient implicit GEMM into partials [splits][K][Cin][taps].
-// dy: channels-last [N, P, Q, Kp]; x: channels-last [N, H, W, Cp] (Cin <= Cp real channels)
+// Pointwise forward (transpose = false): Y[n, k, hw] = sum_c W[k, c] X[n, c, hw] (+ bias[k]).
+// Pointwise dgrad (transpose = true):    dX[n, c, hw] = sum_k W[k, c] dY[n, k, hw].
+// src: [N, Cs, hw]; dst: [N, Cd, hw]; w: [K][C] with (Cs, Cd) = (C, K) or (K, C).
+static int run_pointwise(const float* src, const float* w, const float* bias, float* dst, int N, int C, int K,
+                         int64_t hw, bool transpose, cudaStream_t s) {
+  const int Cs = transpose ? K : C, Cd = transpose ? C : K;
+  const int BN = bn_for(Cd);
+  CUtensorMap ma, mb, mc;
+  PVB2_TRY(nchw_map(&ma, src, N, Cs, hw, 32, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+  uint64_t wd[2] = {(uint64_t)C, (uint64_t)K};
+  uint64_t wst[1] = {(uint64_t)C * 4};
+  if (!transpose) {
+    uint32_t wbox[2] = {32, (uint32_t)BN};
+    PVB2_TRY(encode_tiled(&mb, 2, w, wd, wst, wbox, CU_TENSOR_MAP_SWIZZLE_128B));
+  } else {
+    uint32_t wbox[2] = {32, 32};
+    PVB2_TRY(encode_tiled(&mb, 2, w, wd, wst, wbox, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+  }
+  PVB2_TRY(nchw_map(&mc, dst, N, Cd, hw, 32, CU_TENSOR_MAP_SWIZZLE_NONE));
+  ConvTcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.N = N; a.Cin = Cs; a.Cp = Cs; a.Kout = Cd; a.P = 1; a.Q = (int)hw; a.R = 1; a.S = 1;
+  a.sh = a.sw = 1;
+  a.cblocks = (Cs + 31) / 32;
+  a.kt = (Cd + BN - 1) / BN;
+  a.hwb = (int)((hw + 31) / 32);
+  a.slots = N * a.hwb;
+  a.tiles = (a.slots + 3) / 4 * a.kt;
+  a.epi = kEpiSlots;
+  a.out = dst;
+  a.bias = bias;
+  if (transpose) return launch_bn<kPwDgrad>(BN, ma, mb, mc, a, s);
+  return launch_bn<kPwFwd>(BN, ma, mb, mc, a, s);
+}
+
+// Weight-gradient split-K plan.  kb_total K blocks (32 pixels each) reduce
+// into K x Cin x taps outputs; enough splits to give every SM two tiles,
+// each split keeping at least 8 K blocks.
 struct WgPlan {
   int bw, bh, bni, BN, splits, kb_per, total_kb, ct, kt;
 };
+
+static void plan_splits(WgPlan& w, int taps) {
+  const int base_tiles = w.kt * w.ct * taps;
+  int splits = (2 * num_sms() + base_tiles - 1) / base_tiles;
+  splits = std::min(splits, std::max(1, w.total_kb / 8));
+  splits = std::max(1, std::min(splits, 64));
+  w.kb_per = (w.total_kb + splits - 1) / splits;
+  w.splits = (w.total_kb + w.kb_per - 1) / w.kb_per;
+}
 
 static WgPlan plan_wg(int N, int K, int Cin, int P, int Q, int taps) {
   WgPlan w;
@@ -510,18 +742,27 @@ static WgPlan plan_wg(int N, int K, int Cin, int P, int Q, int taps) {
   w.kt = (K + cBM - 1) / cBM;
   const int tq = (Q + w.bw - 1) / w.bw, tp = (P + w.bh - 1) / w.bh, tn = (N + w.bni - 1) / w.bni;
   w.total_kb = tq * tp * tn;
-  const int base_tiles = w.kt * w.ct * taps;
-  int splits = (2 * num_sms() + base_tiles - 1) / base_tiles;
-  splits = std::min(splits, std::max(1, w.total_kb / 8));
-  splits = std::max(1, std::min(splits, 64));
-  w.kb_per = (w.total_kb + splits - 1) / splits;
-  w.splits = (w.total_kb + w.kb_per - 1) / w.kb_per;
+  plan_splits(w, taps);
   return w;
 }
 
+static WgPlan plan_pw_wg(int N, int K, int C, int64_t hw) {
+  WgPlan w;
+  w.bw = 32; w.bh = 1; w.bni = 1;
+  w.BN = bn_for(C);
+  w.ct = (C + w.BN - 1) / w.BN;
+  w.kt = (K + cBM - 1) / cBM;
+  w.total_kb = N * (int)((hw + 31) / 32);
+  plan_splits(w, 1);
+  return w;
+}
+
+// dy: channels-last [N, P, Q, Kp]; x: channels-last [N, H, W, Cp] (Cin <= Cp real channels);
+// partials [splits][K][Cin][taps]
 static int run_wgrad(const float* dyn, int Kp, const float* xn, int Cp, int N, int H, int W, int P, int Q, int K,
                      int Cin, const Taps& t, int sh, int sw, const WgPlan& p, float* part, cudaStream_t s) {
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mc;
+  memset(&mc, 0, sizeof(mc));
   PVB2_TRY(act_map(&ma, dyn, N, P, Q, Kp, p.bw, p.bh, p.bni, 1, 1, true));
   PVB2_TRY(act_map(&mb, xn, N, H, W, Cp, p.bw, p.bh, p.bni, sw, sh, true));
   ConvTcArgs a;
@@ -542,8 +783,30 @@ static int run_wgrad(const float* dyn, int Kp, const float* xn, int Cp, int N, i
   a.kb_per_split = p.kb_per;
   a.total_kb = p.total_kb;
   a.out = part;
-  const int tiles = a.kt * a.ct * t.nr * t.ns * a.splits;
-  return launch_bn<true>(p.BN, ma, mb, a, tiles, s);
+  a.tiles = a.kt * a.ct * t.nr * t.ns * a.splits;
+  return launch_bn<kWgrad>(p.BN, ma, mb, mc, a, s);
+}
+
+// pointwise weight gradient into partials [splits][K][C]
+static int run_pw_wgrad(const float* dy, const float* x, int N, int C, int K, int64_t hw, const WgPlan& p,
+                        float* part, cudaStream_t s) {
+  CUtensorMap ma, mb, mc;
+  memset(&mc, 0, sizeof(mc));
+  PVB2_TRY(nchw_map(&ma, dy, N, K, hw, cBM, CU_TENSOR_MAP_SWIZZLE_128B));
+  PVB2_TRY(nchw_map(&mb, x, N, C, hw, p.BN, CU_TENSOR_MAP_SWIZZLE_128B));
+  ConvTcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.N = N; a.Cin = C; a.Cp = C; a.Kout = K; a.P = 1; a.Q = (int)hw; a.R = 1; a.S = 1;
+  a.sh = a.sw = 1;
+  a.kt = p.kt;
+  a.ct = p.ct;
+  a.splits = p.splits;
+  a.kb_per_split = p.kb_per;
+  a.total_kb = p.total_kb;
+  a.hwb = (int)((hw + 31) / 32);
+  a.out = part;
+  a.tiles = a.kt * a.ct * a.splits;
+  return launch_bn<kPwWgrad>(p.BN, ma, mb, mc, a, s);
 }
 
 static Taps fwd_taps(const pvb2_conv2d_desc* d) {
@@ -571,14 +834,14 @@ struct Layout {
 
 static Layout fwd_layout(const pvb2_conv2d_desc* d) {
   Layout l;
+  l.a = l.b = l.c = l.total = 0;
+  if (pointwise(d)) return l;
   if (use_fold(d)) {
     const int Cf = fold_channels(d);
-    l.a = 0;
     l.b = align256((size_t)d->N * d->H * d->Q * Cf * 4);
     l.total = l.b + align256((size_t)d->K * d->R * Cf * 4);
   } else {
     const int Cp = round4(d->C);
-    l.a = 0;
     l.b = align256((size_t)d->N * d->H * d->W * Cp * 4);
     l.total = l.b + align256((size_t)d->K * d->R * d->S * Cp * 4);
   }
@@ -588,8 +851,9 @@ static Layout fwd_layout(const pvb2_conv2d_desc* d) {
 
 static Layout dgrad_layout(const pvb2_conv2d_desc* d) {
   Layout l;
+  l.a = l.b = l.c = l.total = 0;
+  if (pointwise(d)) return l;
   const int Kp = round4(d->K);
-  l.a = 0;
   l.b = align256((size_t)d->N * d->P * d->Q * Kp * 4);
   l.total = l.b + align256((size_t)d->C * d->R * d->S * Kp * 4);  // one phase's packed weights at a time
   l.c = l.total;
@@ -598,6 +862,13 @@ static Layout dgrad_layout(const pvb2_conv2d_desc* d) {
 
 static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
   Layout l;
+  l.a = l.b = l.c = l.total = 0;
+  if (pointwise(d)) {
+    WgPlan p = plan_pw_wg(d->N, d->K, d->C, (int64_t)d->H * d->W);
+    if (plan) *plan = p;
+    l.total = p.splits > 1 ? align256((size_t)p.splits * d->K * d->C * 4) : 0;
+    return l;
+  }
   const int Kp = round4(d->K);
   const bool fold = use_fold(d);
   const int Cx = fold ? fold_channels(d) : round4(d->C);
@@ -623,11 +894,17 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
                 size_t ws_bytes, cudaStream_t s, bool* handled) {
   *handled = false;
   if (!tc_conv_shape_ok(d)) return PVB2_OK;
+  const int64_t pq = (int64_t)d->P * d->Q;
+  if (pointwise(d)) {
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return PVB2_OK;
+    PVB2_TRY(run_pointwise(x, w, b, y, d->N, d->C, d->K, pq, false, s));
+    *handled = true;
+    return PVB2_OK;
+  }
   Layout l = fwd_layout(d);
   if (!ws || ws_bytes < l.total) return PVB2_OK;  // not enough scratch: exact path
   float* act = (float*)((char*)ws + l.a);
   float* wp = (float*)((char*)ws + l.b);
-  const int64_t pq = (int64_t)d->P * d->Q;
   if (use_fold(d)) {
     const int Cf = fold_channels(d);
     const int64_t n1 = (int64_t)d->N * d->H * d->Q * Cf;
@@ -663,6 +940,12 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
                      cudaStream_t s, bool* handled) {
   *handled = false;
   if (!tc_conv_shape_ok(d)) return PVB2_OK;
+  if (pointwise(d)) {
+    if (!aligned16(dy) || !aligned16(w) || !aligned16(dx)) return PVB2_OK;
+    PVB2_TRY(run_pointwise(dy, w, nullptr, dx, d->N, d->C, d->K, (int64_t)d->H * d->W, true, s));
+    *handled = true;
+    return PVB2_OK;
+  }
   Layout l = dgrad_layout(d);
   if (!ws || ws_bytes < l.total) return PVB2_OK;
   const int Kp = round4(d->K);
@@ -736,6 +1019,19 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
   if (!tc_conv_shape_ok(d)) return PVB2_OK;
   WgPlan p;
   Layout l = wgrad_layout(d, &p);
+  const int64_t wn = (int64_t)d->K * d->C * d->R * d->S;
+  if (pointwise(d)) {
+    if (!aligned16(x) || !aligned16(dy)) return PVB2_OK;
+    if (p.splits > 1 && (!ws || ws_bytes < l.total)) return PVB2_OK;
+    float* part = p.splits > 1 ? (float*)ws : dw;
+    PVB2_TRY(run_pw_wgrad(dy, x, d->N, d->C, d->K, (int64_t)d->H * d->W, p, part, s));
+    if (p.splits > 1) {
+      sum_partials_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, wn, dw);
+      PVB2_LAUNCH_CHECK();
+    }
+    *handled = true;
+    return PVB2_OK;
+  }
   if (!ws || ws_bytes < l.total) return PVB2_OK;
   const int Kp = round4(d->K);
   float* xn = (float*)((char*)ws + l.a);
@@ -750,17 +1046,19 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
     PVB2_LAUNCH_CHECK();
     PVB2_TRY(run_wgrad(dyn, Kp, xn, Cf, d->N, d->H, d->Q, d->P, d->Q, d->K, Cf, fold_taps(d), d->stride_h, 1, p, part,
                        s));
-    const int64_t wn = (int64_t)d->K * d->C * d->R * d->S;
     unfold_wgrad_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, d->K, d->C, d->R, d->S, Cf, dw);
     PVB2_LAUNCH_CHECK();
   } else {
     const int Cp = round4(d->C);
     PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
+    // one split: the partials layout [1][K][C][R*S] is dW itself
+    float* dst = p.splits > 1 ? part : dw;
     PVB2_TRY(run_wgrad(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h,
-                       d->stride_w, p, part, s));
-    const int64_t wn = (int64_t)d->K * d->C * d->R * d->S;
-    sum_partials_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, wn, dw);
-    PVB2_LAUNCH_CHECK();
+                       d->stride_w, p, dst, s));
+    if (p.splits > 1) {
+      sum_partials_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, wn, dw);
+      PVB2_LAUNCH_CHECK();
+    }
   }
   *handled = true;
   return PVB2_OK;

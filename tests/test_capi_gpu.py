@@ -84,6 +84,14 @@ CONV_SHAPES = [
     (2, 1024, 14, 14, 256, 1, 1, 1, 0, 1, 1),    # layer3 1x1 reduce
     (3, 512, 7, 7, 512, 3, 3, 1, 1, 1, 1),       # layer4 3x3: tiles span two images
     (2, 32, 26, 26, 64, 3, 3, 1, 0, 1, 1),       # MNIST conv2
+    # pointwise (1x1, stride 1) paths that read NCHW directly
+    (4, 36, 12, 12, 40, 1, 1, 1, 0, 1, 1),       # channel tails, 144-pixel images (part-empty slots)
+    (3, 64, 20, 20, 64, 1, 1, 1, 0, 1, 1),       # 13 slots per image: last tile only partly used
+    (2, 256, 28, 28, 512, 1, 1, 1, 0, 1, 1),     # layer2 1x1 expand
+    (2, 512, 7, 7, 2048, 1, 1, 1, 0, 1, 1),      # 49-pixel images: staged path, direct stores
+    # epilogue store boxes
+    (4, 64, 14, 14, 100, 3, 3, 1, 1, 1, 1),      # 14-wide rows stored as whole-row runs; output-channel tail
+    (2, 16, 112, 112, 24, 3, 3, 1, 1, 1, 1),     # two 64-wide pixel blocks per row
 ]
 
 
