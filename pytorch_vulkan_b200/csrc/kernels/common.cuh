@@ -172,6 +172,15 @@ __device__ __forceinline__ void iter_offsets(const IterShape& it, int nargs, int
   }
 }
 
+// true the first time it is called with `mask` on the current device (for
+// per-device one-time setup such as cudaFuncSetAttribute)
+inline bool first_on_device(std::atomic<uint64_t>& mask) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return true;
+  const uint64_t bit = 1ull << (dev & 63);
+  return (mask.fetch_or(bit) & bit) == 0;
+}
+
 inline int grid_for(int64_t n, int block, int max_blocks_per_sm = 8) {
   int64_t b = (n + block - 1) / block;
   int64_t cap = (int64_t)num_sms() * max_blocks_per_sm;

@@ -565,11 +565,9 @@ template <int BN, int MODE>
 static int launch_conv(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const ConvTcArgs& a,
                        cudaStream_t s) {
   constexpr int smem = ConvSmem<BN>::TOTAL + 1024;
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<uint64_t> attr_done{0};
+  if (first_on_device(attr_done))
     PVB2_CUDA_TRY(cudaFuncSetAttribute(conv_tf32_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr = true;
-  }
   if (a.tiles <= 0) return PVB2_OK;
   const int grid = std::min(a.tiles, num_sms());
   conv_tf32_kernel<BN, MODE><<<grid, cThreads, smem, s>>>(ma, mb, mc, a);

@@ -277,12 +277,10 @@ static int make_operand_map(CUtensorMap* map, const pvb2_tensor* t, bool k_is_co
 template <int BN, bool A_MN, bool B_MN>
 static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmEpi& ep, cudaStream_t s) {
   constexpr int smem = GemmSmem<BN>::TOTAL + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static std::atomic<uint64_t> attr_done{0};
+  if (first_on_device(attr_done))
     PVB2_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_kernel<BN, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        smem));
-    attr_set = true;
-  }
   const int tiles = ((ep.M + kBM - 1) / kBM) * ((ep.N + BN - 1) / BN) * ep.batch;
   const int grid = std::min(tiles, num_sms());
   gemm_tf32_kernel<BN, A_MN, B_MN><<<grid, kThreads, smem, s>>>(ma, mb, ep);

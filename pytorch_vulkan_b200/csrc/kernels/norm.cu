@@ -5,7 +5,11 @@
 // batch-norm-over-(1,B,N) trick the reference used for layer norm
 // (norm_ops.cpp:167-351).
 //
-// Batch norm on NCHW-contiguous x runs as two launches:
+// Training batch norm on NCHW-contiguous x whose channels each fit the shared
+// memory of one thread-block cluster (<= 8 CTAs, up to 1.7 MB of fp32 per
+// channel in the forward, 0.85 MB per tensor in the backward) runs as ONE
+// cluster-resident launch that reads its inputs once (bn_fwd_cluster_kernel,
+// bn_bwd_cluster_kernel below).  Larger channels run as two launches:
 //   1. stats:   grid (C, splits); each CTA reduces whole (n, c) planes with
 //               128-bit loads into a shifted sum / sum of squares; the
 //               per-CTA partials go to the caller's workspace.
@@ -16,8 +20,11 @@
 //               save_invstd and updates the running statistics.
 // The backward pass has the same shape: a reduction of (sum dy,
 // sum dy*(x-mean)) per channel, then an apply pass for dx.
+#include <cooperative_groups.h>
 #include <mutex>
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace pvb2 {
 
@@ -275,6 +282,272 @@ __global__ void bn_bwd_eval_kernel(const float* __restrict__ dy, const float* __
   for (int64_t i = threadIdx.x; i < HW; i += blockDim.x) o[i] = g[i] * mul;
 }
 
+// ------------------------------------------- batch norm, cluster-resident
+// When one channel's data fits the shared memory of a thread-block cluster
+// (<= 8 CTAs), the training forward and backward each read their inputs from
+// HBM once: grid (k, C) with clusters of k CTAs along x, CTA r of channel c
+// holds elements [r*chunk, (r+1)*chunk) of the channel's (n, hw) range in
+// shared memory, partial sums meet through distributed shared memory, and
+// the output is written from the resident copy.  The forward computes the
+// variance in two passes over shared memory (mean first, then squared
+// deviations), so no shift is needed.
+constexpr int kBnClThreads = 512;
+constexpr int kBnClMaxCluster = 8;
+constexpr int kBnClSmallBytes = 110 * 1024;  // two CTAs per SM
+constexpr int kBnClBigBytes = 220 * 1024;    // one CTA per SM
+
+// sum over the block; every thread gets the result
+__device__ __forceinline__ float block_allsum(float v, float* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __syncthreads();  // red may still be read by a previous call
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+// cluster-wide sum of one float per CTA, combined in double in rank order
+__device__ __forceinline__ double cluster_sum(cg::cluster_group& cl, float* slot) {
+  double t = 0.0;
+  const int k = (int)cl.num_blocks();
+  for (int q = 0; q < k; ++q) t += (double)*cl.map_shared_rank(slot, q);
+  return t;
+}
+
+// copy this CTA's elements of channel c into shared memory
+__device__ __forceinline__ void bn_cl_load(const float* __restrict__ src, float* __restrict__ dst, int start, int end,
+                                           int HW, int64_t nstride, bool vec) {
+  if (vec) {
+    for (int e = start + 4 * threadIdx.x; e < end; e += 4 * blockDim.x) {
+      const int n = e / HW, i = e - n * HW;
+      *reinterpret_cast<float4*>(dst + (e - start)) = __ldg(reinterpret_cast<const float4*>(src + n * nstride + i));
+    }
+  } else {
+    for (int e = start + threadIdx.x; e < end; e += blockDim.x) {
+      const int n = e / HW, i = e - n * HW;
+      dst[e - start] = __ldg(src + n * nstride + i);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kBnClThreads) bn_fwd_cluster_kernel(
+    const float* __restrict__ x, float* __restrict__ y, int N, int C, int HW, int chunk, int vec,
+    const float* __restrict__ gamma, const float* __restrict__ beta, float* __restrict__ running_mean,
+    float* __restrict__ running_var, float momentum, float eps, float* __restrict__ save_mean,
+    float* __restrict__ save_invstd) {
+  extern __shared__ __align__(16) float sx[];
+  __shared__ float red[32];
+  __shared__ float cl_part[2];
+  __shared__ float s_coef[2];
+  cg::cluster_group cl = cg::this_cluster();
+  const int r = (int)cl.block_rank();
+  const int c = blockIdx.y;
+  const int M = N * HW;
+  const int start = r * chunk, end = min(M, start + chunk), len = max(0, end - start);
+  const int64_t nstride = (int64_t)C * HW;
+  bn_cl_load(x + (int64_t)c * HW, sx, start, end, HW, nstride, vec != 0);
+  __syncthreads();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) s += sx[i];
+  s = block_allsum(s, red);
+  if (threadIdx.x == 0) cl_part[0] = s;
+  cl.sync();
+  const float mean = (float)(cluster_sum(cl, &cl_part[0]) / (double)M);
+  float s2 = 0.f;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) {
+    const float d = sx[i] - mean;
+    s2 += d * d;
+  }
+  s2 = block_allsum(s2, red);
+  if (threadIdx.x == 0) cl_part[1] = s2;
+  cl.sync();
+  if (threadIdx.x == 0) {
+    const double count = (double)M;
+    const double var = cluster_sum(cl, &cl_part[1]) / count;
+    const float invstd = (float)(1.0 / sqrt(var + (double)eps));
+    const float g = gamma ? gamma[c] : 1.f;
+    const float b = beta ? beta[c] : 0.f;
+    const float a = invstd * g;
+    s_coef[0] = a;
+    s_coef[1] = b - mean * a;
+    if (r == 0) {
+      if (save_mean) save_mean[c] = mean;
+      if (save_invstd) save_invstd[c] = invstd;
+      if (running_mean) running_mean[c] = (1.f - momentum) * running_mean[c] + momentum * mean;
+      if (running_var) {
+        const double unbiased = count > 1.0 ? var * count / (count - 1.0) : var;
+        running_var[c] = (1.f - momentum) * running_var[c] + momentum * (float)unbiased;
+      }
+    }
+  }
+  cl.sync();  // peers are done reading cl_part; s_coef is visible block-wide
+  const float a = s_coef[0], b = s_coef[1];
+  float* yc = y + (int64_t)c * HW;
+  if (vec) {
+    for (int e = start + 4 * threadIdx.x; e < end; e += 4 * blockDim.x) {
+      const int n = e / HW, i = e - n * HW;
+      float4 v = *reinterpret_cast<const float4*>(sx + (e - start));
+      v.x = fmaf(v.x, a, b);
+      v.y = fmaf(v.y, a, b);
+      v.z = fmaf(v.z, a, b);
+      v.w = fmaf(v.w, a, b);
+      *reinterpret_cast<float4*>(yc + n * nstride + i) = v;
+    }
+  } else {
+    for (int e = start + threadIdx.x; e < end; e += blockDim.x) {
+      const int n = e / HW, i = e - n * HW;
+      yc[n * nstride + i] = fmaf(sx[e - start], a, b);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kBnClThreads) bn_bwd_cluster_kernel(
+    const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
+    const float* __restrict__ invstd, const float* __restrict__ gamma, int N, int C, int HW, int chunk, int vec,
+    float* __restrict__ dx, float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  extern __shared__ __align__(16) float smem_bn[];
+  float* sdy = smem_bn;
+  float* sx = smem_bn + chunk;
+  __shared__ float red[32];
+  __shared__ float cl_part[2];
+  __shared__ float s_coef[3];
+  cg::cluster_group cl = cg::this_cluster();
+  const int r = (int)cl.block_rank();
+  const int c = blockIdx.y;
+  const int M = N * HW;
+  const int start = r * chunk, end = min(M, start + chunk), len = max(0, end - start);
+  const int64_t nstride = (int64_t)C * HW;
+  bn_cl_load(dy + (int64_t)c * HW, sdy, start, end, HW, nstride, vec != 0);
+  bn_cl_load(x + (int64_t)c * HW, sx, start, end, HW, nstride, vec != 0);
+  __syncthreads();
+  const float m = mean[c];
+  float s_dy = 0.f, s_dot = 0.f;
+  for (int i = threadIdx.x; i < len; i += blockDim.x) {
+    const float g = sdy[i];
+    s_dy += g;
+    s_dot += g * (sx[i] - m);
+  }
+  s_dy = block_allsum(s_dy, red);
+  s_dot = block_allsum(s_dot, red);
+  if (threadIdx.x == 0) {
+    cl_part[0] = s_dy;
+    cl_part[1] = s_dot;
+  }
+  cl.sync();
+  if (threadIdx.x == 0) {
+    const double sdy_all = cluster_sum(cl, &cl_part[0]);
+    const double sdot_all = cluster_sum(cl, &cl_part[1]);
+    const double count = (double)M;
+    const float is = invstd[c];
+    s_coef[0] = (float)(sdy_all / count);              // mean of dy
+    s_coef[1] = (float)(sdot_all / count) * is * is;   // dotp * invstd^2 / count
+    s_coef[2] = is * (gamma ? gamma[c] : 1.f);
+    if (r == 0) {
+      if (dgamma) dgamma[c] = (float)sdot_all * is;
+      if (dbeta) dbeta[c] = (float)sdy_all;
+    }
+  }
+  cl.sync();
+  if (!dx) return;
+  const float gm = s_coef[0], kk = s_coef[1], mul = s_coef[2];
+  float* dxc = dx + (int64_t)c * HW;
+  if (vec) {
+    for (int e = start + 4 * threadIdx.x; e < end; e += 4 * blockDim.x) {
+      const int n = e / HW, i = e - n * HW;
+      const float4 g = *reinterpret_cast<const float4*>(sdy + (e - start));
+      const float4 v = *reinterpret_cast<const float4*>(sx + (e - start));
+      float4 o;
+      o.x = (g.x - gm - (v.x - m) * kk) * mul;
+      o.y = (g.y - gm - (v.y - m) * kk) * mul;
+      o.z = (g.z - gm - (v.z - m) * kk) * mul;
+      o.w = (g.w - gm - (v.w - m) * kk) * mul;
+      *reinterpret_cast<float4*>(dxc + n * nstride + i) = o;
+    }
+  } else {
+    for (int e = start + threadIdx.x; e < end; e += blockDim.x) {
+      const int n = e / HW, i = e - n * HW;
+      dxc[n * nstride + i] = (sdy[e - start] - gm - (sx[e - start] - m) * kk) * mul;
+    }
+  }
+}
+
+struct BnCluster {
+  int k, chunk, smem;
+  bool vec;
+};
+
+// plan a cluster-resident launch holding `arrays` fp32 tensors per element;
+// false when a channel does not fit 8 CTAs' shared memory
+static bool bn_cluster_plan(const BnGeom& g, int arrays, const void* const* ptrs, int nptr, BnCluster* p) {
+  const int64_t M = g.N * g.HW;
+  if (M <= 0 || g.C > 65535 || M > (int64_t)1 << 30) return false;
+  bool vec = (g.HW & 3) == 0;
+  for (int i = 0; i < nptr; ++i)
+    if (ptrs[i] && ((uintptr_t)ptrs[i] & 15)) vec = false;
+  for (int budget : {kBnClSmallBytes, kBnClBigBytes}) {
+    const int64_t per = budget / (4 * arrays) / 4 * 4;  // elements per CTA, multiple of 4
+    const int64_t k = (M + per - 1) / per;
+    if (k > kBnClMaxCluster) continue;
+    int64_t chunk = (M + k - 1) / k;
+    chunk = (chunk + 3) / 4 * 4;
+    p->k = (int)k;
+    p->chunk = (int)chunk;
+    p->smem = (int)(chunk * 4 * arrays);
+    p->vec = vec;
+    return true;
+  }
+  return false;
+}
+
+// launch configuration of a cluster-resident kernel: grid (k, C), clusters (k, 1, 1)
+struct BnClusterLaunch {
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[1];
+  BnClusterLaunch(const BnCluster& p, int C, cudaStream_t s) {
+    cfg = cudaLaunchConfig_t{};
+    cfg.gridDim = dim3((unsigned)p.k, (unsigned)C, 1);
+    cfg.blockDim = dim3(kBnClThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)p.smem;
+    cfg.stream = s;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.k;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+};
+
+static int bn_fwd_cluster(const BnGeom& g, const BnCluster& p, const float* x, float* y, const float* gamma,
+                          const float* beta, float* running_mean, float* running_var, double momentum, double eps,
+                          float* save_mean, float* save_invstd, cudaStream_t s) {
+  static std::atomic<uint64_t> attr_done{0};
+  if (first_on_device(attr_done))
+    PVB2_CUDA_TRY(cudaFuncSetAttribute(bn_fwd_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBnClBigBytes));
+  BnClusterLaunch L(p, (int)g.C, s);
+  PVB2_CUDA_TRY(cudaLaunchKernelEx(&L.cfg, bn_fwd_cluster_kernel, x, y, (int)g.N, (int)g.C, (int)g.HW, p.chunk,
+                                   p.vec ? 1 : 0, gamma, beta, running_mean, running_var, (float)momentum, (float)eps,
+                                   save_mean, save_invstd));
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+static int bn_bwd_cluster(const BnGeom& g, const BnCluster& p, const float* dy, const float* x, const float* mean,
+                          const float* invstd, const float* gamma, float* dx, float* dgamma, float* dbeta,
+                          cudaStream_t s) {
+  static std::atomic<uint64_t> attr_done{0};
+  if (first_on_device(attr_done))
+    PVB2_CUDA_TRY(cudaFuncSetAttribute(bn_bwd_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBnClBigBytes));
+  BnClusterLaunch L(p, (int)g.C, s);
+  PVB2_CUDA_TRY(cudaLaunchKernelEx(&L.cfg, bn_bwd_cluster_kernel, dy, x, mean, invstd, gamma, (int)g.N, (int)g.C,
+                                   (int)g.HW, p.chunk, p.vec ? 1 : 0, dx, dgamma, dbeta));
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
 // ------------------------------------------------------------- layer norm
 // one warp per row; the row is held in registers (N <= 32 * kLnMaxPerLane)
 constexpr int kLnMaxPerLane = 32;
@@ -479,10 +752,15 @@ int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma, const fl
   PVB2_CHECK_ARG(is_contiguous(y) && y->dtype == PVB2_F32, "batch_norm: output must be contiguous float32");
   BnGeom g = bn_geom(x);
   if (g.N * g.HW == 0 || g.C == 0) return PVB2_OK;
+  cudaStream_t s = as_stream(stream);
+  BnCluster cp;
+  const void* ptrs[2] = {x->data, y->data};
+  if (bn_cluster_plan(g, 1, ptrs, 2, &cp))
+    return bn_fwd_cluster(g, cp, (const float*)x->data, (float*)y->data, gamma, beta, running_mean, running_var,
+                          momentum, eps, save_mean, save_invstd, s);
   const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
   PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm: workspace too small (%zu < %zu)",
                  workspace_bytes, need);
-  cudaStream_t s = as_stream(stream);
   float* part = (float*)workspace;
   bn_stats_kernel<<<dim3((unsigned)g.C, (unsigned)g.splits), kBnThreads, 0, s>>>(
       (const float*)x->data, g.N, g.C, g.HW, g.planes_per, g.splits, part);
@@ -511,6 +789,11 @@ int pvb2_batch_norm_fwd_train_noalloc(const pvb2_tensor* x, const float* gamma, 
   PVB2_CHECK_ARG(is_contiguous(y) && y->dtype == PVB2_F32, "batch_norm: output must be contiguous float32");
   BnGeom g = bn_geom(x);
   if (g.N * g.HW == 0 || g.C == 0) return PVB2_OK;
+  BnCluster cp;
+  const void* ptrs[2] = {x->data, y->data};
+  if (bn_cluster_plan(g, 1, ptrs, 2, &cp))  // needs no scratch at all
+    return bn_fwd_cluster(g, cp, (const float*)x->data, (float*)y->data, gamma, beta, running_mean, running_var,
+                          momentum, eps, save_mean, save_invstd, as_stream(stream));
   const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
   PVB2_CHECK_ARG(need <= sizeof(g_bn_scratch),
                  "batch_norm_noalloc: %lld channels need %zu bytes of partials, more than the %zu-byte scratch; "
@@ -557,14 +840,19 @@ int pvb2_batch_norm_bwd(const pvb2_tensor* dy, const pvb2_tensor* x, const float
     // by the caller into running_var (var + eps passed as var, eps = 0).
     PVB2_CHECK_ARG(false, "batch_norm_backward: use pvb2_batch_norm_bwd_eval for eval mode");
   }
-  const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
-  PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm_backward: workspace too small");
-  float* part = (float*)workspace;
   if (g.N * g.HW == 0) {
     if (dgamma) PVB2_CUDA_TRY(cudaMemsetAsync(dgamma, 0, g.C * sizeof(float), s));
     if (dbeta) PVB2_CUDA_TRY(cudaMemsetAsync(dbeta, 0, g.C * sizeof(float), s));
     return PVB2_OK;
   }
+  BnCluster cp;
+  const void* ptrs[3] = {dy->data, x->data, dx ? dx->data : nullptr};
+  if (bn_cluster_plan(g, 2, ptrs, 3, &cp))
+    return bn_bwd_cluster(g, cp, (const float*)dy->data, (const float*)x->data, mean, invstd, gamma,
+                          dx ? (float*)dx->data : nullptr, dgamma, dbeta, s);
+  const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
+  PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm_backward: workspace too small");
+  float* part = (float*)workspace;
   bn_bwd_reduce_kernel<<<dim3((unsigned)g.C, (unsigned)g.splits), kBnThreads, 0, s>>>(
       (const float*)dy->data, (const float*)x->data, mean, g.N, g.C, g.HW, g.planes_per, g.splits, part);
   PVB2_LAUNCH_CHECK();

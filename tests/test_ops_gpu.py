@@ -286,6 +286,28 @@ def test_batch_norm_module(ocl):
     assert _diff(ref(x), bn(x.to(DEV))) < 1e-5
 
 
+BN_SHAPES = [
+    [3, 7, 7, 7],       # one CTA per channel, 49-pixel planes (scalar loads)
+    [16, 8, 56, 56],    # channel split over a 2-CTA cluster
+    [64, 4, 56, 56],    # 8-CTA clusters; the backward needs the one-CTA-per-SM budget
+    [32, 4, 45, 45],    # odd plane size across a cluster
+    [2, 3, 512, 512],   # channels too large for a cluster: two-pass kernels
+]
+
+
+@pytest.mark.parametrize("shape", BN_SHAPES, ids=["x".join(map(str, s)) for s in BN_SHAPES])
+def test_batch_norm_shapes(ocl, shape):
+    C = shape[1]
+    check_module([(shape, -1)], nn.BatchNorm2d(C), paramgen=torch.randn, tol=2e-4, rel=2e-5)
+    ref, bn = nn.BatchNorm2d(C), nn.BatchNorm2d(C).to(DEV)
+    x = _inputs([(shape, -1)], 3)[0] * 3 + 1
+    for _ in range(2):
+        ref(x)
+        bn(x.to(DEV))
+    assert _diff(ref.running_mean, bn.running_mean) < 1e-5
+    assert _diff(ref.running_var, bn.running_var) < 1e-4
+
+
 def test_masked_select_nonzero_print(ocl):
     g = _gen(11)
     x = torch.randn(7, 33, generator=g)
