@@ -288,9 +288,11 @@ __global__ void bn_bwd_eval_kernel(const float* __restrict__ dy, const float* __
 // HBM once: grid (k, C) with clusters of k CTAs along x, CTA r of channel c
 // holds elements [r*chunk, (r+1)*chunk) of the channel's (n, hw) range in
 // shared memory, partial sums meet through distributed shared memory, and
-// the output is written from the resident copy.  The forward computes the
-// variance in two passes over shared memory (mean first, then squared
-// deviations), so no shift is needed.
+// the output is written from the resident copy.  Each CTA reduces its own
+// elements first (the forward in two passes over shared memory: mean, then
+// squared deviations), one cluster barrier publishes the per-CTA results,
+// and every CTA combines them in double in rank order (the forward with
+// Chan's pairwise formula for (count, mean, M2)).
 constexpr int kBnClThreads = 512;
 constexpr int kBnClMaxCluster = 8;
 constexpr int kBnClSmallBytes = 110 * 1024;  // two CTAs per SM
@@ -309,27 +311,55 @@ __device__ __forceinline__ float block_allsum(float v, float* red) {
   return t;
 }
 
-// cluster-wide sum of one float per CTA, combined in double in rank order
-__device__ __forceinline__ double cluster_sum(cg::cluster_group& cl, float* slot) {
-  double t = 0.0;
-  const int k = (int)cl.num_blocks();
-  for (int q = 0; q < k; ++q) t += (double)*cl.map_shared_rank(slot, q);
-  return t;
-}
+// split cluster barrier: arrive (release) once this CTA's distributed
+// shared-memory reads are done, wait (acquire) before leaving
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
-// copy this CTA's elements of channel c into shared memory
+// Position of element e = n*HW + i of one channel, advanced by a fixed step
+// without dividing in the loop.
+struct ChanWalk {
+  int n, i, dn, di, HW;
+  __device__ __forceinline__ ChanWalk(int e0, int step, int hw) : HW(hw) {
+    n = e0 / hw;
+    i = e0 - n * hw;
+    dn = step / hw;
+    di = step - dn * hw;
+  }
+  __device__ __forceinline__ void next() {
+    i += di;
+    n += dn;
+    if (i >= HW) {
+      i -= HW;
+      ++n;
+    }
+  }
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Start asynchronous copies of this CTA's elements [start, end) of channel c
+// into shared memory (16-byte copies when vec: HW % 4 == 0 and aligned).
+// The caller waits with cp_async_wait_all + __syncthreads.
 __device__ __forceinline__ void bn_cl_load(const float* __restrict__ src, float* __restrict__ dst, int start, int end,
                                            int HW, int64_t nstride, bool vec) {
+  const int vw = vec ? 4 : 1;
+  const int step = vw * blockDim.x;
+  int e = start + vw * threadIdx.x;
+  if (e >= end) return;
+  ChanWalk w(e, step, HW);
   if (vec) {
-    for (int e = start + 4 * threadIdx.x; e < end; e += 4 * blockDim.x) {
-      const int n = e / HW, i = e - n * HW;
-      *reinterpret_cast<float4*>(dst + (e - start)) = __ldg(reinterpret_cast<const float4*>(src + n * nstride + i));
-    }
+    for (; e < end; e += step, w.next()) cp_async16(dst + (e - start), src + w.n * nstride + w.i);
   } else {
-    for (int e = start + threadIdx.x; e < end; e += blockDim.x) {
-      const int n = e / HW, i = e - n * HW;
-      dst[e - start] = __ldg(src + n * nstride + i);
-    }
+    for (; e < end; e += step, w.next()) cp_async4(dst + (e - start), src + w.n * nstride + w.i);
   }
 }
 
@@ -340,68 +370,85 @@ __global__ void __launch_bounds__(kBnClThreads) bn_fwd_cluster_kernel(
     float* __restrict__ save_invstd) {
   extern __shared__ __align__(16) float sx[];
   __shared__ float red[32];
-  __shared__ float cl_part[2];
+  __shared__ float cl_part[3];  // count, mean, M2 of this CTA's elements
   __shared__ float s_coef[2];
   cg::cluster_group cl = cg::this_cluster();
-  const int r = (int)cl.block_rank();
+  const int r = (int)cl.block_rank(), k = (int)cl.num_blocks();
   const int c = blockIdx.y;
   const int M = N * HW;
   const int start = r * chunk, end = min(M, start + chunk), len = max(0, end - start);
   const int64_t nstride = (int64_t)C * HW;
   bn_cl_load(x + (int64_t)c * HW, sx, start, end, HW, nstride, vec != 0);
+  cp_async_wait_all();
   __syncthreads();
+  // this CTA's mean and sum of squared deviations: two passes over shared memory
   float s = 0.f;
   for (int i = threadIdx.x; i < len; i += blockDim.x) s += sx[i];
-  s = block_allsum(s, red);
-  if (threadIdx.x == 0) cl_part[0] = s;
-  cl.sync();
-  const float mean = (float)(cluster_sum(cl, &cl_part[0]) / (double)M);
+  const float lmean = len ? block_allsum(s, red) / (float)len : 0.f;
   float s2 = 0.f;
   for (int i = threadIdx.x; i < len; i += blockDim.x) {
-    const float d = sx[i] - mean;
+    const float d = sx[i] - lmean;
     s2 += d * d;
   }
   s2 = block_allsum(s2, red);
-  if (threadIdx.x == 0) cl_part[1] = s2;
+  if (threadIdx.x == 0) {
+    cl_part[0] = (float)len;
+    cl_part[1] = lmean;
+    cl_part[2] = s2;
+  }
   cl.sync();
   if (threadIdx.x == 0) {
-    const double count = (double)M;
-    const double var = cluster_sum(cl, &cl_part[1]) / count;
+    // Chan's pairwise combination, in double, in rank order
+    double n = 0.0, mean = 0.0, m2 = 0.0;
+    for (int q = 0; q < k; ++q) {
+      const float* pq = cl.map_shared_rank(cl_part, q);
+      const double nq = pq[0];
+      if (nq == 0.0) continue;
+      const double nn = n + nq, d = (double)pq[1] - mean;
+      mean += d * nq / nn;
+      m2 += (double)pq[2] + d * d * n * nq / nn;
+      n = nn;
+    }
+    const double var = m2 / n;
     const float invstd = (float)(1.0 / sqrt(var + (double)eps));
+    const float meanf = (float)mean;
     const float g = gamma ? gamma[c] : 1.f;
     const float b = beta ? beta[c] : 0.f;
     const float a = invstd * g;
     s_coef[0] = a;
-    s_coef[1] = b - mean * a;
+    s_coef[1] = b - meanf * a;
     if (r == 0) {
-      if (save_mean) save_mean[c] = mean;
+      if (save_mean) save_mean[c] = meanf;
       if (save_invstd) save_invstd[c] = invstd;
-      if (running_mean) running_mean[c] = (1.f - momentum) * running_mean[c] + momentum * mean;
+      if (running_mean) running_mean[c] = (1.f - momentum) * running_mean[c] + momentum * meanf;
       if (running_var) {
-        const double unbiased = count > 1.0 ? var * count / (count - 1.0) : var;
+        const double unbiased = n > 1.0 ? var * n / (n - 1.0) : var;
         running_var[c] = (1.f - momentum) * running_var[c] + momentum * (float)unbiased;
       }
     }
   }
-  cl.sync();  // peers are done reading cl_part; s_coef is visible block-wide
+  cluster_arrive();  // this CTA is done reading its peers' statistics
+  __syncthreads();
   const float a = s_coef[0], b = s_coef[1];
   float* yc = y + (int64_t)c * HW;
-  if (vec) {
-    for (int e = start + 4 * threadIdx.x; e < end; e += 4 * blockDim.x) {
-      const int n = e / HW, i = e - n * HW;
-      float4 v = *reinterpret_cast<const float4*>(sx + (e - start));
-      v.x = fmaf(v.x, a, b);
-      v.y = fmaf(v.y, a, b);
-      v.z = fmaf(v.z, a, b);
-      v.w = fmaf(v.w, a, b);
-      *reinterpret_cast<float4*>(yc + n * nstride + i) = v;
-    }
-  } else {
-    for (int e = start + threadIdx.x; e < end; e += blockDim.x) {
-      const int n = e / HW, i = e - n * HW;
-      yc[n * nstride + i] = fmaf(sx[e - start], a, b);
+  const int vw = vec ? 4 : 1, step = vw * blockDim.x;
+  int e = start + vw * threadIdx.x;
+  if (e < end) {
+    ChanWalk w(e, step, HW);
+    if (vec) {
+      for (; e < end; e += step, w.next()) {
+        float4 v = *reinterpret_cast<const float4*>(sx + (e - start));
+        v.x = fmaf(v.x, a, b);
+        v.y = fmaf(v.y, a, b);
+        v.z = fmaf(v.z, a, b);
+        v.w = fmaf(v.w, a, b);
+        *reinterpret_cast<float4*>(yc + w.n * nstride + w.i) = v;
+      }
+    } else {
+      for (; e < end; e += step, w.next()) yc[w.n * nstride + w.i] = fmaf(sx[e - start], a, b);
     }
   }
+  cluster_wait();  // no CTA leaves while a peer may still read its statistics
 }
 
 __global__ void __launch_bounds__(kBnClThreads) bn_bwd_cluster_kernel(
@@ -415,13 +462,14 @@ __global__ void __launch_bounds__(kBnClThreads) bn_bwd_cluster_kernel(
   __shared__ float cl_part[2];
   __shared__ float s_coef[3];
   cg::cluster_group cl = cg::this_cluster();
-  const int r = (int)cl.block_rank();
+  const int r = (int)cl.block_rank(), k = (int)cl.num_blocks();
   const int c = blockIdx.y;
   const int M = N * HW;
   const int start = r * chunk, end = min(M, start + chunk), len = max(0, end - start);
   const int64_t nstride = (int64_t)C * HW;
   bn_cl_load(dy + (int64_t)c * HW, sdy, start, end, HW, nstride, vec != 0);
   bn_cl_load(x + (int64_t)c * HW, sx, start, end, HW, nstride, vec != 0);
+  cp_async_wait_all();
   __syncthreads();
   const float m = mean[c];
   float s_dy = 0.f, s_dot = 0.f;
@@ -438,8 +486,12 @@ __global__ void __launch_bounds__(kBnClThreads) bn_bwd_cluster_kernel(
   }
   cl.sync();
   if (threadIdx.x == 0) {
-    const double sdy_all = cluster_sum(cl, &cl_part[0]);
-    const double sdot_all = cluster_sum(cl, &cl_part[1]);
+    double sdy_all = 0.0, sdot_all = 0.0;
+    for (int q = 0; q < k; ++q) {
+      const float* pq = cl.map_shared_rank(cl_part, q);
+      sdy_all += (double)pq[0];
+      sdot_all += (double)pq[1];
+    }
     const double count = (double)M;
     const float is = invstd[c];
     s_coef[0] = (float)(sdy_all / count);              // mean of dy
@@ -450,28 +502,33 @@ __global__ void __launch_bounds__(kBnClThreads) bn_bwd_cluster_kernel(
       if (dbeta) dbeta[c] = (float)sdy_all;
     }
   }
-  cl.sync();
-  if (!dx) return;
-  const float gm = s_coef[0], kk = s_coef[1], mul = s_coef[2];
-  float* dxc = dx + (int64_t)c * HW;
-  if (vec) {
-    for (int e = start + 4 * threadIdx.x; e < end; e += 4 * blockDim.x) {
-      const int n = e / HW, i = e - n * HW;
-      const float4 g = *reinterpret_cast<const float4*>(sdy + (e - start));
-      const float4 v = *reinterpret_cast<const float4*>(sx + (e - start));
-      float4 o;
-      o.x = (g.x - gm - (v.x - m) * kk) * mul;
-      o.y = (g.y - gm - (v.y - m) * kk) * mul;
-      o.z = (g.z - gm - (v.z - m) * kk) * mul;
-      o.w = (g.w - gm - (v.w - m) * kk) * mul;
-      *reinterpret_cast<float4*>(dxc + n * nstride + i) = o;
-    }
-  } else {
-    for (int e = start + threadIdx.x; e < end; e += blockDim.x) {
-      const int n = e / HW, i = e - n * HW;
-      dxc[n * nstride + i] = (sdy[e - start] - gm - (sx[e - start] - m) * kk) * mul;
+  cluster_arrive();  // this CTA is done reading its peers' sums
+  __syncthreads();
+  if (dx) {
+    const float gm = s_coef[0], kk = s_coef[1], mul = s_coef[2];
+    float* dxc = dx + (int64_t)c * HW;
+    const int vw = vec ? 4 : 1, step = vw * blockDim.x;
+    int e = start + vw * threadIdx.x;
+    if (e < end) {
+      ChanWalk w(e, step, HW);
+      if (vec) {
+        for (; e < end; e += step, w.next()) {
+          const float4 g = *reinterpret_cast<const float4*>(sdy + (e - start));
+          const float4 v = *reinterpret_cast<const float4*>(sx + (e - start));
+          float4 o;
+          o.x = (g.x - gm - (v.x - m) * kk) * mul;
+          o.y = (g.y - gm - (v.y - m) * kk) * mul;
+          o.z = (g.z - gm - (v.z - m) * kk) * mul;
+          o.w = (g.w - gm - (v.w - m) * kk) * mul;
+          *reinterpret_cast<float4*>(dxc + w.n * nstride + w.i) = o;
+        }
+      } else {
+        for (; e < end; e += step, w.next())
+          dxc[w.n * nstride + w.i] = (sdy[e - start] - gm - (sx[e - start] - m) * kk) * mul;
+      }
     }
   }
+  cluster_wait();  // no CTA leaves while a peer may still read its sums
 }
 
 struct BnCluster {
