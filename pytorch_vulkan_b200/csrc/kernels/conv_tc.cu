@@ -24,9 +24,10 @@
 //               residue class mod the stride receive a fixed subset of taps, so
 //               each phase is a stride-1 correlation over dY (tap offsets in a
 //               table, weights packed per phase) written to dX with strides.
-//     small C   (the 3-channel stem): the S filter columns fold into channels,
-//               Xf[n, h, q, (s, c)] = X[n, c, h, q*sw + s*dw - pw], so a 7x7/2
-//               conv on 3 channels runs as 7x1 on 21 (padded to 24).
+//     small C   (the 3-channel stem): im2col columns Xcol[n, p, q, (c, r, s)]
+//               (147 for a 7x7 filter on 3 channels, padded to 148) make the
+//               forward a 1x1 GEMM with K = 148 and the weight gradient a
+//               GEMM of Xcol (MN-major) against dY read NCHW (K-major).
 //     wgrad     dW[k, c, r, s] = sum_pix dYnhwc[pix, k] * Xnhwc[shift_rs(pix), c]
 //               GEMM M = 128 output channels, N = BN input channels, K = 32-pixel
 //               blocks (MN-major A and B), one tap per tile.
@@ -59,6 +60,7 @@ enum ConvMode : int {
   kPwDgrad = 2,   // 1x1 stride-1 dgrad: A = dY NCHW slots (MN-major), B = W[K][C] read along C (MN-major)
   kWgrad = 3,     // weight gradient over channels-last tap boxes (A and B MN-major)
   kPwWgrad = 4,   // 1x1 stride-1 weight gradient: A = dY, B = X, both NCHW, K-major along pixels
+  kImWgrad = 5,   // weight gradient over im2col columns: A = Xcol[n][pix][j] (MN-major), B = dY NCHW (K-major)
 };
 
 // how a forward-shaped launch writes its output
@@ -106,9 +108,9 @@ template <int BN, int MODE>
 __global__ void __launch_bounds__(cThreads, 1)
     conv_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, ConvTcArgs a) {
-  constexpr bool WG = MODE == kWgrad || MODE == kPwWgrad;
+  constexpr bool WG = MODE == kWgrad || MODE == kPwWgrad || MODE == kImWgrad;
   constexpr bool PW = MODE == kPwFwd || MODE == kPwDgrad;
-  constexpr bool A_MN = MODE == kPwFwd || MODE == kPwDgrad || MODE == kWgrad;
+  constexpr bool A_MN = MODE == kPwFwd || MODE == kPwDgrad || MODE == kWgrad || MODE == kImWgrad;
   constexpr bool B_MN = MODE == kPwDgrad || MODE == kWgrad;
   using L = ConvSmem<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -229,7 +231,7 @@ __global__ void __launch_bounds__(cThreads, 1)
               tma_load_4d(sb + j * 32 * cBK * 4, &tmB, &full[s_], ctile * BN + 32 * j, q0 * a.sw + a.tap_w[s],
                           p0 * a.sh + a.tap_h[r], n0);
           }
-        } else {  // kPwWgrad: K blocks are (image, 32-pixel slot) pairs
+        } else {  // kPwWgrad / kImWgrad: K blocks are (image, 32-pixel slot) pairs
           int sp, km, ctile, rs;
           wg_tile(tile, sp, km, ctile, rs);
           int kb0, kb1;
@@ -241,7 +243,12 @@ __global__ void __launch_bounds__(cThreads, 1)
             const int n = kb / a.hwb, hw0 = (kb - n * a.hwb) * 32;
             uint8_t* sa = smem + s_ * L::STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
-            tma_load_3d(sa, &tmA, &full[s_], hw0, km * cBM, n);
+            if (MODE == kPwWgrad) {
+              tma_load_3d(sa, &tmA, &full[s_], hw0, km * cBM, n);
+            } else {
+#pragma unroll
+              for (int j = 0; j < cBM / 32; ++j) tma_load_3d(sa + j * 32 * cBK * 4, &tmA, &full[s_], km * cBM + 32 * j, hw0, n);
+            }
             tma_load_3d(sa + L::A_BYTES, &tmB, &full[s_], hw0, ctile * BN, n);
           }
         }
@@ -337,14 +344,16 @@ __global__ void __launch_bounds__(cThreads, 1)
                 if (k < a.Kout) obase[(int64_t)k * a.ok] = a.bias ? v[j] + a.bias[k] : v[j];
               }
             }
-          } else {
+          } else if (bvalid && k0 < a.Kout) {  // warp-uniform: this chunk has output to store
             if (a.bias) {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
                 if (k0 + j < a.Kout) v[j] += a.bias[k0 + j];
             }
+            // boxes alternate per issued store, so the store that last used
+            // this box is the one before the most recent: wait until it has read it
             float* st = stage + (echunk & 1) * 1024;
-            if (lane == 0) bulk_wait_read<1>();  // the store that used this box two chunks ago has read it
+            if (lane == 0) bulk_wait_read<1>();
             __syncwarp();
             if (a.epi == kEpiFlat) {
               const int qq = lane % a.bw, pp = lane / a.bw, pitch = a.ebp * a.Q;
@@ -358,7 +367,7 @@ __global__ void __launch_bounds__(cThreads, 1)
             }
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0 && bvalid && k0 < a.Kout) {
+            if (lane == 0) {
               if (a.epi == kEpiBox) tma_store_4d(&tmC, st, bx, by, k0, bn);
               else tma_store_3d(&tmC, st, bx, k0, bn);
               bulk_commit();
@@ -460,55 +469,69 @@ __global__ void pack_w_phase_kernel(const float* __restrict__ w, float* __restri
   }
 }
 
-// small-C fold: Xf[n, h, q, s*C + c] = X[n, c, h, q*sw + s*dw - pw] (0 outside / in pad channels)
-__global__ void fold_cols_kernel(const float* __restrict__ x, float* __restrict__ xf, int N, int C, int H, int W,
-                                 int Q, int S, int Cf, int sw, int dw, int pw) {
-  const int64_t total = (int64_t)N * H * Q * Cf;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int cf = (int)(i % Cf);
-    const int q = (int)((i / Cf) % Q);
-    const int h = (int)((i / ((int64_t)Cf * Q)) % H);
-    const int64_t n = i / ((int64_t)Cf * Q * H);
-    float v = 0.f;
-    if (cf < S * C) {
-      const int s_ = cf / C, c = cf % C;
-      const int w = q * sw + s_ * dw - pw;
-      if (w >= 0 && w < W) v = x[((n * C + c) * H + h) * W + w];
+// small-C convolutions as a GEMM over im2col columns:
+// Xcol[n, p, q, j] = X[n, c, p*sh - ph + r*dh, q*sw - pw + s*dw] with j = (c*R + r)*S + s
+// (W's own flattening; 0 outside the image and for j >= C*R*S up to Kc).
+// grid (P, N); per-j source offsets in shared memory, float4 stores.
+constexpr int kIm2colMaxK = 256;
+__global__ void im2col_kernel(const float* __restrict__ x, float* __restrict__ xcol, int C, int H, int W, int P,
+                              int Q, int R, int S, int Kc, int sh, int sw, int ph, int pw, int dh, int dw) {
+  __shared__ int jc[kIm2colMaxK], jr[kIm2colMaxK], js[kIm2colMaxK];
+  const int crs = C * R * S;
+  for (int j = threadIdx.x; j < Kc; j += blockDim.x) {
+    const int c = j / (R * S), rs = j - c * R * S;
+    jc[j] = j < crs ? c : -1;
+    jr[j] = (rs / S) * dh - ph;
+    js[j] = (rs % S) * dw - pw;
+  }
+  __syncthreads();
+  const int p = blockIdx.x;
+  const int64_t n = blockIdx.y;
+  const float* xn = x + n * C * H * W;
+  float4* row = reinterpret_cast<float4*>(xcol + ((n * P + p) * Q) * (int64_t)Kc);
+  const int total4 = Q * Kc / 4, step = 4 * blockDim.x;
+  int t4 = threadIdx.x;
+  if (t4 >= total4) return;
+  int q = (4 * t4) / Kc, j0 = 4 * t4 - q * Kc;
+  const int dq = step / Kc, dj = step - dq * Kc;
+  for (; t4 < total4; t4 += blockDim.x) {
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = j0 + u;
+      const int c = jc[j];
+      const int h = p * sh + jr[j], w = q * sw + js[j];
+      v[u] = (c >= 0 && h >= 0 && h < H && w >= 0 && w < W) ? __ldg(xn + ((int64_t)c * H + h) * W + w) : 0.f;
     }
-    xf[i] = v;
+    row[t4] = make_float4(v[0], v[1], v[2], v[3]);
+    j0 += dj;
+    q += dq;
+    if (j0 >= Kc) {
+      j0 -= Kc;
+      ++q;
+    }
   }
 }
 
-// fold weights: Wf[k][r][s*C + c] = W[k][c][r][s]
-__global__ void pack_w_fold_kernel(const float* __restrict__ w, float* __restrict__ wf, int K, int C, int R, int S,
-                                   int Cf) {
-  const int64_t total = (int64_t)K * R * Cf;
+// W [K][crs] -> Wp [K][Kc], zero columns crs..Kc-1
+__global__ void pack_w_rows_kernel(const float* __restrict__ w, float* __restrict__ wp, int K, int crs, int Kc) {
+  const int64_t total = (int64_t)K * Kc;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int cf = (int)(i % Cf);
-    const int r = (int)((i / Cf) % R);
-    const int64_t k = i / ((int64_t)Cf * R);
-    float v = 0.f;
-    if (cf < S * C) {
-      const int s_ = cf / C, c = cf % C;
-      v = w[((k * C + c) * R + r) * S + s_];
-    }
-    wf[i] = v;
+    const int j = (int)(i % Kc);
+    const int64_t k = i / Kc;
+    wp[i] = j < crs ? w[k * crs + j] : 0.f;
   }
 }
 
-// fold wgrad: dW[k][c][r][s] = sum_sp part[sp][k][s*C + c][r]
-__global__ void unfold_wgrad_kernel(const float* __restrict__ part, int splits, int K, int C, int R, int S, int Cf,
-                                    float* __restrict__ dw) {
-  const int64_t total = (int64_t)K * C * R * S;
-  const int64_t per_split = (int64_t)K * Cf * R;
+// dW[k][j] = sum_sp part[sp][j][k] for j < crs (im2col weight gradient partials are [Kc][K])
+__global__ void sum_transpose_kernel(const float* __restrict__ part, int splits, int K, int crs, int Kc,
+                                     float* __restrict__ dw) {
+  const int64_t total = (int64_t)K * crs;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int s_ = (int)(i % S);
-    const int r = (int)((i / S) % R);
-    const int c = (int)((i / ((int64_t)S * R)) % C);
-    const int64_t k = i / ((int64_t)S * R * C);
-    const int64_t src = (k * Cf + (s_ * C + c)) * R + r;
+    const int j = (int)(i % crs);
+    const int64_t k = i / crs;
     float acc = 0.f;
-    for (int sp = 0; sp < splits; ++sp) acc += part[sp * per_split + src];
+    for (int sp = 0; sp < splits; ++sp) acc += part[((int64_t)sp * Kc + j) * K + k];
     dw[i] = acc;
   }
 }
@@ -552,9 +575,14 @@ static bool pointwise(const pvb2_conv2d_desc* d) {
          ((int64_t)d->H * d->W) % 4 == 0 && d->C % 4 == 0 && d->K % 4 == 0;
 }
 
-// fold the S filter columns into channels when the input has few channels
-static bool use_fold(const pvb2_conv2d_desc* d) { return d->C <= 8 && d->S * d->C <= 32; }
-static int fold_channels(const pvb2_conv2d_desc* d) { return round4(d->S * d->C); }
+// Few input channels and a spatial filter (the 3-channel stem): one GEMM
+// over im2col columns instead of R*S taps of a few channels each.  The
+// weight-gradient map needs 16-byte output-plane rows (P*Q % 4 == 0).
+static int im2col_channels(const pvb2_conv2d_desc* d) { return round4(d->C * d->R * d->S); }
+static bool use_im2col(const pvb2_conv2d_desc* d) {
+  return d->C <= 8 && d->R * d->S > 1 && im2col_channels(d) <= kIm2colMaxK && ((int64_t)d->P * d->Q) % 4 == 0 &&
+         d->N <= 65535 && d->P <= 65535;
+}
 
 struct Taps {
   int nr, ns;
@@ -807,6 +835,51 @@ static int run_pw_wgrad(const float* dy, const float* x, int N, int C, int K, in
   return launch_bn<kPwWgrad>(p.BN, ma, mb, mc, a, s);
 }
 
+// im2col weight-gradient plan: GEMM rows = Kc im2col columns, GEMM columns = K
+static WgPlan plan_im_wg(int N, int K, int Kc, int64_t pq) {
+  WgPlan w;
+  w.bw = 32; w.bh = 1; w.bni = 1;
+  w.BN = bn_for(K);
+  w.ct = (K + w.BN - 1) / w.BN;
+  w.kt = (Kc + cBM - 1) / cBM;
+  w.total_kb = N * (int)((pq + 31) / 32);
+  plan_splits(w, 1);
+  return w;
+}
+
+// im2col weight gradient into partials [splits][Kc][K]; xcol: [N][pq][Kc], dy: NCHW [N][K][pq]
+static int run_im_wgrad(const float* xcol, int Kc, const float* dy, int N, int K, int64_t pq, const WgPlan& p,
+                        float* part, cudaStream_t s) {
+  CUtensorMap ma, mb, mc;
+  memset(&mc, 0, sizeof(mc));
+  uint64_t dims[3] = {(uint64_t)Kc, (uint64_t)pq, (uint64_t)N};
+  uint64_t str[2] = {(uint64_t)Kc * 4, (uint64_t)pq * Kc * 4};
+  uint32_t box[3] = {32, 32, 1};
+  PVB2_TRY(encode_tiled(&ma, 3, xcol, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+  PVB2_TRY(nchw_map(&mb, dy, N, K, pq, p.BN, CU_TENSOR_MAP_SWIZZLE_128B));
+  ConvTcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.N = N; a.Cin = K; a.Cp = K; a.Kout = Kc; a.P = 1; a.Q = (int)pq; a.R = 1; a.S = 1;
+  a.sh = a.sw = 1;
+  a.kt = p.kt;
+  a.ct = p.ct;
+  a.splits = p.splits;
+  a.kb_per_split = p.kb_per;
+  a.total_kb = p.total_kb;
+  a.hwb = (int)((pq + 31) / 32);
+  a.out = part;
+  a.tiles = a.kt * a.ct * a.splits;
+  return launch_bn<kImWgrad>(p.BN, ma, mb, mc, a, s);
+}
+
+static int im2col(const pvb2_conv2d_desc* d, const float* x, float* xcol, cudaStream_t s) {
+  const dim3 grid((unsigned)d->P, (unsigned)d->N);
+  im2col_kernel<<<grid, 256, 0, s>>>(x, xcol, d->C, d->H, d->W, d->P, d->Q, d->R, d->S, im2col_channels(d),
+                                     d->stride_h, d->stride_w, d->pad_h, d->pad_w, d->dil_h, d->dil_w);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
 static Taps fwd_taps(const pvb2_conv2d_desc* d) {
   Taps t;
   t.nr = d->R;
@@ -815,13 +888,6 @@ static Taps fwd_taps(const pvb2_conv2d_desc* d) {
     t.h[i] = i * d->dil_h - d->pad_h;
     t.w[i] = i * d->dil_w - d->pad_w;
   }
-  return t;
-}
-
-static Taps fold_taps(const pvb2_conv2d_desc* d) {
-  Taps t = fwd_taps(d);
-  t.ns = 1;
-  for (int i = 0; i < kMaxTaps; ++i) t.w[i] = 0;
   return t;
 }
 
@@ -834,10 +900,10 @@ static Layout fwd_layout(const pvb2_conv2d_desc* d) {
   Layout l;
   l.a = l.b = l.c = l.total = 0;
   if (pointwise(d)) return l;
-  if (use_fold(d)) {
-    const int Cf = fold_channels(d);
-    l.b = align256((size_t)d->N * d->H * d->Q * Cf * 4);
-    l.total = l.b + align256((size_t)d->K * d->R * Cf * 4);
+  if (use_im2col(d)) {
+    const int Kc = im2col_channels(d);
+    l.b = align256((size_t)d->N * d->P * d->Q * Kc * 4);
+    l.total = l.b + align256((size_t)d->K * Kc * 4);
   } else {
     const int Cp = round4(d->C);
     l.b = align256((size_t)d->N * d->H * d->W * Cp * 4);
@@ -867,17 +933,23 @@ static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
     l.total = p.splits > 1 ? align256((size_t)p.splits * d->K * d->C * 4) : 0;
     return l;
   }
+  if (use_im2col(d)) {
+    const int Kc = im2col_channels(d);
+    WgPlan p = plan_im_wg(d->N, d->K, Kc, (int64_t)d->P * d->Q);
+    if (plan) *plan = p;
+    l.c = align256((size_t)d->N * d->P * d->Q * Kc * 4);                     // im2col columns, then partials
+    l.total = l.c + align256((size_t)p.splits * Kc * d->K * 4);
+    return l;
+  }
   const int Kp = round4(d->K);
-  const bool fold = use_fold(d);
-  const int Cx = fold ? fold_channels(d) : round4(d->C);
-  const int Wx = fold ? d->Q : d->W;
-  const int taps = fold ? d->R : d->R * d->S;
-  WgPlan p = plan_wg(d->N, d->K, fold ? Cx : d->C, d->P, d->Q, taps);
+  const int Cx = round4(d->C);
+  const int taps = d->R * d->S;
+  WgPlan p = plan_wg(d->N, d->K, d->C, d->P, d->Q, taps);
   if (plan) *plan = p;
-  l.a = 0;                                                                   // x channels-last (or folded)
-  l.b = align256((size_t)d->N * d->H * Wx * Cx * 4);                         // dy channels-last
+  l.a = 0;                                                                   // x channels-last
+  l.b = align256((size_t)d->N * d->H * d->W * Cx * 4);                       // dy channels-last
   l.c = l.b + align256((size_t)d->N * d->P * d->Q * Kp * 4);                 // partials
-  l.total = l.c + align256((size_t)p.splits * d->K * (fold ? Cx : d->C) * taps * 4);
+  l.total = l.c + align256((size_t)p.splits * d->K * d->C * taps * 4);
   return l;
 }
 
@@ -903,17 +975,17 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
   if (!ws || ws_bytes < l.total) return PVB2_OK;  // not enough scratch: exact path
   float* act = (float*)((char*)ws + l.a);
   float* wp = (float*)((char*)ws + l.b);
-  if (use_fold(d)) {
-    const int Cf = fold_channels(d);
-    const int64_t n1 = (int64_t)d->N * d->H * d->Q * Cf;
-    fold_cols_kernel<<<grid_for(n1, 256), 256, 0, s>>>(x, act, d->N, d->C, d->H, d->W, d->Q, d->S, Cf, d->stride_w,
-                                                        d->dil_w, d->pad_w);
+  if (use_im2col(d)) {
+    const int Kc = im2col_channels(d);
+    PVB2_TRY(im2col(d, x, act, s));
+    const int64_t n2 = (int64_t)d->K * Kc;
+    pack_w_rows_kernel<<<grid_for(n2, 256), 256, 0, s>>>(w, wp, d->K, d->C * d->R * d->S, Kc);
     PVB2_LAUNCH_CHECK();
-    const int64_t n2 = (int64_t)d->K * d->R * Cf;
-    pack_w_fold_kernel<<<grid_for(n2, 256), 256, 0, s>>>(w, wp, d->K, d->C, d->R, d->S, Cf);
-    PVB2_LAUNCH_CHECK();
-    PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, Cf, d->H, d->Q, d->K, fold_taps(d), d->P, d->Q, d->stride_h, 1, 0,
-                          (int64_t)d->K * pq, pq, d->Q, 1, s));
+    Taps t;
+    memset(&t, 0, sizeof(t));
+    t.nr = t.ns = 1;
+    PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, Kc, d->P, d->Q, d->K, t, d->P, d->Q, 1, 1, 0, (int64_t)d->K * pq, pq,
+                          d->Q, 1, s));
   } else {
     const int Cp = round4(d->C);
     PVB2_TRY(to_nhwc(x, act, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
@@ -1031,32 +1103,31 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
     return PVB2_OK;
   }
   if (!ws || ws_bytes < l.total) return PVB2_OK;
+  if (use_im2col(d)) {
+    const int Kc = im2col_channels(d);
+    float* xcol = (float*)ws;
+    float* part = (float*)((char*)ws + l.c);
+    PVB2_TRY(im2col(d, x, xcol, s));
+    PVB2_TRY(run_im_wgrad(xcol, Kc, dy, d->N, d->K, (int64_t)d->P * d->Q, p, part, s));
+    sum_transpose_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, d->K, d->C * d->R * d->S, Kc, dw);
+    PVB2_LAUNCH_CHECK();
+    *handled = true;
+    return PVB2_OK;
+  }
   const int Kp = round4(d->K);
   float* xn = (float*)((char*)ws + l.a);
   float* dyn = (float*)((char*)ws + l.b);
   float* part = (float*)((char*)ws + l.c);
   PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
-  if (use_fold(d)) {
-    const int Cf = fold_channels(d);
-    const int64_t n1 = (int64_t)d->N * d->H * d->Q * Cf;
-    fold_cols_kernel<<<grid_for(n1, 256), 256, 0, s>>>(x, xn, d->N, d->C, d->H, d->W, d->Q, d->S, Cf, d->stride_w,
-                                                        d->dil_w, d->pad_w);
+  const int Cp = round4(d->C);
+  PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
+  // one split: the partials layout [1][K][C][R*S] is dW itself
+  float* dst = p.splits > 1 ? part : dw;
+  PVB2_TRY(run_wgrad(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h, d->stride_w,
+                     p, dst, s));
+  if (p.splits > 1) {
+    sum_partials_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, wn, dw);
     PVB2_LAUNCH_CHECK();
-    PVB2_TRY(run_wgrad(dyn, Kp, xn, Cf, d->N, d->H, d->Q, d->P, d->Q, d->K, Cf, fold_taps(d), d->stride_h, 1, p, part,
-                       s));
-    unfold_wgrad_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, d->K, d->C, d->R, d->S, Cf, dw);
-    PVB2_LAUNCH_CHECK();
-  } else {
-    const int Cp = round4(d->C);
-    PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
-    // one split: the partials layout [1][K][C][R*S] is dW itself
-    float* dst = p.splits > 1 ? part : dw;
-    PVB2_TRY(run_wgrad(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h,
-                       d->stride_w, p, dst, s));
-    if (p.splits > 1) {
-      sum_partials_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, wn, dw);
-      PVB2_LAUNCH_CHECK();
-    }
   }
   *handled = true;
   return PVB2_OK;

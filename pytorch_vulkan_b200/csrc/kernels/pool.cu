@@ -8,37 +8,40 @@
 // backward gathers (each input sums the gradients of the windows that picked
 // it, in increasing output order) instead of scattering with atomics, so dx
 // is deterministic and summed in the same order as the CPU kernel.
+#include <algorithm>
 #include "common.cuh"
 
 namespace pvb2 {
 
+// grid (ceil(P*Q / block), min(planes, 65535)): x covers the positions of
+// one plane (32-bit arithmetic), y strides over planes
 __global__ void maxpool_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t* __restrict__ ind,
                                    int64_t planes, int H, int W, int P, int Q, pvb2_pool2d_desc d) {
-  const int64_t total = planes * P * Q;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int q = (int)(i % Q);
-    const int p = (int)((i / Q) % P);
-    const int64_t plane = i / ((int64_t)P * Q);
-    int h0 = p * d.sh - d.ph, w0 = q * d.sw - d.pw;
-    const int h1 = min(h0 + (d.kh - 1) * d.dh + 1, H);
-    const int w1 = min(w0 + (d.kw - 1) * d.dw + 1, W);
-    while (h0 < 0) h0 += d.dh;
-    while (w0 < 0) w0 += d.dw;
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= P * Q) return;
+  const int q = o % Q, p = o / Q;
+  int h0 = p * d.sh - d.ph, w0 = q * d.sw - d.pw;
+  const int h1 = min(h0 + (d.kh - 1) * d.dh + 1, H);
+  const int w1 = min(w0 + (d.kw - 1) * d.dw + 1, W);
+  while (h0 < 0) h0 += d.dh;
+  while (w0 < 0) w0 += d.dw;
+  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
     const float* xp = x + plane * H * W;
-    int64_t best = (int64_t)h0 * W + w0;
+    int best = h0 * W + w0;
     float bv = -INFINITY;
     for (int h = h0; h < h1; h += d.dh) {
       for (int w = w0; w < w1; w += d.dw) {
-        const int64_t idx = (int64_t)h * W + w;
-        const float v = xp[idx];
+        const int idx = h * W + w;
+        const float v = __ldg(xp + idx);
         if (v > bv || v != v) {
           bv = v;
           best = idx;
         }
       }
     }
-    y[i] = bv;
-    if (ind) ind[i] = best;
+    const int64_t oi = plane * P * Q + o;
+    y[oi] = bv;
+    if (ind) ind[oi] = best;
   }
 }
 
@@ -49,27 +52,26 @@ __device__ __forceinline__ int first_out(int pos, int k, int s, int pad, int dil
   return (num + s - 1) / s;
 }
 
+// grid (ceil(H*W / block), min(planes, 65535)), like the forward
 __global__ void maxpool_bwd_kernel(const float* __restrict__ dy, const int64_t* __restrict__ ind,
                                    float* __restrict__ dx, int64_t planes, int H, int W, int P, int Q,
                                    pvb2_pool2d_desc d) {
-  const int64_t total = planes * H * W;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int w = (int)(i % W);
-    const int h = (int)((i / W) % H);
-    const int64_t plane = i / ((int64_t)H * W);
-    const int p0 = first_out(h, d.kh, d.sh, d.ph, d.dh);
-    const int q0 = first_out(w, d.kw, d.sw, d.pw, d.dw);
-    const int p1 = min((h + d.ph) / d.sh + 1, P);
-    const int q1 = min((w + d.pw) / d.sw + 1, Q);
-    const int64_t me = (int64_t)h * W + w;
+  const int me = blockIdx.x * blockDim.x + threadIdx.x;
+  if (me >= H * W) return;
+  const int w = me % W, h = me / W;
+  const int p0 = first_out(h, d.kh, d.sh, d.ph, d.dh);
+  const int q0 = first_out(w, d.kw, d.sw, d.pw, d.dw);
+  const int p1 = min((h + d.ph) / d.sh + 1, P);
+  const int q1 = min((w + d.pw) / d.sw + 1, Q);
+  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
     const int64_t base = plane * P * Q;
     float acc = 0.f;
     for (int p = p0; p < p1; ++p)
       for (int q = q0; q < q1; ++q) {
-        const int64_t o = base + (int64_t)p * Q + q;
-        if (ind[o] == me) acc += dy[o];
+        const int64_t o = base + p * Q + q;
+        if (__ldg(ind + o) == me) acc += __ldg(dy + o);
       }
-    dx[i] = acc;
+    dx[plane * H * W + me] = acc;
   }
 }
 
@@ -205,7 +207,10 @@ int pvb2_max_pool2d_fwd(const pvb2_pool2d_desc* d, const pvb2_tensor* x, const p
   const int64_t planes = x->sizes[0] * x->sizes[1];
   const int64_t total = planes * y->sizes[2] * y->sizes[3];
   if (total == 0) return PVB2_OK;
-  maxpool_fwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(
+  PVB2_CHECK_ARG(x->sizes[2] * x->sizes[3] < (int64_t)1 << 31, "max_pool2d: plane too large");
+  const int64_t pq = y->sizes[2] * y->sizes[3];
+  const dim3 grid((unsigned)((pq + 255) / 256), (unsigned)std::min<int64_t>(planes, 65535));
+  maxpool_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
       (const float*)x->data, (float*)y->data, indices, planes, (int)x->sizes[2], (int)x->sizes[3], (int)y->sizes[2],
       (int)y->sizes[3], *d);
   PVB2_LAUNCH_CHECK();
@@ -219,7 +224,10 @@ int pvb2_max_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* dy, const 
   const int64_t planes = dx->sizes[0] * dx->sizes[1];
   const int64_t total = planes * dx->sizes[2] * dx->sizes[3];
   if (total == 0) return PVB2_OK;
-  maxpool_bwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(
+  PVB2_CHECK_ARG(dx->sizes[2] * dx->sizes[3] < (int64_t)1 << 31, "max_pool2d_backward: plane too large");
+  const int64_t hw = dx->sizes[2] * dx->sizes[3];
+  const dim3 grid((unsigned)((hw + 255) / 256), (unsigned)std::min<int64_t>(planes, 65535));
+  maxpool_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
       (const float*)dy->data, indices, (float*)dx->data, planes, (int)dx->sizes[2], (int)dx->sizes[3],
       (int)dy->sizes[2], (int)dy->sizes[3], *d);
   PVB2_LAUNCH_CHECK();

@@ -89,9 +89,16 @@ CONV_SHAPES = [
     (3, 64, 20, 20, 64, 1, 1, 1, 0, 1, 1),       # 13 slots per image: last tile only partly used
     (2, 256, 28, 28, 512, 1, 1, 1, 0, 1, 1),     # layer2 1x1 expand
     (2, 512, 7, 7, 2048, 1, 1, 1, 0, 1, 1),      # 49-pixel images: staged path, direct stores
+    # few input channels: GEMMs over im2col columns
+    (2, 1, 28, 28, 32, 5, 5, 1, 0, 1, 1),        # MNIST conv1
+    (3, 3, 30, 30, 24, 3, 3, 1, 1, 2, 1),        # dilated
+    (2, 4, 40, 40, 20, 5, 5, 2, 2, 1, 1),        # strided, 100 columns, output-channel tail
     # epilogue store boxes
     (4, 64, 14, 14, 100, 3, 3, 1, 1, 1, 1),      # 14-wide rows stored as whole-row runs; output-channel tail
     (2, 16, 112, 112, 24, 3, 3, 1, 1, 1, 1),     # two 64-wide pixel blocks per row
+    # many tiles per CTA with fewer output channels than the tile: chunks without a store
+    (4, 3, 224, 224, 32, 3, 3, 1, 1, 1, 1),
+    (16, 64, 56, 56, 32, 1, 1, 1, 0, 1, 1),
 ]
 
 
