@@ -49,7 +49,11 @@
 
 namespace pvb2 {
 
-constexpr int cBM = 128, cBK = 32, cStages = 4, cThreads = 192;
+// Warp roles: warps 0..3 issue TMA loads (one thread each, every fourth ring
+// stage: a thread's bulk-tensor copies are processed one after another, so
+// several issuing warps multiply the load rate), warp 4 allocates TMEM and
+// issues the MMAs, warps 5..8 run the epilogue (TMEM lane quarter = warp % 4).
+constexpr int cBM = 128, cBK = 32, cProducers = 4, cMmaWarp = cProducers, cThreads = (cProducers + 5) * 32;
 
 constexpr int kMaxTaps = 8;
 
@@ -92,17 +96,23 @@ struct ConvTcArgs {
   const float* bias;
 };
 
+// Ring depth: as many stages as fit in 192 KB, a multiple of the producer
+// count so each stage always belongs to the same producer (8 at BN = 64,
+// 4 at 128 and 256).
 template <int BN>
 struct ConvSmem {
   static constexpr int A_BYTES = cBM * cBK * 4;
   static constexpr int B_BYTES = BN * cBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int EPI_OFF = cStages * STAGE_BYTES;  // 4 epilogue warps x 2 boxes of 32 x 32 fp32
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES / cProducers * cProducers;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;  // 4 epilogue warps x 2 boxes of 32 x 32 fp32
   static constexpr int EPI_BYTES = 4 * 2 * 32 * 32 * 4;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
-  static constexpr int TOTAL = BAR_OFF + (2 * cStages + 4) * 8 + 16;
+  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16;
 };
-static_assert(ConvSmem<256>::TOTAL + 1024 <= 232448, "conv tile does not fit in shared memory");
+static_assert(ConvSmem<128>::STAGES % cProducers == 0 && ConvSmem<64>::TOTAL + 1024 <= 232448 && ConvSmem<128>::TOTAL + 1024 <= 232448 &&
+                  ConvSmem<256>::TOTAL + 1024 <= 232448,
+              "conv tile does not fit in shared memory");
 
 template <int BN, int MODE>
 __global__ void __launch_bounds__(cThreads, 1)
@@ -116,6 +126,7 @@ __global__ void __launch_bounds__(cThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + L::BAR_OFF);
+  constexpr int cStages = L::STAGES;
   uint64_t* empty = full + cStages;
   uint64_t* acc_full = empty + cStages;
   uint64_t* acc_empty = acc_full + 2;
@@ -138,7 +149,7 @@ __global__ void __launch_bounds__(cThreads, 1)
     *abort = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  if (warp == cMmaWarp) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -165,8 +176,8 @@ __global__ void __launch_bounds__(cThreads, 1)
     kb1 = min(a.total_kb, kb0 + a.kb_per_split);
   };
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp < cProducers) {
+    // ------------------------------------------------------------ producers
     if (lane == 0) {
       tma_prefetch(&tmA);
       tma_prefetch(&tmB);
@@ -179,6 +190,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = 0; kb < kblocks; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
+            if ((int)(it % cProducers) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
             const int rs = kb / a.cblocks, cb = kb % a.cblocks;
             const int r = rs / a.S, s = rs % a.S;
@@ -192,6 +204,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = 0; kb < a.cblocks; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
+            if ((int)(it % cProducers) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
             uint8_t* sa = smem + s_ * L::STAGE_BYTES;
             uint8_t* sb = sa + L::A_BYTES;
@@ -219,6 +232,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
+            if ((int)(it % cProducers) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
             const int q0 = (kb % a.tq) * a.bw, p0 = ((kb / a.tq) % a.tp) * a.bh, n0 = (kb / (a.tq * a.tp)) * a.bni;
             uint8_t* sa = smem + s_ * L::STAGE_BYTES;
@@ -239,6 +253,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
+            if ((int)(it % cProducers) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
             const int n = kb / a.hwb, hw0 = (kb - n * a.hwb) * 32;
             uint8_t* sa = smem + s_ * L::STAGE_BYTES;
@@ -254,7 +269,7 @@ __global__ void __launch_bounds__(cThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == cMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(cBM, BN, A_MN, B_MN);
@@ -402,7 +417,7 @@ __global__ void __launch_bounds__(cThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == cMmaWarp) {
     if (*abort) {
       const uint64_t t0 = globaltimer();
       while (globaltimer() - t0 < 10000000ull) {

@@ -2,7 +2,7 @@
 //
 // Persistent, warp-specialised kernel (one CTA per SM, 192 threads):
 //   warp 0      TMA producer: one thread streams 128x32 A and BNx32 B tiles
-//               (128-byte swizzle) into a kStages-deep shared-memory ring;
+//               (128-byte swizzle) into a shared-memory ring (4-8 stages);
 //   warp 1      MMA issuer: allocates 2*BN TMEM columns, one thread issues
 //               tcgen05.mma kind::tf32 (M=128, N=BN, K=8) four times per
 //               32-deep K block and releases ring slots with tcgen05.commit;
@@ -22,7 +22,11 @@
 
 namespace pvb2 {
 
-constexpr int kBM = 128, kBK = 32, kStages = 4, kThreads = 192;
+// Warp roles: warps 0..3 issue TMA loads (one thread each, every fourth ring
+// stage: a thread's bulk-tensor copies are processed one after another, so
+// several issuing warps multiply the load rate), warp 4 allocates TMEM and
+// issues the MMAs, warps 5..8 run the epilogue (TMEM lane quarter = warp % 4).
+constexpr int kBM = 128, kBK = 32, kProducers = 4, kMmaWarp = kProducers, kThreads = (kProducers + 5) * 32;
 
 struct GemmEpi {
   float* C;
@@ -34,14 +38,18 @@ struct GemmEpi {
   int a_bcast, b_bcast;   // operand shared by all batches (batch stride 0)
 };
 
+// Ring depth: as many stages as fit in 192 KB, a multiple of the producer
+// count so each stage always belongs to the same producer (8 at BN = 64,
+// 4 at 128 and 256).
 template <int BN>
 struct GemmSmem {
   static constexpr int A_BYTES = kBM * kBK * 4;
   static constexpr int B_BYTES = BN * kBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = kStages * STAGE_BYTES;
-  // full[kStages], empty[kStages], acc_full[2], acc_empty[2], tmem slot, abort
-  static constexpr int TOTAL = BAR_OFF + (2 * kStages + 4) * 8 + 16;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES / kProducers * kProducers;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], tmem slot, abort
+  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16;
 };
 
 template <int BN, bool A_MN, bool B_MN>
@@ -50,6 +58,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = GemmSmem<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  constexpr int kStages = L::STAGES;
   uint64_t* full = (uint64_t*)(smem + L::BAR_OFF);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
@@ -74,14 +83,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  if (warp == kMmaWarp) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp < kProducers) {
+    // ------------------------------------------------------------ producers
     if (lane == 0) {
       tma_prefetch(&tmA);
       tma_prefetch(&tmB);
@@ -92,6 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
+          if ((int)(it % kProducers) != warp) continue;
           if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
           uint8_t* sa = smem + s * L::STAGE_BYTES;
           uint8_t* sb = sa + L::A_BYTES;
@@ -111,7 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(kBM, BN, A_MN, B_MN);
@@ -182,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     if (*abort) {
       // let any MMA still in flight finish before the columns are released
       if (lane == 0) {
