@@ -450,21 +450,66 @@ __global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restri
   }
 }
 
-// forward: W [K][C][R][S] -> Wp [K][R][S][Cp]
-__global__ void pack_w_fwd_kernel(const float* __restrict__ w, float* __restrict__ wp, int K, int C, int Cp, int RS) {
-  const int64_t total = (int64_t)K * RS * Cp;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % Cp);
-    const int rs = (int)((i / Cp) % RS);
-    const int64_t k = i / ((int64_t)Cp * RS);
-    wp[i] = c < C ? w[(k * C + c) * RS + rs] : 0.f;
+// Same transpose with 128-bit accesses when HW % 4 == 0 (Cp is a multiple
+// of 4): a 64-pixel x 32-channel tile per 256-thread block; loads are float4
+// runs of 4 pixels of one channel, stores float4 runs of 4 channels of one
+// pixel.
+__global__ void __launch_bounds__(256) nchw_to_nhwc_v4_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                                              int C, int Cp, int HW) {
+  __shared__ float tile[32][64 + 1];  // odd pitch: the column reads below hit 32 banks
+  const int64_t n = blockIdx.z;
+  const int p0 = blockIdx.x * 64, c0 = blockIdx.y * 32;
+  const float* xn = x + n * C * (int64_t)HW;
+  float* yn = y + n * (int64_t)HW * Cp;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = threadIdx.x + u * 256;  // 32 channels x 16 float4
+    const int c = i >> 4, q4 = (i & 15) * 4;
+    const int p = p0 + q4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c0 + c < C && p < HW) v = __ldg(reinterpret_cast<const float4*>(xn + (int64_t)(c0 + c) * HW + p));
+    tile[c][q4 + 0] = v.x;
+    tile[c][q4 + 1] = v.y;
+    tile[c][q4 + 2] = v.z;
+    tile[c][q4 + 3] = v.w;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = threadIdx.x + u * 256;  // 64 pixels x 8 float4
+    const int q = i >> 3, c4 = (i & 7) * 4;
+    const int p = p0 + q;
+    if (p < HW && c0 + c4 < Cp)
+      *reinterpret_cast<float4*>(yn + (int64_t)p * Cp + c0 + c4) =
+          make_float4(tile[c4][q], tile[c4 + 1][q], tile[c4 + 2][q], tile[c4 + 3][q]);
   }
 }
 
+// forward: W [K][C][R][S] -> Wp [K][R][S][Cp]
+__global__ void pack_w_fwd_kernel(const float* __restrict__ w, float* __restrict__ wp, int K, int C, int Cp, int RS) {
+  const int total = K * RS * Cp;  // weights: far below 2^31 elements (checked by the launcher)
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int c = i % Cp;
+    const int t = i / Cp;
+    const int rs = t % RS, k = t / RS;
+    wp[i] = c < C ? __ldg(w + (k * C + c) * RS + rs) : 0.f;
+  }
+}
+
+// out[i] = sum_k part[k][i] (k = 0..splits-1, in that order); eight splits'
+// loads are issued before they are added
 __global__ void sum_partials_kernel(const float* __restrict__ part, int splits, int64_t n, float* __restrict__ out) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.f;
-    for (int k = 0; k < splits; ++k) s += part[(int64_t)k * n + i];
+    int k = 0;
+    for (; k + 8 <= splits; k += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(part + (int64_t)(k + u) * n + i);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s += v[u];
+    }
+    for (; k < splits; ++k) s += __ldg(part + (int64_t)k * n + i);
     out[i] = s;
   }
 }
@@ -472,59 +517,82 @@ __global__ void sum_partials_kernel(const float* __restrict__ part, int splits, 
 // dgrad phase: Wd[c][t][k] = W[k][c][r_t][s_t] over the phase's tap list
 __global__ void pack_w_phase_kernel(const float* __restrict__ w, float* __restrict__ wd, int K, int Kp, int C, int R,
                                     int S, int nr, int ns, int4 rl, int4 rh, int4 sl, int4 shi) {
-  const int rr[8] = {rl.x, rl.y, rl.z, rl.w, rh.x, rh.y, rh.z, rh.w};
-  const int ss[8] = {sl.x, sl.y, sl.z, sl.w, shi.x, shi.y, shi.z, shi.w};
-  const int64_t total = (int64_t)C * nr * ns * Kp;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int k = (int)(i % Kp);
-    const int t = (int)((i / Kp) % (nr * ns));
-    const int64_t c = i / ((int64_t)Kp * nr * ns);
-    const int r = rr[t / ns], s_ = ss[t % ns];
-    wd[i] = k < K ? w[(((int64_t)k * C + c) * R + r) * S + s_] : 0.f;
+  __shared__ int tap_off[kMaxTaps * kMaxTaps];  // (r_t, s_t) -> r*S + s
+  if (threadIdx.x < nr * ns) {
+    const int a = threadIdx.x / ns, b = threadIdx.x % ns;
+    const int rv[8] = {rl.x, rl.y, rl.z, rl.w, rh.x, rh.y, rh.z, rh.w};
+    const int sv[8] = {sl.x, sl.y, sl.z, sl.w, shi.x, shi.y, shi.z, shi.w};
+    tap_off[threadIdx.x] = rv[a] * S + sv[b];
+  }
+  __syncthreads();
+  const int taps = nr * ns, RS = R * S;
+  const int total = C * taps * Kp;  // weights: far below 2^31 elements (checked by the launcher)
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int k = i % Kp;
+    const int u = i / Kp;
+    const int t = u % taps, c = u / taps;
+    wd[i] = k < K ? __ldg(w + (k * C + c) * RS + tap_off[t]) : 0.f;
   }
 }
 
 // small-C convolutions as a GEMM over im2col columns:
 // Xcol[n, p, q, j] = X[n, c, p*sh - ph + r*dh, q*sw - pw + s*dw] with j = (c*R + r)*S + s
 // (W's own flattening; 0 outside the image and for j >= C*R*S up to Kc).
-// grid (P, N); per-j source offsets in shared memory, float4 stores.
+// grid (P, N): one output row per CTA, in runs of 32 columns.  Loads walk q
+// (neighbouring threads read neighbouring input columns), a shared-memory
+// tile transposes the run, and stores are float4 along j.
 constexpr int kIm2colMaxK = 256;
-__global__ void im2col_kernel(const float* __restrict__ x, float* __restrict__ xcol, int C, int H, int W, int P,
-                              int Q, int R, int S, int Kc, int sh, int sw, int ph, int pw, int dh, int dw) {
-  __shared__ int jc[kIm2colMaxK], jr[kIm2colMaxK], js[kIm2colMaxK];
+constexpr int kIm2colRun = 32;
+__global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ x, float* __restrict__ xcol, int C,
+                                                     int H, int W, int P, int Q, int R, int S, int Kc, int sh, int sw,
+                                                     int ph, int pw, int dh, int dw) {
+  // per column j of this output row: the input row's offset (-1: zero column) and the tap's w shift
+  __shared__ int joff[kIm2colMaxK], js[kIm2colMaxK];
+  __shared__ float tile[kIm2colRun][kIm2colMaxK + 1];
+  const int p = blockIdx.x;
+  const int64_t n = blockIdx.y;
   const int crs = C * R * S;
   for (int j = threadIdx.x; j < Kc; j += blockDim.x) {
     const int c = j / (R * S), rs = j - c * R * S;
-    jc[j] = j < crs ? c : -1;
-    jr[j] = (rs / S) * dh - ph;
+    const int h = p * sh + (rs / S) * dh - ph;
+    joff[j] = (j < crs && h >= 0 && h < H) ? (c * H + h) * W : -1;
     js[j] = (rs % S) * dw - pw;
   }
   __syncthreads();
-  const int p = blockIdx.x;
-  const int64_t n = blockIdx.y;
   const float* xn = x + n * C * H * W;
-  float4* row = reinterpret_cast<float4*>(xcol + ((n * P + p) * Q) * (int64_t)Kc);
-  const int total4 = Q * Kc / 4, step = 4 * blockDim.x;
-  int t4 = threadIdx.x;
-  if (t4 >= total4) return;
-  int q = (4 * t4) / Kc, j0 = 4 * t4 - q * Kc;
-  const int dq = step / Kc, dj = step - dq * Kc;
-  for (; t4 < total4; t4 += blockDim.x) {
-    float v[4];
+  float* row = xcol + ((n * P + p) * Q) * (int64_t)Kc;
+  const int lq = threadIdx.x % kIm2colRun, lj = threadIdx.x / kIm2colRun, jstep = blockDim.x / kIm2colRun;
+  for (int q0 = 0; q0 < Q; q0 += kIm2colRun) {
+    const int q = q0 + lq;
+    const int wq = q * sw;
+    const bool qok = q < Q;
+    // eight loads in flight per thread before their shared-memory stores
+    constexpr int U = 8;
+    for (int jb = lj; jb < Kc; jb += U * jstep) {
+      float v[U];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int j = j0 + u;
-      const int c = jc[j];
-      const int h = p * sh + jr[j], w = q * sw + js[j];
-      v[u] = (c >= 0 && h >= 0 && h < H && w >= 0 && w < W) ? __ldg(xn + ((int64_t)c * H + h) * W + w) : 0.f;
+      for (int u = 0; u < U; ++u) {
+        const int j = jb + u * jstep;
+        v[u] = 0.f;
+        if (j < Kc) {
+          const int ro = joff[j], w = wq + js[j];
+          if (qok && ro >= 0 && (unsigned)w < (unsigned)W) v[u] = __ldg(xn + ro + w);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = jb + u * jstep;
+        if (j < Kc) tile[lq][j] = v[u];
+      }
     }
-    row[t4] = make_float4(v[0], v[1], v[2], v[3]);
-    j0 += dj;
-    q += dq;
-    if (j0 >= Kc) {
-      j0 -= Kc;
-      ++q;
+    __syncthreads();
+    const int nq = min(kIm2colRun, Q - q0), kc4 = Kc / 4;
+    float4* out = reinterpret_cast<float4*>(row + (int64_t)q0 * Kc);
+    for (int t = threadIdx.x; t < nq * kc4; t += blockDim.x) {
+      const int qq = t / kc4, j4 = (t - qq * kc4) * 4;
+      out[t] = make_float4(tile[qq][j4], tile[qq][j4 + 1], tile[qq][j4 + 2], tile[qq][j4 + 3]);
     }
+    __syncthreads();
   }
 }
 
@@ -646,8 +714,13 @@ static int nchw_map(CUtensorMap* m, const float* base, int N, int C, int64_t hw,
 }
 
 static int to_nhwc(const float* x, float* y, int N, int C, int Cp, int64_t HW, cudaStream_t s) {
-  dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((Cp + 31) / 32), (unsigned)N);
-  nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, y, C, Cp, HW);
+  if (HW % 4 == 0 && HW < ((int64_t)1 << 31) && aligned16(x) && aligned16(y)) {
+    dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((Cp + 31) / 32), (unsigned)N);
+    nchw_to_nhwc_v4_kernel<<<grid, 256, 0, s>>>(x, y, C, Cp, (int)HW);
+  } else {
+    dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((Cp + 31) / 32), (unsigned)N);
+    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, y, C, Cp, HW);
+  }
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
@@ -766,11 +839,15 @@ struct WgPlan {
   int bw, bh, bni, BN, splits, kb_per, total_kb, ct, kt;
 };
 
-static void plan_splits(WgPlan& w, int taps) {
+// out_elems: K x Cin x taps weights; in_bytes: the operand bytes the
+// reduction streams.  Splits also cost their partials (written once, read
+// once), so they stop where that traffic would exceed the operands'.
+static void plan_splits(WgPlan& w, int taps, double out_elems, double in_bytes) {
   const int base_tiles = w.kt * w.ct * taps;
   int splits = (2 * num_sms() + base_tiles - 1) / base_tiles;
   splits = std::min(splits, std::max(1, w.total_kb / 8));
   splits = std::max(1, std::min(splits, 64));
+  while (splits > 1 && (double)splits * out_elems * 8.0 > in_bytes) --splits;
   w.kb_per = (w.total_kb + splits - 1) / splits;
   w.splits = (w.total_kb + w.kb_per - 1) / w.kb_per;
 }
@@ -783,7 +860,7 @@ static WgPlan plan_wg(int N, int K, int Cin, int P, int Q, int taps) {
   w.kt = (K + cBM - 1) / cBM;
   const int tq = (Q + w.bw - 1) / w.bw, tp = (P + w.bh - 1) / w.bh, tn = (N + w.bni - 1) / w.bni;
   w.total_kb = tq * tp * tn;
-  plan_splits(w, taps);
+  plan_splits(w, taps, (double)K * Cin * taps, 4.0 * N * P * Q * ((double)K + Cin));
   return w;
 }
 
@@ -794,7 +871,7 @@ static WgPlan plan_pw_wg(int N, int K, int C, int64_t hw) {
   w.ct = (C + w.BN - 1) / w.BN;
   w.kt = (K + cBM - 1) / cBM;
   w.total_kb = N * (int)((hw + 31) / 32);
-  plan_splits(w, 1);
+  plan_splits(w, 1, (double)K * C, 4.0 * N * hw * ((double)K + C));
   return w;
 }
 
@@ -858,7 +935,7 @@ static WgPlan plan_im_wg(int N, int K, int Kc, int64_t pq) {
   w.ct = (K + w.BN - 1) / w.BN;
   w.kt = (Kc + cBM - 1) / cBM;
   w.total_kb = N * (int)((pq + 31) / 32);
-  plan_splits(w, 1);
+  plan_splits(w, 1, (double)K * Kc, 4.0 * N * pq * ((double)K + Kc));
   return w;
 }
 
@@ -888,6 +965,7 @@ static int run_im_wgrad(const float* xcol, int Kc, const float* dy, int N, int K
 }
 
 static int im2col(const pvb2_conv2d_desc* d, const float* x, float* xcol, cudaStream_t s) {
+  PVB2_CHECK_ARG((int64_t)d->C * d->H * d->W < ((int64_t)1 << 31), "conv2d: image too large for im2col");
   const dim3 grid((unsigned)d->P, (unsigned)d->N);
   im2col_kernel<<<grid, 256, 0, s>>>(x, xcol, d->C, d->H, d->W, d->P, d->Q, d->R, d->S, im2col_channels(d),
                                      d->stride_h, d->stride_w, d->pad_h, d->pad_w, d->dil_h, d->dil_w);

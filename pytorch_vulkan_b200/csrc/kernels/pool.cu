@@ -5,16 +5,15 @@
 // avg), :353-445 (max_pool2d_cls) and :448-511 (avg_pool2d).  The reference
 // recomputed the argmax from x in backward; here the forward writes torch's
 // flat h*W+w index so max-pool indices are bit-exact with the CPU, and the
-// backward gathers (each input sums the gradients of the windows that picked
-// it, in increasing output order) instead of scattering with atomics, so dx
-// is deterministic and summed in the same order as the CPU kernel.
+// backward scatters each output's gradient to its index in classes of
+// non-overlapping windows (no atomics), so dx is deterministic.
 #include <algorithm>
 #include "common.cuh"
 
 namespace pvb2 {
 
-// grid (ceil(P*Q / block), min(planes, 65535)): x covers the positions of
-// one plane (32-bit arithmetic), y strides over planes
+// grid (ceil(P*Q / block), min(ceil(planes / 2), 65535)): x covers the
+// positions of one plane (32-bit arithmetic), y strides over pairs of planes
 __global__ void maxpool_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t* __restrict__ ind,
                                    int64_t planes, int H, int W, int P, int Q, pvb2_pool2d_desc d) {
   const int o = blockIdx.x * blockDim.x + threadIdx.x;
@@ -25,23 +24,38 @@ __global__ void maxpool_fwd_kernel(const float* __restrict__ x, float* __restric
   const int w1 = min(w0 + (d.kw - 1) * d.dw + 1, W);
   while (h0 < 0) h0 += d.dh;
   while (w0 < 0) w0 += d.dw;
-  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
-    const float* xp = x + plane * H * W;
-    int best = h0 * W + w0;
-    float bv = -INFINITY;
+  constexpr int kPlanes = 2;
+  for (int64_t plane0 = (int64_t)blockIdx.y * kPlanes; plane0 < planes; plane0 += (int64_t)gridDim.y * kPlanes) {
+    int best[kPlanes];
+    float bv[kPlanes];
+#pragma unroll
+    for (int u = 0; u < kPlanes; ++u) {
+      best[u] = h0 * W + w0;
+      bv[u] = -INFINITY;
+    }
     for (int h = h0; h < h1; h += d.dh) {
       for (int w = w0; w < w1; w += d.dw) {
         const int idx = h * W + w;
-        const float v = __ldg(xp + idx);
-        if (v > bv || v != v) {
-          bv = v;
-          best = idx;
+#pragma unroll
+        for (int u = 0; u < kPlanes; ++u) {
+          if (plane0 + u < planes) {
+            const float v = __ldg(x + (plane0 + u) * H * W + idx);
+            if (v > bv[u] || v != v) {
+              bv[u] = v;
+              best[u] = idx;
+            }
+          }
         }
       }
     }
-    const int64_t oi = plane * P * Q + o;
-    y[oi] = bv;
-    if (ind) ind[oi] = best;
+#pragma unroll
+    for (int u = 0; u < kPlanes; ++u) {
+      if (plane0 + u < planes) {
+        const int64_t oi = (plane0 + u) * P * Q + o;
+        y[oi] = bv[u];
+        if (ind) ind[oi] = best[u];
+      }
+    }
   }
 }
 
@@ -52,26 +66,24 @@ __device__ __forceinline__ int first_out(int pos, int k, int s, int pad, int dil
   return (num + s - 1) / s;
 }
 
-// grid (ceil(H*W / block), min(planes, 65535)), like the forward
-__global__ void maxpool_bwd_kernel(const float* __restrict__ dy, const int64_t* __restrict__ ind,
-                                   float* __restrict__ dx, int64_t planes, int H, int W, int P, int Q,
-                                   pvb2_pool2d_desc d) {
-  const int me = blockIdx.x * blockDim.x + threadIdx.x;
-  if (me >= H * W) return;
-  const int w = me % W, h = me / W;
-  const int p0 = first_out(h, d.kh, d.sh, d.ph, d.dh);
-  const int q0 = first_out(w, d.kw, d.sw, d.pw, d.dw);
-  const int p1 = min((h + d.ph) / d.sh + 1, P);
-  const int q1 = min((w + d.pw) / d.sw + 1, Q);
+// Backward as a deterministic scatter: outputs are split into classes
+// (p mod mh, q mod mw) whose windows never overlap (mh * sh >= the window's
+// height, likewise for widths), and one launch per class adds each output's
+// gradient at its recorded argmax.  Within a launch no two threads touch the
+// same input element; the classes run in a fixed order.  Indices outside the
+// plane are ignored.  grid (ceil(class outputs / block), min(planes, 65535)).
+__global__ void maxpool_bwd_class_kernel(const float* __restrict__ dy, const int64_t* __restrict__ ind,
+                                         float* __restrict__ dx, int64_t planes, int HW, int P, int Q, int mh, int mw,
+                                         int ci, int cj) {
+  const int Pc = (P - ci + mh - 1) / mh, Qc = (Q - cj + mw - 1) / mw;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= Pc * Qc) return;
+  const int a = t / Qc, b = t - a * Qc;
+  const int o = (ci + a * mh) * Q + (cj + b * mw);
+  const int64_t PQ = (int64_t)P * Q;
   for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
-    const int64_t base = plane * P * Q;
-    float acc = 0.f;
-    for (int p = p0; p < p1; ++p)
-      for (int q = q0; q < q1; ++q) {
-        const int64_t o = base + p * Q + q;
-        if (__ldg(ind + o) == me) acc += __ldg(dy + o);
-      }
-    dx[plane * H * W + me] = acc;
+    const int64_t i = __ldg(ind + plane * PQ + o);
+    if (i >= 0 && i < HW) dx[plane * HW + i] += __ldg(dy + plane * PQ + o);
   }
 }
 
@@ -209,7 +221,7 @@ int pvb2_max_pool2d_fwd(const pvb2_pool2d_desc* d, const pvb2_tensor* x, const p
   if (total == 0) return PVB2_OK;
   PVB2_CHECK_ARG(x->sizes[2] * x->sizes[3] < (int64_t)1 << 31, "max_pool2d: plane too large");
   const int64_t pq = y->sizes[2] * y->sizes[3];
-  const dim3 grid((unsigned)((pq + 255) / 256), (unsigned)std::min<int64_t>(planes, 65535));
+  const dim3 grid((unsigned)((pq + 255) / 256), (unsigned)std::min<int64_t>((planes + 1) / 2, 65535));
   maxpool_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
       (const float*)x->data, (float*)y->data, indices, planes, (int)x->sizes[2], (int)x->sizes[3], (int)y->sizes[2],
       (int)y->sizes[3], *d);
@@ -221,16 +233,28 @@ int pvb2_max_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* dy, const 
                         const pvb2_tensor* dx, pvb2_stream stream) {
   PVB2_TRY(check_nchw(dy, "max_pool2d_backward"));
   PVB2_TRY(check_nchw(dx, "max_pool2d_backward"));
+  PVB2_CHECK_ARG(d->kh > 0 && d->kw > 0 && d->sh > 0 && d->sw > 0 && d->dh > 0 && d->dw > 0,
+                 "max_pool2d_backward: kernel, stride and dilation must be positive");
   const int64_t planes = dx->sizes[0] * dx->sizes[1];
-  const int64_t total = planes * dx->sizes[2] * dx->sizes[3];
-  if (total == 0) return PVB2_OK;
-  PVB2_CHECK_ARG(dx->sizes[2] * dx->sizes[3] < (int64_t)1 << 31, "max_pool2d_backward: plane too large");
   const int64_t hw = dx->sizes[2] * dx->sizes[3];
-  const dim3 grid((unsigned)((hw + 255) / 256), (unsigned)std::min<int64_t>(planes, 65535));
-  maxpool_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>(
-      (const float*)dy->data, indices, (float*)dx->data, planes, (int)dx->sizes[2], (int)dx->sizes[3],
-      (int)dy->sizes[2], (int)dy->sizes[3], *d);
-  PVB2_LAUNCH_CHECK();
+  const int64_t pq = dy->sizes[2] * dy->sizes[3];
+  if (planes * hw == 0) return PVB2_OK;
+  PVB2_CHECK_ARG(hw < (int64_t)1 << 31 && pq < (int64_t)1 << 31, "max_pool2d_backward: plane too large");
+  cudaStream_t s = as_stream(stream);
+  PVB2_CUDA_TRY(cudaMemsetAsync(dx->data, 0, (size_t)(planes * hw) * sizeof(float), s));
+  if (pq == 0) return PVB2_OK;
+  const int P = (int)dy->sizes[2], Q = (int)dy->sizes[3];
+  const int mh = ((d->kh - 1) * d->dh + 1 + d->sh - 1) / d->sh;
+  const int mw = ((d->kw - 1) * d->dw + 1 + d->sw - 1) / d->sw;
+  for (int ci = 0; ci < mh; ++ci)
+    for (int cj = 0; cj < mw; ++cj) {
+      const int Pc = (P - ci + mh - 1) / mh, Qc = (Q - cj + mw - 1) / mw;
+      if (Pc <= 0 || Qc <= 0) continue;
+      const dim3 grid((unsigned)(((int64_t)Pc * Qc + 255) / 256), (unsigned)std::min<int64_t>(planes, 65535));
+      maxpool_bwd_class_kernel<<<grid, 256, 0, s>>>((const float*)dy->data, indices, (float*)dx->data, planes,
+                                                    (int)hw, P, Q, mh, mw, ci, cj);
+      PVB2_LAUNCH_CHECK();
+    }
   return PVB2_OK;
 }
 
