@@ -31,8 +31,9 @@
 //     wgrad     dW[k, c, r, s] = sum_pix dYnhwc[pix, k] * Xnhwc[shift_rs(pix), c]
 //               GEMM M = 128 output channels, N = BN input channels, K = 32-pixel
 //               blocks (MN-major A and B), one tap per tile.
-//   Weight gradients split K (pixels) over CTAs into fp32 partials that a
-//   second kernel sums in a fixed order (or go straight to dW with one split).
+//   Weight gradients split K (pixels) over CTAs into fp32 partials (stored
+//   by TMA as row-contiguous 32 x 32 boxes) that a second kernel sums in a
+//   fixed order while transposing them into dW's [K][C][R][S] layout.
 //
 // Epilogue of the forward-shaped launches: each epilogue warp owns 32
 // accumulator rows; per 32-channel chunk it loads TMEM into registers, writes
@@ -391,20 +392,30 @@ __global__ void __launch_bounds__(cThreads, 1)
           }
         }
       } else {
+        // weight-gradient partials [splits * taps][cols][rows] (rows contiguous):
+        // one TMA store per 32 x 32 chunk, clipped at the row / column ends
         int sp, km, ctile, rs;
         wg_tile(tile, sp, km, ctile, rs);
-        const int k = km * cBM + row;
-        const int64_t crs = (int64_t)a.Cin * RS;
-        float* pbase = a.out + ((int64_t)sp * a.Kout + k) * crs + rs;
+        const int m0 = km * cBM + quarter * 32;
+        const int z = sp * RS + rs;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
-          const int c0 = ctile * BN + c * 32;
-          if (k < a.Kout) {
+          const int n0 = ctile * BN + c * 32;
+          if (m0 < a.Kout && n0 < a.Cin) {  // warp-uniform
+            float* st = stage + (echunk & 1) * 1024;
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (c0 + j < a.Cin) pbase[(int64_t)(c0 + j) * RS] = v[j];
+            for (int j = 0; j < 32; ++j) st[j * 32 + lane] = v[j];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tmC, st, m0, n0, z);
+              bulk_commit();
+            }
+            ++echunk;
           }
         }
       }
@@ -493,24 +504,6 @@ __global__ void pack_w_fwd_kernel(const float* __restrict__ w, float* __restrict
     const int t = i / Cp;
     const int rs = t % RS, k = t / RS;
     wp[i] = c < C ? __ldg(w + (k * C + c) * RS + rs) : 0.f;
-  }
-}
-
-// out[i] = sum_k part[k][i] (k = 0..splits-1, in that order); eight splits'
-// loads are issued before they are added
-__global__ void sum_partials_kernel(const float* __restrict__ part, int splits, int64_t n, float* __restrict__ out) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    int k = 0;
-    for (; k + 8 <= splits; k += 8) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldg(part + (int64_t)(k + u) * n + i);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) s += v[u];
-    }
-    for (; k < splits; ++k) s += __ldg(part + (int64_t)k * n + i);
-    out[i] = s;
   }
 }
 
@@ -603,19 +596,6 @@ __global__ void pack_w_rows_kernel(const float* __restrict__ w, float* __restric
     const int j = (int)(i % Kc);
     const int64_t k = i / Kc;
     wp[i] = j < crs ? w[k * crs + j] : 0.f;
-  }
-}
-
-// dW[k][j] = sum_sp part[sp][j][k] for j < crs (im2col weight gradient partials are [Kc][K])
-__global__ void sum_transpose_kernel(const float* __restrict__ part, int splits, int K, int crs, int Kc,
-                                     float* __restrict__ dw) {
-  const int64_t total = (int64_t)K * crs;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int j = (int)(i % crs);
-    const int64_t k = i / crs;
-    float acc = 0.f;
-    for (int sp = 0; sp < splits; ++sp) acc += part[((int64_t)sp * Kc + j) * K + k];
-    dw[i] = acc;
   }
 }
 
@@ -875,8 +855,64 @@ static WgPlan plan_pw_wg(int N, int K, int C, int64_t hw) {
   return w;
 }
 
+// Weight-gradient partials: [splits * taps][cols][round4(rows)] fp32, rows
+// (the GEMM M side) contiguous; the epilogue stores 32 x 32 boxes of it.
+static size_t wg_partial_bytes(int rows, int cols, int z) { return (size_t)z * cols * round4(rows) * 4; }
+static int wg_partial_map(CUtensorMap* mc, float* part, int rows, int cols, int z) {
+  uint64_t dims[3] = {(uint64_t)rows, (uint64_t)cols, (uint64_t)z};
+  uint64_t str[2] = {(uint64_t)round4(rows) * 4, (uint64_t)round4(rows) * cols * 4};
+  uint32_t box[3] = {32, 32, 1};
+  return encode_tiled(mc, 3, part, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// dW from the partials: out[m*osm + n*osn + t*ost] = sum_sp part[sp][t][n][m] for
+// m < mv, n < nv (splits summed in order).  grid (ceil(mv/32), ceil(nv/32), taps),
+// block (32, 8); a 32 x 32 shared tile turns row-contiguous reads into
+// writes along whichever of m / n is contiguous in dW.
+__global__ void wgrad_reduce_kernel(const float* __restrict__ part, int splits, int taps, int cols, int mp, int mv,
+                                    int nv, float* __restrict__ out, int64_t osm, int64_t osn, int64_t ost) {
+  __shared__ float tile[32][33];
+  const int m0 = blockIdx.x * 32, n0 = blockIdx.y * 32, t = blockIdx.z;
+  const int64_t zstride = (int64_t)taps * cols * mp;
+  for (int ny = threadIdx.y; ny < 32; ny += blockDim.y) {
+    const int n = n0 + ny, m = m0 + threadIdx.x;
+    float acc = 0.f;
+    if (n < nv && m < mv) {
+      const float* src = part + ((int64_t)t * cols + n) * mp + m;
+      int sp = 0;
+      for (; sp + 4 <= splits; sp += 4) {
+        const float v0 = __ldg(src + sp * zstride), v1 = __ldg(src + (sp + 1) * zstride);
+        const float v2 = __ldg(src + (sp + 2) * zstride), v3 = __ldg(src + (sp + 3) * zstride);
+        acc = (((acc + v0) + v1) + v2) + v3;
+      }
+      for (; sp < splits; ++sp) acc += __ldg(src + sp * zstride);
+    }
+    tile[ny][threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (osm == 1) {
+    for (int ny = threadIdx.y; ny < 32; ny += blockDim.y) {
+      const int n = n0 + ny, m = m0 + threadIdx.x;
+      if (n < nv && m < mv) out[m + n * osn + t * ost] = tile[ny][threadIdx.x];
+    }
+  } else {
+    for (int my = threadIdx.y; my < 32; my += blockDim.y) {
+      const int m = m0 + my, n = n0 + threadIdx.x;
+      if (n < nv && m < mv) out[m * osm + n * osn + t * ost] = tile[threadIdx.x][my];
+    }
+  }
+}
+
+static int wgrad_reduce(const float* part, int splits, int taps, int rows, int cols, int mv, int nv, float* dw,
+                        int64_t osm, int64_t osn, int64_t ost, cudaStream_t s) {
+  const dim3 grid((unsigned)((mv + 31) / 32), (unsigned)((nv + 31) / 32), (unsigned)taps);
+  wgrad_reduce_kernel<<<grid, dim3(32, 8), 0, s>>>(part, splits, taps, cols, round4(rows), mv, nv, dw, osm, osn, ost);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
 // dy: channels-last [N, P, Q, Kp]; x: channels-last [N, H, W, Cp] (Cin <= Cp real channels);
-// partials [splits][K][Cin][taps]
+// partials [splits * taps][Cin][K]
 static int run_wgrad(const float* dyn, int Kp, const float* xn, int Cp, int N, int H, int W, int P, int Q, int K,
                      int Cin, const Taps& t, int sh, int sw, const WgPlan& p, float* part, cudaStream_t s) {
   CUtensorMap ma, mb, mc;
@@ -902,10 +938,11 @@ static int run_wgrad(const float* dyn, int Kp, const float* xn, int Cp, int N, i
   a.total_kb = p.total_kb;
   a.out = part;
   a.tiles = a.kt * a.ct * t.nr * t.ns * a.splits;
+  PVB2_TRY(wg_partial_map(&mc, part, K, Cin, p.splits * t.nr * t.ns));
   return launch_bn<kWgrad>(p.BN, ma, mb, mc, a, s);
 }
 
-// pointwise weight gradient into partials [splits][K][C]
+// pointwise weight gradient into partials [splits][C][K]
 static int run_pw_wgrad(const float* dy, const float* x, int N, int C, int K, int64_t hw, const WgPlan& p,
                         float* part, cudaStream_t s) {
   CUtensorMap ma, mb, mc;
@@ -924,6 +961,7 @@ static int run_pw_wgrad(const float* dy, const float* x, int N, int C, int K, in
   a.hwb = (int)((hw + 31) / 32);
   a.out = part;
   a.tiles = a.kt * a.ct * a.splits;
+  PVB2_TRY(wg_partial_map(&mc, part, K, C, p.splits));
   return launch_bn<kPwWgrad>(p.BN, ma, mb, mc, a, s);
 }
 
@@ -939,7 +977,7 @@ static WgPlan plan_im_wg(int N, int K, int Kc, int64_t pq) {
   return w;
 }
 
-// im2col weight gradient into partials [splits][Kc][K]; xcol: [N][pq][Kc], dy: NCHW [N][K][pq]
+// im2col weight gradient into partials [splits][K][Kc]; xcol: [N][pq][Kc], dy: NCHW [N][K][pq]
 static int run_im_wgrad(const float* xcol, int Kc, const float* dy, int N, int K, int64_t pq, const WgPlan& p,
                         float* part, cudaStream_t s) {
   CUtensorMap ma, mb, mc;
@@ -961,6 +999,7 @@ static int run_im_wgrad(const float* xcol, int Kc, const float* dy, int N, int K
   a.hwb = (int)((pq + 31) / 32);
   a.out = part;
   a.tiles = a.kt * a.ct * a.splits;
+  PVB2_TRY(wg_partial_map(&mc, part, Kc, K, p.splits));
   return launch_bn<kImWgrad>(p.BN, ma, mb, mc, a, s);
 }
 
@@ -1023,15 +1062,15 @@ static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
   if (pointwise(d)) {
     WgPlan p = plan_pw_wg(d->N, d->K, d->C, (int64_t)d->H * d->W);
     if (plan) *plan = p;
-    l.total = p.splits > 1 ? align256((size_t)p.splits * d->K * d->C * 4) : 0;
+    l.total = align256(wg_partial_bytes(d->K, d->C, p.splits));  // partials only
     return l;
   }
   if (use_im2col(d)) {
     const int Kc = im2col_channels(d);
     WgPlan p = plan_im_wg(d->N, d->K, Kc, (int64_t)d->P * d->Q);
     if (plan) *plan = p;
-    l.c = align256((size_t)d->N * d->P * d->Q * Kc * 4);                     // im2col columns, then partials
-    l.total = l.c + align256((size_t)p.splits * Kc * d->K * 4);
+    l.c = align256((size_t)d->N * d->P * d->Q * Kc * 4);  // im2col columns, then partials
+    l.total = l.c + align256(wg_partial_bytes(Kc, d->K, p.splits));
     return l;
   }
   const int Kp = round4(d->K);
@@ -1039,10 +1078,10 @@ static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
   const int taps = d->R * d->S;
   WgPlan p = plan_wg(d->N, d->K, d->C, d->P, d->Q, taps);
   if (plan) *plan = p;
-  l.a = 0;                                                                   // x channels-last
-  l.b = align256((size_t)d->N * d->H * d->W * Cx * 4);                       // dy channels-last
-  l.c = l.b + align256((size_t)d->N * d->P * d->Q * Kp * 4);                 // partials
-  l.total = l.c + align256((size_t)p.splits * d->K * d->C * taps * 4);
+  l.a = 0;                                                     // x channels-last
+  l.b = align256((size_t)d->N * d->H * d->W * Cx * 4);         // dy channels-last
+  l.c = l.b + align256((size_t)d->N * d->P * d->Q * Kp * 4);   // partials
+  l.total = l.c + align256(wg_partial_bytes(d->K, d->C, p.splits * taps));
   return l;
 }
 
@@ -1182,28 +1221,25 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
   if (!tc_conv_shape_ok(d)) return PVB2_OK;
   WgPlan p;
   Layout l = wgrad_layout(d, &p);
-  const int64_t wn = (int64_t)d->K * d->C * d->R * d->S;
+  if (!ws || ws_bytes < l.total) return PVB2_OK;  // not enough scratch: exact path
+  const int RS = d->R * d->S;
   if (pointwise(d)) {
     if (!aligned16(x) || !aligned16(dy)) return PVB2_OK;
-    if (p.splits > 1 && (!ws || ws_bytes < l.total)) return PVB2_OK;
-    float* part = p.splits > 1 ? (float*)ws : dw;
+    float* part = (float*)ws;
     PVB2_TRY(run_pw_wgrad(dy, x, d->N, d->C, d->K, (int64_t)d->H * d->W, p, part, s));
-    if (p.splits > 1) {
-      sum_partials_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, wn, dw);
-      PVB2_LAUNCH_CHECK();
-    }
+    // partials [sp][c][k] -> dW[k][c]
+    PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->K, d->C, d->K, d->C, dw, d->C, 1, 0, s));
     *handled = true;
     return PVB2_OK;
   }
-  if (!ws || ws_bytes < l.total) return PVB2_OK;
   if (use_im2col(d)) {
-    const int Kc = im2col_channels(d);
+    const int Kc = im2col_channels(d), crs = d->C * RS;
     float* xcol = (float*)ws;
     float* part = (float*)((char*)ws + l.c);
     PVB2_TRY(im2col(d, x, xcol, s));
     PVB2_TRY(run_im_wgrad(xcol, Kc, dy, d->N, d->K, (int64_t)d->P * d->Q, p, part, s));
-    sum_transpose_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, d->K, d->C * d->R * d->S, Kc, dw);
-    PVB2_LAUNCH_CHECK();
+    // partials [sp][k][j] -> dW[k][j] for the crs real columns
+    PVB2_TRY(wgrad_reduce(part, p.splits, 1, Kc, d->K, crs, d->K, dw, 1, crs, 0, s));
     *handled = true;
     return PVB2_OK;
   }
@@ -1214,14 +1250,10 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
   PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
   const int Cp = round4(d->C);
   PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
-  // one split: the partials layout [1][K][C][R*S] is dW itself
-  float* dst = p.splits > 1 ? part : dw;
   PVB2_TRY(run_wgrad(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h, d->stride_w,
-                     p, dst, s));
-  if (p.splits > 1) {
-    sum_partials_kernel<<<grid_for(wn, 256), 256, 0, s>>>(part, p.splits, wn, dw);
-    PVB2_LAUNCH_CHECK();
-  }
+                     p, part, s));
+  // partials [sp][rs][c][k] -> dW[k][c][rs]
+  PVB2_TRY(wgrad_reduce(part, p.splits, RS, d->K, d->C, d->K, d->C, dw, (int64_t)d->C * RS, RS, 1, s));
   *handled = true;
   return PVB2_OK;
 }
