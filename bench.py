@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--model", default=MODEL)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--deadline-s", type=float, default=600.0,
+                    help="multi-GPU runs abort the NCCL communicator and exit 3 after this many seconds")
     return ap.parse_args()
 
 
@@ -144,6 +146,22 @@ def conv_flops_per_step(model, x):
     return total * x.shape[0], conv * x.shape[0]
 
 
+def _watchdog(comm, seconds):
+    """Multi-GPU runs: if the whole run has not finished after `seconds`, abort
+    the NCCL communicator (unblocking any collective waiting for a peer) and
+    exit with status 3 instead of waiting forever."""
+    def fire():
+        sys.stderr.write(f"bench: no completion after {seconds:.0f} s, aborting the NCCL communicator\n")
+        try:
+            comm.close(abort=True)
+        finally:
+            os._exit(3)
+
+    t = threading.Timer(seconds, fire)
+    t.daemon = True
+    t.start()
+
+
 def run_ours(a):
     import pytorch_vulkan_b200 as pvb2
     from pytorch_vulkan_b200 import _C
@@ -154,6 +172,8 @@ def run_ours(a):
     rank, world, local, comm = init_process_group()
     if world == 1:
         torch.ocl.set_device(0)
+    else:
+        _watchdog(comm, a.deadline_s)
     dev = f"ocl:{local}"
     torch.manual_seed(0)
     model = omodels.build(a.model, 0)
@@ -234,8 +254,13 @@ def run_ours(a):
                "d2h_bytes_per_step": 4, "ms_per_step": round(ems, 3)}
 
     # --------------------------------------- dominant kernel class roofline
+    # every rank runs this step (its gradient all-reduces must be matched on
+    # all ranks); rank 0 records it under the profiler
     roof = None
-    if rank == 0:
+    if rank != 0:
+        step(x, y)
+        torch.ocl.synchronize(local)
+    else:
         import csv
         import tempfile
 
