@@ -821,13 +821,14 @@ struct WgPlan {
 
 // out_elems: K x Cin x taps weights; in_bytes: the operand bytes the
 // reduction streams.  Splits also cost their partials (written once, read
-// once), so they stop where that traffic would exceed the operands'.
+// once), so they stop where that traffic would pass a quarter of the
+// operands'.
 static void plan_splits(WgPlan& w, int taps, double out_elems, double in_bytes) {
   const int base_tiles = w.kt * w.ct * taps;
   int splits = (2 * num_sms() + base_tiles - 1) / base_tiles;
   splits = std::min(splits, std::max(1, w.total_kb / 8));
   splits = std::max(1, std::min(splits, 64));
-  while (splits > 1 && (double)splits * out_elems * 8.0 > in_bytes) --splits;
+  while (splits > 1 && (double)splits * out_elems * 8.0 > in_bytes / 4) --splits;
   w.kb_per = (w.total_kb + splits - 1) / splits;
   w.splits = (w.total_kb + w.kb_per - 1) / w.kb_per;
 }

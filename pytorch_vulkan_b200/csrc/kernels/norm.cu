@@ -5,11 +5,10 @@
 // batch-norm-over-(1,B,N) trick the reference used for layer norm
 // (norm_ops.cpp:167-351).
 //
-// Training batch norm on NCHW-contiguous x whose channels each fit the shared
-// memory of one thread-block cluster (<= 8 CTAs, up to 1.7 MB of fp32 per
-// channel in the forward, 0.85 MB per tensor in the backward) runs as ONE
-// cluster-resident launch that reads its inputs once (bn_fwd_cluster_kernel,
-// bn_bwd_cluster_kernel below).  Larger channels run as two launches:
+// Training batch norm runs as two streaming launches over fixed element
+// ranges of each channel (bn_st_* below: statistics, then apply in reverse
+// channel order so the second read mostly hits L2).  Tensors with more than
+// 65535 channels or 2^30 elements per channel use the plane-based kernels:
 //   1. stats:   grid (C, splits); each CTA reduces whole (n, c) planes with
 //               128-bit loads into a shifted sum / sum of squares; the
 //               per-CTA partials go to the caller's workspace.
@@ -20,11 +19,10 @@
 //               save_invstd and updates the running statistics.
 // The backward pass has the same shape: a reduction of (sum dy,
 // sum dy*(x-mean)) per channel, then an apply pass for dx.
-#include <cooperative_groups.h>
+#include <algorithm>
 #include <mutex>
 #include "common.cuh"
 
-namespace cg = cooperative_groups;
 
 namespace pvb2 {
 
@@ -282,40 +280,6 @@ __global__ void bn_bwd_eval_kernel(const float* __restrict__ dy, const float* __
   for (int64_t i = threadIdx.x; i < HW; i += blockDim.x) o[i] = g[i] * mul;
 }
 
-// ------------------------------------------- batch norm, cluster-resident
-// When one channel's data fits the shared memory of a thread-block cluster
-// (<= 8 CTAs), the training forward and backward each read their inputs from
-// HBM once: grid (k, C) with clusters of k CTAs along x, CTA r of channel c
-// holds elements [r*chunk, (r+1)*chunk) of the channel's (n, hw) range in
-// shared memory, partial sums meet through distributed shared memory, and
-// the output is written from the resident copy.  Each CTA reduces its own
-// elements first (the forward in two passes over shared memory: mean, then
-// squared deviations), one cluster barrier publishes the per-CTA results,
-// and every CTA combines them in double in rank order (the forward with
-// Chan's pairwise formula for (count, mean, M2)).
-constexpr int kBnClThreads = 512;
-constexpr int kBnClMaxCluster = 8;
-constexpr int kBnClSmallBytes = 110 * 1024;  // two CTAs per SM
-constexpr int kBnClBigBytes = 220 * 1024;    // one CTA per SM
-
-// sum over the block; every thread gets the result
-__device__ __forceinline__ float block_allsum(float v, float* red) {
-  v = warp_sum(v);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  __syncthreads();  // red may still be read by a previous call
-  if (lane == 0) red[wid] = v;
-  __syncthreads();
-  float t = 0.f;
-  const int nw = blockDim.x >> 5;
-  for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
-}
-
-// split cluster barrier: arrive (release) once this CTA's distributed
-// shared-memory reads are done, wait (acquire) before leaving
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-
 // Position of element e = n*HW + i of one channel, advanced by a fixed step
 // without dividing in the loop.
 struct ChanWalk {
@@ -336,271 +300,347 @@ struct ChanWalk {
   }
 };
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// ------------------------------------------ batch norm, two streaming passes
+// Training batch norm as two grid-wide passes over fixed element ranges:
+//   stats  grid (splits, C): CTA (s, c) reduces elements [s*chunk, (s+1)*chunk)
+//          of channel c's (n, hw) range to a shifted sum and sum of squares
+//          (shift = the channel's first element) in the workspace;
+//   apply  grid (splits, C), channels in reverse order so that the ranges the
+//          stats pass read last (still in L2) are read first: thread 0 folds
+//          the channel's partials in double, then the CTA writes its range.
+// A channel's range is walked with 128-bit accesses when HW % 4 == 0.  The
+// backward has the same shape: sums of dy and dy*(x - mean), then dx.
+constexpr int kBnStThreads = 256;
+constexpr int kBnStChunk = 16384;  // elements of one channel per CTA (64 KB)
 
-// Start asynchronous copies of this CTA's elements [start, end) of channel c
-// into shared memory (16-byte copies when vec: HW % 4 == 0 and aligned).
-// The caller waits with cp_async_wait_all + __syncthreads.
-__device__ __forceinline__ void bn_cl_load(const float* __restrict__ src, float* __restrict__ dst, int start, int end,
-                                           int HW, int64_t nstride, bool vec) {
-  const int vw = vec ? 4 : 1;
-  const int step = vw * blockDim.x;
-  int e = start + vw * threadIdx.x;
-  if (e >= end) return;
-  ChanWalk w(e, step, HW);
-  if (vec) {
-    for (; e < end; e += step, w.next()) cp_async16(dst + (e - start), src + w.n * nstride + w.i);
-  } else {
-    for (; e < end; e += step, w.next()) cp_async4(dst + (e - start), src + w.n * nstride + w.i);
-  }
+struct BnStream {
+  int splits, chunk;
+  bool vec;
+};
+
+// channels on grid y, 32-bit element indices within a channel
+static bool bn_streamable(const BnGeom& g) {
+  return g.C <= 65535 && g.N * g.HW < ((int64_t)1 << 30) && g.N * g.HW > 0;
 }
 
-__global__ void __launch_bounds__(kBnClThreads) bn_fwd_cluster_kernel(
-    const float* __restrict__ x, float* __restrict__ y, int N, int C, int HW, int chunk, int vec,
-    const float* __restrict__ gamma, const float* __restrict__ beta, float* __restrict__ running_mean,
-    float* __restrict__ running_var, float momentum, float eps, float* __restrict__ save_mean,
-    float* __restrict__ save_invstd) {
-  extern __shared__ __align__(16) float sx[];
-  __shared__ float red[32];
-  __shared__ float cl_part[3];  // count, mean, M2 of this CTA's elements
-  __shared__ float s_coef[2];
-  cg::cluster_group cl = cg::this_cluster();
-  const int r = (int)cl.block_rank(), k = (int)cl.num_blocks();
-  const int c = blockIdx.y;
-  const int M = N * HW;
-  const int start = r * chunk, end = min(M, start + chunk), len = max(0, end - start);
-  const int64_t nstride = (int64_t)C * HW;
-  bn_cl_load(x + (int64_t)c * HW, sx, start, end, HW, nstride, vec != 0);
-  cp_async_wait_all();
+static BnStream bn_stream_plan(const BnGeom& g, const void* const* ptrs, int nptr) {
+  BnStream p;
+  const int64_t M = g.N * g.HW;
+  int64_t splits = (M + kBnStChunk - 1) / kBnStChunk;
+  // enough CTAs for every SM twice, but no range below 1024 elements
+  const int64_t want = (2 * (int64_t)num_sms() + g.C - 1) / std::max<int64_t>(g.C, 1);
+  splits = std::max(splits, std::min(want, (M + 1023) / 1024));
+  splits = std::max<int64_t>(1, std::min<int64_t>(splits, 65535));
+  int64_t chunk = (M + splits - 1) / splits;
+  chunk = (chunk + 3) / 4 * 4;
+  p.chunk = (int)chunk;
+  p.splits = (int)((M + chunk - 1) / chunk);
+  p.vec = (g.HW & 3) == 0;
+  for (int i = 0; i < nptr; ++i)
+    if (ptrs[i] && ((uintptr_t)ptrs[i] & 15)) p.vec = false;
+  return p;
+}
+
+// sum of two values over the block; every thread gets the results
+__device__ __forceinline__ void block_allsum2(float& a, float& b, float* red) {
+  a = warp_sum(a);
+  b = warp_sum(b);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   __syncthreads();
-  // this CTA's mean and sum of squared deviations: two passes over shared memory
-  float s = 0.f;
-  for (int i = threadIdx.x; i < len; i += blockDim.x) s += sx[i];
-  const float lmean = len ? block_allsum(s, red) / (float)len : 0.f;
-  float s2 = 0.f;
-  for (int i = threadIdx.x; i < len; i += blockDim.x) {
-    const float d = sx[i] - lmean;
-    s2 += d * d;
+  if (lane == 0) {
+    red[wid] = a;
+    red[32 + wid] = b;
   }
-  s2 = block_allsum(s2, red);
-  if (threadIdx.x == 0) {
-    cl_part[0] = (float)len;
-    cl_part[1] = lmean;
-    cl_part[2] = s2;
+  __syncthreads();
+  a = 0.f;
+  b = 0.f;
+  for (int i = 0; i < nw; ++i) {
+    a += red[i];
+    b += red[32 + i];
   }
-  cl.sync();
-  if (threadIdx.x == 0) {
-    // Chan's pairwise combination, in double, in rank order
-    double n = 0.0, mean = 0.0, m2 = 0.0;
-    for (int q = 0; q < k; ++q) {
-      const float* pq = cl.map_shared_rank(cl_part, q);
-      const double nq = pq[0];
-      if (nq == 0.0) continue;
-      const double nn = n + nq, d = (double)pq[1] - mean;
-      mean += d * nq / nn;
-      m2 += (double)pq[2] + d * d * n * nq / nn;
-      n = nn;
+}
+
+__global__ void __launch_bounds__(kBnStThreads) bn_st_stats_kernel(const float* __restrict__ x, int N, int C, int HW,
+                                                                   int chunk, int splits, int vec,
+                                                                   float* __restrict__ part) {
+  __shared__ float red[64];
+  const int s = blockIdx.x, c = blockIdx.y;
+  const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
+  const int64_t nstride = (int64_t)C * HW;
+  const float* xc = x + (int64_t)c * HW;
+  const float shift = __ldg(xc);
+  float s1 = 0.f, s2 = 0.f;
+  const int vw = vec ? 4 : 1, step = vw * blockDim.x;
+  int e = start + vw * threadIdx.x;
+  if (e < end) {
+    ChanWalk w(e, step, HW);
+    if (vec) {
+      // four 128-bit loads in flight per thread
+      for (; e < end; e += 4 * step) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          v[u] = e + u * step < end ? __ldg(reinterpret_cast<const float4*>(xc + w.n * nstride + w.i))
+                                    : make_float4(shift, shift, shift, shift);
+          w.next();
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float a = v[u].x - shift, b = v[u].y - shift, d = v[u].z - shift, f = v[u].w - shift;
+          s1 += (a + b) + (d + f);
+          s2 += (a * a + b * b) + (d * d + f * f);
+        }
+      }
+    } else {
+      for (; e < end; e += 4 * step) {
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          v[u] = e + u * step < end ? __ldg(xc + w.n * nstride + w.i) : shift;
+          w.next();
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float a = v[u] - shift;
+          s1 += a;
+          s2 += a * a;
+        }
+      }
     }
-    const double var = m2 / n;
+  }
+  block_allsum2(s1, s2, red);
+  if (threadIdx.x == 0) {
+    part[((int64_t)c * splits + s) * 2 + 0] = s1;
+    part[((int64_t)c * splits + s) * 2 + 1] = s2;
+  }
+}
+
+__global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
+    const float* __restrict__ x, float* __restrict__ y, int N, int C, int HW, int chunk, int splits, int vec,
+    const float* __restrict__ part, const float* __restrict__ gamma, const float* __restrict__ beta,
+    float* __restrict__ running_mean, float* __restrict__ running_var, float momentum, float eps,
+    float* __restrict__ save_mean, float* __restrict__ save_invstd) {
+  __shared__ float s_ab[2];
+  const int s = blockIdx.x, c = C - 1 - blockIdx.y;
+  const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
+  const int64_t nstride = (int64_t)C * HW;
+  const float* xc = x + (int64_t)c * HW;
+  if (threadIdx.x == 0) {
+    double s1 = 0.0, s2 = 0.0;
+    for (int k = 0; k < splits; ++k) {
+      s1 += (double)part[((int64_t)c * splits + k) * 2 + 0];
+      s2 += (double)part[((int64_t)c * splits + k) * 2 + 1];
+    }
+    const double count = (double)M;
+    const double m = s1 / count;
+    double var = s2 / count - m * m;
+    if (var < 0.0) var = 0.0;
+    const double mean = m + (double)__ldg(xc);
     const float invstd = (float)(1.0 / sqrt(var + (double)eps));
     const float meanf = (float)mean;
     const float g = gamma ? gamma[c] : 1.f;
     const float b = beta ? beta[c] : 0.f;
     const float a = invstd * g;
-    s_coef[0] = a;
-    s_coef[1] = b - meanf * a;
-    if (r == 0) {
+    s_ab[0] = a;
+    s_ab[1] = b - meanf * a;
+    if (s == 0) {
       if (save_mean) save_mean[c] = meanf;
       if (save_invstd) save_invstd[c] = invstd;
       if (running_mean) running_mean[c] = (1.f - momentum) * running_mean[c] + momentum * meanf;
       if (running_var) {
-        const double unbiased = n > 1.0 ? var * n / (n - 1.0) : var;
+        const double unbiased = count > 1.0 ? var * count / (count - 1.0) : var;
         running_var[c] = (1.f - momentum) * running_var[c] + momentum * (float)unbiased;
       }
     }
   }
-  cluster_arrive();  // this CTA is done reading its peers' statistics
   __syncthreads();
-  const float a = s_coef[0], b = s_coef[1];
+  const float a = s_ab[0], b = s_ab[1];
   float* yc = y + (int64_t)c * HW;
+  const int vw = vec ? 4 : 1, step = vw * blockDim.x;
+  int e = start + vw * threadIdx.x;
+  if (e >= end) return;
+  ChanWalk w(e, step, HW);
+  if (vec) {
+    for (; e < end; e += 4 * step) {
+      float4 v[4];
+      int64_t o[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        o[u] = w.n * nstride + w.i;
+        if (e + u * step < end) v[u] = __ldg(reinterpret_cast<const float4*>(xc + o[u]));
+        w.next();
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (e + u * step < end) {
+          float4 r = v[u];
+          r.x = fmaf(r.x, a, b);
+          r.y = fmaf(r.y, a, b);
+          r.z = fmaf(r.z, a, b);
+          r.w = fmaf(r.w, a, b);
+          *reinterpret_cast<float4*>(yc + o[u]) = r;
+        }
+      }
+    }
+  } else {
+    for (; e < end; e += 4 * step) {
+      float v[4];
+      int64_t o[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        o[u] = w.n * nstride + w.i;
+        if (e + u * step < end) v[u] = __ldg(xc + o[u]);
+        w.next();
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (e + u * step < end) yc[o[u]] = fmaf(v[u], a, b);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
+    const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean, int N, int C, int HW,
+    int chunk, int splits, int vec, float* __restrict__ part) {
+  __shared__ float red[64];
+  const int s = blockIdx.x, c = blockIdx.y;
+  const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
+  const int64_t nstride = (int64_t)C * HW;
+  const float* gc = dy + (int64_t)c * HW;
+  const float* xc = x + (int64_t)c * HW;
+  const float m = mean[c];
+  float sg = 0.f, sd = 0.f;
   const int vw = vec ? 4 : 1, step = vw * blockDim.x;
   int e = start + vw * threadIdx.x;
   if (e < end) {
     ChanWalk w(e, step, HW);
     if (vec) {
       for (; e < end; e += step, w.next()) {
-        float4 v = *reinterpret_cast<const float4*>(sx + (e - start));
-        v.x = fmaf(v.x, a, b);
-        v.y = fmaf(v.y, a, b);
-        v.z = fmaf(v.z, a, b);
-        v.w = fmaf(v.w, a, b);
-        *reinterpret_cast<float4*>(yc + w.n * nstride + w.i) = v;
+        const int64_t o = w.n * nstride + w.i;
+        const float4 g = __ldg(reinterpret_cast<const float4*>(gc + o));
+        const float4 v = __ldg(reinterpret_cast<const float4*>(xc + o));
+        sg += (g.x + g.y) + (g.z + g.w);
+        sd += (g.x * (v.x - m) + g.y * (v.y - m)) + (g.z * (v.z - m) + g.w * (v.w - m));
       }
     } else {
-      for (; e < end; e += step, w.next()) yc[w.n * nstride + w.i] = fmaf(sx[e - start], a, b);
+      for (; e < end; e += 4 * step) {
+        float g[4], v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t o = w.n * nstride + w.i;
+          g[u] = 0.f;
+          v[u] = m;
+          if (e + u * step < end) {
+            g[u] = __ldg(gc + o);
+            v[u] = __ldg(xc + o);
+          }
+          w.next();
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          sg += g[u];
+          sd += g[u] * (v[u] - m);
+        }
+      }
     }
   }
-  cluster_wait();  // no CTA leaves while a peer may still read its statistics
+  block_allsum2(sg, sd, red);
+  if (threadIdx.x == 0) {
+    part[((int64_t)c * splits + s) * 2 + 0] = sg;
+    part[((int64_t)c * splits + s) * 2 + 1] = sd;
+  }
 }
 
-__global__ void __launch_bounds__(kBnClThreads) bn_bwd_cluster_kernel(
+__global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_apply_kernel(
     const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
-    const float* __restrict__ invstd, const float* __restrict__ gamma, int N, int C, int HW, int chunk, int vec,
-    float* __restrict__ dx, float* __restrict__ dgamma, float* __restrict__ dbeta) {
-  extern __shared__ __align__(16) float smem_bn[];
-  float* sdy = smem_bn;
-  float* sx = smem_bn + chunk;
-  __shared__ float red[32];
-  __shared__ float cl_part[2];
-  __shared__ float s_coef[3];
-  cg::cluster_group cl = cg::this_cluster();
-  const int r = (int)cl.block_rank(), k = (int)cl.num_blocks();
-  const int c = blockIdx.y;
-  const int M = N * HW;
-  const int start = r * chunk, end = min(M, start + chunk), len = max(0, end - start);
+    const float* __restrict__ invstd, const float* __restrict__ gamma, int N, int C, int HW, int chunk, int splits,
+    int vec, const float* __restrict__ part, float* __restrict__ dx, float* __restrict__ dgamma,
+    float* __restrict__ dbeta) {
+  __shared__ float s_k[3];
+  const int s = blockIdx.x, c = C - 1 - blockIdx.y;
+  const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
   const int64_t nstride = (int64_t)C * HW;
-  bn_cl_load(dy + (int64_t)c * HW, sdy, start, end, HW, nstride, vec != 0);
-  bn_cl_load(x + (int64_t)c * HW, sx, start, end, HW, nstride, vec != 0);
-  cp_async_wait_all();
-  __syncthreads();
-  const float m = mean[c];
-  float s_dy = 0.f, s_dot = 0.f;
-  for (int i = threadIdx.x; i < len; i += blockDim.x) {
-    const float g = sdy[i];
-    s_dy += g;
-    s_dot += g * (sx[i] - m);
-  }
-  s_dy = block_allsum(s_dy, red);
-  s_dot = block_allsum(s_dot, red);
   if (threadIdx.x == 0) {
-    cl_part[0] = s_dy;
-    cl_part[1] = s_dot;
-  }
-  cl.sync();
-  if (threadIdx.x == 0) {
-    double sdy_all = 0.0, sdot_all = 0.0;
-    for (int q = 0; q < k; ++q) {
-      const float* pq = cl.map_shared_rank(cl_part, q);
-      sdy_all += (double)pq[0];
-      sdot_all += (double)pq[1];
+    double sg = 0.0, sd = 0.0;
+    for (int k = 0; k < splits; ++k) {
+      sg += (double)part[((int64_t)c * splits + k) * 2 + 0];
+      sd += (double)part[((int64_t)c * splits + k) * 2 + 1];
     }
     const double count = (double)M;
     const float is = invstd[c];
-    s_coef[0] = (float)(sdy_all / count);              // mean of dy
-    s_coef[1] = (float)(sdot_all / count) * is * is;   // dotp * invstd^2 / count
-    s_coef[2] = is * (gamma ? gamma[c] : 1.f);
-    if (r == 0) {
-      if (dgamma) dgamma[c] = (float)sdot_all * is;
-      if (dbeta) dbeta[c] = (float)sdy_all;
+    s_k[0] = (float)(sg / count);             // mean of dy
+    s_k[1] = (float)(sd / count) * is * is;   // dotp * invstd^2 / count
+    s_k[2] = is * (gamma ? gamma[c] : 1.f);
+    if (s == 0) {
+      if (dgamma) dgamma[c] = (float)sd * is;
+      if (dbeta) dbeta[c] = (float)sg;
     }
   }
-  cluster_arrive();  // this CTA is done reading its peers' sums
   __syncthreads();
-  if (dx) {
-    const float gm = s_coef[0], kk = s_coef[1], mul = s_coef[2];
-    float* dxc = dx + (int64_t)c * HW;
-    const int vw = vec ? 4 : 1, step = vw * blockDim.x;
-    int e = start + vw * threadIdx.x;
-    if (e < end) {
-      ChanWalk w(e, step, HW);
-      if (vec) {
-        for (; e < end; e += step, w.next()) {
-          const float4 g = *reinterpret_cast<const float4*>(sdy + (e - start));
-          const float4 v = *reinterpret_cast<const float4*>(sx + (e - start));
-          float4 o;
-          o.x = (g.x - gm - (v.x - m) * kk) * mul;
-          o.y = (g.y - gm - (v.y - m) * kk) * mul;
-          o.z = (g.z - gm - (v.z - m) * kk) * mul;
-          o.w = (g.w - gm - (v.w - m) * kk) * mul;
-          *reinterpret_cast<float4*>(dxc + w.n * nstride + w.i) = o;
+  if (!dx) return;
+  const float gm = s_k[0], kk = s_k[1], mul = s_k[2], m = mean[c];
+  const float* gc = dy + (int64_t)c * HW;
+  const float* xc = x + (int64_t)c * HW;
+  float* dc = dx + (int64_t)c * HW;
+  const int vw = vec ? 4 : 1, step = vw * blockDim.x;
+  int e = start + vw * threadIdx.x;
+  if (e >= end) return;
+  ChanWalk w(e, step, HW);
+  if (vec) {
+    for (; e < end; e += step, w.next()) {
+      const int64_t o = w.n * nstride + w.i;
+      const float4 g = __ldg(reinterpret_cast<const float4*>(gc + o));
+      const float4 v = __ldg(reinterpret_cast<const float4*>(xc + o));
+      float4 r;
+      r.x = (g.x - gm - (v.x - m) * kk) * mul;
+      r.y = (g.y - gm - (v.y - m) * kk) * mul;
+      r.z = (g.z - gm - (v.z - m) * kk) * mul;
+      r.w = (g.w - gm - (v.w - m) * kk) * mul;
+      *reinterpret_cast<float4*>(dc + o) = r;
+    }
+  } else {
+    for (; e < end; e += 4 * step) {
+      float g[4], v[4];
+      int64_t o[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        o[u] = w.n * nstride + w.i;
+        if (e + u * step < end) {
+          g[u] = __ldg(gc + o[u]);
+          v[u] = __ldg(xc + o[u]);
         }
-      } else {
-        for (; e < end; e += step, w.next())
-          dxc[w.n * nstride + w.i] = (sdy[e - start] - gm - (sx[e - start] - m) * kk) * mul;
+        w.next();
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (e + u * step < end) dc[o[u]] = (g[u] - gm - (v[u] - m) * kk) * mul;
     }
   }
-  cluster_wait();  // no CTA leaves while a peer may still read its sums
 }
 
-struct BnCluster {
-  int k, chunk, smem;
-  bool vec;
-};
-
-// plan a cluster-resident launch holding `arrays` fp32 tensors per element;
-// false when a channel does not fit 8 CTAs' shared memory
-static bool bn_cluster_plan(const BnGeom& g, int arrays, const void* const* ptrs, int nptr, BnCluster* p) {
-  const int64_t M = g.N * g.HW;
-  if (M <= 0 || g.C > 65535 || M > (int64_t)1 << 30) return false;
-  bool vec = (g.HW & 3) == 0;
-  for (int i = 0; i < nptr; ++i)
-    if (ptrs[i] && ((uintptr_t)ptrs[i] & 15)) vec = false;
-  for (int budget : {kBnClSmallBytes, kBnClBigBytes}) {
-    const int64_t per = budget / (4 * arrays) / 4 * 4;  // elements per CTA, multiple of 4
-    const int64_t k = (M + per - 1) / per;
-    if (k > kBnClMaxCluster) continue;
-    int64_t chunk = (M + k - 1) / k;
-    chunk = (chunk + 3) / 4 * 4;
-    p->k = (int)k;
-    p->chunk = (int)chunk;
-    p->smem = (int)(chunk * 4 * arrays);
-    p->vec = vec;
-    return true;
-  }
-  return false;
-}
-
-// launch configuration of a cluster-resident kernel: grid (k, C), clusters (k, 1, 1)
-struct BnClusterLaunch {
-  cudaLaunchConfig_t cfg;
-  cudaLaunchAttribute attr[1];
-  BnClusterLaunch(const BnCluster& p, int C, cudaStream_t s) {
-    cfg = cudaLaunchConfig_t{};
-    cfg.gridDim = dim3((unsigned)p.k, (unsigned)C, 1);
-    cfg.blockDim = dim3(kBnClThreads, 1, 1);
-    cfg.dynamicSmemBytes = (size_t)p.smem;
-    cfg.stream = s;
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)p.k;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  }
-};
-
-static int bn_fwd_cluster(const BnGeom& g, const BnCluster& p, const float* x, float* y, const float* gamma,
-                          const float* beta, float* running_mean, float* running_var, double momentum, double eps,
-                          float* save_mean, float* save_invstd, cudaStream_t s) {
-  static std::atomic<uint64_t> attr_done{0};
-  if (first_on_device(attr_done))
-    PVB2_CUDA_TRY(cudaFuncSetAttribute(bn_fwd_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBnClBigBytes));
-  BnClusterLaunch L(p, (int)g.C, s);
-  PVB2_CUDA_TRY(cudaLaunchKernelEx(&L.cfg, bn_fwd_cluster_kernel, x, y, (int)g.N, (int)g.C, (int)g.HW, p.chunk,
-                                   p.vec ? 1 : 0, gamma, beta, running_mean, running_var, (float)momentum, (float)eps,
-                                   save_mean, save_invstd));
+static int bn_fwd_stream(const BnGeom& g, const BnStream& p, const float* x, float* y, const float* gamma,
+                         const float* beta, float* running_mean, float* running_var, double momentum, double eps,
+                         float* save_mean, float* save_invstd, float* part, cudaStream_t s) {
+  const dim3 grid((unsigned)p.splits, (unsigned)g.C);
+  bn_st_stats_kernel<<<grid, kBnStThreads, 0, s>>>(x, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits, p.vec ? 1 : 0,
+                                                    part);
+  PVB2_LAUNCH_CHECK();
+  bn_st_apply_kernel<<<grid, kBnStThreads, 0, s>>>(x, y, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits,
+                                                    p.vec ? 1 : 0, part, gamma, beta, running_mean, running_var,
+                                                    (float)momentum, (float)eps, save_mean, save_invstd);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
 
-static int bn_bwd_cluster(const BnGeom& g, const BnCluster& p, const float* dy, const float* x, const float* mean,
-                          const float* invstd, const float* gamma, float* dx, float* dgamma, float* dbeta,
-                          cudaStream_t s) {
-  static std::atomic<uint64_t> attr_done{0};
-  if (first_on_device(attr_done))
-    PVB2_CUDA_TRY(cudaFuncSetAttribute(bn_bwd_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBnClBigBytes));
-  BnClusterLaunch L(p, (int)g.C, s);
-  PVB2_CUDA_TRY(cudaLaunchKernelEx(&L.cfg, bn_bwd_cluster_kernel, dy, x, mean, invstd, gamma, (int)g.N, (int)g.C,
-                                   (int)g.HW, p.chunk, p.vec ? 1 : 0, dx, dgamma, dbeta));
+static int bn_bwd_stream(const BnGeom& g, const BnStream& p, const float* dy, const float* x, const float* mean,
+                         const float* invstd, const float* gamma, float* dx, float* dgamma, float* dbeta, float* part,
+                         cudaStream_t s) {
+  const dim3 grid((unsigned)p.splits, (unsigned)g.C);
+  bn_st_bwd_reduce_kernel<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, (int)g.N, (int)g.C, (int)g.HW, p.chunk,
+                                                         p.splits, p.vec ? 1 : 0, part);
+  PVB2_LAUNCH_CHECK();
+  bn_st_bwd_apply_kernel<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, invstd, gamma, (int)g.N, (int)g.C, (int)g.HW,
+                                                        p.chunk, p.splits, p.vec ? 1 : 0, part, dx, dgamma, dbeta);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
@@ -799,7 +839,9 @@ extern "C" {
 size_t pvb2_batch_norm_workspace_size(const pvb2_tensor* x) {
   if (x->ndim < 2) return 0;
   BnGeom g = bn_geom(x);
-  return (size_t)g.C * g.splits * 2 * sizeof(float);
+  size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
+  if (bn_streamable(g)) need = std::max(need, (size_t)g.C * bn_stream_plan(g, nullptr, 0).splits * 2 * sizeof(float));
+  return need;
 }
 
 int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma, const float* beta, float* running_mean,
@@ -810,11 +852,15 @@ int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma, const fl
   BnGeom g = bn_geom(x);
   if (g.N * g.HW == 0 || g.C == 0) return PVB2_OK;
   cudaStream_t s = as_stream(stream);
-  BnCluster cp;
-  const void* ptrs[2] = {x->data, y->data};
-  if (bn_cluster_plan(g, 1, ptrs, 2, &cp))
-    return bn_fwd_cluster(g, cp, (const float*)x->data, (float*)y->data, gamma, beta, running_mean, running_var,
-                          momentum, eps, save_mean, save_invstd, s);
+  if (bn_streamable(g)) {
+    const void* ptrs[2] = {x->data, y->data};
+    const BnStream p = bn_stream_plan(g, ptrs, 2);
+    const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
+    PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm: workspace too small (%zu < %zu)",
+                   workspace_bytes, need);
+    return bn_fwd_stream(g, p, (const float*)x->data, (float*)y->data, gamma, beta, running_mean, running_var,
+                         momentum, eps, save_mean, save_invstd, (float*)workspace, s);
+  }
   const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
   PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm: workspace too small (%zu < %zu)",
                  workspace_bytes, need);
@@ -846,11 +892,19 @@ int pvb2_batch_norm_fwd_train_noalloc(const pvb2_tensor* x, const float* gamma, 
   PVB2_CHECK_ARG(is_contiguous(y) && y->dtype == PVB2_F32, "batch_norm: output must be contiguous float32");
   BnGeom g = bn_geom(x);
   if (g.N * g.HW == 0 || g.C == 0) return PVB2_OK;
-  BnCluster cp;
-  const void* ptrs[2] = {x->data, y->data};
-  if (bn_cluster_plan(g, 1, ptrs, 2, &cp))  // needs no scratch at all
-    return bn_fwd_cluster(g, cp, (const float*)x->data, (float*)y->data, gamma, beta, running_mean, running_var,
-                          momentum, eps, save_mean, save_invstd, as_stream(stream));
+  if (bn_streamable(g)) {
+    const void* ptrs[2] = {x->data, y->data};
+    const BnStream p = bn_stream_plan(g, ptrs, 2);
+    const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
+    PVB2_CHECK_ARG(need <= sizeof(g_bn_scratch),
+                   "batch_norm_noalloc: %lld channels need %zu bytes of partials, more than the %zu-byte scratch; "
+                   "use pvb2_batch_norm_fwd_train with a workspace",
+                   (long long)g.C, need, sizeof(g_bn_scratch));
+    float* part = nullptr;
+    PVB2_TRY(bn_scratch_address(&part));
+    return bn_fwd_stream(g, p, (const float*)x->data, (float*)y->data, gamma, beta, running_mean, running_var,
+                         momentum, eps, save_mean, save_invstd, part, as_stream(stream));
+  }
   const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
   PVB2_CHECK_ARG(need <= sizeof(g_bn_scratch),
                  "batch_norm_noalloc: %lld channels need %zu bytes of partials, more than the %zu-byte scratch; "
@@ -902,11 +956,14 @@ int pvb2_batch_norm_bwd(const pvb2_tensor* dy, const pvb2_tensor* x, const float
     if (dbeta) PVB2_CUDA_TRY(cudaMemsetAsync(dbeta, 0, g.C * sizeof(float), s));
     return PVB2_OK;
   }
-  BnCluster cp;
-  const void* ptrs[3] = {dy->data, x->data, dx ? dx->data : nullptr};
-  if (bn_cluster_plan(g, 2, ptrs, 3, &cp))
-    return bn_bwd_cluster(g, cp, (const float*)dy->data, (const float*)x->data, mean, invstd, gamma,
-                          dx ? (float*)dx->data : nullptr, dgamma, dbeta, s);
+  if (bn_streamable(g)) {
+    const void* ptrs[3] = {dy->data, x->data, dx ? dx->data : nullptr};
+    const BnStream p = bn_stream_plan(g, ptrs, 3);
+    const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
+    PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm_backward: workspace too small");
+    return bn_bwd_stream(g, p, (const float*)dy->data, (const float*)x->data, mean, invstd, gamma,
+                         dx ? (float*)dx->data : nullptr, dgamma, dbeta, (float*)workspace, s);
+  }
   const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
   PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm_backward: workspace too small");
   float* part = (float*)workspace;
