@@ -599,36 +599,6 @@ __global__ void pack_w_rows_kernel(const float* __restrict__ w, float* __restric
   }
 }
 
-// Strided-convolution dgrad: dX[n, c, h, w] = phase (h % sh, w % sw) buffer
-// element [n, c, h / sh, w / sw], or 0 for a phase no filter tap reaches.
-// grid (ceil(H*W / 256), min(planes, 65535)).
-constexpr int kMaxPhases = 16;
-struct PhaseBufs {
-  const float* p[kMaxPhases];
-  int hph[kMaxPhases], wph[kMaxPhases];
-};
-
-__global__ void phase_interleave_kernel(float* __restrict__ dx, PhaseBufs pb, int64_t planes, int H, int W, int sh,
-                                        int sw) {
-  __shared__ const float* sp[kMaxPhases];
-  __shared__ int shw[kMaxPhases], swp[kMaxPhases];
-  if (threadIdx.x < kMaxPhases) {
-    sp[threadIdx.x] = pb.p[threadIdx.x];
-    shw[threadIdx.x] = pb.hph[threadIdx.x] * pb.wph[threadIdx.x];
-    swp[threadIdx.x] = pb.wph[threadIdx.x];
-  }
-  __syncthreads();
-  const int hw = blockIdx.x * blockDim.x + threadIdx.x;
-  if (hw >= H * W) return;
-  const int h = hw / W, w = hw - (hw / W) * W;
-  const int ph = (h % sh) * sw + (w % sw);
-  const float* src = sp[ph];
-  const int64_t plane_sz = shw[ph];
-  const int off = (h / sh) * swp[ph] + (w / sw);
-  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y)
-    dx[plane * H * W + hw] = src ? __ldg(src + plane * plane_sz + off) : 0.f;
-}
-
 // ------------------------------------------------------------ host side
 static int round4(int c) { return (c + 3) / 4 * 4; }
 static int pow2_at_least(int v, int lo, int hi) {
@@ -851,14 +821,13 @@ struct WgPlan {
 
 // out_elems: K x Cin x taps weights; in_bytes: the operand bytes the
 // reduction streams.  Splits also cost their partials (written once, read
-// once), so they stop where that traffic would pass a quarter of the
-// operands'.
+// once), so they stop where that traffic would pass the operands'.
 static void plan_splits(WgPlan& w, int taps, double out_elems, double in_bytes) {
   const int base_tiles = w.kt * w.ct * taps;
   int splits = (2 * num_sms() + base_tiles - 1) / base_tiles;
   splits = std::min(splits, std::max(1, w.total_kb / 8));
   splits = std::max(1, std::min(splits, 64));
-  while (splits > 1 && (double)splits * out_elems * 8.0 > in_bytes / 4) --splits;
+  while (splits > 1 && (double)splits * out_elems * 8.0 > in_bytes) --splits;
   w.kb_per = (w.total_kb + splits - 1) / splits;
   w.splits = (w.total_kb + w.kb_per - 1) / w.kb_per;
 }
@@ -1076,32 +1045,14 @@ static Layout fwd_layout(const pvb2_conv2d_desc* d) {
   return l;
 }
 
-static bool strided(const pvb2_conv2d_desc* d) { return d->stride_h > 1 || d->stride_w > 1; }
-
-// 1x1, no padding, stride > 1: dX is zero off the stride grid and a pointwise
-// dgrad on it
-static bool strided_pointwise(const pvb2_conv2d_desc* d) {
-  return strided(d) && d->R == 1 && d->S == 1 && d->pad_h == 0 && d->pad_w == 0 && ((int64_t)d->P * d->Q) % 4 == 0 &&
-         d->C % 4 == 0 && d->K % 4 == 0;
-}
-
-// dense [N][C][Hph][Wph] buffers, one per sub-pixel phase, each 256-byte aligned
-static size_t phase_buffers_bytes(const pvb2_conv2d_desc* d) {
-  return align256((size_t)d->N * d->C * d->H * d->W * 4) + (size_t)d->stride_h * d->stride_w * 256;
-}
-
 static Layout dgrad_layout(const pvb2_conv2d_desc* d) {
   Layout l;
   l.a = l.b = l.c = l.total = 0;
   if (pointwise(d)) return l;
-  if (strided_pointwise(d)) {  // phase buffers only
-    l.total = phase_buffers_bytes(d);
-    return l;
-  }
   const int Kp = round4(d->K);
   l.b = align256((size_t)d->N * d->P * d->Q * Kp * 4);
-  l.c = l.b + align256((size_t)d->C * d->R * d->S * Kp * 4);  // one phase's packed weights at a time
-  l.total = l.c + (strided(d) ? phase_buffers_bytes(d) : 0);
+  l.total = l.b + align256((size_t)d->C * d->R * d->S * Kp * 4);  // one phase's packed weights at a time
+  l.c = l.total;
   return l;
 }
 
@@ -1199,40 +1150,9 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
   }
   Layout l = dgrad_layout(d);
   if (!ws || ws_bytes < l.total) return PVB2_OK;
-  const int64_t planes = (int64_t)d->N * d->C, hw = (int64_t)d->H * d->W;
-  // strided convolutions: every phase goes to its own dense buffer (TMA-stored),
-  // then one kernel interleaves the phases into dX
-  PhaseBufs bufs;
-  memset(&bufs, 0, sizeof(bufs));
-  float* phase_base = (float*)((char*)ws + l.c);
-  size_t phase_off = 0;
-  auto phase_buf = [&](int a, int b, int Hph, int Wph) {
-    float* p = (float*)((char*)phase_base + phase_off);
-    phase_off += align256((size_t)planes * Hph * Wph * 4);
-    bufs.p[a * d->stride_w + b] = p;
-    bufs.hph[a * d->stride_w + b] = Hph;
-    bufs.wph[a * d->stride_w + b] = Wph;
-    return p;
-  };
-  auto interleave = [&]() -> int {
-    const dim3 grid((unsigned)((hw + 255) / 256), (unsigned)std::min<int64_t>(planes, 65535));
-    phase_interleave_kernel<<<grid, 256, 0, s>>>(dx, bufs, planes, d->H, d->W, d->stride_h, d->stride_w);
-    PVB2_LAUNCH_CHECK();
-    return PVB2_OK;
-  };
-  if (strided_pointwise(d)) {
-    if (!aligned16(dy) || !aligned16(w)) return PVB2_OK;
-    // only phase (0, 0) receives the single tap; its dX pixels are the dY grid
-    float* p00 = phase_buf(0, 0, d->P, d->Q);
-    PVB2_TRY(run_pointwise(dy, w, nullptr, p00, d->N, d->C, d->K, (int64_t)d->P * d->Q, true, s));
-    PVB2_TRY(interleave());
-    *handled = true;
-    return PVB2_OK;
-  }
   const int Kp = round4(d->K);
   float* dyn = (float*)((char*)ws + l.a);
   float* wd = (float*)((char*)ws + l.b);
-  const bool phased = strided(d);
   bool empty_phase = false;
   Taps ph[16];
   int nph = 0;
@@ -1265,8 +1185,9 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
       pb[nph] = b;
       ph[nph++] = t;
     }
-  if (empty_phase && !phased) PVB2_CUDA_TRY(cudaMemsetAsync(dx, 0, (size_t)planes * hw * sizeof(float), s));
+  if (empty_phase) PVB2_CUDA_TRY(cudaMemsetAsync(dx, 0, (size_t)d->N * d->C * d->H * d->W * sizeof(float), s));
   PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
+  const int64_t hw = (int64_t)d->H * d->W;
   for (int i = 0; i < nph; ++i) {
     const int a = pa[i], b = pb[i];
     Taps t = ph[i];
@@ -1287,17 +1208,9 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
     for (int j = 0; j < t.nr; ++j) off.h[j] = (a + d->pad_h - t.h[j] * d->dil_h) / d->stride_h;
     for (int j = 0; j < t.ns; ++j) off.w[j] = (b + d->pad_w - t.w[j] * d->dil_w) / d->stride_w;
     const int Hph = (d->H - a + d->stride_h - 1) / d->stride_h, Wph = (d->W - b + d->stride_w - 1) / d->stride_w;
-    if (phased) {
-      float* pbuf = phase_buf(a, b, Hph, Wph);
-      PVB2_TRY(run_fwd_like(dyn, wd, nullptr, pbuf, d->N, Kp, d->P, d->Q, d->C, off, Hph, Wph, 1, 1, 0,
-                            (int64_t)d->C * Hph * Wph, (int64_t)Hph * Wph, Wph, 1, s));
-    } else {
-      PVB2_TRY(run_fwd_like(dyn, wd, nullptr, dx, d->N, Kp, d->P, d->Q, d->C, off, Hph, Wph, 1, 1,
-                            (int64_t)a * d->W + b, (int64_t)d->C * hw, hw, (int64_t)d->stride_h * d->W, d->stride_w,
-                            s));
-    }
+    PVB2_TRY(run_fwd_like(dyn, wd, nullptr, dx, d->N, Kp, d->P, d->Q, d->C, off, Hph, Wph, 1, 1,
+                          (int64_t)a * d->W + b, (int64_t)d->C * hw, hw, (int64_t)d->stride_h * d->W, d->stride_w, s));
   }
-  if (phased) PVB2_TRY(interleave());
   *handled = true;
   return PVB2_OK;
 }
