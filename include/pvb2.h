@@ -295,6 +295,19 @@ PVB2_API int pvb2_avg_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* d
 PVB2_API int pvb2_adaptive_avg_pool2d_fwd(const pvb2_tensor* x, const pvb2_tensor* y, pvb2_stream stream);
 PVB2_API int pvb2_adaptive_avg_pool2d_bwd(const pvb2_tensor* dy, const pvb2_tensor* dx, pvb2_stream stream);
 
+/* upsample_nearest2d, _upsample_nearest_exact2d, upsample_bilinear2d and their
+ * backward passes (no reference kernel: the reference ran them on its CPU
+ * fallback, tensor_ops.cpp:423-429, for the nets its README lists).
+ * mode: PVB2_UPSAMPLE_*.  scale_h / scale_w: the input/output coordinate
+ * ratio as torch computes it in fp32 (1/scale_factor when the caller gave
+ * one, else in/out; (in-1)/(out-1) for align_corners bilinear).  x, y (dy, dx)
+ * NCHW contiguous fp32.  Backward passes gather (deterministic). */
+enum { PVB2_UPSAMPLE_NEAREST = 0, PVB2_UPSAMPLE_NEAREST_EXACT = 1, PVB2_UPSAMPLE_BILINEAR = 2 };
+PVB2_API int pvb2_upsample2d_fwd(int mode, int align_corners, float scale_h, float scale_w, const pvb2_tensor* x,
+                                 const pvb2_tensor* y, pvb2_stream stream);
+PVB2_API int pvb2_upsample2d_bwd(int mode, int align_corners, float scale_h, float scale_w, const pvb2_tensor* dy,
+                                 const pvb2_tensor* dx, pvb2_stream stream);
+
 /* ------------------------------------------------------------------ */
 /* softmax and losses (src/loss_ops.cpp)                                */
 /* x viewed as (outer, dim, inner), contiguous.                         */
@@ -329,6 +342,30 @@ enum { PVB2_MATH_TF32 = 0, PVB2_MATH_FP32 = 1, PVB2_MATH_3XTF32 = 2 };
 PVB2_API int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
               const float* bias, int bias_dim, double alpha, double beta, int math,
               pvb2_stream stream);
+
+/* ------------------------------------------------------------------ */
+/* fused scaled-dot-product attention (the reference's ViT attention ran */
+/* as bmm + softmax: mm_bmm_out, vision_ops.cpp:541-626, and            */
+/* _softmax_out / _softmax_backward_data_out, loss_ops.cpp:137-213).    */
+/* Serves _scaled_dot_product_fused_attention_overrideable(_backward).   */
+/* q [B,H,Lq,D], k and v [B,H,Lk,D], any strides over (b, h, l) that     */
+/* keep 16-byte rows, unit stride along d; D in {32, 64, 128}.  No mask  */
+/* or dropout; causal = query i sees keys j <= i.  fp32 throughout.      */
+/* lse: [B,H,Lq] logsumexp of the scaled scores, written by the forward */
+/* and read by the backward.                                            */
+/* ------------------------------------------------------------------ */
+typedef struct pvb2_sdpa_desc {
+  int32_t B, H, Lq, Lk, D;
+  float scale;                 /* usually 1/sqrt(D)                      */
+  int32_t causal;
+} pvb2_sdpa_desc;
+PVB2_API int pvb2_sdpa_fwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tensor* k, const pvb2_tensor* v,
+                           const pvb2_tensor* out, float* lse, pvb2_stream stream);
+PVB2_API size_t pvb2_sdpa_bwd_workspace_size(const pvb2_sdpa_desc* d);
+PVB2_API int pvb2_sdpa_bwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tensor* k, const pvb2_tensor* v,
+                           const pvb2_tensor* out, const pvb2_tensor* dout, const float* lse, const pvb2_tensor* dq,
+                           const pvb2_tensor* dk, const pvb2_tensor* dv, void* workspace, size_t workspace_bytes,
+                           pvb2_stream stream);
 
 /* Tensor-core watchdogs (no counterpart in the reference, whose OpenCL   */
 /* kernels had no internal waits).  Every mbarrier wait in the tcgen05    */

@@ -659,6 +659,156 @@ static at::Tensor native_dropout_backward(const at::Tensor& grad_output, const a
   return gx;
 }
 
+// ------------------------------------------------------------ upsample
+// upsample_nearest2d / _upsample_nearest_exact2d / upsample_bilinear2d and
+// their backward passes; the reference had no device kernel for them (its
+// CPU fallback ran them, tensor_ops.cpp:423-429).  Scales follow torch's fp32
+// rules (area_pixel_compute_scale / compute_scales_value).
+static float up_scale(int64_t in, int64_t out, bool align, std::optional<double> scale, bool linear) {
+  if (linear && align) return out > 1 ? (float)(in - 1) / (float)(out - 1) : 0.f;
+  return (scale.has_value() && *scale > 0.) ? (float)(1.0 / *scale) : (float)in / (float)out;
+}
+
+static at::Tensor& upsample_fwd(const char* name, int mode, const at::Tensor& self, at::IntArrayRef output_size,
+                                bool align, std::optional<double> sh, std::optional<double> sw, at::Tensor& out) {
+  const int dev = self.device().index();
+  DeviceScope scope(dev);
+  OCL_OP(name, dev);
+  TORCH_CHECK(self.dim() == 4 && output_size.size() == 2, name, ": 4-D input and 2 output sizes expected");
+  TORCH_CHECK(self.scalar_type() == at::kFloat, name, ": only float32 is supported");
+  const std::vector<int64_t> osz = {self.size(0), self.size(1), output_size[0], output_size[1]};
+  if (out.sizes() != c10::IntArrayRef(osz)) out.resize_(osz);
+  if (out.numel() == 0) return out;
+  const bool lin = mode == PVB2_UPSAMPLE_BILINEAR;
+  const float fh = up_scale(self.size(2), output_size[0], align, sh, lin);
+  const float fw = up_scale(self.size(3), output_size[1], align, sw, lin);
+  at::Tensor x = contiguous(self);
+  at::Tensor o = out.is_contiguous() ? out : empty(osz, at::kFloat, dev);
+  pvb2_tensor xd = desc(x), od = desc(o);
+  OCL_CHECK(pvb2_upsample2d_fwd(mode, align ? 1 : 0, fh, fw, &xd, &od, stream_for(dev)));
+  write_back(out, o);
+  return out;
+}
+
+static at::Tensor& upsample_bwd(const char* name, int mode, const at::Tensor& grad_output, at::IntArrayRef output_size,
+                                at::IntArrayRef input_size, bool align, std::optional<double> sh,
+                                std::optional<double> sw, at::Tensor& grad_input) {
+  const int dev = grad_output.device().index();
+  DeviceScope scope(dev);
+  OCL_OP(name, dev);
+  TORCH_CHECK(input_size.size() == 4 && output_size.size() == 2, name, ": 4 input and 2 output sizes expected");
+  if (grad_input.sizes() != input_size) grad_input.resize_(input_size);
+  if (grad_input.numel() == 0) return grad_input;
+  const bool lin = mode == PVB2_UPSAMPLE_BILINEAR;
+  const float fh = up_scale(input_size[2], output_size[0], align, sh, lin);
+  const float fw = up_scale(input_size[3], output_size[1], align, sw, lin);
+  at::Tensor gy = contiguous(grad_output);
+  at::Tensor gi = grad_input.is_contiguous() ? grad_input : empty(input_size, at::kFloat, dev);
+  pvb2_tensor gyd = desc(gy), gid = desc(gi);
+  OCL_CHECK(pvb2_upsample2d_bwd(mode, align ? 1 : 0, fh, fw, &gyd, &gid, stream_for(dev)));
+  write_back(grad_input, gi);
+  return grad_input;
+}
+
+static at::Tensor& upsample_nearest2d_out(const at::Tensor& self, at::IntArrayRef osz, std::optional<double> sh,
+                                          std::optional<double> sw, at::Tensor& out) {
+  return upsample_fwd("upsample_nearest2d", PVB2_UPSAMPLE_NEAREST, self, osz, false, sh, sw, out);
+}
+static at::Tensor& upsample_nearest2d_backward_out(const at::Tensor& gy, at::IntArrayRef osz, at::IntArrayRef isz,
+                                                   std::optional<double> sh, std::optional<double> sw,
+                                                   at::Tensor& gi) {
+  return upsample_bwd("upsample_nearest2d_backward", PVB2_UPSAMPLE_NEAREST, gy, osz, isz, false, sh, sw, gi);
+}
+static at::Tensor& upsample_nearest_exact2d_out(const at::Tensor& self, at::IntArrayRef osz, std::optional<double> sh,
+                                                std::optional<double> sw, at::Tensor& out) {
+  return upsample_fwd("_upsample_nearest_exact2d", PVB2_UPSAMPLE_NEAREST_EXACT, self, osz, false, sh, sw, out);
+}
+static at::Tensor& upsample_nearest_exact2d_backward_out(const at::Tensor& gy, at::IntArrayRef osz,
+                                                         at::IntArrayRef isz, std::optional<double> sh,
+                                                         std::optional<double> sw, at::Tensor& gi) {
+  return upsample_bwd("_upsample_nearest_exact2d_backward", PVB2_UPSAMPLE_NEAREST_EXACT, gy, osz, isz, false, sh, sw,
+                      gi);
+}
+static at::Tensor& upsample_bilinear2d_out(const at::Tensor& self, at::IntArrayRef osz, bool align,
+                                           std::optional<double> sh, std::optional<double> sw, at::Tensor& out) {
+  return upsample_fwd("upsample_bilinear2d", PVB2_UPSAMPLE_BILINEAR, self, osz, align, sh, sw, out);
+}
+static at::Tensor& upsample_bilinear2d_backward_out(const at::Tensor& gy, at::IntArrayRef osz, at::IntArrayRef isz,
+                                                    bool align, std::optional<double> sh, std::optional<double> sw,
+                                                    at::Tensor& gi) {
+  return upsample_bwd("upsample_bilinear2d_backward", PVB2_UPSAMPLE_BILINEAR, gy, osz, isz, align, sh, sw, gi);
+}
+
+// ------------------------------------------------------------ MSE / BCE
+// mse_loss and binary_cross_entropy (no reference kernel; its CPU fallback
+// ran them) composed from this backend's own pointwise and reduction kernels.
+// Reduction codes: 0 none, 1 mean, 2 sum.  BCE clamps each log term at -100
+// like the CPU kernel.
+static at::Tensor reduce_loss(const at::Tensor& l, int64_t reduction) {
+  if (reduction == 1) return at::mean(l);
+  if (reduction == 2) return at::sum(l);
+  return l;
+}
+
+static at::Tensor& put(at::Tensor& out, const at::Tensor& v) {
+  if (out.sizes() != v.sizes()) out.resize_(v.sizes());
+  out.copy_(v);
+  return out;
+}
+
+static at::Tensor& mse_loss_out(const at::Tensor& self, const at::Tensor& target, int64_t reduction, at::Tensor& out) {
+  OCL_OP("mse_loss", self.device().index());
+  const at::Tensor d = at::sub(self, target);
+  return put(out, reduce_loss(at::mul(d, d), reduction));
+}
+
+static at::Tensor mse_loss_backward_fn(const at::Tensor& gy, const at::Tensor& self, const at::Tensor& target,
+                                       int64_t reduction) {
+  OCL_OP("mse_loss_backward", self.device().index());
+  const double norm = reduction == 1 ? 2.0 / (double)std::max<int64_t>(self.numel(), 1) : 2.0;
+  return at::mul(at::mul(at::sub(self, target), norm), gy);
+}
+
+static at::Tensor& mse_loss_backward_out(const at::Tensor& gy, const at::Tensor& self, const at::Tensor& target,
+                                         int64_t reduction, at::Tensor& grad_input) {
+  return put(grad_input, mse_loss_backward_fn(gy, self, target, reduction));
+}
+
+static at::Tensor binary_cross_entropy_fn(const at::Tensor& self, const at::Tensor& target,
+                                          const std::optional<at::Tensor>& weight, int64_t reduction) {
+  OCL_OP("binary_cross_entropy", self.device().index());
+  const at::Tensor lx = at::clamp_min(at::log(self), -100.0);
+  const at::Tensor l1x = at::clamp_min(at::log(at::rsub(self, 1.0)), -100.0);
+  // -(t*log x + (1-t)*log(1-x)) = (t - 1)*log(1-x) - t*log x
+  at::Tensor l = at::sub(at::mul(at::sub(target, 1.0), l1x), at::mul(target, lx));
+  if (weight.has_value() && weight->defined()) l = at::mul(l, *weight);
+  return reduce_loss(l, reduction);
+}
+
+static at::Tensor& binary_cross_entropy_out(const at::Tensor& self, const at::Tensor& target,
+                                            const std::optional<at::Tensor>& weight, int64_t reduction,
+                                            at::Tensor& out) {
+  return put(out, binary_cross_entropy_fn(self, target, weight, reduction));
+}
+
+static at::Tensor binary_cross_entropy_backward_fn(const at::Tensor& gy, const at::Tensor& self,
+                                                   const at::Tensor& target, const std::optional<at::Tensor>& weight,
+                                                   int64_t reduction) {
+  OCL_OP("binary_cross_entropy_backward", self.device().index());
+  // (x - t) / max((1 - x) * x, eps) * gy, eps = 1e-12
+  const at::Tensor den = at::clamp_min(at::mul(at::rsub(self, 1.0), self), 1e-12);
+  at::Tensor g = at::mul(at::div(at::sub(self, target), den), gy);
+  if (weight.has_value() && weight->defined()) g = at::mul(g, *weight);
+  if (reduction == 1) g = at::div(g, (double)std::max<int64_t>(self.numel(), 1));
+  return g;
+}
+
+static at::Tensor& binary_cross_entropy_backward_out(const at::Tensor& gy, const at::Tensor& self,
+                                                     const at::Tensor& target, const std::optional<at::Tensor>& weight,
+                                                     int64_t reduction, at::Tensor& grad_input) {
+  return put(grad_input, binary_cross_entropy_backward_fn(gy, self, target, weight, reduction));
+}
+
 }  // namespace ocl
 
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
@@ -690,4 +840,17 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   m.impl("bernoulli_.float", &bernoulli_);
   m.impl("native_dropout", &native_dropout);
   m.impl("native_dropout_backward", &native_dropout_backward);
+  m.impl("upsample_nearest2d.out", &upsample_nearest2d_out);
+  m.impl("upsample_nearest2d_backward.grad_input", &upsample_nearest2d_backward_out);
+  m.impl("_upsample_nearest_exact2d.out", &upsample_nearest_exact2d_out);
+  m.impl("_upsample_nearest_exact2d_backward.grad_input", &upsample_nearest_exact2d_backward_out);
+  m.impl("upsample_bilinear2d.out", &upsample_bilinear2d_out);
+  m.impl("upsample_bilinear2d_backward.grad_input", &upsample_bilinear2d_backward_out);
+  m.impl("mse_loss.out", &mse_loss_out);
+  m.impl("mse_loss_backward", &mse_loss_backward_fn);
+  m.impl("mse_loss_backward.grad_input", &mse_loss_backward_out);
+  m.impl("binary_cross_entropy", &binary_cross_entropy_fn);
+  m.impl("binary_cross_entropy.out", &binary_cross_entropy_out);
+  m.impl("binary_cross_entropy_backward", &binary_cross_entropy_backward_fn);
+  m.impl("binary_cross_entropy_backward.grad_input", &binary_cross_entropy_backward_out);
 }

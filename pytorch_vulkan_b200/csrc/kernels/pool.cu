@@ -197,6 +197,109 @@ __global__ void adaptive_avgpool_bwd_kernel(const float* __restrict__ dy, float*
   }
 }
 
+// ------------------------------------------------------------ upsample
+// source coordinate of output index o along one axis (torch's rules, fp32)
+__device__ __forceinline__ int nearest_src(int o, float scale, int in, int out, bool exact) {
+  if (out == in) return o;
+  if (!exact && out == 2 * in) return o >> 1;
+  const int s = exact ? (int)floorf(((float)o + 0.5f) * scale) : (int)floorf((float)o * scale);
+  return min(s, in - 1);
+}
+
+__device__ __forceinline__ float linear_src(int o, float scale, bool align) {
+  if (align) return scale * (float)o;
+  const float s = scale * ((float)o + 0.5f) - 0.5f;
+  return s < 0.f ? 0.f : s;
+}
+
+// bilinear taps of output index o: i0 = floor(src), i1 = i0 + (i0 < in - 1), weights l0, l1
+__device__ __forceinline__ void linear_taps(int o, float scale, bool align, int in, int& i0, int& i1, float& l0,
+                                            float& l1) {
+  const float src = linear_src(o, scale, align);
+  i0 = (int)src;
+  i1 = i0 + (i0 < in - 1 ? 1 : 0);
+  l1 = src - (float)i0;
+  l0 = 1.f - l1;
+}
+
+// grid (ceil(OH*OW / 256), min(planes, 65535))
+__global__ void upsample_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t planes, int H, int W,
+                                    int OH, int OW, int mode, int align, float sh, float sw) {
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= OH * OW) return;
+  const int oh = o / OW, ow = o - (o / OW) * OW;
+  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
+    const float* xp = x + plane * H * W;
+    float v;
+    if (mode == PVB2_UPSAMPLE_BILINEAR) {
+      int h0, h1, w0, w1;
+      float a0, a1, b0, b1;
+      linear_taps(oh, sh, align != 0, H, h0, h1, a0, a1);
+      linear_taps(ow, sw, align != 0, W, w0, w1, b0, b1);
+      v = a0 * (b0 * __ldg(xp + h0 * W + w0) + b1 * __ldg(xp + h0 * W + w1)) +
+          a1 * (b0 * __ldg(xp + h1 * W + w0) + b1 * __ldg(xp + h1 * W + w1));
+    } else {
+      const bool exact = mode == PVB2_UPSAMPLE_NEAREST_EXACT;
+      v = __ldg(xp + nearest_src(oh, sh, H, OH, exact) * W + nearest_src(ow, sw, W, OW, exact));
+    }
+    y[plane * OH * OW + o] = v;
+  }
+}
+
+// outputs along one axis whose taps may reach input index i: a conservative
+// range (checked exactly by the caller); scale 0 maps every output to 0
+__device__ __forceinline__ void out_range(int i, float scale, int out, int& lo, int& hi) {
+  if (!(scale > 0.f)) {
+    lo = 0;
+    hi = out - 1;
+    return;
+  }
+  lo = max(0, (int)floorf(((float)i - 1.f) / scale) - 2);
+  hi = min(out - 1, (int)ceilf(((float)i + 2.f) / scale) + 2);
+}
+
+// backward as a gather: each input element sums the outputs that sampled it,
+// in increasing output order.  grid (ceil(H*W / 256), min(planes, 65535))
+__global__ void upsample_bwd_kernel(const float* __restrict__ dy, float* __restrict__ dx, int64_t planes, int H, int W,
+                                    int OH, int OW, int mode, int align, float sh, float sw) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= H * W) return;
+  const int ih = i / W, iw = i - (i / W) * W;
+  int ohl, ohh, owl, owh;
+  out_range(ih, sh, OH, ohl, ohh);
+  out_range(iw, sw, OW, owl, owh);
+  const bool exact = mode == PVB2_UPSAMPLE_NEAREST_EXACT;
+  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
+    const float* gp = dy + plane * OH * OW;
+    float acc = 0.f;
+    for (int oh = ohl; oh <= ohh; ++oh) {
+      float wh;
+      if (mode == PVB2_UPSAMPLE_BILINEAR) {
+        int h0, h1;
+        float a0, a1;
+        linear_taps(oh, sh, align != 0, H, h0, h1, a0, a1);
+        wh = (h0 == ih ? a0 : 0.f) + (h1 == ih ? a1 : 0.f);
+      } else {
+        wh = nearest_src(oh, sh, H, OH, exact) == ih ? 1.f : 0.f;
+      }
+      if (wh == 0.f) continue;
+      for (int ow = owl; ow <= owh; ++ow) {
+        float ww;
+        if (mode == PVB2_UPSAMPLE_BILINEAR) {
+          int w0, w1;
+          float b0, b1;
+          linear_taps(ow, sw, align != 0, W, w0, w1, b0, b1);
+          ww = (w0 == iw ? b0 : 0.f) + (w1 == iw ? b1 : 0.f);
+        } else {
+          ww = nearest_src(ow, sw, W, OW, exact) == iw ? 1.f : 0.f;
+        }
+        if (ww != 0.f) acc += wh * ww * __ldg(gp + oh * OW + ow);
+      }
+    }
+    dx[plane * H * W + i] = acc;
+  }
+}
+
 static int check_nchw(const pvb2_tensor* t, const char* what) {
   PVB2_CHECK_ARG(t->dtype == PVB2_F32, "%s: only float32 is supported", what);
   PVB2_CHECK_ARG(t->ndim == 4, "%s: expected a 4-D NCHW tensor", what);
@@ -256,6 +359,45 @@ int pvb2_max_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* dy, const 
       PVB2_LAUNCH_CHECK();
     }
   return PVB2_OK;
+}
+
+static int upsample_launch(bool bwd, int mode, int align, float sh, float sw, const pvb2_tensor* in,
+                           const pvb2_tensor* out, pvb2_stream stream) {
+  const char* what = bwd ? "upsample2d_backward" : "upsample2d";
+  PVB2_TRY(check_nchw(in, what));
+  PVB2_TRY(check_nchw(out, what));
+  PVB2_CHECK_ARG(mode >= PVB2_UPSAMPLE_NEAREST && mode <= PVB2_UPSAMPLE_BILINEAR, "%s: unknown mode %d", what, mode);
+  PVB2_CHECK_ARG(in->sizes[0] == out->sizes[0] && in->sizes[1] == out->sizes[1], "%s: N, C mismatch", what);
+  // forward: in = x (H, W), out = y (OH, OW); backward: in = dy (OH, OW), out = dx (H, W)
+  const pvb2_tensor* small = bwd ? out : in;
+  const pvb2_tensor* big = bwd ? in : out;
+  const int64_t planes = small->sizes[0] * small->sizes[1];
+  const int64_t H = small->sizes[2], W = small->sizes[3], OH = big->sizes[2], OW = big->sizes[3];
+  PVB2_CHECK_ARG(H * W < (int64_t)1 << 31 && OH * OW < (int64_t)1 << 31, "%s: plane too large", what);
+  if (planes == 0 || H * W == 0 || OH * OW == 0) {
+    if (bwd && planes * H * W) PVB2_CUDA_TRY(cudaMemsetAsync(out->data, 0, planes * H * W * 4, as_stream(stream)));
+    return PVB2_OK;
+  }
+  const int64_t pos = bwd ? H * W : OH * OW;
+  const dim3 grid((unsigned)((pos + 255) / 256), (unsigned)std::min<int64_t>(planes, 65535));
+  if (bwd)
+    upsample_bwd_kernel<<<grid, 256, 0, as_stream(stream)>>>((const float*)in->data, (float*)out->data, planes, (int)H,
+                                                             (int)W, (int)OH, (int)OW, mode, align, sh, sw);
+  else
+    upsample_fwd_kernel<<<grid, 256, 0, as_stream(stream)>>>((const float*)in->data, (float*)out->data, planes, (int)H,
+                                                             (int)W, (int)OH, (int)OW, mode, align, sh, sw);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+int pvb2_upsample2d_fwd(int mode, int align_corners, float scale_h, float scale_w, const pvb2_tensor* x,
+                        const pvb2_tensor* y, pvb2_stream stream) {
+  return upsample_launch(false, mode, align_corners, scale_h, scale_w, x, y, stream);
+}
+
+int pvb2_upsample2d_bwd(int mode, int align_corners, float scale_h, float scale_w, const pvb2_tensor* dy,
+                        const pvb2_tensor* dx, pvb2_stream stream) {
+  return upsample_launch(true, mode, align_corners, scale_h, scale_w, dy, dx, stream);
 }
 
 int pvb2_avg_pool2d_fwd(const pvb2_pool2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* y, pvb2_stream stream) {

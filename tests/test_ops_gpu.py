@@ -495,3 +495,45 @@ def test_profile_csv(ocl, tmp_path):
     lines = open(path).read().strip().split("\n")
     assert lines[0] == "section,kernel,start (ms),end (ms),duraion(ms)"
     assert any("mm" in l for l in lines[1:])
+
+
+# upsample and MSE / BCE losses: ops the reference ran on its CPU fallback
+UPSAMPLES = [
+    ("nearest_x2", lambda x: F.interpolate(x, scale_factor=2, mode="nearest")),
+    ("nearest_size", lambda x: F.interpolate(x, size=(11, 13), mode="nearest")),
+    ("nearest_down", lambda x: F.interpolate(x, size=(3, 4), mode="nearest")),
+    ("nearest_exact", lambda x: F.interpolate(x, size=(11, 13), mode="nearest-exact")),
+    ("bilinear_x2", lambda x: F.interpolate(x, scale_factor=2, mode="bilinear", align_corners=False)),
+    ("bilinear_align", lambda x: F.interpolate(x, size=(11, 13), mode="bilinear", align_corners=True)),
+    ("bilinear_down", lambda x: F.interpolate(x, size=(4, 3), mode="bilinear", align_corners=False)),
+    ("bilinear_frac", lambda x: F.interpolate(x, scale_factor=1.7, mode="bilinear", align_corners=False)),
+]
+
+
+@pytest.mark.parametrize("name,call", UPSAMPLES, ids=[u[0] for u in UPSAMPLES])
+def test_upsample(ocl, name, call):
+    check_fwd_bwd([([2, 3, 6, 7], -1)], call, tol=1e-5)
+
+
+@pytest.mark.parametrize("reduction", ["mean", "sum", "none"])
+def test_mse_loss(ocl, reduction):
+    check_fwd_bwd([([4, 5, 6], -1), ([4, 5, 6], -1)], lambda a, b: F.mse_loss(a, b, reduction=reduction), tol=1e-4)
+
+
+@pytest.mark.parametrize("reduction", ["mean", "sum", "none"])
+def test_bce_loss(ocl, reduction):
+    g = _gen(5)
+    p = torch.rand(4, 7, generator=g) * 0.98 + 0.01
+    t = torch.rand(4, 7, generator=g)
+    w = torch.rand(4, 7, generator=g)
+    for weight in (None, w):
+        pc = p.clone().requires_grad_()
+        pd = p.to(DEV).requires_grad_()
+        yc = F.binary_cross_entropy(pc, t, weight=weight, reduction=reduction)
+        yd = F.binary_cross_entropy(pd, t.to(DEV), weight=None if weight is None else weight.to(DEV),
+                                    reduction=reduction)
+        assert _diff(yc, yd) <= 1e-5
+        gy = torch.randn(yc.shape, generator=g) if yc.dim() else torch.tensor(1.0)
+        yc.backward(gy)
+        yd.backward(gy.to(DEV))
+        assert _diff(pc.grad, pd.grad) <= 1e-4
