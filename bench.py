@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--model", default=MODEL)
+    ap.add_argument("--attention", default="fused", choices=["fused", "math"],
+                    help="scaled_dot_product_attention backend for vit_b_16 (math = bmm + softmax + bmm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--deadline-s", type=float, default=600.0,
@@ -175,6 +177,11 @@ def run_ours(a):
     else:
         _watchdog(comm, a.deadline_s)
     dev = f"ocl:{local}"
+    if a.attention == "math":
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        a.sdpa_ctx = sdpa_kernel(SDPBackend.MATH)  # kept alive: closing it restores the backends
+        a.sdpa_ctx.__enter__()
     torch.manual_seed(0)
     model = omodels.build(a.model, 0)
     x_cpu, y_cpu = omodels.make_inputs(a.model, a.batch, 1234 + rank)
@@ -315,6 +322,7 @@ def run_ours(a):
             "config": {"workload": f"{a.model} fp32 train step (fwd+bwd+SGD m0.9), batch {a.batch}/GPU, 3x224x224",
                        "global_batch": a.batch * world, "parallelism": f"dp{world}",
                        "math": ["tf32", "fp32", "3xtf32"][torch.ocl.get_math_mode()],
+                       **({"attention": a.attention} if "vit" in a.model else {}),
                        "l2": "inputs/activations larger than L2 (126 MB) every step",
                        "gflop_per_step": round(total_flops / 1e9, 1)},
             "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,

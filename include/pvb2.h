@@ -212,6 +212,14 @@ enum { PVB2_RED_SUM = 0, PVB2_RED_PROD = 1, PVB2_RED_MAX = 2, PVB2_RED_MIN = 3,
        PVB2_RED_ARGMAX = 4, PVB2_RED_ARGMIN = 5, PVB2_RED_SUMSQ = 6 };
 PVB2_API int pvb2_reduce(int op, const pvb2_tensor* out, const pvb2_tensor* in, double scale,
                 int compute_dtype, pvb2_stream stream);
+/* Same, with scratch for splitting long reduced ranges over many blocks
+ * (partials combined in a fixed order, so results depend only on the
+ * shape).  workspace may be NULL (no split); otherwise it must hold
+ * pvb2_reduce_workspace_size() bytes, which is 0 when no split applies. */
+PVB2_API size_t pvb2_reduce_workspace_size(int op, const pvb2_tensor* out, const pvb2_tensor* in,
+                                           int compute_dtype);
+PVB2_API int pvb2_reduce_ws(int op, const pvb2_tensor* out, const pvb2_tensor* in, double scale,
+                            int compute_dtype, void* workspace, size_t workspace_bytes, pvb2_stream stream);
 
 /* ------------------------------------------------------------------ */
 /* normalisation (src/norm_ops.cpp)                                     */
@@ -361,6 +369,10 @@ typedef struct pvb2_sdpa_desc {
 } pvb2_sdpa_desc;
 PVB2_API int pvb2_sdpa_fwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tensor* k, const pvb2_tensor* v,
                            const pvb2_tensor* out, float* lse, pvb2_stream stream);
+/* Backward workspace: D_i = rowsum(dO * O) and, unless they would pass
+ * 2 GiB, one dQ slice per 64-key block (summed in a fixed order).  A
+ * workspace of only the D_i part (B*H*Lq floats, rounded up to 256 bytes) is
+ * accepted too: dQ is then recomputed per query block. */
 PVB2_API size_t pvb2_sdpa_bwd_workspace_size(const pvb2_sdpa_desc* d);
 PVB2_API int pvb2_sdpa_bwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tensor* k, const pvb2_tensor* v,
                            const pvb2_tensor* out, const pvb2_tensor* dout, const float* lse, const pvb2_tensor* dq,

@@ -45,8 +45,14 @@ static int64_t fused_sdp_choice(const at::Tensor& q, const at::Tensor& k, const 
                                 std::optional<double> scale, bool enable_gqa) {
   (void)is_causal;
   (void)scale;
-  return static_cast<int64_t>(sdpa_covered(q, k, v, mask, dropout_p, enable_gqa) ? at::SDPBackend::overrideable
-                                                                                   : at::SDPBackend::math);
+  // torch.nn.attention.sdpa_kernel([...]) switches backends on and off
+  const auto& ctx = at::globalContext();
+  if (ctx.userEnabledOverrideableSDP() && sdpa_covered(q, k, v, mask, dropout_p, enable_gqa))
+    return static_cast<int64_t>(at::SDPBackend::overrideable);
+  TORCH_CHECK(ctx.userEnabledMathSDP(),
+              "ocl scaled_dot_product_attention: no enabled backend covers these arguments (the fused kernel "
+              "takes 4-D fp32 q/k/v with head dim 32/64/128, no mask and no dropout; math is disabled)");
+  return static_cast<int64_t>(at::SDPBackend::math);
 }
 
 // rows 16-byte aligned and unit stride along the head dimension, or a copy

@@ -363,7 +363,13 @@ static at::Tensor& reduce_out(int op, const at::Tensor& self, at::OptionalIntArr
   int cd = compute_code(out.scalar_type());
   if (op == PVB2_RED_ARGMAX || op == PVB2_RED_ARGMIN) cd = compute_code(self.scalar_type());
   const double scale = mean ? (count ? 1.0 / (double)count : NAN) : 1.0;
-  OCL_CHECK(pvb2_reduce(op, &o, &in, scale, cd, stream_for(dev)));
+  const size_t wsb = pvb2_reduce_workspace_size(op, &o, &in, cd);
+  if (wsb == 0) {
+    OCL_CHECK(pvb2_reduce(op, &o, &in, scale, cd, stream_for(dev)));
+  } else {
+    Workspace ws(wsb, dev);
+    OCL_CHECK(pvb2_reduce_ws(op, &o, &in, scale, cd, ws.get(), ws.bytes, stream_for(dev)));
+  }
   return out;
 }
 

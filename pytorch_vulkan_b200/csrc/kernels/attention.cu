@@ -7,29 +7,52 @@
 // leave shared memory.
 //
 // Layout: Q [B, H, Lq, D], K and V [B, H, Lk, D], any strides over (b, h, l),
-// unit stride along d.  O [B, H, Lq, D] contiguous, logsumexp [B, H, Lq].
-// D is 32, 64 or 128.  No attention mask, no dropout; optional causal mask
-// (query i sees keys j <= i).
+// unit stride along d.  O [B, H, Lq, D], logsumexp [B, H, Lq].  D is 32, 64
+// or 128.  No attention mask, no dropout; optional causal mask (query i sees
+// keys j <= i).
 //
-// Forward: one CTA per (64 queries, head); key blocks of 64 stream through
-// shared memory with the online softmax (running row max m and sum l, the
-// accumulator rescaled by exp(m_old - m_new)).  Thread t owns query row
-// t / 4 and, of that row, keys j = t%4 + 4u of each block and output
-// columns (t%4)*D/4 .. +D/4; the four threads of a row are adjacent lanes.
-// Backward (with D_i = sum_d dO_i,d O_i,d, P_ij = exp(s_ij - lse_i),
-// dS_ij = P_ij (dO_i . V_j - D_i)):
-//   dK, dV: one CTA per (64 keys, head), looping over query blocks:
-//           dV_j += sum_i P_ij dO_i,  dK_j += scale * sum_i dS_ij Q_i
-//   dQ:     one CTA per (64 queries, head), looping over key blocks:
-//           dQ_i += scale * sum_j dS_ij K_j
+// Tiles are 64 queries x 64 keys in shared memory, row-major with 4 floats
+// of padding per row.  256 threads, t = 16 * tr + tc; each tile product is
+// register-blocked so that a thread does 16 FMAs per pair of 16-byte shared
+// loads:
+//   NT  C[m][n] = sum_d A[m][d] B[n][d]   (S = Q K^T, dP = dO V^T)
+//       thread rows m = tr + 16 i, columns n = tc + 16 j (i, j < 4): the 64
+//       scores of a row sit in one half-warp, so row max / sum are four
+//       xor-shuffles;
+//   NN  C[m][c] += sum_k A[m][k] B[k][c]  (O += P V, dQ = dS K), rows as NT;
+//   TN  C[m][c] += sum_r A[r][m] B[r][c]  (dV += P^T dO, dK += dS^T Q),
+//       rows m = 4 tr .. 4 tr + 3;
+// where a thread owns D / 16 of the D output columns c: 2 at 2 tc (D = 32),
+// 4 at 4 tc (D = 64), 4 at 4 tc and 4 at 4 tc + 64 (D = 128), so a
+// half-warp reads a tile row without bank conflicts.
+//
+// Forward: one CTA per (64 queries, head), key blocks streamed with the
+// online softmax (running max m and sum l per row, O rescaled by
+// exp(m_old - m_new)); logsumexp = m + log l.
+// Backward, with D_i = sum_d dO_i,d O_i,d, P_ij = exp(s_ij - lse_i),
+// dS_ij = P_ij (dP_ij - D_i): one CTA per (64 keys, head) loops over the
+// query blocks, accumulating dV_j and dK_j in registers and writing its
+// contribution dS K_j to dQ into a per-key-block slice of the workspace;
+// a reduction kernel sums the slices in key-block order (deterministic).
+// When the caller's workspace cannot hold the slices, a second kernel per
+// (64 queries, head) recomputes S and dP and accumulates dQ instead.
 // All arithmetic is fp32 on the CUDA cores; the exponentials use expf.
 #include <cfloat>
 #include "common.cuh"
 
 namespace pvb2 {
 
-constexpr int kAtB = 64;        // rows (queries or keys) per block
+constexpr int kAtB = 64;  // rows (queries or keys) per tile
 constexpr int kAtThreads = 256;
+constexpr int kAtPS = kAtB + 4;  // pitch of the 64-wide P / dS tiles
+
+template <int D>
+struct AtCfg {
+  static constexpr int PD = D + 4;   // pitch of the D-wide Q / K / V / dO tiles
+  static constexpr int NC = D / 16;  // output columns per thread in NN / TN
+  static constexpr int TILE = kAtB * PD;
+  static constexpr int PTILE = kAtB * kAtPS;
+};
 
 struct AtView {  // one of Q, K, V, O, dO, dQ, dK, dV
   float* p;
@@ -42,123 +65,212 @@ struct AtArgs {
   int causal;
 };
 
-__device__ __forceinline__ const float* at_row(const AtView& v, int b, int h, int l) {
-  return v.p + b * v.sb + h * v.sh + (int64_t)l * v.sl;
-}
-__device__ __forceinline__ float* at_row_w(const AtView& v, int b, int h, int l) {
+__device__ __forceinline__ float* at_row(const AtView& v, int b, int h, int l) {
   return v.p + b * v.sb + h * v.sh + (int64_t)l * v.sl;
 }
 
-// rows [l0, l0+64) of a view into shared memory (pitch floats per row),
-// scaled, zero past `len`
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+__device__ __forceinline__ float f4(const float4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// the thread's D / 16 columns of one tile row
 template <int D>
-__device__ __forceinline__ void at_load(float* s, int pitch, const AtView& v, int b, int h, int l0, int len,
-                                        float mul) {
-  for (int e = threadIdx.x; e < kAtB * (D / 4); e += blockDim.x) {
-    const int r = e / (D / 4), c4 = (e % (D / 4)) * 4;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (l0 + r < len) x = __ldg(reinterpret_cast<const float4*>(at_row(v, b, h, l0 + r) + c4));
-    float* d = s + r * pitch + c4;
-    d[0] = x.x * mul;
-    d[1] = x.y * mul;
-    d[2] = x.z * mul;
-    d[3] = x.w * mul;
+__device__ __forceinline__ void at_frag(const float* row, int tc, float (&b)[AtCfg<D>::NC]) {
+  if constexpr (D == 32) {
+    const float2 v = *reinterpret_cast<const float2*>(row + tc * 2);
+    b[0] = v.x;
+    b[1] = v.y;
+  } else {
+#pragma unroll
+    for (int h = 0; h < D / 64; ++h) {
+      const float4 v = ld4(row + tc * 4 + 64 * h);
+      b[4 * h] = v.x;
+      b[4 * h + 1] = v.y;
+      b[4 * h + 2] = v.z;
+      b[4 * h + 3] = v.w;
+    }
   }
 }
 
-__device__ __forceinline__ float quad_max(float v) {
-  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
-  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
-}
-__device__ __forceinline__ float quad_sum(float v) {
-  v += __shfl_xor_sync(0xffffffffu, v, 1);
-  return v + __shfl_xor_sync(0xffffffffu, v, 2);
+// store a thread's D / 16 columns of one output row, times `mul`
+template <int D>
+__device__ __forceinline__ void at_store_row(float* row, int tc, const float (&v)[AtCfg<D>::NC], float mul) {
+  if constexpr (D == 32) {
+    *reinterpret_cast<float2*>(row + tc * 2) = make_float2(v[0] * mul, v[1] * mul);
+  } else {
+#pragma unroll
+    for (int h = 0; h < D / 64; ++h)
+      *reinterpret_cast<float4*>(row + tc * 4 + 64 * h) =
+          make_float4(v[4 * h] * mul, v[4 * h + 1] * mul, v[4 * h + 2] * mul, v[4 * h + 3] * mul);
+  }
 }
 
+// rows [l0, l0 + 64) of a view into a D-wide tile, times `mul`, zero past `len`
 template <int D>
-struct AtFwdSmem {
-  static constexpr int PQ = D + 1, PK = D + 1, PV = D + 4, PP = kAtB + 1;
-  static constexpr int Q = 0, K = Q + kAtB * PQ, V = K + kAtB * PK, P = V + kAtB * PV;
-  static constexpr int FLOATS = P + kAtB * PP;
-};
+__device__ __forceinline__ void at_load(float* s, const AtView& v, int b, int h, int l0, int len, float mul) {
+  for (int e = threadIdx.x; e < kAtB * (D / 4); e += kAtThreads) {
+    const int r = e / (D / 4), c4 = (e % (D / 4)) * 4;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (l0 + r < len) x = __ldg(reinterpret_cast<const float4*>(at_row(v, b, h, l0 + r) + c4));
+    x.x *= mul;
+    x.y *= mul;
+    x.z *= mul;
+    x.w *= mul;
+    *reinterpret_cast<float4*>(s + r * AtCfg<D>::PD + c4) = x;
+  }
+}
+
+// C = A B^T over the head dimension (both D-wide tiles)
+template <int D>
+__device__ __forceinline__ void at_nt(const float* A, const float* B, int tr, int tc, float (&c)[4][4]) {
+  constexpr int PD = AtCfg<D>::PD;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[i][j] = 0.f;
+#pragma unroll 2
+  for (int d = 0; d < D; d += 4) {
+    float4 a[4], b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = ld4(A + (tr + 16 * i) * PD + d);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) b[j] = ld4(B + (tc + 16 * j) * PD + d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        c[i][j] = fmaf(a[i].x, b[j].x, c[i][j]);
+        c[i][j] = fmaf(a[i].y, b[j].y, c[i][j]);
+        c[i][j] = fmaf(a[i].z, b[j].z, c[i][j]);
+        c[i][j] = fmaf(a[i].w, b[j].w, c[i][j]);
+      }
+  }
+}
+
+// C += A B, A a 64-wide tile (rows tr + 16 i), B a D-wide tile; k < kn
+// (kn a multiple of 4)
+template <int D>
+__device__ __forceinline__ void at_nn(const float* A, const float* B, int kn, int tr, int tc,
+                                      float (&c)[4][AtCfg<D>::NC]) {
+  constexpr int PD = AtCfg<D>::PD, NC = AtCfg<D>::NC;
+  for (int k = 0; k < kn; k += 4) {
+    float4 a[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = ld4(A + (tr + 16 * i) * kAtPS + k);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      float b[NC];
+      at_frag<D>(B + (k + kk) * PD, tc, b);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float av = f4(a[i], kk);
+#pragma unroll
+        for (int e = 0; e < NC; ++e) c[i][e] = fmaf(av, b[e], c[i][e]);
+      }
+    }
+  }
+}
+
+// C += A^T B, A a 64-wide tile (columns 4 tr .. 4 tr + 3), B a D-wide tile;
+// rows r < rn
+template <int D>
+__device__ __forceinline__ void at_tn(const float* A, const float* B, int rn, int tr, int tc,
+                                      float (&c)[4][AtCfg<D>::NC]) {
+  constexpr int PD = AtCfg<D>::PD, NC = AtCfg<D>::NC;
+#pragma unroll 2
+  for (int r = 0; r < rn; ++r) {
+    const float4 a = ld4(A + r * kAtPS + tr * 4);
+    float b[NC];
+    at_frag<D>(B + r * PD, tc, b);
+#pragma unroll
+    for (int e = 0; e < NC; ++e) {
+      c[0][e] = fmaf(a.x, b[e], c[0][e]);
+      c[1][e] = fmaf(a.y, b[e], c[1][e]);
+      c[2][e] = fmaf(a.z, b[e], c[2][e]);
+      c[3][e] = fmaf(a.w, b[e], c[3][e]);
+    }
+  }
+}
+
+__device__ __forceinline__ float half_max(float v) {
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float half_sum(float v) {
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// keys (or queries) of a tile that can matter, rounded up to a multiple of 4
+__device__ __forceinline__ int at_span(int l0, int len) { return (min(kAtB, len - l0) + 3) & ~3; }
 
 template <int D>
 __global__ void __launch_bounds__(kAtThreads) sdpa_fwd_kernel(AtView q, AtView k, AtView v, AtView o,
                                                               float* __restrict__ lse, AtArgs a) {
-  using L = AtFwdSmem<D>;
-  constexpr int DC = D / 4;
+  using C = AtCfg<D>;
+  constexpr int NC = C::NC;
   extern __shared__ __align__(16) float at_smem[];
-  float* Qs = at_smem + L::Q;
-  float* Ks = at_smem + L::K;
-  float* Vs = at_smem + L::V;
-  float* Ps = at_smem + L::P;
+  float* Qs = at_smem;
+  float* Ks = Qs + C::TILE;
+  float* Vs = Ks + C::TILE;
+  float* Ps = Vs + C::TILE;
   const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
   const int q0 = blockIdx.x * kAtB;
-  const int r = threadIdx.x >> 2, g = threadIdx.x & 3;
-  const int qi = q0 + r;
-  at_load<D>(Qs, L::PQ, q, b, h, q0, a.Lq, a.scale);
-  float acc[DC];
+  const int tr = threadIdx.x >> 4, tc = threadIdx.x & 15;
+  at_load<D>(Qs, q, b, h, q0, a.Lq, a.scale);
+  float acc[4][NC];
+  float m[4], l[4];
 #pragma unroll
-  for (int e = 0; e < DC; ++e) acc[e] = 0.f;
-  float m = -FLT_MAX, l = 0.f;
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -FLT_MAX;
+    l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < NC; ++e) acc[i][e] = 0.f;
+  }
   const int kend = a.causal ? min(a.Lk, q0 + kAtB) : a.Lk;
   for (int k0 = 0; k0 < kend; k0 += kAtB) {
-    __syncthreads();  // previous block's K / V / P no longer read
-    at_load<D>(Ks, L::PK, k, b, h, k0, a.Lk, 1.f);
-    at_load<D>(Vs, L::PV, v, b, h, k0, a.Lk, 1.f);
+    __syncthreads();  // previous block's K / V no longer read
+    at_load<D>(Ks, k, b, h, k0, a.Lk, 1.f);
+    at_load<D>(Vs, v, b, h, k0, a.Lk, 1.f);
     __syncthreads();
-    float s[16];
+    float s[4][4];
+    at_nt<D>(Qs, Ks, tr, tc, s);
 #pragma unroll
-    for (int u = 0; u < 16; ++u) s[u] = 0.f;
-    for (int d = 0; d < D; ++d) {
-      const float qd = Qs[r * L::PQ + d];
+    for (int i = 0; i < 4; ++i) {
+      const int qi = q0 + tr + 16 * i;
+      float mx = -FLT_MAX;
 #pragma unroll
-      for (int u = 0; u < 16; ++u) s[u] = fmaf(qd, Ks[(g + 4 * u) * L::PK + d], s[u]);
-    }
-    float mx = -FLT_MAX;
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int kj = k0 + g + 4 * u;
-      const bool ok = kj < a.Lk && !(a.causal && kj > qi);
-      s[u] = ok ? s[u] : -FLT_MAX;
-      mx = fmaxf(mx, s[u]);
-    }
-    mx = quad_max(mx);
-    const float mnew = fmaxf(m, mx);
-    const float alpha = expf(m - mnew);
-    float ps = 0.f;
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const float p = s[u] == -FLT_MAX ? 0.f : expf(s[u] - mnew);
-      Ps[r * L::PP + g + 4 * u] = p;
-      ps += p;
-    }
-    l = l * alpha + quad_sum(ps);
-    m = mnew;
-#pragma unroll
-    for (int e = 0; e < DC; ++e) acc[e] *= alpha;
-    __syncwarp();  // the row's probabilities come from the four adjacent lanes
-    for (int j = 0; j < kAtB; ++j) {
-      const float pj = Ps[r * L::PP + j];
-      const float* vr = Vs + j * L::PV + g * DC;
-#pragma unroll
-      for (int e = 0; e < DC; e += 4) {
-        const float4 vv = *reinterpret_cast<const float4*>(vr + e);
-        acc[e] = fmaf(pj, vv.x, acc[e]);
-        acc[e + 1] = fmaf(pj, vv.y, acc[e + 1]);
-        acc[e + 2] = fmaf(pj, vv.z, acc[e + 2]);
-        acc[e + 3] = fmaf(pj, vv.w, acc[e + 3]);
+      for (int j = 0; j < 4; ++j) {
+        const int kj = k0 + tc + 16 * j;
+        const bool ok = kj < a.Lk && !(a.causal && kj > qi);
+        s[i][j] = ok ? s[i][j] : -FLT_MAX;
+        mx = fmaxf(mx, s[i][j]);
       }
-    }
-  }
-  if (qi < a.Lq) {
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    float* orow = at_row_w(o, b, h, qi) + g * DC;
+      const float mnew = fmaxf(m[i], half_max(mx));
+      const float alpha = expf(m[i] - mnew);
+      float ps = 0.f;
 #pragma unroll
-    for (int e = 0; e < DC; e += 4)
-      *reinterpret_cast<float4*>(orow + e) =
-          make_float4(acc[e] * inv, acc[e + 1] * inv, acc[e + 2] * inv, acc[e + 3] * inv);
-    if (g == 0) lse[(int64_t)bh * a.Lq + qi] = l > 0.f ? m + logf(l) : -FLT_MAX;
+      for (int j = 0; j < 4; ++j) {
+        const float p = s[i][j] == -FLT_MAX ? 0.f : expf(s[i][j] - mnew);
+        Ps[(tr + 16 * i) * kAtPS + tc + 16 * j] = p;
+        ps += p;
+      }
+      l[i] = l[i] * alpha + half_sum(ps);
+      m[i] = mnew;
+#pragma unroll
+      for (int e = 0; e < NC; ++e) acc[i][e] *= alpha;
+    }
+    __syncwarp();  // a row of P is written and read by the same half-warp
+    at_nn<D>(Ps, Vs, at_span(k0, a.Lk), tr, tc, acc);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qi = q0 + tr + 16 * i;
+    if (qi >= a.Lq) continue;
+    at_store_row<D>(at_row(o, b, h, qi), tc, acc[i], l[i] > 0.f ? 1.f / l[i] : 0.f);
+    if (tc == 0) lse[(int64_t)bh * a.Lq + qi] = l[i] > 0.f ? m[i] + logf(l[i]) : -FLT_MAX;
   }
 }
 
@@ -178,177 +290,175 @@ __global__ void sdpa_bwd_di_kernel(AtView dout, AtView out, float* __restrict__ 
   if (lane == 0) di[row] = s;
 }
 
-template <int D>
-struct AtKvSmem {
-  static constexpr int PK = D + 1, PV = D + 1, PQ = D + 4, PG = D + 4, PT = kAtB + 1;
-  static constexpr int K = 0, V = K + kAtB * PK, Q = V + kAtB * PV, G = Q + kAtB * PQ, P = G + kAtB * PG,
-                       S = P + kAtB * PT, LSE = S + kAtB * PT, DI = LSE + kAtB;
-  static constexpr int FLOATS = DI + kAtB;
-};
-
-template <int D>
-__global__ void __launch_bounds__(kAtThreads) sdpa_bwd_dkdv_kernel(AtView q, AtView k, AtView v, AtView dout,
-                                                                   const float* __restrict__ lse,
-                                                                   const float* __restrict__ di, AtView dk,
-                                                                   AtView dv, AtArgs a) {
-  using L = AtKvSmem<D>;
-  constexpr int DC = D / 4;
-  extern __shared__ __align__(16) float at_smem[];
-  float* Ks = at_smem + L::K;
-  float* Vs = at_smem + L::V;
-  float* Qs = at_smem + L::Q;
-  float* Gs = at_smem + L::G;
-  float* Pt = at_smem + L::P;
-  float* St = at_smem + L::S;
-  float* Ls = at_smem + L::LSE;
-  float* Ds = at_smem + L::DI;
-  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
-  const int k0 = blockIdx.x * kAtB;
-  const int j = threadIdx.x >> 2, g = threadIdx.x & 3;
-  const int kj = k0 + j;
-  at_load<D>(Ks, L::PK, k, b, h, k0, a.Lk, 1.f);
-  at_load<D>(Vs, L::PV, v, b, h, k0, a.Lk, 1.f);
-  float dka[DC], dva[DC];
-#pragma unroll
-  for (int e = 0; e < DC; ++e) dka[e] = dva[e] = 0.f;
-  const int qstart = a.causal ? (k0 / kAtB) * kAtB : 0;
-  for (int q0 = qstart; q0 < a.Lq; q0 += kAtB) {
-    __syncthreads();
-    at_load<D>(Qs, L::PQ, q, b, h, q0, a.Lq, 1.f);
-    at_load<D>(Gs, L::PG, dout, b, h, q0, a.Lq, 1.f);
-    if (threadIdx.x < kAtB) {
-      const int qi = q0 + threadIdx.x;
-      Ls[threadIdx.x] = qi < a.Lq ? lse[(int64_t)bh * a.Lq + qi] : 0.f;
-      Ds[threadIdx.x] = qi < a.Lq ? di[(int64_t)bh * a.Lq + qi] : 0.f;
-    }
-    __syncthreads();
-    float s[16], dp[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) s[u] = dp[u] = 0.f;
-    for (int d = 0; d < D; ++d) {
-      const float kd = Ks[j * L::PK + d], vd = Vs[j * L::PV + d];
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int i = g + 4 * u;
-        s[u] = fmaf(Qs[i * L::PQ + d], kd, s[u]);
-        dp[u] = fmaf(Gs[i * L::PG + d], vd, dp[u]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int i = g + 4 * u, qi = q0 + i;
-      const bool ok = qi < a.Lq && kj < a.Lk && !(a.causal && kj > qi);
-      const float p = ok ? expf(s[u] * a.scale - Ls[i]) : 0.f;
-      Pt[j * L::PT + i] = p;
-      St[j * L::PT + i] = p * (dp[u] - Ds[i]);
-    }
-    __syncwarp();  // row j of Pt / St comes from the four adjacent lanes
-    for (int i = 0; i < kAtB; ++i) {
-      const float p = Pt[j * L::PT + i], ds = St[j * L::PT + i];
-      const float* gr = Gs + i * L::PG + g * DC;
-      const float* qr = Qs + i * L::PQ + g * DC;
-#pragma unroll
-      for (int e = 0; e < DC; e += 4) {
-        const float4 gg = *reinterpret_cast<const float4*>(gr + e);
-        const float4 qq = *reinterpret_cast<const float4*>(qr + e);
-        dva[e] = fmaf(p, gg.x, dva[e]);
-        dva[e + 1] = fmaf(p, gg.y, dva[e + 1]);
-        dva[e + 2] = fmaf(p, gg.z, dva[e + 2]);
-        dva[e + 3] = fmaf(p, gg.w, dva[e + 3]);
-        dka[e] = fmaf(ds, qq.x, dka[e]);
-        dka[e + 1] = fmaf(ds, qq.y, dka[e + 1]);
-        dka[e + 2] = fmaf(ds, qq.z, dka[e + 2]);
-        dka[e + 3] = fmaf(ds, qq.w, dka[e + 3]);
-      }
-    }
-  }
-  if (kj < a.Lk) {
-    float* kr = at_row_w(dk, b, h, kj) + g * DC;
-    float* vr = at_row_w(dv, b, h, kj) + g * DC;
-#pragma unroll
-    for (int e = 0; e < DC; e += 4) {
-      *reinterpret_cast<float4*>(kr + e) =
-          make_float4(dka[e] * a.scale, dka[e + 1] * a.scale, dka[e + 2] * a.scale, dka[e + 3] * a.scale);
-      *reinterpret_cast<float4*>(vr + e) = make_float4(dva[e], dva[e + 1], dva[e + 2], dva[e + 3]);
-    }
+// per-query-row logsumexp and D_i of a query block into shared memory
+__device__ __forceinline__ void at_load_rows(float* Ls, float* Ds, const float* lse, const float* di, int64_t bh,
+                                             int q0, int Lq) {
+  if (threadIdx.x < kAtB) {
+    const int qi = q0 + threadIdx.x;
+    Ls[threadIdx.x] = qi < Lq ? lse[bh * Lq + qi] : 0.f;
+    Ds[threadIdx.x] = qi < Lq ? di[bh * Lq + qi] : 0.f;
   }
 }
 
+// P and dS of one (query block, key block) pair into the 64-wide tiles
+// (P only when Ps is given); rows tr + 16 i, keys tc + 16 j
 template <int D>
-struct AtQSmem {
-  static constexpr int PQ = D + 1, PG = D + 1, PK = D + 4, PV = D + 1, PS = kAtB + 1;
-  static constexpr int Q = 0, G = Q + kAtB * PQ, K = G + kAtB * PG, V = K + kAtB * PK, S = V + kAtB * PV;
-  static constexpr int FLOATS = S + kAtB * PS;
-};
+__device__ __forceinline__ void at_probs(const float* Qs, const float* Gs, const float* Ks, const float* Vs,
+                                         const float* Ls, const float* Ds, float* Ps, float* Ss, int q0, int k0,
+                                         const AtArgs& a, int tr, int tc) {
+  float s[4][4];
+  at_nt<D>(Qs, Ks, tr, tc, s);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = tr + 16 * i, qi = q0 + r;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int kj = k0 + tc + 16 * j;
+      const bool ok = qi < a.Lq && kj < a.Lk && !(a.causal && kj > qi);
+      s[i][j] = ok ? expf(s[i][j] - Ls[r]) : 0.f;
+      if (Ps) Ps[r * kAtPS + tc + 16 * j] = s[i][j];
+    }
+  }
+  float dp[4][4];
+  at_nt<D>(Gs, Vs, tr, tc, dp);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = tr + 16 * i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) Ss[r * kAtPS + tc + 16 * j] = s[i][j] * (dp[i][j] - Ds[r]);
+  }
+}
 
+// dK, dV of one key block; with dq_part, also this key block's slice dS K of
+// dQ (not yet times scale) at dq_part[kb][bh][q][:]
+template <int D>
+__global__ void __launch_bounds__(kAtThreads) sdpa_bwd_kv_kernel(AtView q, AtView k, AtView v, AtView dout,
+                                                                 const float* __restrict__ lse,
+                                                                 const float* __restrict__ di, AtView dk,
+                                                                 AtView dv, float* __restrict__ dq_part, AtArgs a) {
+  using C = AtCfg<D>;
+  constexpr int NC = C::NC;
+  extern __shared__ __align__(16) float at_smem[];
+  float* Ks = at_smem;
+  float* Vs = Ks + C::TILE;
+  float* Qs = Vs + C::TILE;
+  float* Gs = Qs + C::TILE;
+  float* Ps = Gs + C::TILE;
+  float* Ss = Ps + C::PTILE;
+  float* Ls = Ss + C::PTILE;
+  float* Ds = Ls + kAtB;
+  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int kb = blockIdx.x, k0 = kb * kAtB;
+  const int tr = threadIdx.x >> 4, tc = threadIdx.x & 15;
+  at_load<D>(Ks, k, b, h, k0, a.Lk, 1.f);
+  at_load<D>(Vs, v, b, h, k0, a.Lk, 1.f);
+  float dka[4][NC], dva[4][NC];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < NC; ++e) dka[i][e] = dva[i][e] = 0.f;
+  const int kspan = at_span(k0, a.Lk);
+  for (int q0 = a.causal ? k0 : 0; q0 < a.Lq; q0 += kAtB) {
+    __syncthreads();  // previous query block's tiles no longer read
+    at_load<D>(Qs, q, b, h, q0, a.Lq, a.scale);
+    at_load<D>(Gs, dout, b, h, q0, a.Lq, 1.f);
+    at_load_rows(Ls, Ds, lse, di, bh, q0, a.Lq);
+    __syncthreads();
+    at_probs<D>(Qs, Gs, Ks, Vs, Ls, Ds, Ps, Ss, q0, k0, a, tr, tc);
+    __syncthreads();  // TN reads columns written by every half-warp
+    const int rn = min(kAtB, a.Lq - q0);
+    at_tn<D>(Ps, Gs, rn, tr, tc, dva);
+    at_tn<D>(Ss, Qs, rn, tr, tc, dka);  // Qs holds scale * Q: dK = scale * dS^T Q
+    if (dq_part) {
+      float dqa[4][NC];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int e = 0; e < NC; ++e) dqa[i][e] = 0.f;
+      at_nn<D>(Ss, Ks, kspan, tr, tc, dqa);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int qi = q0 + tr + 16 * i;
+        if (qi < a.Lq)
+          at_store_row<D>(dq_part + (((int64_t)kb * a.B * a.H + bh) * a.Lq + qi) * D, tc, dqa[i], 1.f);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int kj = k0 + tr * 4 + i;
+    if (kj >= a.Lk) continue;
+    at_store_row<D>(at_row(dk, b, h, kj), tc, dka[i], 1.f);
+    at_store_row<D>(at_row(dv, b, h, kj), tc, dva[i], 1.f);
+  }
+}
+
+// dQ = scale * sum of the per-key-block slices, in key-block order; a causal
+// query row q has slices only from key blocks kb <= q / 64
+template <int D>
+__global__ void sdpa_bwd_dq_reduce_kernel(const float* __restrict__ dq_part, AtView dq, AtArgs a, int nkb) {
+  const int64_t n4 = (int64_t)a.B * a.H * a.Lq * (D / 4);
+  const int64_t slice = (int64_t)a.B * a.H * a.Lq * D;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n4; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / (D / 4);
+    const int c4 = (int)(e % (D / 4)) * 4;
+    const int qi = (int)(row % a.Lq), bh = (int)(row / a.Lq);
+    const int last = a.causal ? min(nkb - 1, qi / kAtB) : nkb - 1;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* p = dq_part + row * D + c4;
+    for (int kb = 0; kb <= last; ++kb) {
+      const float4 x = __ldg(reinterpret_cast<const float4*>(p + kb * slice));
+      s.x += x.x;
+      s.y += x.y;
+      s.z += x.z;
+      s.w += x.w;
+    }
+    *reinterpret_cast<float4*>(at_row(dq, bh / a.H, bh % a.H, qi) + c4) =
+        make_float4(s.x * a.scale, s.y * a.scale, s.z * a.scale, s.w * a.scale);
+  }
+}
+
+// dQ of one query block, recomputing S and dP per key block (used when the
+// workspace has no room for the per-key-block slices)
 template <int D>
 __global__ void __launch_bounds__(kAtThreads) sdpa_bwd_dq_kernel(AtView q, AtView k, AtView v, AtView dout,
                                                                  const float* __restrict__ lse,
                                                                  const float* __restrict__ di, AtView dq, AtArgs a) {
-  using L = AtQSmem<D>;
-  constexpr int DC = D / 4;
+  using C = AtCfg<D>;
+  constexpr int NC = C::NC;
   extern __shared__ __align__(16) float at_smem[];
-  float* Qs = at_smem + L::Q;
-  float* Gs = at_smem + L::G;
-  float* Ks = at_smem + L::K;
-  float* Vs = at_smem + L::V;
-  float* Ss = at_smem + L::S;
+  float* Qs = at_smem;
+  float* Gs = Qs + C::TILE;
+  float* Ks = Gs + C::TILE;
+  float* Vs = Ks + C::TILE;
+  float* Ss = Vs + C::TILE;
+  float* Ls = Ss + C::PTILE;
+  float* Ds = Ls + kAtB;
   const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
   const int q0 = blockIdx.x * kAtB;
-  const int r = threadIdx.x >> 2, g = threadIdx.x & 3;
-  const int qi = q0 + r;
-  at_load<D>(Qs, L::PQ, q, b, h, q0, a.Lq, 1.f);
-  at_load<D>(Gs, L::PG, dout, b, h, q0, a.Lq, 1.f);
-  const float lse_i = qi < a.Lq ? lse[(int64_t)bh * a.Lq + qi] : 0.f;
-  const float di_i = qi < a.Lq ? di[(int64_t)bh * a.Lq + qi] : 0.f;
-  float dqa[DC];
+  const int tr = threadIdx.x >> 4, tc = threadIdx.x & 15;
+  at_load<D>(Qs, q, b, h, q0, a.Lq, a.scale);
+  at_load<D>(Gs, dout, b, h, q0, a.Lq, 1.f);
+  at_load_rows(Ls, Ds, lse, di, bh, q0, a.Lq);
+  float dqa[4][NC];
 #pragma unroll
-  for (int e = 0; e < DC; ++e) dqa[e] = 0.f;
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < NC; ++e) dqa[i][e] = 0.f;
   const int kend = a.causal ? min(a.Lk, q0 + kAtB) : a.Lk;
   for (int k0 = 0; k0 < kend; k0 += kAtB) {
     __syncthreads();
-    at_load<D>(Ks, L::PK, k, b, h, k0, a.Lk, 1.f);
-    at_load<D>(Vs, L::PV, v, b, h, k0, a.Lk, 1.f);
+    at_load<D>(Ks, k, b, h, k0, a.Lk, 1.f);
+    at_load<D>(Vs, v, b, h, k0, a.Lk, 1.f);
     __syncthreads();
-    float s[16], dp[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) s[u] = dp[u] = 0.f;
-    for (int d = 0; d < D; ++d) {
-      const float qd = Qs[r * L::PQ + d], gd = Gs[r * L::PG + d];
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int jj = g + 4 * u;
-        s[u] = fmaf(qd, Ks[jj * L::PK + d], s[u]);
-        dp[u] = fmaf(gd, Vs[jj * L::PV + d], dp[u]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int jj = g + 4 * u, kj = k0 + jj;
-      const bool ok = qi < a.Lq && kj < a.Lk && !(a.causal && kj > qi);
-      const float p = ok ? expf(s[u] * a.scale - lse_i) : 0.f;
-      Ss[r * L::PS + jj] = p * (dp[u] - di_i);
-    }
-    __syncwarp();
-    for (int jj = 0; jj < kAtB; ++jj) {
-      const float ds = Ss[r * L::PS + jj];
-      const float* kr = Ks + jj * L::PK + g * DC;
-#pragma unroll
-      for (int e = 0; e < DC; e += 4) {
-        const float4 kk = *reinterpret_cast<const float4*>(kr + e);
-        dqa[e] = fmaf(ds, kk.x, dqa[e]);
-        dqa[e + 1] = fmaf(ds, kk.y, dqa[e + 1]);
-        dqa[e + 2] = fmaf(ds, kk.z, dqa[e + 2]);
-        dqa[e + 3] = fmaf(ds, kk.w, dqa[e + 3]);
-      }
-    }
+    at_probs<D>(Qs, Gs, Ks, Vs, Ls, Ds, nullptr, Ss, q0, k0, a, tr, tc);
+    __syncwarp();  // a row of dS is written and read by the same half-warp
+    at_nn<D>(Ss, Ks, at_span(k0, a.Lk), tr, tc, dqa);
   }
-  if (qi < a.Lq) {
-    float* qr = at_row_w(dq, b, h, qi) + g * DC;
 #pragma unroll
-    for (int e = 0; e < DC; e += 4)
-      *reinterpret_cast<float4*>(qr + e) =
-          make_float4(dqa[e] * a.scale, dqa[e + 1] * a.scale, dqa[e + 2] * a.scale, dqa[e + 3] * a.scale);
+  for (int i = 0; i < 4; ++i) {
+    const int qi = q0 + tr + 16 * i;
+    if (qi < a.Lq) at_store_row<D>(at_row(dq, b, h, qi), tc, dqa[i], a.scale);
   }
 }
 
@@ -387,7 +497,7 @@ static int at_smem_attr(K kernel, int bytes, std::atomic<uint64_t>& done) {
 template <int D>
 static int at_fwd(const AtView& q, const AtView& k, const AtView& v, const AtView& o, float* lse, const AtArgs& a,
                   cudaStream_t s) {
-  const int smem = AtFwdSmem<D>::FLOATS * 4;
+  const int smem = (3 * AtCfg<D>::TILE + AtCfg<D>::PTILE) * 4;
   static std::atomic<uint64_t> attr{0};
   PVB2_TRY(at_smem_attr(sdpa_fwd_kernel<D>, smem, attr));
   const dim3 grid((unsigned)((a.Lq + kAtB - 1) / kAtB), (unsigned)(a.B * a.H));
@@ -396,20 +506,39 @@ static int at_fwd(const AtView& q, const AtView& k, const AtView& v, const AtVie
   return PVB2_OK;
 }
 
+// workspace: D_i (rounded up to 256 bytes), then, when they fit, the
+// per-key-block dQ slices
+static size_t at_di_bytes(const pvb2_sdpa_desc* d) {
+  return ((size_t)d->B * d->H * d->Lq * sizeof(float) + 255) & ~(size_t)255;
+}
+static size_t at_slice_bytes(const pvb2_sdpa_desc* d) {
+  const size_t nkb = (size_t)(d->Lk + kAtB - 1) / kAtB;
+  return nkb * d->B * d->H * d->Lq * d->D * sizeof(float);
+}
+constexpr size_t kAtSliceCap = (size_t)2 << 30;  // larger slices: dQ is recomputed instead
+
 template <int D>
 static int at_bwd(const AtView& q, const AtView& k, const AtView& v, const AtView& o, const AtView& g,
-                  const float* lse, float* di, const AtView& dq, const AtView& dk, const AtView& dv, const AtArgs& a,
-                  cudaStream_t s) {
+                  const float* lse, float* di, float* dq_part, const AtView& dq, const AtView& dk, const AtView& dv,
+                  const AtArgs& a, cudaStream_t s) {
   const int64_t rows = (int64_t)a.B * a.H * a.Lq;
   sdpa_bwd_di_kernel<D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(g, o, di, a);
   PVB2_LAUNCH_CHECK();
-  const int skv = AtKvSmem<D>::FLOATS * 4, sq = AtQSmem<D>::FLOATS * 4;
+  using C = AtCfg<D>;
+  const int skv = (4 * C::TILE + 2 * C::PTILE + 2 * kAtB) * 4;
   static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
-  PVB2_TRY(at_smem_attr(sdpa_bwd_dkdv_kernel<D>, skv, attr_kv));
-  PVB2_TRY(at_smem_attr(sdpa_bwd_dq_kernel<D>, sq, attr_q));
-  const dim3 gk((unsigned)((a.Lk + kAtB - 1) / kAtB), (unsigned)(a.B * a.H));
-  sdpa_bwd_dkdv_kernel<D><<<gk, kAtThreads, skv, s>>>(q, k, v, g, lse, di, dk, dv, a);
+  PVB2_TRY(at_smem_attr(sdpa_bwd_kv_kernel<D>, skv, attr_kv));
+  const int nkb = (a.Lk + kAtB - 1) / kAtB;
+  const dim3 gk((unsigned)nkb, (unsigned)(a.B * a.H));
+  sdpa_bwd_kv_kernel<D><<<gk, kAtThreads, skv, s>>>(q, k, v, g, lse, di, dk, dv, dq_part, a);
   PVB2_LAUNCH_CHECK();
+  if (dq_part) {
+    sdpa_bwd_dq_reduce_kernel<D><<<grid_for(rows * (D / 4), 256), 256, 0, s>>>(dq_part, dq, a, nkb);
+    PVB2_LAUNCH_CHECK();
+    return PVB2_OK;
+  }
+  const int sq = (4 * C::TILE + C::PTILE + 2 * kAtB) * 4;
+  PVB2_TRY(at_smem_attr(sdpa_bwd_dq_kernel<D>, sq, attr_q));
   const dim3 gq((unsigned)((a.Lq + kAtB - 1) / kAtB), (unsigned)(a.B * a.H));
   sdpa_bwd_dq_kernel<D><<<gq, kAtThreads, sq, s>>>(q, k, v, g, lse, di, dq, a);
   PVB2_LAUNCH_CHECK();
@@ -439,7 +568,10 @@ int pvb2_sdpa_fwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tens
   return at_fwd<128>(qv, kv, vv, ov, lse, a, s);
 }
 
-size_t pvb2_sdpa_bwd_workspace_size(const pvb2_sdpa_desc* d) { return (size_t)d->B * d->H * d->Lq * sizeof(float); }
+size_t pvb2_sdpa_bwd_workspace_size(const pvb2_sdpa_desc* d) {
+  const size_t slices = at_slice_bytes(d);
+  return at_di_bytes(d) + (slices <= kAtSliceCap ? slices : 0);
+}
 
 int pvb2_sdpa_bwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tensor* k, const pvb2_tensor* v,
                   const pvb2_tensor* out, const pvb2_tensor* dout, const float* lse, const pvb2_tensor* dq,
@@ -465,14 +597,17 @@ int pvb2_sdpa_bwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tens
     if (d->Lq > 0) PVB2_TRY(pvb2_fill(dq, 0.0, stream));
     return PVB2_OK;
   }
-  const size_t need = pvb2_sdpa_bwd_workspace_size(d);
-  PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "sdpa_bwd: workspace too small (%zu < %zu)", workspace_bytes,
-                 need);
+  const size_t di_bytes = at_di_bytes(d);
+  PVB2_CHECK_ARG(workspace && workspace_bytes >= di_bytes, "sdpa_bwd: workspace too small (%zu < %zu)",
+                 workspace_bytes, di_bytes);
   const AtArgs a{d->B, d->H, d->Lq, d->Lk, d->scale, d->causal};
   float* di = (float*)workspace;
-  if (d->D == 32) return at_bwd<32>(qv, kv, vv, ov, gv, lse, di, dqv, dkv, dvv, a, s);
-  if (d->D == 64) return at_bwd<64>(qv, kv, vv, ov, gv, lse, di, dqv, dkv, dvv, a, s);
-  return at_bwd<128>(qv, kv, vv, ov, gv, lse, di, dqv, dkv, dvv, a, s);
+  // dQ through the per-key-block slices when they fit, else recomputed
+  float* dq_part =
+      workspace_bytes >= di_bytes + at_slice_bytes(d) ? (float*)((char*)workspace + di_bytes) : nullptr;
+  if (d->D == 32) return at_bwd<32>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, s);
+  if (d->D == 64) return at_bwd<64>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, s);
+  return at_bwd<128>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, s);
 }
 
 }  // extern "C"

@@ -170,6 +170,172 @@ __global__ void reduce_col_kernel(RedShape rs, int op, const void* in, int idt, 
   }
 }
 
+// ---------------------------------------------------------------- 2-D paths
+// After adjacent dims are merged, most reductions are one of
+//   column: out[c] = red_r in[r * rstride + c]      (bias / gamma gradients)
+//   row:    out[k] = red_r in[k * kstride + r]      (last-dim reductions, full sums)
+// with a single reduced stride.  These walk pointers (no index division) and
+// may split the reduced range over S blocks: block s reduces its chunk into
+// partial[s][k], and red_partials_kernel combines the S partials of each
+// output in order s = 0..S-1, so the result depends only on the shape.
+
+template <typename T>
+__device__ __forceinline__ T vinit(int op) {
+  switch (op) {
+    case PVB2_RED_PROD: return (T)1;
+    case PVB2_RED_MAX: return -std::numeric_limits<T>::infinity();
+    case PVB2_RED_MIN: return std::numeric_limits<T>::infinity();
+  }
+  return (T)0;
+}
+
+// NaN wins for max / min, as in red_combine
+template <typename T>
+__device__ __forceinline__ T vcombine(int op, T a, T b) {
+  switch (op) {
+    case PVB2_RED_PROD: return a * b;
+    case PVB2_RED_MAX: return a != a ? a : (b != b ? b : (b > a ? b : a));
+    case PVB2_RED_MIN: return a != a ? a : (b != b ? b : (b < a ? b : a));
+  }
+  return a + b;
+}
+
+template <typename T>
+__device__ __forceinline__ T velem(int op, T x) {
+  return op == PVB2_RED_SUMSQ ? x * x : x;
+}
+
+template <typename T>
+__device__ __forceinline__ T vfinal(int op, T v, T scale) {
+  return (op == PVB2_RED_SUM || op == PVB2_RED_SUMSQ) ? v * scale : v;
+}
+
+struct Red2d {
+  int64_t n_out, n_red;
+  int64_t kstride_in, kstride_out;  // kept dim (column mode: kstride_in == 1)
+  int64_t rstride;                  // reduced dim (row mode: rstride == 1)
+  int64_t chunk;                    // reduced elements per split
+  int splits;
+};
+
+// block (32, 8): x = column, y = row lane; grid (ceil(n_out / 32), splits)
+template <typename T>
+__global__ void __launch_bounds__(256) red2d_col_kernel(Red2d g, int op, const T* __restrict__ in, void* out,
+                                                        int odt, T* __restrict__ partial, T scale) {
+  __shared__ T part[8][33];
+  const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  const int64_t r0 = (int64_t)blockIdx.y * g.chunk;
+  const int64_t r1 = min(g.n_red, r0 + g.chunk);
+  T acc = vinit<T>(op);
+  if (c < g.n_out) {
+    const T* p = in + c + (r0 + threadIdx.y) * g.rstride;
+    const int64_t step = 8 * g.rstride;
+    int64_t r = r0 + threadIdx.y;
+    for (; r + 24 < r1; r += 32, p += 4 * step) {
+      const T x0 = __ldg(p), x1 = __ldg(p + step), x2 = __ldg(p + 2 * step), x3 = __ldg(p + 3 * step);
+      acc = vcombine<T>(op, acc, velem<T>(op, x0));
+      acc = vcombine<T>(op, acc, velem<T>(op, x1));
+      acc = vcombine<T>(op, acc, velem<T>(op, x2));
+      acc = vcombine<T>(op, acc, velem<T>(op, x3));
+    }
+    for (; r < r1; r += 8, p += step) acc = vcombine<T>(op, acc, velem<T>(op, __ldg(p)));
+  }
+  part[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < g.n_out) {
+#pragma unroll
+    for (int k = 1; k < 8; ++k) acc = vcombine<T>(op, acc, part[k][threadIdx.x]);
+    if (g.splits > 1) partial[(int64_t)blockIdx.y * g.n_out + c] = acc;
+    else store_as<T>(out, c * g.kstride_out, odt, vfinal<T>(op, acc, scale));
+  }
+}
+
+// one warp per output row (short rows); 8 rows per 256-thread block
+template <typename T>
+__global__ void __launch_bounds__(256) red2d_row_warp_kernel(Red2d g, int op, const T* __restrict__ in, void* out,
+                                                             int odt, T scale) {
+  const int64_t k = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (k >= g.n_out) return;
+  const T* p = in + k * g.kstride_in;
+  T acc = vinit<T>(op);
+  for (int64_t r = lane; r < g.n_red; r += 32) acc = vcombine<T>(op, acc, velem<T>(op, __ldg(p + r)));
+  for (int s = 16; s > 0; s >>= 1) acc = vcombine<T>(op, acc, __shfl_down_sync(0xffffffffu, acc, s));
+  if (lane == 0) store_as<T>(out, k * g.kstride_out, odt, vfinal<T>(op, acc, scale));
+}
+
+// one 256-thread block per (output row, split)
+template <typename T>
+__global__ void __launch_bounds__(256) red2d_row_block_kernel(Red2d g, int op, const T* __restrict__ in, void* out,
+                                                              int odt, T* __restrict__ partial, T scale) {
+  __shared__ T wacc[8];
+  const int64_t k = blockIdx.x;
+  const int64_t r0 = (int64_t)blockIdx.y * g.chunk;
+  const int64_t r1 = min(g.n_red, r0 + g.chunk);
+  const T* p = in + k * g.kstride_in;
+  T acc = vinit<T>(op);
+  int64_t r = r0 + threadIdx.x;
+  for (; r + 768 < r1; r += 1024) {
+    const T x0 = __ldg(p + r), x1 = __ldg(p + r + 256), x2 = __ldg(p + r + 512), x3 = __ldg(p + r + 768);
+    acc = vcombine<T>(op, acc, velem<T>(op, x0));
+    acc = vcombine<T>(op, acc, velem<T>(op, x1));
+    acc = vcombine<T>(op, acc, velem<T>(op, x2));
+    acc = vcombine<T>(op, acc, velem<T>(op, x3));
+  }
+  for (; r < r1; r += 256) acc = vcombine<T>(op, acc, velem<T>(op, __ldg(p + r)));
+  for (int s = 16; s > 0; s >>= 1) acc = vcombine<T>(op, acc, __shfl_down_sync(0xffffffffu, acc, s));
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) wacc[wid] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    acc = wacc[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) acc = vcombine<T>(op, acc, wacc[w]);
+    if (g.splits > 1) partial[(int64_t)blockIdx.y * g.n_out + k] = acc;
+    else store_as<T>(out, k * g.kstride_out, odt, vfinal<T>(op, acc, scale));
+  }
+}
+
+// out[k] = final(combine_s partial[s][k]); one warp per output, lanes take
+// s = lane, lane + 32, ... and a fixed shuffle tree joins them
+template <typename T>
+__global__ void __launch_bounds__(256) red_partials_kernel(Red2d g, int op, const T* __restrict__ partial, void* out,
+                                                           int odt, T scale) {
+  const int64_t k = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (k >= g.n_out) return;
+  T acc = vinit<T>(op);
+  for (int s = lane; s < g.splits; s += 32) acc = vcombine<T>(op, acc, partial[(int64_t)s * g.n_out + k]);
+  for (int s = 16; s > 0; s >>= 1) acc = vcombine<T>(op, acc, __shfl_down_sync(0xffffffffu, acc, s));
+  if (lane == 0) store_as<T>(out, k * g.kstride_out, odt, vfinal<T>(op, acc, scale));
+}
+
+enum { kRedGeneric = 0, kRedCol = 1, kRedRowWarp = 2, kRedRowBlock = 3 };
+
+template <typename T>
+static int launch_red2d(int mode, const Red2d& g, int op, const void* in, const pvb2_tensor* out, void* partial,
+                        double scale, cudaStream_t s) {
+  T* part = static_cast<T*>(partial);
+  const T* x = static_cast<const T*>(in);
+  if (mode == kRedCol) {
+    dim3 grid((unsigned)((g.n_out + 31) / 32), (unsigned)g.splits);
+    red2d_col_kernel<T><<<grid, dim3(32, 8), 0, s>>>(g, op, x, out->data, out->dtype, part, (T)scale);
+  } else if (mode == kRedRowWarp) {
+    red2d_row_warp_kernel<T><<<(unsigned)((g.n_out + 7) / 8), 256, 0, s>>>(g, op, x, out->data, out->dtype,
+                                                                           (T)scale);
+  } else {
+    dim3 grid((unsigned)g.n_out, (unsigned)g.splits);
+    red2d_row_block_kernel<T><<<grid, 256, 0, s>>>(g, op, x, out->data, out->dtype, part, (T)scale);
+  }
+  PVB2_LAUNCH_CHECK();
+  if (g.splits > 1) {
+    red_partials_kernel<T><<<(unsigned)((g.n_out + 7) / 8), 256, 0, s>>>(g, op, part, out->data, out->dtype,
+                                                                         (T)scale);
+    PVB2_LAUNCH_CHECK();
+  }
+  return PVB2_OK;
+}
+
 template <typename T>
 static int launch_reduce(const RedShape& rs, bool col, int op, const pvb2_tensor* in, const pvb2_tensor* out,
                          int64_t n_out, int64_t n_red, double scale, cudaStream_t s) {
@@ -192,14 +358,25 @@ static int launch_reduce(const RedShape& rs, bool col, int op, const pvb2_tensor
 
 using namespace pvb2;
 
-extern "C" int pvb2_reduce(int op, const pvb2_tensor* out, const pvb2_tensor* in, double scale, int compute_dtype,
-                           pvb2_stream stream) {
+namespace pvb2 {
+
+struct RedPlan {
+  RedShape rs;
+  int64_t n_out = 1, n_red = 1;
+  bool col = false;  // generic kernels: inner memory dim is kept
+  int mode = kRedGeneric;
+  Red2d g;
+  size_t elem = 0;  // partial element size when splitting
+};
+
+// Classify dims (kept / reduced), merge neighbours that are contiguous with
+// one another, and pick a kernel.  Identical for the size query and the launch.
+static int plan_reduce(int op, const pvb2_tensor* out, const pvb2_tensor* in, int compute_dtype, RedPlan& P) {
   PVB2_CHECK_ARG(out->ndim == in->ndim, "pvb2_reduce: out must keep reduced dims (ndim %d vs %d)", out->ndim,
                  in->ndim);
-  RedShape rs;
+  RedShape& rs = P.rs;
   rs.kdim = 0;
   rs.rdim = 0;
-  int64_t n_out = 1, n_red = 1;
   int inner_mem_dim = -1;
   int64_t best = INT64_MAX;
   for (int d = 0; d < in->ndim; ++d) {
@@ -208,41 +385,136 @@ extern "C" int pvb2_reduce(int op, const pvb2_tensor* out, const pvb2_tensor* in
       inner_mem_dim = d;
     }
   }
+  // merged dims, outermost first
+  int nm = 0;
+  bool mk[PVB2_MAX_DIMS];
+  int64_t msz[PVB2_MAX_DIMS], mis[PVB2_MAX_DIMS], mos[PVB2_MAX_DIMS];
   bool inner_kept = false;
   for (int d = 0; d < in->ndim; ++d) {
-    if (out->sizes[d] == in->sizes[d]) {
-      if (in->sizes[d] == 1) continue;
-      rs.ksizes[rs.kdim] = in->sizes[d];
-      rs.k_in_strides[rs.kdim] = in->strides[d];
-      rs.k_out_strides[rs.kdim] = out->strides[d];
-      rs.kdim++;
-      n_out *= in->sizes[d];
+    const bool kept = out->sizes[d] == in->sizes[d];
+    PVB2_CHECK_ARG(kept || out->sizes[d] == 1, "pvb2_reduce: out dim %d must be 1 or match", d);
+    if (in->sizes[d] == 1) continue;
+    if (kept) {
+      P.n_out *= in->sizes[d];
       if (d == inner_mem_dim) inner_kept = true;
     } else {
-      PVB2_CHECK_ARG(out->sizes[d] == 1, "pvb2_reduce: out dim %d must be 1 or match", d);
-      rs.rsizes[rs.rdim] = in->sizes[d];
-      rs.r_in_strides[rs.rdim] = in->strides[d];
+      P.n_red *= in->sizes[d];
+    }
+    const int64_t os = kept ? out->strides[d] : 0;
+    if (nm > 0 && mk[nm - 1] == kept && mis[nm - 1] == in->sizes[d] * in->strides[d] &&
+        mos[nm - 1] == in->sizes[d] * os) {
+      msz[nm - 1] *= in->sizes[d];
+      mis[nm - 1] = in->strides[d];
+      mos[nm - 1] = os;
+      continue;
+    }
+    mk[nm] = kept;
+    msz[nm] = in->sizes[d];
+    mis[nm] = in->strides[d];
+    mos[nm] = os;
+    ++nm;
+  }
+  for (int i = 0; i < nm; ++i) {
+    if (mk[i]) {
+      rs.ksizes[rs.kdim] = msz[i];
+      rs.k_in_strides[rs.kdim] = mis[i];
+      rs.k_out_strides[rs.kdim] = mos[i];
+      rs.kdim++;
+    } else {
+      rs.rsizes[rs.rdim] = msz[i];
+      rs.r_in_strides[rs.rdim] = mis[i];
       rs.rdim++;
-      n_red *= in->sizes[d];
     }
   }
-  if (n_out == 0) return PVB2_OK;
+  P.col = inner_kept && P.n_out >= 32;
+  P.mode = kRedGeneric;
+  const bool fp = compute_dtype == PVB2_F32 || compute_dtype == PVB2_F64;
+  const bool arg = op == PVB2_RED_ARGMAX || op == PVB2_RED_ARGMIN;
+  if (!fp || arg || in->dtype != compute_dtype || P.n_out == 0 || P.n_red == 0 || rs.rdim != 1 || rs.kdim > 1)
+    return PVB2_OK;
+  Red2d& g = P.g;
+  g.n_out = P.n_out;
+  g.n_red = P.n_red;
+  g.kstride_in = rs.kdim ? rs.k_in_strides[0] : 0;
+  g.kstride_out = rs.kdim ? rs.k_out_strides[0] : 0;
+  g.rstride = rs.r_in_strides[0];
+  g.splits = 1;
+  g.chunk = g.n_red;
+  P.elem = compute_dtype == PVB2_F64 ? 8 : 4;
+  const int64_t target = (int64_t)num_sms() * 4;  // 256-thread blocks
+  if (rs.kdim == 1 && g.kstride_in == 1) {
+    P.mode = kRedCol;
+    const int64_t tiles = (g.n_out + 31) / 32;
+    const int64_t s = std::min<int64_t>(std::max<int64_t>(target / tiles, 1), std::max<int64_t>(g.n_red / 64, 1));
+    g.chunk = (g.n_red + s - 1) / s;
+  } else if (g.rstride == 1) {
+    if (g.n_red <= 1024) {
+      P.mode = kRedRowWarp;
+      return PVB2_OK;
+    }
+    P.mode = kRedRowBlock;
+    const int64_t s = std::min<int64_t>(std::max<int64_t>(target / g.n_out, 1), std::max<int64_t>(g.n_red / 4096, 1));
+    g.chunk = (g.n_red + s - 1) / s;
+  } else {
+    return PVB2_OK;
+  }
+  g.chunk = std::max<int64_t>(g.chunk, 1);
+  g.splits = (int)((g.n_red + g.chunk - 1) / g.chunk);
+  return PVB2_OK;
+}
+
+static size_t plan_workspace(const RedPlan& P) {
+  return P.mode != kRedGeneric && P.mode != kRedRowWarp && P.g.splits > 1
+             ? (size_t)P.g.splits * (size_t)P.g.n_out * P.elem
+             : 0;
+}
+
+}  // namespace pvb2
+
+extern "C" size_t pvb2_reduce_workspace_size(int op, const pvb2_tensor* out, const pvb2_tensor* in,
+                                             int compute_dtype) {
+  RedPlan P;
+  if (plan_reduce(op, out, in, compute_dtype, P) != PVB2_OK) return 0;
+  return plan_workspace(P);
+}
+
+extern "C" int pvb2_reduce_ws(int op, const pvb2_tensor* out, const pvb2_tensor* in, double scale,
+                              int compute_dtype, void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+  RedPlan P;
+  const int rc = plan_reduce(op, out, in, compute_dtype, P);
+  if (rc != PVB2_OK) return rc;
+  if (P.n_out == 0) return PVB2_OK;
   cudaStream_t s = as_stream(stream);
-  if (n_red == 0) {
+  if (P.n_red == 0) {
     // empty reduction: identity (sum 0, prod 1); max/min of empty is an error upstream
     double ident = op == PVB2_RED_PROD ? 1.0 : 0.0;
     return pvb2_fill(out, ident, stream);
   }
-  const bool col = inner_kept && n_out >= 32;
+  if (P.mode != kRedGeneric) {
+    if (workspace == nullptr) {  // no scratch: one block per output (column tile) covers the whole range
+      P.g.splits = 1;
+      P.g.chunk = P.g.n_red;
+    } else {
+      const size_t need = plan_workspace(P);
+      PVB2_CHECK_ARG(workspace_bytes >= need, "pvb2_reduce_ws: workspace %zu bytes, need %zu", workspace_bytes, need);
+    }
+    if (compute_dtype == PVB2_F64) return launch_red2d<double>(P.mode, P.g, op, in->data, out, workspace, scale, s);
+    return launch_red2d<float>(P.mode, P.g, op, in->data, out, workspace, scale, s);
+  }
   switch (compute_dtype) {
-    case PVB2_F32: return launch_reduce<float>(rs, col, op, in, out, n_out, n_red, scale, s);
-    case PVB2_F64: return launch_reduce<double>(rs, col, op, in, out, n_out, n_red, scale, s);
+    case PVB2_F32: return launch_reduce<float>(P.rs, P.col, op, in, out, P.n_out, P.n_red, scale, s);
+    case PVB2_F64: return launch_reduce<double>(P.rs, P.col, op, in, out, P.n_out, P.n_red, scale, s);
     case PVB2_I64:
     case PVB2_I32:
     case PVB2_I16:
     case PVB2_I8:
     case PVB2_U8:
-    case PVB2_BOOL: return launch_reduce<int64_t>(rs, col, op, in, out, n_out, n_red, scale, s);
+    case PVB2_BOOL: return launch_reduce<int64_t>(P.rs, P.col, op, in, out, P.n_out, P.n_red, scale, s);
   }
   return fail(PVB2_ERR_UNSUPPORTED, "pvb2_reduce: compute dtype %d", compute_dtype);
+}
+
+extern "C" int pvb2_reduce(int op, const pvb2_tensor* out, const pvb2_tensor* in, double scale, int compute_dtype,
+                           pvb2_stream stream) {
+  return pvb2_reduce_ws(op, out, in, scale, compute_dtype, nullptr, 0, stream);
 }

@@ -129,6 +129,26 @@ __global__ void copy_strided_kernel(IterShape it, void* dst, int ddt, const void
   }
 }
 
+// Same-dtype copy whose innermost dim is unit-stride on both sides (the
+// head split / merge permutes of attention, transposed-batch reshapes): rows
+// of `units` V-sized words, a group of G lanes per row, row offsets from the
+// outer dims computed once per row.  `outer` holds the outer dims with
+// strides in V units.
+template <typename V>
+__global__ void __launch_bounds__(256) copy_rows_kernel(IterShape outer, int64_t rows, int64_t units, int group,
+                                                        V* __restrict__ dst, const V* __restrict__ src) {
+  const int lane = threadIdx.x % group;
+  const int64_t g0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / group;
+  const int64_t gstep = (int64_t)gridDim.x * blockDim.x / group;
+  for (int64_t r = g0; r < rows; r += gstep) {
+    int64_t offs[kMaxArgs];
+    iter_offsets(outer, 2, r, offs);
+    V* d = dst + offs[0];
+    const V* x = src + offs[1];
+    for (int64_t u = lane; u < units; u += group) d[u] = __ldg(x + u);
+  }
+}
+
 // 2-D tiled transpose for the common "make contiguous" case of a permuted
 // fp32 tensor: dst[r][c] = src[c*ld + r] blocks.
 __global__ void transpose_f32_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t rows,
@@ -408,6 +428,47 @@ int pvb2_copy(const pvb2_tensor* dst, const pvb2_tensor* src, pvb2_stream stream
       transpose_f32_kernel<<<grid, dim3(32, 8), 0, s>>>((float*)dst->data, (const float*)src->data, rows, cols,
                                                         batch, it.strides[1][nd - 2], it.strides[1][nd - 1],
                                                         nd == 3 ? it.strides[1][0] : 0);
+      PVB2_LAUNCH_CHECK();
+      return PVB2_OK;
+    }
+  }
+  const int esz = (int)dtype_size(dst->dtype);
+  if (dst->dtype == src->dtype && it.ndim >= 2 && it.strides[0][it.ndim - 1] == 1 &&
+      it.strides[1][it.ndim - 1] == 1 && it.sizes[it.ndim - 1] * esz >= 64 && esz <= 16) {
+    // pick the widest word that every row start and the row length allow
+    const int64_t inner_bytes = it.sizes[it.ndim - 1] * esz;
+    int vb = 16;
+    auto fits = [&](int w) {
+      if (inner_bytes % w || ((uintptr_t)dst->data % w) || ((uintptr_t)src->data % w)) return false;
+      for (int d = 0; d < it.ndim - 1; ++d)
+        if ((it.strides[0][d] * esz) % w || (it.strides[1][d] * esz) % w) return false;
+      return true;
+    };
+    while (vb > esz && !fits(vb)) vb >>= 1;
+    if (vb >= 4 && fits(vb)) {
+      IterShape outer;
+      outer.ndim = it.ndim - 1;
+      int64_t rows = 1;
+      for (int d = 0; d < outer.ndim; ++d) {
+        outer.sizes[d] = it.sizes[d];
+        outer.strides[0][d] = it.strides[0][d] * esz / vb;
+        outer.strides[1][d] = it.strides[1][d] * esz / vb;
+        rows *= it.sizes[d];
+      }
+      const int64_t units = inner_bytes / vb;
+      int group = 4;
+      while (group < 32 && group < units) group <<= 1;
+      const int block = 256;
+      const int grid = grid_for(rows * group, block);
+      if (vb == 16)
+        copy_rows_kernel<float4><<<grid, block, 0, s>>>(outer, rows, units, group, (float4*)dst->data,
+                                                        (const float4*)src->data);
+      else if (vb == 8)
+        copy_rows_kernel<float2><<<grid, block, 0, s>>>(outer, rows, units, group, (float2*)dst->data,
+                                                        (const float2*)src->data);
+      else
+        copy_rows_kernel<float><<<grid, block, 0, s>>>(outer, rows, units, group, (float*)dst->data,
+                                                       (const float*)src->data);
       PVB2_LAUNCH_CHECK();
       return PVB2_OK;
     }

@@ -537,3 +537,78 @@ def test_bce_loss(ocl, reduction):
         yc.backward(gy)
         yd.backward(gy.to(DEV))
         assert _diff(pc.grad, pd.grad) <= 1e-4
+
+
+# reductions at training sizes: split column sums (bias gradients), warp and
+# split-block row reductions, merged dims, strided inputs, NaN propagation
+BIG_REDUCTIONS = [
+    ("bias_grad", [6304, 768], lambda x: x.sum(0)),
+    ("bias_grad_3d", [32, 197, 768], lambda x: x.sum((0, 1))),
+    ("col_narrow", [50000, 8], lambda x: x.sum(0)),
+    ("col_mean", [4096, 1000], lambda x: x.mean(0, keepdim=True)),
+    ("col_max", [3000, 300], lambda x: x.amax(0)),
+    ("col_min", [3000, 300], lambda x: x.amin(0)),
+    ("row_short", [6304, 197], lambda x: x.sum(-1)),
+    ("row_long", [12, 60000], lambda x: x.sum(-1)),
+    ("row_max", [64, 5000], lambda x: x.amax(-1)),
+    ("all", [3, 1000, 1000], lambda x: x.sum()),
+    ("all_mean", [257, 1031], lambda x: x.mean()),
+    ("sumsq", [2048, 512], lambda x: (x * x).sum(0)),
+    ("prod", [64, 300], lambda x: (1 + 0.01 * x).prod(0)),
+    ("transposed", [768, 6304], lambda x: x.t().sum(0)),
+    ("nchw_channels", [16, 64, 28, 28], lambda x: x.sum((0, 2, 3))),
+]
+
+
+@pytest.mark.parametrize("name,shape,call", BIG_REDUCTIONS, ids=[r[0] for r in BIG_REDUCTIONS])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64], ids=["f32", "f64"])
+def test_big_reduction(ocl, name, shape, call, dtype):
+    x = torch.randn(shape, generator=_gen(11), dtype=torch.float64).to(dtype)
+    ref = call(x.double())
+    got = call(x.to(DEV)).cpu()
+    assert got.dtype == dtype and got.shape == ref.shape
+    # fp32 summation error grows like sqrt(n) * eps * |terms|; 1e-5 of the
+    # sum of magnitudes bounds it for every shape here
+    bound = call(x.double().abs()).abs().max().item() if name not in ("col_max", "col_min", "row_max") else 1.0
+    tol = (1e-5 if dtype == torch.float32 else 1e-12) * max(bound, 1.0)
+    assert _diff(ref, got) <= tol
+
+
+def test_reduction_nan_propagates(ocl):
+    x = torch.randn(4096, 64, generator=_gen(12))
+    x[1000, 5] = float("nan")
+    x[3, 63] = float("nan")
+    xd = x.to(DEV)
+    for call in (lambda t: t.amax(0), lambda t: t.amin(0), lambda t: t.sum(0), lambda t: t.amax(-1)):
+        ref, got = call(x), call(xd).cpu()
+        assert torch.equal(ref.isnan(), got.isnan())
+        m = ~ref.isnan()
+        assert _diff(ref[m], got[m]) <= 1e-3
+
+
+def test_reduction_deterministic(ocl):
+    xd = torch.randn(6304, 768, generator=_gen(13)).to(DEV)
+    a, b = xd.sum(0).cpu(), xd.sum(0).cpu()
+    assert torch.equal(a, b)
+
+
+# permuted copies with a unit-stride inner dim (row copies in 16/8/4-byte words)
+ROW_COPIES = [
+    ("qkv_split", torch.float32, [197, 8, 3 * 96], lambda x: x.unflatten(-1, (3, 96)).transpose(0, -2).contiguous()),
+    ("head_merge", torch.float32, [4, 12, 197, 64], lambda x: x.permute(2, 0, 1, 3).contiguous()),
+    ("batch_first", torch.float32, [8, 197, 768], lambda x: x.transpose(0, 1).contiguous()),
+    ("odd_inner", torch.float32, [5, 7, 33], lambda x: x.transpose(0, 1).contiguous()),
+    ("odd_offset", torch.float32, [6, 5, 40], lambda x: x[:, :, 1:37].transpose(0, 1).contiguous()),
+    ("int64", torch.int64, [6, 5, 24], lambda x: x.transpose(0, 1).contiguous()),
+    ("half", torch.float16, [6, 5, 48], lambda x: x.transpose(0, 1).contiguous()),
+    ("bytes", torch.uint8, [6, 5, 160], lambda x: x.transpose(0, 1).contiguous()),
+    ("expanded", torch.float32, [1, 5, 64], lambda x: x.expand(4, 5, 64).transpose(0, 1).contiguous()),
+]
+
+
+@pytest.mark.parametrize("name,dtype,shape,call", ROW_COPIES, ids=[r[0] for r in ROW_COPIES])
+def test_row_copy(ocl, name, dtype, shape, call):
+    x = (torch.randn(shape, generator=_gen(14)) * 50).to(dtype)
+    ref = call(x)
+    got = call(x.to(DEV)).cpu()
+    assert got.is_contiguous() and torch.equal(ref, got)
