@@ -350,6 +350,16 @@ enum { PVB2_MATH_TF32 = 0, PVB2_MATH_FP32 = 1, PVB2_MATH_3XTF32 = 2 };
 PVB2_API int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
               const float* bias, int bias_dim, double alpha, double beta, int math,
               pvb2_stream stream);
+/* Same, with scratch for splitting K over more CTAs when the output has too
+ * few 128 x BN tiles to occupy every SM (a linear layer's weight gradient:
+ * small output, K = tokens); the split partials are summed in a fixed order.
+ * workspace may be NULL (no split); otherwise it holds
+ * pvb2_gemm_workspace_size() bytes, 0 when no split applies. */
+PVB2_API size_t pvb2_gemm_workspace_size(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
+                                         int math);
+PVB2_API int pvb2_gemm_ws(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
+                          const float* bias, int bias_dim, double alpha, double beta, int math,
+                          void* workspace, size_t workspace_bytes, pvb2_stream stream);
 
 /* ------------------------------------------------------------------ */
 /* fused scaled-dot-product attention (the reference's ViT attention ran */

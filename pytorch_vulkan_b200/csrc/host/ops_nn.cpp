@@ -172,7 +172,14 @@ static void gemm(const at::Tensor& a, const at::Tensor& b, const at::Tensor& c, 
                  double alpha, double beta) {
   const int dev = c.device().index();
   pvb2_tensor A = as3d(a), B = as3d(b), C = as3d(c);
-  OCL_CHECK(pvb2_gemm(&A, &B, &C, bias, bias_dim, alpha, beta, math_mode(), stream_for(dev)));
+  const int math = math_mode();
+  const size_t wsb = pvb2_gemm_workspace_size(&A, &B, &C, math);
+  if (wsb == 0) {
+    OCL_CHECK(pvb2_gemm(&A, &B, &C, bias, bias_dim, alpha, beta, math, stream_for(dev)));
+  } else {
+    Workspace ws(wsb, dev);
+    OCL_CHECK(pvb2_gemm_ws(&A, &B, &C, bias, bias_dim, alpha, beta, math, ws.get(), ws.bytes, stream_for(dev)));
+  }
 }
 
 // mm.out, vision_ops.cpp:513-560

@@ -346,6 +346,29 @@ __global__ void binary_generic_kernel(IterShape it, int op, void* out, int odt, 
   }
 }
 
+// fp32 operands whose innermost (merged) dim has unit stride in the output
+// and unit or zero stride in each input (a transposed-batch residual add, a
+// row broadcast): rows of `len` elements, a group of G lanes per row, row
+// offsets from the outer dims computed once per row.
+__global__ void __launch_bounds__(256) binary_f32_rows_kernel(IterShape outer, int64_t rows, int64_t len, int group,
+                                                              int op, float* __restrict__ out,
+                                                              const float* __restrict__ a, int a_unit,
+                                                              const float* __restrict__ b, int b_unit, float p0,
+                                                              float p1) {
+  const int lane = threadIdx.x % group;
+  const int64_t g0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / group;
+  const int64_t gstep = (int64_t)gridDim.x * blockDim.x / group;
+  for (int64_t r = g0; r < rows; r += gstep) {
+    int64_t o[kMaxArgs];
+    iter_offsets(outer, 3, r, o);
+    float* dst = out + o[0];
+    const float* x = a + o[1];
+    const float* y = b + o[2];
+    for (int64_t u = lane; u < len; u += group)
+      dst[u] = binary_apply<float>(op, __ldg(x + u * a_unit), __ldg(y + u * b_unit), p0, p1);
+  }
+}
+
 template <typename T>
 __global__ void binary_scalar_generic_kernel(IterShape it, int op, void* out, int odt, const void* a, int adt,
                                              T sc, int scalar_first, T p0, T p1, int64_t n) {
@@ -574,6 +597,8 @@ int pvb2_unary(int op, const pvb2_tensor* out, const pvb2_tensor* x, double p0, 
   return PVB2_OK;
 }
 
+static inline bool is_compare_op(int op) { return op >= PVB2_BIN_EQ && op <= PVB2_BIN_GE; }
+
 int pvb2_binary(int op, const pvb2_tensor* out, const pvb2_tensor* a, const pvb2_tensor* b, double p0, double p1,
                 int compute_dtype, pvb2_stream stream) {
   const int64_t n = numel(out);
@@ -637,6 +662,27 @@ int pvb2_binary(int op, const pvb2_tensor* out, const pvb2_tensor* a, const pvb2
   make_iter(&it, ts, 3);
   const int block = 256;
   const int grid = grid_for(n, block);
+  const int nd = it.ndim;
+  if (f32 && !is_compare_op(op) && nd >= 1 && it.sizes[nd - 1] >= 32 && it.strides[0][nd - 1] == 1 &&
+      (it.strides[1][nd - 1] == 0 || it.strides[1][nd - 1] == 1) &&
+      (it.strides[2][nd - 1] == 0 || it.strides[2][nd - 1] == 1)) {
+    IterShape outer;
+    outer.ndim = nd - 1;
+    int64_t rows = 1;
+    for (int d = 0; d < nd - 1; ++d) {
+      outer.sizes[d] = it.sizes[d];
+      for (int k = 0; k < 3; ++k) outer.strides[k][d] = it.strides[k][d];
+      rows *= it.sizes[d];
+    }
+    const int64_t len = it.sizes[nd - 1];
+    int group = 32;
+    while (group > 4 && group / 2 >= len) group >>= 1;
+    binary_f32_rows_kernel<<<grid_for(rows * group, block), block, 0, s>>>(
+        outer, rows, len, group, op, (float*)out->data, (const float*)a->data, (int)it.strides[1][nd - 1],
+        (const float*)b->data, (int)it.strides[2][nd - 1], (float)p0, (float)p1);
+    PVB2_LAUNCH_CHECK();
+    return PVB2_OK;
+  }
   switch (compute_dtype) {
     case PVB2_F32:
       binary_generic_kernel<float><<<grid, block, 0, s>>>(it, op, out->data, out->dtype, a->data, a->dtype, b->data,

@@ -11,7 +11,9 @@
 namespace pvb2 {
 
 int gemm_tc(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, const float* bias, int bias_dim,
-            float alpha, float beta, int math, cudaStream_t s, bool* handled);
+            float alpha, float beta, int math, cudaStream_t s, bool* handled, void* workspace,
+            size_t workspace_bytes);
+size_t gemm_tc_workspace(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math);
 
 struct GemmProb {
   int64_t M, N;
@@ -45,19 +47,39 @@ struct GemmProb {
 
 using namespace pvb2;
 
-extern "C" int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, const float* bias,
-                         int bias_dim, double alpha, double beta, int math, pvb2_stream stream) {
+static int gemm_check(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int bias_dim) {
   PVB2_CHECK_ARG(A->ndim == 3 && B->ndim == 3 && C->ndim == 3, "gemm: operands must be 3-D [batch, rows, cols]");
   PVB2_CHECK_ARG(A->dtype == PVB2_F32 && B->dtype == PVB2_F32 && C->dtype == PVB2_F32, "gemm: float32 only");
   const int64_t batch = C->sizes[0], M = C->sizes[1], N = C->sizes[2], K = A->sizes[2];
   PVB2_CHECK_ARG(A->sizes[0] == batch && B->sizes[0] == batch, "gemm: batch mismatch");
   PVB2_CHECK_ARG(A->sizes[1] == M && B->sizes[1] == K && B->sizes[2] == N, "gemm: shape mismatch");
   PVB2_CHECK_ARG(bias_dim == 0 || bias_dim == 1, "gemm: bias_dim must be 0 or 1");
+  return PVB2_OK;
+}
+
+extern "C" size_t pvb2_gemm_workspace_size(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
+                                           int math) {
+  if (gemm_check(A, B, C, 0) != PVB2_OK) return 0;
+  if ((int64_t)C->sizes[0] * C->sizes[1] * C->sizes[2] == 0) return 0;
+  return gemm_tc_workspace(A, B, C, math);
+}
+
+extern "C" int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, const float* bias,
+                         int bias_dim, double alpha, double beta, int math, pvb2_stream stream) {
+  return pvb2_gemm_ws(A, B, C, bias, bias_dim, alpha, beta, math, nullptr, 0, stream);
+}
+
+extern "C" int pvb2_gemm_ws(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, const float* bias,
+                            int bias_dim, double alpha, double beta, int math, void* workspace,
+                            size_t workspace_bytes, pvb2_stream stream) {
+  PVB2_TRY(gemm_check(A, B, C, bias_dim));
+  const int64_t batch = C->sizes[0], M = C->sizes[1], N = C->sizes[2], K = A->sizes[2];
   if (batch * M * N == 0) return PVB2_OK;
   cudaStream_t s = as_stream(stream);
   if (math != PVB2_MATH_FP32) {
     bool handled = false;
-    PVB2_TRY(gemm_tc(A, B, C, bias, bias_dim, (float)alpha, (float)beta, math, s, &handled));
+    PVB2_TRY(gemm_tc(A, B, C, bias, bias_dim, (float)alpha, (float)beta, math, s, &handled, workspace,
+                     workspace_bytes));
     if (handled) return PVB2_OK;
   }
   PVB2_CHECK_ARG(batch <= 65535, "gemm: batch too large");

@@ -7,9 +7,13 @@
 //               tcgen05.mma kind::tf32 (M=128, N=BN, K=8) four times per
 //               32-deep K block and releases ring slots with tcgen05.commit;
 //   warps 2-5   epilogue: drain a finished 128xBN fp32 accumulator from TMEM
-//               (tcgen05.ld 32x32b), apply alpha / beta / bias, store with the
-//               output's strides.  Two TMEM accumulators alternate so the
-//               epilogue of one tile overlaps the main loop of the next.
+//               (tcgen05.ld 32x32b), apply alpha / bias, stage each warp's
+//               32x32 block in shared memory and write it with a TMA tensor
+//               store (row-major C: 128-byte swizzled rows; column-major C:
+//               plain 32x32 box); with beta != 0 or strides TMA cannot
+//               express, per-element stores with C's strides.  Two TMEM
+//               accumulators alternate so the epilogue of one tile overlaps
+//               the main loop of the next.
 // Either operand may be K-major (K contiguous) or MN-major (M/N contiguous),
 // chosen from its strides, so transposed views (linear's W^T, dW = dY^T X)
 // need no copies.  Every wait is bounded (tc_common.cuh).
@@ -36,7 +40,11 @@ struct GemmEpi {
   int bias_dim;           // 1: bias[n], 0: bias[m]
   int M, N, K, batch;
   int a_bcast, b_bcast;   // operand shared by all batches (batch stride 0)
+  int store;              // kStoreScalar / kStoreRows / kStoreCols
+  int splits, kb_per;     // split-K: split s covers K blocks [s * kb_per, (s + 1) * kb_per)
 };
+
+enum { kStoreScalar = 0, kStoreRows = 1, kStoreCols = 2 };
 
 // Ring depth: as many stages as fit in 192 KB, a multiple of the producer
 // count so each stage always belongs to the same producer (8 at BN = 64,
@@ -47,14 +55,16 @@ struct GemmSmem {
   static constexpr int B_BYTES = BN * kBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES / kProducers * kProducers;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;  // 2 x 4 KB store boxes per epilogue warp
+  static constexpr int BAR_OFF = EPI_OFF + 4 * 2 * 4096;
   // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], tmem slot, abort
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16;
 };
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmEpi ep) {
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, GemmEpi ep) {
   using L = GemmSmem<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -68,7 +78,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_m = (ep.M + kBM - 1) / kBM, tiles_n = (ep.N + BN - 1) / BN;
-  const int total_tiles = tiles_m * tiles_n * ep.batch;
+  const int base_tiles = tiles_m * tiles_n * ep.batch;
+  const int total_tiles = base_tiles * ep.splits;  // split-major: tile = sp * base_tiles + base tile
   const int kblocks = (ep.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -96,9 +107,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch(&tmB);
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x) {
-        const int nb = tile % tiles_n, mb = (tile / tiles_n) % tiles_m, z = tile / (tiles_n * tiles_m);
+        const int bt = tile % base_tiles, sp = tile / base_tiles;
+        const int nb = bt % tiles_n, mb = (bt / tiles_n) % tiles_m, z = bt / (tiles_n * tiles_m);
         const int za = ep.a_bcast ? 0 : z, zb = ep.b_bcast ? 0 : z;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        const int kb0 = sp * ep.kb_per, kb1 = min(kblocks, kb0 + ep.kb_per);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if ((int)(it % kProducers) != warp) continue;
@@ -133,7 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&acc_empty[buf], aph ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        const int kb0 = (tile / base_tiles) * ep.kb_per, kb1 = min(kblocks, kb0 + ep.kb_per);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&full[s], ph, abort)) break;
@@ -144,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBK / 8; ++kk) {
             const uint64_t ad = A_MN ? desc_mnmajor(sa, kk, 32 * kBK * 4) : desc_kmajor(sa, kk);
             const uint64_t bd = B_MN ? desc_mnmajor(sb, kk, 32 * kBK * 4) : desc_kmajor(sb, kk);
-            mma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
+            mma_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&empty[s]);
         }
@@ -154,15 +168,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    float* stage = (float*)(smem + L::EPI_OFF) + quarter * 2 * 1024;
+    uint32_t echunk = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
-      const int nb = tile % tiles_n, mb = (tile / tiles_n) % tiles_m, z = tile / (tiles_n * tiles_m);
+      const int bt = tile % base_tiles;
+      const int nb = bt % tiles_n, mb = (bt / tiles_n) % tiles_m, z = bt / (tiles_n * tiles_m);
+      const int zs = z + (tile / base_tiles) * ep.batch;  // z of the split's partial slab
       const int buf = local & 1;
       const uint32_t aph = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[buf], aph, abort)) break;
       tc_fence_after();
-      const int m = mb * kBM + quarter * 32 + lane;
-      float* crow = ep.C + (int64_t)z * ep.scb + (int64_t)m * ep.scm;
+      const int m0 = mb * kBM + quarter * 32;
+      const int m = m0 + lane;
       const bool mrow = m < ep.M;
       const float bias_m = (ep.bias && ep.bias_dim == 0 && mrow) ? ep.bias[m] : 0.f;
 #pragma unroll 1
@@ -170,24 +188,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
         tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + c * 32, v);
         const int n0 = nb * BN + c * 32;
-        if (mrow) {
+        if (ep.store == kStoreScalar) {
+          if (mrow) {
+            float* crow = ep.C + (int64_t)z * ep.scb + (int64_t)m * ep.scm;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + j;
-            if (n < ep.N) {
-              float* p = crow + (int64_t)n * ep.scn;
-              float r = ep.alpha * v[j];
-              if (ep.beta != 0.f) r = fmaf(ep.beta, *p, r);
-              if (ep.bias) r += ep.bias_dim == 1 ? ep.bias[n] : bias_m;
-              *p = r;
+            for (int j = 0; j < 32; ++j) {
+              const int n = n0 + j;
+              if (n < ep.N) {
+                float* p = crow + (int64_t)n * ep.scn;
+                float r = ep.alpha * v[j];
+                if (ep.beta != 0.f) r = fmaf(ep.beta, *p, r);
+                if (ep.bias) r += ep.bias_dim == 1 ? ep.bias[n] : bias_m;
+                *p = r;
+              }
             }
           }
+        } else if (m0 < ep.M && n0 < ep.N) {  // warp-uniform: the box has output to store
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float r = ep.alpha * v[j];
+            if (ep.bias) r += ep.bias_dim == 1 ? (n0 + j < ep.N ? ep.bias[n0 + j] : 0.f) : bias_m;
+            v[j] = r;
+          }
+          // boxes alternate per issued store: wait until the store before the
+          // most recent one has read this box
+          float* st = stage + (echunk & 1) * 1024;
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          if (ep.store == kStoreRows) {
+            // row `lane` of the box, 16-byte chunk q at chunk q ^ (lane % 8)
+            // (the 128-byte swizzle the tensor map applies)
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<float4*>(st + lane * 32 + ((q ^ (lane & 7)) * 4)) =
+                  make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) st[j * 32 + lane] = v[j];
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (ep.store == kStoreRows) tma_store_3d(&tmC, st, n0, m0, zs);
+            else tma_store_3d(&tmC, st, m0, n0, zs);
+            bulk_commit();
+          }
+          ++echunk;
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) bulk_wait_all();  // boxes stay valid until their stores finish
   }
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
@@ -284,45 +337,152 @@ static int make_operand_map(CUtensorMap* map, const pvb2_tensor* t, bool k_is_co
                       *mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// C [batch, M, N] as the TMA store target of 32x32 boxes: kStoreRows when N
+// is the unit-stride dim (boxes of 32 rows x 128 bytes, 128-byte swizzle),
+// kStoreCols when M is, kStoreScalar when the strides or the base do not
+// meet TMA's 16-byte rules.
+static int make_output_map(CUtensorMap* map, const pvb2_tensor* C) {
+  const int64_t Bt = C->sizes[0], M = C->sizes[1], N = C->sizes[2];
+  const int64_t sb = C->strides[0], sm = C->strides[1], sn = C->strides[2];
+  if ((uintptr_t)C->data % 16 != 0) return kStoreScalar;
+  const bool rows = sn == 1 || N == 1;
+  const bool cols = !rows && (sm == 1 || M == 1);
+  if (!rows && !cols) return kStoreScalar;
+  const int64_t inner = rows ? N : M, outer = rows ? M : N;
+  int64_t ostride = rows ? sm : sn;
+  if (outer == 1) ostride = (inner + 3) / 4 * 4;
+  const int64_t bstride = Bt == 1 ? ostride * outer : sb;
+  if (ostride < inner || (ostride * 4) % 16 != 0 || bstride <= 0 || (bstride * 4) % 16 != 0) return kStoreScalar;
+  uint64_t dims[3] = {(uint64_t)inner, (uint64_t)outer, (uint64_t)Bt};
+  uint64_t str[2] = {(uint64_t)ostride * 4, (uint64_t)bstride * 4};
+  uint32_t box[3] = {32, 32, 1};
+  if (encode_tiled(map, 3, C->data, dims, str, box, rows ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE) !=
+      PVB2_OK)
+    return kStoreScalar;
+  return rows ? kStoreRows : kStoreCols;
+}
+
 template <int BN, bool A_MN, bool B_MN>
-static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmEpi& ep, cudaStream_t s) {
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmEpi& ep,
+                       cudaStream_t s) {
   constexpr int smem = GemmSmem<BN>::TOTAL + 1024;
   static std::atomic<uint64_t> attr_done{0};
   if (first_on_device(attr_done))
     PVB2_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_kernel<BN, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        smem));
-  const int tiles = ((ep.M + kBM - 1) / kBM) * ((ep.N + BN - 1) / BN) * ep.batch;
+  const int tiles = ((ep.M + kBM - 1) / kBM) * ((ep.N + BN - 1) / BN) * ep.batch * ep.splits;
   const int grid = std::min(tiles, num_sms());
-  gemm_tf32_kernel<BN, A_MN, B_MN><<<grid, kThreads, smem, s>>>(ma, mb, ep);
+  gemm_tf32_kernel<BN, A_MN, B_MN><<<grid, kThreads, smem, s>>>(ma, mb, mc, ep);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
 
 template <int BN>
-static int dispatch_majors(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmEpi& ep,
-                           cudaStream_t s) {
-  if (!amn && !bmn) return launch_gemm<BN, false, false>(ma, mb, ep, s);
-  if (!amn && bmn) return launch_gemm<BN, false, true>(ma, mb, ep, s);
-  if (amn && !bmn) return launch_gemm<BN, true, false>(ma, mb, ep, s);
-  return launch_gemm<BN, true, true>(ma, mb, ep, s);
+static int dispatch_majors(bool amn, bool bmn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                           const GemmEpi& ep, cudaStream_t s) {
+  if (!amn && !bmn) return launch_gemm<BN, false, false>(ma, mb, mc, ep, s);
+  if (!amn && bmn) return launch_gemm<BN, false, true>(ma, mb, mc, ep, s);
+  if (amn && !bmn) return launch_gemm<BN, true, false>(ma, mb, mc, ep, s);
+  return launch_gemm<BN, true, true>(ma, mb, mc, ep, s);
+}
+
+// Split-K: out[z][m][n] = alpha * sum_s part[s][z][m][n] + beta * C + bias,
+// the S partial slabs (row pitch n4) summed in order s = 0..S-1
+__global__ void gemm_splitk_reduce_kernel(const float* __restrict__ part, int S, int64_t n4, GemmEpi ep) {
+  const int64_t nq = (ep.N + 3) / 4;
+  const int64_t total = (int64_t)ep.batch * ep.M * nq;
+  const int64_t slab = (int64_t)ep.batch * ep.M * n4;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / nq;  // z * M + m
+    const int n = (int)(e % nq) * 4;
+    const int z = (int)(row / ep.M), m = (int)(row % ep.M);
+    const float* p = part + row * n4 + n;
+    float4 acc = __ldg(reinterpret_cast<const float4*>(p));
+    for (int sp = 1; sp < S; ++sp) {
+      const float4 x = __ldg(reinterpret_cast<const float4*>(p + sp * slab));
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+    float* crow = ep.C + (int64_t)z * ep.scb + (int64_t)m * ep.scm;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (n + j >= ep.N) break;
+      float* c = crow + (int64_t)(n + j) * ep.scn;
+      float r = ep.alpha * v[j];
+      if (ep.beta != 0.f) r = fmaf(ep.beta, *c, r);
+      if (ep.bias) r += ep.bias[ep.bias_dim == 1 ? n + j : m];
+      *c = r;
+    }
+  }
+}
+
+// Problem shape, tile width and split count, shared by the workspace query
+// and the launch so both see the same plan.
+struct GemmPlan {
+  bool tc = false;
+  int BN = 256;
+  int splits = 1, kb_per = 0;
+  int64_t n4 = 0;
+  size_t ws_bytes = 0;
+};
+
+static GemmPlan plan_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math) {
+  GemmPlan p;
+  if (math != PVB2_MATH_TF32 || getenv("PVB2_DISABLE_TC")) return p;
+  const int64_t batch = C->sizes[0], M = C->sizes[1], N = C->sizes[2], K = A->sizes[2];
+  // small problems: the SIMT engine is as fast and exact
+  if ((double)M * N * K * batch < (double)(1 << 22) || K < 8) return p;
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2 || batch > 65535) return p;
+  p.tc = true;
+  p.BN = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+  // too few output tiles to fill the SMs and a long K: split K so that every
+  // SM gets work (dW = dY^T X of a linear layer: a small output, K = tokens)
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + p.BN - 1) / p.BN) * batch;
+  const int64_t kblocks = (K + kBK - 1) / kBK;
+  const int sms = num_sms();
+  if (tiles * 2 <= sms && kblocks >= 16) {
+    const int64_t S = std::min<int64_t>(sms / tiles, kblocks / 8);
+    if (S >= 2) {
+      p.kb_per = (int)((kblocks + S - 1) / S);
+      p.splits = (int)((kblocks + p.kb_per - 1) / p.kb_per);
+      p.n4 = (N + 3) / 4 * 4;
+      p.ws_bytes = (size_t)p.splits * batch * M * p.n4 * sizeof(float);
+    }
+  }
+  if (p.splits < 2) {
+    p.splits = 1;
+    p.kb_per = (int)kblocks;
+  }
+  return p;
+}
+
+size_t gemm_tc_workspace(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math) {
+  return plan_gemm(A, B, C, math).ws_bytes;
 }
 
 int gemm_tc(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, const float* bias, int bias_dim,
-            float alpha, float beta, int math, cudaStream_t s, bool* handled) {
+            float alpha, float beta, int math, cudaStream_t s, bool* handled, void* workspace,
+            size_t workspace_bytes) {
   *handled = false;
-  if (math != PVB2_MATH_TF32) return PVB2_OK;
-  if (getenv("PVB2_DISABLE_TC")) return PVB2_OK;
+  GemmPlan plan = plan_gemm(A, B, C, math);
+  if (!plan.tc) return PVB2_OK;
   const int64_t batch = C->sizes[0], M = C->sizes[1], N = C->sizes[2], K = A->sizes[2];
-  // small problems: the SIMT engine is as fast and exact
-  if ((double)M * N * K * batch < (double)(1 << 22) || K < 8) return PVB2_OK;
-  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2 || batch > 65535) return PVB2_OK;
-  const int BN = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+  const int BN = plan.BN;
   CUtensorMap ma, mb;
   bool amn = false, bmn = false;
   int abc = 0, bbc = 0;
   if (make_operand_map(&ma, A, /*k_is_cols=*/true, kBM, &amn, &abc) != PVB2_OK) return PVB2_OK;
   if (make_operand_map(&mb, B, /*k_is_cols=*/false, BN, &bmn, &bbc) != PVB2_OK) return PVB2_OK;
   pvb2::set_error("");
+  // without room for the partial slabs the product runs unsplit
+  const bool split = plan.splits > 1 && workspace && workspace_bytes >= plan.ws_bytes;
+  if (!split) {
+    plan.splits = 1;
+    plan.kb_per = (int)((K + kBK - 1) / kBK);
+  }
   GemmEpi ep;
   ep.C = (float*)C->data;
   ep.scb = C->strides[0];
@@ -338,11 +498,35 @@ int gemm_tc(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, co
   ep.batch = (int)batch;
   ep.a_bcast = abc;
   ep.b_bcast = bbc;
+  ep.splits = plan.splits;
+  ep.kb_per = plan.kb_per;
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  GemmEpi main = ep;
+  if (split) {
+    // the main kernel stores raw partial sums, slab s at z = s * batch + z
+    uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)plan.splits * batch};
+    uint64_t str[2] = {(uint64_t)plan.n4 * 4, (uint64_t)plan.n4 * M * 4};
+    uint32_t box[3] = {32, 32, 1};
+    PVB2_TRY(encode_tiled(&mc, 3, workspace, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    main.store = kStoreRows;
+    main.alpha = 1.f;
+    main.beta = 0.f;
+    main.bias = nullptr;
+  } else {
+    main.store = beta == 0.f ? make_output_map(&mc, C) : kStoreScalar;
+  }
   int st;
-  if (BN == 64) st = dispatch_majors<64>(amn, bmn, ma, mb, ep, s);
-  else if (BN == 128) st = dispatch_majors<128>(amn, bmn, ma, mb, ep, s);
-  else st = dispatch_majors<256>(amn, bmn, ma, mb, ep, s);
+  if (BN == 64) st = dispatch_majors<64>(amn, bmn, ma, mb, mc, main, s);
+  else if (BN == 128) st = dispatch_majors<128>(amn, bmn, ma, mb, mc, main, s);
+  else st = dispatch_majors<256>(amn, bmn, ma, mb, mc, main, s);
   if (st != PVB2_OK) return st;
+  if (split) {
+    const int64_t total = batch * M * ((N + 3) / 4);
+    gemm_splitk_reduce_kernel<<<grid_for(total, 256), 256, 0, s>>>((const float*)workspace, plan.splits, plan.n4,
+                                                                   ep);
+    PVB2_LAUNCH_CHECK();
+  }
   *handled = true;
   return PVB2_OK;
 }

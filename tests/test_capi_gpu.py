@@ -201,6 +201,100 @@ def test_gemm_transposed_operands_capi(lib):
     assert np.all(np.abs(out.cpu().numpy() - ref) <= 2.0 ** -9 * absref + 1e-5)
 
 
+GEMM_OUTPUTS = [
+    # layout of C, batch, M, N, K, bias_dim, beta
+    ("rows", 1, 300, 200, 96, 1, 0.0),           # row-major C, ragged edges: TMA row boxes, clipped
+    ("rows_padded", 2, 130, 96, 256, 0, 0.0),     # row stride N + 4, batched, bias per row
+    ("cols", 1, 200, 160, 192, 1, 0.0),          # C a transposed view: column boxes
+    ("rows_odd_stride", 1, 150, 90, 512, 1, 0.0),  # row stride N + 1: per-element stores
+    ("rows_beta", 1, 256, 256, 128, 1, 0.75),    # beta != 0 reads C: per-element stores
+]
+
+
+@pytest.mark.parametrize("case", GEMM_OUTPUTS, ids=[c[0] for c in GEMM_OUTPUTS])
+def test_gemm_output_layouts_capi(lib, case):
+    """TF32 GEMM epilogue for each output layout (TMA row / column boxes,
+    per-element fallback) against float64; every case is above the size
+    where small products stay on the exact SIMT kernel."""
+    layout, batch, M, N, K, bias_dim, beta = case
+    rng = np.random.default_rng(M + N)
+    a = rng.standard_normal((batch, M, K)).astype(np.float32)
+    b = rng.standard_normal((batch, K, N)).astype(np.float32)
+    c0 = rng.standard_normal((batch, M, N)).astype(np.float32)
+    bias = rng.standard_normal(N if bias_dim == 1 else M).astype(np.float32)
+    ref = np.einsum("bmk,bkn->bmn", a.astype(np.float64), b.astype(np.float64)) * 1.5 + beta * c0
+    ref = ref + (bias[None, None, :] if bias_dim == 1 else bias[None, :, None])
+    absref = np.einsum("bmk,bkn->bmn", np.abs(a).astype(np.float64), np.abs(b).astype(np.float64)) * 1.5
+    if layout == "cols":
+        store = torch.from_numpy(np.ascontiguousarray(c0.transpose(0, 2, 1))).to(DEV)
+        cd = store.transpose(1, 2)
+    elif layout in ("rows_padded", "rows_odd_stride"):
+        pad = 4 if layout == "rows_padded" else 1
+        store = torch.zeros((batch, M, N + pad)).to(DEV)
+        cd = store[:, :, :N]
+        cd.copy_(torch.from_numpy(c0).to(DEV))
+    else:
+        cd = torch.from_numpy(c0).to(DEV)
+    ad, bd, bsd = dev(a), dev(b), dev(bias)
+    sync()
+    ok(lib, lib.pvb2_gemm(ctypes.byref(td(ad)), ctypes.byref(td(bd)), ctypes.byref(td(cd)),
+                          ctypes.c_void_p(bsd.data_ptr()), bias_dim, ctypes.c_double(1.5), ctypes.c_double(beta), 0,
+                          stream()))
+    sync()
+    got = cd.cpu().numpy()
+    assert np.all(np.abs(got - ref) <= 2.0 ** -9 * absref + 1e-4)
+    if layout in ("rows_padded", "rows_odd_stride"):
+        assert store[:, :, N:].abs().max().item() == 0.0  # padding untouched
+
+
+SPLITK = [
+    # batch, M, N, K, A transposed (dY^T), beta
+    (1, 768, 768, 6304, True, 0.0),   # a linear layer's weight gradient: 18 tiles, K = tokens
+    (1, 200, 300, 4000, False, 0.5),  # ragged tiles, beta != 0 (C read in the reduction)
+    (2, 130, 250, 2048, True, 0.0),   # batched
+]
+
+
+@pytest.mark.parametrize("case", SPLITK, ids=["x".join(map(str, c[:4])) for c in SPLITK])
+def test_gemm_split_k_capi(lib, case):
+    """Split-K TF32 GEMM (few output tiles, long K) with its workspace, and the
+    same product unsplit without one, both against float64."""
+    batch, M, N, K, at, beta = case
+    lib.pvb2_gemm_workspace_size.restype = ctypes.c_size_t
+    rng = np.random.default_rng(M + K)
+    a = rng.standard_normal((batch, M, K)).astype(np.float32)
+    b = rng.standard_normal((batch, K, N)).astype(np.float32)
+    c0 = rng.standard_normal((batch, M, N)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    ref = np.einsum("bmk,bkn->bmn", a.astype(np.float64), b.astype(np.float64)) + beta * c0 + bias
+    absref = np.einsum("bmk,bkn->bmn", np.abs(a).astype(np.float64), np.abs(b).astype(np.float64))
+    ad = dev(np.ascontiguousarray(a.transpose(0, 2, 1))).transpose(1, 2) if at else dev(a)
+    bd, bsd = dev(b), dev(bias)
+    outs = []
+    for use_ws in (True, False):
+        cd = dev(c0)
+        wsz = lib.pvb2_gemm_workspace_size(ctypes.byref(td(ad)), ctypes.byref(td(bd)), ctypes.byref(td(cd)), 0)
+        assert wsz > 0
+        ws = torch.empty(wsz // 4 if use_ws else 4).to(DEV)
+        sync()
+        ok(lib, lib.pvb2_gemm_ws(ctypes.byref(td(ad)), ctypes.byref(td(bd)), ctypes.byref(td(cd)),
+                                 ctypes.c_void_p(bsd.data_ptr()), 1, ctypes.c_double(1.0), ctypes.c_double(beta), 0,
+                                 ctypes.c_void_p(ws.data_ptr() if use_ws else None),
+                                 ctypes.c_size_t(wsz if use_ws else 0), stream()))
+        sync()
+        got = cd.cpu().numpy()
+        assert np.all(np.abs(got - ref) <= 2.0 ** -9 * absref + 1e-4), use_ws
+        outs.append(got)
+    # the split partials are summed in a fixed order: repeatable bit for bit
+    cd = dev(c0)
+    ws = torch.empty(wsz // 4).to(DEV)
+    ok(lib, lib.pvb2_gemm_ws(ctypes.byref(td(ad)), ctypes.byref(td(bd)), ctypes.byref(td(cd)),
+                             ctypes.c_void_p(bsd.data_ptr()), 1, ctypes.c_double(1.0), ctypes.c_double(beta), 0,
+                             ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(wsz), stream()))
+    sync()
+    assert np.array_equal(cd.cpu().numpy(), outs[0])
+
+
 @pytest.mark.parametrize("shape", [(4, 3, 5, 6), (64, 64, 56, 56), (2, 8, 7, 7), (3, 5, 1, 1), (0, 4, 3, 3)])
 def test_batch_norm_capi(lib, shape):
     rng = np.random.default_rng(1)

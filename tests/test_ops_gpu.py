@@ -612,3 +612,26 @@ def test_row_copy(ocl, name, dtype, shape, call):
     ref = call(x)
     got = call(x.to(DEV)).cpu()
     assert got.is_contiguous() and torch.equal(ref, got)
+
+
+# fp32 binary ops on strided operands whose inner dim is unit-stride or
+# broadcast (the row-run kernel): transposed residual adds, row / column
+# broadcasts, strided outputs
+ROW_BINARIES = [
+    ("add_transposed", [197, 8, 96], [8, 197, 96], lambda a, b: a.transpose(0, 1) + b),
+    ("sub_both_transposed", [197, 8, 96], [197, 8, 96], lambda a, b: a.transpose(0, 1) - b.transpose(0, 1)),
+    ("mul_col_broadcast", [300, 70], [300, 1], lambda a, b: a * b),
+    ("div_sliced", [40, 130], [40, 100], lambda a, b: a[:, 10:110] / (b.abs() + 0.5)),
+    ("gelu_bwd_transposed", [64, 33, 48], [33, 64, 48],
+     lambda a, b: torch.ops.aten.gelu_backward(a.transpose(0, 1), b)),
+    ("add_alpha", [50, 3, 40], [3, 50, 40], lambda a, b: torch.add(a.transpose(0, 1), b, alpha=-2.5)),
+]
+
+
+@pytest.mark.parametrize("name,sa,sb,call", ROW_BINARIES, ids=[r[0] for r in ROW_BINARIES])
+def test_row_binary(ocl, name, sa, sb, call):
+    g = _gen(15)
+    a, b = torch.randn(sa, generator=g), torch.randn(sb, generator=g)
+    ref = call(a, b)
+    got = call(a.to(DEV), b.to(DEV)).cpu()
+    assert _diff(ref, got) <= 1e-6 * max(1.0, ref.abs().max().item())
