@@ -186,9 +186,10 @@ __global__ void __launch_bounds__(cThreads, 1)
       for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x) {
         if (MODE == kImplicit) {
           int kt, q0, p0, n0;
-          fwd_tile(tile, kt, q0, p0, n0);
-          const int kblocks = RS * a.cblocks;
-          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          fwd_tile(tile / a.splits, kt, q0, p0, n0);
+          int kb0, kb1;
+          wg_range(tile % a.splits, kb0, kb1);
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
             if ((int)(it % cProducers) != warp) continue;
@@ -287,6 +288,8 @@ __global__ void __launch_bounds__(cThreads, 1)
           int sp, km, ctile, rs;
           wg_tile(tile, sp, km, ctile, rs);
           wg_range(sp, kb0, kb1);
+        } else if (MODE == kImplicit) {
+          wg_range(tile % a.splits, kb0, kb1);
         }
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s_ = it % cStages;
@@ -332,14 +335,17 @@ __global__ void __launch_bounds__(cThreads, 1)
           bvalid = slot < a.slots;
         } else {
           int q0, p0, n0;
-          fwd_tile(tile, kt, q0, p0, n0);
+          fwd_tile(tile / a.splits, kt, q0, p0, n0);
+          // split-K partial slab s holds images s * N .. s * N + N - 1
+          const int nsh = (tile % a.splits) * a.N;
           const int q = q0 + row % a.bw, p = p0 + (row / a.bw) % a.bh, n = n0 + row / (a.bw * a.bh);
           valid = q < a.Q && p < a.P && n < a.N;
-          obase = a.out + a.obase + (int64_t)n * a.on + (int64_t)p * a.op + (int64_t)q * a.oq;
+          obase = a.out + a.obase + (int64_t)(n + nsh) * a.on + (int64_t)p * a.op + (int64_t)q * a.oq;
           const int r0 = quarter * 32;
           const int wq = q0 + r0 % a.bw, wp = p0 + (r0 / a.bw) % a.bh;
           bn = n0 + r0 / (a.bw * a.bh);
           bvalid = wq < a.Q && wp < a.P && bn < a.N;
+          bn += nsh;
           if (a.epi == kEpiBox) {
             bx = wq;
             by = wp;
@@ -737,12 +743,99 @@ static int plan_epilogue(ConvTcArgs& a, CUtensorMap* mc, float* out, int N, int 
   return PVB2_OK;
 }
 
+// Split-K for forward-shaped launches whose output has too few 128 x BN
+// tiles to occupy the SMs (ResNet's 7 x 7 and 14 x 14 stages): the taps x
+// channel blocks are divided into S ranges, each range's partial output is
+// TMA-stored raw into slab s of a dense [S][N][K][P][Q] buffer, and
+// conv_splitk_reduce_kernel adds the slabs in order s = 0..S-1 plus the bias.
+// S minimises rounds(S) x (K blocks per split) x (time of one K block)
+// + (time to write and read the slabs), with 60% of the per-SM TF32 rate
+// and 6 TB/s assumed.
+struct FwdSplit {
+  int splits = 1, kb_per = 0;
+  size_t bytes = 0;
+};
+
+static FwdSplit plan_fwd_split(int N, int P, int Q, int K, int taps, int Cp) {
+  FwdSplit f;
+  int bw, bh, bni;
+  pixel_block(P, Q, cBM, bw, bh, bni);
+  const int BN = bn_for(K);
+  const int64_t tiles = (int64_t)((Q + bw - 1) / bw) * ((P + bh - 1) / bh) * ((N + bni - 1) / bni) * ((K + BN - 1) / BN);
+  const int kblocks = taps * ((Cp + 31) / 32);
+  f.kb_per = kblocks;
+  const int sms = num_sms();
+  if (tiles >= sms || kblocks < 8) return f;
+  const double t_kb = 2.0 * cBM * BN * cBK / (0.6 * 816e12 / sms);
+  const double out_bytes = 4.0 * N * K * P * Q;
+  double best = 1e30;
+  for (int S = 1; S <= 8; ++S) {
+    const int kb_per = (kblocks + S - 1) / S;
+    if (S > 1 && kb_per < 4) break;
+    const int Se = (kblocks + kb_per - 1) / kb_per;
+    const int64_t rounds = (tiles * Se + sms - 1) / sms;
+    const double cost = rounds * kb_per * t_kb + (Se > 1 ? 2.0 * Se * out_bytes / 6e12 : 0.0);
+    if (cost < best * 0.97) {  // a split has to win clearly
+      best = cost;
+      f.splits = Se;
+      f.kb_per = kb_per;
+    }
+  }
+  f.bytes = f.splits > 1 ? (size_t)f.splits * N * K * P * Q * 4 : 0;
+  return f;
+}
+
+// out[obase + n*on + k*ok + p*op + q*oq] = sum_s part[s][n][k][p][q] (+ bias[k])
+__global__ void conv_splitk_reduce_kernel(const float* __restrict__ part, int S, int N, int K, int P, int Q,
+                                          const float* __restrict__ bias, float* __restrict__ out, int64_t obase,
+                                          int64_t on, int64_t ok, int64_t op, int64_t oq) {
+  const int64_t slab = (int64_t)N * K * P * Q;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < slab; e += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(e % Q);
+    int64_t r = e / Q;
+    const int p = (int)(r % P);
+    r /= P;
+    const int k = (int)(r % K);
+    const int n = (int)(r / K);
+    float acc = __ldg(part + e);
+    for (int sp = 1; sp < S; ++sp) acc += __ldg(part + sp * slab + e);
+    if (bias) acc += bias[k];
+    out[obase + n * on + k * ok + p * op + q * oq] = acc;
+  }
+}
+
+// the same for a dense NCHW output: 16-byte loads and stores over the flat index
+__global__ void conv_splitk_reduce_dense_kernel(const float* __restrict__ part, int S, int n4, int K, int PQ,
+                                                const float* __restrict__ bias, float* __restrict__ out) {
+  const int64_t slab4 = n4;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n4; e += gridDim.x * blockDim.x) {
+    float4 acc = __ldg(reinterpret_cast<const float4*>(part) + e);
+    for (int sp = 1; sp < S; ++sp) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(part) + sp * slab4 + e);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (bias) {
+      const int i = e * 4;
+      acc.x += bias[(i / PQ) % K];
+      acc.y += bias[((i + 1) / PQ) % K];
+      acc.z += bias[((i + 2) / PQ) % K];
+      acc.w += bias[((i + 3) / PQ) % K];
+    }
+    reinterpret_cast<float4*>(out)[e] = acc;
+  }
+}
+
 // Forward-shaped implicit GEMM.  act: channels-last [N, H, W, Cp]; wpacked:
 // [K][taps][Cp]; output grid P x Q with strides (sh, sw) and tap offsets;
 // out element (n, k, p, q) at out[obase + n*on + k*ok + p*op + q*oq].
+// With a split plan (plan_fwd_split) and `part` holding its slabs, the
+// launch is split-K and a reduction writes `out`.
 static int run_fwd_like(const float* act, const float* wpacked, const float* bias, float* out, int N, int Cp, int H,
                         int W, int K, const Taps& t, int P, int Q, int sh, int sw, int64_t obase, int64_t on,
-                        int64_t ok, int64_t op, int64_t oq, cudaStream_t s) {
+                        int64_t ok, int64_t op, int64_t oq, float* part, size_t part_bytes, cudaStream_t s) {
   if (P <= 0 || Q <= 0 || N <= 0) return PVB2_OK;
   int bw, bh, bni;
   pixel_block(P, Q, cBM, bw, bh, bni);
@@ -772,9 +865,37 @@ static int run_fwd_like(const float* act, const float* wpacked, const float* bia
   a.kt = (K + BN - 1) / BN;
   a.out = out;
   a.bias = bias;
-  a.tiles = a.tq * a.tp * a.tn * a.kt;
-  PVB2_TRY(plan_epilogue(a, &mc, out, N, K, P, Q));
-  return launch_bn<kImplicit>(BN, ma, mb, mc, a, s);
+  const FwdSplit fs = plan_fwd_split(N, P, Q, K, t.nr * t.ns, Cp);
+  const bool split = fs.splits > 1 && part && part_bytes >= fs.bytes;
+  a.splits = split ? fs.splits : 1;
+  a.total_kb = t.nr * t.ns * a.cblocks;
+  a.kb_per_split = split ? fs.kb_per : a.total_kb;
+  a.tiles = a.tq * a.tp * a.tn * a.kt * a.splits;
+  if (!split) {
+    PVB2_TRY(plan_epilogue(a, &mc, out, N, K, P, Q));
+    return launch_bn<kImplicit>(BN, ma, mb, mc, a, s);
+  }
+  // partial slabs: dense NCHW images s * N + n, no bias
+  a.out = part;
+  a.bias = nullptr;
+  a.obase = 0;
+  a.on = (int64_t)K * P * Q;
+  a.ok = (int64_t)P * Q;
+  a.op = Q;
+  a.oq = 1;
+  PVB2_TRY(plan_epilogue(a, &mc, part, N * a.splits, K, P, Q));
+  PVB2_TRY(launch_bn<kImplicit>(BN, ma, mb, mc, a, s));
+  const int64_t slab = (int64_t)N * K * P * Q;
+  const bool dense = obase == 0 && oq == 1 && op == Q && ok == (int64_t)P * Q && on == (int64_t)K * P * Q;
+  if (dense && slab % 4 == 0 && aligned16(out) && slab < ((int64_t)1 << 31)) {
+    conv_splitk_reduce_dense_kernel<<<grid_for(slab / 4, 256), 256, 0, s>>>(part, a.splits, (int)(slab / 4), K,
+                                                                           P * Q, bias, out);
+  } else {
+    conv_splitk_reduce_kernel<<<grid_for(slab, 256), 256, 0, s>>>(part, a.splits, N, K, P, Q, bias, out, obase, on,
+                                                                 ok, op, oq);
+  }
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
 }
 
 // Pointwise forward (transpose = false): Y[n, k, hw] = sum_c W[k, c] X[n, c, hw] (+ bias[k]).
@@ -903,10 +1024,44 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ part, int splits, 
   }
 }
 
+// Same sum for small weights with many splits (too few 32 x 32 tiles to
+// occupy the GPU): one block per (32 m, one n, tap); its G thread rows take
+// splits g, g + G, ... and the G row sums are added in order g = 0..G-1.
+__global__ void wgrad_reduce_split_kernel(const float* __restrict__ part, int splits, int taps, int cols, int mp,
+                                          int mv, float* __restrict__ out, int64_t osm, int64_t osn, int64_t ost) {
+  extern __shared__ float rows_acc[];  // [G][32]
+  const int m = blockIdx.x * 32 + threadIdx.x, n = blockIdx.y, t = blockIdx.z;
+  const int G = blockDim.y;
+  const int64_t zstride = (int64_t)taps * cols * mp;
+  float acc = 0.f;
+  if (m < mv) {
+    const float* src = part + ((int64_t)t * cols + n) * mp + m;
+#pragma unroll 4
+    for (int sp = threadIdx.y; sp < splits; sp += G) acc += __ldg(src + sp * zstride);
+  }
+  rows_acc[threadIdx.y * 32 + threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && m < mv) {
+    float sum = rows_acc[threadIdx.x];
+    for (int g = 1; g < G; ++g) sum += rows_acc[g * 32 + threadIdx.x];
+    out[m * osm + n * osn + t * ost] = sum;
+  }
+}
+
 static int wgrad_reduce(const float* part, int splits, int taps, int rows, int cols, int mv, int nv, float* dw,
                         int64_t osm, int64_t osn, int64_t ost, cudaStream_t s) {
-  const dim3 grid((unsigned)((mv + 31) / 32), (unsigned)((nv + 31) / 32), (unsigned)taps);
-  wgrad_reduce_kernel<<<grid, dim3(32, 8), 0, s>>>(part, splits, taps, cols, round4(rows), mv, nv, dw, osm, osn, ost);
+  const int64_t tiles = (int64_t)((mv + 31) / 32) * ((nv + 31) / 32) * taps;
+  if (tiles >= 2 * num_sms() || splits < 8) {
+    const dim3 grid((unsigned)((mv + 31) / 32), (unsigned)((nv + 31) / 32), (unsigned)taps);
+    wgrad_reduce_kernel<<<grid, dim3(32, 8), 0, s>>>(part, splits, taps, cols, round4(rows), mv, nv, dw, osm, osn,
+                                                     ost);
+  } else {
+    int G = 1;
+    while (G < 32 && G * 8 <= splits) G <<= 1;  // at least 4 splits per thread row
+    const dim3 grid((unsigned)((mv + 31) / 32), (unsigned)nv, (unsigned)taps);
+    wgrad_reduce_split_kernel<<<grid, dim3(32, G), G * 32 * sizeof(float), s>>>(part, splits, taps, cols,
+                                                                               round4(rows), mv, dw, osm, osn, ost);
+  }
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
@@ -1026,6 +1181,7 @@ static Taps fwd_taps(const pvb2_conv2d_desc* d) {
 // -------------------------------------------------------- workspace plans
 struct Layout {
   size_t a, b, c, total;
+  size_t part = 0, part_bytes = 0;  // split-K slabs of forward-shaped launches
 };
 
 static Layout fwd_layout(const pvb2_conv2d_desc* d) {
@@ -1040,6 +1196,10 @@ static Layout fwd_layout(const pvb2_conv2d_desc* d) {
     const int Cp = round4(d->C);
     l.b = align256((size_t)d->N * d->H * d->W * Cp * 4);
     l.total = l.b + align256((size_t)d->K * d->R * d->S * Cp * 4);
+    const FwdSplit fs = plan_fwd_split(d->N, d->P, d->Q, d->K, d->R * d->S, Cp);
+    l.part = l.total;
+    l.part_bytes = fs.bytes;
+    l.total += align256(fs.bytes);
   }
   l.c = l.total;
   return l;
@@ -1052,6 +1212,20 @@ static Layout dgrad_layout(const pvb2_conv2d_desc* d) {
   const int Kp = round4(d->K);
   l.b = align256((size_t)d->N * d->P * d->Q * Kp * 4);
   l.total = l.b + align256((size_t)d->C * d->R * d->S * Kp * 4);  // one phase's packed weights at a time
+  // split-K slabs: the largest any phase needs (phases run one after another)
+  size_t pb = 0;
+  for (int a = 0; a < d->stride_h; ++a)
+    for (int b = 0; b < d->stride_w; ++b) {
+      int nr = 0, ns = 0;
+      for (int r = 0; r < d->R; ++r) nr += ((a + d->pad_h - r * d->dil_h) % d->stride_h + d->stride_h) % d->stride_h == 0;
+      for (int c = 0; c < d->S; ++c) ns += ((b + d->pad_w - c * d->dil_w) % d->stride_w + d->stride_w) % d->stride_w == 0;
+      const int Hph = (d->H - a + d->stride_h - 1) / d->stride_h, Wph = (d->W - b + d->stride_w - 1) / d->stride_w;
+      if (Hph <= 0 || Wph <= 0 || nr == 0 || ns == 0) continue;
+      pb = std::max(pb, plan_fwd_split(d->N, Hph, Wph, d->C, nr * ns, Kp).bytes);
+    }
+  l.part = l.total;
+  l.part_bytes = pb;
+  l.total += align256(pb);
   l.c = l.total;
   return l;
 }
@@ -1117,7 +1291,7 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
     memset(&t, 0, sizeof(t));
     t.nr = t.ns = 1;
     PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, Kc, d->P, d->Q, d->K, t, d->P, d->Q, 1, 1, 0, (int64_t)d->K * pq, pq,
-                          d->Q, 1, s));
+                          d->Q, 1, nullptr, 0, s));
   } else {
     const int Cp = round4(d->C);
     PVB2_TRY(to_nhwc(x, act, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
@@ -1125,7 +1299,8 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
     pack_w_fwd_kernel<<<grid_for(wn, 256), 256, 0, s>>>(w, wp, d->K, d->C, Cp, d->R * d->S);
     PVB2_LAUNCH_CHECK();
     PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, Cp, d->H, d->W, d->K, fwd_taps(d), d->P, d->Q, d->stride_h,
-                          d->stride_w, 0, (int64_t)d->K * pq, pq, d->Q, 1, s));
+                          d->stride_w, 0, (int64_t)d->K * pq, pq, d->Q, 1, (float*)((char*)ws + l.part),
+                          l.part_bytes, s));
   }
   *handled = true;
   return PVB2_OK;
@@ -1209,7 +1384,8 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
     for (int j = 0; j < t.ns; ++j) off.w[j] = (b + d->pad_w - t.w[j] * d->dil_w) / d->stride_w;
     const int Hph = (d->H - a + d->stride_h - 1) / d->stride_h, Wph = (d->W - b + d->stride_w - 1) / d->stride_w;
     PVB2_TRY(run_fwd_like(dyn, wd, nullptr, dx, d->N, Kp, d->P, d->Q, d->C, off, Hph, Wph, 1, 1,
-                          (int64_t)a * d->W + b, (int64_t)d->C * hw, hw, (int64_t)d->stride_h * d->W, d->stride_w, s));
+                          (int64_t)a * d->W + b, (int64_t)d->C * hw, hw, (int64_t)d->stride_h * d->W, d->stride_w,
+                          (float*)((char*)ws + l.part), l.part_bytes, s));
   }
   *handled = true;
   return PVB2_OK;
