@@ -235,6 +235,28 @@ PVB2_API int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma,
                               float* running_mean, float* running_var, double momentum, double eps,
                               const pvb2_tensor* y, float* save_mean, float* save_invstd,
                               void* workspace, size_t workspace_bytes, pvb2_stream stream);
+/* Training forward in two calls, so that a host can fuse what follows the
+ * normalisation into the second pass: pvb2_batch_norm_fwd_stats writes the
+ * per-CTA partial sums of x into the workspace; pvb2_batch_norm_fwd_apply
+ * folds them (mean, invstd, running statistics, save_mean / save_invstd as
+ * pvb2_batch_norm_fwd_train) and writes
+ *     y = act(gamma * (x - mean) * invstd + beta + residual)
+ * with residual optional (NULL, or contiguous and shaped like x) and act the
+ * identity (relu = 0) or ReLU (relu = 1, NaN kept).  With residual NULL and
+ * relu 0 the pair computes exactly what pvb2_batch_norm_fwd_train does.
+ * Both need pvb2_batch_norm_fwd_split_ok(x) (contiguous fp32 NCHW within the
+ * streaming kernels' size limits) and the workspace of
+ * pvb2_batch_norm_workspace_size, untouched between the two calls.  The
+ * reference's torch front end ran batch norm, the residual add and the ReLU
+ * as three ops (norm_ops.cpp:19-84, pointwise_ops.cpp:55-113). */
+PVB2_API int pvb2_batch_norm_fwd_split_ok(const pvb2_tensor* x);
+PVB2_API int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, size_t workspace_bytes,
+                                       pvb2_stream stream);
+PVB2_API int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const float* beta,
+                                       float* running_mean, float* running_var, double momentum, double eps,
+                                       const pvb2_tensor* y, float* save_mean, float* save_invstd,
+                                       const pvb2_tensor* residual, int relu, const void* workspace,
+                                       size_t workspace_bytes, pvb2_stream stream);
 /* Batch-norm training forward that allocates nothing and takes no workspace.
  * No counterpart in the reference: it exists for callers that cannot
  * allocate device memory at the point of the call -- code running while a

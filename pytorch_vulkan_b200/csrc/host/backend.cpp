@@ -146,6 +146,7 @@ void after_op(int d) {
 
 DeviceScope::DeviceScope(const at::Tensor& t) : DeviceScope((int)t.device().index()) {}
 DeviceScope::DeviceScope(int device) {
+  flush_deferred();
   prev = current_device();
   changed = device >= 0 && device != prev;
   if (changed) set_device(device);
@@ -292,6 +293,7 @@ class OclAllocator final : public c10::Allocator {
   c10::DeleterFnPtr raw_deleter() const override { return nullptr; }
 
   void copy_data(void* dest, const void* src, std::size_t count) const override {
+    flush_deferred();
     OCL_CHECK(pvb2_memcpy_async(dest, src, count, 2, current_stream()));
   }
 };
@@ -407,6 +409,7 @@ static std::vector<ProfState>& prof() {
 }
 
 ExecGuard::ExecGuard(const char* n, int dev) : name(n), device(dev), slot(-1) {
+  flush_deferred();
   const int mode = g_trace_mode.load(std::memory_order_relaxed);
   if (mode == 2) fprintf(stderr, "%*s> %s (ocl:%d)\n", 2 * t_depth, "", n, dev);
   ++t_depth;
@@ -526,7 +529,10 @@ class OclGuardImpl final : public c10::impl::DeviceGuardImplInterface {
     set_current_stream_id(idx, s.id());
     return old;
   }
-  void* getStreamNativeHandle(const c10::Stream s) const override { return stream_by_id(s.device_index(), s.id()); }
+  void* getStreamNativeHandle(const c10::Stream s) const override {
+    flush_deferred();  // the caller may launch its own work on the stream
+    return stream_by_id(s.device_index(), s.id());
+  }
   void destroyEvent(void* e, const c10::DeviceIndex) const noexcept override {
     if (e) pvb2_event_destroy(e);
   }
@@ -553,11 +559,13 @@ class OclGuardImpl final : public c10::impl::DeviceGuardImplInterface {
   }
   c10::DeviceIndex deviceCount() const noexcept override { return (c10::DeviceIndex)device_count(); }
   bool queryStream(const c10::Stream& s) const override {
+    flush_deferred();
     int done = 0;
     OCL_CHECK(pvb2_stream_query(stream_by_id(s.device_index(), s.id()), &done));
     return done != 0;
   }
   void synchronizeStream(const c10::Stream& s) const override {
+    flush_deferred();
     OCL_CHECK(pvb2_stream_synchronize(stream_by_id(s.device_index(), s.id())));
   }
   void synchronizeEvent(void* e) const override {
@@ -719,6 +727,7 @@ static void seed_all(uint64_t seed) {
 }
 
 static void synchronize_device(int index) {
+  flush_deferred();
   if (index == -1) {
     for (int d = 0; d < device_count(); ++d) {
       if (!states()[d].ready) continue;
@@ -754,7 +763,10 @@ static void reset_peak(int d) {
   pool.peak_reserved = pool.reserved;
 }
 
-static uintptr_t stream_handle(int d) { return (uintptr_t)stream_for(d < 0 ? current_device() : d); }
+static uintptr_t stream_handle(int d) {
+  flush_deferred();  // the caller may launch its own work on the stream
+  return (uintptr_t)stream_for(d < 0 ? current_device() : d);
+}
 
 // event helpers used by timing code: create/record/elapsed on the current stream
 static uintptr_t event_create(bool timing) {

@@ -1,0 +1,152 @@
+// Deferred batch-norm epilogue.
+//
+// ResNet-style blocks run `y = bn(x); y += identity; y = relu(y)` as three
+// ops, each a full pass over the activation (the reference did the same:
+// norm_ops.cpp:19-84, pointwise_ops.cpp:55-113).  Here a training batch norm
+// launches its statistics pass at once and leaves the normalising pass
+// pending; an in-place add of a residual into its output and an in-place
+// ReLU of its output join that pass (pvb2_batch_norm_fwd_apply with a
+// residual and relu = 1) instead of re-reading the tensor.  Anything else
+// that touches the device first launches what is pending: every op entry
+// (DeviceScope, ExecGuard), stream and event calls, synchronisation.  The
+// pending state holds references to every tensor the pass reads or writes,
+// so none of them can be freed or reused before it runs.  B200_DEFER_BN=0
+// turns the deferral off.
+#include <cstdlib>
+#include <mutex>
+#include <optional>
+
+#include "ocl.h"
+
+namespace ocl {
+
+namespace {
+
+struct PendingBn {
+  at::Tensor x, y, weight, bias, running_mean, running_var, save_mean, save_invstd, residual;
+  double momentum = 0.0, eps = 0.0;
+  c10::DataPtr ws;
+  size_t ws_bytes = 0;
+  pvb2_stream stream = nullptr;
+  int device = 0;
+  bool relu = false;
+};
+
+std::mutex g_mutex;
+std::optional<PendingBn> g_pending;
+std::atomic<bool> g_any{false};
+thread_local bool t_flushing = false;
+
+bool defer_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("B200_DEFER_BN");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+float* fptr(const at::Tensor& t) { return t.defined() ? t.data_ptr<float>() : nullptr; }
+
+void launch(PendingBn& p, const char* name) {
+  DeviceScope scope(p.device);
+  OCL_OP(name, p.device);
+  const pvb2_tensor xd = desc(p.x), yd = desc(p.y);
+  pvb2_tensor rd;
+  if (p.residual.defined()) rd = desc(p.residual);
+  OCL_CHECK(pvb2_batch_norm_fwd_apply(&xd, fptr(p.weight), fptr(p.bias), fptr(p.running_mean), fptr(p.running_var),
+                                      p.momentum, p.eps, &yd, fptr(p.save_mean), fptr(p.save_invstd),
+                                      p.residual.defined() ? &rd : nullptr, p.relu ? 1 : 0, p.ws.get(), p.ws_bytes,
+                                      p.stream));
+}
+
+std::optional<PendingBn> take() {
+  std::lock_guard<std::mutex> g(g_mutex);
+  std::optional<PendingBn> p = std::move(g_pending);
+  g_pending.reset();
+  g_any.store(false, std::memory_order_release);
+  return p;
+}
+
+}  // namespace
+
+void flush_deferred() {
+  if (!g_any.load(std::memory_order_acquire) || t_flushing) return;
+  t_flushing = true;
+  try {
+    std::optional<PendingBn> p = take();
+    if (p) launch(*p, p->residual.defined() ? "native_batch_norm+add_" : "native_batch_norm");
+  } catch (...) {
+    t_flushing = false;
+    throw;
+  }
+  t_flushing = false;
+}
+
+bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optional<at::Tensor>& weight,
+                    const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& running_mean,
+                    const std::optional<at::Tensor>& running_var, const at::Tensor& save_mean,
+                    const at::Tensor& save_invstd, double momentum, double eps, Workspace&& ws, pvb2_stream stream) {
+  if (!defer_enabled()) return false;
+  const pvb2_tensor xd = desc(x);
+  if (!pvb2_batch_norm_fwd_split_ok(&xd)) return false;
+  PendingBn p;
+  p.x = x;
+  p.y = y;
+  auto opt = [](const std::optional<at::Tensor>& t) { return t.has_value() && t->defined() ? *t : at::Tensor(); };
+  p.weight = opt(weight);
+  p.bias = opt(bias);
+  p.running_mean = opt(running_mean);
+  p.running_var = opt(running_var);
+  p.save_mean = save_mean;
+  p.save_invstd = save_invstd;
+  p.momentum = momentum;
+  p.eps = eps;
+  p.ws = std::move(ws.ptr);
+  p.ws_bytes = ws.bytes;
+  p.stream = stream;
+  p.device = (int)x.device().index();
+  OCL_CHECK(pvb2_batch_norm_fwd_stats(&xd, p.ws.get(), p.ws_bytes, stream));
+  for (;;) {
+    flush_deferred();  // one pending pass at a time (another thread may have left one)
+    std::lock_guard<std::mutex> g(g_mutex);
+    if (g_pending.has_value()) continue;
+    g_pending = std::move(p);
+    g_any.store(true, std::memory_order_release);
+    return true;
+  }
+}
+
+static bool same_tensor(const at::Tensor& a, const at::Tensor& b) {
+  return a.defined() && b.defined() && a.data_ptr() == b.data_ptr() && a.sizes().equals(b.sizes()) &&
+         a.strides().equals(b.strides()) && a.scalar_type() == b.scalar_type();
+}
+
+bool fuse_deferred_add(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha) {
+  if (!g_any.load(std::memory_order_acquire)) return false;
+  std::lock_guard<std::mutex> g(g_mutex);
+  if (!g_pending || g_pending->relu || g_pending->residual.defined()) return false;
+  PendingBn& p = *g_pending;
+  if (!same_tensor(self, p.y) || !is_ocl(other) || other.device() != p.y.device()) return false;
+  if (other.scalar_type() != at::kFloat || !other.is_contiguous() || !other.sizes().equals(p.y.sizes())) return false;
+  if (alpha.isComplex() || alpha.toDouble() != 1.0) return false;
+  if (other.is_alias_of(p.y) || other.is_alias_of(p.x)) return false;
+  p.residual = other;
+  return true;
+}
+
+bool fuse_deferred_relu(const at::Tensor& self) {
+  if (!g_any.load(std::memory_order_acquire)) return false;
+  std::optional<PendingBn> p;
+  {
+    std::lock_guard<std::mutex> g(g_mutex);
+    if (!g_pending || !same_tensor(self, g_pending->y)) return false;
+    p = std::move(g_pending);
+    g_pending.reset();
+    g_any.store(false, std::memory_order_release);
+  }
+  p->relu = true;
+  launch(*p, p->residual.defined() ? "native_batch_norm+add_+relu_" : "native_batch_norm+relu_");
+  return true;
+}
+
+}  // namespace ocl

@@ -77,6 +77,21 @@ struct Workspace {
 };
 void allocator_record_stream(const c10::DataPtr& ptr, pvb2_stream stream);
 
+// ------------------------------------------------------ deferred epilogue
+// A training batch norm may leave its normalising pass pending so that an
+// in-place residual add and ReLU of its output join it (deferred.cpp).
+// flush_deferred() launches whatever is pending; every op entry, stream and
+// event call and synchronisation calls it first.
+void flush_deferred();
+bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optional<at::Tensor>& weight,
+                    const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& running_mean,
+                    const std::optional<at::Tensor>& running_var, const at::Tensor& save_mean,
+                    const at::Tensor& save_invstd, double momentum, double eps, Workspace&& ws, pvb2_stream stream);
+// true when `self += other * alpha` was folded into the pending pass
+bool fuse_deferred_add(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha);
+// true when `relu_(self)` was folded into the pending pass (and launched it)
+bool fuse_deferred_relu(const at::Tensor& self);
+
 // ------------------------------------------------------------- settings
 int math_mode();                 // PVB2_MATH_* for convolution / GEMM
 void set_math_mode(int mode);

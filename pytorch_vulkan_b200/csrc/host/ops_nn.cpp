@@ -282,6 +282,10 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
   if (training) {
     at::Tensor mean = empty({C}, at::kFloat, dev), invstd = empty({C}, at::kFloat, dev);
     Workspace ws(pvb2_batch_norm_workspace_size(&xd), dev);
+    // statistics now, the normalising pass when the next op needs it (or
+    // fused with an in-place residual add / ReLU of y)
+    if (defer_bn_apply(x, y, weight, bias, running_mean, running_var, mean, invstd, momentum, eps, std::move(ws), st))
+      return {y, mean, invstd};
     OCL_CHECK(pvb2_batch_norm_fwd_train(&xd, ptr(weight), ptr(bias), ptr(running_mean), ptr(running_var), momentum,
                                         eps, &yd, mean.data_ptr<float>(), invstd.data_ptr<float>(), ws.get(),
                                         ws.bytes, st));

@@ -85,6 +85,14 @@ static int common_compute(const at::Tensor& a, const at::Tensor& b) {
 static at::Tensor& add_out(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha, at::Tensor& out) {
   return binary_out(PVB2_BIN_ADD, self, other, out, sc(alpha), 0.0, arith_compute(out), "add.out");
 }
+// add_.Tensor: in place through add.out (out = self), or folded into a
+// pending batch-norm pass when self is its output
+static at::Tensor& add_inplace(at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha) {
+  if (fuse_deferred_add(self, other, alpha)) return self;
+  TORCH_CHECK(at::can_cast(at::result_type(self, other), self.scalar_type()), "result type ",
+              at::result_type(self, other), " can't be cast to the desired output type ", self.scalar_type());
+  return add_out(self, other, alpha, self);
+}
 static at::Tensor& sub_out(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha, at::Tensor& out) {
   return binary_out(PVB2_BIN_SUB, self, other, out, sc(alpha), 0.0, arith_compute(out), "sub.out");
 }
@@ -158,7 +166,10 @@ static at::Tensor hardtanh_backward(const at::Tensor& grad, const at::Tensor& se
 
 // relu / relu_, :55-113
 static at::Tensor relu(const at::Tensor& self) { return unary_new(PVB2_UN_RELU, self, 0, 0, "relu"); }
-static at::Tensor& relu_(at::Tensor& self) { return unary_out(PVB2_UN_RELU, self, self, 0, 0, "relu_"); }
+static at::Tensor& relu_(at::Tensor& self) {
+  if (fuse_deferred_relu(self)) return self;  // joined a pending batch-norm pass
+  return unary_out(PVB2_UN_RELU, self, self, 0, 0, "relu_");
+}
 
 // gelu / gelu_backward, :1324-1393
 static at::Tensor& gelu_out(const at::Tensor& self, c10::string_view approximate, at::Tensor& out) {
@@ -794,6 +805,7 @@ static void fused_sgd_(at::TensorList self, at::TensorList grads, at::TensorList
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   using namespace ocl;
   m.impl("add.out", &add_out);
+  m.impl("add_.Tensor", &add_inplace);
   m.impl("sub.out", &sub_out);
   m.impl("mul.out", &mul_out);
   m.impl("div.out", &div_out);

@@ -415,11 +415,20 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_stats_kernel(const float* 
   }
 }
 
+// y = act(a * x + b + residual): residual optional (same layout as x), act
+// the identity or ReLU (NaN kept, as torch's relu); the epilogue of
+// `bn(x) (+ identity)` followed by an in-place ReLU, fused by the host
+__device__ __forceinline__ float bn_epi(float v, const float* res, int64_t o, int relu) {
+  if (res) v += __ldg(res + o);
+  if (relu) v = v != v ? v : (v > 0.f ? v : 0.f);
+  return v;
+}
+
 __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
     const float* __restrict__ x, float* __restrict__ y, int N, int C, int HW, int chunk, int splits, int vec,
     const float* __restrict__ part, const float* __restrict__ gamma, const float* __restrict__ beta,
     float* __restrict__ running_mean, float* __restrict__ running_var, float momentum, float eps,
-    float* __restrict__ save_mean, float* __restrict__ save_invstd) {
+    float* __restrict__ save_mean, float* __restrict__ save_invstd, const float* __restrict__ residual, int relu) {
   __shared__ float s_ab[2];
   const int s = blockIdx.x, c = C - 1 - blockIdx.y;
   const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
@@ -456,10 +465,12 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
   __syncthreads();
   const float a = s_ab[0], b = s_ab[1];
   float* yc = y + (int64_t)c * HW;
+  const float* rc = residual ? residual + (int64_t)c * HW : nullptr;
   const int vw = vec ? 4 : 1, step = vw * blockDim.x;
   int e = start + vw * threadIdx.x;
   if (e >= end) return;
   ChanWalk w(e, step, HW);
+  const bool plain = rc == nullptr && !relu;
   if (vec) {
     for (; e < end; e += 4 * step) {
       float4 v[4];
@@ -478,6 +489,12 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
           r.y = fmaf(r.y, a, b);
           r.z = fmaf(r.z, a, b);
           r.w = fmaf(r.w, a, b);
+          if (!plain) {
+            r.x = bn_epi(r.x, rc, o[u], relu);
+            r.y = bn_epi(r.y, rc, o[u] + 1, relu);
+            r.z = bn_epi(r.z, rc, o[u] + 2, relu);
+            r.w = bn_epi(r.w, rc, o[u] + 3, relu);
+          }
           *reinterpret_cast<float4*>(yc + o[u]) = r;
         }
       }
@@ -494,7 +511,7 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u)
-        if (e + u * step < end) yc[o[u]] = fmaf(v[u], a, b);
+        if (e + u * step < end) yc[o[u]] = bn_epi(fmaf(v[u], a, b), rc, o[u], relu);
     }
   }
 }
@@ -627,7 +644,7 @@ static int bn_fwd_stream(const BnGeom& g, const BnStream& p, const float* x, flo
   PVB2_LAUNCH_CHECK();
   bn_st_apply_kernel<<<grid, kBnStThreads, 0, s>>>(x, y, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits,
                                                     p.vec ? 1 : 0, part, gamma, beta, running_mean, running_var,
-                                                    (float)momentum, (float)eps, save_mean, save_invstd);
+                                                    (float)momentum, (float)eps, save_mean, save_invstd, nullptr, 0);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
@@ -872,6 +889,58 @@ int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma, const fl
   bn_apply_kernel<<<(unsigned)(g.N * g.C), threads, 0, s>>>((const float*)x->data, (float*)y->data, g.N, g.C, g.HW,
                                                             g.splits, part, gamma, beta, running_mean, running_var,
                                                             (float)momentum, (float)eps, save_mean, save_invstd);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+int pvb2_batch_norm_fwd_split_ok(const pvb2_tensor* x) {
+  if (!x || x->ndim < 2 || x->dtype != PVB2_F32 || !is_contiguous(x)) return 0;
+  const BnGeom g = bn_geom(x);
+  return g.N * g.HW > 0 && g.C > 0 && bn_streamable(g) ? 1 : 0;
+}
+
+int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+  PVB2_TRY(check_bn_x(x));
+  PVB2_CHECK_ARG(pvb2_batch_norm_fwd_split_ok(x), "batch_norm: input not supported by the split forward");
+  const BnGeom g = bn_geom(x);
+  const void* ptrs[1] = {x->data};
+  const BnStream p = bn_stream_plan(g, ptrs, 1);
+  const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
+  PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm: workspace too small (%zu < %zu)", workspace_bytes,
+                 need);
+  const dim3 grid((unsigned)p.splits, (unsigned)g.C);
+  bn_st_stats_kernel<<<grid, kBnStThreads, 0, as_stream(stream)>>>((const float*)x->data, (int)g.N, (int)g.C,
+                                                                  (int)g.HW, p.chunk, p.splits, p.vec ? 1 : 0,
+                                                                  (float*)workspace);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const float* beta, float* running_mean,
+                              float* running_var, double momentum, double eps, const pvb2_tensor* y,
+                              float* save_mean, float* save_invstd, const pvb2_tensor* residual, int relu,
+                              const void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+  PVB2_TRY(check_bn_x(x));
+  PVB2_CHECK_ARG(pvb2_batch_norm_fwd_split_ok(x), "batch_norm: input not supported by the split forward");
+  PVB2_CHECK_ARG(is_contiguous(y) && y->dtype == PVB2_F32 && numel(y) == numel(x),
+                 "batch_norm: output must be contiguous float32 of the input's size");
+  if (residual) {
+    PVB2_CHECK_ARG(is_contiguous(residual) && residual->dtype == PVB2_F32 && residual->ndim == x->ndim,
+                   "batch_norm: residual must be contiguous float32 of the input's shape");
+    for (int d = 0; d < x->ndim; ++d)
+      PVB2_CHECK_ARG(residual->sizes[d] == x->sizes[d], "batch_norm: residual shape differs at dim %d", d);
+  }
+  const BnGeom g = bn_geom(x);
+  const void* ptrs[3] = {x->data, y->data, residual ? residual->data : nullptr};
+  const BnStream p = bn_stream_plan(g, ptrs, 3);
+  const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
+  PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm: workspace too small (%zu < %zu)", workspace_bytes,
+                 need);
+  const dim3 grid((unsigned)p.splits, (unsigned)g.C);
+  bn_st_apply_kernel<<<grid, kBnStThreads, 0, as_stream(stream)>>>(
+      (const float*)x->data, (float*)y->data, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits, p.vec ? 1 : 0,
+      (const float*)workspace, gamma, beta, running_mean, running_var, (float)momentum, (float)eps, save_mean,
+      save_invstd, residual ? (const float*)residual->data : nullptr, relu ? 1 : 0);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }

@@ -416,3 +416,39 @@ def test_invalid_arguments_are_reported(lib):
     st = lib.pvb2_conv2d_fwd(ctypes.byref(d), ctypes.byref(td(x)), ctypes.c_void_p(w.data_ptr()), None,
                              ctypes.byref(td(y)), None, ctypes.c_size_t(0), stream())
     assert st == 1 and b"output size" in lib.pvb2_last_error()
+
+
+@pytest.mark.parametrize("residual,relu", [(False, False), (False, True), (True, True), (True, False)])
+def test_batch_norm_split_fwd_capi(lib, residual, relu):
+    """pvb2_batch_norm_fwd_stats + pvb2_batch_norm_fwd_apply (with the fused
+    residual / ReLU epilogue) against the numpy restatement."""
+    rng = np.random.default_rng(21)
+    shape = (6, 24, 13, 11)
+    x = (rng.standard_normal(shape) * 2 + 1).astype(np.float32)
+    r = rng.standard_normal(shape).astype(np.float32)
+    C = shape[1]
+    gam, bet = rng.standard_normal(C).astype(np.float32), rng.standard_normal(C).astype(np.float32)
+    rm, rv = np.zeros(C, np.float32), np.ones(C, np.float32)
+    xd, rd, gd, bd, rmd, rvd = dev(x), dev(r), dev(gam), dev(bet), dev(rm), dev(rv)
+    yd = torch.empty(shape).to(DEV)
+    md, isd = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    assert lib.pvb2_batch_norm_fwd_split_ok(ctypes.byref(td(xd))) == 1
+    wsz = lib.pvb2_batch_norm_workspace_size(ctypes.byref(td(xd)))
+    ws = torch.empty(max(wsz, 4), dtype=torch.uint8).to(DEV)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    sync()
+    ok(lib, lib.pvb2_batch_norm_fwd_stats(ctypes.byref(td(xd)), ptr(ws), ctypes.c_size_t(ws.numel()), stream()))
+    ok(lib, lib.pvb2_batch_norm_fwd_apply(ctypes.byref(td(xd)), ptr(gd), ptr(bd), ptr(rmd), ptr(rvd),
+                                          ctypes.c_double(0.1), ctypes.c_double(1e-5), ctypes.byref(td(yd)), ptr(md),
+                                          ptr(isd), ctypes.byref(td(rd)) if residual else None, int(relu), ptr(ws),
+                                          ctypes.c_size_t(ws.numel()), stream()))
+    sync()
+    y, mean, invstd, nrm, nrv = npref.batch_norm_train(x, gam, bet, rm, rv, 0.1, 1e-5)
+    if residual:
+        y = y + r
+    if relu:
+        y = np.maximum(y, 0)
+    assert np.abs(yd.cpu().numpy() - y).max() < 1e-4
+    assert np.abs(md.cpu().numpy() - mean).max() < 1e-5
+    assert np.abs(rmd.cpu().numpy() - nrm).max() < 1e-5
+    assert np.abs(rvd.cpu().numpy() - nrv).max() < 1e-4

@@ -1,0 +1,151 @@
+"""Deferred batch-norm pass: a training batch norm leaves its normalising
+pass pending and an in-place residual add / ReLU of its output joins it
+(csrc/host/deferred.cpp).  Every way the output can be read before, between
+or instead of those ops must see exactly what the three separate ops give;
+checked against torch-CPU on the same inputs (the reference's own arbiter,
+tests/test_op.py:14-150 of the reference)."""
+import copy
+
+import pytest
+import torch
+import torch.nn as nn
+
+pytestmark = pytest.mark.gpu
+DEV = "ocl:0"
+
+
+def _bn_pair(C, seed):
+    torch.manual_seed(seed)
+    cpu = nn.BatchNorm2d(C)
+    with torch.no_grad():
+        cpu.weight.uniform_(0.5, 1.5)
+        cpu.bias.uniform_(-0.5, 0.5)
+    dev = nn.BatchNorm2d(C).to(DEV)
+    dev.load_state_dict(cpu.state_dict())
+    return cpu.train(), dev.train()
+
+
+def _x(shape, seed):
+    return torch.randn(shape, generator=torch.Generator().manual_seed(seed)) * 2 + 0.3
+
+
+def _close(a, b, tol=2e-5):
+    return (a.detach().double() - b.detach().cpu().double()).abs().max().item() <= tol * max(1.0, a.abs().max().item())
+
+
+def _check_bn_state(cpu, dev):
+    assert _close(cpu.running_mean, dev.running_mean)
+    assert _close(cpu.running_var, dev.running_var)
+
+
+SHAPES = [(8, 64, 28, 28), (4, 32, 7, 7), (2, 3, 5, 6)]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["x".join(map(str, s)) for s in SHAPES])
+def test_bn_relu_inplace(ocl, shape):
+    cpu, dev = _bn_pair(shape[1], 1)
+    x = _x(shape, 2)
+    ref = torch.relu_(cpu(x))
+    got = torch.relu_(dev(x.to(DEV)))
+    assert _close(ref, got)
+    _check_bn_state(cpu, dev)
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["x".join(map(str, s)) for s in SHAPES])
+def test_bn_add_relu_inplace(ocl, shape):
+    cpu, dev = _bn_pair(shape[1], 3)
+    x, r = _x(shape, 4), _x(shape, 5)
+    y = cpu(x)
+    y += r
+    ref = torch.relu_(y)
+    yd = dev(x.to(DEV))
+    yd += r.to(DEV)
+    got = torch.relu_(yd)
+    assert _close(ref, got)
+    _check_bn_state(cpu, dev)
+
+
+def test_bn_output_read_before_relu(ocl):
+    cpu, dev = _bn_pair(16, 6)
+    x = _x((4, 16, 9, 9), 7)
+    y = cpu(x)
+    yd = dev(x.to(DEV))
+    assert _close(y, yd.cpu())          # the copy to the host launches the pending pass
+    assert _close(torch.relu_(y), torch.relu_(yd))
+
+
+def test_bn_add_then_other_op(ocl):
+    cpu, dev = _bn_pair(16, 8)
+    x, r = _x((4, 16, 9, 9), 9), _x((4, 16, 9, 9), 10)
+    y = cpu(x)
+    y += r
+    yd = dev(x.to(DEV))
+    yd += r.to(DEV)
+    assert _close(y * 2, yd * 2)        # another op flushes with the residual folded in
+
+
+def test_bn_out_of_place_relu(ocl):
+    cpu, dev = _bn_pair(8, 11)
+    x = _x((2, 8, 10, 10), 12)
+    y = cpu(x)
+    yd = dev(x.to(DEV))
+    assert _close(torch.relu(y), torch.relu(yd))
+    assert _close(y, yd)                # y itself keeps the batch-norm values
+
+
+def test_bn_self_add_and_view_relu(ocl):
+    cpu, dev = _bn_pair(8, 13)
+    x = _x((2, 8, 10, 10), 14)
+    y = cpu(x)
+    y += y                              # aliasing residual: not folded
+    yd = dev(x.to(DEV))
+    yd += yd
+    assert _close(y, yd)
+    cpu2, dev2 = _bn_pair(8, 15)
+    y = cpu2(x)
+    yd = dev2(x.to(DEV))
+    torch.relu_(y[:1])                  # ReLU of a view: not folded
+    torch.relu_(yd[:1])
+    assert _close(y, yd)
+
+
+def test_bn_then_synchronize_and_stats(ocl):
+    cpu, dev = _bn_pair(32, 16)
+    x = _x((8, 32, 6, 6), 17)
+    y = cpu(x)
+    yd = dev(x.to(DEV))
+    torch.ocl.synchronize()
+    _check_bn_state(cpu, dev)
+    assert _close(y, yd)
+
+
+def test_bottleneck_forward_backward(ocl):
+    """conv -> bn -> relu_ -> conv -> bn -> += identity -> relu_, forward and
+    backward, in exact-fp32 math so that only the fusion is under test."""
+    old = torch.ocl.get_math_mode()
+    torch.ocl.set_math_mode(1)
+    try:
+        torch.manual_seed(18)
+        C = 32
+        blk = nn.ModuleDict({"c1": nn.Conv2d(C, C, 3, padding=1, bias=False), "b1": nn.BatchNorm2d(C),
+                             "c2": nn.Conv2d(C, C, 3, padding=1, bias=False), "b2": nn.BatchNorm2d(C)})
+
+        def run(m, x):
+            out = torch.relu_(m["b1"](m["c1"](x)))
+            out = m["b2"](m["c2"](out))
+            out += x
+            return torch.relu_(out)
+
+        dev = copy.deepcopy(blk).to(DEV)
+        x = _x((4, C, 14, 14), 19)
+        xc, xd = x.clone().requires_grad_(), x.to(DEV).requires_grad_()
+        yc, yd = run(blk, xc), run(dev, xd)
+        assert _close(yc, yd, 1e-4)
+        g = _x(yc.shape, 20)
+        yc.backward(g)
+        yd.backward(g.to(DEV))
+        assert _close(xc.grad, xd.grad, 1e-4)
+        for (n, p), (_, q) in zip(blk.named_parameters(), dev.named_parameters()):
+            assert _close(p.grad, q.grad, 1e-4), n
+    finally:
+        torch.ocl.set_math_mode(old)
