@@ -537,17 +537,14 @@ __global__ void pack_w_phase_kernel(const float* __restrict__ w, float* __restri
 // small-C convolutions as a GEMM over im2col columns:
 // Xcol[n, p, q, j] = X[n, c, p*sh - ph + r*dh, q*sw - pw + s*dw] with j = (c*R + r)*S + s
 // (W's own flattening; 0 outside the image and for j >= C*R*S up to Kc).
-// grid (P, N): one output row per CTA, in runs of 32 columns.  Loads walk q
-// (neighbouring threads read neighbouring input columns), a shared-memory
-// tile transposes the run, and stores are float4 along j.
+// grid (P, N): one output row per CTA; each thread gathers four columns and
+// writes them as one 16-byte store, consecutive threads consecutive stores.
 constexpr int kIm2colMaxK = 256;
-constexpr int kIm2colRun = 32;
 __global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ x, float* __restrict__ xcol, int C,
                                                      int H, int W, int P, int Q, int R, int S, int Kc, int sh, int sw,
                                                      int ph, int pw, int dh, int dw) {
   // per column j of this output row: the input row's offset (-1: zero column) and the tap's w shift
   __shared__ int joff[kIm2colMaxK], js[kIm2colMaxK];
-  __shared__ float tile[kIm2colRun][kIm2colMaxK + 1];
   const int p = blockIdx.x;
   const int64_t n = blockIdx.y;
   const int crs = C * R * S;
@@ -559,39 +556,55 @@ __global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ x
   }
   __syncthreads();
   const float* xn = x + n * C * H * W;
-  float* row = xcol + ((n * P + p) * Q) * (int64_t)Kc;
-  const int lq = threadIdx.x % kIm2colRun, lj = threadIdx.x / kIm2colRun, jstep = blockDim.x / kIm2colRun;
-  for (int q0 = 0; q0 < Q; q0 += kIm2colRun) {
-    const int q = q0 + lq;
+  // the row's Q x Kc columns as consecutive 16-byte stores; the gathered
+  // loads of neighbouring threads hit the same few input rows (L1)
+  const int kc4 = Kc / 4, total = Q * kc4;
+  float4* out = reinterpret_cast<float4*>(xcol + ((n * P + p) * Q) * (int64_t)Kc);
+  for (int t = threadIdx.x; t < total; t += blockDim.x) {
+    const int q = t / kc4, j = (t - q * kc4) * 4;
     const int wq = q * sw;
-    const bool qok = q < Q;
-    // eight loads in flight per thread before their shared-memory stores
-    constexpr int U = 8;
-    for (int jb = lj; jb < Kc; jb += U * jstep) {
-      float v[U];
+    float v[4];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int j = jb + u * jstep;
-        v[u] = 0.f;
-        if (j < Kc) {
-          const int ro = joff[j], w = wq + js[j];
-          if (qok && ro >= 0 && (unsigned)w < (unsigned)W) v[u] = __ldg(xn + ro + w);
-        }
-      }
+    for (int e = 0; e < 4; ++e) {
+      const int ro = joff[j + e], w = wq + js[j + e];
+      v[e] = (ro >= 0 && (unsigned)w < (unsigned)W) ? __ldg(xn + ro + w) : 0.f;
+    }
+    out[t] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+// Strided 1x1 convolutions (ResNet's downsampling projections) as
+// pointwise ones over the sampled pixels.
+// xs[plane][p][q] = x[plane][p*sh][q*sw]; one thread per sampled element,
+// 32-bit index arithmetic (the host keeps the element count below 2^31)
+__global__ void subsample_kernel(const float* __restrict__ x, float* __restrict__ xs, int total, int H, int W, int P,
+                                 int Q, int sh, int sw) {
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int q = e % Q, r = e / Q;
+    const int p = r % P, pl = r / P;
+    xs[e] = __ldg(x + ((int64_t)pl * H + p * sh) * W + q * sw);
+  }
+}
+
+// dx[plane][h][w] = t[plane][h/sh][w/sw] on the sampled pixels, 0 elsewhere,
+// written whole (no separate clearing pass) as 16-byte stores; W % 4 == 0
+// and fewer than 2^31 float4 of dx (checked on the host)
+__global__ void scatter_strided_kernel(const float* __restrict__ t, float* __restrict__ dx, int total4, int H, int W,
+                                       int P, int Q, int sh, int sw) {
+  const int w4 = W / 4;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total4; e += gridDim.x * blockDim.x) {
+    const int w0 = (e % w4) * 4, r = e / w4;
+    const int h = r % H, pl = r / H;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (h % sh == 0 && h / sh < P) {
+      const float* row = t + ((int64_t)pl * P + h / sh) * Q;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int j = jb + u * jstep;
-        if (j < Kc) tile[lq][j] = v[u];
+      for (int u = 0; u < 4; ++u) {
+        const int w = w0 + u;
+        if (w % sw == 0 && w / sw < Q) v[u] = __ldg(row + w / sw);
       }
     }
-    __syncthreads();
-    const int nq = min(kIm2colRun, Q - q0), kc4 = Kc / 4;
-    float4* out = reinterpret_cast<float4*>(row + (int64_t)q0 * Kc);
-    for (int t = threadIdx.x; t < nq * kc4; t += blockDim.x) {
-      const int qq = t / kc4, j4 = (t - qq * kc4) * 4;
-      out[t] = make_float4(tile[qq][j4], tile[qq][j4 + 1], tile[qq][j4 + 2], tile[qq][j4 + 3]);
-    }
-    __syncthreads();
+    reinterpret_cast<float4*>(dx)[e] = make_float4(v[0], v[1], v[2], v[3]);
   }
 }
 
@@ -642,6 +655,23 @@ static bool tc_conv_shape_ok(const pvb2_conv2d_desc* d) {
 static bool pointwise(const pvb2_conv2d_desc* d) {
   return d->R == 1 && d->S == 1 && d->stride_h == 1 && d->stride_w == 1 && d->pad_h == 0 && d->pad_w == 0 &&
          ((int64_t)d->H * d->W) % 4 == 0 && d->C % 4 == 0 && d->K % 4 == 0;
+}
+
+// 1x1, strided, no padding, with 16-byte sampled rows: a pointwise
+// convolution over the sampled pixels xs (a dense [N][C][P][Q] copy)
+static bool strided_pointwise(const pvb2_conv2d_desc* d) {
+  return d->R == 1 && d->S == 1 && (d->stride_h > 1 || d->stride_w > 1) && d->pad_h == 0 && d->pad_w == 0 &&
+         ((int64_t)d->P * d->Q) % 4 == 0 && d->C % 4 == 0 && d->K % 4 == 0 && d->W % 4 == 0 &&
+         d->P == (d->H - 1) / d->stride_h + 1 && d->Q == (d->W - 1) / d->stride_w + 1 &&
+         (int64_t)d->N * d->C * d->H * d->W < ((int64_t)1 << 31);
+}
+static size_t sampled_bytes(const pvb2_conv2d_desc* d) { return (size_t)d->N * d->C * d->P * d->Q * 4; }
+static int subsample(const pvb2_conv2d_desc* d, const float* x, float* xs, cudaStream_t s) {
+  const int64_t total = (int64_t)d->N * d->C * d->P * d->Q;
+  subsample_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, xs, (int)total, d->H, d->W, d->P, d->Q, d->stride_h,
+                                                         d->stride_w);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
 }
 
 // Few input channels and a spatial filter (the 3-channel stem): one GEMM
@@ -1188,6 +1218,10 @@ static Layout fwd_layout(const pvb2_conv2d_desc* d) {
   Layout l;
   l.a = l.b = l.c = l.total = 0;
   if (pointwise(d)) return l;
+  if (strided_pointwise(d)) {
+    l.total = l.c = align256(sampled_bytes(d));  // xs
+    return l;
+  }
   if (use_im2col(d)) {
     const int Kc = im2col_channels(d);
     l.b = align256((size_t)d->N * d->P * d->Q * Kc * 4);
@@ -1209,6 +1243,10 @@ static Layout dgrad_layout(const pvb2_conv2d_desc* d) {
   Layout l;
   l.a = l.b = l.c = l.total = 0;
   if (pointwise(d)) return l;
+  if (strided_pointwise(d)) {
+    l.total = l.c = align256(sampled_bytes(d));  // dX on the sampled pixels
+    return l;
+  }
   const int Kp = round4(d->K);
   l.b = align256((size_t)d->N * d->P * d->Q * Kp * 4);
   l.total = l.b + align256((size_t)d->C * d->R * d->S * Kp * 4);  // one phase's packed weights at a time
@@ -1237,6 +1275,13 @@ static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
     WgPlan p = plan_pw_wg(d->N, d->K, d->C, (int64_t)d->H * d->W);
     if (plan) *plan = p;
     l.total = align256(wg_partial_bytes(d->K, d->C, p.splits));  // partials only
+    return l;
+  }
+  if (strided_pointwise(d)) {
+    WgPlan p = plan_pw_wg(d->N, d->K, d->C, (int64_t)d->P * d->Q);
+    if (plan) *plan = p;
+    l.c = align256(sampled_bytes(d));  // xs, then partials
+    l.total = l.c + align256(wg_partial_bytes(d->K, d->C, p.splits));
     return l;
   }
   if (use_im2col(d)) {
@@ -1279,6 +1324,14 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
   }
   Layout l = fwd_layout(d);
   if (!ws || ws_bytes < l.total) return PVB2_OK;  // not enough scratch: exact path
+  if (strided_pointwise(d)) {
+    if (!aligned16(w) || !aligned16(y)) return PVB2_OK;
+    float* xs = (float*)ws;
+    PVB2_TRY(subsample(d, x, xs, s));
+    PVB2_TRY(run_pointwise(xs, w, b, y, d->N, d->C, d->K, pq, false, s));
+    *handled = true;
+    return PVB2_OK;
+  }
   float* act = (float*)((char*)ws + l.a);
   float* wp = (float*)((char*)ws + l.b);
   if (use_im2col(d)) {
@@ -1325,6 +1378,17 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
   }
   Layout l = dgrad_layout(d);
   if (!ws || ws_bytes < l.total) return PVB2_OK;
+  if (strided_pointwise(d)) {
+    if (!aligned16(dy) || !aligned16(w) || !aligned16(dx)) return PVB2_OK;
+    float* t = (float*)ws;
+    PVB2_TRY(run_pointwise(dy, w, nullptr, t, d->N, d->C, d->K, (int64_t)d->P * d->Q, true, s));
+    const int64_t total4 = (int64_t)d->N * d->C * d->H * d->W / 4;
+    scatter_strided_kernel<<<grid_for(total4, 256), 256, 0, s>>>(t, dx, (int)total4, d->H, d->W, d->P, d->Q,
+                                                                  d->stride_h, d->stride_w);
+    PVB2_LAUNCH_CHECK();
+    *handled = true;
+    return PVB2_OK;
+  }
   const int Kp = round4(d->K);
   float* dyn = (float*)((char*)ws + l.a);
   float* wd = (float*)((char*)ws + l.b);
@@ -1404,6 +1468,16 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
     float* part = (float*)ws;
     PVB2_TRY(run_pw_wgrad(dy, x, d->N, d->C, d->K, (int64_t)d->H * d->W, p, part, s));
     // partials [sp][c][k] -> dW[k][c]
+    PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->K, d->C, d->K, d->C, dw, d->C, 1, 0, s));
+    *handled = true;
+    return PVB2_OK;
+  }
+  if (strided_pointwise(d)) {
+    if (!aligned16(dy)) return PVB2_OK;
+    float* xs = (float*)ws;
+    float* part = (float*)((char*)ws + l.c);
+    PVB2_TRY(subsample(d, x, xs, s));
+    PVB2_TRY(run_pw_wgrad(dy, xs, d->N, d->C, d->K, (int64_t)d->P * d->Q, p, part, s));
     PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->K, d->C, d->K, d->C, dw, d->C, 1, 0, s));
     *handled = true;
     return PVB2_OK;

@@ -84,6 +84,9 @@ CONV_SHAPES = [
     (2, 1024, 14, 14, 256, 1, 1, 1, 0, 1, 1),    # layer3 1x1 reduce
     (3, 512, 7, 7, 512, 3, 3, 1, 1, 1, 1),       # layer4 3x3: tiles span two images; split-K fwd / dgrad
     (2, 128, 14, 14, 256, 3, 3, 2, 1, 1, 1),     # strided, few tiles: split-K in every dgrad phase
+    (2, 256, 56, 56, 512, 1, 1, 2, 0, 1, 1),     # strided 1x1 projection: pointwise over sampled pixels
+    (3, 64, 15, 15, 128, 1, 1, 2, 0, 1, 1),      # strided 1x1 with 8 x 8 = 64 sampled pixels per image
+    (2, 64, 14, 14, 128, 1, 1, 2, 0, 1, 1),      # strided 1x1 with 49 sampled pixels: staged path
     (2, 32, 26, 26, 64, 3, 3, 1, 0, 1, 1),       # MNIST conv2
     # pointwise (1x1, stride 1) paths that read NCHW directly
     (4, 36, 12, 12, 40, 1, 1, 1, 0, 1, 1),       # channel tails, 144-pixel images (part-empty slots)
