@@ -97,21 +97,24 @@ struct ConvTcArgs {
   const float* bias;
 };
 
-// Ring depth: as many stages as fit in 192 KB, a multiple of the producer
-// count so each stage always belongs to the same producer (8 at BN = 64,
-// 4 at 128 and 256).
+// Ring depth: as many stages as fit in 192 KB (8 at BN = 64, 6 at 128, 4 at
+// 256).  Iteration i goes to stage i % STAGES and producer i % 4, so with 6
+// stages a stage passes between producers; that is safe because every
+// producer waits for the stage's previous use to be consumed (empty barrier)
+// and the MMA consumes the ring in order, so no waiter is ever more than one
+// phase ahead of a barrier.
 template <int BN>
 struct ConvSmem {
   static constexpr int A_BYTES = cBM * cBK * 4;
   static constexpr int B_BYTES = BN * cBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES / cProducers * cProducers;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;  // 4 epilogue warps x 2 boxes of 32 x 32 fp32
   static constexpr int EPI_BYTES = 4 * 2 * 32 * 32 * 4;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16;
 };
-static_assert(ConvSmem<128>::STAGES % cProducers == 0 && ConvSmem<64>::TOTAL + 1024 <= 232448 && ConvSmem<128>::TOTAL + 1024 <= 232448 &&
+static_assert(ConvSmem<256>::STAGES >= cProducers && ConvSmem<64>::TOTAL + 1024 <= 232448 && ConvSmem<128>::TOTAL + 1024 <= 232448 &&
                   ConvSmem<256>::TOTAL + 1024 <= 232448,
               "conv tile does not fit in shared memory");
 

@@ -46,15 +46,18 @@ struct GemmEpi {
 
 enum { kStoreScalar = 0, kStoreRows = 1, kStoreCols = 2 };
 
-// Ring depth: as many stages as fit in 192 KB, a multiple of the producer
-// count so each stage always belongs to the same producer (8 at BN = 64,
-// 4 at 128 and 256).
+// Ring depth: as many stages as fit in 192 KB (8 at BN = 64, 6 at 128, 4 at
+// 256).  Iteration i goes to stage i % STAGES and producer i % 4, so with 6
+// stages a stage passes between producers; that is safe because every
+// producer waits for the stage's previous use to be consumed (empty barrier)
+// and the MMA consumes the ring in order, so no waiter is ever more than one
+// phase ahead of a barrier.
 template <int BN>
 struct GemmSmem {
   static constexpr int A_BYTES = kBM * kBK * 4;
   static constexpr int B_BYTES = BN * kBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES / kProducers * kProducers;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;  // 2 x 4 KB store boxes per epilogue warp
   static constexpr int BAR_OFF = EPI_OFF + 4 * 2 * 4096;
   // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], tmem slot, abort
