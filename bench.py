@@ -34,6 +34,11 @@ sys.path.insert(0, HERE)
 
 MODEL = "resnet50"
 GFLOP_PER_IMAGE = 24.30  # fwd+bwd conv/linear 2*MAC, torch.utils.flop_counter
+# DRAM bytes of one ResNet-50 step's convolution launches per image: 3.18 GB
+# read + 0.025 GB written over the 170 conv_tf32_kernel launches of a batch-16
+# step under ncu (cold L2 per launch), divided by 16 images
+# (profiles/conv_tf32_kernel_resnet50_b16.md)
+CONV_DRAM_BYTES_PER_IMAGE = 3.204e9 / 16
 
 
 def parse():
@@ -299,7 +304,9 @@ def run_ours(a):
                 "achieved": round(achieved, 2), "peak": round(tf32_peak, 1), "unit": "TFLOP/s",
                 "frac": round(achieved / tf32_peak, 4),
                 "peak_note": "TF32 dense = 1/2 of measured bf16 (MEASURED_PEAKS.json)" if peaks else "fallback",
-                "traffic": None, "conv_ms_per_step": round(conv_ms, 3), "conv_launch_groups": n_conv,
+                "traffic": (round(CONV_DRAM_BYTES_PER_IMAGE * a.batch) if a.model == MODEL else None),
+                "traffic_unit": "bytes per step (all convolution launches; ncu, cold L2, batch 16 scaled)",
+                "conv_ms_per_step": round(conv_ms, 3), "conv_launch_groups": n_conv,
                 "conv_gflop_per_step": round(conv_flops / 1e9, 1),
                 "top_ops_ms": dict(sorted(per_op.items(), key=lambda kv: -kv[1])[:8])}
 
