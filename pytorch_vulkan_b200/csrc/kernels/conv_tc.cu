@@ -542,7 +542,7 @@ __global__ void pack_w_phase_kernel(const float* __restrict__ w, float* __restri
 // (W's own flattening; 0 outside the image and for j >= C*R*S up to Kc).
 // grid (P, N): one output row per CTA; each thread gathers four columns and
 // writes them as one 16-byte store, consecutive threads consecutive stores.
-constexpr int kIm2colMaxK = 256;
+constexpr int kIm2colMaxK = 1024;
 __global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ x, float* __restrict__ xcol, int C,
                                                      int H, int W, int P, int Q, int R, int S, int Kc, int sh, int sw,
                                                      int ph, int pw, int dh, int dw) {
@@ -643,11 +643,13 @@ static void pixel_block(int P, int Q, int pixels, int& bw, int& bh, int& bni) {
 
 static bool tc_conv_enabled() { return getenv("PVB2_DISABLE_TC") == nullptr; }
 
+// implicit launches step their TMA boxes by the stride: bw * stride <= 256
+static bool stride_ok_for_boxes(const pvb2_conv2d_desc* d) { return d->stride_w <= 4 && d->stride_h <= 4; }
+
 static bool tc_conv_shape_ok(const pvb2_conv2d_desc* d) {
   if (d->groups != 1 || d->math != PVB2_MATH_TF32 || !tc_conv_enabled()) return false;
   const double macs = (double)d->N * d->P * d->Q * d->K * d->C * d->R * d->S;
   if (macs < (double)(1 << 19)) return false;
-  if (d->stride_w > 4 || d->stride_h > 4) return false;  // TMA boxes: bw*stride <= 256
   if (d->R > kMaxTaps || d->S > kMaxTaps) return false;
   if (d->K < 8) return false;
   return true;
@@ -1349,6 +1351,7 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
     PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, Kc, d->P, d->Q, d->K, t, d->P, d->Q, 1, 1, 0, (int64_t)d->K * pq, pq,
                           d->Q, 1, nullptr, 0, s));
   } else {
+    if (!stride_ok_for_boxes(d)) return PVB2_OK;
     const int Cp = round4(d->C);
     PVB2_TRY(to_nhwc(x, act, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
     const int64_t wn = (int64_t)d->K * d->R * d->S * Cp;
@@ -1381,6 +1384,7 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
   }
   Layout l = dgrad_layout(d);
   if (!ws || ws_bytes < l.total) return PVB2_OK;
+  if (!strided_pointwise(d) && !stride_ok_for_boxes(d)) return PVB2_OK;
   if (strided_pointwise(d)) {
     if (!aligned16(dy) || !aligned16(w) || !aligned16(dx)) return PVB2_OK;
     float* t = (float*)ws;
@@ -1496,6 +1500,7 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
     *handled = true;
     return PVB2_OK;
   }
+  if (!stride_ok_for_boxes(d)) return PVB2_OK;
   const int Kp = round4(d->K);
   float* xn = (float*)((char*)ws + l.a);
   float* dyn = (float*)((char*)ws + l.b);

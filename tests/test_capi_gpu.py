@@ -97,6 +97,7 @@ CONV_SHAPES = [
     (2, 1, 28, 28, 32, 5, 5, 1, 0, 1, 1),        # MNIST conv1
     (3, 3, 30, 30, 24, 3, 3, 1, 1, 2, 1),        # dilated
     (2, 4, 40, 40, 20, 5, 5, 2, 2, 1, 1),        # strided, 100 columns, output-channel tail
+    (2, 3, 224, 224, 768, 16, 16, 16, 0, 1, 1),  # ViT-B/16 patch embedding: 768 columns, stride 16
     # epilogue store boxes
     (4, 64, 14, 14, 100, 3, 3, 1, 1, 1, 1),      # 14-wide rows stored as whole-row runs; output-channel tail
     (2, 16, 112, 112, 24, 3, 3, 1, 1, 1, 1),     # two 64-wide pixel blocks per row
