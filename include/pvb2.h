@@ -235,6 +235,18 @@ PVB2_API int pvb2_batch_norm_fwd_train(const pvb2_tensor* x, const float* gamma,
                               float* running_mean, float* running_var, double momentum, double eps,
                               const pvb2_tensor* y, float* save_mean, float* save_invstd,
                               void* workspace, size_t workspace_bytes, pvb2_stream stream);
+/* Training backward below a ReLU: grad_above is the gradient of the ReLU's
+ * output relu_out; the gradient of the batch-norm output,
+ *     dy = relu_out <= 0 ? 0 : grad_above     (threshold_backward),
+ * is formed in the first pass, stored to dy, and the backward proceeds as
+ * pvb2_batch_norm_bwd (train) would on it.  One pass fewer than
+ * threshold_backward followed by pvb2_batch_norm_bwd (norm_ops.cpp:87-164,
+ * pointwise_ops.cpp:437-455).  Needs pvb2_batch_norm_fwd_split_ok(x). */
+PVB2_API int pvb2_batch_norm_bwd_relu(const pvb2_tensor* grad_above, const pvb2_tensor* relu_out,
+                                      const pvb2_tensor* x, const float* gamma, const float* mean,
+                                      const float* invstd, const pvb2_tensor* dy, const pvb2_tensor* dx,
+                                      float* dgamma, float* dbeta, void* workspace, size_t workspace_bytes,
+                                      pvb2_stream stream);
 /* Training forward in two calls, so that a host can fuse what follows the
  * normalisation into the second pass: pvb2_batch_norm_fwd_stats writes the
  * per-CTA partial sums of x into the workspace; pvb2_batch_norm_fwd_apply

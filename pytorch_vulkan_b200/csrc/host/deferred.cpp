@@ -1,4 +1,4 @@
-// Deferred batch-norm epilogue.
+// Deferred batch-norm epilogue (forward) and ReLU gradient (backward).
 //
 // ResNet-style blocks run `y = bn(x); y += identity; y = relu(y)` as three
 // ops, each a full pass over the activation (the reference did the same:
@@ -10,8 +10,13 @@
 // that touches the device first launches what is pending: every op entry
 // (DeviceScope, ExecGuard), stream and event calls, synchronisation.  The
 // pending state holds references to every tensor the pass reads or writes,
-// so none of them can be freed or reused before it runs.  B200_DEFER_BN=0
-// turns the deferral off.
+// so none of them can be freed or reused before it runs.
+//
+// Backward, the mirror image: threshold_backward (the ReLU gradient) is left
+// pending, and when the next op is the backward of the batch norm that fed
+// that ReLU, its first pass forms the gradient from the ReLU output on the
+// fly (pvb2_batch_norm_bwd_relu), still storing it to the op's output tensor.
+// B200_DEFER_BN=0 turns both deferrals off.
 #include <cstdlib>
 #include <mutex>
 #include <optional>
@@ -32,8 +37,15 @@ struct PendingBn {
   bool relu = false;
 };
 
+struct PendingThr {  // grad_input = self <= 0 ? 0 : grad
+  at::Tensor grad, self, out;
+  pvb2_stream stream = nullptr;
+  int device = 0;
+};
+
 std::mutex g_mutex;
 std::optional<PendingBn> g_pending;
+std::optional<PendingThr> g_thr;
 std::atomic<bool> g_any{false};
 thread_local bool t_flushing = false;
 
@@ -59,10 +71,18 @@ void launch(PendingBn& p, const char* name) {
                                       p.stream));
 }
 
-std::optional<PendingBn> take() {
+void launch_thr(PendingThr& t) {
+  DeviceScope scope(t.device);
+  OCL_OP("threshold_backward", t.device);
+  const pvb2_tensor od = desc(t.out), gd = desc(t.grad), sd = desc(t.self);
+  OCL_CHECK(pvb2_binary(PVB2_BIN_THRESHOLD_BWD, &od, &gd, &sd, 0.0, 0.0, PVB2_F32, t.stream));
+}
+
+std::pair<std::optional<PendingBn>, std::optional<PendingThr>> take() {
   std::lock_guard<std::mutex> g(g_mutex);
-  std::optional<PendingBn> p = std::move(g_pending);
+  std::pair<std::optional<PendingBn>, std::optional<PendingThr>> p{std::move(g_pending), std::move(g_thr)};
   g_pending.reset();
+  g_thr.reset();
   g_any.store(false, std::memory_order_release);
   return p;
 }
@@ -73,8 +93,9 @@ void flush_deferred() {
   if (!g_any.load(std::memory_order_acquire) || t_flushing) return;
   t_flushing = true;
   try {
-    std::optional<PendingBn> p = take();
-    if (p) launch(*p, p->residual.defined() ? "native_batch_norm+add_" : "native_batch_norm");
+    auto p = take();
+    if (p.first) launch(*p.first, p.first->residual.defined() ? "native_batch_norm+add_" : "native_batch_norm");
+    if (p.second) launch_thr(*p.second);
   } catch (...) {
     t_flushing = false;
     throw;
@@ -109,7 +130,7 @@ bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optiona
   for (;;) {
     flush_deferred();  // one pending pass at a time (another thread may have left one)
     std::lock_guard<std::mutex> g(g_mutex);
-    if (g_pending.has_value()) continue;
+    if (g_pending.has_value() || g_thr.has_value()) continue;
     g_pending = std::move(p);
     g_any.store(true, std::memory_order_release);
     return true;
@@ -146,6 +167,40 @@ bool fuse_deferred_relu(const at::Tensor& self) {
   }
   p->relu = true;
   launch(*p, p->residual.defined() ? "native_batch_norm+add_+relu_" : "native_batch_norm+relu_");
+  return true;
+}
+
+bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const at::Tensor& out) {
+  if (!defer_enabled()) return false;
+  for (const at::Tensor* t : {&grad, &self, &out})
+    if (!is_ocl(*t) || t->scalar_type() != at::kFloat || !t->is_contiguous() || !t->sizes().equals(out.sizes()))
+      return false;
+  if (grad.device() != out.device() || self.device() != out.device()) return false;
+  if (out.is_alias_of(self) || out.is_alias_of(grad) || out.numel() == 0) return false;
+  PendingThr t;
+  t.grad = grad;
+  t.self = self;
+  t.out = out;
+  t.device = (int)out.device().index();
+  t.stream = stream_for(t.device);
+  for (;;) {
+    flush_deferred();
+    std::lock_guard<std::mutex> g(g_mutex);
+    if (g_pending.has_value() || g_thr.has_value()) continue;
+    g_thr = std::move(t);
+    g_any.store(true, std::memory_order_release);
+    return true;
+  }
+}
+
+bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out) {
+  if (!g_any.load(std::memory_order_acquire)) return false;
+  std::lock_guard<std::mutex> g(g_mutex);
+  if (!g_thr || !same_tensor(grad_out, g_thr->out)) return false;
+  *grad_above = g_thr->grad;
+  *relu_out = g_thr->self;
+  g_thr.reset();
+  g_any.store(false, std::memory_order_release);
   return true;
 }
 

@@ -91,6 +91,12 @@ bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optiona
 bool fuse_deferred_add(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha);
 // true when `relu_(self)` was folded into the pending pass (and launched it)
 bool fuse_deferred_relu(const at::Tensor& self);
+// threshold_backward(grad, self, 0) into `out`, left pending (true) so that a
+// following batch-norm backward can form it in its first pass
+bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const at::Tensor& out);
+// when the pending threshold_backward wrote grad_out: hand over its inputs
+// (the batch-norm backward then stores grad_out itself) and clear it
+bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out);
 
 // ------------------------------------------------------------- settings
 int math_mode();                 // PVB2_MATH_* for convolution / GEMM

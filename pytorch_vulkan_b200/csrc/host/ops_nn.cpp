@@ -303,9 +303,17 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward
     const std::optional<at::Tensor>& save_mean, const std::optional<at::Tensor>& save_invstd, bool train, double eps,
     std::array<bool, 3> output_mask) {
   const int dev = input.device().index();
+  // grad_out still pending as ReLU's gradient: form it in the first pass
+  at::Tensor relu_grad, relu_out;
+  bool below_relu = false;
+  if (train && input.is_contiguous() && input.scalar_type() == at::kFloat && save_mean.has_value() &&
+      save_invstd.has_value()) {
+    const pvb2_tensor xd0 = desc(input);
+    below_relu = pvb2_batch_norm_fwd_split_ok(&xd0) && take_deferred_threshold(grad_out, &relu_grad, &relu_out);
+  }
   DeviceScope scope(dev);
-  OCL_OP("native_batch_norm_backward", dev);
-  at::Tensor x = contiguous(input), gy = contiguous(grad_out);
+  OCL_OP(below_relu ? "threshold_backward+native_batch_norm_backward" : "native_batch_norm_backward", dev);
+  at::Tensor x = contiguous(input), gy = below_relu ? grad_out : contiguous(grad_out);
   const int64_t C = x.size(1);
   const float* g = weight.has_value() && weight->defined() ? weight->data_ptr<float>() : nullptr;
   at::Tensor gx, gw, gb;
@@ -319,6 +327,14 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward
     pvb2_tensor gxd;
     if (output_mask[0]) gxd = desc(gx);
     Workspace ws(pvb2_batch_norm_workspace_size(&xd), dev);
+    if (below_relu) {
+      const pvb2_tensor rgd = desc(relu_grad), rod = desc(relu_out);
+      OCL_CHECK(pvb2_batch_norm_bwd_relu(&rgd, &rod, &xd, g, save_mean->data_ptr<float>(),
+                                         save_invstd->data_ptr<float>(), &gyd, output_mask[0] ? &gxd : nullptr,
+                                         output_mask[1] ? gw.data_ptr<float>() : nullptr,
+                                         output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, st));
+      return {gx, gw, gb};
+    }
     OCL_CHECK(pvb2_batch_norm_bwd(&gyd, &xd, g, save_mean->data_ptr<float>(), save_invstd->data_ptr<float>(), 1,
                                   output_mask[0] ? &gxd : nullptr, output_mask[1] ? gw.data_ptr<float>() : nullptr,
                                   output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, st));

@@ -138,6 +138,10 @@ COMPARE_OUT(ge, PVB2_BIN_GE)
 // threshold_backward, :437-455:  grad_input = self <= threshold ? 0 : grad
 static at::Tensor& threshold_backward_out(const at::Tensor& grad, const at::Tensor& self, const at::Scalar& threshold,
                                           at::Tensor& grad_input) {
+  // ReLU's gradient: left pending for a following batch-norm backward
+  if (!threshold.isComplex() && threshold.toDouble() == 0.0 && is_ocl(grad) && is_ocl(self) && is_ocl(grad_input) &&
+      grad_input.sizes().equals(grad.sizes()) && defer_threshold_bwd(grad, self, grad_input))
+    return grad_input;
   return binary_out(PVB2_BIN_THRESHOLD_BWD, grad, self, grad_input, sc(threshold), 0, arith_compute(grad_input),
                     "threshold_backward");
 }

@@ -518,13 +518,19 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
 
 __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
     const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean, int N, int C, int HW,
-    int chunk, int splits, int vec, float* __restrict__ part) {
+    int chunk, int splits, int vec, float* __restrict__ part, const float* __restrict__ relu_y,
+    float* __restrict__ dy_out) {
+  // with relu_y: `dy` is the gradient above a ReLU whose output is relu_y;
+  // the gradient below it, (relu_y <= 0 ? 0 : dy) as threshold_backward
+  // computes it, is formed here, stored to dy_out and used for the sums
   __shared__ float red[64];
   const int s = blockIdx.x, c = blockIdx.y;
   const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
   const int64_t nstride = (int64_t)C * HW;
   const float* gc = dy + (int64_t)c * HW;
   const float* xc = x + (int64_t)c * HW;
+  const float* yc = relu_y ? relu_y + (int64_t)c * HW : nullptr;
+  float* oc = relu_y ? dy_out + (int64_t)c * HW : nullptr;
   const float m = mean[c];
   float sg = 0.f, sd = 0.f;
   const int vw = vec ? 4 : 1, step = vw * blockDim.x;
@@ -534,8 +540,16 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
     if (vec) {
       for (; e < end; e += step, w.next()) {
         const int64_t o = w.n * nstride + w.i;
-        const float4 g = __ldg(reinterpret_cast<const float4*>(gc + o));
+        float4 g = __ldg(reinterpret_cast<const float4*>(gc + o));
         const float4 v = __ldg(reinterpret_cast<const float4*>(xc + o));
+        if (yc) {
+          const float4 r = __ldg(reinterpret_cast<const float4*>(yc + o));
+          g.x = r.x <= 0.f ? 0.f : g.x;
+          g.y = r.y <= 0.f ? 0.f : g.y;
+          g.z = r.z <= 0.f ? 0.f : g.z;
+          g.w = r.w <= 0.f ? 0.f : g.w;
+          *reinterpret_cast<float4*>(oc + o) = g;
+        }
         sg += (g.x + g.y) + (g.z + g.w);
         sd += (g.x * (v.x - m) + g.y * (v.y - m)) + (g.z * (v.z - m) + g.w * (v.w - m));
       }
@@ -550,6 +564,10 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
           if (e + u * step < end) {
             g[u] = __ldg(gc + o);
             v[u] = __ldg(xc + o);
+            if (yc) {
+              g[u] = __ldg(yc + o) <= 0.f ? 0.f : g[u];
+              oc[o] = g[u];
+            }
           }
           w.next();
         }
@@ -651,11 +669,12 @@ static int bn_fwd_stream(const BnGeom& g, const BnStream& p, const float* x, flo
 
 static int bn_bwd_stream(const BnGeom& g, const BnStream& p, const float* dy, const float* x, const float* mean,
                          const float* invstd, const float* gamma, float* dx, float* dgamma, float* dbeta, float* part,
-                         cudaStream_t s) {
+                         cudaStream_t s, const float* relu_y = nullptr, float* dy_out = nullptr) {
   const dim3 grid((unsigned)p.splits, (unsigned)g.C);
   bn_st_bwd_reduce_kernel<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, (int)g.N, (int)g.C, (int)g.HW, p.chunk,
-                                                         p.splits, p.vec ? 1 : 0, part);
+                                                         p.splits, p.vec ? 1 : 0, part, relu_y, dy_out);
   PVB2_LAUNCH_CHECK();
+  if (relu_y) dy = dy_out;  // the apply pass reads the gradient below the ReLU
   bn_st_bwd_apply_kernel<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, invstd, gamma, (int)g.N, (int)g.C, (int)g.HW,
                                                         p.chunk, p.splits, p.vec ? 1 : 0, part, dx, dgamma, dbeta);
   PVB2_LAUNCH_CHECK();
@@ -1044,6 +1063,26 @@ int pvb2_batch_norm_bwd(const pvb2_tensor* dy, const pvb2_tensor* x, const float
       dx ? (float*)dx->data : nullptr, dgamma, dbeta);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
+}
+
+int pvb2_batch_norm_bwd_relu(const pvb2_tensor* grad_above, const pvb2_tensor* relu_out, const pvb2_tensor* x,
+                             const float* gamma, const float* mean, const float* invstd, const pvb2_tensor* dy,
+                             const pvb2_tensor* dx, float* dgamma, float* dbeta, void* workspace,
+                             size_t workspace_bytes, pvb2_stream stream) {
+  PVB2_TRY(check_bn_x(x));
+  for (const pvb2_tensor* t : {grad_above, relu_out, dy}) {
+    PVB2_CHECK_ARG(t && is_contiguous(t) && t->dtype == PVB2_F32 && numel(t) == numel(x),
+                   "batch_norm_backward_relu: gradients and ReLU output must be contiguous float32 like x");
+  }
+  PVB2_CHECK_ARG(pvb2_batch_norm_fwd_split_ok(x), "batch_norm_backward_relu: input not supported");
+  const BnGeom g = bn_geom(x);
+  const void* ptrs[5] = {grad_above->data, relu_out->data, x->data, dy->data, dx ? dx->data : nullptr};
+  const BnStream p = bn_stream_plan(g, ptrs, 5);
+  const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
+  PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm_backward: workspace too small");
+  return bn_bwd_stream(g, p, (const float*)grad_above->data, (const float*)x->data, mean, invstd, gamma,
+                       dx ? (float*)dx->data : nullptr, dgamma, dbeta, (float*)workspace, as_stream(stream),
+                       (const float*)relu_out->data, (float*)dy->data);
 }
 
 int pvb2_batch_norm_bwd_eval(const pvb2_tensor* dy, const float* gamma, const float* running_var, double eps,

@@ -149,3 +149,24 @@ def test_bottleneck_forward_backward(ocl):
             assert _close(p.grad, q.grad, 1e-4), n
     finally:
         torch.ocl.set_math_mode(old)
+
+
+def test_relu_grad_into_bn_backward(ocl):
+    """threshold_backward left pending and formed inside the batch-norm
+    backward; and the same when the batch-norm output also has a second
+    consumer (its gradient is then a sum, and the pending op runs alone)."""
+    for second_use in (False, True):
+        cpu, dev = _bn_pair(24, 30 + second_use)
+        x = _x((4, 24, 10, 10), 31)
+        g1, g2 = _x((4, 24, 10, 10), 32), _x((4, 24, 10, 10), 33)
+        grads = []
+        for m, d in ((cpu, "cpu"), (dev, DEV)):
+            xx = x.detach().clone().to(d).requires_grad_()
+            y = m(xx)
+            loss = (torch.relu(y) * g1.to(d)).sum()
+            if second_use:
+                loss = loss + (y * g2.to(d)).sum()
+            loss.backward()
+            grads.append((xx.grad, m.weight.grad, m.bias.grad))
+        for a, b in zip(*grads):
+            assert _close(a, b, 1e-4)
