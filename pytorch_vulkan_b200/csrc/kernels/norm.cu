@@ -826,6 +826,146 @@ __global__ void ln_bwd_param_final_kernel(const float* __restrict__ part, int sp
   if (dbeta) dbeta[j] = b;
 }
 
+// ---- rows of N = 128 * NC floats (N <= 1024, 16-byte aligned): a warp per
+// row, lane l owning the float4 columns 4 l + 128 k (k < NC), the row held in
+// registers
+template <int NC>
+__global__ void __launch_bounds__(256) ln_fwd_v4_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta, int64_t M, float eps,
+                                                        float* __restrict__ y, float* __restrict__ mean_out,
+                                                        float* __restrict__ rstd_out) {
+  constexpr int N = 128 * NC;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * N);
+  float4 v[NC];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    v[k] = __ldg(xr + lane + 32 * k);
+    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / (float)N;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = 1.f / sqrtf(q / (float)N + eps);
+  float4* yr = reinterpret_cast<float4*>(y + row * N);
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    float4 o = make_float4((v[k].x - mean) * rstd, (v[k].y - mean) * rstd, (v[k].z - mean) * rstd,
+                           (v[k].w - mean) * rstd);
+    if (gamma) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + lane + 32 * k);
+      o = make_float4(o.x * g.x, o.y * g.y, o.z * g.z, o.w * g.w);
+    }
+    if (beta) {
+      const float4 b = __ldg(reinterpret_cast<const float4*>(beta) + lane + 32 * k);
+      o = make_float4(o.x + b.x, o.y + b.y, o.z + b.z, o.w + b.w);
+    }
+    yr[lane + 32 * k] = o;
+  }
+  if (lane == 0) {
+    if (mean_out) mean_out[row] = mean;
+    if (rstd_out) rstd_out[row] = rstd;
+  }
+}
+
+// Backward for such rows: CTA b (8 warps) takes rows [b R, (b + 1) R), a warp
+// per row; dx = rstd (g - mean(g) - xhat mean(g xhat)) with g = dy gamma, and
+// each lane accumulates its columns' dy xhat and dy over the CTA's rows; the
+// eight warps' sums are added in warp order into part[b][0 | 1][N]
+// (gamma, beta), which ln_bwd_param_final_kernel sums over CTAs in order.
+template <int NC>
+__global__ void __launch_bounds__(256, NC <= 6 ? 2 : 1) ln_bwd_v4_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                                           const float* __restrict__ mean,
+                                                           const float* __restrict__ rstd,
+                                                           const float* __restrict__ gamma, int64_t M, int R,
+                                                           float* __restrict__ dx, float* __restrict__ part) {
+  constexpr int N = 128 * NC;
+  __shared__ float4 acc[2][32 * NC];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  float4 dg[NC], db[NC];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) dg[k] = db[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int64_t r0 = (int64_t)blockIdx.x * R, r1 = min(M, r0 + R);
+  for (int64_t row = r0 + warp; row < r1; row += 8) {
+    const float4* gr = reinterpret_cast<const float4*>(dy + row * N);
+    const float4* xr = reinterpret_cast<const float4*>(x + row * N);
+    const float m = __ldg(mean + row), r = __ldg(rstd + row);
+    float4 d[NC], v[NC];  // v becomes xhat
+    float sg = 0.f, sgx = 0.f;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+      d[k] = __ldg(gr + lane + 32 * k);
+      v[k] = __ldg(xr + lane + 32 * k);
+      v[k] = make_float4((v[k].x - m) * r, (v[k].y - m) * r, (v[k].z - m) * r, (v[k].w - m) * r);
+      dg[k] = make_float4(fmaf(d[k].x, v[k].x, dg[k].x), fmaf(d[k].y, v[k].y, dg[k].y),
+                          fmaf(d[k].z, v[k].z, dg[k].z), fmaf(d[k].w, v[k].w, dg[k].w));
+      db[k] = make_float4(db[k].x + d[k].x, db[k].y + d[k].y, db[k].z + d[k].z, db[k].w + d[k].w);
+      const float4 gm = gamma ? __ldg(g4 + lane + 32 * k) : make_float4(1.f, 1.f, 1.f, 1.f);
+      d[k] = make_float4(d[k].x * gm.x, d[k].y * gm.y, d[k].z * gm.z, d[k].w * gm.w);  // d becomes g
+      sg += (d[k].x + d[k].y) + (d[k].z + d[k].w);
+      sgx += (d[k].x * v[k].x + d[k].y * v[k].y) + (d[k].z * v[k].z + d[k].w * v[k].w);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      sg += __shfl_xor_sync(0xffffffffu, sg, o);
+      sgx += __shfl_xor_sync(0xffffffffu, sgx, o);
+    }
+    if (dx) {
+      const float a = sg / (float)N, b = sgx / (float)N;
+      float4* o = reinterpret_cast<float4*>(dx + row * N);
+#pragma unroll
+      for (int k = 0; k < NC; ++k)
+        o[lane + 32 * k] = make_float4(r * (d[k].x - a - v[k].x * b), r * (d[k].y - a - v[k].y * b),
+                                       r * (d[k].z - a - v[k].z * b), r * (d[k].w - a - v[k].w * b));
+    }
+  }
+  if (!part) return;
+  for (int w = 0; w < 8; ++w) {
+    if (warp == w) {
+#pragma unroll
+      for (int k = 0; k < NC; ++k) {
+        float4& a = acc[0][lane + 32 * k];
+        float4& b = acc[1][lane + 32 * k];
+        if (w == 0) {
+          a = dg[k];
+          b = db[k];
+        } else {
+          a = make_float4(a.x + dg[k].x, a.y + dg[k].y, a.z + dg[k].z, a.w + dg[k].w);
+          b = make_float4(b.x + db[k].x, b.y + db[k].y, b.z + db[k].z, b.w + db[k].w);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  float4* pg = reinterpret_cast<float4*>(part + ((int64_t)blockIdx.x * 2) * N);
+  for (int i = threadIdx.x; i < 32 * NC; i += blockDim.x) {
+    pg[i] = acc[0][i];
+    pg[32 * NC + i] = acc[1][i];
+  }
+}
+
+// rows per CTA of ln_bwd_v4_kernel: about two CTAs per SM, a multiple of 8
+static int ln_bwd_rows(int64_t M) {
+  int64_t r = (M + 2 * num_sms() - 1) / (2 * num_sms());
+  r = (r + 7) / 8 * 8;
+  return (int)std::max<int64_t>(r, 8);
+}
+static bool ln_vec_ok(int64_t N, std::initializer_list<const void*> ptrs) {
+  if (N % 128 != 0 || N > 1024) return false;
+  for (const void* p : ptrs)
+    if (p && ((uintptr_t)p & 15)) return false;
+  return true;
+}
+
 static int ln_splits(int64_t M) {
   int64_t s = (M + 63) / 64;
   if (s > 256) s = 256;
@@ -1102,7 +1242,15 @@ int pvb2_layer_norm_fwd(const float* x, const float* gamma, const float* beta, i
   if (M == 0) return PVB2_OK;
   PVB2_CHECK_ARG(N > 0, "layer_norm: N must be positive");
   cudaStream_t s = as_stream(stream);
-  if (N <= 32 * kLnMaxPerLane) {
+  if (ln_vec_ok(N, {x, gamma, beta, y})) {
+    const unsigned grid = (unsigned)((M + 7) / 8);
+    switch (N / 128) {
+#define LN_FWD(NC) \
+  case NC: ln_fwd_v4_kernel<NC><<<grid, 256, 0, s>>>(x, gamma, beta, M, (float)eps, y, mean, rstd); break;
+      LN_FWD(1) LN_FWD(2) LN_FWD(3) LN_FWD(4) LN_FWD(5) LN_FWD(6) LN_FWD(7) LN_FWD(8)
+#undef LN_FWD
+    }
+  } else if (N <= 32 * kLnMaxPerLane) {
     const int warps = 8;
     ln_fwd_kernel<<<(unsigned)((M + warps - 1) / warps), warps * 32, 0, s>>>(x, gamma, beta, M, N, (float)eps, y,
                                                                             mean, rstd);
@@ -1114,7 +1262,8 @@ int pvb2_layer_norm_fwd(const float* x, const float* gamma, const float* beta, i
 }
 
 size_t pvb2_layer_norm_bwd_workspace_size(int64_t M, int64_t N) {
-  return (size_t)ln_splits(M) * 2 * (size_t)N * sizeof(float);
+  const int64_t ctas = (M + ln_bwd_rows(M) - 1) / ln_bwd_rows(M);
+  return (size_t)std::max<int64_t>(ln_splits(M), ctas) * 2 * (size_t)N * sizeof(float);
 }
 
 int pvb2_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
@@ -1124,6 +1273,26 @@ int pvb2_layer_norm_bwd(const float* dy, const float* x, const float* mean, cons
   if (M == 0) {
     if (dgamma) PVB2_CUDA_TRY(cudaMemsetAsync(dgamma, 0, N * sizeof(float), s));
     if (dbeta) PVB2_CUDA_TRY(cudaMemsetAsync(dbeta, 0, N * sizeof(float), s));
+    return PVB2_OK;
+  }
+  if (ln_vec_ok(N, {dy, x, gamma, dx, workspace}) && M < ((int64_t)1 << 31)) {
+    const int R = ln_bwd_rows(M);
+    const int64_t ctas = (M + R - 1) / R;
+    const bool params = dgamma || dbeta;
+    PVB2_CHECK_ARG(!params || (workspace && workspace_bytes >= (size_t)ctas * 2 * N * sizeof(float)),
+                   "layer_norm_backward: workspace too small");
+    float* part = params ? (float*)workspace : nullptr;
+    switch (N / 128) {
+#define LN_BWD(NC) \
+  case NC: ln_bwd_v4_kernel<NC><<<(unsigned)ctas, 256, 0, s>>>(dy, x, mean, rstd, gamma, M, R, dx, part); break;
+      LN_BWD(1) LN_BWD(2) LN_BWD(3) LN_BWD(4) LN_BWD(5) LN_BWD(6) LN_BWD(7) LN_BWD(8)
+#undef LN_BWD
+    }
+    PVB2_LAUNCH_CHECK();
+    if (params) {
+      ln_bwd_param_final_kernel<<<(unsigned)((N + 255) / 256), 256, 0, s>>>(part, (int)ctas, N, dgamma, dbeta);
+      PVB2_LAUNCH_CHECK();
+    }
     return PVB2_OK;
   }
   if (dx) {

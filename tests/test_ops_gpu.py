@@ -635,3 +635,30 @@ def test_row_binary(ocl, name, sa, sb, call):
     ref = call(a, b)
     got = call(a.to(DEV), b.to(DEV)).cpu()
     assert _diff(ref, got) <= 1e-6 * max(1.0, ref.abs().max().item())
+
+
+# layer norm over rows of 128 * k floats (vectorised kernels, fused parameter
+# gradients) and other widths (per-element kernels), against float64
+@pytest.mark.parametrize("rows,n,affine", [(6304, 768, True), (100, 1024, True), (37, 128, False), (513, 256, True),
+                                           (50, 100, True), (8, 2048, True)])
+def test_layer_norm_rows(ocl, rows, n, affine):
+    g = _gen(40)
+    x = torch.randn(rows, n, generator=g) * 3 + 1
+    gy = torch.randn(rows, n, generator=g)
+    ln = nn.LayerNorm(n, elementwise_affine=affine)
+    if affine:
+        with torch.no_grad():
+            ln.weight.copy_(torch.randn(n, generator=g))
+            ln.bias.copy_(torch.randn(n, generator=g))
+    ref = nn.LayerNorm(n, elementwise_affine=affine).double()
+    ref.load_state_dict(ln.state_dict())
+    dev = ln.to(DEV)
+    xr, xd = x.double().requires_grad_(), x.to(DEV).requires_grad_()
+    yr, yd = ref(xr), dev(xd)
+    yr.backward(gy.double())
+    yd.backward(gy.to(DEV))
+    assert _diff(yr, yd) <= 1e-5 * max(1.0, yr.abs().max().item())
+    assert _diff(xr.grad, xd.grad) <= 1e-4 * max(1.0, xr.grad.abs().max().item())
+    if affine:
+        for pr, pd in ((ref.weight, dev.weight), (ref.bias, dev.bias)):
+            assert _diff(pr.grad, pd.grad) <= 1e-5 * max(1.0, pr.grad.abs().sum().item() / n)
