@@ -643,14 +643,16 @@ static void pixel_block(int P, int Q, int pixels, int& bw, int& bh, int& bni) {
 
 static bool tc_conv_enabled() { return getenv("PVB2_DISABLE_TC") == nullptr; }
 
-// implicit launches step their TMA boxes by the stride: bw * stride <= 256
-static bool stride_ok_for_boxes(const pvb2_conv2d_desc* d) { return d->stride_w <= 4 && d->stride_h <= 4; }
+// implicit launches step their TMA boxes by the stride (bw * stride <= 256)
+// and keep the filter taps of a row / column in fixed arrays
+static bool stride_ok_for_boxes(const pvb2_conv2d_desc* d) {
+  return d->stride_w <= 4 && d->stride_h <= 4 && d->R <= kMaxTaps && d->S <= kMaxTaps;
+}
 
 static bool tc_conv_shape_ok(const pvb2_conv2d_desc* d) {
   if (d->groups != 1 || d->math != PVB2_MATH_TF32 || !tc_conv_enabled()) return false;
   const double macs = (double)d->N * d->P * d->Q * d->K * d->C * d->R * d->S;
   if (macs < (double)(1 << 19)) return false;
-  if (d->R > kMaxTaps || d->S > kMaxTaps) return false;
   if (d->K < 8) return false;
   return true;
 }

@@ -350,21 +350,25 @@ __global__ void binary_generic_kernel(IterShape it, int op, void* out, int odt, 
 // and unit or zero stride in each input (a transposed-batch residual add, a
 // row broadcast): rows of `len` elements, a group of G lanes per row, row
 // offsets from the outer dims computed once per row.
-__global__ void __launch_bounds__(256) binary_f32_rows_kernel(IterShape outer, int64_t rows, int64_t len, int group,
-                                                              int op, float* __restrict__ out,
-                                                              const float* __restrict__ a, int a_unit,
-                                                              const float* __restrict__ b, int b_unit, float p0,
-                                                              float p1) {
+// A long row is cut into pieces of `piece` elements (a group per piece) so
+// that few-row shapes (a [B, L*C] broadcast add) still fill the GPU.
+__global__ void __launch_bounds__(256) binary_f32_rows_kernel(IterShape outer, int64_t rows, int64_t len,
+                                                              int64_t piece, int group, int op,
+                                                              float* __restrict__ out, const float* __restrict__ a,
+                                                              int a_unit, const float* __restrict__ b, int b_unit,
+                                                              float p0, float p1) {
   const int lane = threadIdx.x % group;
+  const int64_t pieces = (len + piece - 1) / piece;
   const int64_t g0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / group;
   const int64_t gstep = (int64_t)gridDim.x * blockDim.x / group;
-  for (int64_t r = g0; r < rows; r += gstep) {
+  for (int64_t gi = g0; gi < rows * pieces; gi += gstep) {
+    const int64_t r = gi / pieces, u0 = (gi - r * pieces) * piece, u1 = min(len, u0 + piece);
     int64_t o[kMaxArgs];
     iter_offsets(outer, 3, r, o);
     float* dst = out + o[0];
     const float* x = a + o[1];
     const float* y = b + o[2];
-    for (int64_t u = lane; u < len; u += group)
+    for (int64_t u = u0 + lane; u < u1; u += group)
       dst[u] = binary_apply<float>(op, __ldg(x + u * a_unit), __ldg(y + u * b_unit), p0, p1);
   }
 }
@@ -677,8 +681,10 @@ int pvb2_binary(int op, const pvb2_tensor* out, const pvb2_tensor* a, const pvb2
     const int64_t len = it.sizes[nd - 1];
     int group = 32;
     while (group > 4 && group / 2 >= len) group >>= 1;
-    binary_f32_rows_kernel<<<grid_for(rows * group, block), block, 0, s>>>(
-        outer, rows, len, group, op, (float*)out->data, (const float*)a->data, (int)it.strides[1][nd - 1],
+    const int64_t piece = 1024;
+    const int64_t groups = rows * ((len + piece - 1) / piece);
+    binary_f32_rows_kernel<<<grid_for(groups * group, block), block, 0, s>>>(
+        outer, rows, len, piece, group, op, (float*)out->data, (const float*)a->data, (int)it.strides[1][nd - 1],
         (const float*)b->data, (int)it.strides[2][nd - 1], (float)p0, (float)p1);
     PVB2_LAUNCH_CHECK();
     return PVB2_OK;

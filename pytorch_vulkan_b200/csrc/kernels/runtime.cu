@@ -134,18 +134,21 @@ __global__ void copy_strided_kernel(IterShape it, void* dst, int ddt, const void
 // of `units` V-sized words, a group of G lanes per row, row offsets from the
 // outer dims computed once per row.  `outer` holds the outer dims with
 // strides in V units.
+// (long rows are cut into pieces of `piece` words, a group per piece)
 template <typename V>
-__global__ void __launch_bounds__(256) copy_rows_kernel(IterShape outer, int64_t rows, int64_t units, int group,
-                                                        V* __restrict__ dst, const V* __restrict__ src) {
+__global__ void __launch_bounds__(256) copy_rows_kernel(IterShape outer, int64_t rows, int64_t units, int64_t piece,
+                                                        int group, V* __restrict__ dst, const V* __restrict__ src) {
   const int lane = threadIdx.x % group;
+  const int64_t pieces = (units + piece - 1) / piece;
   const int64_t g0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / group;
   const int64_t gstep = (int64_t)gridDim.x * blockDim.x / group;
-  for (int64_t r = g0; r < rows; r += gstep) {
+  for (int64_t gi = g0; gi < rows * pieces; gi += gstep) {
+    const int64_t r = gi / pieces, u0 = (gi - r * pieces) * piece, u1 = min(units, u0 + piece);
     int64_t offs[kMaxArgs];
     iter_offsets(outer, 2, r, offs);
     V* d = dst + offs[0];
     const V* x = src + offs[1];
-    for (int64_t u = lane; u < units; u += group) d[u] = __ldg(x + u);
+    for (int64_t u = u0 + lane; u < u1; u += group) d[u] = __ldg(x + u);
   }
 }
 
@@ -458,16 +461,17 @@ int pvb2_copy(const pvb2_tensor* dst, const pvb2_tensor* src, pvb2_stream stream
       const int64_t units = inner_bytes / vb;
       int group = 4;
       while (group < 32 && group < units) group <<= 1;
+      const int64_t piece = 16384 / vb;  // 16 KB per group at most
       const int block = 256;
-      const int grid = grid_for(rows * group, block);
+      const int grid = grid_for(rows * ((units + piece - 1) / piece) * group, block);
       if (vb == 16)
-        copy_rows_kernel<float4><<<grid, block, 0, s>>>(outer, rows, units, group, (float4*)dst->data,
+        copy_rows_kernel<float4><<<grid, block, 0, s>>>(outer, rows, units, piece, group, (float4*)dst->data,
                                                         (const float4*)src->data);
       else if (vb == 8)
-        copy_rows_kernel<float2><<<grid, block, 0, s>>>(outer, rows, units, group, (float2*)dst->data,
+        copy_rows_kernel<float2><<<grid, block, 0, s>>>(outer, rows, units, piece, group, (float2*)dst->data,
                                                         (const float2*)src->data);
       else
-        copy_rows_kernel<float><<<grid, block, 0, s>>>(outer, rows, units, group, (float*)dst->data,
+        copy_rows_kernel<float><<<grid, block, 0, s>>>(outer, rows, units, piece, group, (float*)dst->data,
                                                        (const float*)src->data);
       PVB2_LAUNCH_CHECK();
       return PVB2_OK;

@@ -603,6 +603,7 @@ ROW_COPIES = [
     ("half", torch.float16, [6, 5, 48], lambda x: x.transpose(0, 1).contiguous()),
     ("bytes", torch.uint8, [6, 5, 160], lambda x: x.transpose(0, 1).contiguous()),
     ("expanded", torch.float32, [1, 5, 64], lambda x: x.expand(4, 5, 64).transpose(0, 1).contiguous()),
+    ("long_rows", torch.float32, [3, 70004], lambda x: x[:, 2:70002].contiguous()),
 ]
 
 
@@ -625,6 +626,7 @@ ROW_BINARIES = [
     ("gelu_bwd_transposed", [64, 33, 48], [33, 64, 48],
      lambda a, b: torch.ops.aten.gelu_backward(a.transpose(0, 1), b)),
     ("add_alpha", [50, 3, 40], [3, 50, 40], lambda a, b: torch.add(a.transpose(0, 1), b, alpha=-2.5)),
+    ("pos_embedding", [32, 197, 768], [1, 197, 768], lambda a, b: a + b),  # few rows of 151296 elements
 ]
 
 
