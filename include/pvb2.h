@@ -410,6 +410,8 @@ typedef struct pvb2_sdpa_desc {
   int32_t B, H, Lq, Lk, D;
   float scale;                 /* usually 1/sqrt(D)                      */
   int32_t causal;
+  int32_t math;                /* PVB2_MATH_TF32: tensor cores (D 32, 64); */
+                               /* PVB2_MATH_FP32: exact fp32 CUDA cores     */
 } pvb2_sdpa_desc;
 PVB2_API int pvb2_sdpa_fwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tensor* k, const pvb2_tensor* v,
                            const pvb2_tensor* out, float* lse, pvb2_stream stream);

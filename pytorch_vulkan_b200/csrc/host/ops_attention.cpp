@@ -72,6 +72,7 @@ static pvb2_sdpa_desc sdpa_desc(const at::Tensor& q, const at::Tensor& k, bool i
   d.D = (int32_t)q.size(3);
   d.scale = (float)(scale.has_value() ? *scale : 1.0 / std::sqrt((double)d.D));
   d.causal = is_causal ? 1 : 0;
+  d.math = math_mode() == PVB2_MATH_FP32 ? PVB2_MATH_FP32 : PVB2_MATH_TF32;
   return d;
 }
 

@@ -36,7 +36,9 @@
 // a reduction kernel sums the slices in key-block order (deterministic).
 // When the caller's workspace cannot hold the slices, a second kernel per
 // (64 queries, head) recomputes S and dP and accumulates dQ instead.
-// All arithmetic is fp32 on the CUDA cores; the exponentials use expf.
+// In exact-fp32 math mode all arithmetic is fp32 on the CUDA cores; in the
+// default TF32 mode (D = 32 or 64) the tile products run on the tensor cores
+// (the kernels below the SIMT ones).  The exponentials use expf.
 #include <cfloat>
 #include "common.cuh"
 
@@ -462,6 +464,281 @@ __global__ void __launch_bounds__(kAtThreads) sdpa_bwd_dq_kernel(AtView q, AtVie
   }
 }
 
+// ------------------------------------------------- TF32 tensor-core kernels
+// The default math mode (TF32, as for convolutions and GEMMs) runs the tile
+// products on the tensor cores with warp-level mma.sync.m16n8k8 TF32
+// (operands rounded to TF32 with cvt.rna, fp32 accumulation); D = 32 or 64.
+// 128 threads, four warps of 16 rows each; fragment layouts of m16n8k8
+// (g = lane / 4, t = lane % 4):  A a0 (g, t) a1 (g+8, t) a2 (g, t+4)
+// a3 (g+8, t+4);  B b0 (t, g) b1 (t+4, g);  C c0 (g, 2t) c1 (g, 2t+1)
+// c2 (g+8, 2t) c3 (g+8, 2t+1).  Shared tiles use a row pitch of D + 4
+// (4 mod 32 banks: the (g, t) fragment reads are conflict-free).
+constexpr int kTcThreads = 128;
+constexpr int kTcPS = kAtB + 4;  // pitch of the 64-wide P / dS tiles
+
+__device__ __forceinline__ uint32_t tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma8(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// A fragment of rows r0 .. r0+15, columns k0 .. k0+7 of a row-major tile
+__device__ __forceinline__ void frag_a(uint32_t (&a)[4], const float* T, int pitch, int r0, int k0, int g, int t) {
+  a[0] = tf32(T[(r0 + g) * pitch + k0 + t]);
+  a[1] = tf32(T[(r0 + g + 8) * pitch + k0 + t]);
+  a[2] = tf32(T[(r0 + g) * pitch + k0 + t + 4]);
+  a[3] = tf32(T[(r0 + g + 8) * pitch + k0 + t + 4]);
+}
+// A fragment read transposed: element (m, k) at T[k][m]
+__device__ __forceinline__ void frag_a_t(uint32_t (&a)[4], const float* T, int pitch, int m0, int k0, int g, int t) {
+  a[0] = tf32(T[(k0 + t) * pitch + m0 + g]);
+  a[1] = tf32(T[(k0 + t) * pitch + m0 + g + 8]);
+  a[2] = tf32(T[(k0 + t + 4) * pitch + m0 + g]);
+  a[3] = tf32(T[(k0 + t + 4) * pitch + m0 + g + 8]);
+}
+
+// rows [l0, l0 + 64) of a view into a tile of pitch PITCH, times `mul`
+template <int D, int PITCH>
+__device__ __forceinline__ void tc_load(float* s, const AtView& v, int b, int h, int l0, int len, float mul) {
+  for (int e = threadIdx.x; e < kAtB * (D / 4); e += kTcThreads) {
+    const int r = e / (D / 4), c4 = (e % (D / 4)) * 4;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (l0 + r < len) x = __ldg(reinterpret_cast<const float4*>(at_row(v, b, h, l0 + r) + c4));
+    x.x *= mul;
+    x.y *= mul;
+    x.z *= mul;
+    x.w *= mul;
+    *reinterpret_cast<float4*>(s + r * PITCH + c4) = x;
+  }
+}
+
+__device__ __forceinline__ float quad_max2(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+__device__ __forceinline__ float quad_sum2(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
+
+// forward: CTA = 64 queries of a head; warp w owns query rows 16 w .. 16 w + 15
+template <int D>
+__global__ void __launch_bounds__(kTcThreads) sdpa_fwd_tc_kernel(AtView q, AtView k, AtView v, AtView o,
+                                                                 float* __restrict__ lse, AtArgs a) {
+  constexpr int PQ = D + 4, PV = D + 8, NT = D / 8;
+  extern __shared__ __align__(16) float at_smem[];
+  float* Qs = at_smem;
+  float* Ks = Qs + kAtB * PQ;
+  float* Vs = Ks + kAtB * PQ;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  float* Ps = Vs + kAtB * PV + warp * 16 * kTcPS;
+  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int q0 = blockIdx.x * kAtB, r0 = warp * 16;
+  tc_load<D, PQ>(Qs, q, b, h, q0, a.Lq, a.scale);
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+  float m[2] = {-FLT_MAX, -FLT_MAX}, l[2] = {0.f, 0.f};
+  const int kend = a.causal ? min(a.Lk, q0 + kAtB) : a.Lk;
+  for (int k0 = 0; k0 < kend; k0 += kAtB) {
+    __syncthreads();  // previous block's K / V no longer read
+    tc_load<D, PQ>(Ks, k, b, h, k0, a.Lk, 1.f);
+    tc_load<D, PV>(Vs, v, b, h, k0, a.Lk, 1.f);
+    __syncthreads();
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D; kk += 8) {
+      uint32_t af[4];
+      frag_a(af, Qs, PQ, r0, kk, g, t);
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+        mma8(s[n], af, tf32(Ks[(n * 8 + g) * PQ + kk + t]), tf32(Ks[(n * 8 + g) * PQ + kk + t + 4]));
+    }
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int qi = q0 + r0 + g + 8 * hr;
+      float mx = -FLT_MAX;
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int kj = k0 + n * 8 + 2 * t + j;
+          const bool ok = kj < a.Lk && !(a.causal && kj > qi);
+          s[n][2 * hr + j] = ok ? s[n][2 * hr + j] : -FLT_MAX;
+          mx = fmaxf(mx, s[n][2 * hr + j]);
+        }
+      const float mnew = fmaxf(m[hr], quad_max2(mx));
+      const float alpha = expf(m[hr] - mnew);
+      float ps = 0.f;
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float p = s[n][2 * hr + j] == -FLT_MAX ? 0.f : expf(s[n][2 * hr + j] - mnew);
+          Ps[(g + 8 * hr) * kTcPS + n * 8 + 2 * t + j] = p;
+          ps += p;
+        }
+      l[hr] = l[hr] * alpha + quad_sum2(ps);
+      m[hr] = mnew;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        acc[n][2 * hr] *= alpha;
+        acc[n][2 * hr + 1] *= alpha;
+      }
+    }
+    __syncwarp();  // the warp's P rows are read back as A fragments
+    const int kspan = at_span(k0, a.Lk);
+    for (int kk = 0; kk < kspan; kk += 8) {
+      uint32_t af[4];
+      frag_a(af, Ps, kTcPS, 0, kk, g, t);
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+        mma8(acc[n], af, tf32(Vs[(kk + t) * PV + n * 8 + g]), tf32(Vs[(kk + t + 4) * PV + n * 8 + g]));
+    }
+    __syncwarp();  // P rows may be rewritten by the next block
+  }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int qi = q0 + r0 + g + 8 * hr;
+    if (qi >= a.Lq) continue;
+    const float inv = l[hr] > 0.f ? 1.f / l[hr] : 0.f;
+    float* orow = at_row(o, b, h, qi);
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+      *reinterpret_cast<float2*>(orow + n * 8 + 2 * t) = make_float2(acc[n][2 * hr] * inv, acc[n][2 * hr + 1] * inv);
+    if (t == 0) lse[(int64_t)bh * a.Lq + qi] = l[hr] > 0.f ? m[hr] + logf(l[hr]) : -FLT_MAX;
+  }
+}
+
+// backward per 64-key block: warp w owns keys 16 w .. 16 w + 15 for S^T, dP^T,
+// dV, dK and query rows 16 w .. 16 w + 15 for this block's dQ slice
+template <int D>
+__global__ void __launch_bounds__(kTcThreads) sdpa_bwd_kv_tc_kernel(AtView q, AtView k, AtView v, AtView dout,
+                                                                    const float* __restrict__ lse,
+                                                                    const float* __restrict__ di, AtView dk,
+                                                                    AtView dv, float* __restrict__ dq_part,
+                                                                    AtArgs a) {
+  constexpr int PQ = D + 4, NT = D / 8;
+  extern __shared__ __align__(16) float at_smem[];
+  float* Ks = at_smem;
+  float* Vs = Ks + kAtB * PQ;
+  float* Qs = Vs + kAtB * PQ;
+  float* Gs = Qs + kAtB * PQ;
+  float* PTs = Gs + kAtB * PQ;  // P^T  [key][query]
+  float* STs = PTs + kAtB * kTcPS;  // dS^T [key][query]
+  float* Ls = STs + kAtB * kTcPS;
+  float* Ds = Ls + kAtB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  const int kb = blockIdx.x, k0 = kb * kAtB, r0 = warp * 16;
+  tc_load<D, PQ>(Ks, k, b, h, k0, a.Lk, 1.f);
+  tc_load<D, PQ>(Vs, v, b, h, k0, a.Lk, 1.f);
+  float dka[NT][4], dva[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dka[n][e] = dva[n][e] = 0.f;
+  for (int q0 = a.causal ? k0 : 0; q0 < a.Lq; q0 += kAtB) {
+    __syncthreads();  // previous query block's tiles no longer read
+    tc_load<D, PQ>(Qs, q, b, h, q0, a.Lq, a.scale);
+    tc_load<D, PQ>(Gs, dout, b, h, q0, a.Lq, 1.f);
+    at_load_rows(Ls, Ds, lse, di, bh, q0, a.Lq);
+    __syncthreads();
+    // S^T and dP^T for the warp's 16 keys x 64 queries
+    float st[8][4], dp[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) st[n][e] = dp[n][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D; kk += 8) {
+      uint32_t ak[4], av[4];
+      frag_a(ak, Ks, PQ, r0, kk, g, t);
+      frag_a(av, Vs, PQ, r0, kk, g, t);
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        const int qr = (n * 8 + g) * PQ + kk + t;
+        mma8(st[n], ak, tf32(Qs[qr]), tf32(Qs[qr + 4]));
+        mma8(dp[n], av, tf32(Gs[qr]), tf32(Gs[qr + 4]));
+      }
+    }
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int kr = r0 + g + 8 * hr, kj = k0 + kr;
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int qc = n * 8 + 2 * t + j, qi = q0 + qc;
+          const bool ok = qi < a.Lq && kj < a.Lk && !(a.causal && kj > qi);
+          const float p = ok ? expf(st[n][2 * hr + j] - Ls[qc]) : 0.f;
+          PTs[kr * kTcPS + qc] = p;
+          STs[kr * kTcPS + qc] = p * (dp[n][2 * hr + j] - Ds[qc]);
+        }
+    }
+    __syncwarp();  // the warp's own P^T / dS^T rows are its A fragments below
+    const int rn = at_span(q0, a.Lq);
+    for (int kk = 0; kk < rn; kk += 8) {
+      uint32_t ap[4], as[4];
+      frag_a(ap, PTs, kTcPS, r0, kk, g, t);
+      frag_a(as, STs, kTcPS, r0, kk, g, t);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int r = (kk + t) * PQ + n * 8 + g;
+        mma8(dva[n], ap, tf32(Gs[r]), tf32(Gs[r + 4 * PQ]));
+        mma8(dka[n], as, tf32(Qs[r]), tf32(Qs[r + 4 * PQ]));  // Qs holds scale * Q
+      }
+    }
+    if (dq_part) {
+      __syncthreads();  // every warp's dS^T rows are read below
+      float dqa[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) dqa[n][0] = dqa[n][1] = dqa[n][2] = dqa[n][3] = 0.f;
+      const int kspan = at_span(k0, a.Lk);
+      for (int kk = 0; kk < kspan; kk += 8) {
+        uint32_t as[4];
+        frag_a_t(as, STs, kTcPS, r0, kk, g, t);  // dS (query r0.., key kk..) = dS^T transposed
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          const int r = (kk + t) * PQ + n * 8 + g;
+          mma8(dqa[n], as, tf32(Ks[r]), tf32(Ks[r + 4 * PQ]));
+        }
+      }
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int qi = q0 + r0 + g + 8 * hr;
+        if (qi >= a.Lq) continue;
+        float* row = dq_part + (((int64_t)kb * a.B * a.H + bh) * a.Lq + qi) * D;
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+          *reinterpret_cast<float2*>(row + n * 8 + 2 * t) = make_float2(dqa[n][2 * hr], dqa[n][2 * hr + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int kj = k0 + r0 + g + 8 * hr;
+    if (kj >= a.Lk) continue;
+    float* kr = at_row(dk, b, h, kj);
+    float* vr = at_row(dv, b, h, kj);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      *reinterpret_cast<float2*>(kr + n * 8 + 2 * t) = make_float2(dka[n][2 * hr], dka[n][2 * hr + 1]);
+      *reinterpret_cast<float2*>(vr + n * 8 + 2 * t) = make_float2(dva[n][2 * hr], dva[n][2 * hr + 1]);
+    }
+  }
+}
+
 // ------------------------------------------------------------ host side
 static int at_view(const pvb2_tensor* t, int B, int H, int L, int D, const char* what, AtView* v) {
   PVB2_CHECK_ARG(t && t->dtype == PVB2_F32 && t->ndim == 4, "sdpa: %s must be a 4-D float32 tensor", what);
@@ -496,11 +773,21 @@ static int at_smem_attr(K kernel, int bytes, std::atomic<uint64_t>& done) {
 
 template <int D>
 static int at_fwd(const AtView& q, const AtView& k, const AtView& v, const AtView& o, float* lse, const AtArgs& a,
-                  cudaStream_t s) {
+                  bool tc, cudaStream_t s) {
+  const dim3 grid((unsigned)((a.Lq + kAtB - 1) / kAtB), (unsigned)(a.B * a.H));
+  if constexpr (D <= 64) {
+    if (tc) {
+      const int smem = (2 * kAtB * (D + 4) + kAtB * (D + 8) + 4 * 16 * kTcPS) * 4;
+      static std::atomic<uint64_t> attr_tc{0};
+      PVB2_TRY(at_smem_attr(sdpa_fwd_tc_kernel<D>, smem, attr_tc));
+      sdpa_fwd_tc_kernel<D><<<grid, kTcThreads, smem, s>>>(q, k, v, o, lse, a);
+      PVB2_LAUNCH_CHECK();
+      return PVB2_OK;
+    }
+  }
   const int smem = (3 * AtCfg<D>::TILE + AtCfg<D>::PTILE) * 4;
   static std::atomic<uint64_t> attr{0};
   PVB2_TRY(at_smem_attr(sdpa_fwd_kernel<D>, smem, attr));
-  const dim3 grid((unsigned)((a.Lq + kAtB - 1) / kAtB), (unsigned)(a.B * a.H));
   sdpa_fwd_kernel<D><<<grid, kAtThreads, smem, s>>>(q, k, v, o, lse, a);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
@@ -520,18 +807,30 @@ constexpr size_t kAtSliceCap = (size_t)2 << 30;  // larger slices: dQ is recompu
 template <int D>
 static int at_bwd(const AtView& q, const AtView& k, const AtView& v, const AtView& o, const AtView& g,
                   const float* lse, float* di, float* dq_part, const AtView& dq, const AtView& dk, const AtView& dv,
-                  const AtArgs& a, cudaStream_t s) {
+                  const AtArgs& a, bool tc, cudaStream_t s) {
   const int64_t rows = (int64_t)a.B * a.H * a.Lq;
   sdpa_bwd_di_kernel<D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(g, o, di, a);
   PVB2_LAUNCH_CHECK();
   using C = AtCfg<D>;
-  const int skv = (4 * C::TILE + 2 * C::PTILE + 2 * kAtB) * 4;
-  static std::atomic<uint64_t> attr_kv{0}, attr_q{0};
-  PVB2_TRY(at_smem_attr(sdpa_bwd_kv_kernel<D>, skv, attr_kv));
+  static std::atomic<uint64_t> attr_kv{0}, attr_q{0}, attr_tc{0};
   const int nkb = (a.Lk + kAtB - 1) / kAtB;
   const dim3 gk((unsigned)nkb, (unsigned)(a.B * a.H));
-  sdpa_bwd_kv_kernel<D><<<gk, kAtThreads, skv, s>>>(q, k, v, g, lse, di, dk, dv, dq_part, a);
-  PVB2_LAUNCH_CHECK();
+  bool done = false;
+  if constexpr (D <= 64) {
+    if (tc) {
+      const int stc = (4 * kAtB * (D + 4) + 2 * kAtB * kTcPS + 2 * kAtB) * 4;
+      PVB2_TRY(at_smem_attr(sdpa_bwd_kv_tc_kernel<D>, stc, attr_tc));
+      sdpa_bwd_kv_tc_kernel<D><<<gk, kTcThreads, stc, s>>>(q, k, v, g, lse, di, dk, dv, dq_part, a);
+      PVB2_LAUNCH_CHECK();
+      done = true;
+    }
+  }
+  if (!done) {
+    const int skv = (4 * C::TILE + 2 * C::PTILE + 2 * kAtB) * 4;
+    PVB2_TRY(at_smem_attr(sdpa_bwd_kv_kernel<D>, skv, attr_kv));
+    sdpa_bwd_kv_kernel<D><<<gk, kAtThreads, skv, s>>>(q, k, v, g, lse, di, dk, dv, dq_part, a);
+    PVB2_LAUNCH_CHECK();
+  }
   if (dq_part) {
     sdpa_bwd_dq_reduce_kernel<D><<<grid_for(rows * (D / 4), 256), 256, 0, s>>>(dq_part, dq, a, nkb);
     PVB2_LAUNCH_CHECK();
@@ -563,9 +862,10 @@ int pvb2_sdpa_fwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tens
   if ((int64_t)d->B * d->H * d->Lq == 0) return PVB2_OK;
   const AtArgs a{d->B, d->H, d->Lq, d->Lk, d->scale, d->causal};
   cudaStream_t s = as_stream(stream);
-  if (d->D == 32) return at_fwd<32>(qv, kv, vv, ov, lse, a, s);
-  if (d->D == 64) return at_fwd<64>(qv, kv, vv, ov, lse, a, s);
-  return at_fwd<128>(qv, kv, vv, ov, lse, a, s);
+  const bool tc = d->math == PVB2_MATH_TF32;
+  if (d->D == 32) return at_fwd<32>(qv, kv, vv, ov, lse, a, tc, s);
+  if (d->D == 64) return at_fwd<64>(qv, kv, vv, ov, lse, a, tc, s);
+  return at_fwd<128>(qv, kv, vv, ov, lse, a, tc, s);
 }
 
 size_t pvb2_sdpa_bwd_workspace_size(const pvb2_sdpa_desc* d) {
@@ -605,9 +905,10 @@ int pvb2_sdpa_bwd(const pvb2_sdpa_desc* d, const pvb2_tensor* q, const pvb2_tens
   // dQ through the per-key-block slices when they fit, else recomputed
   float* dq_part =
       workspace_bytes >= di_bytes + at_slice_bytes(d) ? (float*)((char*)workspace + di_bytes) : nullptr;
-  if (d->D == 32) return at_bwd<32>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, s);
-  if (d->D == 64) return at_bwd<64>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, s);
-  return at_bwd<128>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, s);
+  const bool tc = d->math == PVB2_MATH_TF32;
+  if (d->D == 32) return at_bwd<32>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, tc, s);
+  if (d->D == 64) return at_bwd<64>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, tc, s);
+  return at_bwd<128>(qv, kv, vv, ov, gv, lse, di, dq_part, dqv, dkv, dvv, a, tc, s);
 }
 
 }  // extern "C"

@@ -42,8 +42,24 @@ def _make(B, H, L, D, layout, g):
     return torch.randn(B, H, L, D, generator=g)
 
 
+# exact fp32 (CUDA-core kernels) at fp32 accuracy; TF32 tensor cores (the
+# default math mode, D = 32 / 64) within 5e-3 of each tensor's magnitude --
+# TF32 operands carry 11 significant bits
+MATH = [("fp32", 1, 1e-5), ("tf32", 0, 5e-3)]
+
+
+@pytest.mark.parametrize("math_name,mode,tol", MATH, ids=[m[0] for m in MATH])
 @pytest.mark.parametrize("case", CASES, ids=["-".join(map(str, c)) for c in CASES])
-def test_sdpa_fused_matches_float64(ocl, case):
+def test_sdpa_fused_matches_float64(ocl, case, math_name, mode, tol):
+    old = torch.ocl.get_math_mode()
+    torch.ocl.set_math_mode(mode)
+    try:
+        _sdpa_case(case, tol)
+    finally:
+        torch.ocl.set_math_mode(old)
+
+
+def _sdpa_case(case, tol):
     B, H, Lq, Lk, D, causal, layout = case
     g = torch.Generator().manual_seed(B * 100 + Lq)
     q, k, v = _make(B, H, Lq, D, layout, g), _make(B, H, Lk, D, layout, g), _make(B, H, Lk, D, layout, g)
@@ -59,10 +75,10 @@ def test_sdpa_fused_matches_float64(ocl, case):
         s = s.masked_fill(torch.ones(Lq, Lk, dtype=torch.bool).triu(1), float("-inf"))
     o64 = torch.softmax(s, -1) @ v64
     o64.backward(dout.double())
-    assert _rel(o64, od) < 1e-5
-    assert _rel(q64.grad, qd.grad) < 1e-5
-    assert _rel(k64.grad, kd.grad) < 1e-5
-    assert _rel(v64.grad, vd.grad) < 1e-5
+    assert _rel(o64, od) < tol
+    assert _rel(q64.grad, qd.grad) < tol
+    assert _rel(k64.grad, kd.grad) < tol
+    assert _rel(v64.grad, vd.grad) < tol
 
 
 def test_sdpa_unsupported_falls_back_to_math(ocl):
@@ -128,7 +144,8 @@ def test_sdpa_backward_without_slice_workspace(ocl):
 
     class Desc(ctypes.Structure):
         _fields_ = [("B", ctypes.c_int32), ("H", ctypes.c_int32), ("Lq", ctypes.c_int32), ("Lk", ctypes.c_int32),
-                    ("D", ctypes.c_int32), ("scale", ctypes.c_float), ("causal", ctypes.c_int32)]
+                    ("D", ctypes.c_int32), ("scale", ctypes.c_float), ("causal", ctypes.c_int32),
+                    ("math", ctypes.c_int32)]
 
     def td(t):
         return T(t.data_ptr(), (ctypes.c_int64 * 8)(*t.shape), (ctypes.c_int64 * 8)(*t.stride()), t.dim(), 0)
@@ -142,7 +159,7 @@ def test_sdpa_backward_without_slice_workspace(ocl):
         g = torch.Generator().manual_seed(40 + causal)
         q, k, v = (torch.randn(B, H, n, D, generator=g) for n in (Lq, Lk, Lk))
         dout = torch.randn(B, H, Lq, D, generator=g)
-        d = Desc(B, H, Lq, Lk, D, 1.0 / math.sqrt(D), causal)
+        d = Desc(B, H, Lq, Lk, D, 1.0 / math.sqrt(D), causal, 1)  # exact fp32 kernels
         qd, kd, vd, gd = (t.to(DEV) for t in (q, k, v, dout))
         od = torch.empty_like(qd)
         lse = torch.empty(B, H, Lq, device=DEV)
