@@ -492,33 +492,38 @@ __device__ __forceinline__ void mma8(float (&c)[4], const uint32_t (&a)[4], uint
 
 // A fragment of rows r0 .. r0+15, columns k0 .. k0+7 of a row-major tile
 __device__ __forceinline__ void frag_a(uint32_t (&a)[4], const float* T, int pitch, int r0, int k0, int g, int t) {
-  a[0] = tf32(T[(r0 + g) * pitch + k0 + t]);
-  a[1] = tf32(T[(r0 + g + 8) * pitch + k0 + t]);
-  a[2] = tf32(T[(r0 + g) * pitch + k0 + t + 4]);
-  a[3] = tf32(T[(r0 + g + 8) * pitch + k0 + t + 4]);
+  a[0] = __float_as_uint(T[(r0 + g) * pitch + k0 + t]);
+  a[1] = __float_as_uint(T[(r0 + g + 8) * pitch + k0 + t]);
+  a[2] = __float_as_uint(T[(r0 + g) * pitch + k0 + t + 4]);
+  a[3] = __float_as_uint(T[(r0 + g + 8) * pitch + k0 + t + 4]);
 }
 // A fragment read transposed: element (m, k) at T[k][m]
 __device__ __forceinline__ void frag_a_t(uint32_t (&a)[4], const float* T, int pitch, int m0, int k0, int g, int t) {
-  a[0] = tf32(T[(k0 + t) * pitch + m0 + g]);
-  a[1] = tf32(T[(k0 + t) * pitch + m0 + g + 8]);
-  a[2] = tf32(T[(k0 + t + 4) * pitch + m0 + g]);
-  a[3] = tf32(T[(k0 + t + 4) * pitch + m0 + g + 8]);
+  a[0] = __float_as_uint(T[(k0 + t) * pitch + m0 + g]);
+  a[1] = __float_as_uint(T[(k0 + t) * pitch + m0 + g + 8]);
+  a[2] = __float_as_uint(T[(k0 + t + 4) * pitch + m0 + g]);
+  a[3] = __float_as_uint(T[(k0 + t + 4) * pitch + m0 + g + 8]);
 }
 
-// rows [l0, l0 + 64) of a view into a tile of pitch PITCH, times `mul`
+// rows [l0, l0 + 64) of a view into a tile of pitch PITCH, times `mul`,
+// rounded to TF32
 template <int D, int PITCH>
 __device__ __forceinline__ void tc_load(float* s, const AtView& v, int b, int h, int l0, int len, float mul) {
   for (int e = threadIdx.x; e < kAtB * (D / 4); e += kTcThreads) {
     const int r = e / (D / 4), c4 = (e % (D / 4)) * 4;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
     if (l0 + r < len) x = __ldg(reinterpret_cast<const float4*>(at_row(v, b, h, l0 + r) + c4));
-    x.x *= mul;
-    x.y *= mul;
-    x.z *= mul;
-    x.w *= mul;
+    x.x = __uint_as_float(tf32(x.x * mul));
+    x.y = __uint_as_float(tf32(x.y * mul));
+    x.z = __uint_as_float(tf32(x.z * mul));
+    x.w = __uint_as_float(tf32(x.w * mul));
     *reinterpret_cast<float4*>(s + r * PITCH + c4) = x;
   }
 }
+
+// tiles hold TF32-rounded values (rounded once when stored), so fragments
+// are plain reinterpretations
+__device__ __forceinline__ uint32_t u32(float x) { return __float_as_uint(x); }
 
 __device__ __forceinline__ float quad_max2(float v) {
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
@@ -562,7 +567,7 @@ __global__ void __launch_bounds__(kTcThreads) sdpa_fwd_tc_kernel(AtView q, AtVie
       frag_a(af, Qs, PQ, r0, kk, g, t);
 #pragma unroll
       for (int n = 0; n < 8; ++n)
-        mma8(s[n], af, tf32(Ks[(n * 8 + g) * PQ + kk + t]), tf32(Ks[(n * 8 + g) * PQ + kk + t + 4]));
+        mma8(s[n], af, u32(Ks[(n * 8 + g) * PQ + kk + t]), u32(Ks[(n * 8 + g) * PQ + kk + t + 4]));
     }
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
@@ -585,7 +590,7 @@ __global__ void __launch_bounds__(kTcThreads) sdpa_fwd_tc_kernel(AtView q, AtVie
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const float p = s[n][2 * hr + j] == -FLT_MAX ? 0.f : expf(s[n][2 * hr + j] - mnew);
-          Ps[(g + 8 * hr) * kTcPS + n * 8 + 2 * t + j] = p;
+          Ps[(g + 8 * hr) * kTcPS + n * 8 + 2 * t + j] = __uint_as_float(tf32(p));
           ps += p;
         }
       l[hr] = l[hr] * alpha + quad_sum2(ps);
@@ -603,7 +608,7 @@ __global__ void __launch_bounds__(kTcThreads) sdpa_fwd_tc_kernel(AtView q, AtVie
       frag_a(af, Ps, kTcPS, 0, kk, g, t);
 #pragma unroll
       for (int n = 0; n < NT; ++n)
-        mma8(acc[n], af, tf32(Vs[(kk + t) * PV + n * 8 + g]), tf32(Vs[(kk + t + 4) * PV + n * 8 + g]));
+        mma8(acc[n], af, u32(Vs[(kk + t) * PV + n * 8 + g]), u32(Vs[(kk + t + 4) * PV + n * 8 + g]));
     }
     __syncwarp();  // P rows may be rewritten by the next block
   }
@@ -668,8 +673,8 @@ __global__ void __launch_bounds__(kTcThreads) sdpa_bwd_kv_tc_kernel(AtView q, At
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         const int qr = (n * 8 + g) * PQ + kk + t;
-        mma8(st[n], ak, tf32(Qs[qr]), tf32(Qs[qr + 4]));
-        mma8(dp[n], av, tf32(Gs[qr]), tf32(Gs[qr + 4]));
+        mma8(st[n], ak, u32(Qs[qr]), u32(Qs[qr + 4]));
+        mma8(dp[n], av, u32(Gs[qr]), u32(Gs[qr + 4]));
       }
     }
 #pragma unroll
@@ -682,8 +687,8 @@ __global__ void __launch_bounds__(kTcThreads) sdpa_bwd_kv_tc_kernel(AtView q, At
           const int qc = n * 8 + 2 * t + j, qi = q0 + qc;
           const bool ok = qi < a.Lq && kj < a.Lk && !(a.causal && kj > qi);
           const float p = ok ? expf(st[n][2 * hr + j] - Ls[qc]) : 0.f;
-          PTs[kr * kTcPS + qc] = p;
-          STs[kr * kTcPS + qc] = p * (dp[n][2 * hr + j] - Ds[qc]);
+          PTs[kr * kTcPS + qc] = __uint_as_float(tf32(p));
+          STs[kr * kTcPS + qc] = __uint_as_float(tf32(p * (dp[n][2 * hr + j] - Ds[qc])));
         }
     }
     __syncwarp();  // the warp's own P^T / dS^T rows are its A fragments below
@@ -695,8 +700,8 @@ __global__ void __launch_bounds__(kTcThreads) sdpa_bwd_kv_tc_kernel(AtView q, At
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         const int r = (kk + t) * PQ + n * 8 + g;
-        mma8(dva[n], ap, tf32(Gs[r]), tf32(Gs[r + 4 * PQ]));
-        mma8(dka[n], as, tf32(Qs[r]), tf32(Qs[r + 4 * PQ]));  // Qs holds scale * Q
+        mma8(dva[n], ap, u32(Gs[r]), u32(Gs[r + 4 * PQ]));
+        mma8(dka[n], as, u32(Qs[r]), u32(Qs[r + 4 * PQ]));  // Qs holds scale * Q
       }
     }
     if (dq_part) {
@@ -711,7 +716,7 @@ __global__ void __launch_bounds__(kTcThreads) sdpa_bwd_kv_tc_kernel(AtView q, At
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
           const int r = (kk + t) * PQ + n * 8 + g;
-          mma8(dqa[n], as, tf32(Ks[r]), tf32(Ks[r + 4 * PQ]));
+          mma8(dqa[n], as, u32(Ks[r]), u32(Ks[r + 4 * PQ]));
         }
       }
 #pragma unroll
