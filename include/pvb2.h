@@ -254,8 +254,11 @@ PVB2_API int pvb2_batch_norm_bwd_relu(const pvb2_tensor* grad_above, const pvb2_
  * pvb2_batch_norm_fwd_train) and writes
  *     y = act(gamma * (x - mean) * invstd + beta + residual)
  * with residual optional (NULL, or contiguous and shaped like x) and act the
- * identity (relu = 0) or ReLU (relu = 1, NaN kept).  With residual NULL and
- * relu 0 the pair computes exactly what pvb2_batch_norm_fwd_train does.
+ * identity (relu = 0) or ReLU (relu = 1, NaN kept).  With sum_out given (it
+ * needs a residual, and may be the residual tensor itself), y receives the
+ * plain normalised values and sum_out the epilogue result.  With residual
+ * NULL and relu 0 the pair computes exactly what pvb2_batch_norm_fwd_train
+ * does.
  * Both need pvb2_batch_norm_fwd_split_ok(x) (contiguous fp32 NCHW within the
  * streaming kernels' size limits) and the workspace of
  * pvb2_batch_norm_workspace_size, untouched between the two calls.  The
@@ -267,8 +270,8 @@ PVB2_API int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, si
 PVB2_API int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const float* beta,
                                        float* running_mean, float* running_var, double momentum, double eps,
                                        const pvb2_tensor* y, float* save_mean, float* save_invstd,
-                                       const pvb2_tensor* residual, int relu, const void* workspace,
-                                       size_t workspace_bytes, pvb2_stream stream);
+                                       const pvb2_tensor* residual, int relu, const pvb2_tensor* sum_out,
+                                       const void* workspace, size_t workspace_bytes, pvb2_stream stream);
 /* Batch-norm training forward that allocates nothing and takes no workspace.
  * No counterpart in the reference: it exists for callers that cannot
  * allocate device memory at the point of the call -- code running while a

@@ -28,7 +28,9 @@ namespace ocl {
 namespace {
 
 struct PendingBn {
-  at::Tensor x, y, weight, bias, running_mean, running_var, save_mean, save_invstd, residual;
+  // out: where the epilogue result goes when it is not y itself (an in-place
+  // add into another tensor of the pending output, `out += y`)
+  at::Tensor x, y, weight, bias, running_mean, running_var, save_mean, save_invstd, residual, out;
   double momentum = 0.0, eps = 0.0;
   c10::DataPtr ws;
   size_t ws_bytes = 0;
@@ -63,12 +65,13 @@ void launch(PendingBn& p, const char* name) {
   DeviceScope scope(p.device);
   OCL_OP(name, p.device);
   const pvb2_tensor xd = desc(p.x), yd = desc(p.y);
-  pvb2_tensor rd;
+  pvb2_tensor rd, od;
   if (p.residual.defined()) rd = desc(p.residual);
+  if (p.out.defined()) od = desc(p.out);
   OCL_CHECK(pvb2_batch_norm_fwd_apply(&xd, fptr(p.weight), fptr(p.bias), fptr(p.running_mean), fptr(p.running_var),
                                       p.momentum, p.eps, &yd, fptr(p.save_mean), fptr(p.save_invstd),
-                                      p.residual.defined() ? &rd : nullptr, p.relu ? 1 : 0, p.ws.get(), p.ws_bytes,
-                                      p.stream));
+                                      p.residual.defined() ? &rd : nullptr, p.relu ? 1 : 0,
+                                      p.out.defined() ? &od : nullptr, p.ws.get(), p.ws_bytes, p.stream));
 }
 
 void launch_thr(PendingThr& t) {
@@ -147,11 +150,19 @@ bool fuse_deferred_add(const at::Tensor& self, const at::Tensor& other, const at
   std::lock_guard<std::mutex> g(g_mutex);
   if (!g_pending || g_pending->relu || g_pending->residual.defined()) return false;
   PendingBn& p = *g_pending;
-  if (!same_tensor(self, p.y) || !is_ocl(other) || other.device() != p.y.device()) return false;
-  if (other.scalar_type() != at::kFloat || !other.is_contiguous() || !other.sizes().equals(p.y.sizes())) return false;
   if (alpha.isComplex() || alpha.toDouble() != 1.0) return false;
-  if (other.is_alias_of(p.y) || other.is_alias_of(p.x)) return false;
-  p.residual = other;
+  // `y += other` (ResNet's out += identity) or `self += y` (the same add when
+  // the identity branch is the pending batch norm: a downsampling
+  // projection); the sum is the same either way, y + other == other + y
+  const bool y_is_self = same_tensor(self, p.y);
+  const at::Tensor& r = y_is_self ? other : self;
+  if (!y_is_self && !same_tensor(other, p.y)) return false;
+  if (!is_ocl(r) || r.device() != p.y.device() || r.scalar_type() != at::kFloat || !r.is_contiguous() ||
+      !r.sizes().equals(p.y.sizes()))
+    return false;
+  if (r.is_alias_of(p.y) || r.is_alias_of(p.x)) return false;
+  p.residual = r;
+  if (!y_is_self) p.out = self;  // y stays the plain normalised values
   return true;
 }
 
@@ -160,7 +171,7 @@ bool fuse_deferred_relu(const at::Tensor& self) {
   std::optional<PendingBn> p;
   {
     std::lock_guard<std::mutex> g(g_mutex);
-    if (!g_pending || !same_tensor(self, g_pending->y)) return false;
+    if (!g_pending || !same_tensor(self, g_pending->out.defined() ? g_pending->out : g_pending->y)) return false;
     p = std::move(g_pending);
     g_pending.reset();
     g_any.store(false, std::memory_order_release);

@@ -428,7 +428,8 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
     const float* __restrict__ x, float* __restrict__ y, int N, int C, int HW, int chunk, int splits, int vec,
     const float* __restrict__ part, const float* __restrict__ gamma, const float* __restrict__ beta,
     float* __restrict__ running_mean, float* __restrict__ running_var, float momentum, float eps,
-    float* __restrict__ save_mean, float* __restrict__ save_invstd, const float* __restrict__ residual, int relu) {
+    float* __restrict__ save_mean, float* __restrict__ save_invstd, const float* __restrict__ residual, int relu,
+    float* __restrict__ sum_out) {
   __shared__ float s_ab[2];
   const int s = blockIdx.x, c = C - 1 - blockIdx.y;
   const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
@@ -466,6 +467,10 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
   const float a = s_ab[0], b = s_ab[1];
   float* yc = y + (int64_t)c * HW;
   const float* rc = residual ? residual + (int64_t)c * HW : nullptr;
+  // with sum_out: y keeps the normalised values and the epilogue result goes
+  // to sum_out (which may be the residual itself: each element is read, then
+  // written, by the same thread)
+  float* sc = sum_out ? sum_out + (int64_t)c * HW : nullptr;
   const int vw = vec ? 4 : 1, step = vw * blockDim.x;
   int e = start + vw * threadIdx.x;
   if (e >= end) return;
@@ -489,13 +494,14 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
           r.y = fmaf(r.y, a, b);
           r.z = fmaf(r.z, a, b);
           r.w = fmaf(r.w, a, b);
+          if (sc) *reinterpret_cast<float4*>(yc + o[u]) = r;
           if (!plain) {
             r.x = bn_epi(r.x, rc, o[u], relu);
             r.y = bn_epi(r.y, rc, o[u] + 1, relu);
             r.z = bn_epi(r.z, rc, o[u] + 2, relu);
             r.w = bn_epi(r.w, rc, o[u] + 3, relu);
           }
-          *reinterpret_cast<float4*>(yc + o[u]) = r;
+          *reinterpret_cast<float4*>((sc ? sc : yc) + o[u]) = r;
         }
       }
     }
@@ -511,7 +517,15 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u)
-        if (e + u * step < end) yc[o[u]] = bn_epi(fmaf(v[u], a, b), rc, o[u], relu);
+        if (e + u * step < end) {
+          const float r = fmaf(v[u], a, b);
+          if (sc) {
+            yc[o[u]] = r;
+            sc[o[u]] = bn_epi(r, rc, o[u], relu);
+          } else {
+            yc[o[u]] = bn_epi(r, rc, o[u], relu);
+          }
+        }
     }
   }
 }
@@ -662,7 +676,8 @@ static int bn_fwd_stream(const BnGeom& g, const BnStream& p, const float* x, flo
   PVB2_LAUNCH_CHECK();
   bn_st_apply_kernel<<<grid, kBnStThreads, 0, s>>>(x, y, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits,
                                                     p.vec ? 1 : 0, part, gamma, beta, running_mean, running_var,
-                                                    (float)momentum, (float)eps, save_mean, save_invstd, nullptr, 0);
+                                                    (float)momentum, (float)eps, save_mean, save_invstd, nullptr, 0,
+                                                    nullptr);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
@@ -1078,7 +1093,8 @@ int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, size_t work
 int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const float* beta, float* running_mean,
                               float* running_var, double momentum, double eps, const pvb2_tensor* y,
                               float* save_mean, float* save_invstd, const pvb2_tensor* residual, int relu,
-                              const void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+                              const pvb2_tensor* sum_out, const void* workspace, size_t workspace_bytes,
+                              pvb2_stream stream) {
   PVB2_TRY(check_bn_x(x));
   PVB2_CHECK_ARG(pvb2_batch_norm_fwd_split_ok(x), "batch_norm: input not supported by the split forward");
   PVB2_CHECK_ARG(is_contiguous(y) && y->dtype == PVB2_F32 && numel(y) == numel(x),
@@ -1089,9 +1105,13 @@ int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const fl
     for (int d = 0; d < x->ndim; ++d)
       PVB2_CHECK_ARG(residual->sizes[d] == x->sizes[d], "batch_norm: residual shape differs at dim %d", d);
   }
+  if (sum_out) {
+    PVB2_CHECK_ARG(residual && is_contiguous(sum_out) && sum_out->dtype == PVB2_F32 && numel(sum_out) == numel(x),
+                   "batch_norm: sum_out needs a residual and must be contiguous float32 of the input's size");
+  }
   const BnGeom g = bn_geom(x);
-  const void* ptrs[3] = {x->data, y->data, residual ? residual->data : nullptr};
-  const BnStream p = bn_stream_plan(g, ptrs, 3);
+  const void* ptrs[4] = {x->data, y->data, residual ? residual->data : nullptr, sum_out ? sum_out->data : nullptr};
+  const BnStream p = bn_stream_plan(g, ptrs, 4);
   const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
   PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm: workspace too small (%zu < %zu)", workspace_bytes,
                  need);
@@ -1099,7 +1119,8 @@ int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const fl
   bn_st_apply_kernel<<<grid, kBnStThreads, 0, as_stream(stream)>>>(
       (const float*)x->data, (float*)y->data, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits, p.vec ? 1 : 0,
       (const float*)workspace, gamma, beta, running_mean, running_var, (float)momentum, (float)eps, save_mean,
-      save_invstd, residual ? (const float*)residual->data : nullptr, relu ? 1 : 0);
+      save_invstd, residual ? (const float*)residual->data : nullptr, relu ? 1 : 0,
+      sum_out ? (float*)sum_out->data : nullptr);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }

@@ -444,8 +444,8 @@ def test_batch_norm_split_fwd_capi(lib, residual, relu):
     ok(lib, lib.pvb2_batch_norm_fwd_stats(ctypes.byref(td(xd)), ptr(ws), ctypes.c_size_t(ws.numel()), stream()))
     ok(lib, lib.pvb2_batch_norm_fwd_apply(ctypes.byref(td(xd)), ptr(gd), ptr(bd), ptr(rmd), ptr(rvd),
                                           ctypes.c_double(0.1), ctypes.c_double(1e-5), ctypes.byref(td(yd)), ptr(md),
-                                          ptr(isd), ctypes.byref(td(rd)) if residual else None, int(relu), ptr(ws),
-                                          ctypes.c_size_t(ws.numel()), stream()))
+                                          ptr(isd), ctypes.byref(td(rd)) if residual else None, int(relu), None,
+                                          ptr(ws), ctypes.c_size_t(ws.numel()), stream()))
     sync()
     y, mean, invstd, nrm, nrv = npref.batch_norm_train(x, gam, bet, rm, rv, 0.1, 1e-5)
     if residual:

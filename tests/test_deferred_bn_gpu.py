@@ -170,3 +170,23 @@ def test_relu_grad_into_bn_backward(ocl):
             grads.append((xx.grad, m.weight.grad, m.bias.grad))
         for a, b in zip(*grads):
             assert _close(a, b, 1e-4)
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["x".join(map(str, s)) for s in SHAPES])
+def test_identity_bn_add_relu(ocl, shape):
+    """`out += identity; relu_(out)` where identity is the pending batch norm
+    (a downsampling projection): folded with a separate output; identity keeps
+    its own values."""
+    cpu, dev = _bn_pair(shape[1], 60)
+    x, o = _x(shape, 61), _x(shape, 62)
+    ident = cpu(x)
+    out = o.clone()
+    out += ident
+    ref = torch.relu_(out)
+    ident_d = dev(x.to(DEV))
+    out_d = o.to(DEV)
+    out_d += ident_d
+    got = torch.relu_(out_d)
+    assert _close(ref, got)
+    assert _close(ident, ident_d)
+    _check_bn_state(cpu, dev)

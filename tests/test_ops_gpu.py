@@ -664,3 +664,21 @@ def test_layer_norm_rows(ocl, rows, n, affine):
     if affine:
         for pr, pd in ((ref.weight, dev.weight), (ref.bias, dev.bias)):
             assert _diff(pr.grad, pd.grad) <= 1e-5 * max(1.0, pr.grad.abs().sum().item() / n)
+
+
+# max-pool forward bit-exact (values and, through the gradient routing,
+# indices) also with ties (integer inputs), padding, dilation, ceil mode; the
+# backward adds overlapping windows' gradients in its own fixed order
+@pytest.mark.parametrize("k,s,p,d,ceil", [(3, 2, 1, 1, False), (3, 1, 1, 1, False), (2, 2, 0, 1, False),
+                                          (3, 2, 0, 2, True), (5, 3, 2, 1, True)])
+def test_max_pool_ties_dilation_ceil(ocl, k, s, p, d, ceil):
+    g = _gen(50)
+    x = torch.randint(0, 4, (3, 5, 17, 19), generator=g).float()
+    xc, xd = x.clone().requires_grad_(), x.to(DEV).requires_grad_()
+    yc = F.max_pool2d(xc, k, s, p, d, ceil_mode=ceil)
+    yd = F.max_pool2d(xd, k, s, p, d, ceil_mode=ceil)
+    gy = torch.randn(yc.shape, generator=g)
+    yc.backward(gy)
+    yd.backward(gy.to(DEV))
+    assert torch.equal(yc, yd.cpu())
+    assert _diff(xc.grad, xd.grad) <= 1e-5
