@@ -449,6 +449,24 @@ typedef struct pvb2_conv2d_desc {
 } pvb2_conv2d_desc;
 /* which: 0 fwd, 1 bwd data, 2 bwd filter */
 PVB2_API size_t pvb2_conv2d_workspace_size(const pvb2_conv2d_desc* d, int which);
+/* Keeping the staged input between forward and weight gradient: the
+ * tensor-core paths read x as a channels-last copy or as im2col columns,
+ * made in the forward and again in the weight gradient.
+ * pvb2_conv2d_staged_input_bytes gives that copy's size (0 when the path
+ * stages nothing); pvb2_conv2d_fwd_staged leaves it in the caller's `staged`
+ * buffer (*staged_written = 1 when it did), and
+ * pvb2_conv2d_bwd_filter_staged reads it from there instead of staging x
+ * again.  The caller keeps the buffer between the calls and passes it only
+ * while x is unchanged.  The reference staged nothing (its kernels read
+ * NCHW directly, vision_ops.cpp:61-186). */
+PVB2_API size_t pvb2_conv2d_staged_input_bytes(const pvb2_conv2d_desc* d);
+PVB2_API int pvb2_conv2d_fwd_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const float* w,
+                                    const float* b, const pvb2_tensor* y, void* workspace, size_t workspace_bytes,
+                                    float* staged, size_t staged_bytes, int* staged_written, pvb2_stream stream);
+PVB2_API int pvb2_conv2d_bwd_filter_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x,
+                                           const pvb2_tensor* dy, float* dw, float* db, void* workspace,
+                                           size_t workspace_bytes, const float* staged, size_t staged_bytes,
+                                           pvb2_stream stream);
 /* convolution_overrideable, vision_ops.cpp:61-113: y = conv(x, w) + b
  * x [N,C,H,W], w [K,C/g,R,S] contiguous, y [N,K,P,Q]; x/y NCHW-contiguous
  * or channels-last.  b may be NULL. */

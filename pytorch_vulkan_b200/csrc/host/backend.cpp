@@ -346,6 +346,7 @@ c10::Allocator* allocator() { return &g_allocator; }
 REGISTER_ALLOCATOR(c10::DeviceType::PrivateUse1, &g_allocator);
 
 static void empty_cache_all() {
+  clear_staged_inputs();
   for (int d = 0; d < device_count(); ++d) {
     if (!states()[d].ready) continue;
     DeviceScope scope(d);
@@ -798,6 +799,7 @@ PYBIND11_MODULE(_C, m) {
   m.def("impl_synchronize_device", &synchronize_device, "wait for device work (-1 = all devices)");
   m.def("impl_is_bad_fork", []() { return g_bad_fork.load(); });
   m.def("impl_empty_cache", &empty_cache_all, "release cached device blocks");
+  m.def("impl_staged_input_bytes", &staged_input_bytes, "bytes of convolution inputs kept for the weight gradient");
   m.def("impl_enable_profiling", &enable_profiling);
   m.def("impl_start_profiling", &start_profiling);
   m.def("impl_stop_profiling", &stop_profiling);

@@ -98,6 +98,12 @@ bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const a
 // (the batch-norm backward then stores grad_out itself) and clear it
 bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out);
 
+// ------------------------------------------ staged convolution inputs
+// Channels-last / im2col copies of convolution inputs kept from a training
+// forward for the weight gradient (ops_nn.cpp); released by empty_cache.
+void clear_staged_inputs();
+size_t staged_input_bytes();  // bytes the kept copies hold now
+
 // ------------------------------------------------------------- settings
 int math_mode();                 // PVB2_MATH_* for convolution / GEMM
 void set_math_mode(int mode);

@@ -7,6 +7,11 @@
 // torch op pair (max_pool2d_with_indices[_backward]) instead of the
 // reference's autograd override (vision_ops.cpp:353-445), so the indices are
 // the CPU's, bit for bit.
+#include <deque>
+#include <mutex>
+
+#include <ATen/core/grad_mode.h>
+
 #include "ocl.h"
 
 namespace ocl {
@@ -67,6 +72,104 @@ static pvb2_conv2d_desc tconv_desc(const at::Tensor& x, const at::Tensor& w, at:
   return d;
 }
 
+// ------------------------------------------- staged input kept for wgrad
+// The tensor-core convolution reads its input as a channels-last copy (or
+// im2col columns) that it makes on the device, and the weight gradient reads
+// the same copy.  A training forward (grad mode on, weight requiring grad)
+// leaves it in a buffer kept here, keyed by the input's storage, offset,
+// sizes, strides, version counter and the convolution's geometry; the
+// backward that finds a match reads it instead of staging its input again
+// and drops the entry.  Entries also go when their input's storage is freed,
+// oldest first past a byte cap (B200_CONV_STAGE_CACHE_MB, default 4096;
+// 0 turns the cache off), and on empty_cache.  Forward and backward run on
+// the device's one stream, so the buffer is stream-ordered like any
+// workspace.
+namespace {
+struct StagedInput {
+  explicit StagedInput(c10::weak_intrusive_ptr<c10::StorageImpl> s) : storage(std::move(s)) {}
+  c10::weak_intrusive_ptr<c10::StorageImpl> storage;
+  int64_t offset = 0, version = 0;
+  std::vector<int64_t> sizes, strides;
+  pvb2_conv2d_desc d;
+  int device = 0;
+  c10::DataPtr buf;
+  size_t bytes = 0;
+};
+
+std::mutex g_stage_mutex;
+// never destroyed: entries may outlive the allocator at process exit
+std::deque<StagedInput>& staged_inputs() {
+  static auto* q = new std::deque<StagedInput>();
+  return *q;
+}
+size_t g_staged_bytes = 0;
+
+size_t stage_cap() {
+  static const size_t cap = [] {
+    const char* v = getenv("B200_CONV_STAGE_CACHE_MB");
+    const long long mb = v ? atoll(v) : 4096;
+    return mb > 0 ? (size_t)mb << 20 : (size_t)0;
+  }();
+  return cap;
+}
+
+bool same_desc(const pvb2_conv2d_desc& a, const pvb2_conv2d_desc& b) {
+  return a.N == b.N && a.C == b.C && a.H == b.H && a.W == b.W && a.K == b.K && a.R == b.R && a.S == b.S &&
+         a.P == b.P && a.Q == b.Q && a.stride_h == b.stride_h && a.stride_w == b.stride_w && a.pad_h == b.pad_h &&
+         a.pad_w == b.pad_w && a.dil_h == b.dil_h && a.dil_w == b.dil_w && a.groups == b.groups && a.math == b.math;
+}
+
+bool staged_matches(const StagedInput& e, const at::Tensor& x, const pvb2_conv2d_desc& d) {
+  if (e.storage.expired()) return false;
+  return e.storage.lock().get() == x.storage().unsafeGetStorageImpl() && e.offset == x.storage_offset() &&
+         e.version == x._version() && x.sizes().equals(e.sizes) && x.strides().equals(e.strides) &&
+         e.device == (int)x.device().index() && same_desc(e.d, d);
+}
+
+// drop entries whose input is gone, then the oldest until `need` more fits
+void staged_make_room(size_t need) {
+  auto& q = staged_inputs();
+  for (auto it = q.begin(); it != q.end();) {
+    if (it->storage.expired()) {
+      g_staged_bytes -= it->bytes;
+      it = q.erase(it);
+    } else {
+      ++it;
+    }
+  }
+  while (!q.empty() && g_staged_bytes + need > stage_cap()) {
+    g_staged_bytes -= q.front().bytes;
+    q.pop_front();
+  }
+}
+
+// the backward's lookup: hands over the buffer (the entry is dropped)
+c10::DataPtr take_staged_input(const at::Tensor& x, const pvb2_conv2d_desc& d, size_t* bytes) {
+  std::lock_guard<std::mutex> g(g_stage_mutex);
+  auto& q = staged_inputs();
+  for (auto it = q.begin(); it != q.end(); ++it) {
+    if (!staged_matches(*it, x, d)) continue;
+    c10::DataPtr p = std::move(it->buf);
+    *bytes = it->bytes;
+    g_staged_bytes -= it->bytes;
+    q.erase(it);
+    return p;
+  }
+  return c10::DataPtr();
+}
+}  // namespace
+
+size_t staged_input_bytes() {
+  std::lock_guard<std::mutex> g(g_stage_mutex);
+  return g_staged_bytes;
+}
+
+void clear_staged_inputs() {
+  std::lock_guard<std::mutex> g(g_stage_mutex);
+  staged_inputs().clear();
+  g_staged_bytes = 0;
+}
+
 // convolution_overrideable, vision_ops.cpp:61-113
 static at::Tensor convolution(const at::Tensor& input, const at::Tensor& weight, const std::optional<at::Tensor>& bias,
                               at::IntArrayRef stride, at::IntArrayRef padding, at::IntArrayRef dilation,
@@ -89,7 +192,35 @@ static at::Tensor convolution(const at::Tensor& input, const at::Tensor& weight,
     if (y.numel() == 0) return y;
     Workspace ws(pvb2_conv2d_workspace_size(&d, 0), dev);
     pvb2_tensor xd = desc(x), yd = desc(y);
-    OCL_CHECK(pvb2_conv2d_fwd(&d, &xd, w.data_ptr<float>(), b, &yd, ws.get(), ws.bytes, st));
+    const size_t sb = at::GradMode::is_enabled() && weight.requires_grad() && stage_cap() > 0
+                          ? pvb2_conv2d_staged_input_bytes(&d)
+                          : 0;
+    if (sb == 0 || sb > stage_cap()) {
+      OCL_CHECK(pvb2_conv2d_fwd(&d, &xd, w.data_ptr<float>(), b, &yd, ws.get(), ws.bytes, st));
+      return y;
+    }
+    {
+      std::lock_guard<std::mutex> g(g_stage_mutex);
+      staged_make_room(sb);
+    }
+    Workspace staged(sb, dev);
+    int written = 0;
+    OCL_CHECK(pvb2_conv2d_fwd_staged(&d, &xd, w.data_ptr<float>(), b, &yd, ws.get(), ws.bytes,
+                                     (float*)staged.get(), sb, &written, st));
+    if (written) {
+      StagedInput e(x.storage().getWeakStorageImpl());
+      e.offset = x.storage_offset();
+      e.version = x._version();
+      e.sizes = x.sizes().vec();
+      e.strides = x.strides().vec();
+      e.d = d;
+      e.device = dev;
+      e.buf = std::move(staged.ptr);
+      e.bytes = sb;
+      std::lock_guard<std::mutex> g(g_stage_mutex);
+      g_staged_bytes += sb;
+      staged_inputs().push_back(std::move(e));
+    }
     return y;
   }
   pvb2_conv2d_desc d = tconv_desc(x, w, stride, padding, dilation, output_padding, groups);
@@ -129,8 +260,11 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward(
       if (output_mask[1]) gw = empty(w.sizes(), at::kFloat, dev);
       if (output_mask[2]) gb = empty({d.K}, at::kFloat, dev);
       Workspace ws(output_mask[1] ? pvb2_conv2d_workspace_size(&d, 2) : 0, dev);
-      OCL_CHECK(pvb2_conv2d_bwd_filter(&d, &xd, &gyd, output_mask[1] ? gw.data_ptr<float>() : nullptr,
-                                       output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, st));
+      size_t sb = 0;
+      c10::DataPtr staged = output_mask[1] ? take_staged_input(x, d, &sb) : c10::DataPtr();
+      OCL_CHECK(pvb2_conv2d_bwd_filter_staged(&d, &xd, &gyd, output_mask[1] ? gw.data_ptr<float>() : nullptr,
+                                              output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes,
+                                              (const float*)staged.get(), sb, st));
     }
     return {gx, gw, gb};
   }

@@ -16,12 +16,13 @@
 namespace pvb2 {
 
 int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const float* b, float* y, void* ws,
-                size_t ws_bytes, cudaStream_t s, bool* handled);
+                size_t ws_bytes, cudaStream_t s, bool* handled, float* staged, bool* staged_written);
 int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, void* ws,
                      size_t ws_bytes, cudaStream_t s, bool* handled);
 int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* dy, float* dw, void* ws,
-                       size_t ws_bytes, cudaStream_t s, bool* handled);
+                       size_t ws_bytes, cudaStream_t s, bool* handled, const float* staged);
 size_t conv_tc_workspace(const pvb2_conv2d_desc* d, int which);
+size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d);
 
 struct ConvGeom {
   int N, C, H, W, K, R, S, P, Q, sh, sw, ph, pw, dh, dw, G, Cg, Kg;
@@ -350,8 +351,20 @@ size_t pvb2_conv2d_workspace_size(const pvb2_conv2d_desc* d, int which) {
   return need > tc ? need : tc;
 }
 
+size_t pvb2_conv2d_staged_input_bytes(const pvb2_conv2d_desc* d) {
+  if (check_desc(d) != PVB2_OK || d->math != PVB2_MATH_TF32 || is_depthwise(geom(d))) return 0;
+  return conv_tc_staged_bytes(d);
+}
+
 int pvb2_conv2d_fwd(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const float* w, const float* b,
                     const pvb2_tensor* y, void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+  return pvb2_conv2d_fwd_staged(d, x, w, b, y, workspace, workspace_bytes, nullptr, 0, nullptr, stream);
+}
+
+int pvb2_conv2d_fwd_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const float* w, const float* b,
+                           const pvb2_tensor* y, void* workspace, size_t workspace_bytes, float* staged,
+                           size_t staged_bytes, int* staged_written, pvb2_stream stream) {
+  if (staged_written) *staged_written = 0;
   PVB2_TRY(check_desc(d));
   PVB2_TRY(check_t(x, d->N, d->C, d->H, d->W, "input"));
   PVB2_TRY(check_t(y, d->N, d->K, d->P, d->Q, "output"));
@@ -365,8 +378,14 @@ int pvb2_conv2d_fwd(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const float
     return PVB2_OK;
   }
   if (d->math == PVB2_MATH_TF32) {
-    bool handled = false;
-    PVB2_TRY(conv_tc_fwd(d, (const float*)x->data, w, b, (float*)y->data, workspace, workspace_bytes, s, &handled));
+    bool handled = false, written = false;
+    if (staged) {
+      PVB2_CHECK_ARG(staged_bytes >= conv_tc_staged_bytes(d) && ((uintptr_t)staged & 15) == 0,
+                     "conv2d_fwd_staged: staged buffer too small or not 16-byte aligned");
+    }
+    PVB2_TRY(conv_tc_fwd(d, (const float*)x->data, w, b, (float*)y->data, workspace, workspace_bytes, s, &handled,
+                         staged && conv_tc_staged_bytes(d) > 0 ? staged : nullptr, &written));
+    if (staged_written) *staged_written = written ? 1 : 0;
     if (handled) return PVB2_OK;
   }
   ConvFwdProb pb;
@@ -414,6 +433,12 @@ int pvb2_conv2d_bwd_data(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const
 
 int pvb2_conv2d_bwd_filter(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* dy, float* dw,
                            float* db, void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+  return pvb2_conv2d_bwd_filter_staged(d, x, dy, dw, db, workspace, workspace_bytes, nullptr, 0, stream);
+}
+
+int pvb2_conv2d_bwd_filter_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* dy,
+                                  float* dw, float* db, void* workspace, size_t workspace_bytes,
+                                  const float* staged, size_t staged_bytes, pvb2_stream stream) {
   PVB2_TRY(check_desc(d));
   PVB2_TRY(check_t(x, d->N, d->C, d->H, d->W, "input"));
   PVB2_TRY(check_t(dy, d->N, d->K, d->P, d->Q, "grad_output"));
@@ -440,8 +465,13 @@ int pvb2_conv2d_bwd_filter(const pvb2_conv2d_desc* d, const pvb2_tensor* x, cons
   }
   if (d->math == PVB2_MATH_TF32) {
     bool handled = false;
+    if (staged) {
+      PVB2_CHECK_ARG(conv_tc_staged_bytes(d) > 0 && staged_bytes >= conv_tc_staged_bytes(d) &&
+                         ((uintptr_t)staged & 15) == 0,
+                     "conv2d_bwd_filter_staged: staged input does not match this convolution");
+    }
     PVB2_TRY(conv_tc_bwd_filter(d, (const float*)x->data, (const float*)dy->data, dw, workspace, workspace_bytes, s,
-                                &handled));
+                                &handled, staged));
     if (handled) return PVB2_OK;
   }
   const int splits = wgrad_splits(g);

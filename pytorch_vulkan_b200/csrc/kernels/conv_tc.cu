@@ -1318,9 +1318,22 @@ size_t conv_tc_workspace(const pvb2_conv2d_desc* d, int which) {
   return wgrad_layout(d, nullptr).total;
 }
 
+// The input as the forward and weight-gradient launches read it (channels-
+// last copy or im2col columns): its size when this path stages one, else 0.
+// A caller may keep the forward's copy for the weight gradient.
+size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d) {
+  if (!tc_conv_shape_ok(d) || pointwise(d) || strided_pointwise(d)) return 0;
+  if (use_im2col(d)) return (size_t)d->N * d->P * d->Q * im2col_channels(d) * 4;
+  if (!stride_ok_for_boxes(d)) return 0;
+  return (size_t)d->N * d->H * d->W * round4(d->C) * 4;
+}
+
+// `staged` (conv_tc_staged_bytes long, or null): where the staged input goes
+// instead of the workspace; *staged_written says whether it was filled
 int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const float* b, float* y, void* ws,
-                size_t ws_bytes, cudaStream_t s, bool* handled) {
+                size_t ws_bytes, cudaStream_t s, bool* handled, float* staged, bool* staged_written) {
   *handled = false;
+  if (staged_written) *staged_written = false;
   if (!tc_conv_shape_ok(d)) return PVB2_OK;
   const int64_t pq = (int64_t)d->P * d->Q;
   if (pointwise(d)) {
@@ -1339,7 +1352,7 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
     *handled = true;
     return PVB2_OK;
   }
-  float* act = (float*)((char*)ws + l.a);
+  float* act = staged ? staged : (float*)((char*)ws + l.a);
   float* wp = (float*)((char*)ws + l.b);
   if (use_im2col(d)) {
     const int Kc = im2col_channels(d);
@@ -1363,6 +1376,7 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
                           d->stride_w, 0, (int64_t)d->K * pq, pq, d->Q, 1, (float*)((char*)ws + l.part),
                           l.part_bytes, s));
   }
+  if (staged_written) *staged_written = staged != nullptr;
   *handled = true;
   return PVB2_OK;
 }
@@ -1464,8 +1478,9 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
   return PVB2_OK;
 }
 
+// `staged`: the forward's staged copy of this x (conv_tc_fwd), or null
 int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* dy, float* dw, void* ws,
-                       size_t ws_bytes, cudaStream_t s, bool* handled) {
+                       size_t ws_bytes, cudaStream_t s, bool* handled, const float* staged) {
   *handled = false;
   if (!tc_conv_shape_ok(d)) return PVB2_OK;
   WgPlan p;
@@ -1493,9 +1508,9 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
   }
   if (use_im2col(d)) {
     const int Kc = im2col_channels(d), crs = d->C * RS;
-    float* xcol = (float*)ws;
+    float* xcol = staged ? const_cast<float*>(staged) : (float*)ws;
     float* part = (float*)((char*)ws + l.c);
-    PVB2_TRY(im2col(d, x, xcol, s));
+    if (!staged) PVB2_TRY(im2col(d, x, xcol, s));
     PVB2_TRY(run_im_wgrad(xcol, Kc, dy, d->N, d->K, (int64_t)d->P * d->Q, p, part, s));
     // partials [sp][k][j] -> dW[k][j] for the crs real columns
     PVB2_TRY(wgrad_reduce(part, p.splits, 1, Kc, d->K, crs, d->K, dw, 1, crs, 0, s));
@@ -1504,12 +1519,12 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
   }
   if (!stride_ok_for_boxes(d)) return PVB2_OK;
   const int Kp = round4(d->K);
-  float* xn = (float*)((char*)ws + l.a);
+  float* xn = staged ? const_cast<float*>(staged) : (float*)((char*)ws + l.a);
   float* dyn = (float*)((char*)ws + l.b);
   float* part = (float*)((char*)ws + l.c);
   PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
   const int Cp = round4(d->C);
-  PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
+  if (!staged) PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
   PVB2_TRY(run_wgrad(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h, d->stride_w,
                      p, part, s));
   // partials [sp][rs][c][k] -> dW[k][c][rs]
