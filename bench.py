@@ -289,7 +289,7 @@ def run_ours(a):
                 top = r["section"] == ""
                 if top:
                     per_op[r["kernel"]] = per_op.get(r["kernel"], 0.0) + d
-                if top and r["kernel"] in ("convolution", "convolution_backward"):
+                if top and r["kernel"].startswith("convolution"):  # + the dgrad launches that also form an add
                     conv_ms += d
                     n_conv += 1
         peaks = {}

@@ -459,6 +459,21 @@ PVB2_API size_t pvb2_conv2d_workspace_size(const pvb2_conv2d_desc* d, int which)
  * again.  The caller keeps the buffer between the calls and passes it only
  * while x is unchanged.  The reference staged nothing (its kernels read
  * NCHW directly, vision_ops.cpp:61-186). */
+/* Input gradient accumulated into another gradient in one pass:
+ * dx = conv2d_bwd_data(dy, w) + addend, the sum formed in the dgrad's
+ * epilogue (a residual block's first convolution, whose input gradient the
+ * autograd engine adds to the identity branch's; the reference ran the
+ * dgrad, vision_ops.cpp:116-186, then its add, pointwise_ops.cpp:133-172).
+ * Offered for 1x1 stride-1 convolutions on the TF32 path with 16-byte
+ * aligned operands: pvb2_conv2d_bwd_data_acc_ok says whether the pointers
+ * and descriptor qualify (1) or not (0), and pvb2_conv2d_bwd_data_acc
+ * returns PVB2_ERR_UNSUPPORTED when they do not.  addend may be dx itself
+ * (an in-place accumulation); otherwise it must not overlap dx, dy or w.
+ * Each element is dgrad + addend rounded once, as the separate add gives. */
+PVB2_API int pvb2_conv2d_bwd_data_acc_ok(const pvb2_conv2d_desc* d, const void* dy, const float* w,
+                                         const void* dx, const void* addend);
+PVB2_API int pvb2_conv2d_bwd_data_acc(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const float* w,
+                                      const pvb2_tensor* dx, const pvb2_tensor* addend, pvb2_stream stream);
 PVB2_API size_t pvb2_conv2d_staged_input_bytes(const pvb2_conv2d_desc* d);
 PVB2_API int pvb2_conv2d_fwd_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const float* w,
                                     const float* b, const pvb2_tensor* y, void* workspace, size_t workspace_bytes,

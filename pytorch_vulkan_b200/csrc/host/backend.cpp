@@ -145,8 +145,8 @@ void after_op(int d) {
 }
 
 DeviceScope::DeviceScope(const at::Tensor& t) : DeviceScope((int)t.device().index()) {}
-DeviceScope::DeviceScope(int device) {
-  flush_deferred();
+DeviceScope::DeviceScope(int device, bool flush) {
+  if (flush) flush_deferred();
   prev = current_device();
   changed = device >= 0 && device != prev;
   if (changed) set_device(device);

@@ -16,7 +16,16 @@
 // pending, and when the next op is the backward of the batch norm that fed
 // that ReLU, its first pass forms the gradient from the ReLU output on the
 // fly (pvb2_batch_norm_bwd_relu), still storing it to the op's output tensor.
-// B200_DEFER_BN=0 turns both deferrals off.
+//
+// Input gradients of 1x1 stride-1 convolutions (a residual block's first
+// convolution) are left pending as well: when the next op adds that gradient
+// to another (the autograd engine summing the identity branch's gradient
+// with it), the dgrad's epilogue forms the sum (pvb2_conv2d_bwd_data_acc)
+// and the gradient itself is not written.  A record of it stays behind,
+// holding its storage only weakly: the next flush writes the gradient after
+// all if its storage is still alive (someone kept it), and otherwise (the
+// engine dropped it after the add, the usual case) just forgets it.
+// B200_DEFER_BN=0 turns all three deferrals off.
 #include <cstdlib>
 #include <mutex>
 #include <optional>
@@ -45,9 +54,21 @@ struct PendingThr {  // grad_input = self <= 0 ? 0 : grad
   int device = 0;
 };
 
+struct PendingDgrad {  // gx = conv2d_bwd_data(gy, w)
+  pvb2_conv2d_desc d;
+  at::Tensor gy, w, gx;
+  pvb2_stream stream = nullptr;
+  int device = 0;
+  // after a fused add: gx is not held, only its storage weakly, with its
+  // descriptor; written at the next flush if that storage is still alive
+  std::optional<c10::weak_intrusive_ptr<c10::StorageImpl>> unwritten;
+  pvb2_tensor gx_desc;
+};
+
 std::mutex g_mutex;
 std::optional<PendingBn> g_pending;
 std::optional<PendingThr> g_thr;
+std::optional<PendingDgrad> g_dgrad;
 std::atomic<bool> g_any{false};
 thread_local bool t_flushing = false;
 
@@ -81,14 +102,37 @@ void launch_thr(PendingThr& t) {
   OCL_CHECK(pvb2_binary(PVB2_BIN_THRESHOLD_BWD, &od, &gd, &sd, 0.0, 0.0, PVB2_F32, t.stream));
 }
 
-std::pair<std::optional<PendingBn>, std::optional<PendingThr>> take() {
+// dx: where the gradient goes (gx, or the sum's output when addend is set)
+void launch_dgrad(PendingDgrad& p, const at::Tensor& dx, const at::Tensor& addend) {
+  DeviceScope scope(p.device);
+  OCL_OP(addend.defined() ? "convolution_backward+add" : "convolution_backward", p.device);
+  const pvb2_tensor gyd = desc(p.gy), dxd = desc(dx);
+  if (addend.defined()) {
+    const pvb2_tensor ad = desc(addend);
+    OCL_CHECK(pvb2_conv2d_bwd_data_acc(&p.d, &gyd, p.w.data_ptr<float>(), &dxd, &ad, p.stream));
+    return;
+  }
+  Workspace ws(pvb2_conv2d_workspace_size(&p.d, 1), p.device);
+  OCL_CHECK(pvb2_conv2d_bwd_data(&p.d, &gyd, p.w.data_ptr<float>(), &dxd, ws.get(), ws.bytes, p.stream));
+}
+
+struct Taken {
+  std::optional<PendingBn> bn;
+  std::optional<PendingThr> thr;
+  std::optional<PendingDgrad> dgrad;
+};
+
+Taken take() {
   std::lock_guard<std::mutex> g(g_mutex);
-  std::pair<std::optional<PendingBn>, std::optional<PendingThr>> p{std::move(g_pending), std::move(g_thr)};
+  Taken t{std::move(g_pending), std::move(g_thr), std::move(g_dgrad)};
   g_pending.reset();
   g_thr.reset();
+  g_dgrad.reset();
   g_any.store(false, std::memory_order_release);
-  return p;
+  return t;
 }
+
+bool anything_pending() { return g_pending.has_value() || g_thr.has_value() || g_dgrad.has_value(); }
 
 }  // namespace
 
@@ -97,8 +141,20 @@ void flush_deferred() {
   t_flushing = true;
   try {
     auto p = take();
-    if (p.first) launch(*p.first, p.first->residual.defined() ? "native_batch_norm+add_" : "native_batch_norm");
-    if (p.second) launch_thr(*p.second);
+    if (p.bn) launch(*p.bn, p.bn->residual.defined() ? "native_batch_norm+add_" : "native_batch_norm");
+    if (p.thr) launch_thr(*p.thr);
+    if (p.dgrad && !p.dgrad->unwritten) launch_dgrad(*p.dgrad, p.dgrad->gx, at::Tensor());
+    if (p.dgrad && p.dgrad->unwritten) {
+      const c10::intrusive_ptr<c10::StorageImpl> st = p.dgrad->unwritten->lock();
+      if (st && st->data() == p.dgrad->gx_desc.data) {  // kept by someone: write it now
+        PendingDgrad& q = *p.dgrad;
+        DeviceScope scope(q.device);
+        OCL_OP("convolution_backward", q.device);
+        const pvb2_tensor gyd = desc(q.gy);
+        Workspace ws(pvb2_conv2d_workspace_size(&q.d, 1), q.device);
+        OCL_CHECK(pvb2_conv2d_bwd_data(&q.d, &gyd, q.w.data_ptr<float>(), &q.gx_desc, ws.get(), ws.bytes, q.stream));
+      }
+    }
   } catch (...) {
     t_flushing = false;
     throw;
@@ -133,7 +189,7 @@ bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optiona
   for (;;) {
     flush_deferred();  // one pending pass at a time (another thread may have left one)
     std::lock_guard<std::mutex> g(g_mutex);
-    if (g_pending.has_value() || g_thr.has_value()) continue;
+    if (anything_pending()) continue;
     g_pending = std::move(p);
     g_any.store(true, std::memory_order_release);
     return true;
@@ -197,7 +253,7 @@ bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const a
   for (;;) {
     flush_deferred();
     std::lock_guard<std::mutex> g(g_mutex);
-    if (g_pending.has_value() || g_thr.has_value()) continue;
+    if (anything_pending()) continue;
     g_thr = std::move(t);
     g_any.store(true, std::memory_order_release);
     return true;
@@ -213,6 +269,75 @@ bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above,
   g_thr.reset();
   g_any.store(false, std::memory_order_release);
   return true;
+}
+
+bool conv_dgrad_deferrable(const pvb2_conv2d_desc& d, const at::Tensor& gy, const at::Tensor& w, const at::Tensor& gx) {
+  return defer_enabled() && gx.numel() > 0 &&
+         pvb2_conv2d_bwd_data_acc_ok(&d, gy.data_ptr(), w.data_ptr<float>(), gx.data_ptr(), gx.data_ptr()) == 1;
+}
+
+void defer_conv_dgrad(const pvb2_conv2d_desc& d, const at::Tensor& gy, const at::Tensor& w, const at::Tensor& gx) {
+  PendingDgrad p;
+  p.d = d;
+  p.gy = gy;
+  p.w = w;
+  p.gx = gx;
+  p.device = (int)gx.device().index();
+  p.stream = stream_for(p.device);
+  for (;;) {
+    flush_deferred();
+    std::lock_guard<std::mutex> g(g_mutex);
+    if (anything_pending()) continue;
+    g_dgrad = std::move(p);
+    g_any.store(true, std::memory_order_release);
+    return;
+  }
+}
+
+bool fuse_deferred_dgrad_add(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha,
+                             const at::Tensor& out) {
+  if (!g_any.load(std::memory_order_acquire)) return false;
+  std::optional<PendingDgrad> p;
+  at::Tensor addend;
+  {
+    std::lock_guard<std::mutex> g(g_mutex);
+    if (!g_dgrad || alpha.isComplex() || alpha.toDouble() != 1.0) return false;
+    const PendingDgrad& q = *g_dgrad;
+    const bool gx_self = same_tensor(self, q.gx), gx_other = same_tensor(other, q.gx);
+    if (gx_self == gx_other) return false;  // neither operand, or gx + gx
+    addend = gx_self ? other : self;
+    for (const at::Tensor* t : {static_cast<const at::Tensor*>(&addend), &out})
+      if (!is_ocl(*t) || t->device() != q.gx.device() || t->scalar_type() != at::kFloat || !t->is_contiguous() ||
+          !t->sizes().equals(q.gx.sizes()))
+        return false;
+    // the sum goes to `out`: gx itself (an in-place add into it) or apart from it
+    if (!same_tensor(out, q.gx) && out.is_alias_of(q.gx)) return false;
+    // the addend is read where the sum is stored: the same tensor or apart
+    if (!same_tensor(addend, out) && addend.is_alias_of(out)) return false;
+    if (out.is_alias_of(q.gy) || out.is_alias_of(q.w)) return false;
+    if (pvb2_conv2d_bwd_data_acc_ok(&q.d, q.gy.data_ptr(), q.w.data_ptr<float>(), out.data_ptr(),
+                                    addend.data_ptr()) != 1)
+      return false;
+    p = std::move(g_dgrad);
+    g_dgrad.reset();
+    g_any.store(false, std::memory_order_release);
+  }
+  launch_dgrad(*p, out, addend);
+  if (same_tensor(out, p->gx)) return true;
+  // gx was not written: leave the record that writes it if it is still
+  // alive at the next flush (installed after the launch, whose own device
+  // entry flushes)
+  p->gx_desc = desc(p->gx);
+  p->unwritten = p->gx.storage().getWeakStorageImpl();
+  p->gx = at::Tensor();
+  for (;;) {
+    flush_deferred();  // one pending record at a time (another thread may have left one)
+    std::lock_guard<std::mutex> g(g_mutex);
+    if (anything_pending()) continue;
+    g_dgrad = std::move(p);
+    g_any.store(true, std::memory_order_release);
+    return true;
+  }
 }
 
 }  // namespace ocl

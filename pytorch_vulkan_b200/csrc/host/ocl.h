@@ -36,7 +36,10 @@ struct DeviceScope {
   int prev;
   bool changed;
   explicit DeviceScope(const at::Tensor& t);
-  explicit DeviceScope(int device);
+  // flush = false: only makes `device` current, leaving deferred work
+  // pending (allocations, which neither launch work nor read memory: every
+  // pending launch holds references to the tensors it touches)
+  explicit DeviceScope(int device, bool flush = true);
   ~DeviceScope();
 };
 
@@ -97,6 +100,14 @@ bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const a
 // when the pending threshold_backward wrote grad_out: hand over its inputs
 // (the batch-norm backward then stores grad_out itself) and clear it
 bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out);
+// input gradient of a convolution whose dgrad can also form a sum
+// (pvb2_conv2d_bwd_data_acc_ok), left pending so that a following add of it
+// joins the dgrad's epilogue
+bool conv_dgrad_deferrable(const pvb2_conv2d_desc& d, const at::Tensor& gy, const at::Tensor& w, const at::Tensor& gx);
+void defer_conv_dgrad(const pvb2_conv2d_desc& d, const at::Tensor& gy, const at::Tensor& w, const at::Tensor& gx);
+// true when `out = self + other * alpha` was formed by the pending dgrad
+bool fuse_deferred_dgrad_add(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha,
+                             const at::Tensor& out);
 
 // ------------------------------------------ staged convolution inputs
 // Channels-last / im2col copies of convolution inputs kept from a training

@@ -250,8 +250,12 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward(
   if (!transposed) {
     pvb2_conv2d_desc d = conv_desc(x, w, stride, padding, dilation, groups);
     pvb2_tensor xd = desc(x), gyd = desc(gy);
+    bool dgrad_later = false;  // left pending after the weight gradient (deferred.cpp)
     if (output_mask[0]) {
       gx = empty(x.sizes(), at::kFloat, dev);
+      dgrad_later = conv_dgrad_deferrable(d, gy, w, gx);
+    }
+    if (output_mask[0] && !dgrad_later) {
       Workspace ws(pvb2_conv2d_workspace_size(&d, 1), dev);
       pvb2_tensor gxd = desc(gx);
       OCL_CHECK(pvb2_conv2d_bwd_data(&d, &gyd, w.data_ptr<float>(), &gxd, ws.get(), ws.bytes, st));
@@ -266,6 +270,7 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward(
                                               output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes,
                                               (const float*)staged.get(), sb, st));
     }
+    if (dgrad_later) defer_conv_dgrad(d, gy, w, gx);
     return {gx, gw, gb};
   }
   // transposed: forward was y = dgrad(x); so dx = conv_fwd(dy), dw = wgrad(input=dy, grad=x)

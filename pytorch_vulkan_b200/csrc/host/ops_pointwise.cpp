@@ -82,7 +82,9 @@ static int common_compute(const at::Tensor& a, const at::Tensor& b) {
   }
 
 // add.out / sub.out: pointwise_ops.cpp:133-172, :206-210
+// (or formed by a pending convolution dgrad whose result is one operand)
 static at::Tensor& add_out(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha, at::Tensor& out) {
+  if (fuse_deferred_dgrad_add(self, other, alpha, out)) return out;
   return binary_out(PVB2_BIN_ADD, self, other, out, sc(alpha), 0.0, arith_compute(out), "add.out");
 }
 // add_.Tensor: in place through add.out (out = self), or folded into a

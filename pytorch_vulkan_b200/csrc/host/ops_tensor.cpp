@@ -80,7 +80,7 @@ pvb2_tensor desc_expanded(const at::Tensor& t, c10::IntArrayRef sizes) {
 }
 
 at::Tensor empty(c10::IntArrayRef sizes, c10::ScalarType dtype, int device, c10::MemoryFormat mf) {
-  DeviceScope scope(device);
+  DeviceScope scope(device, /*flush=*/false);
   c10::DispatchKeySet ks(c10::DispatchKey::PrivateUse1);
   return at::detail::empty_generic(sizes, allocator(), ks, dtype, mf);
 }
@@ -88,7 +88,7 @@ at::Tensor empty(c10::IntArrayRef sizes, c10::ScalarType dtype, int device, c10:
 at::Tensor empty_like_dev(const at::Tensor& t) { return empty(t.sizes(), t.scalar_type(), t.device().index()); }
 
 at::Tensor empty_strided_dev(c10::IntArrayRef sizes, c10::IntArrayRef strides, c10::ScalarType dtype, int device) {
-  DeviceScope scope(device);
+  DeviceScope scope(device, /*flush=*/false);
   c10::DispatchKeySet ks(c10::DispatchKey::PrivateUse1);
   return at::detail::empty_strided_generic(sizes, strides, allocator(), ks, dtype);
 }

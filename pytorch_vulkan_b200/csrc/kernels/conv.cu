@@ -23,6 +23,10 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
                        size_t ws_bytes, cudaStream_t s, bool* handled, const float* staged);
 size_t conv_tc_workspace(const pvb2_conv2d_desc* d, int which);
 size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d);
+bool conv_tc_bwd_data_acc_ok(const pvb2_conv2d_desc* d, const void* dy, const void* w, const void* dx,
+                             const void* addend);
+int conv_tc_bwd_data_acc(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, const float* addend,
+                         cudaStream_t s);
 
 struct ConvGeom {
   int N, C, H, W, K, R, S, P, Q, sh, sw, ph, pw, dh, dw, G, Cg, Kg;
@@ -429,6 +433,25 @@ int pvb2_conv2d_bwd_data(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const
   pb.w = w;
   pb.dx = (float*)dx->data;
   return launch_igemm_simt(pb, s);
+}
+
+int pvb2_conv2d_bwd_data_acc_ok(const pvb2_conv2d_desc* d, const void* dy, const float* w, const void* dx,
+                                 const void* addend) {
+  if (check_desc(d) != PVB2_OK || is_depthwise(geom(d))) return 0;
+  return conv_tc_bwd_data_acc_ok(d, dy, w, dx, addend) ? 1 : 0;
+}
+
+int pvb2_conv2d_bwd_data_acc(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const float* w, const pvb2_tensor* dx,
+                             const pvb2_tensor* addend, pvb2_stream stream) {
+  PVB2_TRY(check_desc(d));
+  PVB2_TRY(check_t(dy, d->N, d->K, d->P, d->Q, "grad_output"));
+  PVB2_TRY(check_t(dx, d->N, d->C, d->H, d->W, "grad_input"));
+  PVB2_TRY(check_t(addend, d->N, d->C, d->H, d->W, "addend"));
+  if (!pvb2_conv2d_bwd_data_acc_ok(d, dy->data, w, dx->data, addend->data))
+    return fail(PVB2_ERR_UNSUPPORTED, "conv2d_bwd_data_acc: not a tensor-core 1x1 stride-1 convolution");
+  if ((int64_t)d->N * d->C * d->H * d->W == 0) return PVB2_OK;
+  return conv_tc_bwd_data_acc(d, (const float*)dy->data, w, (float*)dx->data, (const float*)addend->data,
+                              as_stream(stream));
 }
 
 int pvb2_conv2d_bwd_filter(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* dy, float* dw,

@@ -95,6 +95,8 @@ struct ConvTcArgs {
   int epi, ebq, ebp;                  // EpiMode and its box extents
   float* out;
   const float* bias;
+  // pointwise dgrad only: dX = dgrad + addend (same NCHW layout as dX; may be dX itself)
+  const float* addend;
 };
 
 // Ring depth: as many stages as fit in 192 KB (8 at BN = 64, 6 at 128, 4 at
@@ -117,6 +119,35 @@ struct ConvSmem {
 static_assert(ConvSmem<256>::STAGES >= cProducers && ConvSmem<64>::TOTAL + 1024 <= 232448 && ConvSmem<128>::TOTAL + 1024 <= 232448 &&
                   ConvSmem<256>::TOTAL + 1024 <= 232448,
               "conv tile does not fit in shared memory");
+
+// The addend's 32 x 32 box (pixels bx.., channels k0..) of image n, one
+// 128-byte run per channel; indices past the plane or the channels are
+// clamped to the box's last valid pixel / channel (read, then masked off by
+// the caller), so the 32 loads carry no branches and issue back to back.
+// Every address read lies in the box this warp stores next, so an addend
+// that is the output itself is read before it is overwritten.
+__device__ __forceinline__ void load_addend_chunk(const ConvTcArgs& a, int n, int bx, int k0, int lane,
+                                                  float (&pre)[32]) {
+  const int px = min(bx + lane, a.Q - 1);
+  const float* ad = a.addend + (int64_t)n * a.Kout * a.Q + px;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) pre[j] = ad[(int64_t)min(k0 + j, a.Kout - 1) * a.Q];
+}
+
+// L2 prefetch of a warp's BN-channel addend box (pixels bx..bx+31 of image
+// n): lane j takes channel rows j, j + 32, ...; a 32-pixel run may straddle
+// two 128-byte lines, so both ends are fetched.  Clamped like the loads.
+template <int BN>
+__device__ __forceinline__ void prefetch_addend_l2(const ConvTcArgs& a, int n, int bx, int k0, int lane) {
+  const float* img = a.addend + (int64_t)n * a.Kout * a.Q;
+  const int p0 = min(bx, a.Q - 1), p1 = min(bx + 31, a.Q - 1);
+#pragma unroll
+  for (int c = 0; c < BN / 32; ++c) {
+    const float* row = img + (int64_t)min(k0 + c * 32 + lane, a.Kout - 1) * a.Q;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(row + p0));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(row + p1));
+  }
+}
 
 template <int BN, int MODE>
 __global__ void __launch_bounds__(cThreads, 1)
@@ -322,6 +353,24 @@ __global__ void __launch_bounds__(cThreads, 1)
     for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t aph = (local >> 1) & 1;
+      // pointwise dgrad with an addend: its first chunk is loaded before
+      // the accumulator is ready, each next one while a chunk is stored
+      float pre[32];
+      if (PW && a.addend) {
+        const int slot = (tile / a.kt) * 4 + quarter;
+        if (slot < a.slots) {
+          const int n = slot / a.hwb;
+          load_addend_chunk(a, n, (slot - n * a.hwb) * 32, (tile % a.kt) * BN, lane, pre);
+        }
+        // and the whole of this warp's box of the next tile goes to L2 now,
+        // a tile ahead, so the per-chunk loads above find it there
+        const int next = tile + gridDim.x;
+        const int slot2 = (next / a.kt) * 4 + quarter;
+        if (next < total_tiles && slot2 < a.slots) {
+          const int n2 = slot2 / a.hwb;
+          prefetch_addend_l2<BN>(a, n2, (slot2 - n2 * a.hwb) * 32, (next % a.kt) * BN, lane);
+        }
+      }
       if (!mbar_wait(&acc_full[buf], aph, abort)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN;
@@ -374,6 +423,13 @@ __global__ void __launch_bounds__(cThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j)
                 if (k0 + j < a.Kout) v[j] += a.bias[k0 + j];
+            }
+            if (PW && a.addend) {
+              // a gradient accumulated into this one (prefetched in `pre`)
+              const bool px_ok = bx + lane < a.Q;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += (px_ok && k0 + j < a.Kout) ? pre[j] : 0.0f;
+              if (c + 1 < BN / 32 && k0 + 32 < a.Kout) load_addend_chunk(a, bn, bx, k0 + 32, lane, pre);
             }
             // boxes alternate per issued store, so the store that last used
             // this box is the one before the most recent: wait until it has read it
@@ -939,7 +995,7 @@ static int run_fwd_like(const float* act, const float* wpacked, const float* bia
 // Pointwise dgrad (transpose = true):    dX[n, c, hw] = sum_k W[k, c] dY[n, k, hw].
 // src: [N, Cs, hw]; dst: [N, Cd, hw]; w: [K][C] with (Cs, Cd) = (C, K) or (K, C).
 static int run_pointwise(const float* src, const float* w, const float* bias, float* dst, int N, int C, int K,
-                         int64_t hw, bool transpose, cudaStream_t s) {
+                         int64_t hw, bool transpose, cudaStream_t s, const float* addend = nullptr) {
   const int Cs = transpose ? K : C, Cd = transpose ? C : K;
   const int BN = bn_for(Cd);
   CUtensorMap ma, mb, mc;
@@ -966,6 +1022,7 @@ static int run_pointwise(const float* src, const float* w, const float* bias, fl
   a.epi = kEpiSlots;
   a.out = dst;
   a.bias = bias;
+  a.addend = addend;
   if (transpose) return launch_bn<kPwDgrad>(BN, ma, mb, mc, a, s);
   return launch_bn<kPwFwd>(BN, ma, mb, mc, a, s);
 }
@@ -1379,6 +1436,19 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
   if (staged_written) *staged_written = staged != nullptr;
   *handled = true;
   return PVB2_OK;
+}
+
+// dX = dgrad + addend in the dgrad's own epilogue, for the 1x1 stride-1
+// convolutions whose dgrad is a pointwise GEMM (a residual block's first
+// convolution, whose input gradient is summed with the identity branch's)
+bool conv_tc_bwd_data_acc_ok(const pvb2_conv2d_desc* d, const void* dy, const void* w, const void* dx,
+                             const void* addend) {
+  return tc_conv_shape_ok(d) && pointwise(d) && aligned16(dy) && aligned16(w) && aligned16(dx) && aligned16(addend);
+}
+
+int conv_tc_bwd_data_acc(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, const float* addend,
+                         cudaStream_t s) {
+  return run_pointwise(dy, w, nullptr, dx, d->N, d->C, d->K, (int64_t)d->H * d->W, true, s, addend);
 }
 
 static int pos_mod(int a, int m) { return ((a % m) + m) % m; }
