@@ -79,15 +79,18 @@ static pvb2_conv2d_desc tconv_desc(const at::Tensor& x, const at::Tensor& w, at:
 // leaves it in a buffer kept here, keyed by the input's storage, offset,
 // sizes, strides, version counter and the convolution's geometry; the
 // backward that finds a match reads it instead of staging its input again
-// and drops the entry.  Entries also go when their input's storage is freed,
-// oldest first past a byte cap (B200_CONV_STAGE_CACHE_MB, default 4096;
-// 0 turns the cache off), and on empty_cache.  Forward and backward run on
-// the device's one stream, so the buffer is stream-ordered like any
-// workspace.
+// and drops the entry.  Entries also go when their input's storage is freed
+// or the input is modified (its version counter moves), oldest first past a
+// byte cap (B200_CONV_STAGE_CACHE_MB, default 4096;
+// 0 turns the cache off), and on empty_cache.  The autograd engine runs a
+// backward on the stream its forward used, so the buffer is written and read
+// in that stream's order, like any workspace.
 namespace {
 struct StagedInput {
-  explicit StagedInput(c10::weak_intrusive_ptr<c10::StorageImpl> s) : storage(std::move(s)) {}
+  StagedInput(c10::weak_intrusive_ptr<c10::StorageImpl> s, c10::VariableVersion v)
+      : storage(std::move(s)), vc(std::move(v)) {}
   c10::weak_intrusive_ptr<c10::StorageImpl> storage;
+  c10::VariableVersion vc;  // the input's version counter (shared, not the tensor)
   int64_t offset = 0, version = 0;
   std::vector<int64_t> sizes, strides;
   pvb2_conv2d_desc d;
@@ -126,11 +129,12 @@ bool staged_matches(const StagedInput& e, const at::Tensor& x, const pvb2_conv2d
          e.device == (int)x.device().index() && same_desc(e.d, d);
 }
 
-// drop entries whose input is gone, then the oldest until `need` more fits
+// drop entries whose input is gone or has changed since (they can never
+// match again), then the oldest until `need` more fits
 void staged_make_room(size_t need) {
   auto& q = staged_inputs();
   for (auto it = q.begin(); it != q.end();) {
-    if (it->storage.expired()) {
+    if (it->storage.expired() || (int64_t)it->vc.current_version() != it->version) {
       g_staged_bytes -= it->bytes;
       it = q.erase(it);
     } else {
@@ -192,7 +196,8 @@ static at::Tensor convolution(const at::Tensor& input, const at::Tensor& weight,
     if (y.numel() == 0) return y;
     Workspace ws(pvb2_conv2d_workspace_size(&d, 0), dev);
     pvb2_tensor xd = desc(x), yd = desc(y);
-    const size_t sb = at::GradMode::is_enabled() && weight.requires_grad() && stage_cap() > 0
+    const size_t sb = at::GradMode::is_enabled() && weight.requires_grad() && stage_cap() > 0 &&
+                              x.unsafeGetTensorImpl()->version_counter().enabled()
                           ? pvb2_conv2d_staged_input_bytes(&d)
                           : 0;
     if (sb == 0 || sb > stage_cap()) {
@@ -208,7 +213,7 @@ static at::Tensor convolution(const at::Tensor& input, const at::Tensor& weight,
     OCL_CHECK(pvb2_conv2d_fwd_staged(&d, &xd, w.data_ptr<float>(), b, &yd, ws.get(), ws.bytes,
                                      (float*)staged.get(), sb, &written, st));
     if (written) {
-      StagedInput e(x.storage().getWeakStorageImpl());
+      StagedInput e(x.storage().getWeakStorageImpl(), x.unsafeGetTensorImpl()->version_counter());
       e.offset = x.storage_offset();
       e.version = x._version();
       e.sizes = x.sizes().vec();

@@ -176,6 +176,12 @@ def test_autograd_cache_ignores_changed_or_freed_inputs(ocl):
         b = torch.randn(2, 8, 20, 20).to(DEV)
         conv(b)
         assert p._C.impl_staged_input_bytes() == kept
+        # an input modified in place after its forward: its copy can never
+        # be used again and goes on the next forward
+        b.add_(1.0)
+        c = torch.randn(2, 8, 20, 20).to(DEV)
+        conv(c)
+        assert p._C.impl_staged_input_bytes() == kept
         torch.ocl.empty_cache()
         assert p._C.impl_staged_input_bytes() == 0
     finally:

@@ -682,3 +682,39 @@ def test_max_pool_ties_dilation_ceil(ocl, k, s, p, d, ceil):
     yd.backward(gy.to(DEV))
     assert torch.equal(yc, yd.cpu())
     assert _diff(xc.grad, xd.grad) <= 1e-5
+
+
+def test_copy_stream_pipeline(ocl):
+    """Host-to-device copies on a second stream ordered against compute on
+    the current one with events: the pipeline bench.py's end-to-end figure
+    uses (each batch copied while the previous step computes)."""
+    xs = [torch.randn(4, 3, 64, 64, generator=_gen(s)).pin_memory() for s in range(4)]
+    bufs = [torch.empty(4, 3, 64, 64, device=DEV) for _ in range(2)]
+    copy_s = torch.Stream(device=DEV)
+    ready = [torch.Event(device=DEV) for _ in range(2)]
+    free = [torch.Event(device=DEV) for _ in range(2)]
+    conv = nn.Conv2d(3, 8, 3, padding=1).to(DEV)
+    ref = nn.Conv2d(3, 8, 3, padding=1)
+    ref.load_state_dict({k: v.cpu() for k, v in conv.state_dict().items()})
+
+    def load(i):
+        with copy_s:
+            if i >= 2:
+                free[i % 2].wait()
+            bufs[i % 2].copy_(xs[i], non_blocking=True)
+            ready[i % 2].record()
+
+    load(0)
+    outs = []
+    for i in range(len(xs)):
+        ready[i % 2].wait()
+        with torch.no_grad():
+            y = conv(bufs[i % 2]).sum((1, 2, 3))
+        free[i % 2].record()
+        if i + 1 < len(xs):
+            load(i + 1)
+        outs.append(y.cpu())
+    for i, x in enumerate(xs):
+        with torch.no_grad():
+            r = ref(x).sum((1, 2, 3))
+        assert (outs[i] - r).abs().max().item() <= 1e-2 * r.abs().max().item() + 1e-3
