@@ -506,23 +506,35 @@ __global__ void __launch_bounds__(cThreads, 1)
 
 // ------------------------------------------------------ layout kernels
 // x [N, C, HW] -> y [N, HW, Cp], channels C..Cp-1 zero
-__global__ void nchw_to_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int C, int Cp, int64_t HW) {
-  __shared__ float tile[32][33];
-  const int64_t n = blockIdx.z;
-  const int64_t p0 = (int64_t)blockIdx.x * 32;
+// Same transpose for any HW (7x7 planes) over the flattened pixel index
+// g = n * HW + p: 64-pixel x 32-channel tiles run over the images back to
+// back, so a 49-pixel plane leaves no part-empty tile.  A warp loads 32
+// consecutive pixels of one channel (one run, split at most once at an image
+// boundary) and stores 32 consecutive channels of one pixel.
+__global__ void __launch_bounds__(256) nchw_to_nhwc_flat_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                                                int C, int Cp, int64_t HW, int64_t pixels) {
+  __shared__ float tile[32][64 + 1];  // odd pitch: the column reads below hit 32 banks
+  const int64_t g0 = (int64_t)blockIdx.x * 64;
   const int c0 = blockIdx.y * 32;
-  const float* xn = x + n * C * HW;
-  float* yn = y + n * HW * Cp;
-  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-    const int c = c0 + j;
-    const int64_t p = p0 + threadIdx.x;
-    tile[j][threadIdx.x] = (c < C && p < HW) ? xn[(int64_t)c * HW + p] : 0.f;
+  const int pl = threadIdx.x & 63;
+  const int64_t g = g0 + pl;
+  const bool gv = g < pixels;
+  int64_t base = 0;
+  if (gv) {
+    const int64_t n = g / HW;
+    base = n * C * HW + (g - n * HW);
+  }
+#pragma unroll
+  for (int k = threadIdx.x >> 6; k < 32; k += 4) {
+    const int c = c0 + k;
+    tile[k][pl] = (gv && c < C) ? __ldg(x + base + (int64_t)c * HW) : 0.f;
   }
   __syncthreads();
-  for (int j = threadIdx.y; j < 32; j += blockDim.y) {
-    const int64_t p = p0 + j;
-    const int c = c0 + threadIdx.x;
-    if (p < HW && c < Cp) yn[p * Cp + c] = tile[threadIdx.x][j];
+  const int cl = threadIdx.x & 31;
+#pragma unroll
+  for (int k = threadIdx.x >> 5; k < 64; k += 8) {
+    const int64_t gp = g0 + k;
+    if (gp < pixels && c0 + cl < Cp) y[gp * Cp + c0 + cl] = tile[cl][k];
   }
 }
 
@@ -797,8 +809,9 @@ static int to_nhwc(const float* x, float* y, int N, int C, int Cp, int64_t HW, c
     dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((Cp + 31) / 32), (unsigned)N);
     nchw_to_nhwc_v4_kernel<<<grid, 256, 0, s>>>(x, y, C, Cp, (int)HW);
   } else {
-    dim3 grid((unsigned)((HW + 31) / 32), (unsigned)((Cp + 31) / 32), (unsigned)N);
-    nchw_to_nhwc_kernel<<<grid, dim3(32, 8), 0, s>>>(x, y, C, Cp, HW);
+    const int64_t pixels = (int64_t)N * HW;
+    dim3 grid((unsigned)((pixels + 63) / 64), (unsigned)((Cp + 31) / 32));
+    nchw_to_nhwc_flat_kernel<<<grid, 256, 0, s>>>(x, y, C, Cp, HW, pixels);
   }
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
