@@ -66,6 +66,37 @@ def test_launcher_argument_checks_need_no_gpu():
     assert b"shape mismatch" in lib.pvb2_last_error()
 
 
+class _Conv(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ["N", "C", "H", "W", "K", "R", "S", "P", "Q", "stride_h", "stride_w",
+                                             "pad_h", "pad_w", "dil_h", "dil_w", "groups", "math"]]
+
+
+def _conv(N, C, H, W, K, R, st, pd, math=0):
+    P = (H + 2 * pd - R) // st + 1
+    return _Conv(N, C, H, W, K, R, R, P, P, st, st, pd, pd, 1, 1, 1, math)
+
+
+def test_conv_path_queries_need_no_gpu():
+    """Which tensor-core path a convolution takes is host logic: the size of
+    the staged input a training forward can keep for its weight gradient
+    (channels-last copy, im2col columns, or none), and whether a dgrad can
+    also form a sum in its epilogue (1x1 stride 1, 16-byte planes, TF32)."""
+    lib = ctypes.CDLL(LIB)
+    lib.pvb2_conv2d_staged_input_bytes.restype = ctypes.c_size_t
+    q = lambda d: lib.pvb2_conv2d_staged_input_bytes(ctypes.byref(d))
+    assert q(_conv(64, 64, 56, 56, 64, 3, 1, 1)) == 64 * 56 * 56 * 64 * 4       # channels-last copy
+    assert q(_conv(64, 3, 224, 224, 64, 7, 2, 3)) == 64 * 112 * 112 * 148 * 4   # stem: im2col columns (147 -> 148)
+    assert q(_conv(64, 256, 56, 56, 64, 1, 1, 0)) == 0                          # pointwise: reads NCHW
+    assert q(_conv(64, 64, 56, 56, 64, 3, 1, 1, math=1)) == 0                   # exact fp32: SIMT path
+    al = ctypes.c_void_p(1 << 20)
+    ok = lambda d, p=al: lib.pvb2_conv2d_bwd_data_acc_ok(ctypes.byref(d), p, p, p, p)
+    assert ok(_conv(64, 256, 56, 56, 64, 1, 1, 0)) == 1
+    assert ok(_conv(64, 256, 56, 56, 64, 1, 1, 0), ctypes.c_void_p((1 << 20) + 4)) == 0  # not 16-byte aligned
+    assert ok(_conv(64, 2048, 7, 7, 512, 1, 1, 0)) == 0    # 49-pixel planes
+    assert ok(_conv(64, 64, 56, 56, 64, 3, 1, 1)) == 0     # 3x3
+    assert ok(_conv(64, 256, 56, 56, 64, 1, 1, 0, math=1)) == 0
+
+
 def test_package_registers_ocl_module():
     import pytorch_vulkan_b200 as pkg
 
