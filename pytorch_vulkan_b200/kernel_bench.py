@@ -1,0 +1,107 @@
+"""Per-kernel timing through the C-ABI (libpvb2.so via ctypes, device memory
+from the `ocl` backend), for looking at one launch alone under a profiler.
+
+    python -m pytorch_vulkan_b200.kernel_bench dgrad_acc [--n 32] [--c 256] [--hw 56] [--k 64]
+
+`dgrad_acc`: the 1x1 stride-1 convolution input gradient dX[n, c] =
+sum_k W[k, c] dY[n, k] (a residual block's first convolution), first plain
+(`pvb2_conv2d_bwd_data`), then with the other input gradient summed in its
+epilogue (`pvb2_conv2d_bwd_data_acc`).  Each is run 3 times untimed, then 10
+times between device events; the line printed per variant gives the mean
+launch time and the algorithmic bytes (dY read, dX written, addend read) per
+second.  Launch order: 13 plain, then 13 accumulating.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import os
+
+import torch
+
+import pytorch_vulkan_b200 as _pkg
+
+_LIB = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libpvb2.so")
+
+
+class _Tensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("sizes", ctypes.c_int64 * 8), ("strides", ctypes.c_int64 * 8),
+                ("ndim", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+
+class _Conv(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ["N", "C", "H", "W", "K", "R", "S", "P", "Q", "stride_h", "stride_w",
+                                             "pad_h", "pad_w", "dil_h", "dil_w", "groups", "math"]]
+
+
+def _desc(t: torch.Tensor) -> _Tensor:
+    assert t.dtype == torch.float32
+    return _Tensor(t.data_ptr(), (ctypes.c_int64 * 8)(*t.shape), (ctypes.c_int64 * 8)(*t.stride()), t.dim(), 0)
+
+
+def _time(fn, dev: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.ocl.synchronize()
+    e0, e1 = _pkg._C.impl_event_create(True), _pkg._C.impl_event_create(True)
+    _pkg._C.impl_event_record(e0, dev)
+    for _ in range(10):
+        fn()
+    _pkg._C.impl_event_record(e1, dev)
+    torch.ocl.synchronize()
+    ms = _pkg._C.impl_event_elapsed_ms(e0, e1) / 10
+    _pkg._C.impl_event_destroy(e0)
+    _pkg._C.impl_event_destroy(e1)
+    return ms
+
+
+def dgrad_acc(n: int, c: int, hw: int, k: int, dev: int = 0) -> None:
+    lib = ctypes.CDLL(_LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+    lib.pvb2_conv2d_workspace_size.restype = ctypes.c_size_t
+    d = _Conv(n, c, hw, hw, k, 1, 1, hw, hw, 1, 1, 0, 0, 1, 1, 1, 0)  # TF32 math
+    name = f"ocl:{dev}"
+    g = torch.Generator().manual_seed(0)
+    gy = torch.randn(n, k, hw, hw, generator=g).to(name)
+    w = (torch.randn(k, c, 1, 1, generator=g) * 0.1).to(name)
+    addend = torch.randn(n, c, hw, hw, generator=g).to(name)
+    out = torch.empty(n, c, hw, hw).to(name)
+    ws = torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), 1), 4), dtype=torch.uint8).to(name)
+    stream = ctypes.c_void_p(_pkg._C.impl_stream_handle(dev))
+    gyd, outd, addd = _desc(gy), _desc(out), _desc(addend)
+    wp = ctypes.c_void_p(w.data_ptr())
+
+    def check(status):
+        if status != 0:
+            raise RuntimeError(lib.pvb2_last_error().decode())
+
+    def plain():
+        check(lib.pvb2_conv2d_bwd_data(ctypes.byref(d), ctypes.byref(gyd), wp, ctypes.byref(outd),
+                                       ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()), stream))
+
+    def acc():
+        check(lib.pvb2_conv2d_bwd_data_acc(ctypes.byref(d), ctypes.byref(gyd), wp, ctypes.byref(outd),
+                                           ctypes.byref(addd), stream))
+
+    pixels = n * hw * hw
+    for label, fn, planes in (("plain", plain, k + c), ("acc", acc, k + 2 * c)):
+        ms = _time(fn, dev)
+        gbs = pixels * planes * 4 / (ms * 1e-3) / 1e9
+        print(f"{label}: {ms * 1e3:.1f} us per launch, {gbs:.0f} GB/s algorithmic "
+              f"(N={n}, {k} -> {c} channels, {hw}x{hw})")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=["dgrad_acc"])
+    ap.add_argument("--n", type=int, default=32)
+    ap.add_argument("--c", type=int, default=256)
+    ap.add_argument("--hw", type=int, default=56)
+    ap.add_argument("--k", type=int, default=64)
+    a = ap.parse_args()
+    torch.ocl.set_device(0)
+    dgrad_acc(a.n, a.c, a.hw, a.k)
+
+
+if __name__ == "__main__":
+    main()
