@@ -149,6 +149,7 @@ void staged_make_room(size_t need) {
 
 // the backward's lookup: hands over the buffer (the entry is dropped)
 c10::DataPtr take_staged_input(const at::Tensor& x, const pvb2_conv2d_desc& d, size_t* bytes) {
+  if (!x.unsafeGetTensorImpl()->version_counter().enabled()) return c10::DataPtr();  // never cached
   std::lock_guard<std::mutex> g(g_stage_mutex);
   auto& q = staged_inputs();
   for (auto it = q.begin(); it != q.end(); ++it) {
