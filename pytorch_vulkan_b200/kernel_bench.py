@@ -2,6 +2,8 @@
 from the `ocl` backend), for looking at one launch alone under a profiler.
 
     python -m pytorch_vulkan_b200.kernel_bench dgrad_acc [--n 32] [--c 256] [--hw 56] [--k 64]
+    python -m pytorch_vulkan_b200.kernel_bench conv --which fwd|dgrad|wgrad [--n 32] [--c 64] [--hw 56]
+           [--k 64] [--r 3] [--stride 1] [--pad 1]
 
 `dgrad_acc`: the 1x1 stride-1 convolution input gradient dX[n, c] =
 sum_k W[k, c] dY[n, k] (a residual block's first convolution), first plain
@@ -10,6 +12,11 @@ epilogue (`pvb2_conv2d_bwd_data_acc`).  Each is run 3 times untimed, then 10
 times between device events; the line printed per variant gives the mean
 launch time and the algorithmic bytes (dY read, dX written, addend read) per
 second.  Launch order: 13 plain, then 13 accumulating.
+
+`conv`: one convolution pass (TF32) through `pvb2_conv2d_fwd`,
+`pvb2_conv2d_bwd_data` or `pvb2_conv2d_bwd_filter`, 3 untimed and 10 timed
+calls (each call may launch staging / packing / reduction kernels beside the
+tensor-core one); prints the mean time per call and its TFLOP/s.
 """
 from __future__ import annotations
 
@@ -91,16 +98,61 @@ def dgrad_acc(n: int, c: int, hw: int, k: int, dev: int = 0) -> None:
               f"(N={n}, {k} -> {c} channels, {hw}x{hw})")
 
 
+def conv(which: str, n: int, c: int, hw: int, k: int, r: int, stride: int, pad: int, dev: int = 0) -> None:
+    lib = ctypes.CDLL(_LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+    lib.pvb2_conv2d_workspace_size.restype = ctypes.c_size_t
+    p = (hw + 2 * pad - r) // stride + 1
+    d = _Conv(n, c, hw, hw, k, r, r, p, p, stride, stride, pad, pad, 1, 1, 1, 0)  # TF32 math
+    name = f"ocl:{dev}"
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(n, c, hw, hw, generator=g).to(name)
+    w = (torch.randn(k, c, r, r, generator=g) * 0.1).to(name)
+    y = torch.randn(n, k, p, p, generator=g).to(name)
+    dx = torch.empty(n, c, hw, hw).to(name)
+    dw = torch.empty(k, c, r, r).to(name)
+    slot = {"fwd": 0, "dgrad": 1, "wgrad": 2}[which]
+    ws = torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), slot), 4), dtype=torch.uint8).to(name)
+    stream = ctypes.c_void_p(_pkg._C.impl_stream_handle(dev))
+    xd, yd, dxd = _desc(x), _desc(y), _desc(dx)
+    wsp, wsn = ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel())
+
+    def run():
+        if which == "fwd":
+            st = lib.pvb2_conv2d_fwd(ctypes.byref(d), ctypes.byref(xd), ctypes.c_void_p(w.data_ptr()), None,
+                                     ctypes.byref(yd), wsp, wsn, stream)
+        elif which == "dgrad":
+            st = lib.pvb2_conv2d_bwd_data(ctypes.byref(d), ctypes.byref(yd), ctypes.c_void_p(w.data_ptr()),
+                                          ctypes.byref(dxd), wsp, wsn, stream)
+        else:
+            st = lib.pvb2_conv2d_bwd_filter(ctypes.byref(d), ctypes.byref(xd), ctypes.byref(yd),
+                                            ctypes.c_void_p(dw.data_ptr()), None, wsp, wsn, stream)
+        if st != 0:
+            raise RuntimeError(lib.pvb2_last_error().decode())
+
+    ms = _time(run, dev)
+    flop = 2.0 * n * p * p * k * c * r * r
+    print(f"conv {which}: {ms * 1e3:.1f} us per call, {flop / (ms * 1e-3) / 1e12:.1f} TFLOP/s "
+          f"(N={n}, {c} -> {k} channels, {hw}x{hw}, {r}x{r} stride {stride} pad {pad})")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["dgrad_acc"])
+    ap.add_argument("kernel", choices=["dgrad_acc", "conv"])
+    ap.add_argument("--which", choices=["fwd", "dgrad", "wgrad"], default="fwd")
     ap.add_argument("--n", type=int, default=32)
-    ap.add_argument("--c", type=int, default=256)
+    ap.add_argument("--c", type=int, default=None)
     ap.add_argument("--hw", type=int, default=56)
     ap.add_argument("--k", type=int, default=64)
+    ap.add_argument("--r", type=int, default=3)
+    ap.add_argument("--stride", type=int, default=1)
+    ap.add_argument("--pad", type=int, default=None)
     a = ap.parse_args()
     torch.ocl.set_device(0)
-    dgrad_acc(a.n, a.c, a.hw, a.k)
+    if a.kernel == "dgrad_acc":
+        dgrad_acc(a.n, 256 if a.c is None else a.c, a.hw, a.k)
+    else:
+        conv(a.which, a.n, 64 if a.c is None else a.c, a.hw, a.k, a.r, a.stride, a.r // 2 if a.pad is None else a.pad)
 
 
 if __name__ == "__main__":
