@@ -12,7 +12,10 @@ batch copied from pinned host memory (on a copy stream, overlapping the
 previous step) and the loss read back every step.  The roofline
 object covers the dominant kernel class (the convolutions, fwd+bwd); the CPU
 baseline is the torch-CPU step (the reference's validation path) timed on
-this host on a bounded sample.
+this host at the configuration's batch (2 warm-up + 3 timed steps).  A second
+roofline object, `roofline_bn`, covers the batch-norm class (forward with its
+fused residual add / ReLU, backward with its fused ReLU gradient) against the
+measured HBM copy bandwidth.
 
 `--impl reference` times the reference's CPU path (torch-CPU ATen, as its
 tests/validate_network.py runs it) for the same workload on all host cores;
@@ -35,11 +38,19 @@ sys.path.insert(0, HERE)
 
 MODEL = "resnet50"
 GFLOP_PER_IMAGE = 24.30  # fwd+bwd conv/linear 2*MAC, torch.utils.flop_counter
-# DRAM bytes of one ResNet-50 step's convolution launches per image: 3.18 GB
-# read + 0.025 GB written over the 170 conv_tf32_kernel launches of a batch-16
-# step under ncu (cold L2 per launch), divided by 16 images
-# (profiles/conv_tf32_kernel_resnet50_b16.md)
-CONV_DRAM_BYTES_PER_IMAGE = 3.204e9 / 16
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
 
 
 def parse():
@@ -122,8 +133,10 @@ def run_reference(a):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    sample = min(a.batch, 16)  # a bounded sample of the per-GPU batch per step
-    steps = max(1, min(a.steps, 8))
+    # every step is the full per-GPU batch of the configuration; the step
+    # count is bounded so the run stays within a few minutes on the host cores
+    sample = a.batch
+    steps = max(1, min(a.steps, 10))
     warm = max(1, min(a.warmup, 2))
     dt, used = ostep.time_cpu_steps(a.model, sample, steps, warm, threads)
     v = sample / dt
@@ -131,10 +144,13 @@ def run_reference(a):
         "impl": "reference", "metric": "train images/sec (fp32)", "value": round(v, 3), "unit": "images/s",
         "n_gpus": a.gpus, "steps": steps, "warmup": warm, "ms_per_step": round(dt * 1000, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{a.model} fp32 train step, batch {a.batch}/GPU, 3x224x224, SGD m0.9",
-                   "sample": f"{sample} images per step", "path": "torch-CPU ATen (reference CPU validation path)"},
+        "config": {"workload": f"{a.model} fp32 train step (fwd+bwd+SGD m0.9), batch {a.batch}/GPU, 3x224x224",
+                   "global_batch": a.batch, "sample": f"{sample} images per step (the full per-GPU batch)",
+                   "path": "torch-CPU ATen (reference CPU validation path)"},
         "cpu_baseline": {"value": round(v, 3), "unit": "images/s", "cores": used, "kind": "port",
-                         "sample": f"{steps} steps x {sample} images of the {a.model} workload on torch-CPU"},
+                         "cpu": cpu_model(),
+                         "sample": f"{warm} warm-up + {steps} timed steps x {sample} images of the {a.model} "
+                                   f"workload on torch-CPU"},
         "e2e": {"value": round(v, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -154,6 +170,42 @@ def conv_flops_per_step(model, x):
     return total * x.shape[0], conv * x.shape[0]
 
 
+def bn_roofline(rows, bn_numel, hbm_gbs, measured):
+    """HBM roofline of the batch-norm class in one profiled step.
+
+    Device time: every op row whose name holds "batch_norm" (statistics,
+    normalising passes with their fused residual add / ReLU, backward passes
+    with their fused ReLU gradient).  Algorithmic bytes per element of a
+    layer's input: forward 8 (read x, write y) + 4 when the residual add is
+    fused (read the other summand); backward 12 (read dy and x, write dx) + 4
+    when the ReLU gradient is fused (read the ReLU output).  The normalising
+    passes run in forward call order and the backward passes in reverse, so
+    row i of each kind belongs to batch norm i (resp. n-1-i)."""
+    ms = sum(d for k, d in rows if "batch_norm" in k)
+    if not bn_numel or ms <= 0:
+        return None
+    n = len(bn_numel)
+    # a forward batch norm appears as one row, or as a statistics row followed
+    # (later) by its deferred normalising row "native_batch_norm.apply[+...]"
+    applies = [k for k, _ in rows if k.startswith("native_batch_norm.apply")]
+    bwd = [k for k, _ in rows if "native_batch_norm_backward" in k]
+    fwd_b = sum(8 * e for e in bn_numel)
+    if len(applies) == n:
+        fwd_b += sum(4 * e for e, k in zip(bn_numel, applies) if "+add_" in k)
+    bwd_b = sum(12 * e for e in bn_numel)
+    if len(bwd) == n:
+        bwd_b += sum(4 * e for e, k in zip(reversed(bn_numel), bwd) if "threshold_backward" in k)
+    total = fwd_b + bwd_b
+    achieved = total / (ms / 1000.0) / 1e9
+    return {"bound": "hbm", "kernel": "batch norm fwd+bwd (all batch-norm launches of one step)",
+            "achieved": round(achieved, 1), "peak": round(hbm_gbs, 1), "unit": "GB/s",
+            "frac": round(achieved / hbm_gbs, 4),
+            "peak_note": "measured HBM copy (MEASURED_PEAKS.json)" if measured else "fallback 6650 GB/s",
+            "traffic": None, "bn_ms_per_step": round(ms, 3), "bn_layers": n,
+            "algorithmic_gb_per_step": round(total / 1e9, 3), "fused_adds": sum("+add_" in k for k in applies),
+            "fused_relu_grads": sum("threshold_backward" in k for k in bwd)}
+
+
 def _watchdog(comm, seconds):
     """Multi-GPU runs: if the whole run has not finished after `seconds`, abort
     the NCCL communicator (unblocking any collective waiting for a peer) and
@@ -171,11 +223,10 @@ def _watchdog(comm, seconds):
 
 
 def run_ours(a):
-    import pytorch_vulkan_b200 as pvb2
+    import pytorch_vulkan_b200 as pvb2  # noqa: F401
     from pytorch_vulkan_b200 import _C
+    from pytorch_vulkan_b200 import workloads
     from pytorch_vulkan_b200.distributed import DistributedDataParallel, init_process_group
-
-    from oracle import models as omodels
 
     rank, world, local, comm = init_process_group()
     if world == 1:
@@ -189,14 +240,14 @@ def run_ours(a):
         a.sdpa_ctx = sdpa_kernel(SDPBackend.MATH)  # kept alive: closing it restores the backends
         a.sdpa_ctx.__enter__()
     torch.manual_seed(0)
-    model = omodels.build(a.model, 0)
-    x_cpu, y_cpu = omodels.make_inputs(a.model, a.batch, 1234 + rank)
+    model = workloads.build(a.model, 0)
+    x_cpu, y_cpu = workloads.make_inputs(a.model, a.batch, 1234 + rank)
     total_flops, conv_flops = conv_flops_per_step(model, x_cpu) if rank == 0 else (0, 0)
     model = model.to(dev)
     model.train()
     net = DistributedDataParallel(model, comm) if world > 1 else model
     opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9, fused=True)
-    loss_fn = omodels.loss_fn(a.model)
+    loss_fn = workloads.loss_fn(a.model)
     x = x_cpu.to(dev)
     y = y_cpu.to(dev)
 
@@ -287,7 +338,7 @@ def run_ours(a):
     # --------------------------------------- dominant kernel class roofline
     # every rank runs this step (its gradient all-reduces must be matched on
     # all ranks); rank 0 records it under the profiler
-    roof = None
+    roof = roof_bn = None
     if rank != 0:
         step(x, y)
         torch.ocl.synchronize(local)
@@ -295,39 +346,50 @@ def run_ours(a):
         import csv
         import tempfile
 
+        # element counts of every batch norm's input, in call order
+        bn_numel = []
+        hooks = [m.register_forward_hook(lambda mod, inp, out: bn_numel.append(inp[0].numel()))
+                 for m in model.modules() if isinstance(m, torch.nn.modules.batchnorm._BatchNorm)]
         path = os.path.join(tempfile.mkdtemp(), "prof.csv")
         with torch.ocl.profile(local, path):
             step(x, y)
             torch.ocl.synchronize(local)
+        for h in hooks:
+            h.remove()
         conv_ms = 0.0
         n_conv = 0
         per_op = {}
+        rows = []
         with open(path) as f:
             for r in csv.DictReader(f):
                 d = float(r["duraion(ms)"])
-                top = r["section"] == ""
-                if top:
+                if r["section"] == "":
+                    rows.append((r["kernel"], d))
                     per_op[r["kernel"]] = per_op.get(r["kernel"], 0.0) + d
-                if top and r["kernel"].startswith("convolution"):  # + the dgrad launches that also form an add
-                    conv_ms += d
-                    n_conv += 1
+                    if r["kernel"].startswith("convolution"):  # + the dgrad launches that also form an add
+                        conv_ms += d
+                        n_conv += 1
         peaks = {}
         try:
             peaks = json.load(open(os.path.join(HERE, "MEASURED_PEAKS.json")))
         except Exception:
             pass
         bf16 = peaks.get("bf16_tflops", 1590.0)
+        hbm = peaks.get("hbm_gbs", 6650.0)
         tf32_peak = bf16 / 2.0
         achieved = conv_flops / (conv_ms / 1000.0) / 1e12 if conv_ms > 0 else 0.0
         roof = {"bound": "tensor", "kernel": "convolution fwd+bwd (all conv launches of one step)",
                 "achieved": round(achieved, 2), "peak": round(tf32_peak, 1), "unit": "TFLOP/s",
                 "frac": round(achieved / tf32_peak, 4),
-                "peak_note": "TF32 dense = 1/2 of measured bf16 (MEASURED_PEAKS.json)" if peaks else "fallback",
-                "traffic": (round(CONV_DRAM_BYTES_PER_IMAGE * a.batch) if a.model == MODEL else None),
-                "traffic_unit": "bytes per step (all convolution launches; ncu, cold L2, batch 16 scaled)",
+                "peak_note": ("TF32 dense = 1/2 of measured burst bf16 (MEASURED_PEAKS.json)" if peaks
+                              else "TF32 dense = 1/2 of the fallback bf16 1590 TFLOP/s"),
+                # per-launch DRAM traffic is captured per kernel variant under ncu
+                # (profiles/); the per-step sum of those captures is not formed here
+                "traffic": None,
                 "conv_ms_per_step": round(conv_ms, 3), "conv_launch_groups": n_conv,
                 "conv_gflop_per_step": round(conv_flops / 1e9, 1),
                 "top_ops_ms": dict(sorted(per_op.items(), key=lambda kv: -kv[1])[:8])}
+        roof_bn = bn_roofline(rows, bn_numel, hbm, bool(peaks))
 
     # ------------------------------------------------------- CPU baseline
     cpu = None
@@ -335,10 +397,11 @@ def run_ours(a):
         from oracle import step as ostep
 
         threads = os.cpu_count() or 1
-        sample = 8
-        dt, used = ostep.time_cpu_steps(a.model, sample, 2, 1, threads)
-        cpu = {"value": round(sample / dt, 3), "unit": "images/s", "cores": used, "kind": "port",
-               "sample": f"2 timed steps x {sample} images of {a.model} on torch-CPU ATen (reference CPU path)"}
+        sample = a.batch
+        dt, used = ostep.time_cpu_steps(a.model, sample, 3, 2, threads)
+        cpu = {"value": round(sample / dt, 3), "unit": "images/s", "cores": used, "kind": "port", "cpu": cpu_model(),
+               "sample": f"2 warm-up + 3 timed steps x {sample} images of {a.model} on torch-CPU ATen "
+                         f"(reference CPU path)"}
 
     if rank == 0:
         line = {
@@ -351,7 +414,7 @@ def run_ours(a):
                        **({"attention": a.attention} if "vit" in a.model else {}),
                        "l2": "inputs/activations larger than L2 (126 MB) every step",
                        "gflop_per_step": round(total_flops / 1e9, 1)},
-            "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,
+            "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "roofline_bn": roof_bn, "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -280,9 +280,14 @@ PVB2_API int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma,
  * hand out only their tensors' pointers.  Results equal
  * pvb2_batch_norm_fwd_train's.  Its scratch (per-CTA partial sums) is a
  * fixed 1 MiB array inside this library, resident on every GPU that loads
- * it until the process exits; inputs needing more than
- * PVB2_BN_NOALLOC_SCRATCH_BYTES of partials (about 130k channels and up)
- * are rejected with PVB2_ERR_INVALID.  The first call on each device looks
+ * it until the process exits.  The partials take C x splits x 8 bytes, and
+ * splits grows with N*H*W (about N*H*W / 16384 per channel for large
+ * inputs, at most N on the path for inputs of 2^30 or more elements per
+ * channel), so inputs needing more than PVB2_BN_NOALLOC_SCRATCH_BYTES are
+ * rejected with PVB2_ERR_INVALID: roughly, inputs of more than about 2^31
+ * elements whatever their channel count, or more than about 130k channels.
+ * A call is accepted whenever pvb2_batch_norm_workspace_size(x) is at most
+ * PVB2_BN_NOALLOC_SCRATCH_BYTES.  The first call on each device looks
  * up that device's copy of the array (make it before any stream capture).
  * All calls share the one array: calls that may overlap on the GPU (other
  * streams, other host threads) race and must be serialised by the caller. */
@@ -381,7 +386,8 @@ PVB2_API int pvb2_nll_loss_bwd(const float* grad_out, const int64_t* target, con
 /* bias: NULL, or [N] (bias_dim=1) / [M] (bias_dim=0), added after      */
 /* alpha/beta.                                                          */
 /* math: 0 = TF32 tensor cores where the shapes allow, 1 = exact fp32   */
-/*       (SIMT), 2 = 3xTF32 split (fp32-accurate on tensor cores).      */
+/*       (SIMT).  2 (3xTF32) is reserved: GEMM and convolution entry    */
+/*       points reject it with PVB2_ERR_UNSUPPORTED.                    */
 /* ------------------------------------------------------------------ */
 enum { PVB2_MATH_TF32 = 0, PVB2_MATH_FP32 = 1, PVB2_MATH_3XTF32 = 2 };
 PVB2_API int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
@@ -394,6 +400,11 @@ PVB2_API int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_te
  * pvb2_gemm_workspace_size() bytes, 0 when no split applies. */
 PVB2_API size_t pvb2_gemm_workspace_size(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
                                          int math);
+/* Which engine pvb2_gemm runs these operands on (host logic, no GPU
+ * needed): 1 the TF32 tensor cores, 0 exact fp32 on the CUDA cores, -1 an
+ * invalid request.  The operands' data pointers and strides count (TMA
+ * wants 16-byte aligned bases and row pitches). */
+PVB2_API int pvb2_gemm_path(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math);
 PVB2_API int pvb2_gemm_ws(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C,
                           const float* bias, int bias_dim, double alpha, double beta, int math,
                           void* workspace, size_t workspace_bytes, pvb2_stream stream);
@@ -475,6 +486,15 @@ PVB2_API int pvb2_conv2d_bwd_data_acc_ok(const pvb2_conv2d_desc* d, const void* 
 PVB2_API int pvb2_conv2d_bwd_data_acc(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const float* w,
                                       const pvb2_tensor* dx, const pvb2_tensor* addend, pvb2_stream stream);
 PVB2_API size_t pvb2_conv2d_staged_input_bytes(const pvb2_conv2d_desc* d);
+/* Which engine a convolution pass runs on (host logic, no GPU needed):
+ * which = 0 forward, 1 input gradient, 2 weight gradient.  Returns 1 for the
+ * TF32 tensor cores, 0 for exact fp32 on the CUDA cores (math = 1, grouped
+ * and depthwise convolutions, shapes too small or not expressible as TMA
+ * boxes), -1 for an invalid descriptor.  Assumes 16-byte aligned tensors
+ * and the workspace of pvb2_conv2d_workspace_size.  No counterpart in the
+ * reference (whose dlprim kernels had one precision); it tells a caller,
+ * and the TF32-emulating oracle, where operands are cut to TF32. */
+PVB2_API int pvb2_conv2d_path(const pvb2_conv2d_desc* d, int which);
 PVB2_API int pvb2_conv2d_fwd_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const float* w,
                                     const float* b, const pvb2_tensor* y, void* workspace, size_t workspace_bytes,
                                     float* staged, size_t staged_bytes, int* staged_written, pvb2_stream stream);

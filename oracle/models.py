@@ -1,70 +1,22 @@
-"""Workload definitions of the training hot path (test infrastructure only).
+"""The workload definitions (test infrastructure view).
 
-The five configurations of the benchmark: an MNIST-shaped CNN, ResNet-18,
-ResNet-50, MobileNet-v2 and ViT-B/16, all fp32, random-initialised from a
-seed (pretrained weights need a network and are not used).  The torchvision
-builders are the same models the reference validates in
-tests/validate_network.py:249-292.
+The builders, seeded inputs and losses live in
+``pytorch_vulkan_b200/workloads.py``, a definitions-only module shared with
+the benchmark; it is loaded here by file path so that importing the oracle
+never loads the backend's native libraries.
 """
-from __future__ import annotations
+import importlib.util as _ilu
+import os as _os
 
-import torch
-import torch.nn as nn
-import torch.nn.functional as F
+_path = _os.path.join(_os.path.dirname(_os.path.dirname(_os.path.abspath(__file__))), "pytorch_vulkan_b200",
+                      "workloads.py")
+_spec = _ilu.spec_from_file_location("_pvb2_workloads", _path)
+_mod = _ilu.module_from_spec(_spec)
+_spec.loader.exec_module(_mod)
 
-
-class MnistCNN(nn.Module):
-    """conv 1->32 3x3 -> ReLU -> conv 32->64 3x3 -> ReLU -> maxpool 2 ->
-    flatten 9216 -> linear 128 -> ReLU -> linear 10 -> log_softmax.
-    (Differs from the reference's mnist.py:12-44 net on purpose: this is the
-    benchmark's MNIST-shaped configuration.)"""
-
-    def __init__(self):
-        super().__init__()
-        self.conv1 = nn.Conv2d(1, 32, 3, 1)
-        self.conv2 = nn.Conv2d(32, 64, 3, 1)
-        self.fc1 = nn.Linear(9216, 128)
-        self.fc2 = nn.Linear(128, 10)
-
-    def forward(self, x):
-        x = F.relu(self.conv1(x))
-        x = F.relu(self.conv2(x))
-        x = F.max_pool2d(x, 2)
-        x = torch.flatten(x, 1)
-        x = F.relu(self.fc1(x))
-        return F.log_softmax(self.fc2(x), dim=1)
-
-
-# name -> (builder, input shape (C,H,W), classes, default per-GPU batch, loss)
-CONFIGS = {
-    "mnist": (lambda: MnistCNN(), (1, 28, 28), 10, 64, "nll"),
-    "resnet18": (lambda: __import__("torchvision").models.resnet18(), (3, 224, 224), 1000, 64, "ce"),
-    "resnet50": (lambda: __import__("torchvision").models.resnet50(), (3, 224, 224), 1000, 64, "ce"),
-    "mobilenet_v2": (lambda: __import__("torchvision").models.mobilenet_v2(), (3, 224, 224), 1000, 128, "ce"),
-    "vit_b_16": (lambda: __import__("torchvision").models.vit_b_16(), (3, 224, 224), 1000, 32, "ce"),
-}
-
-# algorithmic work per image, fwd+bwd (2*MAC of conv/linear/bmm)
-GFLOP_PER_IMAGE = {"mnist": 0.072, "resnet18": 10.65, "resnet50": 24.30, "mobilenet_v2": 1.81, "vit_b_16": 100.9}
-
-
-def build(name: str, seed: int = 0) -> nn.Module:
-    """Weights from torch.manual_seed(seed) with the default (Kaiming-uniform) init, on CPU."""
-    torch.manual_seed(seed)
-    return CONFIGS[name][0]()
-
-
-def make_inputs(name: str, batch: int, seed: int = 1234):
-    """Seeded synthetic inputs: MNIST x~U[0,1), labels 0-9; ImageNet-shaped x~N(0,1), labels 0-999."""
-    _, shape, classes, _, _ = CONFIGS[name]
-    g = torch.Generator().manual_seed(seed)
-    if name == "mnist":
-        x = torch.rand((batch, *shape), generator=g)
-    else:
-        x = torch.randn((batch, *shape), generator=g)
-    y = torch.randint(0, classes, (batch,), generator=g)
-    return x, y
-
-
-def loss_fn(name: str):
-    return F.nll_loss if CONFIGS[name][4] == "nll" else F.cross_entropy
+MnistCNN = _mod.MnistCNN
+CONFIGS = _mod.CONFIGS
+GFLOP_PER_IMAGE = _mod.GFLOP_PER_IMAGE
+build = _mod.build
+make_inputs = _mod.make_inputs
+loss_fn = _mod.loss_fn

@@ -167,7 +167,7 @@ class _OCL:
 
     @staticmethod
     def set_math_mode(mode: int):
-        """0 = TF32 tensor cores (default), 1 = exact fp32 (SIMT), 2 = 3xTF32."""
+        """0 = TF32 tensor cores (default), 1 = exact fp32 (SIMT); other values raise."""
         _C.impl_set_math_mode(int(mode))
 
     @staticmethod

@@ -33,6 +33,7 @@ KLIB = os.path.join(LIBDIR, "libpvb2.so")
 EXT = os.path.join(PKG, "_C.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+CUDA_INC = os.path.join(os.path.dirname(os.path.dirname(NVCC)), "include")
 CXX = os.environ.get("PVB2_CXX", "/usr/bin/g++")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUTLASS_INC = None  # kernels are hand-written; CuTe headers are not needed
@@ -71,12 +72,13 @@ def _torch_flags():
     py_inc = sysconfig.get_paths()["include"]
     cflags = ["-O2", "-std=c++17", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_C",
               "-DTORCH_API_INCLUDE_EXTENSION_H", "-Wno-unused-parameter", "-Wno-sign-compare"]
-    for i in incs + [py_inc, INCLUDE]:
+    # the CUDA include tree only for the header-only NVTX v3 ranges of the op guard
+    for i in incs + [py_inc, CUDA_INC, INCLUDE]:
         cflags += ["-isystem" if i != INCLUDE else "-I", i]
     ldflags = []
     for d in libdirs:
         ldflags += ["-L", d, f"-Wl,-rpath,{d}"]
-    ldflags += ["-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python"]
+    ldflags += ["-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python", "-ldl"]
     return cflags, ldflags
 
 

@@ -11,6 +11,7 @@
 #include <ATen/core/GeneratorForPrivateuseone.h>
 #include <ATen/detail/PrivateUse1HooksInterface.h>
 #include <c10/core/impl/DeviceGuardImplInterface.h>
+#include <nvtx3/nvToolsExt.h>
 #include <pthread.h>
 #include <torch/extension.h>
 
@@ -383,7 +384,8 @@ static PinnedAllocator g_pinned;
 static std::atomic<int> g_math{env_int("B200_MATH_MODE", "OCL_MATH_MODE", PVB2_MATH_TF32)};
 int math_mode() { return g_math.load(); }
 void set_math_mode(int m) {
-  TORCH_CHECK(m >= 0 && m <= 2, "ocl: math mode must be 0 (tf32), 1 (fp32) or 2 (3xtf32)");
+  TORCH_CHECK(m == PVB2_MATH_TF32 || m == PVB2_MATH_FP32,
+              "ocl: math mode must be 0 (TF32 tensor cores) or 1 (exact fp32); 3xTF32 (2) is not implemented");
   g_math = m;
 }
 
@@ -411,6 +413,10 @@ static std::vector<ProfState>& prof() {
 
 ExecGuard::ExecGuard(const char* n, int dev) : name(n), device(dev), slot(-1) {
   flush_deferred();
+  // a named range per op for timeline profilers (Nsight Systems, ncu --nvtx),
+  // the counterpart of the reference's per-op section (src/guard.cpp:5-14);
+  // without an attached tool this is a call through a null-checked pointer
+  nvtxRangePushA(n);
   const int mode = g_trace_mode.load(std::memory_order_relaxed);
   if (mode == 2) fprintf(stderr, "%*s> %s (ocl:%d)\n", 2 * t_depth, "", n, dev);
   ++t_depth;
@@ -444,6 +450,7 @@ ExecGuard::~ExecGuard() {
   }
   if (std::uncaught_exceptions() > 0 && g_trace_mode.load() >= 1)
     fprintf(stderr, "ocl: exception in op %s (ocl:%d)\n", name, device);
+  nvtxRangePop();
   if (device >= 0) after_op(device);
 }
 

@@ -141,7 +141,7 @@ void flush_deferred() {
   t_flushing = true;
   try {
     auto p = take();
-    if (p.bn) launch(*p.bn, p.bn->residual.defined() ? "native_batch_norm+add_" : "native_batch_norm");
+    if (p.bn) launch(*p.bn, p.bn->residual.defined() ? "native_batch_norm.apply+add_" : "native_batch_norm.apply");
     if (p.thr) launch_thr(*p.thr);
     if (p.dgrad && !p.dgrad->unwritten) launch_dgrad(*p.dgrad, p.dgrad->gx, at::Tensor());
     if (p.dgrad && p.dgrad->unwritten) {
@@ -233,7 +233,7 @@ bool fuse_deferred_relu(const at::Tensor& self) {
     g_any.store(false, std::memory_order_release);
   }
   p->relu = true;
-  launch(*p, p->residual.defined() ? "native_batch_norm+add_+relu_" : "native_batch_norm+relu_");
+  launch(*p, p->residual.defined() ? "native_batch_norm.apply+add_+relu_" : "native_batch_norm.apply+relu_");
   return true;
 }
 

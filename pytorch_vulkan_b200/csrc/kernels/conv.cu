@@ -23,6 +23,7 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
                        size_t ws_bytes, cudaStream_t s, bool* handled, const float* staged);
 size_t conv_tc_workspace(const pvb2_conv2d_desc* d, int which);
 size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d);
+bool conv_tc_path(const pvb2_conv2d_desc* d, int which);
 bool conv_tc_bwd_data_acc_ok(const pvb2_conv2d_desc* d, const void* dy, const void* w, const void* dx,
                              const void* addend);
 int conv_tc_bwd_data_acc(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, const float* addend,
@@ -321,6 +322,8 @@ static int wgrad_splits(const ConvGeom& g) {
 }
 
 static int check_desc(const pvb2_conv2d_desc* d) {
+  if (d->math != PVB2_MATH_TF32 && d->math != PVB2_MATH_FP32)
+    return fail(PVB2_ERR_UNSUPPORTED, "conv2d: math mode %d is not implemented (0 = TF32, 1 = exact fp32)", d->math);
   PVB2_CHECK_ARG(d->groups >= 1 && d->C % d->groups == 0 && d->K % d->groups == 0,
                  "conv2d: channels must divide groups");
   PVB2_CHECK_ARG(d->stride_h > 0 && d->stride_w > 0 && d->dil_h > 0 && d->dil_w > 0,
@@ -353,6 +356,12 @@ size_t pvb2_conv2d_workspace_size(const pvb2_conv2d_desc* d, int which) {
   }
   size_t tc = conv_tc_workspace(d, which);
   return need > tc ? need : tc;
+}
+
+int pvb2_conv2d_path(const pvb2_conv2d_desc* d, int which) {
+  if (check_desc(d) != PVB2_OK || which < 0 || which > 2) return -1;
+  if (is_depthwise(geom(d))) return 0;
+  return conv_tc_path(d, which) ? 1 : 0;
 }
 
 size_t pvb2_conv2d_staged_input_bytes(const pvb2_conv2d_desc* d) {

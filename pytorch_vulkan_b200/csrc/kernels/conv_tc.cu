@@ -1398,6 +1398,16 @@ size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d) {
   return (size_t)d->N * d->H * d->W * round4(d->C) * 4;
 }
 
+// whether conv_tc_fwd (which 0), conv_tc_bwd_data (1) or conv_tc_bwd_filter
+// (2) take the tensor-core path, given 16-byte aligned tensors and the
+// workspace that conv_tc_workspace reports; mirrors their conditions
+bool conv_tc_path(const pvb2_conv2d_desc* d, int which) {
+  if (!tc_conv_shape_ok(d)) return false;
+  if (pointwise(d) || strided_pointwise(d)) return true;
+  if (which != 1 && use_im2col(d)) return true;
+  return stride_ok_for_boxes(d);
+}
+
 // `staged` (conv_tc_staged_bytes long, or null): where the staged input goes
 // instead of the workspace; *staged_written says whether it was filled
 int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const float* b, float* y, void* ws,

@@ -14,6 +14,7 @@ int gemm_tc(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, co
             float alpha, float beta, int math, cudaStream_t s, bool* handled, void* workspace,
             size_t workspace_bytes);
 size_t gemm_tc_workspace(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math);
+bool gemm_tc_path(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math);
 
 struct GemmProb {
   int64_t M, N;
@@ -64,6 +65,13 @@ extern "C" size_t pvb2_gemm_workspace_size(const pvb2_tensor* A, const pvb2_tens
   return gemm_tc_workspace(A, B, C, math);
 }
 
+extern "C" int pvb2_gemm_path(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math) {
+  if (gemm_check(A, B, C, 0) != PVB2_OK) return -1;
+  if (math != PVB2_MATH_TF32 && math != PVB2_MATH_FP32) return -1;
+  if ((int64_t)C->sizes[0] * C->sizes[1] * C->sizes[2] == 0) return 0;
+  return gemm_tc_path(A, B, C, math) ? 1 : 0;
+}
+
 extern "C" int pvb2_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, const float* bias,
                          int bias_dim, double alpha, double beta, int math, pvb2_stream stream) {
   return pvb2_gemm_ws(A, B, C, bias, bias_dim, alpha, beta, math, nullptr, 0, stream);
@@ -73,6 +81,8 @@ extern "C" int pvb2_gemm_ws(const pvb2_tensor* A, const pvb2_tensor* B, const pv
                             int bias_dim, double alpha, double beta, int math, void* workspace,
                             size_t workspace_bytes, pvb2_stream stream) {
   PVB2_TRY(gemm_check(A, B, C, bias_dim));
+  if (math != PVB2_MATH_TF32 && math != PVB2_MATH_FP32)
+    return fail(PVB2_ERR_UNSUPPORTED, "gemm: math mode %d is not implemented (0 = TF32, 1 = exact fp32)", math);
   const int64_t batch = C->sizes[0], M = C->sizes[1], N = C->sizes[2], K = A->sizes[2];
   if (batch * M * N == 0) return PVB2_OK;
   cudaStream_t s = as_stream(stream);

@@ -297,8 +297,15 @@ int encode_tiled(CUtensorMap* map, int rank, const void* base, const uint64_t* d
 // cols = N (`k_is_cols` says which).  *mn_major reports whether the unit-stride
 // dim is M/N (true) or K (false).  Returns PVB2_ERR_UNSUPPORTED when TMA's
 // alignment rules (16-byte base and strides) do not hold.
-static int make_operand_map(CUtensorMap* map, const pvb2_tensor* t, bool k_is_cols, int mn_box, bool* mn_major,
-                            int* bcast) {
+struct OperandLayout {
+  bool mn_major;
+  int bcast;
+  uint64_t dims[3], str[2];
+};
+
+// the TMA view of an operand (no driver call): dims and byte strides, or
+// PVB2_ERR_UNSUPPORTED when the alignment rules do not hold
+static int operand_layout(const pvb2_tensor* t, bool k_is_cols, OperandLayout* o) {
   const int64_t Bt = t->sizes[0], R = t->sizes[1], Cc = t->sizes[2];
   const int64_t s0 = t->strides[0], s1 = t->strides[1], s2 = t->strides[2];
   int64_t inner, outer, ostride;
@@ -317,16 +324,29 @@ static int make_operand_map(CUtensorMap* map, const pvb2_tensor* t, bool k_is_co
     return PVB2_ERR_UNSUPPORTED;
   }
   const bool inner_is_k = inner_is_cols == k_is_cols;
-  *mn_major = !inner_is_k;
+  o->mn_major = !inner_is_k;
   if (outer == 1) ostride = (inner + 3) / 4 * 4;
   if (ostride <= 0 || (ostride * 4) % 16 != 0) return PVB2_ERR_UNSUPPORTED;
-  *bcast = (Bt > 1 && s0 == 0) ? 1 : 0;
-  const int64_t nb = (*bcast || Bt == 1) ? 1 : Bt;
+  o->bcast = (Bt > 1 && s0 == 0) ? 1 : 0;
+  const int64_t nb = (o->bcast || Bt == 1) ? 1 : Bt;
   const int64_t bstride = nb == 1 ? ostride * outer : s0;
   if (bstride <= 0 || (bstride * 4) % 16 != 0) return PVB2_ERR_UNSUPPORTED;
   if ((uintptr_t)t->data % 16 != 0) return PVB2_ERR_UNSUPPORTED;
-  uint64_t dims[3] = {(uint64_t)inner, (uint64_t)outer, (uint64_t)nb};
-  uint64_t str[2] = {(uint64_t)ostride * 4, (uint64_t)bstride * 4};
+  o->dims[0] = (uint64_t)inner;
+  o->dims[1] = (uint64_t)outer;
+  o->dims[2] = (uint64_t)nb;
+  o->str[0] = (uint64_t)ostride * 4;
+  o->str[1] = (uint64_t)bstride * 4;
+  return PVB2_OK;
+}
+
+static int make_operand_map(CUtensorMap* map, const pvb2_tensor* t, bool k_is_cols, int mn_box, bool* mn_major,
+                            int* bcast) {
+  OperandLayout o;
+  const int st = operand_layout(t, k_is_cols, &o);
+  if (st != PVB2_OK) return st;
+  *mn_major = o.mn_major;
+  *bcast = o.bcast;
   uint32_t box[3];
   if (*mn_major) {
     box[0] = 32;  // 128 bytes along M/N
@@ -336,7 +356,7 @@ static int make_operand_map(CUtensorMap* map, const pvb2_tensor* t, bool k_is_co
     box[1] = (uint32_t)mn_box;
   }
   box[2] = 1;
-  return encode_tiled(map, 3, t->data, dims, str, box,
+  return encode_tiled(map, 3, t->data, o.dims, o.str, box,
                       *mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
@@ -464,6 +484,13 @@ static GemmPlan plan_gemm(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2
 
 size_t gemm_tc_workspace(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math) {
   return plan_gemm(A, B, C, math).ws_bytes;
+}
+
+// whether gemm_tc runs this product on the tensor cores (host logic only)
+bool gemm_tc_path(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, int math) {
+  if (!plan_gemm(A, B, C, math).tc) return false;
+  OperandLayout o;
+  return operand_layout(A, true, &o) == PVB2_OK && operand_layout(B, false, &o) == PVB2_OK;
 }
 
 int gemm_tc(const pvb2_tensor* A, const pvb2_tensor* B, const pvb2_tensor* C, const float* bias, int bias_dim,

@@ -1146,9 +1146,9 @@ int pvb2_batch_norm_fwd_train_noalloc(const pvb2_tensor* x, const float* gamma, 
     const BnStream p = bn_stream_plan(g, ptrs, 2);
     const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
     PVB2_CHECK_ARG(need <= sizeof(g_bn_scratch),
-                   "batch_norm_noalloc: %lld channels need %zu bytes of partials, more than the %zu-byte scratch; "
-                   "use pvb2_batch_norm_fwd_train with a workspace",
-                   (long long)g.C, need, sizeof(g_bn_scratch));
+                   "batch_norm_noalloc: %lld channels x %d splits need %zu bytes of partials, more than the "
+                   "%zu-byte scratch; use pvb2_batch_norm_fwd_train with a workspace",
+                   (long long)g.C, p.splits, need, sizeof(g_bn_scratch));
     float* part = nullptr;
     PVB2_TRY(bn_scratch_address(&part));
     return bn_fwd_stream(g, p, (const float*)x->data, (float*)y->data, gamma, beta, running_mean, running_var,
@@ -1156,9 +1156,9 @@ int pvb2_batch_norm_fwd_train_noalloc(const pvb2_tensor* x, const float* gamma, 
   }
   const size_t need = (size_t)g.C * g.splits * 2 * sizeof(float);
   PVB2_CHECK_ARG(need <= sizeof(g_bn_scratch),
-                 "batch_norm_noalloc: %lld channels need %zu bytes of partials, more than the %zu-byte scratch; "
-                 "use pvb2_batch_norm_fwd_train with a workspace",
-                 (long long)g.C, need, sizeof(g_bn_scratch));
+                 "batch_norm_noalloc: %lld channels x %d splits need %zu bytes of partials, more than the "
+                 "%zu-byte scratch; use pvb2_batch_norm_fwd_train with a workspace",
+                 (long long)g.C, g.splits, need, sizeof(g_bn_scratch));
   float* part = nullptr;
   PVB2_TRY(bn_scratch_address(&part));
   cudaStream_t s = as_stream(stream);

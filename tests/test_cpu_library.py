@@ -118,3 +118,47 @@ def test_no_cpu_fallback_without_device():
         pytest.skip("a device is visible")
     with pytest.raises(RuntimeError):
         torch.empty(3, device="ocl")
+
+
+def test_reference_package_name_imports():
+    """`import pytorch_ocl` works unchanged (python/pytorch_ocl/__init__.py:1-2):
+    the package re-exports the reference's pt_ocl `impl_*` names and helpers."""
+    import pytorch_ocl
+    from pytorch_ocl import pt_ocl
+
+    for name in ["impl_custom_device", "impl_seed_all", "impl_synchronize_device", "impl_is_bad_fork",
+                 "impl_empty_cache", "impl_enable_profiling", "impl_start_profiling", "impl_stop_profiling"]:
+        assert callable(getattr(pt_ocl, name)), name
+        assert getattr(pytorch_ocl, name) is getattr(pt_ocl, name)
+    for name in ["synchronize", "manual_seed_all", "empty_cache"]:
+        assert callable(getattr(pytorch_ocl, name)), name
+    assert torch._C._get_privateuse1_backend_name() == "ocl"
+    assert pytorch_ocl._device_index("ocl:3") == 3
+
+
+def test_unimplemented_math_mode_is_rejected():
+    """3xTF32 (math mode 2) is not implemented: the host refuses it and the
+    C-ABI convolution / GEMM entry points return PVB2_ERR_UNSUPPORTED."""
+    import pytorch_vulkan_b200  # noqa: F401
+
+    with pytest.raises(RuntimeError):
+        torch.ocl.set_math_mode(2)
+    assert torch.ocl.get_math_mode() in (0, 1)
+    lib = ctypes.CDLL(LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+
+    class T(ctypes.Structure):
+        _fields_ = [("data", ctypes.c_void_p), ("sizes", ctypes.c_int64 * 8), ("strides", ctypes.c_int64 * 8),
+                    ("ndim", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+    a = T(None, (ctypes.c_int64 * 8)(1, 3, 4), (ctypes.c_int64 * 8)(12, 4, 1), 3, 0)
+    b = T(None, (ctypes.c_int64 * 8)(1, 4, 5), (ctypes.c_int64 * 8)(20, 5, 1), 3, 0)
+    c = T(None, (ctypes.c_int64 * 8)(1, 3, 5), (ctypes.c_int64 * 8)(15, 5, 1), 3, 0)
+    assert lib.pvb2_gemm(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), None, 1, ctypes.c_double(1.0),
+                         ctypes.c_double(0.0), 2, None) == 2
+    x = T(None, (ctypes.c_int64 * 8)(1, 4, 8, 8), (ctypes.c_int64 * 8)(256, 64, 8, 1), 4, 0)
+    y = T(None, (ctypes.c_int64 * 8)(1, 4, 8, 8), (ctypes.c_int64 * 8)(256, 64, 8, 1), 4, 0)
+    d = _conv(1, 4, 8, 8, 4, 3, 1, 1, math=2)
+    assert lib.pvb2_conv2d_fwd(ctypes.byref(d), ctypes.byref(x), None, None, ctypes.byref(y), None,
+                               ctypes.c_size_t(0), None) == 2
+    assert b"math mode 2" in lib.pvb2_last_error()

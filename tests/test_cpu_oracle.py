@@ -125,3 +125,113 @@ def test_workload_inputs_are_seeded():
     assert torch.equal(x1, x2) and torch.equal(y1, y2)
     x, y = models.make_inputs("mnist", 4)
     assert x.min() >= 0 and x.max() < 1 and y.max() < 10
+
+
+# ------------------------------------------------------ TF32 emulation
+def test_tf32_conversions():
+    """cut_tf32 clears the low 13 mantissa bits; round_tf32 rounds to 10
+    mantissa bits with ties away from zero (cvt.rna.tf32.f32)."""
+    from oracle.tf32 import cut_tf32, round_tf32
+
+    ulp = 2.0 ** -10  # one TF32 unit at 1.0
+    x = torch.tensor([1.0 + 0.75 * ulp, -(1.0 + 0.75 * ulp), 1.0 + 0.5 * ulp, -(1.0 + 0.5 * ulp), 1.0 + 0.25 * ulp,
+                      3.0, 0.0, 1.0 + ulp], dtype=torch.float32)
+    assert cut_tf32(x).tolist() == [1.0, -1.0, 1.0, -1.0, 1.0, 3.0, 0.0, 1.0 + ulp]
+    assert round_tf32(x).tolist() == [1.0 + ulp, -(1.0 + ulp), 1.0 + ulp, -(1.0 + ulp), 1.0, 3.0, 0.0, 1.0 + ulp]
+    g = torch.Generator().manual_seed(3)
+    y = torch.randn(10000, generator=g)
+    for f in (cut_tf32, round_tf32):
+        z = f(y)
+        assert ((z.view(torch.int32) & 0x1FFF) == 0).all()
+        assert ((z - y).abs() <= y.abs() * 2.0 ** -10).all()
+    assert ((round_tf32(y) - y).abs() <= y.abs() * 2.0 ** -11 * (1 + 1e-6)).all()
+    # float64 input: the fp32 value is converted, the result comes back in float64
+    assert cut_tf32(y.double()).dtype == torch.float64
+    assert torch.equal(cut_tf32(y.double()).float(), cut_tf32(y))
+
+
+def test_tf32_emulation_identity_and_cut():
+    """Tf32Emulation(None) reproduces plain torch through the same autograd
+    functions; with every pass on the tensor cores the forward and both
+    gradients equal the plain ops applied to cut operands."""
+    from oracle.tf32 import Paths, Tf32Emulation, cut_tf32
+
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(2, 8, 9, 9, generator=g, dtype=torch.float64)
+    w = torch.randn(6, 8, 3, 3, generator=g, dtype=torch.float64)
+    b = torch.randn(6, generator=g, dtype=torch.float64)
+    dy = torch.randn(2, 6, 5, 5, generator=g, dtype=torch.float64)
+
+    def run(paths):
+        xr, wr, br = (t.clone().requires_grad_() for t in (x, w, b))
+        with Tf32Emulation(paths):
+            y = F.conv2d(xr, wr, br, 2, 1)
+        y.backward(dy)
+        return y.detach(), xr.grad, wr.grad, br.grad
+
+    plain = F.conv2d(x, w, b, 2, 1)
+    y0, gx0, gw0, gb0 = run(None)
+    assert torch.equal(y0, plain)
+    allp = Paths(conv=lambda *a: True, linear=lambda *a: True, attention=lambda d: True)
+    y1, gx1, gw1, gb1 = run(allp)
+    assert torch.allclose(y1, F.conv2d(cut_tf32(x), cut_tf32(w), b, 2, 1), rtol=1e-12, atol=1e-12)
+    assert torch.allclose(gx1, torch.nn.grad.conv2d_input(x.shape, cut_tf32(w), cut_tf32(dy), 2, 1), rtol=1e-12,
+                          atol=1e-12)
+    assert torch.allclose(gw1, torch.nn.grad.conv2d_weight(cut_tf32(x), w.shape, cut_tf32(dy), 2, 1), rtol=1e-12,
+                          atol=1e-12)
+    assert torch.equal(gb1, dy.sum((0, 2, 3)))
+    assert not torch.equal(y1, y0)
+    # linear: y = x W^T + b, dX = dY W, dW = dY^T X, each with cut operands
+    xl = torch.randn(3, 5, 16, generator=g, dtype=torch.float64, requires_grad=True)
+    wl = torch.randn(7, 16, generator=g, dtype=torch.float64, requires_grad=True)
+    with Tf32Emulation(allp):
+        yl = F.linear(xl, wl)
+    dyl = torch.randn(3, 5, 7, generator=g, dtype=torch.float64)
+    yl.backward(dyl)
+    assert torch.allclose(yl, cut_tf32(xl) @ cut_tf32(wl).t(), rtol=1e-12, atol=1e-12)
+    assert torch.allclose(xl.grad, cut_tf32(dyl) @ cut_tf32(wl), rtol=1e-12, atol=1e-12)
+    assert torch.allclose(wl.grad, cut_tf32(dyl).reshape(-1, 7).t() @ cut_tf32(xl).reshape(-1, 16), rtol=1e-12,
+                          atol=1e-12)
+
+
+def test_tf32_emulated_attention_matches_torch_without_rounding():
+    """The emulated attention (exact branch) is softmax(q k^T s) v with its
+    gradients; the rounded branch stays within the TF32 rounding of it."""
+    from oracle.tf32 import Paths, Tf32Emulation
+
+    g = torch.Generator().manual_seed(9)
+    q, k, v = (torch.randn(2, 3, 11, 8, generator=g, dtype=torch.float64) for _ in range(3))
+    do = torch.randn(2, 3, 11, 8, generator=g, dtype=torch.float64)
+    out = []
+    for paths in (None, Paths(conv=None, linear=None, attention=lambda d: True)):
+        qr, kr, vr = (t.clone().requires_grad_() for t in (q, k, v))
+        with Tf32Emulation(paths):
+            o = F.scaled_dot_product_attention(qr, kr, vr)
+        o.backward(do)
+        out.append((o.detach(), qr.grad, kr.grad, vr.grad))
+    qr, kr, vr = (t.clone().requires_grad_() for t in (q, k, v))
+    ref = torch.softmax(qr @ kr.transpose(-1, -2) / 8 ** 0.5, -1) @ vr
+    ref.backward(do)
+    for a, b in zip(out[0], (ref.detach(), qr.grad, kr.grad, vr.grad)):
+        assert torch.allclose(a, b, rtol=1e-10, atol=1e-10)
+    for a, b in zip(out[1], out[0]):
+        assert (a - b).norm() <= 2e-3 * b.norm()
+
+
+def test_ppm_fixture():
+    """The reference's validation images (tests/golden/ppm_samples.pt) are the
+    raw RGB bytes of tests/samples/*.ppm; where the reference tree is present
+    the fixture is re-read from it and compared byte for byte."""
+    import importlib.util
+
+    d = torch.load(os.path.join(GOLDEN, "ppm_samples.pt"))
+    assert d["images"].shape == (4, 224, 224, 3) and d["images"].dtype == torch.uint8
+    assert d["labels"].tolist() == [281, 207, 87, 1]
+    assert d["names"] == ["cat", "dog", "parrot", "goldfish"]
+    ref = "/root/reference/tests/samples"
+    if os.path.isdir(ref):
+        spec = importlib.util.spec_from_file_location("mkppm", os.path.join(GOLDEN, "make_ppm_fixture.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        for i, n in enumerate(d["names"]):
+            assert torch.equal(mod.read_ppm(os.path.join(ref, n + ".ppm")), d["images"][i]), n

@@ -3,52 +3,45 @@ torch-CPU oracle -- the reference's tests/validate_network.py:62-122 harness
 (same weights and inputs; output, loss, every parameter gradient and the
 state after an SGD-momentum step are compared).
 
-Exact-fp32 math (math=1): each tensor is compared as described below.  With
-TF32 tensor cores (math=0) the comparison has to account for how sensitive
-the step is: truncating the weights to TF32 alone (mantissa cut to 10 bits)
-moves ResNet-50's fp64 gradients by ~100% (median, batch 2), MobileNet-v2's
-by ~75% and ResNet-18's by ~20% at random init.  So in TF32 mode the
-device's global relative gradient error (all gradients concatenated) and its
-output / loss errors must be within 3x of that TF32-truncated-weights fp64
-run's (plus 1e-3).
+Each tensor is measured against a float64 CPU run of the same step (the
+ground truth) computing the arithmetic the device states:
+* exact-fp32 math (math=1): plain float64;
+* TF32 math (math=0): float64 with every tensor-core operand cut to TF32
+  exactly where the device cuts it (``oracle.tf32.Tf32Emulation``; which
+  convolution / linear / attention passes run on the tensor cores comes from
+  the device library's own path queries, ``tests/tf32_paths.py``).
+The device's relative Frobenius error per tensor must be within 10x the
+error of the same (emulated) step run in fp32 on the CPU, plus a floor of
+1e-3, and so must the global error over all gradients.  Training-mode batch
+norm makes deep gradients of random-init networks ill-conditioned (fp32
+rounding alone moves some ResNet-50 batch-norm bias gradients by ~50% at
+batch 16), and the fp32 CPU run measures that per tensor; tensors that are
+well-conditioned (the output, the loss, most weight gradients) are held to
+close to the CPU's own fp32 error.  The reference's pass criterion (max abs
+diff <= 1e-2 against torch-CPU fp32, validate_network.py:119) is checked
+where it is meaningful with random weights (MNIST; the reference's own
+images in test_ppm_validation_gpu.py).
 
-The reference's pass criterion is max abs diff <= 1e-2 (validate_network.py:119,
-with pretrained weights and real images).  With random-init weights and the
-small batches a CPU-side test can afford, training-mode batch norm makes deep
-gradients ill-conditioned: torch-CPU fp32 run with 1 and with 8 threads
-disagrees by up to 0.18 abs / 14% relative on ResNet-50's gradients.  So each
-tensor is measured against a float64 CPU run of the same step (the ground
-truth): the device's relative Frobenius error must be within 10x torch-CPU
-fp32's own error plus a floor: 2e-2 with TF32 tensor cores; 1e-3 in exact-fp32
-math, because a last-bit difference in an activation can flip a ReLU sign or
-a max-pool argmax and route a whole gradient element elsewhere (on the
-MNIST net only the gradients upstream of the pool move, while conv2.bias,
-the routing-invariant sum of dy, matches to 1e-7).  The reference's max-abs
-figure is reported alongside.
-
-Batch sizes are reduced so the CPU side finishes in seconds; the layer
-shapes are those of the benchmark configurations.  MobileNet-v2's classifier
+Batch sizes are reduced so the CPU side finishes in seconds, except one
+ResNet-50 step at the benchmark's batch of 64 (TF32), which runs the tile,
+split-K and staging plans the benchmark runs.  MobileNet-v2's classifier
 dropout is set to p=0 for the comparison (the device draws its own Philox
-stream); ViT-B/16's dropout is 0 by default."""
+stream); ViT-B/16's zero-initialised head (torchvision's init) is given
+random weights so that gradients reach the encoder."""
 import copy
+import json
+import os
 
 import pytest
 import torch
 
+import tf32_paths
 from oracle import models, step
+from oracle.tf32 import Tf32Emulation
 
 pytestmark = pytest.mark.gpu
 DEV = "ocl:0"
-FLOOR = {0: 2e-2, 1: 1e-3}
-
-
-def tf32_truncated(model):
-    """copy of `model` with every floating parameter's mantissa cut to TF32's 10 bits"""
-    m = copy.deepcopy(model)
-    with torch.no_grad():
-        for p in m.parameters():
-            p.copy_((p.detach().view(torch.int32) & ~0x1FFF).view(torch.float32))
-    return m
+FLOOR = 1e-3
 
 
 def global_rel(a, truth, prefix="grad."):
@@ -56,6 +49,22 @@ def global_rel(a, truth, prefix="grad."):
     num = sum(((a[k] - truth[k]) ** 2).sum().item() for k in keys)
     den = sum((truth[k] ** 2).sum().item() for k in keys)
     return (num / max(den, 1e-300)) ** 0.5
+
+
+def _log(rec):
+    path = os.environ.get("PVB2_PARITY_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(rec) + "\n")
+
+
+def oracle_runs(name, batch, model, math, steps=1):
+    """(float64 truth, fp32 CPU run) of the step, in the device's arithmetic"""
+    paths = tf32_paths.device_paths() if math == 0 else None
+    with Tf32Emulation(paths):
+        _, ref64 = step.cpu_reference(name, batch, steps=steps, model=copy.deepcopy(model), dtype=torch.float64)
+        _, ref32 = step.cpu_reference(name, batch, steps=steps, model=copy.deepcopy(model))
+    return ref64, ref32
 
 
 def run_parity(name, batch, math=0, steps=1, prep=None):
@@ -66,10 +75,7 @@ def run_parity(name, batch, math=0, steps=1, prep=None):
         if prep:
             prep(model)
         dev_model = copy.deepcopy(model).to(DEV)
-        _, ref64 = step.cpu_reference(name, batch, steps=steps, model=copy.deepcopy(model), dtype=torch.float64)
-        if math == 0:
-            _, pert64 = step.cpu_reference(name, batch, steps=steps, model=tf32_truncated(model), dtype=torch.float64)
-        _, ref32 = step.cpu_reference(name, batch, steps=steps, model=model)
+        ref64, ref32 = oracle_runs(name, batch, model, math, steps)
         x, y = models.make_inputs(name, batch, 1234)
         opt = torch.optim.SGD(dev_model.parameters(), lr=0.01, momentum=0.9)
         dev_model.train()
@@ -77,21 +83,18 @@ def run_parity(name, batch, math=0, steps=1, prep=None):
             out, l = step.train_step(dev_model, x.to(DEV), y.to(DEV), models.loss_fn(name), opt)
         got = step.snapshot(dev_model, out, l, with_state=True)
         assert set(ref32) == set(got)
-        worst_abs = step.max_abs_diff(ref32, got)
         e_dev = step.frob_rel(got, ref64)
-        if math == 0:
-            e_pert = step.frob_rel(pert64, ref64)
-            g_dev, g_pert = global_rel(got, ref64), global_rel(pert64, ref64)
-            assert g_dev <= 3 * g_pert + 1e-3, f"{name}: gradient error {g_dev} vs TF32-weights {g_pert}"
-            for k in ("output", "loss"):
-                assert e_dev[k] <= 3 * e_pert[k] + 1e-3, f"{name}: {k} error {e_dev[k]} vs TF32-weights {e_pert[k]}"
-            return g_dev, worst_abs
         e_cpu = step.frob_rel(ref32, ref64)
-        bad = {k: (e_dev[k], e_cpu[k]) for k in e_dev if e_dev[k] > 10 * e_cpu[k] + FLOOR[math]}
-        worst_rel = max(e_dev.items(), key=lambda kv: kv[1])
-        assert not bad, f"{name}: {len(bad)} tensors off (dev err, cpu err): {list(bad.items())[:5]}; " \
-                        f"max abs vs cpu fp32 {worst_abs}"
-        return worst_rel, worst_abs
+        g_dev, g_cpu = global_rel(got, ref64), global_rel(ref32, ref64)
+        ratio = {k: e_dev[k] / (10 * e_cpu[k] + FLOOR) for k in e_dev}
+        worst = max(ratio.items(), key=lambda kv: kv[1])
+        _log({"test": f"{name}_b{batch}_math{math}", "worst_key": worst[0], "worst_ratio": worst[1],
+              "worst_dev_err": e_dev[worst[0]], "worst_cpu_err": e_cpu[worst[0]], "global_dev": g_dev,
+              "global_cpu": g_cpu, "output_dev": e_dev["output"], "output_cpu": e_cpu["output"]})
+        bad = {k: (e_dev[k], e_cpu[k]) for k in e_dev if e_dev[k] > 10 * e_cpu[k] + FLOOR}
+        assert not bad, f"{name} (math {math}): {len(bad)} tensors off (dev err, cpu err): {list(bad.items())[:5]}"
+        assert g_dev <= 10 * g_cpu + FLOOR, f"{name} (math {math}): global gradient error {g_dev} vs cpu {g_cpu}"
+        return worst
     finally:
         torch.ocl.set_math_mode(old)
 
@@ -112,32 +115,43 @@ def test_mnist_step(ocl, math):
 
 @pytest.mark.parametrize("math", [0, 1])
 def test_resnet18_step(ocl, math):
-    run_parity("resnet18", 4, math=math)
+    run_parity("resnet18", 16, math=math)
 
 
 @pytest.mark.parametrize("math", [0, 1])
 def test_resnet50_step(ocl, math):
-    run_parity("resnet50", 2, math=math)
+    run_parity("resnet50", 16, math=math)
+
+
+def test_resnet50_step_benchmark_batch(ocl):
+    """The benchmark's configuration itself: batch 64, TF32."""
+    run_parity("resnet50", 64, math=0)
+
+
+def _no_dropout(m):
+    m.classifier[0].p = 0.0
 
 
 @pytest.mark.parametrize("math", [0, 1])
 def test_mobilenet_v2_step(ocl, math):
-    def no_dropout(m):
-        m.classifier[0].p = 0.0
+    run_parity("mobilenet_v2", 16, math=math, prep=_no_dropout)
 
-    run_parity("mobilenet_v2", 4, math=math, prep=no_dropout)
+
+def _random_head(m):
+    g = torch.Generator().manual_seed(1)
+    with torch.no_grad():
+        m.heads.head.weight.copy_(torch.randn(m.heads.head.weight.shape, generator=g) * 0.02)
 
 
 @pytest.mark.parametrize("math", [0, 1])
 def test_vit_b_16_step(ocl, math):
-    run_parity("vit_b_16", 2, math=math)
+    run_parity("vit_b_16", 2, math=math, prep=_random_head)
 
 
 def test_resnet50_full_batch_properties(ocl):
-    """At the benchmark batch (64) the CPU oracle is too slow per test; check
-    size-independent properties instead: the loss is finite and near ln(1000)
-    at init, BN running stats moved, and two identical runs are bit-identical
-    (deterministic kernels)."""
+    """Size-independent properties at the benchmark batch (64), over two
+    steps: the loss is finite and near ln(1000) at init, BN running stats
+    moved, and two identical runs are bit-identical (deterministic kernels)."""
     losses = []
     for _ in range(2):
         model = models.build("resnet50", 0).to(DEV)
