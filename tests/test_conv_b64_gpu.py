@@ -15,9 +15,11 @@ are the ones a batch-64 test has to exercise.  For each geometry:
 
 Oracle: float64 convolution of operands cut to TF32 (``oracle.tf32.cut_tf32``,
 the tensor core's conversion), so the device's only remaining error is its
-fp32 accumulation; the elementwise bound is 2^-14 x the same convolution of
+fp32 accumulation; the elementwise bound is 2^-17 x the same convolution of
 the absolute values (the TF32 rounding bound of the per-op tests,
-test_capi_gpu.py, is 2^-9).  To keep the CPU side to seconds the forward and
+test_capi_gpu.py, is 2^-9; the largest error measured on a B200 is 1.2e-6
+of |x||w|, 0.16 of this bound, while plain fp32 arithmetic without the TF32
+cut lands 13-95x above it, so the bound tells the two apart).  To keep the CPU side to seconds the forward and
 dgrad are checked on three whole images (0, 37, 63: each image's output
 depends only on its own input) and the weight gradient on eight output
 channels spread over K (each reduces over all 64 images).
@@ -36,7 +38,7 @@ from test_capi_gpu import LIB, Conv, ok, stream, sync, td
 
 pytestmark = pytest.mark.gpu
 DEV = "ocl:0"
-BOUND = 2.0 ** -14
+BOUND = 2.0 ** -17
 IMAGES = [0, 37, 63]
 
 # N, C, H, W, K, R, stride, pad  (every distinct geometry of torchvision's resnet50, batch 64)
@@ -88,7 +90,7 @@ def _check(name, got, ref, scale, geom):
         with open(path, "a") as f:
             f.write(json.dumps({"test": f"conv_b64_{name}", "geom": geom, "max_ratio_to_bound": ratio,
                                 "max_rel_to_abs_conv": (err / (scale + 1e-30)).max().item()}) + "\n")
-    assert ratio <= 1.0, f"{name}: error {ratio:.3g}x the bound 2^-14 * |x||w| (geometry {geom})"
+    assert ratio <= 1.0, f"{name}: error {ratio:.3g}x the bound 2^-17 * |x||w| (geometry {geom})"
 
 
 @pytest.mark.parametrize("geom", R50, ids=["x".join(map(str, g)) for g in R50])
@@ -137,8 +139,8 @@ def test_resnet50_conv_b64(lib, geom):
                                                   ctypes.c_void_p(buf.data_ptr()), ctypes.c_size_t(nb), s))
         sync()
         assert written.value == 1
-        assert torch.equal(y2, y), "staged forward differs from the plain forward"
-        assert torch.equal(gw2, gw), "weight gradient from the staged copy differs from the plain one"
+        assert torch.equal(y2.cpu(), y.cpu()), "staged forward differs from the plain forward"
+        assert torch.equal(gw2.cpu(), gw.cpu()), "weight gradient from the staged copy differs from the plain one"
 
     # accumulating dgrad: dgrad + addend rounded once, as a separate fp32 add
     if lib.pvb2_conv2d_bwd_data_acc_ok(ctypes.byref(d), ctypes.c_void_p(gyd.data_ptr()),
@@ -149,7 +151,7 @@ def test_resnet50_conv_b64(lib, geom):
         ok(lib, lib.pvb2_conv2d_bwd_data_acc(ctypes.byref(d), ctypes.byref(td(gyd)), ctypes.c_void_p(wd.data_ptr()),
                                              ctypes.byref(td(acc)), ctypes.byref(td(addend)), s))
         sync()
-        assert torch.equal(acc, gx + addend), "accumulating dgrad differs from dgrad + addend"
+        assert torch.equal(acc.cpu(), gx.cpu() + addend.cpu()), "accumulating dgrad differs from dgrad + addend"
 
     # oracle: float64 on TF32-cut operands
     xt, wt, gt = cut_tf32(x).double(), cut_tf32(w).double(), cut_tf32(gy).double()

@@ -11,13 +11,25 @@ ground truth) computing the arithmetic the device states:
   convolution / linear / attention passes run on the tensor cores comes from
   the device library's own path queries, ``tests/tf32_paths.py``).
 The device's relative Frobenius error per tensor must be within 10x the
-error of the same (emulated) step run in fp32 on the CPU, plus a floor of
-1e-3, and so must the global error over all gradients.  Training-mode batch
-norm makes deep gradients of random-init networks ill-conditioned (fp32
-rounding alone moves some ResNet-50 batch-norm bias gradients by ~50% at
-batch 16), and the fp32 CPU run measures that per tensor; tensors that are
-well-conditioned (the output, the loss, most weight gradients) are held to
-close to the CPU's own fp32 error.  The reference's pass criterion (max abs
+error of the same (emulated) step run in fp32 on the CPU, plus a floor:
+* output and loss: floor 1e-5, so the forward pass is held to the CPU's own
+  fp32 error;
+* every gradient and updated state tensor: floor 2e-2, and the global error
+  over all gradients: floor 1e-2.  A backward pass also routes gradient
+  through discrete decisions (ReLU masks, max-pool argmaxes) taken on values
+  that differ in their last bits between any two fp32 runs; an element
+  within an ulp of a ReLU's threshold or of a pool window's tie goes one way
+  on one run and the other way on another, which moves a whole layer's
+  gradient by about 1% relative from there on (measured: ResNet-18 with the
+  reference's images, where torch-CPU fp32 itself shows one such event at
+  layer3 and the device one at layer4).  The floors cover a few such
+  events; errors of the arithmetic itself are held by the per-op tests
+  (test_capi_gpu.py, and test_conv_b64_gpu.py at 2^-17 of |x||w| against
+  the same TF32 emulation).
+Training-mode batch norm makes deep gradients of random-init networks
+ill-conditioned (fp32 rounding alone moves some ResNet-50 batch-norm bias
+gradients by ~50% at batch 16), and the fp32 CPU run measures that per
+tensor.  The reference's pass criterion (max abs
 diff <= 1e-2 against torch-CPU fp32, validate_network.py:119) is checked
 where it is meaningful with random weights (MNIST; the reference's own
 images in test_ppm_validation_gpu.py).
@@ -41,7 +53,13 @@ from oracle.tf32 import Tf32Emulation
 
 pytestmark = pytest.mark.gpu
 DEV = "ocl:0"
-FLOOR = 1e-3
+FLOOR_FWD = 1e-5     # output, loss
+FLOOR = 2e-2         # each gradient / state tensor
+FLOOR_GLOBAL = 1e-2  # all gradients together
+
+
+def floor_for(key):
+    return FLOOR_FWD if key in ("output", "loss") else FLOOR
 
 
 def global_rel(a, truth, prefix="grad."):
@@ -86,14 +104,15 @@ def run_parity(name, batch, math=0, steps=1, prep=None):
         e_dev = step.frob_rel(got, ref64)
         e_cpu = step.frob_rel(ref32, ref64)
         g_dev, g_cpu = global_rel(got, ref64), global_rel(ref32, ref64)
-        ratio = {k: e_dev[k] / (10 * e_cpu[k] + FLOOR) for k in e_dev}
+        ratio = {k: e_dev[k] / (10 * e_cpu[k] + floor_for(k)) for k in e_dev}
         worst = max(ratio.items(), key=lambda kv: kv[1])
         _log({"test": f"{name}_b{batch}_math{math}", "worst_key": worst[0], "worst_ratio": worst[1],
               "worst_dev_err": e_dev[worst[0]], "worst_cpu_err": e_cpu[worst[0]], "global_dev": g_dev,
               "global_cpu": g_cpu, "output_dev": e_dev["output"], "output_cpu": e_cpu["output"]})
-        bad = {k: (e_dev[k], e_cpu[k]) for k in e_dev if e_dev[k] > 10 * e_cpu[k] + FLOOR}
+        bad = {k: (e_dev[k], e_cpu[k]) for k in e_dev if e_dev[k] > 10 * e_cpu[k] + floor_for(k)}
         assert not bad, f"{name} (math {math}): {len(bad)} tensors off (dev err, cpu err): {list(bad.items())[:5]}"
-        assert g_dev <= 10 * g_cpu + FLOOR, f"{name} (math {math}): global gradient error {g_dev} vs cpu {g_cpu}"
+        assert g_dev <= 10 * g_cpu + FLOOR_GLOBAL, \
+            f"{name} (math {math}): global gradient error {g_dev} vs cpu {g_cpu}"
         return worst
     finally:
         torch.ocl.set_math_mode(old)

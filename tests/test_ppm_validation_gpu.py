@@ -19,9 +19,14 @@ Criteria:
   ViT-B/16.  ResNet-50 with random weights is too ill-conditioned for an
   absolute criterion (torch-CPU fp32 itself is 0.27 away from float64 on the
   stem's weight gradient, whose entries reach 19), so it is held, per tensor,
-  to 10x torch-CPU fp32's own error against float64 plus 1e-3.
+  to 10x torch-CPU fp32's own error against float64 plus the floors below.
 * TF32 math (math=0): every network per tensor against the TF32-emulating
-  float64 oracle, within 10x the emulated fp32 CPU run's error plus 1e-3.
+  float64 oracle, within 10x the emulated fp32 CPU run's error plus a floor.
+The floors are those of test_network_gpu.py: 1e-5 for the output, 2e-2 for
+each gradient (a few ReLU-mask or max-pool-argmax decisions taken the other
+way on values within an ulp of the threshold move a layer's gradient by
+about 1% relative; the ResNet-18 run here shows one such event on the
+device, at layer4, and torch-CPU fp32 one at layer3).
 """
 import copy
 import json
@@ -39,7 +44,11 @@ from oracle.tf32 import Tf32Emulation
 pytestmark = pytest.mark.gpu
 DEV = "ocl:0"
 HERE = os.path.dirname(os.path.abspath(__file__))
-FLOOR = 1e-3
+FLOOR_FWD, FLOOR = 1e-5, 2e-2
+
+
+def floor_for(key):
+    return FLOOR_FWD if key == "output" else FLOOR
 
 
 def ppm_batch():
@@ -109,10 +118,10 @@ def test_reference_images(ocl, name, train, math):
         t64 = cpu_step(model, x, y, train, torch.float64)
         t32 = cpu_step(model, x, y, train, torch.float32)
     e_dev, e_cpu = rel(got, t64), rel(t32, t64)
-    bad = {k: (e_dev[k], e_cpu[k]) for k in t64 if e_dev[k] > 10 * e_cpu[k] + FLOOR}
+    bad = {k: (e_dev[k], e_cpu[k]) for k in t64 if e_dev[k] > 10 * e_cpu[k] + floor_for(k)}
     path = os.environ.get("PVB2_PARITY_LOG")
     if path:
-        worst = max(t64, key=lambda k: e_dev[k] / (10 * e_cpu[k] + FLOOR))
+        worst = max(t64, key=lambda k: e_dev[k] / (10 * e_cpu[k] + floor_for(k)))
         with open(path, "a") as f:
             f.write(json.dumps({"test": f"ppm_{name}_math{math}", "max_abs_vs_cpu_fp32": max_abs,
                                 "worst_key": worst, "worst_dev_err": e_dev[worst],
