@@ -53,8 +53,13 @@ namespace pvb2 {
 // Warp roles: warps 0..3 issue TMA loads (one thread each, every fourth ring
 // stage: a thread's bulk-tensor copies are processed one after another, so
 // several issuing warps multiply the load rate), warp 4 allocates TMEM and
-// issues the MMAs, warps 5..8 run the epilogue (TMEM lane quarter = warp % 4).
-constexpr int cBM = 128, cBK = 32, cProducers = 4, cMmaWarp = cProducers, cThreads = (cProducers + 5) * 32;
+// issues the MMAs, warps 5..12 run the epilogue.  A warp may read only the
+// TMEM lane quarter warp % 4, so two epilogue warps share each quarter and
+// split its 32-column chunks by parity: warp w takes chunks c with
+// c % 2 == (w - 5) / 4.  Each epilogue warp stores through its own 4 KB box,
+// so eight TMA stores per SM are in flight while the next chunks are loaded.
+constexpr int cBM = 128, cBK = 32, cProducers = 4, cMmaWarp = cProducers, cEpiWarps = 8,
+              cThreads = (cProducers + 1 + cEpiWarps) * 32;
 
 constexpr int kMaxTaps = 8;
 
@@ -111,8 +116,8 @@ struct ConvSmem {
   static constexpr int B_BYTES = BN * cBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
-  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;  // 4 epilogue warps x 2 boxes of 32 x 32 fp32
-  static constexpr int EPI_BYTES = 4 * 2 * 32 * 32 * 4;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;  // one box of 32 x 32 fp32 per epilogue warp
+  static constexpr int EPI_BYTES = cEpiWarps * 32 * 32 * 4;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 4) * 8 + 16;
 };
@@ -134,15 +139,16 @@ __device__ __forceinline__ void load_addend_chunk(const ConvTcArgs& a, int n, in
   for (int j = 0; j < 32; ++j) pre[j] = ad[(int64_t)min(k0 + j, a.Kout - 1) * a.Q];
 }
 
-// L2 prefetch of a warp's BN-channel addend box (pixels bx..bx+31 of image
-// n): lane j takes channel rows j, j + 32, ...; a 32-pixel run may straddle
-// two 128-byte lines, so both ends are fetched.  Clamped like the loads.
+// L2 prefetch of a warp's chunks of the BN-channel addend box (pixels
+// bx..bx+31 of image n; chunks c = half, half + 2, ...): lane j takes
+// channel row 32 c + j of each; a 32-pixel run may straddle two 128-byte
+// lines, so both ends are fetched.  Clamped like the loads.
 template <int BN>
-__device__ __forceinline__ void prefetch_addend_l2(const ConvTcArgs& a, int n, int bx, int k0, int lane) {
+__device__ __forceinline__ void prefetch_addend_l2(const ConvTcArgs& a, int n, int bx, int k0, int lane, int half) {
   const float* img = a.addend + (int64_t)n * a.Kout * a.Q;
   const int p0 = min(bx, a.Q - 1), p1 = min(bx + 31, a.Q - 1);
 #pragma unroll
-  for (int c = 0; c < BN / 32; ++c) {
+  for (int c = half; c < BN / 32; c += 2) {
     const float* row = img + (int64_t)min(k0 + c * 32 + lane, a.Kout - 1) * a.Q;
     asm volatile("prefetch.global.L2 [%0];" ::"l"(row + p0));
     asm volatile("prefetch.global.L2 [%0];" ::"l"(row + p1));
@@ -179,7 +185,7 @@ __global__ void __launch_bounds__(cThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], cEpiWarps);
     }
     *abort = 0;
     fence_barrier_init();
@@ -345,30 +351,31 @@ __global__ void __launch_bounds__(cThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;
+    const int ew = warp - cMmaWarp - 1;   // epilogue warp 0..7
+    const int quarter = warp & 3;         // TMEM lane quarter this warp may read
+    const int half = ew >> 2;             // chunks c with c % 2 == half
     const int row = quarter * 32 + lane;  // TMEM lane = accumulator row
-    float* stage = (float*)(smem + L::EPI_OFF) + quarter * 2 * 1024;
-    uint32_t echunk = 0;
+    float* st = (float*)(smem + L::EPI_OFF) + ew * 1024;
     int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t aph = (local >> 1) & 1;
-      // pointwise dgrad with an addend: its first chunk is loaded before
-      // the accumulator is ready, each next one while a chunk is stored
+      // pointwise dgrad with an addend: this warp's first chunk is loaded
+      // before the accumulator is ready, each next one while a chunk is stored
       float pre[32];
       if (PW && a.addend) {
         const int slot = (tile / a.kt) * 4 + quarter;
         if (slot < a.slots) {
           const int n = slot / a.hwb;
-          load_addend_chunk(a, n, (slot - n * a.hwb) * 32, (tile % a.kt) * BN, lane, pre);
+          load_addend_chunk(a, n, (slot - n * a.hwb) * 32, (tile % a.kt) * BN + half * 32, lane, pre);
         }
-        // and the whole of this warp's box of the next tile goes to L2 now,
-        // a tile ahead, so the per-chunk loads above find it there
+        // and this warp's chunks of the next tile go to L2 now, a tile
+        // ahead, so the per-chunk loads above find them there
         const int next = tile + gridDim.x;
         const int slot2 = (next / a.kt) * 4 + quarter;
         if (next < total_tiles && slot2 < a.slots) {
           const int n2 = slot2 / a.hwb;
-          prefetch_addend_l2<BN>(a, n2, (slot2 - n2 * a.hwb) * 32, (next % a.kt) * BN, lane);
+          prefetch_addend_l2<BN>(a, n2, (slot2 - n2 * a.hwb) * 32, (next % a.kt) * BN, lane, half);
         }
       }
       if (!mbar_wait(&acc_full[buf], aph, abort)) break;
@@ -406,7 +413,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           }
         }
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           const int k0 = kt * BN + c * 32;
@@ -429,12 +436,10 @@ __global__ void __launch_bounds__(cThreads, 1)
               const bool px_ok = bx + lane < a.Q;
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += (px_ok && k0 + j < a.Kout) ? pre[j] : 0.0f;
-              if (c + 1 < BN / 32 && k0 + 32 < a.Kout) load_addend_chunk(a, bn, bx, k0 + 32, lane, pre);
+              if (c + 2 < BN / 32 && k0 + 64 < a.Kout) load_addend_chunk(a, bn, bx, k0 + 64, lane, pre);
             }
-            // boxes alternate per issued store, so the store that last used
-            // this box is the one before the most recent: wait until it has read it
-            float* st = stage + (echunk & 1) * 1024;
-            if (lane == 0) bulk_wait_read<1>();
+            // the box's previous store must have read it before it is rewritten
+            if (lane == 0) bulk_wait_read<0>();
             __syncwarp();
             if (a.epi == kEpiFlat) {
               const int qq = lane % a.bw, pp = lane / a.bw, pitch = a.ebp * a.Q;
@@ -453,7 +458,6 @@ __global__ void __launch_bounds__(cThreads, 1)
               else tma_store_3d(&tmC, st, bx, k0, bn);
               bulk_commit();
             }
-            ++echunk;
           }
         }
       } else {
@@ -464,13 +468,12 @@ __global__ void __launch_bounds__(cThreads, 1)
         const int m0 = km * cBM + quarter * 32;
         const int z = sp * RS + rs;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           const int n0 = ctile * BN + c * 32;
           if (m0 < a.Kout && n0 < a.Cin) {  // warp-uniform
-            float* st = stage + (echunk & 1) * 1024;
-            if (lane == 0) bulk_wait_read<1>();
+            if (lane == 0) bulk_wait_read<0>();
             __syncwarp();
 #pragma unroll
             for (int j = 0; j < 32; ++j) st[j * 32 + lane] = v[j];
@@ -480,7 +483,6 @@ __global__ void __launch_bounds__(cThreads, 1)
               tma_store_3d(&tmC, st, m0, n0, z);
               bulk_commit();
             }
-            ++echunk;
           }
         }
       }

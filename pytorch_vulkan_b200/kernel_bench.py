@@ -17,6 +17,11 @@ second.  Launch order: 13 plain, then 13 accumulating.
 `pvb2_conv2d_bwd_data` or `pvb2_conv2d_bwd_filter`, 3 untimed and 10 timed
 calls (each call may launch staging / packing / reduction kernels beside the
 tensor-core one); prints the mean time per call and its TFLOP/s.
+
+`r50`: every distinct convolution of ResNet-50 at batch --n (default 64),
+each pass timed as `conv` does, with the number of times the geometry occurs
+in one training step; prints per pass the time, TFLOP/s and algorithmic
+GB/s (input read + output written once), and the step's weighted totals.
 """
 from __future__ import annotations
 
@@ -136,11 +141,85 @@ def conv(which: str, n: int, c: int, hw: int, k: int, r: int, stride: int, pad: 
           f"(N={n}, {c} -> {k} channels, {hw}x{hw}, {r}x{r} stride {stride} pad {pad})")
 
 
+# N-independent ResNet-50 geometries: (C, H, K, R, stride, pad, count per step, input gradient needed)
+R50 = [
+    (3, 224, 64, 7, 2, 3, 1, False), (64, 56, 64, 1, 1, 0, 1, True), (64, 56, 64, 3, 1, 1, 3, True),
+    (64, 56, 256, 1, 1, 0, 4, True), (256, 56, 64, 1, 1, 0, 2, True), (256, 56, 128, 1, 1, 0, 1, True),
+    (128, 56, 128, 3, 2, 1, 1, True), (128, 28, 512, 1, 1, 0, 4, True), (256, 56, 512, 1, 2, 0, 1, True),
+    (512, 28, 128, 1, 1, 0, 3, True), (128, 28, 128, 3, 1, 1, 3, True), (512, 28, 256, 1, 1, 0, 1, True),
+    (256, 28, 256, 3, 2, 1, 1, True), (256, 14, 1024, 1, 1, 0, 6, True), (512, 28, 1024, 1, 2, 0, 1, True),
+    (1024, 14, 256, 1, 1, 0, 5, True), (256, 14, 256, 3, 1, 1, 5, True), (1024, 14, 512, 1, 1, 0, 1, True),
+    (512, 14, 512, 3, 2, 1, 1, True), (512, 7, 2048, 1, 1, 0, 3, True), (1024, 14, 2048, 1, 2, 0, 1, True),
+    (2048, 7, 512, 1, 1, 0, 2, True), (512, 7, 512, 3, 1, 1, 2, True),
+]
+
+
+def r50(n: int, dev: int = 0) -> None:
+    lib = ctypes.CDLL(_LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+    lib.pvb2_conv2d_workspace_size.restype = ctypes.c_size_t
+    name = f"ocl:{dev}"
+    stream = ctypes.c_void_p(_pkg._C.impl_stream_handle(dev))
+    tot = {"fwd": 0.0, "dgrad": 0.0, "wgrad": 0.0}
+    flops = 0.0
+    print(f"{'C':>5} {'HW':>4} {'K':>5} {'R':>2} {'s':>2} {'x':>2} | "
+          f"{'fwd us':>8} {'TF/s':>6} {'GB/s':>6} | {'dgrad us':>8} {'TF/s':>6} {'GB/s':>6} | "
+          f"{'wgrad us':>8} {'TF/s':>6} {'GB/s':>6}")
+    for (c, hw, k, r, st, pd, cnt, need_dx) in R50:
+        p = (hw + 2 * pd - r) // st + 1
+        d = _Conv(n, c, hw, hw, k, r, r, p, p, st, st, pd, pd, 1, 1, 1, 0)
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(n, c, hw, hw, generator=g).to(name)
+        w = (torch.randn(k, c, r, r, generator=g) * 0.1).to(name)
+        y = torch.randn(n, k, p, p, generator=g).to(name)
+        dx = torch.empty(n, c, hw, hw).to(name)
+        dw = torch.empty(k, c, r, r).to(name)
+        ws = [torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), i), 4), dtype=torch.uint8).to(name)
+              for i in range(3)]
+        xd, yd, dxd = _desc(x), _desc(y), _desc(dx)
+        wp = ctypes.c_void_p(w.data_ptr())
+        calls = {
+            "fwd": lambda: lib.pvb2_conv2d_fwd(ctypes.byref(d), ctypes.byref(xd), wp, None, ctypes.byref(yd),
+                                               ctypes.c_void_p(ws[0].data_ptr()), ctypes.c_size_t(ws[0].numel()),
+                                               stream),
+            "dgrad": lambda: lib.pvb2_conv2d_bwd_data(ctypes.byref(d), ctypes.byref(yd), wp, ctypes.byref(dxd),
+                                                      ctypes.c_void_p(ws[1].data_ptr()),
+                                                      ctypes.c_size_t(ws[1].numel()), stream),
+            "wgrad": lambda: lib.pvb2_conv2d_bwd_filter(ctypes.byref(d), ctypes.byref(xd), ctypes.byref(yd),
+                                                        ctypes.c_void_p(dw.data_ptr()), None,
+                                                        ctypes.c_void_p(ws[2].data_ptr()),
+                                                        ctypes.c_size_t(ws[2].numel()), stream),
+        }
+        fl = 2.0 * n * p * p * k * c * r * r
+        xb, yb, wb = 4.0 * n * c * hw * hw, 4.0 * n * k * p * p, 4.0 * k * c * r * r
+        bytes_ = {"fwd": xb + wb + yb, "dgrad": yb + wb + xb, "wgrad": xb + yb + wb}
+        cols = []
+        for which in ("fwd", "dgrad", "wgrad"):
+            if which == "dgrad" and not need_dx:
+                cols.append(f"{'-':>8} {'-':>6} {'-':>6}")
+                continue
+
+            def run(f=calls[which]):
+                st_ = f()
+                if st_ != 0:
+                    raise RuntimeError(lib.pvb2_last_error().decode())
+
+            ms = _time(run, dev)
+            tot[which] += ms * cnt
+            flops += fl * cnt
+            cols.append(f"{ms * 1e3:8.1f} {fl / (ms * 1e-3) / 1e12:6.1f} {bytes_[which] / (ms * 1e-3) / 1e9:6.0f}")
+        print(f"{c:5d} {hw:4d} {k:5d} {r:2d} {st:2d} {cnt:2d} | " + " | ".join(cols))
+    ms = sum(tot.values())
+    print(f"step total (weighted by count): fwd {tot['fwd']:.3f} ms, dgrad {tot['dgrad']:.3f} ms, "
+          f"wgrad {tot['wgrad']:.3f} ms; {ms:.3f} ms, {flops / (ms * 1e-3) / 1e12:.1f} TFLOP/s over "
+          f"{flops / 1e9:.1f} GFLOP")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["dgrad_acc", "conv"])
+    ap.add_argument("kernel", choices=["dgrad_acc", "conv", "r50"])
     ap.add_argument("--which", choices=["fwd", "dgrad", "wgrad"], default="fwd")
-    ap.add_argument("--n", type=int, default=32)
+    ap.add_argument("--n", type=int, default=None, help="batch (default 32; 64 for r50)")
     ap.add_argument("--c", type=int, default=None)
     ap.add_argument("--hw", type=int, default=56)
     ap.add_argument("--k", type=int, default=64)
@@ -149,10 +228,14 @@ def main() -> None:
     ap.add_argument("--pad", type=int, default=None)
     a = ap.parse_args()
     torch.ocl.set_device(0)
+    if a.kernel == "r50":
+        r50(64 if a.n is None else a.n)
+        return
+    n = 32 if a.n is None else a.n
     if a.kernel == "dgrad_acc":
-        dgrad_acc(a.n, 256 if a.c is None else a.c, a.hw, a.k)
+        dgrad_acc(n, 256 if a.c is None else a.c, a.hw, a.k)
     else:
-        conv(a.which, a.n, 64 if a.c is None else a.c, a.hw, a.k, a.r, a.stride, a.r // 2 if a.pad is None else a.pad)
+        conv(a.which, n, 64 if a.c is None else a.c, a.hw, a.k, a.r, a.stride, a.r // 2 if a.pad is None else a.pad)
 
 
 if __name__ == "__main__":
