@@ -96,6 +96,7 @@ struct ConvTcArgs {
   int ct;                             // wgrad: input-channel tiles ceil(Cin / BN)
   int splits, kb_per_split, total_kb; // wgrad split-K over pixel blocks
   int hwb, slots;                     // pointwise: 32-pixel slots per image, slots in all images
+  int win, wq;                        // kImWgrad over filter-row windows (win = 1): output width Q
   int tiles;                          // tiles of this launch
   int epi, ebq, ebp;                  // EpiMode and its box extents
   float* out;
@@ -302,6 +303,17 @@ __global__ void __launch_bounds__(cThreads, 1)
             mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
             if (MODE == kPwWgrad) {
               tma_load_3d(sa, &tmA, &full[s_], hw0, km * cBM, n);
+            } else if (a.win) {
+              // rows km * 128 + 32 j .. : filter row 4 km + j, its 32-float
+              // window of each pixel; the 32 pixels as two 16-pixel runs,
+              // each inside one output row (Q % 16 == 0)
+#pragma unroll
+              for (int j = 0; j < cBM / 32; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int pq = hw0 + 16 * h, p = pq / a.wq, q = pq - p * a.wq;
+                  tma_load_4d(sa + j * 32 * cBK * 4 + h * 16 * 128, &tmA, &full[s_], 0, q, p * a.sh + km * 4 + j, n);
+                }
             } else {
 #pragma unroll
               for (int j = 0; j < cBM / 32; ++j) tma_load_3d(sa + j * 32 * cBK * 4, &tmA, &full[s_], km * cBM + 32 * j, hw0, n);
@@ -646,6 +658,60 @@ __global__ void __launch_bounds__(256) im2col_kernel(const float* __restrict__ x
   }
 }
 
+// ------------------------------------------- windowed few-channel filters
+// A convolution with few input channels (C <= 4) and a short filter row
+// (S <= 8, the 3-channel 7x7 stem) reads its input as a zero-padded
+// channels-last copy xw[n][hp][wp][4] (hp = h + pad_h, wp = w + pad_w, four
+// channel slots, unused ones zero).  For output (p, q) and filter row r the
+// S taps x 4 channels of the row are the 32 consecutive floats starting at
+// xw[n][p*sh + r][q*sw][0] (8 pixels; the taps past S have zero weights), so
+// a TMA map whose q dimension steps sw pixels (overlapping windows) gives
+// each output pixel its row-r window as one 128-byte K block: the forward is
+// an implicit GEMM over R K blocks with no im2col columns, and the weight
+// gradient a GEMM of the windows (MN-major) against dY.
+// Padded extents: rows (P - 1) * sh + 8 and columns (Q - 1) * sw + 8, so
+// every window of filter rows 0..7 lies inside the copy.
+__global__ void __launch_bounds__(256) pad_window_kernel(const float* __restrict__ x, float4* __restrict__ xw, int C,
+                                                         int H, int W, int Hp, int Wp, int ph, int pw,
+                                                         int64_t total) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int wp = (int)(e % Wp);
+    const int64_t r = e / Wp;
+    const int hp = (int)(r % Hp);
+    const int64_t n = r / Hp;
+    const int h = hp - ph, w = wp - pw;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if ((unsigned)h < (unsigned)H && (unsigned)w < (unsigned)W) {
+      const float* xp = x + ((n * C) * H + h) * (int64_t)W + w;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c < C) v[c] = __ldg(xp + (int64_t)c * H * W);
+    }
+    xw[e] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+// wp[k][r][s * 4 + c] = w[k][c][r][s] (zero for s >= S or c >= C)
+__global__ void pack_w_window_kernel(const float* __restrict__ w, float* __restrict__ wp, int K, int C, int R, int S) {
+  const int total = K * R * 32;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int j = e % 32, r = (e / 32) % R, k = e / (32 * R);
+    const int s = j / 4, c = j % 4;
+    wp[e] = (s < S && c < C) ? w[((k * C + c) * R + r) * S + s] : 0.f;
+  }
+}
+
+// dw[k][c][r][s] = t[k][r * 32 + s * 4 + c]: the windowed weight gradient
+// (rows = filter row x window element) back in the weight's layout
+__global__ void unwindow_wgrad_kernel(const float* __restrict__ t, int ld, float* __restrict__ dw, int K, int C, int R,
+                                      int S) {
+  const int total = K * C * R * S;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int s = e % S, r = (e / S) % R, c = (e / (S * R)) % C, k = e / (S * R * C);
+    dw[e] = t[(int64_t)k * ld + r * 32 + s * 4 + c];
+  }
+}
+
 // Strided 1x1 convolutions (ResNet's downsampling projections) as
 // pointwise ones over the sampled pixels.
 // xs[plane][p][q] = x[plane][p*sh][q*sw]; one thread per sampled element,
@@ -758,6 +824,40 @@ static int im2col_channels(const pvb2_conv2d_desc* d) { return round4(d->C * d->
 static bool use_im2col(const pvb2_conv2d_desc* d) {
   return d->C <= 8 && d->R * d->S > 1 && im2col_channels(d) <= kIm2colMaxK && ((int64_t)d->P * d->Q) % 4 == 0 &&
          d->N <= 65535 && d->P <= 65535;
+}
+
+// Few input channels and filter rows of at most 8 taps over a large image
+// (the 3-channel 7x7 stem): filter-row windows of a padded channels-last
+// copy instead of im2col columns (pad_window_kernel).  The weight gradient
+// reads each 32-pixel K block as two 16-pixel runs of one output row.
+static bool use_window(const pvb2_conv2d_desc* d) {
+  return d->C <= 4 && d->S <= 8 && d->R <= kMaxTaps && d->R * d->S >= 25 && d->dil_h == 1 && d->dil_w == 1 &&
+         d->stride_h <= 8 && d->stride_w <= 8 && d->Q % 16 == 0 && ((int64_t)d->P * d->Q) % 4 == 0 &&
+         d->N <= 65535;
+}
+static int win_hp(const pvb2_conv2d_desc* d) { return (d->P - 1) * d->stride_h + 8; }
+static int win_wp(const pvb2_conv2d_desc* d) { return (d->Q - 1) * d->stride_w + 8; }
+static size_t win_bytes(const pvb2_conv2d_desc* d) { return (size_t)d->N * win_hp(d) * win_wp(d) * 16; }
+
+static int pad_window(const pvb2_conv2d_desc* d, const float* x, float* xw, cudaStream_t s) {
+  const int64_t total = (int64_t)d->N * win_hp(d) * win_wp(d);
+  pad_window_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, (float4*)xw, d->C, d->H, d->W, win_hp(d), win_wp(d),
+                                                          d->pad_h, d->pad_w, total);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
+}
+
+// the windows as a 4-D map (32 floats, Q output columns stepping sw pixels,
+// padded rows, images); box (32, bq, brows, bn), row element stride es_h
+static int window_map(CUtensorMap* m, const float* xw, const pvb2_conv2d_desc* d, uint32_t bq, uint32_t brows,
+                      uint32_t bn, uint32_t es_h, bool mn_major) {
+  const uint64_t wp = win_wp(d), hp = win_hp(d);
+  uint64_t dims[4] = {32, (uint64_t)d->Q, hp, (uint64_t)d->N};
+  uint64_t str[3] = {(uint64_t)d->stride_w * 16, wp * 16, hp * wp * 16};
+  uint32_t box[4] = {32, bq, brows, bn};
+  uint32_t es[4] = {1, 1, es_h, 1};
+  return encode_tiled(m, 4, xw, dims, str, box, mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, es);
 }
 
 struct Taps {
@@ -941,16 +1041,24 @@ __global__ void conv_splitk_reduce_dense_kernel(const float* __restrict__ part, 
 // out element (n, k, p, q) at out[obase + n*on + k*ok + p*op + q*oq].
 // With a split plan (plan_fwd_split) and `part` holding its slabs, the
 // launch is split-K and a reduction writes `out`.
+// `win` (or null): act is that convolution's window copy (pad_window), read
+// through window_map with the row stride sh (sw must be 1: the map's q
+// dimension already steps the convolution's stride)
 static int run_fwd_like(const float* act, const float* wpacked, const float* bias, float* out, int N, int Cp, int H,
                         int W, int K, const Taps& t, int P, int Q, int sh, int sw, int64_t obase, int64_t on,
-                        int64_t ok, int64_t op, int64_t oq, float* part, size_t part_bytes, cudaStream_t s) {
+                        int64_t ok, int64_t op, int64_t oq, float* part, size_t part_bytes, cudaStream_t s,
+                        const pvb2_conv2d_desc* win = nullptr) {
   if (P <= 0 || Q <= 0 || N <= 0) return PVB2_OK;
   int bw, bh, bni;
   pixel_block(P, Q, cBM, bw, bh, bni);
   const int BN = bn_for(K);
   CUtensorMap ma, mb, mc;
   memset(&mc, 0, sizeof(mc));
-  PVB2_TRY(act_map(&ma, act, N, H, W, Cp, bw, bh, bni, sw, sh, false));
+  if (win) {
+    PVB2_TRY(window_map(&ma, act, win, (uint32_t)bw, (uint32_t)(bh * sh), (uint32_t)bni, (uint32_t)sh, false));
+  } else {
+    PVB2_TRY(act_map(&ma, act, N, H, W, Cp, bw, bh, bni, sw, sh, false));
+  }
   const int taps = t.nr * t.ns;
   uint64_t wd[2] = {(uint64_t)taps * Cp, (uint64_t)K};
   uint64_t wst[1] = {(uint64_t)taps * Cp * 4};
@@ -1242,14 +1350,19 @@ static WgPlan plan_im_wg(int N, int K, int Kc, int64_t pq) {
 }
 
 // im2col weight gradient into partials [splits][K][Kc]; xcol: [N][pq][Kc], dy: NCHW [N][K][pq]
+// `win` (or null): xcol is that convolution's window copy and Kc = R * 32
 static int run_im_wgrad(const float* xcol, int Kc, const float* dy, int N, int K, int64_t pq, const WgPlan& p,
-                        float* part, cudaStream_t s) {
+                        float* part, cudaStream_t s, const pvb2_conv2d_desc* win = nullptr) {
   CUtensorMap ma, mb, mc;
   memset(&mc, 0, sizeof(mc));
-  uint64_t dims[3] = {(uint64_t)Kc, (uint64_t)pq, (uint64_t)N};
-  uint64_t str[2] = {(uint64_t)Kc * 4, (uint64_t)pq * Kc * 4};
-  uint32_t box[3] = {32, 32, 1};
-  PVB2_TRY(encode_tiled(&ma, 3, xcol, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+  if (win) {
+    PVB2_TRY(window_map(&ma, xcol, win, 16, 1, 1, 1, true));
+  } else {
+    uint64_t dims[3] = {(uint64_t)Kc, (uint64_t)pq, (uint64_t)N};
+    uint64_t str[2] = {(uint64_t)Kc * 4, (uint64_t)pq * Kc * 4};
+    uint32_t box[3] = {32, 32, 1};
+    PVB2_TRY(encode_tiled(&ma, 3, xcol, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+  }
   PVB2_TRY(nchw_map(&mb, dy, N, K, pq, p.BN, CU_TENSOR_MAP_SWIZZLE_128B));
   ConvTcArgs a;
   memset(&a, 0, sizeof(a));
@@ -1261,6 +1374,11 @@ static int run_im_wgrad(const float* xcol, int Kc, const float* dy, int N, int K
   a.kb_per_split = p.kb_per;
   a.total_kb = p.total_kb;
   a.hwb = (int)((pq + 31) / 32);
+  if (win) {
+    a.win = 1;
+    a.wq = win->Q;
+    a.sh = win->stride_h;
+  }
   a.out = part;
   a.tiles = a.kt * a.ct * a.splits;
   PVB2_TRY(wg_partial_map(&mc, part, Kc, K, p.splits));
@@ -1301,7 +1419,14 @@ static Layout fwd_layout(const pvb2_conv2d_desc* d) {
     l.total = l.c = align256(sampled_bytes(d));  // xs
     return l;
   }
-  if (use_im2col(d)) {
+  if (use_window(d)) {
+    l.b = align256(win_bytes(d));
+    l.total = l.b + align256((size_t)d->K * d->R * 32 * 4);
+    const FwdSplit fs = plan_fwd_split(d->N, d->P, d->Q, d->K, d->R, 32);
+    l.part = l.total;
+    l.part_bytes = fs.bytes;
+    l.total += align256(fs.bytes);
+  } else if (use_im2col(d)) {
     const int Kc = im2col_channels(d);
     l.b = align256((size_t)d->N * d->P * d->Q * Kc * 4);
     l.total = l.b + align256((size_t)d->K * Kc * 4);
@@ -1363,6 +1488,15 @@ static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
     l.total = l.c + align256(wg_partial_bytes(d->K, d->C, p.splits));
     return l;
   }
+  if (use_window(d)) {
+    const int Kc = d->R * 32;
+    WgPlan p = plan_im_wg(d->N, d->K, Kc, (int64_t)d->P * d->Q);
+    if (plan) *plan = p;
+    l.c = align256(win_bytes(d));                                 // window copy, then partials,
+    l.b = l.c + align256(wg_partial_bytes(Kc, d->K, p.splits));   // then the summed [K][Kc]
+    l.total = l.b + align256((size_t)d->K * Kc * 4);
+    return l;
+  }
   if (use_im2col(d)) {
     const int Kc = im2col_channels(d);
     WgPlan p = plan_im_wg(d->N, d->K, Kc, (int64_t)d->P * d->Q);
@@ -1395,6 +1529,7 @@ size_t conv_tc_workspace(const pvb2_conv2d_desc* d, int which) {
 // A caller may keep the forward's copy for the weight gradient.
 size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d) {
   if (!tc_conv_shape_ok(d) || pointwise(d) || strided_pointwise(d)) return 0;
+  if (use_window(d)) return win_bytes(d);
   if (use_im2col(d)) return (size_t)d->N * d->P * d->Q * im2col_channels(d) * 4;
   if (!stride_ok_for_boxes(d)) return 0;
   return (size_t)d->N * d->H * d->W * round4(d->C) * 4;
@@ -1406,7 +1541,7 @@ size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d) {
 bool conv_tc_path(const pvb2_conv2d_desc* d, int which) {
   if (!tc_conv_shape_ok(d)) return false;
   if (pointwise(d) || strided_pointwise(d)) return true;
-  if (which != 1 && use_im2col(d)) return true;
+  if (which != 1 && (use_window(d) || use_im2col(d))) return true;
   return stride_ok_for_boxes(d);
 }
 
@@ -1436,7 +1571,19 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
   }
   float* act = staged ? staged : (float*)((char*)ws + l.a);
   float* wp = (float*)((char*)ws + l.b);
-  if (use_im2col(d)) {
+  if (use_window(d)) {
+    PVB2_TRY(pad_window(d, x, act, s));
+    const int64_t n2 = (int64_t)d->K * d->R * 32;
+    pack_w_window_kernel<<<grid_for(n2, 256), 256, 0, s>>>(w, wp, d->K, d->C, d->R, d->S);
+    PVB2_LAUNCH_CHECK();
+    Taps t;
+    memset(&t, 0, sizeof(t));
+    t.nr = d->R;
+    t.ns = 1;
+    for (int r = 0; r < d->R; ++r) t.h[r] = r;
+    PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, 32, d->H, d->W, d->K, t, d->P, d->Q, d->stride_h, 1, 0,
+                          (int64_t)d->K * pq, pq, d->Q, 1, (float*)((char*)ws + l.part), l.part_bytes, s, d));
+  } else if (use_im2col(d)) {
     const int Kc = im2col_channels(d);
     PVB2_TRY(im2col(d, x, act, s));
     const int64_t n2 = (int64_t)d->K * Kc;
@@ -1598,6 +1745,21 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
     PVB2_TRY(subsample(d, x, xs, s));
     PVB2_TRY(run_pw_wgrad(dy, xs, d->N, d->C, d->K, (int64_t)d->P * d->Q, p, part, s));
     PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->K, d->C, d->K, d->C, dw, d->C, 1, 0, s));
+    *handled = true;
+    return PVB2_OK;
+  }
+  if (use_window(d)) {
+    const int Kc = d->R * 32;
+    float* xw = staged ? const_cast<float*>(staged) : (float*)ws;
+    float* part = (float*)((char*)ws + l.c);
+    float* sum = (float*)((char*)ws + l.b);
+    if (!staged) PVB2_TRY(pad_window(d, x, xw, s));
+    PVB2_TRY(run_im_wgrad(xw, Kc, dy, d->N, d->K, (int64_t)d->P * d->Q, p, part, s, d));
+    // partials [sp][k][r * 32 + j] -> sum[k][r * 32 + j] -> dW[k][c][r][s]
+    PVB2_TRY(wgrad_reduce(part, p.splits, 1, Kc, d->K, Kc, d->K, sum, 1, Kc, 0, s));
+    const int64_t nw = (int64_t)d->K * d->C * RS;
+    unwindow_wgrad_kernel<<<grid_for(nw, 256), 256, 0, s>>>(sum, Kc, dw, d->K, d->C, d->R, d->S);
+    PVB2_LAUNCH_CHECK();
     *handled = true;
     return PVB2_OK;
   }

@@ -85,7 +85,7 @@ def test_conv_path_queries_need_no_gpu():
     lib.pvb2_conv2d_staged_input_bytes.restype = ctypes.c_size_t
     q = lambda d: lib.pvb2_conv2d_staged_input_bytes(ctypes.byref(d))
     assert q(_conv(64, 64, 56, 56, 64, 3, 1, 1)) == 64 * 56 * 56 * 64 * 4       # channels-last copy
-    assert q(_conv(64, 3, 224, 224, 64, 7, 2, 3)) == 64 * 112 * 112 * 148 * 4   # stem: im2col columns (147 -> 148)
+    assert q(_conv(64, 3, 224, 224, 64, 7, 2, 3)) == 64 * 230 * 230 * 16       # stem: padded 4-channel row windows
     assert q(_conv(64, 256, 56, 56, 64, 1, 1, 0)) == 0                          # pointwise: reads NCHW
     assert q(_conv(64, 64, 56, 56, 64, 3, 1, 1, math=1)) == 0                   # exact fp32: SIMT path
     al = ctypes.c_void_p(1 << 20)
