@@ -24,6 +24,12 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
 size_t conv_tc_workspace(const pvb2_conv2d_desc* d, int which);
 size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d);
 bool conv_tc_path(const pvb2_conv2d_desc* d, int which);
+size_t dw_wgrad_workspace(const pvb2_conv2d_desc* d);
+int dw_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const float* b, float* y, cudaStream_t s,
+           bool* handled);
+int dw_dgrad(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, cudaStream_t s, bool* handled);
+int dw_wgrad(const pvb2_conv2d_desc* d, const float* x, const float* dy, float* dw, void* ws, size_t ws_bytes,
+             cudaStream_t s, bool* handled);
 bool conv_tc_bwd_data_acc_ok(const pvb2_conv2d_desc* d, const void* dy, const void* w, const void* dx,
                              const void* addend);
 int conv_tc_bwd_data_acc(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, const float* addend,
@@ -226,7 +232,8 @@ __global__ void conv_bias_grad_kernel(const float* __restrict__ dy, int N, int K
 
 // ------------------------------------------------------------- depthwise
 // groups == C == K (channel multiplier 1): each output reads an R x S window
-// of its own channel.
+// of its own channel.  These direct kernels serve the filter sizes the
+// shared-memory-staged stencils of depthwise.cu do not take (3x3, 5x5).
 __global__ void dw_fwd_kernel(ConvGeom g, const float* __restrict__ x, const float* __restrict__ w,
                               const float* __restrict__ bias, float* __restrict__ y) {
   const int64_t total = (int64_t)g.N * g.K * g.P * g.Q;
@@ -354,6 +361,7 @@ size_t pvb2_conv2d_workspace_size(const pvb2_conv2d_desc* d, int which) {
   if (which == 2 && !is_depthwise(g)) {
     need = (size_t)wgrad_splits(g) * g.K * ((size_t)g.Cg * g.R * g.S) * sizeof(float);
   }
+  if (which == 2 && is_depthwise(g)) need = dw_wgrad_workspace(d);
   size_t tc = conv_tc_workspace(d, which);
   return need > tc ? need : tc;
 }
@@ -385,6 +393,10 @@ int pvb2_conv2d_fwd_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x, cons
   cudaStream_t s = as_stream(stream);
   if ((int64_t)g.N * g.K * g.P * g.Q == 0) return PVB2_OK;
   if (is_depthwise(g)) {
+    PVB2_CHECK_ARG(is_contiguous(x) && is_contiguous(y), "conv2d: depthwise tensors must be contiguous NCHW");
+    bool handled = false;
+    PVB2_TRY(dw_fwd(d, (const float*)x->data, w, b, (float*)y->data, s, &handled));
+    if (handled) return PVB2_OK;
     const int64_t total = (int64_t)g.N * g.K * g.P * g.Q;
     dw_fwd_kernel<<<grid_for(total, 256), 256, 0, s>>>(g, (const float*)x->data, w, b, (float*)y->data);
     PVB2_LAUNCH_CHECK();
@@ -422,6 +434,10 @@ int pvb2_conv2d_bwd_data(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const
   cudaStream_t s = as_stream(stream);
   if ((int64_t)g.N * g.C * g.H * g.W == 0) return PVB2_OK;
   if (is_depthwise(g)) {
+    PVB2_CHECK_ARG(is_contiguous(dy) && is_contiguous(dx), "conv2d: depthwise tensors must be contiguous NCHW");
+    bool handled = false;
+    PVB2_TRY(dw_dgrad(d, (const float*)dy->data, w, (float*)dx->data, s, &handled));
+    if (handled) return PVB2_OK;
     const int64_t total = (int64_t)g.N * g.C * g.H * g.W;
     dw_bwd_data_kernel<<<grid_for(total, 256), 256, 0, s>>>(g, (const float*)dy->data, w, (float*)dx->data);
     PVB2_LAUNCH_CHECK();
@@ -491,6 +507,10 @@ int pvb2_conv2d_bwd_filter_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* 
     return PVB2_OK;
   }
   if (is_depthwise(g)) {
+    PVB2_CHECK_ARG(is_contiguous(x) && is_contiguous(dy), "conv2d: depthwise tensors must be contiguous NCHW");
+    bool handled = false;
+    PVB2_TRY(dw_wgrad(d, (const float*)x->data, (const float*)dy->data, dw, workspace, workspace_bytes, s, &handled));
+    if (handled) return PVB2_OK;
     dw_bwd_filter_kernel<<<g.C * g.R * g.S, 256, 0, s>>>(g, (const float*)x->data, (const float*)dy->data, dw);
     PVB2_LAUNCH_CHECK();
     return PVB2_OK;

@@ -18,6 +18,10 @@ second.  Launch order: 13 plain, then 13 accumulating.
 calls (each call may launch staging / packing / reduction kernels beside the
 tensor-core one); prints the mean time per call and its TFLOP/s.
 
+`dw`: MobileNet-v2's depthwise 3x3 convolutions at batch --n (default 128),
+each pass timed as `conv` does, with algorithmic GB/s (input read + output
+written once; the filter is negligible) against the measured HBM copy rate.
+
 `r50`: every distinct convolution of ResNet-50 at batch --n (default 64),
 each pass timed as `conv` does, with the number of times the geometry occurs
 in one training step; prints per pass the time, TFLOP/s and algorithmic
@@ -215,9 +219,69 @@ def r50(n: int, dev: int = 0) -> None:
           f"{flops / 1e9:.1f} GFLOP")
 
 
+# MobileNet-v2 depthwise layers: (channels, input size, stride, count per step)
+MBV2_DW = [(32, 112, 1, 1), (96, 112, 2, 1), (144, 56, 1, 1), (144, 56, 2, 1), (192, 28, 1, 2), (192, 28, 2, 1),
+           (384, 14, 1, 4), (576, 14, 1, 2), (576, 14, 2, 1), (960, 7, 1, 3)]
+
+
+def depthwise(n: int, dev: int = 0) -> None:
+    lib = ctypes.CDLL(_LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+    lib.pvb2_conv2d_workspace_size.restype = ctypes.c_size_t
+    name = f"ocl:{dev}"
+    stream = ctypes.c_void_p(_pkg._C.impl_stream_handle(dev))
+    try:
+        import json
+        peak = json.load(open(os.path.join(os.path.dirname(os.path.dirname(_LIB)), "..", "MEASURED_PEAKS.json")))[
+            "hbm_gbs"]
+    except Exception:
+        peak = 6650.0
+    tot = {"fwd": 0.0, "dgrad": 0.0, "wgrad": 0.0}
+    byts = {"fwd": 0.0, "dgrad": 0.0, "wgrad": 0.0}
+    print(f"{'C':>5} {'HW':>4} {'s':>2} {'x':>2} | {'fwd us':>8} {'GB/s':>6} | {'dgrad us':>8} {'GB/s':>6} | "
+          f"{'wgrad us':>8} {'GB/s':>6}")
+    for (c, hw, st, cnt) in MBV2_DW:
+        p = (hw + 2 - 3) // st + 1
+        d = _Conv(n, c, hw, hw, c, 3, 3, p, p, st, st, 1, 1, 1, 1, c, 0)
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(n, c, hw, hw, generator=g).to(name)
+        w = torch.randn(c, 1, 3, 3, generator=g).to(name)
+        y = torch.randn(n, c, p, p, generator=g).to(name)
+        dx = torch.empty(n, c, hw, hw).to(name)
+        dw = torch.empty(c, 1, 3, 3).to(name)
+        ws = torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), 2), 4), dtype=torch.uint8).to(name)
+        xd, yd, dxd = _desc(x), _desc(y), _desc(dx)
+        wp = ctypes.c_void_p(w.data_ptr())
+        calls = {
+            "fwd": lambda: lib.pvb2_conv2d_fwd(ctypes.byref(d), ctypes.byref(xd), wp, None, ctypes.byref(yd), None,
+                                               ctypes.c_size_t(0), stream),
+            "dgrad": lambda: lib.pvb2_conv2d_bwd_data(ctypes.byref(d), ctypes.byref(yd), wp, ctypes.byref(dxd), None,
+                                                      ctypes.c_size_t(0), stream),
+            "wgrad": lambda: lib.pvb2_conv2d_bwd_filter(ctypes.byref(d), ctypes.byref(xd), ctypes.byref(yd),
+                                                        ctypes.c_void_p(dw.data_ptr()), None,
+                                                        ctypes.c_void_p(ws.data_ptr()),
+                                                        ctypes.c_size_t(ws.numel()), stream),
+        }
+        b = 4.0 * n * c * (hw * hw + p * p)
+        cols = []
+        for which in ("fwd", "dgrad", "wgrad"):
+            def run(f=calls[which]):
+                if f() != 0:
+                    raise RuntimeError(lib.pvb2_last_error().decode())
+
+            ms = _time(run, dev)
+            tot[which] += ms * cnt
+            byts[which] += b * cnt
+            cols.append(f"{ms * 1e3:8.1f} {b / (ms * 1e-3) / 1e9:6.0f}")
+        print(f"{c:5d} {hw:4d} {st:2d} {cnt:2d} | " + " | ".join(cols))
+    for k in tot:
+        print(f"{k}: {tot[k]:.3f} ms per step, {byts[k] / (tot[k] * 1e-3) / 1e9:.0f} GB/s algorithmic "
+              f"= {byts[k] / (tot[k] * 1e-3) / 1e9 / peak:.2f} of {peak:.0f} GB/s")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["dgrad_acc", "conv", "r50"])
+    ap.add_argument("kernel", choices=["dgrad_acc", "conv", "r50", "dw"])
     ap.add_argument("--which", choices=["fwd", "dgrad", "wgrad"], default="fwd")
     ap.add_argument("--n", type=int, default=None, help="batch (default 32; 64 for r50)")
     ap.add_argument("--c", type=int, default=None)
@@ -230,6 +294,9 @@ def main() -> None:
     torch.ocl.set_device(0)
     if a.kernel == "r50":
         r50(64 if a.n is None else a.n)
+        return
+    if a.kernel == "dw":
+        depthwise(128 if a.n is None else a.n)
         return
     n = 32 if a.n is None else a.n
     if a.kernel == "dgrad_acc":

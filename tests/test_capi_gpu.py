@@ -104,6 +104,15 @@ CONV_SHAPES = [
     # many tiles per CTA with fewer output channels than the tile: chunks without a store
     (4, 3, 224, 224, 32, 3, 3, 1, 1, 1, 1),
     (16, 64, 56, 56, 32, 1, 1, 1, 0, 1, 1),
+    # depthwise (groups = C = K): MobileNet-v2's 3x3 layers through the staged stencils
+    (2, 32, 112, 112, 32, 3, 3, 1, 1, 1, 32),    # 32 x 64 output tiles
+    (2, 96, 112, 112, 96, 3, 3, 2, 1, 1, 96),    # stride 2
+    (3, 144, 56, 56, 144, 3, 3, 1, 1, 1, 144),
+    (4, 576, 14, 14, 576, 3, 3, 2, 1, 1, 576),   # 7x7 outputs: several whole planes per CTA
+    (4, 960, 7, 7, 960, 3, 3, 1, 1, 1, 960),
+    (2, 16, 20, 20, 16, 5, 5, 1, 2, 1, 16),      # 5x5
+    (2, 8, 9, 11, 8, 3, 3, 1, 1, 2, 8),          # dilation 2, odd plane
+    (3, 8, 13, 13, 8, 7, 7, 1, 3, 1, 8),         # 7x7 filter: direct kernels
 ]
 
 
