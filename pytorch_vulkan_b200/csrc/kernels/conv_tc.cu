@@ -1182,6 +1182,11 @@ static WgPlan plan_wg(int N, int K, int Cin, int P, int Q, int taps) {
   return w;
 }
 
+// A pointwise weight gradient with fewer than 128 output channels would use
+// half of each 128-row tile; with at least 128 input channels the roles swap
+// (M = input channels, N = output channels: dW^T = X dY^T), filling it.
+static bool pw_wg_swap(const pvb2_conv2d_desc* d) { return d->K < 128 && d->C >= 128; }
+
 static WgPlan plan_pw_wg(int N, int K, int C, int64_t hw) {
   WgPlan w;
   w.bw = 32; w.bh = 1; w.bni = 1;
@@ -1476,13 +1481,15 @@ static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
   Layout l;
   l.a = l.b = l.c = l.total = 0;
   if (pointwise(d)) {
-    WgPlan p = plan_pw_wg(d->N, d->K, d->C, (int64_t)d->H * d->W);
+    WgPlan p = pw_wg_swap(d) ? plan_pw_wg(d->N, d->C, d->K, (int64_t)d->H * d->W)
+                             : plan_pw_wg(d->N, d->K, d->C, (int64_t)d->H * d->W);
     if (plan) *plan = p;
     l.total = align256(wg_partial_bytes(d->K, d->C, p.splits));  // partials only
     return l;
   }
   if (strided_pointwise(d)) {
-    WgPlan p = plan_pw_wg(d->N, d->K, d->C, (int64_t)d->P * d->Q);
+    WgPlan p = pw_wg_swap(d) ? plan_pw_wg(d->N, d->C, d->K, (int64_t)d->P * d->Q)
+                             : plan_pw_wg(d->N, d->K, d->C, (int64_t)d->P * d->Q);
     if (plan) *plan = p;
     l.c = align256(sampled_bytes(d));  // xs, then partials
     l.total = l.c + align256(wg_partial_bytes(d->K, d->C, p.splits));
@@ -1732,9 +1739,15 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
   if (pointwise(d)) {
     if (!aligned16(x) || !aligned16(dy)) return PVB2_OK;
     float* part = (float*)ws;
-    PVB2_TRY(run_pw_wgrad(dy, x, d->N, d->C, d->K, (int64_t)d->H * d->W, p, part, s));
-    // partials [sp][c][k] -> dW[k][c]
-    PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->K, d->C, d->K, d->C, dw, d->C, 1, 0, s));
+    if (pw_wg_swap(d)) {
+      // partials [sp][k][c] -> dW[k][c]
+      PVB2_TRY(run_pw_wgrad(x, dy, d->N, d->K, d->C, (int64_t)d->H * d->W, p, part, s));
+      PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->C, d->K, d->C, d->K, dw, 1, d->C, 0, s));
+    } else {
+      PVB2_TRY(run_pw_wgrad(dy, x, d->N, d->C, d->K, (int64_t)d->H * d->W, p, part, s));
+      // partials [sp][c][k] -> dW[k][c]
+      PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->K, d->C, d->K, d->C, dw, d->C, 1, 0, s));
+    }
     *handled = true;
     return PVB2_OK;
   }
@@ -1743,8 +1756,13 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
     float* xs = (float*)ws;
     float* part = (float*)((char*)ws + l.c);
     PVB2_TRY(subsample(d, x, xs, s));
-    PVB2_TRY(run_pw_wgrad(dy, xs, d->N, d->C, d->K, (int64_t)d->P * d->Q, p, part, s));
-    PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->K, d->C, d->K, d->C, dw, d->C, 1, 0, s));
+    if (pw_wg_swap(d)) {
+      PVB2_TRY(run_pw_wgrad(xs, dy, d->N, d->K, d->C, (int64_t)d->P * d->Q, p, part, s));
+      PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->C, d->K, d->C, d->K, dw, 1, d->C, 0, s));
+    } else {
+      PVB2_TRY(run_pw_wgrad(dy, xs, d->N, d->C, d->K, (int64_t)d->P * d->Q, p, part, s));
+      PVB2_TRY(wgrad_reduce(part, p.splits, 1, d->K, d->C, d->K, d->C, dw, d->C, 1, 0, s));
+    }
     *handled = true;
     return PVB2_OK;
   }

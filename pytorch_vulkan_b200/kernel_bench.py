@@ -22,6 +22,13 @@ tensor-core one); prints the mean time per call and its TFLOP/s.
 each pass timed as `conv` does, with algorithmic GB/s (input read + output
 written once; the filter is negligible) against the measured HBM copy rate.
 
+`bn`: the batch-norm passes of ResNet-50's activation shapes at batch --n
+(default 64): statistics, normalising pass with ReLU, and the backward's
+reduce and apply passes with the ReLU gradient (pvb2_batch_norm_fwd_stats,
+pvb2_batch_norm_fwd_apply, pvb2_batch_norm_bwd_relu), each timed alone, with
+the bytes each pass moves and its algorithmic bytes per element (8 forward,
+16 backward with the ReLU mask).
+
 `r50`: every distinct convolution of ResNet-50 at batch --n (default 64),
 each pass timed as `conv` does, with the number of times the geometry occurs
 in one training step; prints per pass the time, TFLOP/s and algorithmic
@@ -279,9 +286,68 @@ def depthwise(n: int, dev: int = 0) -> None:
               f"= {byts[k] / (tot[k] * 1e-3) / 1e9 / peak:.2f} of {peak:.0f} GB/s")
 
 
+# ResNet-50 batch-norm inputs: (channels, plane size, count per step)
+R50_BN = [(64, 112, 1), (64, 56, 6), (256, 56, 4), (128, 56, 1), (128, 28, 7), (512, 28, 5), (256, 28, 1),
+          (256, 14, 11), (1024, 14, 7), (512, 14, 1), (512, 7, 5), (2048, 7, 4)]
+
+
+def batch_norm(n: int, dev: int = 0) -> None:
+    lib = ctypes.CDLL(_LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+    lib.pvb2_batch_norm_workspace_size.restype = ctypes.c_size_t
+    name = f"ocl:{dev}"
+    stream = ctypes.c_void_p(_pkg._C.impl_stream_handle(dev))
+    p_ = lambda t: ctypes.c_void_p(t.data_ptr())
+    tot = {"stats": 0.0, "apply": 0.0, "bwd": 0.0}
+    alg = {"fwd": 0.0, "bwd": 0.0}
+    print(f"{'C':>5} {'HW':>4} {'x':>2} | {'stats us':>8} {'GB/s':>6} | {'apply us':>8} {'GB/s':>6} | "
+          f"{'bwd us':>8} {'GB/s':>6}")
+    for (c, hw, cnt) in R50_BN:
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(n, c, hw, hw, generator=g).to(name)
+        y = torch.empty_like(x)
+        dy = torch.randn(n, c, hw, hw, generator=g).to(name)
+        dyo = torch.empty_like(x)
+        dx = torch.empty_like(x)
+        gam, bet = torch.ones(c).to(name), torch.zeros(c).to(name)
+        rm, rv, mean, inv = (torch.zeros(c).to(name) for _ in range(4))
+        dg, db = torch.empty(c).to(name), torch.empty(c).to(name)
+        xd, yd, dyd, dyod, dxd = (_desc(t) for t in (x, y, dy, dyo, dx))
+        ws = torch.empty(max(lib.pvb2_batch_norm_workspace_size(ctypes.byref(xd)), 16), dtype=torch.uint8).to(name)
+        wsp, wsn = p_(ws), ctypes.c_size_t(ws.numel())
+
+        def chk(st):
+            if st != 0:
+                raise RuntimeError(lib.pvb2_last_error().decode())
+
+        stats = lambda: chk(lib.pvb2_batch_norm_fwd_stats(ctypes.byref(xd), wsp, wsn, stream))
+        apply = lambda: chk(lib.pvb2_batch_norm_fwd_apply(ctypes.byref(xd), p_(gam), p_(bet), p_(rm), p_(rv),
+                                                          ctypes.c_double(0.1), ctypes.c_double(1e-5),
+                                                          ctypes.byref(yd), p_(mean), p_(inv), None, 1, None, wsp,
+                                                          wsn, stream))
+        bwd = lambda: chk(lib.pvb2_batch_norm_bwd_relu(ctypes.byref(dyd), ctypes.byref(yd), ctypes.byref(xd),
+                                                       p_(gam), p_(mean), p_(inv), ctypes.byref(dyod),
+                                                       ctypes.byref(dxd), p_(dg), p_(db), wsp, wsn, stream))
+        stats()
+        apply()
+        e = x.numel()
+        ms = {k: _time(f, dev) for k, f in (("stats", stats), ("apply", apply), ("bwd", bwd))}
+        moved = {"stats": 4.0 * e, "apply": 8.0 * e, "bwd": 28.0 * e}
+        for k in tot:
+            tot[k] += ms[k] * cnt
+        alg["fwd"] += 8.0 * e * cnt
+        alg["bwd"] += 16.0 * e * cnt
+        print(f"{c:5d} {hw:4d} {cnt:2d} | " + " | ".join(
+            f"{ms[k] * 1e3:8.1f} {moved[k] / (ms[k] * 1e-3) / 1e9:6.0f}" for k in ("stats", "apply", "bwd")))
+    fwd = tot["stats"] + tot["apply"]
+    print(f"step: stats {tot['stats']:.3f} ms, apply {tot['apply']:.3f} ms, backward {tot['bwd']:.3f} ms; "
+          f"forward {alg['fwd'] / (fwd * 1e-3) / 1e9:.0f} GB/s algorithmic, backward "
+          f"{alg['bwd'] / (tot['bwd'] * 1e-3) / 1e9:.0f} GB/s algorithmic")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["dgrad_acc", "conv", "r50", "dw"])
+    ap.add_argument("kernel", choices=["dgrad_acc", "conv", "r50", "dw", "bn"])
     ap.add_argument("--which", choices=["fwd", "dgrad", "wgrad"], default="fwd")
     ap.add_argument("--n", type=int, default=None, help="batch (default 32; 64 for r50)")
     ap.add_argument("--c", type=int, default=None)
@@ -297,6 +363,9 @@ def main() -> None:
         return
     if a.kernel == "dw":
         depthwise(128 if a.n is None else a.n)
+        return
+    if a.kernel == "bn":
+        batch_norm(64 if a.n is None else a.n)
         return
     n = 32 if a.n is None else a.n
     if a.kernel == "dgrad_acc":
