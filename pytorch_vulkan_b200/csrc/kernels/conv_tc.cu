@@ -71,6 +71,8 @@ enum ConvMode : int {
   kWgrad = 3,     // weight gradient over channels-last tap boxes (A and B MN-major)
   kPwWgrad = 4,   // 1x1 stride-1 weight gradient: A = dY, B = X, both NCHW, K-major along pixels
   kImWgrad = 5,   // weight gradient over im2col columns: A = Xcol[n][pix][j] (MN-major), B = dY NCHW (K-major)
+  kWgradT = 6,    // weight gradient, at most 64 input and output channels: A = two taps' channels-last x
+                  // boxes (M = tap pair x 64 channels), B = dY (N = output channels); both MN-major
 };
 
 // how a forward-shaped launch writes its output
@@ -160,10 +162,10 @@ template <int BN, int MODE>
 __global__ void __launch_bounds__(cThreads, 1)
     conv_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, ConvTcArgs a) {
-  constexpr bool WG = MODE == kWgrad || MODE == kPwWgrad || MODE == kImWgrad;
+  constexpr bool WG = MODE == kWgrad || MODE == kPwWgrad || MODE == kImWgrad || MODE == kWgradT;
   constexpr bool PW = MODE == kPwFwd || MODE == kPwDgrad;
-  constexpr bool A_MN = MODE == kPwFwd || MODE == kPwDgrad || MODE == kWgrad || MODE == kImWgrad;
-  constexpr bool B_MN = MODE == kPwDgrad || MODE == kWgrad;
+  constexpr bool A_MN = MODE == kPwFwd || MODE == kPwDgrad || MODE == kWgrad || MODE == kImWgrad || MODE == kWgradT;
+  constexpr bool B_MN = MODE == kPwDgrad || MODE == kWgrad || MODE == kWgradT;
   using L = ConvSmem<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -265,6 +267,33 @@ __global__ void __launch_bounds__(cThreads, 1)
 #pragma unroll
               for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * 32 * cBK * 4, &tmB, &full[s_], kt * BN + 32 * j, kb * 32);
             }
+          }
+        } else if (MODE == kWgradT) {
+          // tile (split, tap pair): rows 32 j .. of A are tap 2 pair + j / 2,
+          // input channels 32 (j % 2) ..; a pair past the last tap loads the
+          // last tap again (its rows are not stored)
+          int sp, km, ctile, pr;
+          wg_tile(tile, sp, km, ctile, pr);
+          int kb0, kb1;
+          wg_range(sp, kb0, kb1);
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s_ = it % cStages;
+            const uint32_t ph = (it / cStages) & 1;
+            if ((int)(it % cProducers) != warp) continue;
+            if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
+            const int q0 = (kb % a.tq) * a.bw, p0 = ((kb / a.tq) % a.tp) * a.bh, n0 = (kb / (a.tq * a.tp)) * a.bni;
+            uint8_t* sa = smem + s_ * L::STAGE_BYTES;
+            uint8_t* sb = sa + L::A_BYTES;
+            mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
+#pragma unroll
+            for (int j = 0; j < cBM / 32; ++j) {
+              const int tap = min(2 * pr + (j >> 1), RS - 1), r = tap / a.S, s = tap - r * a.S;
+              tma_load_4d(sa + j * 32 * cBK * 4, &tmA, &full[s_], 32 * (j & 1), q0 * a.sw + a.tap_w[s],
+                          p0 * a.sh + a.tap_h[r], n0);
+            }
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              tma_load_4d(sb + j * 32 * cBK * 4, &tmB, &full[s_], ctile * BN + 32 * j, q0, p0, n0);
           }
         } else if (MODE == kWgrad) {
           int sp, km, ctile, rs;
@@ -468,6 +497,36 @@ __global__ void __launch_bounds__(cThreads, 1)
             if (lane == 0) {
               if (a.epi == kEpiBox) tma_store_4d(&tmC, st, bx, by, k0, bn);
               else tma_store_3d(&tmC, st, bx, k0, bn);
+              bulk_commit();
+            }
+          }
+        }
+      } else if (MODE == kWgradT) {
+        // partials [splits * taps][input channel][output channel]: TMEM row
+        // (tap 2 pair + quarter / 2, channel 32 (quarter % 2) + lane) holds
+        // the output channels along its columns, stored as a row-major
+        // 128-byte-swizzled box (lane writes its eight 16-byte pieces at
+        // piece ^ (lane % 8), conflict-free per quarter warp)
+        int sp, km, ctile, pr;
+        wg_tile(tile, sp, km, ctile, pr);
+        const int tap = 2 * pr + (quarter >> 1), c0 = (quarter & 1) * 32;
+        const bool rows_ok = tap < RS && c0 < a.Cin;
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          const int k0 = ctile * BN + c * 32;
+          if (rows_ok && k0 < a.Kout) {  // warp-uniform
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
+            float4* rowp = reinterpret_cast<float4*>(st + lane * 32);
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch)
+              rowp[ch ^ (lane & 7)] = make_float4(v[4 * ch], v[4 * ch + 1], v[4 * ch + 2], v[4 * ch + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tmC, st, k0, c0, sp * RS + tap);
               bulk_commit();
             }
           }
@@ -1319,6 +1378,59 @@ static int run_wgrad(const float* dyn, int Kp, const float* xn, int Cp, int N, i
   return launch_bn<kWgrad>(p.BN, ma, mb, mc, a, s);
 }
 
+// Weight gradients with at most 64 input and output channels (ResNet's
+// layer1 3x3): two taps x 64 input channels fill the 128 accumulator rows
+// (kWgradT) instead of 64 output channels leaving half of them empty.
+static bool use_wgrad_t(const pvb2_conv2d_desc* d) { return d->K <= 64 && d->C <= 64 && d->R * d->S >= 2; }
+
+static WgPlan plan_wg_t(int N, int K, int Cin, int P, int Q, int taps) {
+  WgPlan w;
+  pixel_block(P, Q, cBK, w.bw, w.bh, w.bni);
+  w.BN = 64;
+  w.kt = 1;
+  w.ct = (K + 63) / 64;
+  const int tq = (Q + w.bw - 1) / w.bw, tp = (P + w.bh - 1) / w.bh, tn = (N + w.bni - 1) / w.bni;
+  w.total_kb = tq * tp * tn;
+  plan_splits(w, (taps + 1) / 2, (double)K * Cin * taps, 4.0 * N * P * Q * ((double)K + Cin));
+  return w;
+}
+
+// dy: channels-last [N, P, Q, Kp]; x: channels-last [N, H, W, Cp]; partials
+// [splits * taps][Cin][K] (the layout run_wgrad writes)
+static int run_wgrad_t(const float* dyn, int Kp, const float* xn, int Cp, int N, int H, int W, int P, int Q, int K,
+                       int Cin, const Taps& t, int sh, int sw, const WgPlan& p, float* part, cudaStream_t s) {
+  CUtensorMap ma, mb, mc;
+  PVB2_TRY(act_map(&ma, xn, N, H, W, Cp, p.bw, p.bh, p.bni, sw, sh, true));
+  PVB2_TRY(act_map(&mb, dyn, N, P, Q, Kp, p.bw, p.bh, p.bni, 1, 1, true));
+  const int taps = t.nr * t.ns;
+  {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)Cin, (uint64_t)p.splits * taps};
+    uint64_t str[2] = {(uint64_t)round4(K) * 4, (uint64_t)round4(K) * Cin * 4};
+    uint32_t box[3] = {32, 32, 1};
+    PVB2_TRY(encode_tiled(&mc, 3, part, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  ConvTcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.N = N; a.Cin = Cin; a.Cp = Cp; a.Kout = K; a.P = P; a.Q = Q; a.R = t.nr; a.S = t.ns;
+  a.sh = sh; a.sw = sw;
+  for (int i = 0; i < kMaxTaps; ++i) {
+    a.tap_h[i] = t.h[i];
+    a.tap_w[i] = t.w[i];
+  }
+  a.bw = p.bw; a.bh = p.bh; a.bni = p.bni;
+  a.tq = (Q + p.bw - 1) / p.bw;
+  a.tp = (P + p.bh - 1) / p.bh;
+  a.tn = (N + p.bni - 1) / p.bni;
+  a.kt = 1;
+  a.ct = p.ct;
+  a.splits = p.splits;
+  a.kb_per_split = p.kb_per;
+  a.total_kb = p.total_kb;
+  a.out = part;
+  a.tiles = a.ct * ((taps + 1) / 2) * a.splits;
+  return launch_conv<64, kWgradT>(ma, mb, mc, a, s);
+}
+
 // pointwise weight gradient into partials [splits][C][K]
 static int run_pw_wgrad(const float* dy, const float* x, int N, int C, int K, int64_t hw, const WgPlan& p,
                         float* part, cudaStream_t s) {
@@ -1515,7 +1627,8 @@ static Layout wgrad_layout(const pvb2_conv2d_desc* d, WgPlan* plan) {
   const int Kp = round4(d->K);
   const int Cx = round4(d->C);
   const int taps = d->R * d->S;
-  WgPlan p = plan_wg(d->N, d->K, d->C, d->P, d->Q, taps);
+  WgPlan p = use_wgrad_t(d) ? plan_wg_t(d->N, d->K, d->C, d->P, d->Q, taps)
+                            : plan_wg(d->N, d->K, d->C, d->P, d->Q, taps);
   if (plan) *plan = p;
   l.a = 0;                                                     // x channels-last
   l.b = align256((size_t)d->N * d->H * d->W * Cx * 4);         // dy channels-last
@@ -1800,8 +1913,13 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
   PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
   const int Cp = round4(d->C);
   if (!staged) PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
-  PVB2_TRY(run_wgrad(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h, d->stride_w,
-                     p, part, s));
+  if (use_wgrad_t(d)) {
+    PVB2_TRY(run_wgrad_t(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h,
+                         d->stride_w, p, part, s));
+  } else {
+    PVB2_TRY(run_wgrad(dyn, Kp, xn, Cp, d->N, d->H, d->W, d->P, d->Q, d->K, d->C, fwd_taps(d), d->stride_h,
+                       d->stride_w, p, part, s));
+  }
   // partials [sp][rs][c][k] -> dW[k][c][rs]
   PVB2_TRY(wgrad_reduce(part, p.splits, RS, d->K, d->C, d->K, d->C, dw, (int64_t)d->C * RS, RS, 1, s));
   *handled = true;
