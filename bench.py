@@ -335,6 +335,20 @@ def run_ours(a):
                "h2d_bytes_per_step": int(x.numel() * x.element_size() + y.numel() * y.element_size()),
                "d2h_bytes_per_step": 4, "ms_per_step": round(ems, 3)}
 
+    # ------------------------------- data parallel: exposure and agreement
+    # the last step's gradient all-reduce time past the end of backward, and
+    # a bit-for-bit comparison of every rank's parameters with rank 0's (a
+    # run whose ranks diverged is not a data-parallel run and fails)
+    dp = None
+    if world > 1:
+        exposed = max_over_ranks(net.exposed_comm_ms())
+        agree = net.params_agree()
+        dp = {"exposed_comm_ms_last_step": round(exposed, 4), "params_agree_across_ranks": bool(agree),
+              "buckets": len(net.buckets)}
+        if not agree:
+            sys.stderr.write("bench: ranks hold different parameters after the timed steps\n")
+            sys.exit(4)
+
     # --------------------------------------- dominant kernel class roofline
     # every rank runs this step (its gradient all-reduces must be matched on
     # all ranks); rank 0 records it under the profiler
@@ -415,6 +429,7 @@ def run_ours(a):
                        "l2": "inputs/activations larger than L2 (126 MB) every step",
                        "gflop_per_step": round(total_flops / 1e9, 1)},
             "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "roofline_bn": roof_bn, "cpu_baseline": cpu,
+            **({"dp": dp} if dp else {}),
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

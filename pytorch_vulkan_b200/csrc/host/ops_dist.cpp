@@ -71,6 +71,11 @@ static void stream_wait_stream(int dev, int64_t waiter, int64_t waitee) {
   OCL_CHECK(pvb2_event_destroy(e));  // destruction is deferred by CUDA until the wait resolves
 }
 static void stream_synchronize(int dev, int64_t id) { OCL_CHECK(pvb2_stream_synchronize(stream_of(dev, id))); }
+// record a (timing) event of impl_event_create on stream `id` of device `dev`
+static void event_record_stream(uintptr_t e, int dev, int64_t id) {
+  DeviceScope scope(dev);
+  OCL_CHECK(pvb2_event_record((pvb2_event)e, stream_of(dev, id)));
+}
 static void record_stream(const at::Tensor& t, int64_t id) {
   allocator_record_stream(t.storage().data_ptr(), stream_of(t.device().index(), id));
 }
@@ -112,6 +117,7 @@ void register_dist_bindings(pybind11::module& m) {
   m.def("impl_set_stream", &set_stream);
   m.def("impl_stream_wait_stream", &stream_wait_stream);
   m.def("impl_stream_synchronize", &stream_synchronize);
+  m.def("impl_event_record_stream", &event_record_stream);
   m.def("impl_record_stream", &record_stream);
   m.def("impl_flatten_multi", &flatten_multi);
 }

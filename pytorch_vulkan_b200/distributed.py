@@ -12,7 +12,12 @@ Gradient buckets (about 25 MB, filled in reverse registration order, which
 is close to the order backward produces them) are flattened into one buffer
 by a single multi-tensor kernel as soon as their last gradient is
 accumulated, then all-reduced (average) on a separate communication stream
-while the rest of backward runs.  After backward the compute stream waits
+while the rest of backward runs.  The bucket of the first-registered
+parameters, which backward finishes last, is kept small (about 2 MB), so
+the all-reduce left after backward ends is short; ``exposed_comm_ms`` reports
+how long the communication stream ran past the end of backward in the last
+step (device events), and ``params_agree`` checks that every rank holds
+bit-identical parameters.  After backward the compute stream waits
 for the communication stream and every parameter's ``.grad`` is pointed at
 its slice of the reduced bucket, so the optimizer reads the averaged
 gradients with no copy back.
@@ -95,7 +100,7 @@ class DistributedDataParallel(torch.nn.Module):
     state from rank 0, bucketed gradient averaging overlapped with backward."""
 
     def __init__(self, module: torch.nn.Module, comm: Optional[Communicator] = None, bucket_cap_mb: float = 25.0,
-                 group=None):
+                 group=None, last_bucket_cap_mb: float = 2.0):
         super().__init__()
         self.module = module
         self.comm = comm
@@ -105,17 +110,20 @@ class DistributedDataParallel(torch.nn.Module):
         self.device = params[0].device if params else torch.device("cpu")
         self.on_ocl = self.device.type == "ocl"
         cap = int(bucket_cap_mb * 1024 * 1024 / 4)
-        self.buckets: List[_Bucket] = []
+        first_cap = int(last_bucket_cap_mb * 1024 * 1024 / 4)
+        # groups in registration order, the first one small; reduced last-first
+        groups: List[List[torch.nn.Parameter]] = []
         cur: List[torch.nn.Parameter] = []
         size = 0
-        for p in reversed(params):
+        for p in params:
             cur.append(p)
             size += p.numel()
-            if size >= cap:
-                self.buckets.append(_Bucket(cur, self.device))
+            if size >= (first_cap if not groups else cap):
+                groups.append(cur)
                 cur, size = [], 0
         if cur:
-            self.buckets.append(_Bucket(cur, self.device))
+            groups.append(cur)
+        self.buckets: List[_Bucket] = [_Bucket(list(reversed(g)), self.device) for g in reversed(groups)]
         self._owner = {}
         for b in self.buckets:
             for p in b.params:
@@ -123,6 +131,10 @@ class DistributedDataParallel(torch.nn.Module):
                 p.register_post_accumulate_grad_hook(self._hook)
         self._queued = False
         self._launched: List[_Bucket] = []
+        self._ev = None
+        if self.on_ocl and self.world > 1:
+            self._ev = (_C.impl_event_create(True), _C.impl_event_create(True))
+        self._timed = False
         self._broadcast_state()
 
     # -- initial state: every rank starts from rank 0's weights and buffers
@@ -179,7 +191,41 @@ class DistributedDataParallel(torch.nn.Module):
                 self._launch(b)
         if self.on_ocl:
             dev = self.device.index or 0
+            # backward's last kernel vs the communication stream's last all-reduce
+            _C.impl_event_record_stream(self._ev[0], dev, _C.impl_get_stream(dev))
+            _C.impl_event_record_stream(self._ev[1], dev, self.comm.stream)
+            self._timed = True
             _C.impl_stream_wait_stream(dev, _C.impl_get_stream(dev), self.comm.stream)
         for b in self.buckets:
             for p, off in zip(b.params, b.offsets):
                 p.grad = b.flat[off:off + p.numel()].view_as(p)
+
+    def exposed_comm_ms(self) -> float:
+        """Device time the gradient all-reduces ran past the end of the last
+        backward (0 when they finished first); synchronises on the events."""
+        if not self._timed:
+            return 0.0
+        return max(0.0, _C.impl_event_elapsed_ms(self._ev[0], self._ev[1]))
+
+    def params_agree(self) -> bool:
+        """True when every rank's parameters and floating buffers equal rank
+        0's bit for bit (rank 0's flat copy broadcast, the per-rank maximum
+        difference all-reduced with MAX)."""
+        if self.world == 1:
+            return True
+        ts = [t.detach() for t in list(self.module.parameters()) + list(self.module.buffers()) if t.is_floating_point()]
+        if self.on_ocl:
+            flat = torch.empty(sum(t.numel() for t in ts), dtype=torch.float32, device=self.device)
+            _C.impl_flatten_multi([t.contiguous() for t in ts], flat, 0, 1.0)
+            ref = flat.clone()
+            self.comm.broadcast_(ref, 0, stream=0)
+            d = (flat - ref).abs().max().reshape(1)
+            self.comm.allreduce_(d, SUM, stream=0)  # any nonzero difference anywhere stays nonzero
+            torch.ocl.synchronize(self.device)
+            return d.item() == 0.0
+        flat = torch.cat([t.reshape(-1).float() for t in ts])
+        ref = flat.clone()
+        dist.broadcast(ref, 0, group=self.group)
+        d = (flat - ref).abs().max().reshape(1)
+        dist.all_reduce(d, op=dist.ReduceOp.MAX, group=self.group)
+        return d.item() == 0.0

@@ -8,6 +8,9 @@ here without a GPU:
   * the averaged gradients of 2 ranks x 4 samples equal the gradients of one
     process on all 8 samples (mean loss), with many small buckets;
   * rank 0's initial weights reach rank 1;
+  * the first-registered parameters form the last, small bucket, and
+    params_agree() reports equal parameters after an SGD step and a
+    difference once one rank's weights move;
   * a rank that raises before the exchange makes the other rank's collective
     fail within the process-group timeout instead of hanging.
 """
@@ -51,7 +54,7 @@ def _worker(rank, world, port, out, mode):
         with torch.no_grad():  # rank 1 starts from different weights: DDP must broadcast rank 0's
             for p in model.parameters():
                 p.add_(1.0)
-    ddp = DistributedDataParallel(model, None, bucket_cap_mb=0.0005)  # many small buckets
+    ddp = DistributedDataParallel(model, None, bucket_cap_mb=0.0005, last_bucket_cap_mb=0.0002)  # many small buckets
     x, y = _data()
     xs, ys = x[rank * 4:(rank + 1) * 4], y[rank * 4:(rank + 1) * 4]
     try:
@@ -61,6 +64,14 @@ def _worker(rank, world, port, out, mode):
         loss.backward()
         out[rank] = {n: p.grad.clone() for n, p in model.named_parameters()}
         out[f"w{rank}"] = {n: p.detach().clone() for n, p in model.named_parameters()}
+        # bucket order: the last bucket holds the first-registered parameter
+        out[f"last{rank}"] = [tuple(p.shape) for p in ddp.buckets[-1].params]
+        torch.optim.SGD(model.parameters(), lr=0.1).step()
+        out[f"agree{rank}"] = ddp.params_agree()
+        if rank == 1:
+            with torch.no_grad():
+                next(model.parameters()).add_(1e-3)
+        out[f"disagree{rank}"] = not ddp.params_agree()
     except Exception as e:  # noqa: BLE001
         out[f"err{rank}"] = type(e).__name__ + ": " + str(e)[:200]
     finally:
@@ -95,6 +106,10 @@ def test_bucketed_average_equals_full_batch():
         assert torch.allclose(out[0][n], p.grad, atol=1e-6), n
         assert torch.allclose(out[1][n], p.grad, atol=1e-6), n
         assert torch.equal(out["w0"][n], out["w1"][n]), n  # rank 0's weights broadcast
+    first = tuple(next(model.parameters()).shape)
+    assert first in out["last0"] and out["last0"] == out["last1"]
+    assert out["agree0"] and out["agree1"]
+    assert out["disagree0"] and out["disagree1"]
 
 
 def test_failed_rank_is_reported_not_hung():
