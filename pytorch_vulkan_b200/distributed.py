@@ -208,12 +208,13 @@ class DistributedDataParallel(torch.nn.Module):
         return max(0.0, _C.impl_event_elapsed_ms(self._ev[0], self._ev[1]))
 
     def params_agree(self) -> bool:
-        """True when every rank's parameters and floating buffers equal rank
-        0's bit for bit (rank 0's flat copy broadcast, the per-rank maximum
-        difference all-reduced with MAX)."""
+        """True when every rank's parameters equal rank 0's bit for bit (rank
+        0's flat copy broadcast, the per-rank maximum differences summed).
+        Buffers are not compared: batch-norm running statistics follow each
+        rank's own batches, as with DDP's broadcast_buffers=False."""
         if self.world == 1:
             return True
-        ts = [t.detach() for t in list(self.module.parameters()) + list(self.module.buffers()) if t.is_floating_point()]
+        ts = [p.detach() for p in self.module.parameters()]
         if self.on_ocl:
             flat = torch.empty(sum(t.numel() for t in ts), dtype=torch.float32, device=self.device)
             _C.impl_flatten_multi([t.contiguous() for t in ts], flat, 0, 1.0)
