@@ -247,6 +247,16 @@ PVB2_API int pvb2_batch_norm_bwd_relu(const pvb2_tensor* grad_above, const pvb2_
                                       const float* invstd, const pvb2_tensor* dy, const pvb2_tensor* dx,
                                       float* dgamma, float* dbeta, void* workspace, size_t workspace_bytes,
                                       pvb2_stream stream);
+/* The same below ReLU (act = 1, exactly pvb2_batch_norm_bwd_relu) or ReLU6
+ * (act = 2): with act_out the ReLU6 output,
+ *     dy = (act_out <= 0 || act_out >= 6) ? 0 : grad_above
+ * as hardtanh_backward(grad_above, act_out, 0, 6) computes it
+ * (pointwise_ops.cpp:559-603).  MobileNet-v2's conv -> batch norm -> ReLU6. */
+PVB2_API int pvb2_batch_norm_bwd_act(int act, const pvb2_tensor* grad_above, const pvb2_tensor* act_out,
+                                     const pvb2_tensor* x, const float* gamma, const float* mean,
+                                     const float* invstd, const pvb2_tensor* dy, const pvb2_tensor* dx,
+                                     float* dgamma, float* dbeta, void* workspace, size_t workspace_bytes,
+                                     pvb2_stream stream);
 /* Training forward in two calls, so that a host can fuse what follows the
  * normalisation into the second pass: pvb2_batch_norm_fwd_stats writes the
  * per-CTA partial sums of x into the workspace; pvb2_batch_norm_fwd_apply
@@ -254,23 +264,26 @@ PVB2_API int pvb2_batch_norm_bwd_relu(const pvb2_tensor* grad_above, const pvb2_
  * pvb2_batch_norm_fwd_train) and writes
  *     y = act(gamma * (x - mean) * invstd + beta + residual)
  * with residual optional (NULL, or contiguous and shaped like x) and act the
- * identity (relu = 0) or ReLU (relu = 1, NaN kept).  With sum_out given (it
- * needs a residual, and may be the residual tensor itself), y receives the
- * plain normalised values and sum_out the epilogue result.  With residual
- * NULL and relu 0 the pair computes exactly what pvb2_batch_norm_fwd_train
+ * identity (act = 0), ReLU (act = 1) or ReLU6 = hardtanh(0, 6) (act = 2),
+ * NaN kept by both; other values are rejected.  With sum_out given (it may
+ * be the residual tensor itself), y receives the plain normalised values and
+ * sum_out the epilogue result (a host keeps a copy of the values before an
+ * in-place activation this way, or adds the output into another tensor).  With residual
+ * NULL and act 0 the pair computes exactly what pvb2_batch_norm_fwd_train
  * does.
  * Both need pvb2_batch_norm_fwd_split_ok(x) (contiguous fp32 NCHW within the
  * streaming kernels' size limits) and the workspace of
  * pvb2_batch_norm_workspace_size, untouched between the two calls.  The
  * reference's torch front end ran batch norm, the residual add and the ReLU
- * as three ops (norm_ops.cpp:19-84, pointwise_ops.cpp:55-113). */
+ * (or ReLU6) as three ops (norm_ops.cpp:19-84, pointwise_ops.cpp:55-113,
+ * :559-603). */
 PVB2_API int pvb2_batch_norm_fwd_split_ok(const pvb2_tensor* x);
 PVB2_API int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, size_t workspace_bytes,
                                        pvb2_stream stream);
 PVB2_API int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const float* beta,
                                        float* running_mean, float* running_var, double momentum, double eps,
                                        const pvb2_tensor* y, float* save_mean, float* save_invstd,
-                                       const pvb2_tensor* residual, int relu, const pvb2_tensor* sum_out,
+                                       const pvb2_tensor* residual, int act, const pvb2_tensor* sum_out,
                                        const void* workspace, size_t workspace_bytes, pvb2_stream stream);
 /* Batch-norm training forward that allocates nothing and takes no workspace.
  * No counterpart in the reference: it exists for callers that cannot

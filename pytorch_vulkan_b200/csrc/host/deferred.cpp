@@ -6,16 +6,22 @@
 // launches its statistics pass at once and leaves the normalising pass
 // pending; an in-place add of a residual into its output and an in-place
 // ReLU of its output join that pass (pvb2_batch_norm_fwd_apply with a
-// residual and relu = 1) instead of re-reading the tensor.  Anything else
+// residual and act = 1), as does MobileNet's in-place ReLU6 (act = 2),
+// instead of re-reading the tensor.  The autograd kernel of an in-place
+// hardtanh_ first clones its input (the backward reads the values before the
+// activation): a copy of the pending output into a fresh contiguous tensor
+// joins the pass too, which then writes the plain values to the copy and the
+// activated ones to y.  Anything else
 // that touches the device first launches what is pending: every op entry
 // (DeviceScope, ExecGuard), stream and event calls, synchronisation.  The
 // pending state holds references to every tensor the pass reads or writes,
 // so none of them can be freed or reused before it runs.
 //
-// Backward, the mirror image: threshold_backward (the ReLU gradient) is left
-// pending, and when the next op is the backward of the batch norm that fed
-// that ReLU, its first pass forms the gradient from the ReLU output on the
-// fly (pvb2_batch_norm_bwd_relu), still storing it to the op's output tensor.
+// Backward, the mirror image: threshold_backward (the ReLU gradient) or
+// hardtanh_backward(.., 0, 6) (ReLU6's) is left pending, and when the next op
+// is the backward of the batch norm that fed that activation, its first pass
+// forms the gradient from the activation's output on the fly
+// (pvb2_batch_norm_bwd_act), still storing it to the op's output tensor.
 //
 // Input gradients of 1x1 stride-1 convolutions (a residual block's first
 // convolution) are left pending as well: when the next op adds that gradient
@@ -39,17 +45,20 @@ namespace {
 struct PendingBn {
   // out: where the epilogue result goes when it is not y itself (an in-place
   // add into another tensor of the pending output, `out += y`)
-  at::Tensor x, y, weight, bias, running_mean, running_var, save_mean, save_invstd, residual, out;
+  // copy: a tensor that takes the plain normalised values, y then taking the
+  // epilogue result (a clone of y made before an in-place activation)
+  at::Tensor x, y, weight, bias, running_mean, running_var, save_mean, save_invstd, residual, out, copy;
   double momentum = 0.0, eps = 0.0;
   c10::DataPtr ws;
   size_t ws_bytes = 0;
   pvb2_stream stream = nullptr;
   int device = 0;
-  bool relu = false;
+  int act = 0;  // 0 none, 1 ReLU, 2 ReLU6
 };
 
-struct PendingThr {  // grad_input = self <= 0 ? 0 : grad
+struct PendingThr {  // act 1: out = self <= 0 ? 0 : grad; act 2: (self <= 0 || self >= 6) ? 0 : grad
   at::Tensor grad, self, out;
+  int act = 1;
   pvb2_stream stream = nullptr;
   int device = 0;
 };
@@ -82,24 +91,43 @@ bool defer_enabled() {
 
 float* fptr(const at::Tensor& t) { return t.defined() ? t.data_ptr<float>() : nullptr; }
 
-void launch(PendingBn& p, const char* name) {
+// the op name of a pending pass, by what joined it
+const char* apply_name(const PendingBn& p) {
+  static const char* const names[2][2][3] = {
+      {{"native_batch_norm.apply", "native_batch_norm.apply+relu_", "native_batch_norm.apply+hardtanh_"},
+       {"native_batch_norm.apply+add_", "native_batch_norm.apply+add_+relu_",
+        "native_batch_norm.apply+add_+hardtanh_"}},
+      {{"native_batch_norm.apply+copy_", "native_batch_norm.apply+copy_+relu_",
+        "native_batch_norm.apply+copy_+hardtanh_"},
+       {"native_batch_norm.apply+copy_+add_", "native_batch_norm.apply+copy_+add_+relu_",
+        "native_batch_norm.apply+copy_+add_+hardtanh_"}}};
+  return names[p.copy.defined()][p.residual.defined()][p.act];
+}
+
+void launch(PendingBn& p) {
   DeviceScope scope(p.device);
-  OCL_OP(name, p.device);
-  const pvb2_tensor xd = desc(p.x), yd = desc(p.y);
+  OCL_OP(apply_name(p), p.device);
+  // the kernel's y takes the plain values, its sum_out the epilogue result
+  const at::Tensor& plain = p.copy.defined() ? p.copy : p.y;
+  const at::Tensor& epi = p.copy.defined() ? p.y : p.out;
+  const pvb2_tensor xd = desc(p.x), yd = desc(plain);
   pvb2_tensor rd, od;
   if (p.residual.defined()) rd = desc(p.residual);
-  if (p.out.defined()) od = desc(p.out);
+  if (epi.defined()) od = desc(epi);
   OCL_CHECK(pvb2_batch_norm_fwd_apply(&xd, fptr(p.weight), fptr(p.bias), fptr(p.running_mean), fptr(p.running_var),
                                       p.momentum, p.eps, &yd, fptr(p.save_mean), fptr(p.save_invstd),
-                                      p.residual.defined() ? &rd : nullptr, p.relu ? 1 : 0,
-                                      p.out.defined() ? &od : nullptr, p.ws.get(), p.ws_bytes, p.stream));
+                                      p.residual.defined() ? &rd : nullptr, p.act, epi.defined() ? &od : nullptr,
+                                      p.ws.get(), p.ws_bytes, p.stream));
 }
 
 void launch_thr(PendingThr& t) {
   DeviceScope scope(t.device);
-  OCL_OP("threshold_backward", t.device);
+  OCL_OP(t.act == 2 ? "hardtanh_backward" : "threshold_backward", t.device);
   const pvb2_tensor od = desc(t.out), gd = desc(t.grad), sd = desc(t.self);
-  OCL_CHECK(pvb2_binary(PVB2_BIN_THRESHOLD_BWD, &od, &gd, &sd, 0.0, 0.0, PVB2_F32, t.stream));
+  if (t.act == 2)
+    OCL_CHECK(pvb2_binary(PVB2_BIN_HARDTANH_BWD, &od, &gd, &sd, 0.0, 6.0, PVB2_F32, t.stream));
+  else
+    OCL_CHECK(pvb2_binary(PVB2_BIN_THRESHOLD_BWD, &od, &gd, &sd, 0.0, 0.0, PVB2_F32, t.stream));
 }
 
 // dx: where the gradient goes (gx, or the sum's output when addend is set)
@@ -141,7 +169,7 @@ void flush_deferred() {
   t_flushing = true;
   try {
     auto p = take();
-    if (p.bn) launch(*p.bn, p.bn->residual.defined() ? "native_batch_norm.apply+add_" : "native_batch_norm.apply");
+    if (p.bn) launch(*p.bn);
     if (p.thr) launch_thr(*p.thr);
     if (p.dgrad && !p.dgrad->unwritten) launch_dgrad(*p.dgrad, p.dgrad->gx, at::Tensor());
     if (p.dgrad && p.dgrad->unwritten) {
@@ -204,7 +232,7 @@ static bool same_tensor(const at::Tensor& a, const at::Tensor& b) {
 bool fuse_deferred_add(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha) {
   if (!g_any.load(std::memory_order_acquire)) return false;
   std::lock_guard<std::mutex> g(g_mutex);
-  if (!g_pending || g_pending->relu || g_pending->residual.defined()) return false;
+  if (!g_pending || g_pending->act || g_pending->residual.defined() || g_pending->copy.defined()) return false;
   PendingBn& p = *g_pending;
   if (alpha.isComplex() || alpha.toDouble() != 1.0) return false;
   // `y += other` (ResNet's out += identity) or `self += y` (the same add when
@@ -222,7 +250,23 @@ bool fuse_deferred_add(const at::Tensor& self, const at::Tensor& other, const at
   return true;
 }
 
-bool fuse_deferred_relu(const at::Tensor& self) {
+bool fuse_deferred_copy(const at::Tensor& dst, const at::Tensor& src) {
+  if (!g_any.load(std::memory_order_acquire)) return false;
+  std::lock_guard<std::mutex> g(g_mutex);
+  if (!g_pending || g_pending->act || g_pending->residual.defined() || g_pending->copy.defined()) return false;
+  PendingBn& p = *g_pending;
+  if (!same_tensor(src, p.y)) return false;
+  if (!is_ocl(dst) || dst.device() != p.y.device() || dst.scalar_type() != at::kFloat || !dst.is_contiguous() ||
+      !dst.sizes().equals(p.y.sizes()))
+    return false;
+  for (const at::Tensor* t : {&p.x, &p.y, &p.weight, &p.bias, &p.running_mean, &p.running_var, &p.save_mean,
+                              &p.save_invstd})
+    if (t->defined() && dst.is_alias_of(*t)) return false;
+  p.copy = dst;
+  return true;
+}
+
+bool fuse_deferred_act(const at::Tensor& self, int act) {
   if (!g_any.load(std::memory_order_acquire)) return false;
   std::optional<PendingBn> p;
   {
@@ -232,12 +276,12 @@ bool fuse_deferred_relu(const at::Tensor& self) {
     g_pending.reset();
     g_any.store(false, std::memory_order_release);
   }
-  p->relu = true;
-  launch(*p, p->residual.defined() ? "native_batch_norm.apply+add_+relu_" : "native_batch_norm.apply+relu_");
+  p->act = act;
+  launch(*p);
   return true;
 }
 
-bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const at::Tensor& out) {
+bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const at::Tensor& out, int act) {
   if (!defer_enabled()) return false;
   for (const at::Tensor* t : {&grad, &self, &out})
     if (!is_ocl(*t) || t->scalar_type() != at::kFloat || !t->is_contiguous() || !t->sizes().equals(out.sizes()))
@@ -248,6 +292,7 @@ bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const a
   t.grad = grad;
   t.self = self;
   t.out = out;
+  t.act = act;
   t.device = (int)out.device().index();
   t.stream = stream_for(t.device);
   for (;;) {
@@ -260,12 +305,13 @@ bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const a
   }
 }
 
-bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out) {
+bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out, int* act) {
   if (!g_any.load(std::memory_order_acquire)) return false;
   std::lock_guard<std::mutex> g(g_mutex);
   if (!g_thr || !same_tensor(grad_out, g_thr->out)) return false;
   *grad_above = g_thr->grad;
   *relu_out = g_thr->self;
+  *act = g_thr->act;
   g_thr.reset();
   g_any.store(false, std::memory_order_release);
   return true;

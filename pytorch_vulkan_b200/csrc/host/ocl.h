@@ -92,14 +92,19 @@ bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optiona
                     const at::Tensor& save_invstd, double momentum, double eps, Workspace&& ws, pvb2_stream stream);
 // true when `self += other * alpha` was folded into the pending pass
 bool fuse_deferred_add(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha);
-// true when `relu_(self)` was folded into the pending pass (and launched it)
-bool fuse_deferred_relu(const at::Tensor& self);
-// threshold_backward(grad, self, 0) into `out`, left pending (true) so that a
-// following batch-norm backward can form it in its first pass
-bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const at::Tensor& out);
-// when the pending threshold_backward wrote grad_out: hand over its inputs
-// (the batch-norm backward then stores grad_out itself) and clear it
-bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out);
+// true when `dst.copy_(src)` of the pending pass's output into a contiguous
+// tensor was folded into that pass (dst then takes the plain normalised values)
+bool fuse_deferred_copy(const at::Tensor& dst, const at::Tensor& src);
+// true when `relu_(self)` (act 1) or `hardtanh_(self, 0, 6)` (act 2) was
+// folded into the pending pass (and launched it)
+bool fuse_deferred_act(const at::Tensor& self, int act);
+// threshold_backward(grad, self, 0) (act 1) or hardtanh_backward(grad, self,
+// 0, 6) (act 2) into `out`, left pending (true) so that a following
+// batch-norm backward can form it in its first pass
+bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const at::Tensor& out, int act);
+// when the pending activation gradient wrote grad_out: hand over its inputs
+// and kind (the batch-norm backward then stores grad_out itself) and clear it
+bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out, int* act);
 // input gradient of a convolution whose dgrad can also form a sum
 // (pvb2_conv2d_bwd_data_acc_ok), left pending so that a following add of it
 // joins the dgrad's epilogue

@@ -448,16 +448,21 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward
     const std::optional<at::Tensor>& save_mean, const std::optional<at::Tensor>& save_invstd, bool train, double eps,
     std::array<bool, 3> output_mask) {
   const int dev = input.device().index();
-  // grad_out still pending as ReLU's gradient: form it in the first pass
+  // grad_out still pending as a ReLU's or ReLU6's gradient: form it in the
+  // first pass
   at::Tensor relu_grad, relu_out;
   bool below_relu = false;
+  int act = 0;
   if (train && input.is_contiguous() && input.scalar_type() == at::kFloat && save_mean.has_value() &&
       save_invstd.has_value()) {
     const pvb2_tensor xd0 = desc(input);
-    below_relu = pvb2_batch_norm_fwd_split_ok(&xd0) && take_deferred_threshold(grad_out, &relu_grad, &relu_out);
+    below_relu = pvb2_batch_norm_fwd_split_ok(&xd0) && take_deferred_threshold(grad_out, &relu_grad, &relu_out, &act);
   }
   DeviceScope scope(dev);
-  OCL_OP(below_relu ? "threshold_backward+native_batch_norm_backward" : "native_batch_norm_backward", dev);
+  OCL_OP(!below_relu ? "native_batch_norm_backward"
+                     : (act == 2 ? "hardtanh_backward+native_batch_norm_backward"
+                                 : "threshold_backward+native_batch_norm_backward"),
+         dev);
   at::Tensor x = contiguous(input), gy = below_relu ? grad_out : contiguous(grad_out);
   const int64_t C = x.size(1);
   const float* g = weight.has_value() && weight->defined() ? weight->data_ptr<float>() : nullptr;
@@ -474,10 +479,10 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward
     Workspace ws(pvb2_batch_norm_workspace_size(&xd), dev);
     if (below_relu) {
       const pvb2_tensor rgd = desc(relu_grad), rod = desc(relu_out);
-      OCL_CHECK(pvb2_batch_norm_bwd_relu(&rgd, &rod, &xd, g, save_mean->data_ptr<float>(),
-                                         save_invstd->data_ptr<float>(), &gyd, output_mask[0] ? &gxd : nullptr,
-                                         output_mask[1] ? gw.data_ptr<float>() : nullptr,
-                                         output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, st));
+      OCL_CHECK(pvb2_batch_norm_bwd_act(act, &rgd, &rod, &xd, g, save_mean->data_ptr<float>(),
+                                        save_invstd->data_ptr<float>(), &gyd, output_mask[0] ? &gxd : nullptr,
+                                        output_mask[1] ? gw.data_ptr<float>() : nullptr,
+                                        output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, st));
       return {gx, gw, gb};
     }
     OCL_CHECK(pvb2_batch_norm_bwd(&gyd, &xd, g, save_mean->data_ptr<float>(), save_invstd->data_ptr<float>(), 1,

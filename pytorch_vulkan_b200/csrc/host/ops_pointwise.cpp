@@ -142,7 +142,7 @@ static at::Tensor& threshold_backward_out(const at::Tensor& grad, const at::Tens
                                           at::Tensor& grad_input) {
   // ReLU's gradient: left pending for a following batch-norm backward
   if (!threshold.isComplex() && threshold.toDouble() == 0.0 && is_ocl(grad) && is_ocl(self) && is_ocl(grad_input) &&
-      grad_input.sizes().equals(grad.sizes()) && defer_threshold_bwd(grad, self, grad_input))
+      grad_input.sizes().equals(grad.sizes()) && defer_threshold_bwd(grad, self, grad_input, 1))
     return grad_input;
   return binary_out(PVB2_BIN_THRESHOLD_BWD, grad, self, grad_input, sc(threshold), 0, arith_compute(grad_input),
                     "threshold_backward");
@@ -152,7 +152,11 @@ static at::Tensor& threshold_backward_out(const at::Tensor& grad, const at::Tens
 static at::Tensor hardtanh(const at::Tensor& self, const at::Scalar& mn, const at::Scalar& mx) {
   return unary_new(PVB2_UN_HARDTANH, self, sc(mn), sc(mx), "hardtanh");
 }
+static bool is_relu6(const at::Scalar& mn, const at::Scalar& mx) {
+  return !mn.isComplex() && !mx.isComplex() && mn.toDouble() == 0.0 && mx.toDouble() == 6.0;
+}
 static at::Tensor& hardtanh_(at::Tensor& self, const at::Scalar& mn, const at::Scalar& mx) {
+  if (is_relu6(mn, mx) && fuse_deferred_act(self, 2)) return self;  // joined a pending batch-norm pass
   return unary_out(PVB2_UN_HARDTANH, self, self, sc(mn), sc(mx), "hardtanh_");
 }
 static at::Tensor& hardtanh_out(const at::Tensor& self, const at::Scalar& mn, const at::Scalar& mx, at::Tensor& out) {
@@ -160,6 +164,10 @@ static at::Tensor& hardtanh_out(const at::Tensor& self, const at::Scalar& mn, co
 }
 static at::Tensor& hardtanh_backward_out(const at::Tensor& grad, const at::Tensor& self, const at::Scalar& mn,
                                          const at::Scalar& mx, at::Tensor& grad_input) {
+  // ReLU6's gradient: left pending for a following batch-norm backward
+  if (is_relu6(mn, mx) && is_ocl(grad) && is_ocl(self) && is_ocl(grad_input) &&
+      grad_input.sizes().equals(grad.sizes()) && defer_threshold_bwd(grad, self, grad_input, 2))
+    return grad_input;
   return binary_out(PVB2_BIN_HARDTANH_BWD, grad, self, grad_input, sc(mn), sc(mx), arith_compute(grad_input),
                     "hardtanh_backward");
 }
@@ -173,7 +181,7 @@ static at::Tensor hardtanh_backward(const at::Tensor& grad, const at::Tensor& se
 // relu / relu_, :55-113
 static at::Tensor relu(const at::Tensor& self) { return unary_new(PVB2_UN_RELU, self, 0, 0, "relu"); }
 static at::Tensor& relu_(at::Tensor& self) {
-  if (fuse_deferred_relu(self)) return self;  // joined a pending batch-norm pass
+  if (fuse_deferred_act(self, 1)) return self;  // joined a pending batch-norm pass
   return unary_out(PVB2_UN_RELU, self, self, 0, 0, "relu_");
 }
 

@@ -190,6 +190,7 @@ void copy_into(const at::Tensor& dst, const at::Tensor& src, bool non_blocking) 
   } else if (src_dev && dst_dev) {
     const int dd = dst.device().index(), sd = src.device().index();
     if (dd == sd) {
+      if (fuse_deferred_copy(dst, src)) return;  // joined a pending batch-norm pass
       DeviceScope scope(dd);
       OCL_OP("copy_d2d", dd);
       pvb2_tensor d = desc(dst), s = desc(src);

@@ -416,19 +416,28 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_stats_kernel(const float* 
 }
 
 // y = act(a * x + b + residual): residual optional (same layout as x), act
-// the identity or ReLU (NaN kept, as torch's relu); the epilogue of
-// `bn(x) (+ identity)` followed by an in-place ReLU, fused by the host
-__device__ __forceinline__ float bn_epi(float v, const float* res, int64_t o, int relu) {
+// the identity (0), ReLU (1) or ReLU6 = hardtanh(0, 6) (2), NaN kept in both
+// as torch's relu and hardtanh keep it; the epilogue of `bn(x) (+ identity)`
+// followed by an in-place activation, fused by the host
+__device__ __forceinline__ float bn_epi(float v, const float* res, int64_t o, int act) {
   if (res) v += __ldg(res + o);
-  if (relu) v = v != v ? v : (v > 0.f ? v : 0.f);
+  if (act == 1) v = v != v ? v : (v > 0.f ? v : 0.f);
+  if (act == 2) v = v != v ? v : (v < 0.f ? 0.f : (v > 6.f ? 6.f : v));
   return v;
+}
+
+// the gradient below the activation bn_epi applied, from its output r and the
+// gradient g above it: ReLU as threshold_backward (r <= 0 ? 0 : g), ReLU6 as
+// hardtanh_backward ((r <= 0 || r >= 6) ? 0 : g); NaN outputs pass g
+__device__ __forceinline__ float act_grad(float r, float g, int act) {
+  return (r <= 0.f || (act == 2 && r >= 6.f)) ? 0.f : g;
 }
 
 __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
     const float* __restrict__ x, float* __restrict__ y, int N, int C, int HW, int chunk, int splits, int vec,
     const float* __restrict__ part, const float* __restrict__ gamma, const float* __restrict__ beta,
     float* __restrict__ running_mean, float* __restrict__ running_var, float momentum, float eps,
-    float* __restrict__ save_mean, float* __restrict__ save_invstd, const float* __restrict__ residual, int relu,
+    float* __restrict__ save_mean, float* __restrict__ save_invstd, const float* __restrict__ residual, int act,
     float* __restrict__ sum_out) {
   __shared__ float s_ab[2];
   const int s = blockIdx.x, c = C - 1 - blockIdx.y;
@@ -475,7 +484,7 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
   int e = start + vw * threadIdx.x;
   if (e >= end) return;
   ChanWalk w(e, step, HW);
-  const bool plain = rc == nullptr && !relu;
+  const bool plain = rc == nullptr && !act;
   if (vec) {
     for (; e < end; e += 4 * step) {
       float4 v[4];
@@ -496,10 +505,10 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
           r.w = fmaf(r.w, a, b);
           if (sc) *reinterpret_cast<float4*>(yc + o[u]) = r;
           if (!plain) {
-            r.x = bn_epi(r.x, rc, o[u], relu);
-            r.y = bn_epi(r.y, rc, o[u] + 1, relu);
-            r.z = bn_epi(r.z, rc, o[u] + 2, relu);
-            r.w = bn_epi(r.w, rc, o[u] + 3, relu);
+            r.x = bn_epi(r.x, rc, o[u], act);
+            r.y = bn_epi(r.y, rc, o[u] + 1, act);
+            r.z = bn_epi(r.z, rc, o[u] + 2, act);
+            r.w = bn_epi(r.w, rc, o[u] + 3, act);
           }
           *reinterpret_cast<float4*>((sc ? sc : yc) + o[u]) = r;
         }
@@ -521,9 +530,9 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
           const float r = fmaf(v[u], a, b);
           if (sc) {
             yc[o[u]] = r;
-            sc[o[u]] = bn_epi(r, rc, o[u], relu);
+            sc[o[u]] = bn_epi(r, rc, o[u], act);
           } else {
-            yc[o[u]] = bn_epi(r, rc, o[u], relu);
+            yc[o[u]] = bn_epi(r, rc, o[u], act);
           }
         }
     }
@@ -533,10 +542,11 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
 __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
     const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean, int N, int C, int HW,
     int chunk, int splits, int vec, float* __restrict__ part, const float* __restrict__ relu_y,
-    float* __restrict__ dy_out) {
-  // with relu_y: `dy` is the gradient above a ReLU whose output is relu_y;
-  // the gradient below it, (relu_y <= 0 ? 0 : dy) as threshold_backward
-  // computes it, is formed here, stored to dy_out and used for the sums
+    float* __restrict__ dy_out, int act) {
+  // with relu_y: `dy` is the gradient above an activation (act 1 ReLU, 2
+  // ReLU6) whose output is relu_y; the gradient below it, as
+  // threshold_backward or hardtanh_backward computes it (act_grad), is
+  // formed here, stored to dy_out and used for the sums
   __shared__ float red[64];
   const int s = blockIdx.x, c = blockIdx.y;
   const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
@@ -558,10 +568,10 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
         const float4 v = __ldg(reinterpret_cast<const float4*>(xc + o));
         if (yc) {
           const float4 r = __ldg(reinterpret_cast<const float4*>(yc + o));
-          g.x = r.x <= 0.f ? 0.f : g.x;
-          g.y = r.y <= 0.f ? 0.f : g.y;
-          g.z = r.z <= 0.f ? 0.f : g.z;
-          g.w = r.w <= 0.f ? 0.f : g.w;
+          g.x = act_grad(r.x, g.x, act);
+          g.y = act_grad(r.y, g.y, act);
+          g.z = act_grad(r.z, g.z, act);
+          g.w = act_grad(r.w, g.w, act);
           *reinterpret_cast<float4*>(oc + o) = g;
         }
         sg += (g.x + g.y) + (g.z + g.w);
@@ -579,7 +589,7 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
             g[u] = __ldg(gc + o);
             v[u] = __ldg(xc + o);
             if (yc) {
-              g[u] = __ldg(yc + o) <= 0.f ? 0.f : g[u];
+              g[u] = act_grad(__ldg(yc + o), g[u], act);
               oc[o] = g[u];
             }
           }
@@ -684,12 +694,12 @@ static int bn_fwd_stream(const BnGeom& g, const BnStream& p, const float* x, flo
 
 static int bn_bwd_stream(const BnGeom& g, const BnStream& p, const float* dy, const float* x, const float* mean,
                          const float* invstd, const float* gamma, float* dx, float* dgamma, float* dbeta, float* part,
-                         cudaStream_t s, const float* relu_y = nullptr, float* dy_out = nullptr) {
+                         cudaStream_t s, const float* relu_y = nullptr, float* dy_out = nullptr, int act = 0) {
   const dim3 grid((unsigned)p.splits, (unsigned)g.C);
   bn_st_bwd_reduce_kernel<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, (int)g.N, (int)g.C, (int)g.HW, p.chunk,
-                                                         p.splits, p.vec ? 1 : 0, part, relu_y, dy_out);
+                                                         p.splits, p.vec ? 1 : 0, part, relu_y, dy_out, act);
   PVB2_LAUNCH_CHECK();
-  if (relu_y) dy = dy_out;  // the apply pass reads the gradient below the ReLU
+  if (relu_y) dy = dy_out;  // the apply pass reads the gradient below the activation
   bn_st_bwd_apply_kernel<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, invstd, gamma, (int)g.N, (int)g.C, (int)g.HW,
                                                         p.chunk, p.splits, p.vec ? 1 : 0, part, dx, dgamma, dbeta);
   PVB2_LAUNCH_CHECK();
@@ -1092,10 +1102,11 @@ int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, size_t work
 
 int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const float* beta, float* running_mean,
                               float* running_var, double momentum, double eps, const pvb2_tensor* y,
-                              float* save_mean, float* save_invstd, const pvb2_tensor* residual, int relu,
+                              float* save_mean, float* save_invstd, const pvb2_tensor* residual, int act,
                               const pvb2_tensor* sum_out, const void* workspace, size_t workspace_bytes,
                               pvb2_stream stream) {
   PVB2_TRY(check_bn_x(x));
+  PVB2_CHECK_ARG(act >= 0 && act <= 2, "batch_norm: activation %d is not 0 (none), 1 (ReLU) or 2 (ReLU6)", act);
   PVB2_CHECK_ARG(pvb2_batch_norm_fwd_split_ok(x), "batch_norm: input not supported by the split forward");
   PVB2_CHECK_ARG(is_contiguous(y) && y->dtype == PVB2_F32 && numel(y) == numel(x),
                  "batch_norm: output must be contiguous float32 of the input's size");
@@ -1106,8 +1117,8 @@ int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const fl
       PVB2_CHECK_ARG(residual->sizes[d] == x->sizes[d], "batch_norm: residual shape differs at dim %d", d);
   }
   if (sum_out) {
-    PVB2_CHECK_ARG(residual && is_contiguous(sum_out) && sum_out->dtype == PVB2_F32 && numel(sum_out) == numel(x),
-                   "batch_norm: sum_out needs a residual and must be contiguous float32 of the input's size");
+    PVB2_CHECK_ARG(is_contiguous(sum_out) && sum_out->dtype == PVB2_F32 && numel(sum_out) == numel(x),
+                   "batch_norm: sum_out must be contiguous float32 of the input's size");
   }
   const BnGeom g = bn_geom(x);
   const void* ptrs[4] = {x->data, y->data, residual ? residual->data : nullptr, sum_out ? sum_out->data : nullptr};
@@ -1119,7 +1130,7 @@ int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const fl
   bn_st_apply_kernel<<<grid, kBnStThreads, 0, as_stream(stream)>>>(
       (const float*)x->data, (float*)y->data, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits, p.vec ? 1 : 0,
       (const float*)workspace, gamma, beta, running_mean, running_var, (float)momentum, (float)eps, save_mean,
-      save_invstd, residual ? (const float*)residual->data : nullptr, relu ? 1 : 0,
+      save_invstd, residual ? (const float*)residual->data : nullptr, act,
       sum_out ? (float*)sum_out->data : nullptr);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
@@ -1230,6 +1241,15 @@ int pvb2_batch_norm_bwd_relu(const pvb2_tensor* grad_above, const pvb2_tensor* r
                              const float* gamma, const float* mean, const float* invstd, const pvb2_tensor* dy,
                              const pvb2_tensor* dx, float* dgamma, float* dbeta, void* workspace,
                              size_t workspace_bytes, pvb2_stream stream) {
+  return pvb2_batch_norm_bwd_act(1, grad_above, relu_out, x, gamma, mean, invstd, dy, dx, dgamma, dbeta, workspace,
+                                 workspace_bytes, stream);
+}
+
+int pvb2_batch_norm_bwd_act(int act, const pvb2_tensor* grad_above, const pvb2_tensor* relu_out,
+                            const pvb2_tensor* x, const float* gamma, const float* mean, const float* invstd,
+                            const pvb2_tensor* dy, const pvb2_tensor* dx, float* dgamma, float* dbeta,
+                            void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+  PVB2_CHECK_ARG(act == 1 || act == 2, "batch_norm_backward: activation %d is not 1 (ReLU) or 2 (ReLU6)", act);
   PVB2_TRY(check_bn_x(x));
   for (const pvb2_tensor* t : {grad_above, relu_out, dy}) {
     PVB2_CHECK_ARG(t && is_contiguous(t) && t->dtype == PVB2_F32 && numel(t) == numel(x),
@@ -1243,7 +1263,7 @@ int pvb2_batch_norm_bwd_relu(const pvb2_tensor* grad_above, const pvb2_tensor* r
   PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm_backward: workspace too small");
   return bn_bwd_stream(g, p, (const float*)grad_above->data, (const float*)x->data, mean, invstd, gamma,
                        dx ? (float*)dx->data : nullptr, dgamma, dbeta, (float*)workspace, as_stream(stream),
-                       (const float*)relu_out->data, (float*)dy->data);
+                       (const float*)relu_out->data, (float*)dy->data, act);
 }
 
 int pvb2_batch_norm_bwd_eval(const pvb2_tensor* dy, const float* gamma, const float* running_var, double eps,

@@ -1,5 +1,5 @@
 """Deferred batch-norm pass: a training batch norm leaves its normalising
-pass pending and an in-place residual add / ReLU of its output joins it
+pass pending and an in-place residual add / ReLU / ReLU6 of its output joins it
 (csrc/host/deferred.cpp).  Every way the output can be read before, between
 or instead of those ops must see exactly what the three separate ops give;
 checked against torch-CPU on the same inputs (the reference's own arbiter,
@@ -189,4 +189,114 @@ def test_identity_bn_add_relu(ocl, shape):
     got = torch.relu_(out_d)
     assert _close(ref, got)
     assert _close(ident, ident_d)
+    _check_bn_state(cpu, dev)
+
+
+def _bn_pair_wide(C, seed):
+    """gamma in [2, 4] so that a good share of the outputs pass 6 and ReLU6
+    clamps (and masks the gradient) at both ends"""
+    cpu, dev = _bn_pair(C, seed)
+    with torch.no_grad():
+        cpu.weight.uniform_(2.0, 4.0)
+        dev.weight.copy_(cpu.weight)
+    return cpu, dev
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["x".join(map(str, s)) for s in SHAPES])
+def test_bn_relu6_inplace(ocl, shape):
+    """MobileNet-v2's batch norm -> ReLU6(inplace=True): hardtanh_(y, 0, 6)
+    joins the pending pass"""
+    cpu, dev = _bn_pair_wide(shape[1], 70)
+    x = _x(shape, 71)
+    ref = nn.functional.relu6(cpu(x), inplace=True)
+    got = nn.functional.relu6(dev(x.to(DEV)), inplace=True)
+    assert (ref == 6).any() and (ref == 0).any()
+    assert _close(ref, got)
+    _check_bn_state(cpu, dev)
+
+
+def test_bn_hardtanh_other_bounds_not_folded(ocl):
+    cpu, dev = _bn_pair_wide(16, 72)
+    x = _x((4, 16, 9, 9), 73)
+    ref = nn.functional.hardtanh(cpu(x), -1.0, 2.0, inplace=True)
+    got = nn.functional.hardtanh(dev(x.to(DEV)), -1.0, 2.0, inplace=True)
+    assert _close(ref, got)
+
+
+def test_relu6_grad_into_bn_backward(ocl):
+    """hardtanh_backward(.., 0, 6) left pending and formed inside the
+    batch-norm backward; with a second consumer of the batch-norm output the
+    pending op runs alone"""
+    for second_use in (False, True):
+        cpu, dev = _bn_pair_wide(24, 74 + second_use)
+        x = _x((4, 24, 10, 10), 76)
+        g1, g2 = _x((4, 24, 10, 10), 77), _x((4, 24, 10, 10), 78)
+        grads = []
+        for m, d in ((cpu, "cpu"), (dev, DEV)):
+            xx = x.detach().clone().to(d).requires_grad_()
+            y = m(xx)
+            a = nn.functional.relu6(y, inplace=not second_use)
+            loss = (a * g1.to(d)).sum()
+            if second_use:
+                loss = loss + (y * g2.to(d)).sum()
+            loss.backward()
+            grads.append((xx.grad, m.weight.grad, m.bias.grad))
+        for a, b in zip(*grads):
+            assert _close(a, b, 1e-4)
+
+
+def test_inverted_residual_forward_backward(ocl):
+    """MobileNet-v2's inverted residual (1x1 expand -> bn -> ReLU6 -> 3x3
+    depthwise -> bn -> ReLU6 -> 1x1 project -> bn, + x), forward and backward
+    in exact-fp32 math"""
+    old = torch.ocl.get_math_mode()
+    torch.ocl.set_math_mode(1)
+    try:
+        torch.manual_seed(79)
+        C, E = 24, 96
+        blk = nn.Sequential(nn.Conv2d(C, E, 1, bias=False), nn.BatchNorm2d(E), nn.ReLU6(inplace=True),
+                            nn.Conv2d(E, E, 3, padding=1, groups=E, bias=False), nn.BatchNorm2d(E),
+                            nn.ReLU6(inplace=True), nn.Conv2d(E, C, 1, bias=False), nn.BatchNorm2d(C))
+        with torch.no_grad():
+            for m in blk:
+                if isinstance(m, nn.BatchNorm2d):
+                    m.weight.uniform_(1.0, 4.0)
+        dev = copy.deepcopy(blk).to(DEV)
+        x = _x((4, C, 14, 14), 80)
+        xc, xd = x.clone().requires_grad_(), x.to(DEV).requires_grad_()
+        yc, yd = xc + blk(xc), xd + dev(xd)
+        assert _close(yc, yd, 1e-4)
+        g = _x(yc.shape, 81)
+        yc.backward(g)
+        yd.backward(g.to(DEV))
+        assert _close(xc.grad, xd.grad, 1e-4)
+        for (n, p), (_, q) in zip(blk.named_parameters(), dev.named_parameters()):
+            assert _close(p.grad, q.grad, 1e-4), n
+    finally:
+        torch.ocl.set_math_mode(old)
+
+
+@pytest.mark.parametrize("then", ["relu_", "relu6_", "add_", "mul", "none"])
+def test_bn_clone_joins_pass(ocl, then):
+    """a clone of the pending output (what autograd takes before an in-place
+    activation) joins the pass; the clone keeps the plain values whatever
+    happens to the output next"""
+    cpu, dev = _bn_pair_wide(16, 82)
+    x, r = _x((4, 16, 9, 9), 83), _x((4, 16, 9, 9), 84)
+
+    def run(m, d):
+        y = m(x.to(d))
+        c = y.clone()
+        if then == "relu_":
+            torch.relu_(y)
+        elif then == "relu6_":
+            nn.functional.relu6(y, inplace=True)
+        elif then == "add_":
+            y += r.to(d)
+        elif then == "mul":
+            y = y * 2
+        return y, c
+
+    (y0, c0), (y1, c1) = run(cpu, "cpu"), run(dev, DEV)
+    assert _close(c0, c1) and _close(y0, y1)
     _check_bn_state(cpu, dev)
