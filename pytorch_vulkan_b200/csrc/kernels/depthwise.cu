@@ -1,26 +1,27 @@
-// Depthwise convolution (groups == C == K, one filter per channel) as
-// shared-memory-staged stencils; MobileNet-v2's 3x3 layers at stride 1 and 2.
+// Depthwise convolution (groups == C == K, one filter per channel);
+// MobileNet-v2's 3x3 layers at stride 1 and 2.
 //
 // Replaces dlprim's grouped Conv2DForward / Conv2DBackwardData /
 // Conv2DBackwardFilter as convolution_overrideable reached them with
 // groups = C (src/vision_ops.cpp:30-59, 61-186).  All three are bound by
-// HBM (4 B per input and output element, the filter is tiny), so each CTA
-// reads a tile of its input plane once into shared memory, halo included,
-// and every thread computes its outputs from there.
+// HBM (4 B per input and output element, the filter is tiny).
 //
-//   forward  a CTA covers a TH x TW output tile of PP consecutive planes
-//            (n, c) (several whole planes when a plane is small: 7x7, 14x14),
-//            staging the (TH-1)*sh + (R-1)*dh + 1 by (TW-1)*sw + (S-1)*dw + 1
-//            input window of each and the planes' filters.
-//   dgrad    the same over a TH x TW tile of dX: the dY rows and columns the
-//            tile's taps reach are staged, each dX element sums the taps
-//            whose source position is a multiple of the stride.
-//   wgrad    a CTA takes one channel and a range of images; for each image
-//            it stages x and dY tile by tile and every thread adds its
-//            outputs' R*S products into registers.  The CTA's per-tap sums
-//            (fixed-order block reduction) are partials [C][chunks][R*S],
-//            summed in chunk order by dw_wgrad_reduce_kernel, so the result
-//            depends only on the shapes.
+//   3x3 (dilation 1, stride 1 or 2): direct register-blocked kernels, each
+//   thread four adjacent outputs of a row from 16-byte global loads, the
+//   overlap between neighbours served by L1 (dw3_*):
+//     forward  over x; the stride-1 input gradient is the same kernel over
+//              dY with the flipped filter and padding 2 - pad.
+//     dgrad    stride 2 (pad 1) by sub-pixel phases: a thread makes a 2 x 8
+//              block of dX from a 2 x 5 block of dY.
+//     wgrad    CTA (channel, chunk of its (image, row, column-group) items)
+//              sums dY * x per tap in registers, block-reduces in a fixed
+//              order to partials [C][9][chunks], and one warp per (c, tap)
+//              sums those in a fixed order, so the result depends only on
+//              the shapes.
+//   Other filters (5x5, other strides): shared-memory-staged tiles, each
+//   CTA staging a tile of its input plane with its halo and every thread
+//   computing its outputs from there (dw_*_tile_kernel); their weight
+//   gradient writes partials [C][chunks][taps] summed in chunk order.
 #include <algorithm>
 
 #include "common.cuh"
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(kDwThreads) dw_dgrad_tile_kernel(DwGeom g, con
   }
 }
 
-// ----------------------------------------- 3x3 forward, four outputs a thread
+// ------------------------------------------------- 3x3 direct kernels
 // Division by a runtime divisor d as a multiply-high and shift (Granlund and
 // Montgomery's method, as CUTLASS's FastDivmod states it): m = ceil(2^p / d),
 // p = 31 + ceil(log2 d); exact for dividends below 2^31.
@@ -247,199 +248,214 @@ static FastDiv fast_div(int d) {
 __device__ __forceinline__ int fdiv(int n, const FastDiv& f) {
   return f.d > 1 ? (int)(__umulhi((uint32_t)n, f.m) >> f.s) : n;
 }
-__device__ __forceinline__ FastDiv fast_div_device(int d) {
-  FastDiv f{d, 0, 0};
-  if (d > 1) {
-    const int l = 32 - __clz(d - 1);  // ceil(log2 d)
-    const int p = 31 + l;
-    f.m = (uint32_t)(((1ull << p) + (uint64_t)d - 1) / (uint64_t)d);
-    f.s = (uint32_t)(p - 32);
-  }
-  return f;
-}
 
-// 3x3 depthwise, dilation 1, stride SH in both dimensions (1 or 2), as a
-// forward over planes H x W into P x Q.  A CTA stages PP whole planes or a
-// strip of TH output rows of one plane (rows of IW4 floats, a multiple of 4,
-// smem column c holding input column c - pw), then each thread computes
-// items of four adjacent outputs of a row from registers: per filter row it
-// reads the 6 (SH = 1) or 9 (SH = 2) inputs the four windows span with
-// 16-byte shared loads.  FLIP reverses the filter: the stride-1 input
-// gradient is this forward over dY with the flipped filter and padding
-// 2 - pad.
-// Staging of rows [0, ih) of pp planes into [pp][IH][IW4]: smem column c
-// holds input column c - pw of input row h0 + i (zero outside the plane).
-// Wide rows go one warp per row, four rows' loads in flight per warp;
-// narrow rows (small planes) as one flat element loop, so no lane idles.
-__device__ __forceinline__ void dw_stage_rows(float* __restrict__ sm, const float* __restrict__ x, int64_t plane0,
-                                              int64_t pstride, int pp, int ih, int IH, int IW4, int h0, int pw, int H,
-                                              int W, int64_t HW, const FastDiv& fiw4, const FastDiv& fih) {
-  if (IW4 >= 64) {
-    const int rows = pp * ih, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r0 = warp; r0 < rows; r0 += 4 * (kDwThreads / 32)) {
+// 3x3 depthwise, dilation 1, stride SH in both dimensions (1 or 2), pad 0..2.
+// Each thread computes an "item" of four adjacent outputs of one row
+// straight from global memory: per filter row it loads the inputs the four
+// windows span into registers (16-byte loads for the aligned interior when
+// VEC) and does the 36 multiply-adds there.  Neighbouring items read
+// overlapping inputs, which the L1 cache serves, so HBM sees each input about
+// once.  There is no shared-memory staging and no barrier, so every thread's
+// loads are in flight together and the warps of an SM overlap them; the
+// staged version of these kernels (rows to shared memory, barrier, compute)
+// ran at a third of the bandwidth.
+//
+// dw3_row: v[t] = row[c0 + t] for t <= 3*SH + 2 (the span of four windows),
+// zero outside [0, W) or when the row lies outside the plane (rok false).
+// VEC: pad 1, so c0 + 1 is a multiple of 4*SH, and the 4*SH columns from
+// there lie inside the row (W a multiple of 4*SH, rows 16-byte aligned).
+template <int SH, bool VEC>
+__device__ __forceinline__ void dw3_row(const float* __restrict__ row, bool rok, int c0, int W,
+                                        float (&v)[4 * SH + 2]) {
+  if (VEC) {
+    if (rok) {
+      v[0] = c0 >= 0 ? __ldg(row + c0) : 0.f;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int rr = r0 + u * (kDwThreads / 32);
-        if (rr >= rows) break;
-        const int pl = rr / ih, i = rr - pl * ih, h = h0 + i;
-        const float* xr = x + (plane0 + pl) * pstride + (int64_t)h * W;
-        float* dst = sm + (pl * IH + i) * IW4;
-        const bool hok = (unsigned)h < (unsigned)H;
-        for (int c = lane; c < IW4; c += 32) {
-          const int ww = c - pw;
-          dst[c] = hok && (unsigned)ww < (unsigned)W ? __ldg(xr + ww) : 0.f;
-        }
+      for (int k = 0; k < SH; ++k) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(row + c0 + 1 + 4 * k));
+        v[1 + 4 * k] = t.x;
+        v[2 + 4 * k] = t.y;
+        v[3 + 4 * k] = t.z;
+        v[4 + 4 * k] = t.w;
       }
-    }
-  } else {
-    const int total = pp * ih * IW4;
-#pragma unroll 4
-    for (int e = threadIdx.x; e < total; e += kDwThreads) {
-      const int rr = fdiv(e, fiw4), c = e - rr * IW4;
-      const int pl = fdiv(rr, fih), i = rr - pl * ih, h = h0 + i, ww = c - pw;
-      sm[(pl * IH + i) * IW4 + c] = (unsigned)h < (unsigned)H && (unsigned)ww < (unsigned)W
-                                        ? __ldg(x + (plane0 + pl) * pstride + (int64_t)h * W + ww)
-                                        : 0.f;
-    }
-  }
-  (void)HW;
-}
-
-template <int SH, bool FLIP>
-__global__ void __launch_bounds__(kDwThreads) dw3_fwd4_kernel(DwGeom g, int IW4, FastDiv fnq, FastDiv fth,
-                                                              FastDiv fiw4, FastDiv fih,
-                                                              const float* __restrict__ x,
-                                                              const float* __restrict__ w,
-                                                              const float* __restrict__ bias, float* __restrict__ y) {
-  extern __shared__ __align__(16) float sm[];
-  const int tiles = g.tiles_h;
-  const int64_t grp = blockIdx.x / tiles;
-  const int p0 = (int)(blockIdx.x - grp * tiles) * g.TH;
-  const int64_t plane0 = grp * g.PP;
-  const int pp = (int)min((int64_t)g.PP, (int64_t)g.N * g.C - plane0);
-  const int win = g.IH * IW4;
-  float* wsm = sm + g.PP * win;  // filters [PP][9]
-  const int h0 = p0 * SH - g.ph;
-  const int64_t HW = (int64_t)g.H * g.W, PQ = (int64_t)g.P * g.Q;
-  // stage the rows this CTA's outputs read (a short last strip reads fewer)
-  const int th0 = min(g.TH, g.P - p0), ih = (th0 - 1) * SH + 3;
-  dw_stage_rows(sm, x, plane0, HW, pp, pp > 1 ? g.IH : ih, g.IH, IW4, h0, g.pw, g.H, g.W, HW, fiw4,
-                pp > 1 ? fih : fast_div_device(ih));
-  for (int e = threadIdx.x; e < pp * 9; e += kDwThreads) {
-    const int pl = e / 9, t = e - pl * 9;
-    wsm[e] = __ldg(w + (int64_t)((plane0 + pl) % g.C) * 9 + (FLIP ? 8 - t : t));
-  }
-  __syncthreads();
-  const int th = min(g.TH, g.P - p0), nq = fnq.d;
-  const int items = pp * th * nq;
-  const bool vec_out = (g.Q & 3) == 0;
-  for (int e = threadIdx.x; e < items; e += kDwThreads) {
-    const int rowall = fdiv(e, fnq), jq = e - rowall * nq;
-    const int pl = pp > 1 ? fdiv(rowall, fth) : 0, i = rowall - pl * th;
-    const float* wk = wsm + pl * 9;
-    const float b0 = bias ? __ldg(bias + (plane0 + pl) % g.C) : 0.f;
-    float acc[4] = {b0, b0, b0, b0};
-    const float* src = sm + pl * win + (i * SH) * IW4 + jq * 4 * SH;
-#pragma unroll
-    for (int a = 0; a < 3; ++a) {
-      const float* r = src + a * IW4;
-      float v[4 * SH + 2];
-      const float4 v0 = *reinterpret_cast<const float4*>(r);
-      v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
-      if (SH == 1) {
-        const float2 v1 = *reinterpret_cast<const float2*>(r + 4);
-        v[4] = v1.x; v[5] = v1.y;
-      } else {
-        const float4 v1 = *reinterpret_cast<const float4*>(r + 4);
-        v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
-        v[8] = r[8];
-      }
-      const float w0 = wk[a * 3], w1 = wk[a * 3 + 1], w2 = wk[a * 3 + 2];
-#pragma unroll
-      for (int o = 0; o < 4; ++o) {
-        acc[o] = fmaf(v[o * SH], w0, acc[o]);
-        acc[o] = fmaf(v[o * SH + 1], w1, acc[o]);
-        acc[o] = fmaf(v[o * SH + 2], w2, acc[o]);
-      }
-    }
-    const int q0 = jq * 4;
-    float* yr = y + (plane0 + pl) * PQ + (int64_t)(p0 + i) * g.Q + q0;
-    if (vec_out) {
-      *reinterpret_cast<float4*>(yr) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      // stride 1 reads one column past the four (stride 2 needs none)
+      v[4 * SH + 1] = SH == 1 && c0 + 5 < W ? __ldg(row + c0 + 5) : 0.f;
     } else {
 #pragma unroll
-      for (int o = 0; o < 4; ++o)
-        if (q0 + o < g.Q) yr[o] = acc[o];
+      for (int t = 0; t < 4 * SH + 2; ++t) v[t] = 0.f;
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < 4 * SH + 2; ++t) {
+      const int c = c0 + t;
+      v[t] = rok && t <= 3 * SH + 2 && (unsigned)c < (unsigned)W ? __ldg(row + c) : 0.f;
     }
   }
 }
 
-// 3x3 weight gradient (dilation 1, stride SH): CTA (channel, image chunk)
-// stages, per step, pp images' x rows ([pp][IH][IW4], as the forward) and
-// dY rows ([pp][TH][Q4], zero past Q), then each thread takes items of four
-// adjacent outputs and adds dY * x for the 9 taps into registers; the CTA's
-// sums go to part[c][chunk][9] by a fixed-order block reduction.
-template <int SH>
-__global__ void __launch_bounds__(kDwThreads) dw3_wgrad4_kernel(DwGeom g, int IW4, FastDiv fnq, FastDiv fth,
-                                                                FastDiv fiw4, FastDiv fih, FastDiv fq4,
-                                                                const float* __restrict__ x,
-                                                                const float* __restrict__ dy, int per_chunk,
-                                                                float* __restrict__ part) {
-  extern __shared__ __align__(16) float sm[];
+// Forward over planes [planes][H][W] into [planes][P][Q]; items in
+// (plane, p, jq) order, jq fastest, so a warp's loads and stores run along
+// rows.  FLIP reverses the filter: the stride-1 input gradient is this
+// forward over dY with the flipped filter and padding 2 - pad.
+template <int SH, bool FLIP, bool VEC>
+__global__ void __launch_bounds__(kDwThreads) dw3_fwd_kernel(int items, int H, int W, int P, int Q, int ph, int pw,
+                                                             FastDiv fpq, FastDiv fnq, FastDiv fc,
+                                                             const float* __restrict__ x,
+                                                             const float* __restrict__ w,
+                                                             const float* __restrict__ bias, float* __restrict__ y) {
+  const int e = blockIdx.x * kDwThreads + threadIdx.x;
+  if (e >= items) return;
+  const int plane = fdiv(e, fpq), rem = e - plane * fpq.d;
+  const int p = fdiv(rem, fnq), jq = rem - p * fnq.d;
+  const int c = plane - fdiv(plane, fc) * fc.d;
+  float wk[9];
+#pragma unroll
+  for (int t = 0; t < 9; ++t) wk[t] = __ldg(w + c * 9 + (FLIP ? 8 - t : t));
+  const float b0 = bias ? __ldg(bias + c) : 0.f;
+  float acc[4] = {b0, b0, b0, b0};
+  const float* xp = x + (int64_t)plane * H * W;
+  const int h0 = p * SH - ph, c0 = jq * 4 * SH - pw;
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    const int h = h0 + a;
+    const bool rok = (unsigned)h < (unsigned)H;
+    float v[4 * SH + 2];
+    dw3_row<SH, VEC>(xp + (int64_t)(rok ? h : 0) * W, rok, c0, W, v);
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+      acc[o] = fmaf(v[o * SH], wk[a * 3], acc[o]);
+      acc[o] = fmaf(v[o * SH + 1], wk[a * 3 + 1], acc[o]);
+      acc[o] = fmaf(v[o * SH + 2], wk[a * 3 + 2], acc[o]);
+    }
+  }
+  const int q0 = jq * 4;
+  float* yr = y + (int64_t)plane * P * Q + (int64_t)p * Q + q0;
+  if (VEC) {
+    *reinterpret_cast<float4*>(yr) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  } else {
+#pragma unroll
+    for (int o = 0; o < 4; ++o)
+      if (q0 + o < Q) yr[o] = acc[o];
+  }
+}
+
+// Stride-2 input gradient, pad 1, by sub-pixel phases: with
+// y[p][q] = sum_ab x[2p-1+a][2q-1+b] w[a][b], the even rows of dX take filter
+// row 1 of dY row i, the odd rows filter row 2 of dY row i and filter row 0
+// of dY row i + 1 (columns alike).  An item is dX rows 2i, 2i+1 by columns
+// 8j .. 8j+7, made from dY rows i, i+1, columns 4j .. 4j+4 (zero past the
+// plane).  VEC: H = 2P, W = 2Q, Q a multiple of 4 (every store in range,
+// 16-byte aligned).
+template <bool VEC>
+__global__ void __launch_bounds__(kDwThreads) dw3_s2_dgrad_kernel(int items, int H, int W, int P, int Q, FastDiv fij,
+                                                                  FastDiv fnj, FastDiv fc,
+                                                                  const float* __restrict__ dy,
+                                                                  const float* __restrict__ w,
+                                                                  float* __restrict__ dx) {
+  const int e = blockIdx.x * kDwThreads + threadIdx.x;
+  if (e >= items) return;
+  const int plane = fdiv(e, fij), rem = e - plane * fij.d;
+  const int i = fdiv(rem, fnj), j = rem - i * fnj.d;
+  const int c = plane - fdiv(plane, fc) * fc.d;
+  float wk[9];
+#pragma unroll
+  for (int t = 0; t < 9; ++t) wk[t] = __ldg(w + c * 9 + t);
+  const float* gp = dy + (int64_t)plane * P * Q;
+  const int q0 = 4 * j;
+  float d[2][5];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int pr = i + r;
+    const bool rok = pr < P;
+    const float* row = gp + (int64_t)(rok ? pr : 0) * Q;
+    if (VEC) {
+      if (rok) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(row + q0));
+        d[r][0] = t.x;
+        d[r][1] = t.y;
+        d[r][2] = t.z;
+        d[r][3] = t.w;
+        d[r][4] = q0 + 4 < Q ? __ldg(row + q0 + 4) : 0.f;
+      } else {
+#pragma unroll
+        for (int u = 0; u < 5; ++u) d[r][u] = 0.f;
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < 5; ++u) d[r][u] = rok && q0 + u < Q ? __ldg(row + q0 + u) : 0.f;
+    }
+  }
+  float ev[8], od[8];  // dX rows 2i and 2i + 1
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    ev[2 * u] = d[0][u] * wk[4];
+    ev[2 * u + 1] = fmaf(d[0][u + 1], wk[3], d[0][u] * wk[5]);
+    od[2 * u] = fmaf(d[1][u], wk[1], d[0][u] * wk[7]);
+    od[2 * u + 1] = fmaf(d[1][u + 1], wk[0], fmaf(d[1][u], wk[2], fmaf(d[0][u + 1], wk[6], d[0][u] * wk[8])));
+  }
+  const int h = 2 * i, w0 = 8 * j;
+  float* xr = dx + (int64_t)plane * H * W + (int64_t)h * W + w0;
+  if (VEC) {
+    *reinterpret_cast<float4*>(xr) = make_float4(ev[0], ev[1], ev[2], ev[3]);
+    *reinterpret_cast<float4*>(xr + 4) = make_float4(ev[4], ev[5], ev[6], ev[7]);
+    *reinterpret_cast<float4*>(xr + W) = make_float4(od[0], od[1], od[2], od[3]);
+    *reinterpret_cast<float4*>(xr + W + 4) = make_float4(od[4], od[5], od[6], od[7]);
+  } else {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (w0 + u < W) {
+        xr[u] = ev[u];
+        if (h + 1 < H) xr[W + u] = od[u];
+      }
+  }
+}
+
+// Weight gradient: CTA (channel c, chunk k) over grid (C, J) sums, for its
+// items (n, p, jq) of channel c, dY[n][c][p][4jq..] * x under each of the 9
+// taps in registers, then reduces them over the block in a fixed order into
+// part[(c * 9 + tap) * J + k]; dw3_wgrad_reduce_kernel sums the J partials.
+template <int SH, bool VEC>
+__global__ void __launch_bounds__(kDwThreads) dw3_wgrad_kernel(int C, int H, int W, int P, int Q, int ph, int pw,
+                                                               int total, int per, FastDiv fpq, FastDiv fnq,
+                                                               const float* __restrict__ x,
+                                                               const float* __restrict__ dy,
+                                                               float* __restrict__ part) {
   __shared__ float red[kDwThreads / 32][9];
   const int c = blockIdx.x, k = blockIdx.y;
-  const int n0 = k * per_chunk, n1 = min(g.N, n0 + per_chunk);
-  const int nq = fnq.d, Q4 = nq * 4;
-  float* dsm = sm + g.PP * g.IH * IW4;
-  const int64_t HW = (int64_t)g.H * g.W, PQ = (int64_t)g.P * g.Q;
-  const int64_t xstride = (int64_t)g.C * HW, ystride = (int64_t)g.C * PQ;
+  const int e0 = k * per, e1 = min(total, e0 + per);
+  const int64_t HW = (int64_t)H * W, PQ = (int64_t)P * Q;
   float acc[9];
 #pragma unroll
   for (int t = 0; t < 9; ++t) acc[t] = 0.f;
-  for (int n = n0; n < n1; n += g.PP) {
-    const int pp = min(g.PP, n1 - n);
-    const float* xb = x + ((int64_t)n * g.C + c) * HW;
-    const float* yb = dy + ((int64_t)n * g.C + c) * PQ;
-    for (int t = 0; t < g.tiles_h; ++t) {
-      const int p0 = t * g.TH, th = min(g.TH, g.P - p0), ih = (th - 1) * SH + 3, h0 = p0 * SH - g.ph;
-      const FastDiv fthr = pp > 1 ? fth : fast_div_device(th);
-      __syncthreads();  // the previous step's rows are no longer read
-      dw_stage_rows(sm, xb, 0, xstride, pp, pp > 1 ? g.IH : ih, g.IH, IW4, h0, g.pw, g.H, g.W, HW, fiw4,
-                    pp > 1 ? fih : fast_div_device(ih));
-      const int dtotal = pp * th * Q4;
-#pragma unroll 4
-      for (int e = threadIdx.x; e < dtotal; e += kDwThreads) {
-        const int rr = fdiv(e, fq4), j = e - rr * Q4, pl = fdiv(rr, fthr), i = rr - pl * th;
-        dsm[(pl * g.TH + i) * Q4 + j] = j < g.Q ? __ldg(yb + pl * ystride + (int64_t)(p0 + i) * g.Q + j) : 0.f;
-      }
-      __syncthreads();
-      const int items = pp * th * nq;
-      for (int e = threadIdx.x; e < items; e += kDwThreads) {
-        const int rowall = fdiv(e, fnq), jq = e - rowall * nq;
-        const int pl = fdiv(rowall, fthr), i = rowall - pl * th;
-        const float4 d = *reinterpret_cast<const float4*>(dsm + (pl * g.TH + i) * Q4 + jq * 4);
-        const float dv[4] = {d.x, d.y, d.z, d.w};
-        const float* src = sm + (pl * g.IH + i * SH) * IW4 + jq * 4 * SH;
+  for (int e = e0 + threadIdx.x; e < e1; e += kDwThreads) {
+    const int n = fdiv(e, fpq), rem = e - n * fpq.d;
+    const int p = fdiv(rem, fnq), jq = rem - p * fnq.d;
+    const int64_t plane = (int64_t)n * C + c;
+    const int q0 = jq * 4;
+    const float* gr = dy + plane * PQ + (int64_t)p * Q + q0;
+    float dv[4];
+    if (VEC) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(gr));
+      dv[0] = t.x;
+      dv[1] = t.y;
+      dv[2] = t.z;
+      dv[3] = t.w;
+    } else {
 #pragma unroll
-        for (int a = 0; a < 3; ++a) {
-          const float* r = src + a * IW4;
-          float v[4 * SH + 2];
-          const float4 v0 = *reinterpret_cast<const float4*>(r);
-          v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
-          if (SH == 1) {
-            const float2 v1 = *reinterpret_cast<const float2*>(r + 4);
-            v[4] = v1.x; v[5] = v1.y;
-          } else {
-            const float4 v1 = *reinterpret_cast<const float4*>(r + 4);
-            v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
-            v[8] = r[8];
-          }
+      for (int o = 0; o < 4; ++o) dv[o] = q0 + o < Q ? __ldg(gr + o) : 0.f;
+    }
+    const float* xp = x + plane * HW;
+    const int h0 = p * SH - ph, c0 = jq * 4 * SH - pw;
 #pragma unroll
-          for (int o = 0; o < 4; ++o)
+    for (int a = 0; a < 3; ++a) {
+      const int h = h0 + a;
+      const bool rok = (unsigned)h < (unsigned)H;
+      float v[4 * SH + 2];
+      dw3_row<SH, VEC>(xp + (int64_t)(rok ? h : 0) * W, rok, c0, W, v);
 #pragma unroll
-            for (int b = 0; b < 3; ++b) acc[a * 3 + b] = fmaf(dv[o], v[o * SH + b], acc[a * 3 + b]);
-        }
-      }
+      for (int o = 0; o < 4; ++o)
+#pragma unroll
+        for (int b = 0; b < 3; ++b) acc[a * 3 + b] = fmaf(dv[o], v[o * SH + b], acc[a * 3 + b]);
     }
   }
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -454,8 +470,22 @@ __global__ void __launch_bounds__(kDwThreads) dw3_wgrad4_kernel(DwGeom g, int IW
   if (threadIdx.x < 9) {
     float v = 0.f;
     for (int i = 0; i < kDwThreads / 32; ++i) v += red[i][threadIdx.x];
-    part[((int64_t)c * gridDim.y + k) * 9 + threadIdx.x] = v;
+    part[((int64_t)c * 9 + threadIdx.x) * gridDim.y + k] = v;
   }
+}
+
+// dw[c * 9 + tap] = the J partials of (c, tap), one warp each: lane l sums
+// partials l, l + 32, ... in order, then a fixed butterfly (the result
+// depends only on the shapes)
+__global__ void dw3_wgrad_reduce_kernel(const float* __restrict__ part, int rows, int J, float* __restrict__ dw) {
+  const int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const float* pr = part + (int64_t)r * J;
+  float v = 0.f;
+  for (int i = lane; i < J; i += 32) v += pr[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) dw[r] = v;
 }
 
 // ---------------------------------------------------------- weight grad
@@ -559,8 +589,65 @@ static bool dw_tiled_ok(const pvb2_conv2d_desc* d, bool dgrad) {
   return groups * g.tiles_h * g.tiles_w < ((int64_t)1 << 31);
 }
 
-// image chunks of the weight gradient: about eight CTAs per SM, each taking
-// a run of images of one channel
+// ---------------------------------------------- 3x3 direct: host side
+// 3x3, dilation 1, equal strides of 1 or 2, pads up to 2 (the stride-1 input
+// gradient runs as a forward with padding 2 - pad)
+static bool dw3_ok(const pvb2_conv2d_desc* d) {
+  return d->R == 3 && d->S == 3 && d->dil_h == 1 && d->dil_w == 1 && d->stride_h == d->stride_w &&
+         (d->stride_h == 1 || d->stride_h == 2) && d->pad_h >= 0 && d->pad_h <= 2 && d->pad_w >= 0 &&
+         d->pad_w <= 2;
+}
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+// the 16-byte paths of dw3_row and the four-output stores: pad 1, rows and
+// planes 16-byte aligned, every item's interior inside the row
+static bool dw3_vec(int W, int Q, int st, int pw, const void* a, const void* b) {
+  return pw == 1 && W % 4 == 0 && Q % 4 == 0 && W >= st * Q && aligned16(a) && aligned16(b);
+}
+
+// forward over [planes][H][W] -> [planes][P][Q] with stride st and pads
+// (ph, pw); false when the item count does not fit an int
+template <bool FLIP>
+static bool dw3_launch(int64_t planes, int C, int H, int W, int P, int Q, int st, int ph, int pw, const float* x,
+                       const float* w, const float* b, float* y, cudaStream_t s) {
+  const int nq = (Q + 3) / 4;
+  const int64_t items = planes * P * nq;
+  if (items >= ((int64_t)1 << 31) - kDwThreads) return false;
+  const unsigned blocks = (unsigned)((items + kDwThreads - 1) / kDwThreads);
+  const FastDiv fpq = fast_div(P * nq), fnq = fast_div(nq), fc = fast_div(C);
+  const bool vec = dw3_vec(W, Q, st, pw, x, y);
+#define PVB2_DW3_FWD(SH, V)                                                                                        \
+  dw3_fwd_kernel<SH, FLIP, V><<<blocks, kDwThreads, 0, s>>>((int)items, H, W, P, Q, ph, pw, fpq, fnq, fc, x, w, b, \
+                                                            y)
+  if (st == 1) {
+    if (vec) PVB2_DW3_FWD(1, true);
+    else PVB2_DW3_FWD(1, false);
+  } else {
+    if (vec) PVB2_DW3_FWD(2, true);
+    else PVB2_DW3_FWD(2, false);
+  }
+#undef PVB2_DW3_FWD
+  return true;
+}
+
+// weight-gradient chunks per channel: about eight CTAs per SM in all, each
+// with at least eight items per thread
+static int dw3_wgrad_chunks(const pvb2_conv2d_desc* d, int* per) {
+  const int64_t total = (int64_t)d->N * d->P * ((d->Q + 3) / 4);
+  const int64_t most = std::max<int64_t>(1, total / (8 * kDwThreads));
+  int64_t J = std::min<int64_t>(most, std::max(1, (8 * num_sms() + d->C - 1) / std::max(d->C, 1)));
+  J = std::min<int64_t>(J, 65535);
+  *per = (int)((total + J - 1) / J);
+  return (int)((total + *per - 1) / *per);
+}
+
+static bool dw3_wgrad_ok(const pvb2_conv2d_desc* d) {
+  return dw3_ok(d) && (int64_t)d->N * d->P * ((d->Q + 3) / 4) < ((int64_t)1 << 31) - kDwThreads;
+}
+
+// image chunks of the tiled weight gradient: about eight CTAs per SM, each
+// taking a run of images of one channel
 static int dw_chunks(const pvb2_conv2d_desc* d, int* per_chunk) {
   int chunks = std::max(1, std::min(d->N, (8 * num_sms() + d->C - 1) / std::max(d->C, 1)));
   *per_chunk = (d->N + chunks - 1) / chunks;
@@ -568,70 +655,27 @@ static int dw_chunks(const pvb2_conv2d_desc* d, int* per_chunk) {
   return std::min(chunks, 65535);
 }
 
-// scratch of the tiled weight gradient (0: the tiled path does not apply)
-static bool dw3_ok(const pvb2_conv2d_desc* d);
-
+// scratch of the weight gradient (0: neither the direct nor the tiled path
+// applies)
 size_t dw_wgrad_workspace(const pvb2_conv2d_desc* d) {
+  if (dw3_wgrad_ok(d)) {
+    int per = 0;
+    return (size_t)d->C * 9 * dw3_wgrad_chunks(d, &per) * sizeof(float);
+  }
   const DwGeom g = dw_geom(d, false);
   if (!((d->R == 3 && d->S == 3) || (d->R == 5 && d->S == 5))) return 0;
-  if (!dw3_ok(d) && g.IH * g.IW + g.TH * g.TW > kDwSmemFloats) return 0;
+  if (g.IH * g.IW + g.TH * g.TW > kDwSmemFloats) return 0;
   int per = 0;
   const int chunks = dw_chunks(d, &per);
   return (size_t)d->C * chunks * d->R * d->S * sizeof(float);
 }
 
-// dw3_fwd4_kernel over planes H x W -> P x Q (3x3, dilation 1, stride st in
-// both dimensions): about 1024 four-output items per CTA, whole planes when a
-// plane has at most 512 items, else strips of rows; false when the staged
-// rows do not fit
-static bool dw3_plan(DwGeom& g, int st, int* iw4, FastDiv* fnq, FastDiv* fth) {
-  const int nq = (g.Q + 3) / 4;
-  *iw4 = (4 * nq * st + 3 + 3) / 4 * 4;
-  auto ih = [&](int th) { return (th - 1) * st + 3; };
-  if (g.P * nq <= 512) {
-    g.TH = g.P;
-    g.PP = std::max(1, 1024 / (g.P * nq));
-    while (g.PP > 1 && g.PP * (ih(g.TH) * *iw4 + 9) > kDwSmemFloats) --g.PP;
-  } else {
-    g.PP = 1;
-    g.TH = std::max(1, std::min(g.P, 1024 / nq));
-    while (g.TH > 1 && ih(g.TH) * *iw4 + 9 > kDwSmemFloats) --g.TH;
-  }
-  g.IH = ih(g.TH);
-  g.TW = g.Q;
-  g.tiles_h = (g.P + g.TH - 1) / g.TH;
-  g.tiles_w = 1;
-  *fnq = fast_div(nq);
-  *fth = fast_div(g.TH);
-  return g.PP * (g.IH * *iw4 + 9) <= kDwSmemFloats && (int64_t)g.N * g.C * g.P * g.Q < ((int64_t)1 << 31);
-}
-
-static bool dw3_ok(const pvb2_conv2d_desc* d) {
-  return d->R == 3 && d->S == 3 && d->dil_h == 1 && d->dil_w == 1 && d->stride_h == d->stride_w &&
-         (d->stride_h == 1 || d->stride_h == 2);
-}
-
-template <bool FLIP>
-static bool dw3_launch(DwGeom g, int st, const float* x, const float* w, const float* b, float* y, cudaStream_t s) {
-  int iw4 = 0;
-  FastDiv fnq, fth;
-  if (!dw3_plan(g, st, &iw4, &fnq, &fth)) return false;
-  const int64_t blocks = ((int64_t)g.N * g.C + g.PP - 1) / g.PP * g.tiles_h;
-  if (blocks >= ((int64_t)1 << 31)) return false;
-  const size_t smem = (size_t)g.PP * (g.IH * iw4 + 9) * sizeof(float);
-  const FastDiv fiw4 = fast_div(iw4), fih = fast_div(g.IH);
-  if (st == 1)
-    dw3_fwd4_kernel<1, FLIP><<<(unsigned)blocks, kDwThreads, smem, s>>>(g, iw4, fnq, fth, fiw4, fih, x, w, b, y);
-  else
-    dw3_fwd4_kernel<2, FLIP><<<(unsigned)blocks, kDwThreads, smem, s>>>(g, iw4, fnq, fth, fiw4, fih, x, w, b, y);
-  return true;
-}
-
-// *handled = false: not a shape the tiled kernels take (the caller runs the
-// direct kernels)
+// *handled = false: not a shape the direct or tiled kernels take (the
+// caller runs the generic kernels)
 int dw_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const float* b, float* y, cudaStream_t s,
            bool* handled) {
-  if (dw3_ok(d) && dw3_launch<false>(dw_geom(d, false), d->stride_h, x, w, b, y, s)) {
+  if (dw3_ok(d) && dw3_launch<false>((int64_t)d->N * d->C, d->C, d->H, d->W, d->P, d->Q, d->stride_h, d->pad_h,
+                                     d->pad_w, x, w, b, y, s)) {
     PVB2_LAUNCH_CHECK();
     *handled = true;
     return PVB2_OK;
@@ -655,16 +699,28 @@ int dw_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const floa
 }
 
 int dw_dgrad(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, cudaStream_t s, bool* handled) {
-  if (dw3_ok(d) && d->stride_h == 1) {
-    // stride 1: the forward of dY with the flipped filter and padding 2 - pad
-    DwGeom g = dw_geom(d, false);
-    g.H = d->P;
-    g.W = d->Q;
-    g.P = d->H;
-    g.Q = d->W;
-    g.ph = 2 - d->pad_h;
-    g.pw = 2 - d->pad_w;
-    if (dw3_launch<true>(g, 1, dy, w, nullptr, dx, s)) {
+  // stride 1: the forward of dY with the flipped filter and padding 2 - pad
+  if (dw3_ok(d) && d->stride_h == 1 &&
+      dw3_launch<true>((int64_t)d->N * d->C, d->C, d->P, d->Q, d->H, d->W, 1, 2 - d->pad_h, 2 - d->pad_w, dy, w,
+                       nullptr, dx, s)) {
+    PVB2_LAUNCH_CHECK();
+    *handled = true;
+    return PVB2_OK;
+  }
+  // stride 2, pad 1: sub-pixel phases, an item of 2 x 8 dX outputs a thread
+  if (dw3_ok(d) && d->stride_h == 2 && d->pad_h == 1 && d->pad_w == 1) {
+    const int ir = (d->H + 1) / 2, nj = (d->W + 7) / 8;
+    const int64_t items = (int64_t)d->N * d->C * ir * nj;
+    if (items < ((int64_t)1 << 31) - kDwThreads) {
+      const unsigned blocks = (unsigned)((items + kDwThreads - 1) / kDwThreads);
+      const FastDiv fij = fast_div(ir * nj), fnj = fast_div(nj), fc = fast_div(d->C);
+      const bool vec = d->H == 2 * d->P && d->W == 2 * d->Q && d->Q % 4 == 0 && aligned16(dy) && aligned16(dx);
+      if (vec)
+        dw3_s2_dgrad_kernel<true><<<blocks, kDwThreads, 0, s>>>((int)items, d->H, d->W, d->P, d->Q, fij, fnj, fc,
+                                                                dy, w, dx);
+      else
+        dw3_s2_dgrad_kernel<false><<<blocks, kDwThreads, 0, s>>>((int)items, d->H, d->W, d->P, d->Q, fij, fnj, fc,
+                                                                 dy, w, dx);
       PVB2_LAUNCH_CHECK();
       *handled = true;
       return PVB2_OK;
@@ -688,59 +744,40 @@ int dw_dgrad(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* 
   return PVB2_OK;
 }
 
-// dw3_wgrad4_kernel's steps: about 1024 items per step, whole planes of up to
-// `per` images when a plane has at most 512 items, else strips of rows
-static bool dw3_wgrad_plan(const pvb2_conv2d_desc* d, int per, DwGeom& g, int* iw4) {
-  g = dw_geom(d, false);
-  const int st = d->stride_h, nq = (d->Q + 3) / 4, Q4 = nq * 4;
-  *iw4 = (4 * nq * st + 3 + 3) / 4 * 4;
-  auto ih = [&](int th) { return (th - 1) * st + 3; };
-  auto fl = [&](int pp, int th) { return (int64_t)pp * (ih(th) * *iw4 + th * Q4); };
-  if (d->P * nq <= 512) {
-    g.TH = d->P;
-    g.PP = std::max(1, std::min(per, 1024 / (d->P * nq)));
-    while (g.PP > 1 && fl(g.PP, g.TH) > kDwSmemFloats) --g.PP;
-  } else {
-    g.PP = 1;
-    g.TH = std::max(1, std::min(d->P, 1024 / nq));
-    while (g.TH > 1 && fl(1, g.TH) > kDwSmemFloats) --g.TH;
-  }
-  g.IH = ih(g.TH);
-  g.tiles_h = (d->P + g.TH - 1) / g.TH;
-  return fl(g.PP, g.TH) <= kDwSmemFloats;
-}
-
 int dw_wgrad(const pvb2_conv2d_desc* d, const float* x, const float* dy, float* dw, void* ws, size_t ws_bytes,
              cudaStream_t s, bool* handled) {
   const size_t need = dw_wgrad_workspace(d);
   *handled = need > 0 && ws && ws_bytes >= need;
   if (!*handled) return PVB2_OK;
-  if (dw3_ok(d)) {
-    int per = 0, iw4 = 0;
-    const int chunks = dw_chunks(d, &per);
-    DwGeom g;
-    if (dw3_wgrad_plan(d, per, g, &iw4)) {
-      const int nq = (d->Q + 3) / 4;
-      const size_t smem = (size_t)g.PP * (g.IH * iw4 + g.TH * nq * 4) * sizeof(float);
-      const FastDiv fnq = fast_div(nq), fth = fast_div(g.TH), fiw4 = fast_div(iw4), fih = fast_div(g.IH),
-                    fq4 = fast_div(nq * 4);
-      float* part = (float*)ws;
-      const dim3 grid((unsigned)d->C, (unsigned)chunks);
-      if (d->stride_h == 1)
-        dw3_wgrad4_kernel<1><<<grid, kDwThreads, smem, s>>>(g, iw4, fnq, fth, fiw4, fih, fq4, x, dy, per, part);
-      else
-        dw3_wgrad4_kernel<2><<<grid, kDwThreads, smem, s>>>(g, iw4, fnq, fth, fiw4, fih, fq4, x, dy, per, part);
-      PVB2_LAUNCH_CHECK();
-      dw_wgrad_reduce_kernel<<<grid_for((int64_t)d->C * 9, 256), 256, 0, s>>>(part, d->C, chunks, 9, dw);
-      PVB2_LAUNCH_CHECK();
-      return PVB2_OK;
+  float* part = (float*)ws;
+  if (dw3_wgrad_ok(d)) {
+    int per = 0;
+    const int J = dw3_wgrad_chunks(d, &per);
+    const int nq = (d->Q + 3) / 4, total = d->N * d->P * nq;
+    const FastDiv fpq = fast_div(d->P * nq), fnq = fast_div(nq);
+    const bool vec = dw3_vec(d->W, d->Q, d->stride_h, d->pad_w, x, dy);
+    const dim3 grid((unsigned)d->C, (unsigned)J);
+#define PVB2_DW3_WG(SH, V)                                                                                   \
+  dw3_wgrad_kernel<SH, V><<<grid, kDwThreads, 0, s>>>(d->C, d->H, d->W, d->P, d->Q, d->pad_h, d->pad_w, total, \
+                                                      per, fpq, fnq, x, dy, part)
+    if (d->stride_h == 1) {
+      if (vec) PVB2_DW3_WG(1, true);
+      else PVB2_DW3_WG(1, false);
+    } else {
+      if (vec) PVB2_DW3_WG(2, true);
+      else PVB2_DW3_WG(2, false);
     }
+#undef PVB2_DW3_WG
+    PVB2_LAUNCH_CHECK();
+    const int rows = d->C * 9;
+    dw3_wgrad_reduce_kernel<<<(rows + 7) / 8, 256, 0, s>>>(part, rows, J, dw);
+    PVB2_LAUNCH_CHECK();
+    return PVB2_OK;
   }
   DwGeom g = dw_geom(d, false);
   g.PP = 1;
   int per = 0;
   const int chunks = dw_chunks(d, &per);
-  float* part = (float*)ws;
   const dim3 grid((unsigned)d->C, (unsigned)chunks);
   const size_t smem = (size_t)(g.IH * g.IW + g.TH * g.TW) * sizeof(float);
   const dim3 blk(32, kDwThreads / 32);

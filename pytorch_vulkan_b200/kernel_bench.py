@@ -33,6 +33,8 @@ the bytes each pass moves and its algorithmic bytes per element (8 forward,
 each pass timed as `conv` does, with the number of times the geometry occurs
 in one training step; prints per pass the time, TFLOP/s and algorithmic
 GB/s (input read + output written once), and the step's weighted totals.
+`mbv2`: the same for MobileNet-v2's dense convolutions (stem, 1x1 expansions
+and projections) at batch --n (default 128).
 """
 from __future__ import annotations
 
@@ -165,7 +167,21 @@ R50 = [
 ]
 
 
-def r50(n: int, dev: int = 0) -> None:
+# MobileNet-v2's dense convolutions (the stem and every 1x1 expansion and
+# projection; the depthwise ones are in MBV2_DW), same fields as R50
+MBV2 = [
+    (3, 224, 32, 3, 2, 1, 1, False), (32, 112, 16, 1, 1, 0, 1, True), (16, 112, 96, 1, 1, 0, 1, True),
+    (96, 56, 24, 1, 1, 0, 1, True), (24, 56, 144, 1, 1, 0, 2, True), (144, 56, 24, 1, 1, 0, 1, True),
+    (144, 28, 32, 1, 1, 0, 1, True), (32, 28, 192, 1, 1, 0, 3, True), (192, 28, 32, 1, 1, 0, 2, True),
+    (192, 14, 64, 1, 1, 0, 1, True), (64, 14, 384, 1, 1, 0, 4, True), (384, 14, 64, 1, 1, 0, 3, True),
+    (384, 14, 96, 1, 1, 0, 1, True), (96, 14, 576, 1, 1, 0, 3, True), (576, 14, 96, 1, 1, 0, 2, True),
+    (576, 7, 160, 1, 1, 0, 1, True), (160, 7, 960, 1, 1, 0, 3, True), (960, 7, 160, 1, 1, 0, 2, True),
+    (960, 7, 320, 1, 1, 0, 1, True), (320, 7, 1280, 1, 1, 0, 1, True),
+]
+
+
+def r50(n: int, dev: int = 0, table=None) -> None:
+    table = R50 if table is None else table
     lib = ctypes.CDLL(_LIB)
     lib.pvb2_last_error.restype = ctypes.c_char_p
     lib.pvb2_conv2d_workspace_size.restype = ctypes.c_size_t
@@ -176,7 +192,7 @@ def r50(n: int, dev: int = 0) -> None:
     print(f"{'C':>5} {'HW':>4} {'K':>5} {'R':>2} {'s':>2} {'x':>2} | "
           f"{'fwd us':>8} {'TF/s':>6} {'GB/s':>6} | {'dgrad us':>8} {'TF/s':>6} {'GB/s':>6} | "
           f"{'wgrad us':>8} {'TF/s':>6} {'GB/s':>6}")
-    for (c, hw, k, r, st, pd, cnt, need_dx) in R50:
+    for (c, hw, k, r, st, pd, cnt, need_dx) in table:
         p = (hw + 2 * pd - r) // st + 1
         d = _Conv(n, c, hw, hw, k, r, r, p, p, st, st, pd, pd, 1, 1, 1, 0)
         g = torch.Generator().manual_seed(0)
@@ -347,7 +363,7 @@ def batch_norm(n: int, dev: int = 0) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["dgrad_acc", "conv", "r50", "dw", "bn"])
+    ap.add_argument("kernel", choices=["dgrad_acc", "conv", "r50", "mbv2", "dw", "bn"])
     ap.add_argument("--which", choices=["fwd", "dgrad", "wgrad"], default="fwd")
     ap.add_argument("--n", type=int, default=None, help="batch (default 32; 64 for r50)")
     ap.add_argument("--c", type=int, default=None)
@@ -360,6 +376,9 @@ def main() -> None:
     torch.ocl.set_device(0)
     if a.kernel == "r50":
         r50(64 if a.n is None else a.n)
+        return
+    if a.kernel == "mbv2":
+        r50(128 if a.n is None else a.n, table=MBV2)
         return
     if a.kernel == "dw":
         depthwise(128 if a.n is None else a.n)

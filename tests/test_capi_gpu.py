@@ -104,12 +104,17 @@ CONV_SHAPES = [
     # many tiles per CTA with fewer output channels than the tile: chunks without a store
     (4, 3, 224, 224, 32, 3, 3, 1, 1, 1, 1),
     (16, 64, 56, 56, 32, 1, 1, 1, 0, 1, 1),
-    # depthwise (groups = C = K): MobileNet-v2's 3x3 layers through the staged stencils
-    (2, 32, 112, 112, 32, 3, 3, 1, 1, 1, 32),    # 32 x 64 output tiles
-    (2, 96, 112, 112, 96, 3, 3, 2, 1, 1, 96),    # stride 2
+    # depthwise (groups = C = K): MobileNet-v2's 3x3 layers through the direct kernels
+    (2, 32, 112, 112, 32, 3, 3, 1, 1, 1, 32),    # 16-byte loads and stores
+    (2, 96, 112, 112, 96, 3, 3, 2, 1, 1, 96),    # stride 2: sub-pixel input gradient, 16-byte paths
     (3, 144, 56, 56, 144, 3, 3, 1, 1, 1, 144),
-    (4, 576, 14, 14, 576, 3, 3, 2, 1, 1, 576),   # 7x7 outputs: several whole planes per CTA
+    (2, 192, 28, 28, 192, 3, 3, 2, 1, 1, 192),   # 14-wide outputs: scalar paths
+    (4, 576, 14, 14, 576, 3, 3, 2, 1, 1, 576),
     (4, 960, 7, 7, 960, 3, 3, 1, 1, 1, 960),
+    (2, 24, 15, 13, 24, 3, 3, 2, 1, 1, 24),      # odd planes at stride 2 (last dX row has one phase)
+    (2, 8, 10, 12, 8, 3, 3, 2, 0, 1, 8),         # stride 2 pad 0: tiled input gradient
+    (2, 8, 9, 10, 8, 3, 3, 1, 0, 1, 8),          # stride 1 pad 0 (input gradient with pad 2)
+    (2, 8, 9, 10, 8, 3, 3, 1, 2, 1, 8),          # stride 1 pad 2 (input gradient with pad 0)
     (2, 16, 20, 20, 16, 5, 5, 1, 2, 1, 16),      # 5x5
     (2, 8, 9, 11, 8, 3, 3, 1, 1, 2, 8),          # dilation 2, odd plane
     (3, 8, 13, 13, 8, 7, 7, 1, 3, 1, 8),         # 7x7 filter: direct kernels
