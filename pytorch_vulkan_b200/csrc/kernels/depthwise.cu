@@ -262,27 +262,40 @@ __device__ __forceinline__ int fdiv(int n, const FastDiv& f) {
 //
 // dw3_row: v[t] = row[c0 + t] for t <= 3*SH + 2 (the span of four windows),
 // zero outside [0, W) or when the row lies outside the plane (rok false).
-// VEC: pad 1, so c0 + 1 is a multiple of 4*SH, and the 4*SH columns from
-// there lie inside the row (W a multiple of 4*SH, rows 16-byte aligned).
+// VEC: pad 1, so c0 + 1 = 4*SH*jq, and the 4*SH columns from there lie inside
+// the row (W a multiple of 4*SH, rows 16-byte aligned); they come as 16-byte
+// loads, and the halo columns (c0, and c0 + 5 at stride 1) from the
+// neighbouring lanes, which hold items jq - 1 and jq + 1 of the same row
+// (items run jq fastest); only a lane at the warp's edge loads one itself,
+// and at the row's ends the halo is padding.  Every lane of the warp must
+// call it (it shuffles); a lane past the last item passes rok = false.
 template <int SH, bool VEC>
-__device__ __forceinline__ void dw3_row(const float* __restrict__ row, bool rok, int c0, int W,
+__device__ __forceinline__ void dw3_row(const float* __restrict__ row, bool rok, int c0, int W, int jq, int nq,
                                         float (&v)[4 * SH + 2]) {
   if (VEC) {
-    if (rok) {
-      v[0] = c0 >= 0 ? __ldg(row + c0) : 0.f;
+    const int lane = threadIdx.x & 31;
+    // the lanes that cannot take a halo column from a neighbour load it, in
+    // the same batch as the 16-byte loads (not after the shuffles, which
+    // would add a second memory round trip for the whole warp)
+    const bool own_left = lane == 0 && jq > 0, own_right = SH == 1 && (lane == 31 || jq == nq - 1);
+    const float eL = own_left && rok ? __ldg(row + c0) : 0.f;
+    const float eR = own_right && rok && c0 + 5 < W ? __ldg(row + c0 + 5) : 0.f;
 #pragma unroll
-      for (int k = 0; k < SH; ++k) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(row + c0 + 1 + 4 * k));
-        v[1 + 4 * k] = t.x;
-        v[2 + 4 * k] = t.y;
-        v[3 + 4 * k] = t.z;
-        v[4 + 4 * k] = t.w;
-      }
-      // stride 1 reads one column past the four (stride 2 needs none)
-      v[4 * SH + 1] = SH == 1 && c0 + 5 < W ? __ldg(row + c0 + 5) : 0.f;
+    for (int k = 0; k < SH; ++k) {
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rok) t = __ldg(reinterpret_cast<const float4*>(row + c0 + 1 + 4 * k));
+      v[1 + 4 * k] = t.x;
+      v[2 + 4 * k] = t.y;
+      v[3 + 4 * k] = t.z;
+      v[4 + 4 * k] = t.w;
+    }
+    const float left = __shfl_up_sync(0xffffffffu, v[4 * SH], 1);
+    v[0] = jq == 0 ? 0.f : (lane > 0 ? left : eL);
+    if (SH == 1) {
+      const float right = __shfl_down_sync(0xffffffffu, v[1], 1);
+      v[5] = own_right ? eR : right;
     } else {
-#pragma unroll
-      for (int t = 0; t < 4 * SH + 2; ++t) v[t] = 0.f;
+      v[4 * SH + 1] = 0.f;  // stride 2 spans 4 * SH + 1 columns
     }
   } else {
 #pragma unroll
@@ -303,8 +316,11 @@ __global__ void __launch_bounds__(kDwThreads) dw3_fwd_kernel(int items, int H, i
                                                              const float* __restrict__ x,
                                                              const float* __restrict__ w,
                                                              const float* __restrict__ bias, float* __restrict__ y) {
-  const int e = blockIdx.x * kDwThreads + threadIdx.x;
-  if (e >= items) return;
+  // a lane past the last item computes item items - 1 with zero inputs and
+  // stores nothing: it only takes part in dw3_row's shuffles
+  const int e0 = blockIdx.x * kDwThreads + threadIdx.x;
+  const bool valid = e0 < items;
+  const int e = valid ? e0 : items - 1;
   const int plane = fdiv(e, fpq), rem = e - plane * fpq.d;
   const int p = fdiv(rem, fnq), jq = rem - p * fnq.d;
   const int c = plane - fdiv(plane, fc) * fc.d;
@@ -318,9 +334,9 @@ __global__ void __launch_bounds__(kDwThreads) dw3_fwd_kernel(int items, int H, i
 #pragma unroll
   for (int a = 0; a < 3; ++a) {
     const int h = h0 + a;
-    const bool rok = (unsigned)h < (unsigned)H;
+    const bool rok = valid && (unsigned)h < (unsigned)H;
     float v[4 * SH + 2];
-    dw3_row<SH, VEC>(xp + (int64_t)(rok ? h : 0) * W, rok, c0, W, v);
+    dw3_row<SH, VEC>(xp + (int64_t)((unsigned)h < (unsigned)H ? h : 0) * W, rok, c0, W, jq, fnq.d, v);
 #pragma unroll
     for (int o = 0; o < 4; ++o) {
       acc[o] = fmaf(v[o * SH], wk[a * 3], acc[o]);
@@ -328,6 +344,7 @@ __global__ void __launch_bounds__(kDwThreads) dw3_fwd_kernel(int items, int H, i
       acc[o] = fmaf(v[o * SH + 2], wk[a * 3 + 2], acc[o]);
     }
   }
+  if (!valid) return;
   const int q0 = jq * 4;
   float* yr = y + (int64_t)plane * P * Q + (int64_t)p * Q + q0;
   if (VEC) {
@@ -352,8 +369,10 @@ __global__ void __launch_bounds__(kDwThreads) dw3_s2_dgrad_kernel(int items, int
                                                                   const float* __restrict__ dy,
                                                                   const float* __restrict__ w,
                                                                   float* __restrict__ dx) {
-  const int e = blockIdx.x * kDwThreads + threadIdx.x;
-  if (e >= items) return;
+  // a lane past the last item takes part in the shuffles with zeros
+  const int e0 = blockIdx.x * kDwThreads + threadIdx.x;
+  const bool valid = e0 < items;
+  const int e = valid ? e0 : items - 1;
   const int plane = fdiv(e, fij), rem = e - plane * fij.d;
   const int i = fdiv(rem, fnj), j = rem - i * fnj.d;
   const int c = plane - fdiv(plane, fc) * fc.d;
@@ -366,25 +385,27 @@ __global__ void __launch_bounds__(kDwThreads) dw3_s2_dgrad_kernel(int items, int
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int pr = i + r;
-    const bool rok = pr < P;
-    const float* row = gp + (int64_t)(rok ? pr : 0) * Q;
+    const bool rok = valid && pr < P;
+    const float* row = gp + (int64_t)(pr < P ? pr : 0) * Q;
     if (VEC) {
-      if (rok) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(row + q0));
-        d[r][0] = t.x;
-        d[r][1] = t.y;
-        d[r][2] = t.z;
-        d[r][3] = t.w;
-        d[r][4] = q0 + 4 < Q ? __ldg(row + q0 + 4) : 0.f;
-      } else {
-#pragma unroll
-        for (int u = 0; u < 5; ++u) d[r][u] = 0.f;
-      }
+      // column 4j + 4 is the next lane's first (item j + 1 of the same row),
+      // padding past the row's last item; a lane at the warp's edge loads it
+      const bool edge = (threadIdx.x & 31) == 31 && j < fnj.d - 1;
+      const float eR = edge && rok ? __ldg(row + q0 + 4) : 0.f;
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rok) t = __ldg(reinterpret_cast<const float4*>(row + q0));
+      d[r][0] = t.x;
+      d[r][1] = t.y;
+      d[r][2] = t.z;
+      d[r][3] = t.w;
+      const float right = __shfl_down_sync(0xffffffffu, t.x, 1);
+      d[r][4] = j == fnj.d - 1 ? 0.f : (edge ? eR : right);
     } else {
 #pragma unroll
       for (int u = 0; u < 5; ++u) d[r][u] = rok && q0 + u < Q ? __ldg(row + q0 + u) : 0.f;
     }
   }
+  if (!valid) return;
   float ev[8], od[8];  // dX rows 2i and 2i + 1
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
@@ -427,22 +448,30 @@ __global__ void __launch_bounds__(kDwThreads) dw3_wgrad_kernel(int C, int H, int
   float acc[9];
 #pragma unroll
   for (int t = 0; t < 9; ++t) acc[t] = 0.f;
-  for (int e = e0 + threadIdx.x; e < e1; e += kDwThreads) {
+  // every thread runs the same number of iterations (dw3_row shuffles); a
+  // lane past e1 loads the inputs of its item (the chunk may end inside a
+  // row, and the last item's halo column comes from that lane) but adds
+  // nothing (zero dY); past the last item of all it takes that one
+  for (int base = e0; base < e1; base += kDwThreads) {
+    const bool valid = base + (int)threadIdx.x < e1;
+    const int e = min(base + (int)threadIdx.x, total - 1);
     const int n = fdiv(e, fpq), rem = e - n * fpq.d;
     const int p = fdiv(rem, fnq), jq = rem - p * fnq.d;
     const int64_t plane = (int64_t)n * C + c;
     const int q0 = jq * 4;
     const float* gr = dy + plane * PQ + (int64_t)p * Q + q0;
-    float dv[4];
+    float dv[4] = {0.f, 0.f, 0.f, 0.f};
     if (VEC) {
-      const float4 t = __ldg(reinterpret_cast<const float4*>(gr));
-      dv[0] = t.x;
-      dv[1] = t.y;
-      dv[2] = t.z;
-      dv[3] = t.w;
+      if (valid) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(gr));
+        dv[0] = t.x;
+        dv[1] = t.y;
+        dv[2] = t.z;
+        dv[3] = t.w;
+      }
     } else {
 #pragma unroll
-      for (int o = 0; o < 4; ++o) dv[o] = q0 + o < Q ? __ldg(gr + o) : 0.f;
+      for (int o = 0; o < 4; ++o) dv[o] = valid && q0 + o < Q ? __ldg(gr + o) : 0.f;
     }
     const float* xp = x + plane * HW;
     const int h0 = p * SH - ph, c0 = jq * 4 * SH - pw;
@@ -451,7 +480,7 @@ __global__ void __launch_bounds__(kDwThreads) dw3_wgrad_kernel(int C, int H, int
       const int h = h0 + a;
       const bool rok = (unsigned)h < (unsigned)H;
       float v[4 * SH + 2];
-      dw3_row<SH, VEC>(xp + (int64_t)(rok ? h : 0) * W, rok, c0, W, v);
+      dw3_row<SH, VEC>(xp + (int64_t)(rok ? h : 0) * W, rok, c0, W, jq, fnq.d, v);
 #pragma unroll
       for (int o = 0; o < 4; ++o)
 #pragma unroll
