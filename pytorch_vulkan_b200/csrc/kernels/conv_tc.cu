@@ -73,6 +73,8 @@ enum ConvMode : int {
   kImWgrad = 5,   // weight gradient over im2col columns: A = Xcol[n][pix][j] (MN-major), B = dY NCHW (K-major)
   kWgradT = 6,    // weight gradient, at most 64 input and output channels: A = two taps' channels-last x
                   // boxes (M = tap pair x 64 channels), B = dY (N = output channels); both MN-major
+  kImplicit2 = 7, // kImplicit with two 32-channel blocks per ring stage (eight MMAs per mbarrier wait), for
+                  // BN <= 128, where four MMAs take less time than the wait itself
 };
 
 // how a forward-shaped launch writes its output
@@ -99,6 +101,7 @@ struct ConvTcArgs {
   int splits, kb_per_split, total_kb; // wgrad split-K over pixel blocks
   int hwb, slots;                     // pointwise: 32-pixel slots per image, slots in all images
   int win, wq;                        // kImWgrad over filter-row windows (win = 1): output width Q
+  int cpairs;                         // kImplicit2: ceil(cblocks / 2), the channel-block pairs per tap
   int tiles;                          // tiles of this launch
   int epi, ebq, ebp;                  // EpiMode and its box extents
   float* out;
@@ -113,10 +116,14 @@ struct ConvTcArgs {
 // producer waits for the stage's previous use to be consumed (empty barrier)
 // and the MMA consumes the ring in order, so no waiter is ever more than one
 // phase ahead of a barrier.
-template <int BN>
+//
+// KB 32-channel blocks per stage (kImplicit2: 2).  An mbarrier wait costs
+// the MMA-issuing thread about 180 cycles, as much as three 128x64x8 TF32
+// MMAs; a stage of two channel blocks (eight MMAs) hides it at BN = 128.
+template <int BN, int KB = 1>
 struct ConvSmem {
-  static constexpr int A_BYTES = cBM * cBK * 4;
-  static constexpr int B_BYTES = BN * cBK * 4;
+  static constexpr int A_BYTES = KB * cBM * cBK * 4;
+  static constexpr int B_BYTES = KB * BN * cBK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;  // one box of 32 x 32 fp32 per epilogue warp
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(cThreads, 1)
   constexpr bool PW = MODE == kPwFwd || MODE == kPwDgrad;
   constexpr bool A_MN = MODE == kPwFwd || MODE == kPwDgrad || MODE == kWgrad || MODE == kImWgrad || MODE == kWgradT;
   constexpr bool B_MN = MODE == kPwDgrad || MODE == kWgrad || MODE == kWgradT;
-  using L = ConvSmem<BN>;
+  using L = ConvSmem<BN, MODE == kImplicit2 ? 2 : 1>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + L::BAR_OFF);
@@ -222,12 +229,40 @@ __global__ void __launch_bounds__(cThreads, 1)
 
   if (warp < cProducers) {
     // ------------------------------------------------------------ producers
-    if (lane == 0) {
+    // issuing warps: at most one per ring stage, so that each warp's
+    // previous stage had its use STAGES back consumed and no parity wait on
+    // an empty barrier is ever two phases ahead of it
+    constexpr int nissue = cStages < cProducers ? cStages : cProducers;
+    if (lane == 0 && warp < nissue) {
       tma_prefetch(&tmA);
       tma_prefetch(&tmB);
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x) {
-        if (MODE == kImplicit) {
+        if (MODE == kImplicit2) {
+          int kt, q0, p0, n0;
+          fwd_tile(tile / a.splits, kt, q0, p0, n0);
+          int kb0, kb1;
+          wg_range(tile % a.splits, kb0, kb1);
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int s_ = it % cStages;
+            const uint32_t ph = (it / cStages) & 1;
+            if ((int)(it % nissue) != warp) continue;
+            if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
+            // stage = tap rs, channel blocks 2 cp and 2 cp + 1 (past the
+            // channels A reads zeros, so an odd last block adds nothing)
+            const int rs = kb / a.cpairs, cp = kb - rs * a.cpairs;
+            const int r = rs / a.S, s = rs % a.S;
+            uint8_t* sa = smem + s_ * L::STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int cb = 2 * cp + h;
+              tma_load_4d(sa + h * cBM * cBK * 4, &tmA, &full[s_], cb * 32, q0 * a.sw + a.tap_w[s],
+                          p0 * a.sh + a.tap_h[r], n0);
+              tma_load_2d(sa + L::A_BYTES + h * BN * cBK * 4, &tmB, &full[s_], rs * a.Cp + cb * 32, kt * BN);
+            }
+          }
+        } else if (MODE == kImplicit) {
           int kt, q0, p0, n0;
           fwd_tile(tile / a.splits, kt, q0, p0, n0);
           int kb0, kb1;
@@ -369,7 +404,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           int sp, km, ctile, rs;
           wg_tile(tile, sp, km, ctile, rs);
           wg_range(sp, kb0, kb1);
-        } else if (MODE == kImplicit) {
+        } else if (MODE == kImplicit || MODE == kImplicit2) {
           wg_range(tile % a.splits, kb0, kb1);
         }
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
@@ -379,11 +414,20 @@ __global__ void __launch_bounds__(cThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s_ * L::STAGE_BYTES);
           const uint32_t sb = sa + L::A_BYTES;
+          if (MODE == kImplicit2) {
 #pragma unroll
-          for (int kk = 0; kk < cBK / 8; ++kk) {
-            const uint64_t ad = A_MN ? desc_mnmajor(sa, kk, 32 * cBK * 4) : desc_kmajor(sa, kk);
-            const uint64_t bd = B_MN ? desc_mnmajor(sb, kk, 32 * cBK * 4) : desc_kmajor(sb, kk);
-            mma_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int kk = 0; kk < cBK / 8; ++kk)
+                mma_tf32(d_tmem, desc_kmajor(sa + h * cBM * cBK * 4, kk), desc_kmajor(sb + h * BN * cBK * 4, kk),
+                         idesc, (kb > kb0 || h > 0 || kk > 0) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < cBK / 8; ++kk) {
+              const uint64_t ad = A_MN ? desc_mnmajor(sa, kk, 32 * cBK * 4) : desc_kmajor(sa, kk);
+              const uint64_t bd = B_MN ? desc_mnmajor(sb, kk, 32 * cBK * 4) : desc_kmajor(sb, kk);
+              mma_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
           }
           mma_commit(&empty[s_]);
         }
@@ -927,7 +971,7 @@ struct Taps {
 template <int BN, int MODE>
 static int launch_conv(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const ConvTcArgs& a,
                        cudaStream_t s) {
-  constexpr int smem = ConvSmem<BN>::TOTAL + 1024;
+  constexpr int smem = ConvSmem<BN, MODE == kImplicit2 ? 2 : 1>::TOTAL + 1024;
   static std::atomic<uint64_t> attr_done{0};
   if (first_on_device(attr_done))
     PVB2_CUDA_TRY(cudaFuncSetAttribute(conv_tf32_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -1023,17 +1067,23 @@ struct FwdSplit {
   size_t bytes = 0;
 };
 
+// the ring stage of a forward-shaped implicit launch: two channel blocks
+// (kImplicit2) when BN <= 128 and there are at least two
+static bool implicit_pairs(int K, int Cp) { return bn_for(K) <= 128 && (Cp + 31) / 32 >= 2; }
+
 static FwdSplit plan_fwd_split(int N, int P, int Q, int K, int taps, int Cp) {
   FwdSplit f;
   int bw, bh, bni;
   pixel_block(P, Q, cBM, bw, bh, bni);
   const int BN = bn_for(K);
   const int64_t tiles = (int64_t)((Q + bw - 1) / bw) * ((P + bh - 1) / bh) * ((N + bni - 1) / bni) * ((K + BN - 1) / BN);
-  const int kblocks = taps * ((Cp + 31) / 32);
+  // K blocks here are ring stages (channel-block pairs for kImplicit2)
+  const int per_stage = implicit_pairs(K, Cp) ? 2 : 1;
+  const int kblocks = taps * (((Cp + 31) / 32 + per_stage - 1) / per_stage);
   f.kb_per = kblocks;
   const int sms = num_sms();
-  if (tiles >= sms || kblocks < 8) return f;
-  const double t_kb = 2.0 * cBM * BN * cBK / (0.6 * 816e12 / sms);
+  if (tiles >= sms || kblocks * per_stage < 8) return f;
+  const double t_kb = per_stage * 2.0 * cBM * BN * cBK / (0.6 * 816e12 / sms);
   const double out_bytes = 4.0 * N * K * P * Q;
   double best = 1e30;
   for (int S = 1; S <= 8; ++S) {
@@ -1133,6 +1183,7 @@ static int run_fwd_like(const float* act, const float* wpacked, const float* bia
   }
   a.obase = obase; a.on = on; a.ok = ok; a.op = op; a.oq = oq;
   a.cblocks = (Cp + 31) / 32;
+  a.cpairs = (a.cblocks + 1) / 2;
   a.bw = bw; a.bh = bh; a.bni = bni;
   a.tq = (Q + bw - 1) / bw;
   a.tp = (P + bh - 1) / bh;
@@ -1140,15 +1191,19 @@ static int run_fwd_like(const float* act, const float* wpacked, const float* bia
   a.kt = (K + BN - 1) / BN;
   a.out = out;
   a.bias = bias;
+  const bool pairs = implicit_pairs(K, Cp);
   const FwdSplit fs = plan_fwd_split(N, P, Q, K, t.nr * t.ns, Cp);
   const bool split = fs.splits > 1 && part && part_bytes >= fs.bytes;
   a.splits = split ? fs.splits : 1;
-  a.total_kb = t.nr * t.ns * a.cblocks;
+  a.total_kb = t.nr * t.ns * (pairs ? a.cpairs : a.cblocks);  // ring stages
   a.kb_per_split = split ? fs.kb_per : a.total_kb;
   a.tiles = a.tq * a.tp * a.tn * a.kt * a.splits;
+  auto launch = [&]() {
+    return pairs ? launch_bn<kImplicit2>(BN, ma, mb, mc, a, s) : launch_bn<kImplicit>(BN, ma, mb, mc, a, s);
+  };
   if (!split) {
     PVB2_TRY(plan_epilogue(a, &mc, out, N, K, P, Q));
-    return launch_bn<kImplicit>(BN, ma, mb, mc, a, s);
+    return launch();
   }
   // partial slabs: dense NCHW images s * N + n, no bias
   a.out = part;
@@ -1159,7 +1214,7 @@ static int run_fwd_like(const float* act, const float* wpacked, const float* bia
   a.op = Q;
   a.oq = 1;
   PVB2_TRY(plan_epilogue(a, &mc, part, N * a.splits, K, P, Q));
-  PVB2_TRY(launch_bn<kImplicit>(BN, ma, mb, mc, a, s));
+  PVB2_TRY(launch());
   const int64_t slab = (int64_t)N * K * P * Q;
   const bool dense = obase == 0 && oq == 1 && op == Q && ok == (int64_t)P * Q && on == (int64_t)K * P * Q;
   if (dense && slab % 4 == 0 && aligned16(out) && slab < ((int64_t)1 << 31)) {
