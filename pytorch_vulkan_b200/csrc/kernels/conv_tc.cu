@@ -73,9 +73,12 @@ enum ConvMode : int {
   kImWgrad = 5,   // weight gradient over im2col columns: A = Xcol[n][pix][j] (MN-major), B = dY NCHW (K-major)
   kWgradT = 6,    // weight gradient, at most 64 input and output channels: A = two taps' channels-last x
                   // boxes (M = tap pair x 64 channels), B = dY (N = output channels); both MN-major
-  kImplicit2 = 7, // kImplicit with two 32-channel blocks per ring stage (eight MMAs per mbarrier wait), for
-                  // BN <= 128, where four MMAs take less time than the wait itself
 };
+// A launch stages KB K blocks per ring stage (the kernel's third template
+// parameter): 2 for BN <= 128 in the implicit forward / dgrad (two 32-channel
+// blocks of one tap) and the pointwise, implicit and two-tap weight
+// gradients (two 32-pixel blocks), so that one mbarrier wait of the MMA
+// thread covers eight MMAs instead of four.
 
 // how a forward-shaped launch writes its output
 enum EpiMode : int {
@@ -101,7 +104,7 @@ struct ConvTcArgs {
   int splits, kb_per_split, total_kb; // wgrad split-K over pixel blocks
   int hwb, slots;                     // pointwise: 32-pixel slots per image, slots in all images
   int win, wq;                        // kImWgrad over filter-row windows (win = 1): output width Q
-  int cpairs;                         // kImplicit2: ceil(cblocks / 2), the channel-block pairs per tap
+  int cpairs;                         // kImplicit with KB = 2: ceil(cblocks / 2), the channel-block pairs per tap
   int tiles;                          // tiles of this launch
   int epi, ebq, ebp;                  // EpiMode and its box extents
   float* out;
@@ -117,7 +120,7 @@ struct ConvTcArgs {
 // and the MMA consumes the ring in order, so no waiter is ever more than one
 // phase ahead of a barrier.
 //
-// KB 32-channel blocks per stage (kImplicit2: 2).  An mbarrier wait costs
+// KB K blocks of 32 per stage.  An mbarrier wait costs
 // the MMA-issuing thread about 180 cycles, as much as three 128x64x8 TF32
 // MMAs; a stage of two channel blocks (eight MMAs) hides it at BN = 128.
 template <int BN, int KB = 1>
@@ -165,7 +168,7 @@ __device__ __forceinline__ void prefetch_addend_l2(const ConvTcArgs& a, int n, i
   }
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, int KB>
 __global__ void __launch_bounds__(cThreads, 1)
     conv_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, ConvTcArgs a) {
@@ -173,7 +176,8 @@ __global__ void __launch_bounds__(cThreads, 1)
   constexpr bool PW = MODE == kPwFwd || MODE == kPwDgrad;
   constexpr bool A_MN = MODE == kPwFwd || MODE == kPwDgrad || MODE == kWgrad || MODE == kImWgrad || MODE == kWgradT;
   constexpr bool B_MN = MODE == kPwDgrad || MODE == kWgrad || MODE == kWgradT;
-  using L = ConvSmem<BN, MODE == kImplicit2 ? 2 : 1>;
+  using L = ConvSmem<BN, KB>;
+  constexpr int A_BLK = L::A_BYTES / KB, B_BLK = L::B_BYTES / KB;  // one K block's A / B bytes
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = (uint64_t*)(smem + L::BAR_OFF);
@@ -238,7 +242,7 @@ __global__ void __launch_bounds__(cThreads, 1)
       tma_prefetch(&tmB);
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < total_tiles && !*abort; tile += gridDim.x) {
-        if (MODE == kImplicit2) {
+        if (MODE == kImplicit && KB == 2) {
           int kt, q0, p0, n0;
           fwd_tile(tile / a.splits, kt, q0, p0, n0);
           int kb0, kb1;
@@ -270,7 +274,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
-            if ((int)(it % cProducers) != warp) continue;
+            if ((int)(it % nissue) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
             const int rs = kb / a.cblocks, cb = kb % a.cblocks;
             const int r = rs / a.S, s = rs % a.S;
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = 0; kb < a.cblocks; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
-            if ((int)(it % cProducers) != warp) continue;
+            if ((int)(it % nissue) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
             uint8_t* sa = smem + s_ * L::STAGE_BYTES;
             uint8_t* sb = sa + L::A_BYTES;
@@ -314,21 +318,27 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
-            if ((int)(it % cProducers) != warp) continue;
+            if ((int)(it % nissue) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
-            const int q0 = (kb % a.tq) * a.bw, p0 = ((kb / a.tq) % a.tp) * a.bh, n0 = (kb / (a.tq * a.tp)) * a.bni;
-            uint8_t* sa = smem + s_ * L::STAGE_BYTES;
-            uint8_t* sb = sa + L::A_BYTES;
             mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
+            // pixel blocks KB kb .. KB kb + KB - 1 (a block past the last
+            // image lies outside the maps and loads zeros)
 #pragma unroll
-            for (int j = 0; j < cBM / 32; ++j) {
-              const int tap = min(2 * pr + (j >> 1), RS - 1), r = tap / a.S, s = tap - r * a.S;
-              tma_load_4d(sa + j * 32 * cBK * 4, &tmA, &full[s_], 32 * (j & 1), q0 * a.sw + a.tap_w[s],
-                          p0 * a.sh + a.tap_h[r], n0);
+            for (int h = 0; h < KB; ++h) {
+              const int pb = kb * KB + h;
+              const int q0 = (pb % a.tq) * a.bw, p0 = ((pb / a.tq) % a.tp) * a.bh, n0 = (pb / (a.tq * a.tp)) * a.bni;
+              uint8_t* sa = smem + s_ * L::STAGE_BYTES + h * A_BLK;
+              uint8_t* sb = smem + s_ * L::STAGE_BYTES + L::A_BYTES + h * B_BLK;
+#pragma unroll
+              for (int j = 0; j < cBM / 32; ++j) {
+                const int tap = min(2 * pr + (j >> 1), RS - 1), r = tap / a.S, s = tap - r * a.S;
+                tma_load_4d(sa + j * 32 * cBK * 4, &tmA, &full[s_], 32 * (j & 1), q0 * a.sw + a.tap_w[s],
+                            p0 * a.sh + a.tap_h[r], n0);
+              }
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j)
+                tma_load_4d(sb + j * 32 * cBK * 4, &tmB, &full[s_], ctile * BN + 32 * j, q0, p0, n0);
             }
-#pragma unroll
-            for (int j = 0; j < BN / 32; ++j)
-              tma_load_4d(sb + j * 32 * cBK * 4, &tmB, &full[s_], ctile * BN + 32 * j, q0, p0, n0);
           }
         } else if (MODE == kWgrad) {
           int sp, km, ctile, rs;
@@ -339,18 +349,23 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
-            if ((int)(it % cProducers) != warp) continue;
+            if ((int)(it % nissue) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
-            const int q0 = (kb % a.tq) * a.bw, p0 = ((kb / a.tq) % a.tp) * a.bh, n0 = (kb / (a.tq * a.tp)) * a.bni;
-            uint8_t* sa = smem + s_ * L::STAGE_BYTES;
-            uint8_t* sb = sa + L::A_BYTES;
             mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
 #pragma unroll
-            for (int j = 0; j < cBM / 32; ++j) tma_load_4d(sa + j * 32 * cBK * 4, &tmA, &full[s_], km * cBM + 32 * j, q0, p0, n0);
+            for (int h = 0; h < KB; ++h) {
+              const int pb = kb * KB + h;
+              const int q0 = (pb % a.tq) * a.bw, p0 = ((pb / a.tq) % a.tp) * a.bh, n0 = (pb / (a.tq * a.tp)) * a.bni;
+              uint8_t* sa = smem + s_ * L::STAGE_BYTES + h * A_BLK;
+              uint8_t* sb = smem + s_ * L::STAGE_BYTES + L::A_BYTES + h * B_BLK;
 #pragma unroll
-            for (int j = 0; j < BN / 32; ++j)
-              tma_load_4d(sb + j * 32 * cBK * 4, &tmB, &full[s_], ctile * BN + 32 * j, q0 * a.sw + a.tap_w[s],
-                          p0 * a.sh + a.tap_h[r], n0);
+              for (int j = 0; j < cBM / 32; ++j)
+                tma_load_4d(sa + j * 32 * cBK * 4, &tmA, &full[s_], km * cBM + 32 * j, q0, p0, n0);
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j)
+                tma_load_4d(sb + j * 32 * cBK * 4, &tmB, &full[s_], ctile * BN + 32 * j, q0 * a.sw + a.tap_w[s],
+                            p0 * a.sh + a.tap_h[r], n0);
+            }
           }
         } else {  // kPwWgrad / kImWgrad: K blocks are (image, 32-pixel slot) pairs
           int sp, km, ctile, rs;
@@ -360,14 +375,22 @@ __global__ void __launch_bounds__(cThreads, 1)
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int s_ = it % cStages;
             const uint32_t ph = (it / cStages) & 1;
-            if ((int)(it % cProducers) != warp) continue;
+            if ((int)(it % nissue) != warp) continue;
             if (!mbar_wait(&empty[s_], ph ^ 1, abort)) break;
-            const int n = kb / a.hwb, hw0 = (kb - n * a.hwb) * 32;
             uint8_t* sa = smem + s_ * L::STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s_], L::STAGE_BYTES);
             if (MODE == kPwWgrad) {
-              tma_load_3d(sa, &tmA, &full[s_], hw0, km * cBM, n);
-            } else if (a.win) {
+              // slots KB kb ..; one past the last image loads zeros
+#pragma unroll
+              for (int h = 0; h < KB; ++h) {
+                const int sl = kb * KB + h, n = sl / a.hwb, hw0 = (sl - n * a.hwb) * 32;
+                tma_load_3d(sa + h * A_BLK, &tmA, &full[s_], hw0, km * cBM, n);
+                tma_load_3d(sa + L::A_BYTES + h * B_BLK, &tmB, &full[s_], hw0, ctile * BN, n);
+              }
+              continue;
+            }
+            const int n = kb / a.hwb, hw0 = (kb - n * a.hwb) * 32;
+            if (a.win) {
               // rows km * 128 + 32 j .. : filter row 4 km + j, its 32-float
               // window of each pixel; the 32 pixels as two 16-pixel runs,
               // each inside one output row (Q % 16 == 0)
@@ -404,7 +427,7 @@ __global__ void __launch_bounds__(cThreads, 1)
           int sp, km, ctile, rs;
           wg_tile(tile, sp, km, ctile, rs);
           wg_range(sp, kb0, kb1);
-        } else if (MODE == kImplicit || MODE == kImplicit2) {
+        } else if (MODE == kImplicit) {
           wg_range(tile % a.splits, kb0, kb1);
         }
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
@@ -414,21 +437,15 @@ __global__ void __launch_bounds__(cThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s_ * L::STAGE_BYTES);
           const uint32_t sb = sa + L::A_BYTES;
-          if (MODE == kImplicit2) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-              for (int kk = 0; kk < cBK / 8; ++kk)
-                mma_tf32(d_tmem, desc_kmajor(sa + h * cBM * cBK * 4, kk), desc_kmajor(sb + h * BN * cBK * 4, kk),
-                         idesc, (kb > kb0 || h > 0 || kk > 0) ? 1u : 0u);
-          } else {
+          for (int h = 0; h < KB; ++h)
 #pragma unroll
             for (int kk = 0; kk < cBK / 8; ++kk) {
-              const uint64_t ad = A_MN ? desc_mnmajor(sa, kk, 32 * cBK * 4) : desc_kmajor(sa, kk);
-              const uint64_t bd = B_MN ? desc_mnmajor(sb, kk, 32 * cBK * 4) : desc_kmajor(sb, kk);
-              mma_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+              const uint32_t ah = sa + h * A_BLK, bh = sb + h * B_BLK;
+              const uint64_t ad = A_MN ? desc_mnmajor(ah, kk, 32 * cBK * 4) : desc_kmajor(ah, kk);
+              const uint64_t bd = B_MN ? desc_mnmajor(bh, kk, 32 * cBK * 4) : desc_kmajor(bh, kk);
+              mma_tf32(d_tmem, ad, bd, idesc, (kb > kb0 || h > 0 || kk > 0) ? 1u : 0u);
             }
-          }
           mma_commit(&empty[s_]);
         }
         mma_commit(&acc_full[buf]);
@@ -968,16 +985,17 @@ struct Taps {
   int h[kMaxTaps], w[kMaxTaps];
 };
 
-template <int BN, int MODE>
+template <int BN, int MODE, int KB = 1>
 static int launch_conv(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const ConvTcArgs& a,
                        cudaStream_t s) {
-  constexpr int smem = ConvSmem<BN, MODE == kImplicit2 ? 2 : 1>::TOTAL + 1024;
+  constexpr int smem = ConvSmem<BN, KB>::TOTAL + 1024;
   static std::atomic<uint64_t> attr_done{0};
   if (first_on_device(attr_done))
-    PVB2_CUDA_TRY(cudaFuncSetAttribute(conv_tf32_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    PVB2_CUDA_TRY(
+        cudaFuncSetAttribute(conv_tf32_kernel<BN, MODE, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   if (a.tiles <= 0) return PVB2_OK;
   const int grid = std::min(a.tiles, num_sms());
-  conv_tf32_kernel<BN, MODE><<<grid, cThreads, smem, s>>>(ma, mb, mc, a);
+  conv_tf32_kernel<BN, MODE, KB><<<grid, cThreads, smem, s>>>(ma, mb, mc, a);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
@@ -988,6 +1006,15 @@ static int launch_bn(int BN, const CUtensorMap& ma, const CUtensorMap& mb, const
   if (BN == 64) return launch_conv<64, MODE>(ma, mb, mc, a, s);
   if (BN == 128) return launch_conv<128, MODE>(ma, mb, mc, a, s);
   return launch_conv<256, MODE>(ma, mb, mc, a, s);
+}
+
+// the same with two K blocks per stage (BN <= 128 only)
+template <int MODE>
+static int launch_bn2(int BN, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                      const ConvTcArgs& a, cudaStream_t s) {
+  PVB2_CHECK_ARG(BN <= 128, "conv: two K blocks per stage need BN <= 128");
+  if (BN == 64) return launch_conv<64, MODE, 2>(ma, mb, mc, a, s);
+  return launch_conv<128, MODE, 2>(ma, mb, mc, a, s);
 }
 
 // channels-last activations [N, H, W, Cp] as a 4-D map (Cp, W, H, N)
@@ -1068,7 +1095,7 @@ struct FwdSplit {
 };
 
 // the ring stage of a forward-shaped implicit launch: two channel blocks
-// (kImplicit2) when BN <= 128 and there are at least two
+// (KB = 2) when BN <= 128 and there are at least two
 static bool implicit_pairs(int K, int Cp) { return bn_for(K) <= 128 && (Cp + 31) / 32 >= 2; }
 
 static FwdSplit plan_fwd_split(int N, int P, int Q, int K, int taps, int Cp) {
@@ -1077,7 +1104,7 @@ static FwdSplit plan_fwd_split(int N, int P, int Q, int K, int taps, int Cp) {
   pixel_block(P, Q, cBM, bw, bh, bni);
   const int BN = bn_for(K);
   const int64_t tiles = (int64_t)((Q + bw - 1) / bw) * ((P + bh - 1) / bh) * ((N + bni - 1) / bni) * ((K + BN - 1) / BN);
-  // K blocks here are ring stages (channel-block pairs for kImplicit2)
+  // K blocks here are ring stages (channel-block pairs when KB = 2)
   const int per_stage = implicit_pairs(K, Cp) ? 2 : 1;
   const int kblocks = taps * (((Cp + 31) / 32 + per_stage - 1) / per_stage);
   f.kb_per = kblocks;
@@ -1199,7 +1226,7 @@ static int run_fwd_like(const float* act, const float* wpacked, const float* bia
   a.kb_per_split = split ? fs.kb_per : a.total_kb;
   a.tiles = a.tq * a.tp * a.tn * a.kt * a.splits;
   auto launch = [&]() {
-    return pairs ? launch_bn<kImplicit2>(BN, ma, mb, mc, a, s) : launch_bn<kImplicit>(BN, ma, mb, mc, a, s);
+    return pairs ? launch_bn2<kImplicit>(BN, ma, mb, mc, a, s) : launch_bn<kImplicit>(BN, ma, mb, mc, a, s);
   };
   if (!split) {
     PVB2_TRY(plan_epilogue(a, &mc, out, N, K, P, Q));
@@ -1267,9 +1294,16 @@ static int run_pointwise(const float* src, const float* w, const float* bias, fl
 // Weight-gradient split-K plan.  kb_total K blocks (32 pixels each) reduce
 // into K x Cin x taps outputs; enough splits to give every SM two tiles,
 // each split keeping at least 8 K blocks.
+// total_kb, kb_per: ring stages of kbs 32-pixel blocks each (kbs = 2 when
+// BN <= 128: one mbarrier wait per eight MMAs)
 struct WgPlan {
   int bw, bh, bni, BN, splits, kb_per, total_kb, ct, kt;
+  int kbs = 1;
 };
+static void set_stages(WgPlan& w, int blocks) {
+  w.kbs = w.BN <= 128 && blocks >= 2 ? 2 : 1;
+  w.total_kb = (blocks + w.kbs - 1) / w.kbs;
+}
 
 // out_elems: K x Cin x taps weights; in_bytes: the operand bytes the
 // reduction streams.  Splits also cost their partials (written once, read
@@ -1291,7 +1325,7 @@ static WgPlan plan_wg(int N, int K, int Cin, int P, int Q, int taps) {
   w.ct = (Cin + w.BN - 1) / w.BN;
   w.kt = (K + cBM - 1) / cBM;
   const int tq = (Q + w.bw - 1) / w.bw, tp = (P + w.bh - 1) / w.bh, tn = (N + w.bni - 1) / w.bni;
-  w.total_kb = tq * tp * tn;
+  set_stages(w, tq * tp * tn);
   plan_splits(w, taps, (double)K * Cin * taps, 4.0 * N * P * Q * ((double)K + Cin));
   return w;
 }
@@ -1307,7 +1341,7 @@ static WgPlan plan_pw_wg(int N, int K, int C, int64_t hw) {
   w.BN = bn_for(C);
   w.ct = (C + w.BN - 1) / w.BN;
   w.kt = (K + cBM - 1) / cBM;
-  w.total_kb = N * (int)((hw + 31) / 32);
+  set_stages(w, N * (int)((hw + 31) / 32));
   plan_splits(w, 1, (double)K * C, 4.0 * N * hw * ((double)K + C));
   return w;
 }
@@ -1430,7 +1464,7 @@ static int run_wgrad(const float* dyn, int Kp, const float* xn, int Cp, int N, i
   a.out = part;
   a.tiles = a.kt * a.ct * t.nr * t.ns * a.splits;
   PVB2_TRY(wg_partial_map(&mc, part, K, Cin, p.splits * t.nr * t.ns));
-  return launch_bn<kWgrad>(p.BN, ma, mb, mc, a, s);
+  return p.kbs == 2 ? launch_bn2<kWgrad>(p.BN, ma, mb, mc, a, s) : launch_bn<kWgrad>(p.BN, ma, mb, mc, a, s);
 }
 
 // Weight gradients with at most 64 input and output channels (ResNet's
@@ -1445,7 +1479,7 @@ static WgPlan plan_wg_t(int N, int K, int Cin, int P, int Q, int taps) {
   w.kt = 1;
   w.ct = (K + 63) / 64;
   const int tq = (Q + w.bw - 1) / w.bw, tp = (P + w.bh - 1) / w.bh, tn = (N + w.bni - 1) / w.bni;
-  w.total_kb = tq * tp * tn;
+  set_stages(w, tq * tp * tn);
   plan_splits(w, (taps + 1) / 2, (double)K * Cin * taps, 4.0 * N * P * Q * ((double)K + Cin));
   return w;
 }
@@ -1483,7 +1517,7 @@ static int run_wgrad_t(const float* dyn, int Kp, const float* xn, int Cp, int N,
   a.total_kb = p.total_kb;
   a.out = part;
   a.tiles = a.ct * ((taps + 1) / 2) * a.splits;
-  return launch_conv<64, kWgradT>(ma, mb, mc, a, s);
+  return p.kbs == 2 ? launch_conv<64, kWgradT, 2>(ma, mb, mc, a, s) : launch_conv<64, kWgradT>(ma, mb, mc, a, s);
 }
 
 // pointwise weight gradient into partials [splits][C][K]
@@ -1506,7 +1540,7 @@ static int run_pw_wgrad(const float* dy, const float* x, int N, int C, int K, in
   a.out = part;
   a.tiles = a.kt * a.ct * a.splits;
   PVB2_TRY(wg_partial_map(&mc, part, K, C, p.splits));
-  return launch_bn<kPwWgrad>(p.BN, ma, mb, mc, a, s);
+  return p.kbs == 2 ? launch_bn2<kPwWgrad>(p.BN, ma, mb, mc, a, s) : launch_bn<kPwWgrad>(p.BN, ma, mb, mc, a, s);
 }
 
 // im2col weight-gradient plan: GEMM rows = Kc im2col columns, GEMM columns = K
