@@ -300,3 +300,74 @@ def test_bn_clone_joins_pass(ocl, then):
     (y0, c0), (y1, c1) = run(cpu, "cpu"), run(dev, DEV)
     assert _close(c0, c1) and _close(y0, y1)
     _check_bn_state(cpu, dev)
+
+
+def _relu6_grads(make, dev):
+    """forward + backward of make(x) on `dev`: (output, x.grad)"""
+    x = _x((2, 8, 6, 6), 90).to(dev).requires_grad_()
+    y = make(x)
+    y.backward(_x(y.shape, 91).to(dev))
+    return y.detach().cpu(), x.grad.cpu()
+
+
+def test_relu6_inplace_saves_output_not_a_clone(ocl, tmp_path):
+    """hardtanh_ under autograd (csrc/host/ops_autograd.cpp) saves its output:
+    the batch norm's pending pass takes the ReLU6 with no clone folded in, and
+    the gradients equal torch-CPU's (whose kernel clones the input)"""
+    cpu, dev = _bn_pair_wide(8, 92)
+    path = str(tmp_path / "prof.csv")
+    x = _x((4, 8, 9, 9), 93)
+    xc, xd = x.clone().requires_grad_(), x.to(DEV).requires_grad_()
+    yc = nn.functional.relu6(cpu(xc), inplace=True)
+    with torch.ocl.profile(DEV, path):
+        yd = nn.functional.relu6(dev(xd), inplace=True)
+        torch.ocl.synchronize()
+    ops = [line.split(",")[1] for line in open(path).read().splitlines()[1:]]
+    assert "native_batch_norm.apply+hardtanh_" in ops, ops
+    assert not any("copy" in o for o in ops), ops
+    g = _x(yc.shape, 94)
+    yc.backward(g)
+    yd.backward(g.to(DEV))
+    assert _close(yc, yd) and _close(xc.grad, xd.grad, 1e-4)
+    for p, q in zip(cpu.parameters(), dev.parameters()):
+        assert _close(p.grad, q.grad, 1e-4)
+
+
+@pytest.mark.parametrize("case", ["view", "min_ge_max", "no_grad_input"])
+def test_hardtanh_inplace_other_cases_follow_torch(ocl, case):
+    """the cases the output-saving kernel leaves to torch's own autograd
+    kernel give torch-CPU's results"""
+    def make(x):
+        y = x * 1.5 + 0.5
+        if case == "view":
+            nn.functional.hardtanh(y[:, :4], 0.0, 6.0, inplace=True)
+        elif case == "min_ge_max":
+            nn.functional.hardtanh(y, 1.0, 1.0, inplace=True)
+        else:
+            y = y + x.detach()
+            nn.functional.relu6(y, inplace=True)
+        return y
+
+    (y0, g0), (y1, g1) = _relu6_grads(make, "cpu"), _relu6_grads(make, DEV)
+    assert _close(y0, y1) and _close(g0, g1, 1e-5)
+
+
+def test_hardtanh_inplace_no_grad_and_leaf(ocl):
+    x = _x((3, 5), 95).to(DEV)
+    with torch.no_grad():
+        v = x._version
+        nn.functional.relu6(x, inplace=True)
+        assert x._version == v + 1
+    assert _close(nn.functional.relu6(_x((3, 5), 95)), x)
+    leaf = _x((3, 5), 96).to(DEV).requires_grad_()
+    with pytest.raises(RuntimeError):
+        nn.functional.relu6(leaf, inplace=True)
+
+
+def test_relu6_output_modified_before_backward_raises(ocl):
+    """like relu_, the saved output must not change before backward"""
+    x = _x((2, 4, 5, 5), 97).to(DEV).requires_grad_()
+    y = nn.functional.relu6(x * 2.0, inplace=True)
+    y.add_(1.0)
+    with pytest.raises(RuntimeError):
+        y.sum().backward()
