@@ -9,7 +9,8 @@ Prints ONE JSON line (rank 0).  `value` is whole-job images/s with inputs
 resident in HBM (device-timed with events on the backend stream, max over
 ranks); `e2e` is the same metric through the public API with each step's
 batch copied from pinned host memory (on a copy stream, overlapping the
-previous step) and the loss read back every step.  The roofline
+previous step) and every step's loss copied back to pinned host memory and
+read by the host after it has enqueued the next step.  The roofline
 object covers the dominant kernel class (the convolutions, fwd+bwd); the CPU
 baseline is the torch-CPU step (the reference's validation path) timed on
 this host at the configuration's batch (2 warm-up + 3 timed steps).  A second
@@ -314,15 +315,30 @@ def run_ours(a):
                 bufs[i % 2][1].copy_(yp, non_blocking=True)
                 ready[i % 2].record()
 
+        # each step's loss goes to pinned host memory on the compute stream
+        # right after the step; the host reads it once the next step is
+        # enqueued (a training loop that logs the loss one step behind), so
+        # the device is never left waiting for the host between steps
+        loss_h = [torch.empty((), dtype=torch.float32, pin_memory=True) for _ in range(2)]
+        loss_ev = [torch.Event(device=dev) for _ in range(2)]
+        losses = []
+
         def run_e2e(n):
+            losses.clear()
             load(0)
             for i in range(n):
                 ready[i % 2].wait()
                 l = step(*bufs[i % 2])
                 free[i % 2].record()
+                loss_h[i % 2].copy_(l.detach(), non_blocking=True)
+                loss_ev[i % 2].record()
                 if i + 1 < n:
                     load(i + 1)
-                l.item()
+                if i > 0:
+                    loss_ev[(i - 1) % 2].synchronize()
+                    losses.append(loss_h[(i - 1) % 2].item())
+            loss_ev[(n - 1) % 2].synchronize()
+            losses.append(loss_h[(n - 1) % 2].item())
 
         run_e2e(2)
         barrier()
