@@ -947,11 +947,11 @@ static bool use_im2col(const pvb2_conv2d_desc* d) {
 }
 
 // Few input channels and filter rows of at most 8 taps over a large image
-// (the 3-channel 7x7 stem): filter-row windows of a padded channels-last
+// (ResNet's 3-channel 7x7 stem, MobileNet-v2's 3x3): filter-row windows of a padded channels-last
 // copy instead of im2col columns (pad_window_kernel).  The weight gradient
 // reads each 32-pixel K block as two 16-pixel runs of one output row.
 static bool use_window(const pvb2_conv2d_desc* d) {
-  return d->C <= 4 && d->S <= 8 && d->R <= kMaxTaps && d->R * d->S >= 25 && d->dil_h == 1 && d->dil_w == 1 &&
+  return d->C <= 4 && d->S <= 8 && d->R <= kMaxTaps && d->R * d->S >= 9 && d->dil_h == 1 && d->dil_w == 1 &&
          d->stride_h <= 8 && d->stride_w <= 8 && d->Q % 16 == 0 && ((int64_t)d->P * d->Q) % 4 == 0 &&
          d->N <= 65535;
 }
@@ -1437,6 +1437,7 @@ static int wgrad_reduce(const float* part, int splits, int taps, int rows, int c
   } else {
     int G = 1;
     while (G < 32 && G * 8 <= splits) G <<= 1;  // at least 4 splits per thread row
+    if (G < 32 && G * 4 <= splits && splits >= 128) G <<= 1;  // one batch of loads per row
     const dim3 grid((unsigned)((mv + 31) / 32), (unsigned)nv, (unsigned)taps);
     wgrad_reduce_split_kernel<<<grid, dim3(32, G), G * 32 * sizeof(float), s>>>(part, splits, taps, cols,
                                                                                round4(rows), mv, dw, osm, osn, ost);
