@@ -470,3 +470,60 @@ def test_batch_norm_split_fwd_capi(lib, residual, relu):
     assert np.abs(md.cpu().numpy() - mean).max() < 1e-5
     assert np.abs(rmd.cpu().numpy() - nrm).max() < 1e-5
     assert np.abs(rvd.cpu().numpy() - nrv).max() < 1e-4
+
+
+def test_batch_norm_relu6_capi(lib):
+    """ReLU6 through the split batch norm: pvb2_batch_norm_fwd_apply with
+    act = 2 and sum_out (plain values to y, clamped ones to sum_out, no
+    residual), then pvb2_batch_norm_bwd_act with act = 2 (the hardtanh
+    gradient (out <= 0 || out >= 6) ? 0 : g formed in the first pass),
+    against the numpy restatements; act values other than 0-2 are refused."""
+    rng = np.random.default_rng(23)
+    shape = (4, 16, 12, 10)
+    x = (rng.standard_normal(shape) * 2 + 1).astype(np.float32)
+    C = shape[1]
+    gam = rng.uniform(2.0, 4.0, C).astype(np.float32)  # a good share of the outputs past 6
+    bet = rng.standard_normal(C).astype(np.float32)
+    rm, rv = np.zeros(C, np.float32), np.ones(C, np.float32)
+    xd, gd, bd, rmd, rvd = dev(x), dev(gam), dev(bet), dev(rm), dev(rv)
+    yd, od = torch.empty(shape).to(DEV), torch.empty(shape).to(DEV)
+    md, isd = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    wsz = lib.pvb2_batch_norm_workspace_size(ctypes.byref(td(xd)))
+    ws = torch.empty(max(wsz, 4), dtype=torch.uint8).to(DEV)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    sync()
+    ok(lib, lib.pvb2_batch_norm_fwd_stats(ctypes.byref(td(xd)), ptr(ws), ctypes.c_size_t(ws.numel()), stream()))
+    apply = lambda act: lib.pvb2_batch_norm_fwd_apply(
+        ctypes.byref(td(xd)), ptr(gd), ptr(bd), ptr(rmd), ptr(rvd), ctypes.c_double(0.1), ctypes.c_double(1e-5),
+        ctypes.byref(td(yd)), ptr(md), ptr(isd), None, act, ctypes.byref(td(od)), ptr(ws),
+        ctypes.c_size_t(ws.numel()), stream())
+    assert apply(3) == 1 and b"activation" in lib.pvb2_last_error()
+    ok(lib, apply(2))
+    sync()
+    y, mean, invstd, _, _ = npref.batch_norm_train(x, gam, bet, rm, rv, 0.1, 1e-5)
+    out = np.clip(y, 0.0, 6.0)
+    assert (out == 6.0).any() and (out == 0.0).any()
+    assert np.abs(yd.cpu().numpy() - y).max() < 1e-4
+    assert np.abs(od.cpu().numpy() - out).max() < 1e-4
+
+    g = rng.standard_normal(shape).astype(np.float32)
+    gdv = dev(g)
+    dyd, dxd = torch.empty(shape).to(DEV), torch.empty(shape).to(DEV)
+    dgam, dbet = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    outd = od.clone()
+    sync()
+    ok(lib, lib.pvb2_batch_norm_bwd_act(2, ctypes.byref(td(gdv)), ctypes.byref(td(outd)), ctypes.byref(td(xd)),
+                                        ptr(gd), ptr(md), ptr(isd), ctypes.byref(td(dyd)), ctypes.byref(td(dxd)),
+                                        ptr(dgam), ptr(dbet), ptr(ws), ctypes.c_size_t(ws.numel()), stream()))
+    assert lib.pvb2_batch_norm_bwd_act(3, ctypes.byref(td(gdv)), ctypes.byref(td(outd)), ctypes.byref(td(xd)),
+                                       ptr(gd), ptr(md), ptr(isd), ctypes.byref(td(dyd)), ctypes.byref(td(dxd)),
+                                       ptr(dgam), ptr(dbet), ptr(ws), ctypes.c_size_t(ws.numel()), stream()) == 1
+    sync()
+    o = od.cpu().numpy()
+    dy = np.where((o <= 0.0) | (o >= 6.0), 0.0, g).astype(np.float32)
+    assert np.array_equal(dyd.cpu().numpy(), dy)
+    dx, dgr, dbr = npref.batch_norm_backward(dy, x, gam, md.cpu().numpy(), isd.cpu().numpy())
+    scale = np.abs(dx).max()
+    assert np.abs(dxd.cpu().numpy() - dx).max() < 1e-4 * scale
+    assert np.abs(dgam.cpu().numpy() - dgr).max() < 1e-3 * np.abs(dgr).max()
+    assert np.abs(dbet.cpu().numpy() - dbr).max() < 1e-3 * np.abs(dbr).max()
