@@ -66,24 +66,50 @@ __device__ __forceinline__ int first_out(int pos, int k, int s, int pad, int dil
   return (num + s - 1) / s;
 }
 
-// Backward as a deterministic scatter: outputs are split into classes
-// (p mod mh, q mod mw) whose windows never overlap (mh * sh >= the window's
-// height, likewise for widths), and one launch per class adds each output's
-// gradient at its recorded argmax.  Within a launch no two threads touch the
-// same input element; the classes run in a fixed order.  Indices outside the
-// plane are ignored.  grid (ceil(class outputs / block), min(planes, 65535)).
-__global__ void maxpool_bwd_class_kernel(const float* __restrict__ dy, const int64_t* __restrict__ ind,
-                                         float* __restrict__ dx, int64_t planes, int HW, int P, int Q, int mh, int mw,
-                                         int ci, int cj) {
-  const int Pc = (P - ci + mh - 1) / mh, Qc = (Q - cj + mw - 1) / mw;
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= Pc * Qc) return;
-  const int a = t / Qc, b = t - a * Qc;
-  const int o = (ci + a * mh) * Q + (cj + b * mw);
+// Backward as a gather: each input element sums, in increasing output index
+// (the order in which torch-CPU's scatter adds them, so the sums are the
+// same), the gradients of the outputs whose window can hold it and whose
+// recorded argmax it is.  Every dX element is written once, coalesced, so
+// there is no clearing pass and no read-modify-write; the few outputs each
+// element consults are read by its neighbours too and come from L1.
+// grid (ceil(H*W / block), min(planes, 128)): each thread works its
+// position's candidate outputs out once and walks planes.
+__global__ void maxpool_bwd_gather_kernel(const float* __restrict__ dy, const int64_t* __restrict__ ind,
+                                          float* __restrict__ dx, int64_t planes, int H, int W, int P, int Q,
+                                          pvb2_pool2d_desc d) {
+  const int HW = H * W;
+  const int pos = blockIdx.x * blockDim.x + threadIdx.x;
+  if (pos >= HW) return;
+  const int h = pos / W, w = pos - h * W;
+  const int p0 = first_out(h, d.kh, d.sh, d.ph, d.dh), p1 = min(P - 1, (h + d.ph) / d.sh);
+  const int q0 = first_out(w, d.kw, d.sw, d.pw, d.dw), q1 = min(Q - 1, (w + d.pw) / d.sw);
   const int64_t PQ = (int64_t)P * Q;
-  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
-    const int64_t i = __ldg(ind + plane * PQ + o);
-    if (i >= 0 && i < HW) dx[plane * HW + i] += __ldg(dy + plane * PQ + o);
+  // four planes at a time, their loads issued together
+  constexpr int kU = 4;
+  for (int64_t plane0 = blockIdx.y; plane0 < planes; plane0 += (int64_t)kU * gridDim.y) {
+    float acc[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) acc[u] = 0.f;
+    for (int p = p0; p <= p1; ++p)
+      for (int q = q0; q <= q1; ++q) {
+        const int o = p * Q + q;
+        int64_t iv[kU];
+        float gv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int64_t plane = plane0 + (int64_t)u * gridDim.y;
+          iv[u] = plane < planes ? __ldg(ind + plane * PQ + o) : -1;
+          gv[u] = plane < planes ? __ldg(dy + plane * PQ + o) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          if (iv[u] == pos) acc[u] += gv[u];
+      }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t plane = plane0 + (int64_t)u * gridDim.y;
+      if (plane < planes) dx[plane * HW + pos] = acc[u];
+    }
   }
 }
 
@@ -344,20 +370,15 @@ int pvb2_max_pool2d_bwd(const pvb2_pool2d_desc* d, const pvb2_tensor* dy, const 
   if (planes * hw == 0) return PVB2_OK;
   PVB2_CHECK_ARG(hw < (int64_t)1 << 31 && pq < (int64_t)1 << 31, "max_pool2d_backward: plane too large");
   cudaStream_t s = as_stream(stream);
-  PVB2_CUDA_TRY(cudaMemsetAsync(dx->data, 0, (size_t)(planes * hw) * sizeof(float), s));
-  if (pq == 0) return PVB2_OK;
-  const int P = (int)dy->sizes[2], Q = (int)dy->sizes[3];
-  const int mh = ((d->kh - 1) * d->dh + 1 + d->sh - 1) / d->sh;
-  const int mw = ((d->kw - 1) * d->dw + 1 + d->sw - 1) / d->sw;
-  for (int ci = 0; ci < mh; ++ci)
-    for (int cj = 0; cj < mw; ++cj) {
-      const int Pc = (P - ci + mh - 1) / mh, Qc = (Q - cj + mw - 1) / mw;
-      if (Pc <= 0 || Qc <= 0) continue;
-      const dim3 grid((unsigned)(((int64_t)Pc * Qc + 255) / 256), (unsigned)std::min<int64_t>(planes, 65535));
-      maxpool_bwd_class_kernel<<<grid, 256, 0, s>>>((const float*)dy->data, indices, (float*)dx->data, planes,
-                                                    (int)hw, P, Q, mh, mw, ci, cj);
-      PVB2_LAUNCH_CHECK();
-    }
+  if (pq == 0) {
+    PVB2_CUDA_TRY(cudaMemsetAsync(dx->data, 0, (size_t)(planes * hw) * sizeof(float), s));
+    return PVB2_OK;
+  }
+  const dim3 grid((unsigned)((hw + 255) / 256), (unsigned)std::min<int64_t>(planes, 128));
+  maxpool_bwd_gather_kernel<<<grid, 256, 0, s>>>((const float*)dy->data, indices, (float*)dx->data, planes,
+                                                 (int)dx->sizes[2], (int)dx->sizes[3], (int)dy->sizes[2],
+                                                 (int)dy->sizes[3], *d);
+  PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
 
