@@ -280,6 +280,12 @@ PVB2_API int pvb2_batch_norm_bwd_act(int act, const pvb2_tensor* grad_above, con
 PVB2_API int pvb2_batch_norm_fwd_split_ok(const pvb2_tensor* x);
 PVB2_API int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, size_t workspace_bytes,
                                        pvb2_stream stream);
+/* The same, also adding 1 to *counter (device memory, or NULL) in the same
+ * launch: the batch-norm module's num_batches_tracked += 1 (torch's
+ * BatchNorm2d.forward in training), which otherwise costs a launch of its
+ * own per layer. */
+PVB2_API int pvb2_batch_norm_fwd_stats_count(const pvb2_tensor* x, void* workspace, size_t workspace_bytes,
+                                             int64_t* counter, pvb2_stream stream);
 PVB2_API int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const float* beta,
                                        float* running_mean, float* running_var, double momentum, double eps,
                                        const pvb2_tensor* y, float* save_mean, float* save_invstd,

@@ -31,7 +31,11 @@
 // holding its storage only weakly: the next flush writes the gradient after
 // all if its storage is still alive (someone kept it), and otherwise (the
 // engine dropped it after the add, the usual case) just forgets it.
-// B200_DEFER_BN=0 turns all three deferrals off.
+// A training batch norm's module first adds 1 to its num_batches_tracked
+// (an int64 scalar): that add is left pending too, and the batch norm that
+// follows hands it to its statistics kernel (pvb2_batch_norm_fwd_stats_count)
+// instead of a launch of its own; any other op launches it as the add it is.
+// B200_DEFER_BN=0 turns all four deferrals off.
 #include <cstdlib>
 #include <mutex>
 #include <optional>
@@ -78,6 +82,7 @@ std::mutex g_mutex;
 std::optional<PendingBn> g_pending;
 std::optional<PendingThr> g_thr;
 std::optional<PendingDgrad> g_dgrad;
+std::optional<at::Tensor> g_counter;  // a pending `+= 1` of this int64 scalar
 std::atomic<bool> g_any{false};
 thread_local bool t_flushing = false;
 
@@ -148,19 +153,23 @@ struct Taken {
   std::optional<PendingBn> bn;
   std::optional<PendingThr> thr;
   std::optional<PendingDgrad> dgrad;
+  std::optional<at::Tensor> counter;
 };
 
 Taken take() {
   std::lock_guard<std::mutex> g(g_mutex);
-  Taken t{std::move(g_pending), std::move(g_thr), std::move(g_dgrad)};
+  Taken t{std::move(g_pending), std::move(g_thr), std::move(g_dgrad), std::move(g_counter)};
   g_pending.reset();
   g_thr.reset();
   g_dgrad.reset();
+  g_counter.reset();
   g_any.store(false, std::memory_order_release);
   return t;
 }
 
-bool anything_pending() { return g_pending.has_value() || g_thr.has_value() || g_dgrad.has_value(); }
+bool anything_pending() {
+  return g_pending.has_value() || g_thr.has_value() || g_dgrad.has_value() || g_counter.has_value();
+}
 
 }  // namespace
 
@@ -169,6 +178,7 @@ void flush_deferred() {
   t_flushing = true;
   try {
     auto p = take();
+    if (p.counter) p.counter->add_(1);  // the add itself (t_flushing: not deferred again)
     if (p.bn) launch(*p.bn);
     if (p.thr) launch_thr(*p.thr);
     if (p.dgrad && !p.dgrad->unwritten) launch_dgrad(*p.dgrad, p.dgrad->gx, at::Tensor());
@@ -193,7 +203,8 @@ void flush_deferred() {
 bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optional<at::Tensor>& weight,
                     const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& running_mean,
                     const std::optional<at::Tensor>& running_var, const at::Tensor& save_mean,
-                    const at::Tensor& save_invstd, double momentum, double eps, Workspace&& ws, pvb2_stream stream) {
+                    const at::Tensor& save_invstd, double momentum, double eps, Workspace&& ws, pvb2_stream stream,
+                    int64_t* counter) {
   if (!defer_enabled()) return false;
   const pvb2_tensor xd = desc(x);
   if (!pvb2_batch_norm_fwd_split_ok(&xd)) return false;
@@ -213,7 +224,7 @@ bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optiona
   p.ws_bytes = ws.bytes;
   p.stream = stream;
   p.device = (int)x.device().index();
-  OCL_CHECK(pvb2_batch_norm_fwd_stats(&xd, p.ws.get(), p.ws_bytes, stream));
+  OCL_CHECK(pvb2_batch_norm_fwd_stats_count(&xd, p.ws.get(), p.ws_bytes, counter, stream));
   for (;;) {
     flush_deferred();  // one pending pass at a time (another thread may have left one)
     std::lock_guard<std::mutex> g(g_mutex);
@@ -384,6 +395,35 @@ bool fuse_deferred_dgrad_add(const at::Tensor& self, const at::Tensor& other, co
     g_any.store(true, std::memory_order_release);
     return true;
   }
+}
+
+// `self += 1` of an int64 scalar (a batch norm's num_batches_tracked) left
+// pending for the statistics launch of the batch norm that follows
+bool defer_counter_increment(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha) {
+  if (!defer_enabled() || t_flushing) return false;
+  if (!is_ocl(self) || self.scalar_type() != at::kLong || self.numel() != 1 || !self.is_contiguous()) return false;
+  if (!other.device().is_cpu() || other.numel() != 1 || other.is_floating_point() || other.is_complex() ||
+      other.scalar_type() == at::kBool)
+    return false;
+  if (alpha.isComplex() || alpha.isFloatingPoint() || alpha.toLong() != 1 || other.item().toLong() != 1) return false;
+  for (;;) {
+    flush_deferred();
+    std::lock_guard<std::mutex> g(g_mutex);
+    if (anything_pending()) continue;
+    g_counter = self;
+    g_any.store(true, std::memory_order_release);
+    return true;
+  }
+}
+
+at::Tensor take_pending_counter(int device) {
+  if (!g_any.load(std::memory_order_acquire)) return at::Tensor();
+  std::lock_guard<std::mutex> g(g_mutex);
+  if (!g_counter || g_counter->device().index() != device) return at::Tensor();
+  at::Tensor t = std::move(*g_counter);
+  g_counter.reset();
+  g_any.store(anything_pending(), std::memory_order_release);
+  return t;
 }
 
 }  // namespace ocl

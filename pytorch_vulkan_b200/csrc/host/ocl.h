@@ -89,7 +89,15 @@ void flush_deferred();
 bool defer_bn_apply(const at::Tensor& x, const at::Tensor& y, const std::optional<at::Tensor>& weight,
                     const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& running_mean,
                     const std::optional<at::Tensor>& running_var, const at::Tensor& save_mean,
-                    const at::Tensor& save_invstd, double momentum, double eps, Workspace&& ws, pvb2_stream stream);
+                    const at::Tensor& save_invstd, double momentum, double eps, Workspace&& ws, pvb2_stream stream,
+                    int64_t* counter);
+// `self += other * alpha` of an int64 scalar by 1 (a batch norm's
+// num_batches_tracked) left pending (true) for the statistics kernel of the
+// training batch norm that follows; any other op launches it first
+bool defer_counter_increment(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha);
+// the pending increment's tensor when it lives on `device` (cleared), else
+// an undefined tensor
+at::Tensor take_pending_counter(int device);
 // true when `self += other * alpha` was folded into the pending pass
 bool fuse_deferred_add(const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha);
 // true when `dst.copy_(src)` of the pending pass's output into a contiguous

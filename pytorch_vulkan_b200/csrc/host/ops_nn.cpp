@@ -9,6 +9,7 @@
 // the CPU's, bit for bit.
 #include <deque>
 #include <mutex>
+#include <utility>
 
 #include <ATen/core/grad_mode.h>
 
@@ -411,31 +412,54 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
     const std::optional<at::Tensor>& running_mean, const std::optional<at::Tensor>& running_var, bool training,
     double momentum, double eps) {
   const int dev = input.device().index();
+  TORCH_CHECK(input.scalar_type() == at::kFloat, "ocl batch_norm: float32 only");
+  for (const auto* t : {&weight, &bias, &running_mean, &running_var})
+    if (t->has_value() && (*t)->defined()) TORCH_CHECK((*t)->is_contiguous(), "ocl batch_norm: parameters must be contiguous");
+  // the module's `num_batches_tracked += 1` just before, when it was left
+  // pending: taken before the op entry flushes it, applied by the
+  // statistics kernel below (or launched as the add it is)
+  at::Tensor counter = training ? take_pending_counter(dev) : at::Tensor();
+  auto count_apart = [&] {
+    if (counter.defined()) std::exchange(counter, at::Tensor()).add_(1);
+  };
+  try {
+    DeviceScope scope(dev);
+    OCL_OP("native_batch_norm", dev);
+    at::Tensor x = contiguous(input);
+    const int64_t C = x.size(1);
+    auto ptr = [](const std::optional<at::Tensor>& t) -> float* {
+      return t.has_value() && t->defined() ? t->data_ptr<float>() : nullptr;
+    };
+    at::Tensor y = empty(x.sizes(), at::kFloat, dev);
+    pvb2_tensor xd = desc(x), yd = desc(y);
+    pvb2_stream st = stream_for(dev);
+    if (training) {
+      at::Tensor mean = empty({C}, at::kFloat, dev), invstd = empty({C}, at::kFloat, dev);
+      Workspace ws(pvb2_batch_norm_workspace_size(&xd), dev);
+      // statistics now, the normalising pass when the next op needs it (or
+      // fused with an in-place residual add / ReLU of y)
+      if (defer_bn_apply(x, y, weight, bias, running_mean, running_var, mean, invstd, momentum, eps, std::move(ws), st,
+                         counter.defined() ? counter.data_ptr<int64_t>() : nullptr))
+        return {y, mean, invstd};
+      count_apart();
+      OCL_CHECK(pvb2_batch_norm_fwd_train(&xd, ptr(weight), ptr(bias), ptr(running_mean), ptr(running_var),
+                                          momentum, eps, &yd, mean.data_ptr<float>(), invstd.data_ptr<float>(),
+                                          ws.get(), ws.bytes, st));
+      return {y, mean, invstd};
+    }
+  } catch (...) {
+    count_apart();
+    throw;
+  }
   DeviceScope scope(dev);
   OCL_OP("native_batch_norm", dev);
-  TORCH_CHECK(input.scalar_type() == at::kFloat, "ocl batch_norm: float32 only");
   at::Tensor x = contiguous(input);
-  const int64_t C = x.size(1);
   auto ptr = [](const std::optional<at::Tensor>& t) -> float* {
     return t.has_value() && t->defined() ? t->data_ptr<float>() : nullptr;
   };
-  for (const auto* t : {&weight, &bias, &running_mean, &running_var})
-    if (t->has_value() && (*t)->defined()) TORCH_CHECK((*t)->is_contiguous(), "ocl batch_norm: parameters must be contiguous");
   at::Tensor y = empty(x.sizes(), at::kFloat, dev);
   pvb2_tensor xd = desc(x), yd = desc(y);
   pvb2_stream st = stream_for(dev);
-  if (training) {
-    at::Tensor mean = empty({C}, at::kFloat, dev), invstd = empty({C}, at::kFloat, dev);
-    Workspace ws(pvb2_batch_norm_workspace_size(&xd), dev);
-    // statistics now, the normalising pass when the next op needs it (or
-    // fused with an in-place residual add / ReLU of y)
-    if (defer_bn_apply(x, y, weight, bias, running_mean, running_var, mean, invstd, momentum, eps, std::move(ws), st))
-      return {y, mean, invstd};
-    OCL_CHECK(pvb2_batch_norm_fwd_train(&xd, ptr(weight), ptr(bias), ptr(running_mean), ptr(running_var), momentum,
-                                        eps, &yd, mean.data_ptr<float>(), invstd.data_ptr<float>(), ws.get(),
-                                        ws.bytes, st));
-    return {y, mean, invstd};
-  }
   TORCH_CHECK(ptr(running_mean) && ptr(running_var), "ocl batch_norm: running stats required in eval mode");
   OCL_CHECK(pvb2_batch_norm_fwd_eval(&xd, ptr(weight), ptr(bias), ptr(running_mean), ptr(running_var), eps, &yd, st));
   return {y, empty({0}, at::kFloat, dev), empty({0}, at::kFloat, dev)};

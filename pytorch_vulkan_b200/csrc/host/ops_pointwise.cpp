@@ -90,7 +90,7 @@ static at::Tensor& add_out(const at::Tensor& self, const at::Tensor& other, cons
 // add_.Tensor: in place through add.out (out = self), or folded into a
 // pending batch-norm pass when self is its output
 static at::Tensor& add_inplace(at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha) {
-  if (fuse_deferred_add(self, other, alpha)) return self;
+  if (fuse_deferred_add(self, other, alpha) || defer_counter_increment(self, other, alpha)) return self;
   TORCH_CHECK(at::can_cast(at::result_type(self, other), self.scalar_type()), "result type ",
               at::result_type(self, other), " can't be cast to the desired output type ", self.scalar_type());
   return add_out(self, other, alpha, self);

@@ -360,11 +360,16 @@ __device__ __forceinline__ void block_allsum2(float& a, float& b, float* red) {
   }
 }
 
+// counter (or null): an int64 the first CTA's first thread increments (the
+// module's num_batches_tracked, whose `+= 1` the host hands over instead of
+// launching a kernel for it)
 __global__ void __launch_bounds__(kBnStThreads) bn_st_stats_kernel(const float* __restrict__ x, int N, int C, int HW,
                                                                    int chunk, int splits, int vec,
-                                                                   float* __restrict__ part) {
+                                                                   float* __restrict__ part,
+                                                                   long long* __restrict__ counter) {
   __shared__ float red[64];
   const int s = blockIdx.x, c = blockIdx.y;
+  if (counter && s == 0 && c == 0 && threadIdx.x == 0) *counter += 1;
   const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
   const int64_t nstride = (int64_t)C * HW;
   const float* xc = x + (int64_t)c * HW;
@@ -682,7 +687,7 @@ static int bn_fwd_stream(const BnGeom& g, const BnStream& p, const float* x, flo
                          float* save_mean, float* save_invstd, float* part, cudaStream_t s) {
   const dim3 grid((unsigned)p.splits, (unsigned)g.C);
   bn_st_stats_kernel<<<grid, kBnStThreads, 0, s>>>(x, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits, p.vec ? 1 : 0,
-                                                    part);
+                                                    part, nullptr);
   PVB2_LAUNCH_CHECK();
   bn_st_apply_kernel<<<grid, kBnStThreads, 0, s>>>(x, y, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits,
                                                     p.vec ? 1 : 0, part, gamma, beta, running_mean, running_var,
@@ -1084,6 +1089,11 @@ int pvb2_batch_norm_fwd_split_ok(const pvb2_tensor* x) {
 }
 
 int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+  return pvb2_batch_norm_fwd_stats_count(x, workspace, workspace_bytes, nullptr, stream);
+}
+
+int pvb2_batch_norm_fwd_stats_count(const pvb2_tensor* x, void* workspace, size_t workspace_bytes, int64_t* counter,
+                                    pvb2_stream stream) {
   PVB2_TRY(check_bn_x(x));
   PVB2_CHECK_ARG(pvb2_batch_norm_fwd_split_ok(x), "batch_norm: input not supported by the split forward");
   const BnGeom g = bn_geom(x);
@@ -1095,7 +1105,7 @@ int pvb2_batch_norm_fwd_stats(const pvb2_tensor* x, void* workspace, size_t work
   const dim3 grid((unsigned)p.splits, (unsigned)g.C);
   bn_st_stats_kernel<<<grid, kBnStThreads, 0, as_stream(stream)>>>((const float*)x->data, (int)g.N, (int)g.C,
                                                                   (int)g.HW, p.chunk, p.splits, p.vec ? 1 : 0,
-                                                                  (float*)workspace);
+                                                                  (float*)workspace, (long long*)counter);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }

@@ -371,3 +371,53 @@ def test_relu6_output_modified_before_backward_raises(ocl):
     y.add_(1.0)
     with pytest.raises(RuntimeError):
         y.sum().backward()
+
+
+@pytest.mark.parametrize("shape", SHAPES + [(16, 24)], ids=["x".join(map(str, s)) for s in SHAPES + [(16, 24)]])
+@pytest.mark.parametrize("momentum", [0.1, None], ids=["m0.1", "cumulative"])
+def test_num_batches_tracked_joins_stats(ocl, shape, momentum, tmp_path):
+    """the module's num_batches_tracked += 1 is applied by the following
+    training batch norm's statistics kernel (no launch of its own); the
+    count and the running statistics equal torch-CPU's, with momentum=None
+    (which reads the count on the host) too"""
+    C = shape[1]
+    mk = nn.BatchNorm2d if len(shape) == 4 else nn.BatchNorm1d
+    torch.manual_seed(98)
+    cpu = mk(C, momentum=momentum).train()
+    dev = mk(C, momentum=momentum).to(DEV).train()
+    dev.load_state_dict(cpu.state_dict())
+    path = str(tmp_path / "prof.csv")
+    with torch.ocl.profile(DEV, path):
+        for i in range(4):
+            x = _x(shape, 99 + i)
+            assert _close(cpu(x), dev(x.to(DEV)))
+        torch.ocl.synchronize()
+    ops = [line.split(",")[1] for line in open(path).read().splitlines()[1:]]
+    if momentum is not None:
+        assert not any(o.startswith("add") for o in ops), ops
+    assert dev.num_batches_tracked.item() == cpu.num_batches_tracked.item() == 4
+    _check_bn_state(cpu, dev)
+
+
+def test_pending_count_read_or_followed_by_other_ops(ocl):
+    """a pending count is applied before anything else reads it"""
+    cpu, dev = _bn_pair(8, 103)
+    x = _x((2, 8, 4, 4), 104)
+    cpu(x), dev(x.to(DEV))
+    dev.num_batches_tracked.add_(1)
+    assert dev.num_batches_tracked.item() == 2
+    dev.num_batches_tracked.add_(1)
+    t = dev.num_batches_tracked * 10  # another op on the counter itself
+    assert t.item() == 30
+    dev.num_batches_tracked.add_(1)
+    dev.eval()(x.to(DEV))  # an eval batch norm does not take it
+    assert dev.num_batches_tracked.item() == 4
+    dev.train()
+    dev.num_batches_tracked.add_(2)  # not an increment by one: a plain add
+    dev.num_batches_tracked.add_(1, alpha=3)
+    assert dev.num_batches_tracked.item() == 9
+    c = dev.num_batches_tracked.clone()
+    dev.num_batches_tracked.add_(1)
+    c.add_(1)  # another counter: the first one is launched first
+    dev(x.to(DEV))
+    assert (dev.num_batches_tracked.item(), c.item()) == (11, 10)
