@@ -181,6 +181,28 @@ inline bool first_on_device(std::atomic<uint64_t>& mask) {
   return (mask.fetch_or(bit) & bit) == 0;
 }
 
+// Division by a runtime divisor d as a multiply-high and shift (Granlund and
+// Montgomery's method, as CUTLASS's FastDivmod states it): m = ceil(2^p / d),
+// p = 31 + ceil(log2 d); exact for dividends below 2^31.
+struct FastDiv {
+  int d;
+  uint32_t m, s;
+};
+inline FastDiv fast_div(int d) {
+  FastDiv f{d, 0, 0};
+  if (d > 1) {
+    int l = 0;
+    while ((1ll << l) < d) ++l;
+    const int p = 31 + l;
+    f.m = (uint32_t)(((1ull << p) + (uint64_t)d - 1) / (uint64_t)d);
+    f.s = (uint32_t)(p - 32);
+  }
+  return f;
+}
+__device__ __forceinline__ int fdiv(int n, const FastDiv& f) {
+  return f.d > 1 ? (int)(__umulhi((uint32_t)n, f.m) >> f.s) : n;
+}
+
 inline int grid_for(int64_t n, int block, int max_blocks_per_sm = 8) {
   int64_t b = (n + block - 1) / block;
   int64_t cap = (int64_t)num_sms() * max_blocks_per_sm;

@@ -707,15 +707,22 @@ __global__ void __launch_bounds__(256) nchw_to_nhwc_v4_kernel(const float* __res
   }
 }
 
-// forward: W [K][C][R][S] -> Wp [K][R][S][Cp]
-__global__ void pack_w_fwd_kernel(const float* __restrict__ w, float* __restrict__ wp, int K, int C, int Cp, int RS) {
-  const int total = K * RS * Cp;  // weights: far below 2^31 elements (checked by the launcher)
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const int c = i % Cp;
-    const int t = i / Cp;
-    const int rs = t % RS, k = t / RS;
-    wp[i] = c < C ? __ldg(w + (k * C + c) * RS + rs) : 0.f;
-  }
+// forward: W [K][C][R][S] -> Wp [K][R][S][Cp].  One warp per 32 channels
+// of one k: lane c reads its R*S taps (its first load brings the warp's
+// 32 x R*S contiguous values into L1, the others hit there) and each tap is
+// one 128-byte run of Wp.  128-thread blocks, K * ceil(Cp / 32) warps.
+__global__ void __launch_bounds__(128) pack_w_fwd_kernel(const float* __restrict__ w, float* __restrict__ wp, int K,
+                                                         int C, int Cp, int RS) {
+  const int nb = (Cp + 31) / 32;
+  const int warp = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (warp >= K * nb) return;
+  const int k = warp / nb, c = (warp - k * nb) * 32 + lane;
+  if (c >= Cp) return;
+  const float* src = w + ((int64_t)k * C + c) * RS;
+  float* dst = wp + (int64_t)k * RS * Cp + c;
+  const bool in = c < C;
+#pragma unroll 4
+  for (int rs = 0; rs < RS; ++rs) dst[(int64_t)rs * Cp] = in ? __ldg(src + rs) : 0.f;
 }
 
 // dgrad phase: Wd[c][t][k] = W[k][c][r_t][s_t] over the phase's tap list
@@ -835,25 +842,29 @@ __global__ void unwindow_wgrad_kernel(const float* __restrict__ t, int ld, float
 // Strided 1x1 convolutions (ResNet's downsampling projections) as
 // pointwise ones over the sampled pixels.
 // xs[plane][p][q] = x[plane][p*sh][q*sw]; one thread per sampled element,
-// 32-bit index arithmetic (the host keeps the element count below 2^31)
-__global__ void subsample_kernel(const float* __restrict__ x, float* __restrict__ xs, int total, int H, int W, int P,
-                                 int Q, int sh, int sw) {
+// 32-bit index arithmetic (the host keeps the element count below 2^31),
+// divisions by Q and P as multiply-highs
+__global__ void subsample_kernel(const float* __restrict__ x, float* __restrict__ xs, int total, int H, int W,
+                                 FastDiv Q, FastDiv P, int sh, int sw) {
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
-    const int q = e % Q, r = e / Q;
-    const int p = r % P, pl = r / P;
+    const int r = fdiv(e, Q), q = e - r * Q.d;
+    const int pl = fdiv(r, P), p = r - pl * P.d;
     xs[e] = __ldg(x + ((int64_t)pl * H + p * sh) * W + q * sw);
   }
 }
 
 // dx[plane][h][w] = t[plane][h/sh][w/sw] on the sampled pixels, 0 elsewhere,
 // written whole (no separate clearing pass) as 16-byte stores; W % 4 == 0
-// and fewer than 2^31 float4 of dx (checked on the host)
-__global__ void scatter_strided_kernel(const float* __restrict__ t, float* __restrict__ dx, int total4, int H, int W,
-                                       int P, int Q, int sh, int sw) {
-  const int w4 = W / 4;
+// and fewer than 2^31 float4 of dx (checked on the host).  ST is the stride
+// in both dimensions when it is known at compile time (2), else 0 and the
+// runtime sh, sw apply; the row and plane come from multiply-highs.
+template <int ST>
+__global__ void scatter_strided_kernel(const float* __restrict__ t, float* __restrict__ dx, int total4, FastDiv w4,
+                                       FastDiv H, int P, int Q, int sh_rt, int sw_rt) {
+  const int sh = ST ? ST : sh_rt, sw = ST ? ST : sw_rt;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total4; e += gridDim.x * blockDim.x) {
-    const int w0 = (e % w4) * 4, r = e / w4;
-    const int h = r % H, pl = r / H;
+    const int r = fdiv(e, w4), w0 = (e - r * w4.d) * 4;
+    const int pl = fdiv(r, H), h = r - pl * H.d;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     if (h % sh == 0 && h / sh < P) {
       const float* row = t + ((int64_t)pl * P + h / sh) * Q;
@@ -931,8 +942,8 @@ static bool strided_pointwise(const pvb2_conv2d_desc* d) {
 static size_t sampled_bytes(const pvb2_conv2d_desc* d) { return (size_t)d->N * d->C * d->P * d->Q * 4; }
 static int subsample(const pvb2_conv2d_desc* d, const float* x, float* xs, cudaStream_t s) {
   const int64_t total = (int64_t)d->N * d->C * d->P * d->Q;
-  subsample_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, xs, (int)total, d->H, d->W, d->P, d->Q, d->stride_h,
-                                                         d->stride_w);
+  subsample_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, xs, (int)total, d->H, d->W, fast_div(d->Q),
+                                                         fast_div(d->P), d->stride_h, d->stride_w);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
@@ -1817,8 +1828,8 @@ int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const
     if (!stride_ok_for_boxes(d)) return PVB2_OK;
     const int Cp = round4(d->C);
     PVB2_TRY(to_nhwc(x, act, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
-    const int64_t wn = (int64_t)d->K * d->R * d->S * Cp;
-    pack_w_fwd_kernel<<<grid_for(wn, 256), 256, 0, s>>>(w, wp, d->K, d->C, Cp, d->R * d->S);
+    const int64_t fwarps = (int64_t)d->K * ((Cp + 31) / 32);
+    pack_w_fwd_kernel<<<(unsigned)((fwarps + 3) / 4), 128, 0, s>>>(w, wp, d->K, d->C, Cp, d->R * d->S);
     PVB2_LAUNCH_CHECK();
     PVB2_TRY(run_fwd_like(act, wp, b, y, d->N, Cp, d->H, d->W, d->K, fwd_taps(d), d->P, d->Q, d->stride_h,
                           d->stride_w, 0, (int64_t)d->K * pq, pq, d->Q, 1, (float*)((char*)ws + l.part),
@@ -1867,8 +1878,12 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
     float* t = (float*)ws;
     PVB2_TRY(run_pointwise(dy, w, nullptr, t, d->N, d->C, d->K, (int64_t)d->P * d->Q, true, s));
     const int64_t total4 = (int64_t)d->N * d->C * d->H * d->W / 4;
-    scatter_strided_kernel<<<grid_for(total4, 256), 256, 0, s>>>(t, dx, (int)total4, d->H, d->W, d->P, d->Q,
-                                                                  d->stride_h, d->stride_w);
+    const FastDiv w4 = fast_div(d->W / 4), hd = fast_div(d->H);
+    if (d->stride_h == 2 && d->stride_w == 2)
+      scatter_strided_kernel<2><<<grid_for(total4, 256), 256, 0, s>>>(t, dx, (int)total4, w4, hd, d->P, d->Q, 2, 2);
+    else
+      scatter_strided_kernel<0><<<grid_for(total4, 256), 256, 0, s>>>(t, dx, (int)total4, w4, hd, d->P, d->Q,
+                                                                       d->stride_h, d->stride_w);
     PVB2_LAUNCH_CHECK();
     *handled = true;
     return PVB2_OK;

@@ -227,28 +227,6 @@ __global__ void __launch_bounds__(kDwThreads) dw_dgrad_tile_kernel(DwGeom g, con
 }
 
 // ------------------------------------------------- 3x3 direct kernels
-// Division by a runtime divisor d as a multiply-high and shift (Granlund and
-// Montgomery's method, as CUTLASS's FastDivmod states it): m = ceil(2^p / d),
-// p = 31 + ceil(log2 d); exact for dividends below 2^31.
-struct FastDiv {
-  int d;
-  uint32_t m, s;
-};
-static FastDiv fast_div(int d) {
-  FastDiv f{d, 0, 0};
-  if (d > 1) {
-    int l = 0;
-    while ((1ll << l) < d) ++l;
-    const int p = 31 + l;
-    f.m = (uint32_t)(((1ull << p) + (uint64_t)d - 1) / (uint64_t)d);
-    f.s = (uint32_t)(p - 32);
-  }
-  return f;
-}
-__device__ __forceinline__ int fdiv(int n, const FastDiv& f) {
-  return f.d > 1 ? (int)(__umulhi((uint32_t)n, f.m) >> f.s) : n;
-}
-
 // 3x3 depthwise, dilation 1, stride SH in both dimensions (1 or 2), pad 0..2.
 // Each thread computes an "item" of four adjacent outputs of one row
 // straight from global memory: per filter row it loads the inputs the four

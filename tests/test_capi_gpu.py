@@ -88,6 +88,12 @@ CONV_SHAPES = [
     (3, 64, 15, 15, 128, 1, 1, 2, 0, 1, 1),      # strided 1x1 with 8 x 8 = 64 sampled pixels per image
     (2, 64, 14, 14, 128, 1, 1, 2, 0, 1, 1),      # strided 1x1 with 49 sampled pixels: staged path
     (2, 32, 26, 26, 64, 3, 3, 1, 0, 1, 1),       # MNIST conv2
+    # weight packing: 49 taps (phase packs of 5 channels), strided 5x5 phases,
+    # a channel count padded inside its last 64-channel chunk
+    (2, 22, 17, 17, 40, 7, 7, 1, 3, 1, 1),
+    (2, 12, 15, 15, 36, 5, 5, 2, 2, 1, 1),
+    (2, 66, 9, 9, 20, 3, 3, 1, 1, 1, 1),
+    (2, 16, 12, 12, 32, 1, 1, 3, 0, 1, 1),       # strided 1x1 at stride 3: the scatter's runtime-stride form
     # pointwise (1x1, stride 1) paths that read NCHW directly
     (4, 36, 12, 12, 40, 1, 1, 1, 0, 1, 1),       # channel tails, 144-pixel images (part-empty slots)
     (3, 64, 20, 20, 64, 1, 1, 1, 0, 1, 1),       # 13 slots per image: last tile only partly used
