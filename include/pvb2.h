@@ -521,6 +521,27 @@ PVB2_API int pvb2_conv2d_bwd_filter_staged(const pvb2_conv2d_desc* d, const pvb2
                                            const pvb2_tensor* dy, float* dw, float* db, void* workspace,
                                            size_t workspace_bytes, const float* staged, size_t staged_bytes,
                                            pvb2_stream stream);
+/* Keeping the staged output gradient between input and weight gradient:
+ * both passes of the tap-box path (3x3 and larger filters, and 1x1 layers
+ * whose planes are not a multiple of 4 pixels) read dy as a channels-last
+ * copy with K padded to 4.  pvb2_conv2d_staged_grad_bytes gives its size
+ * (0 when either pass reads dy another way); pvb2_conv2d_bwd_data_staged
+ * leaves the copy in the caller's `staged_dy` buffer (*staged_written = 1
+ * when it did), and pvb2_conv2d_bwd_filter_staged_grad reads it from there
+ * (staged_dy non-null) beside the forward's staged x, instead of staging dy
+ * a second time.  The caller passes it only while dy is unchanged.  The
+ * reference's convolution_backward (vision_ops.cpp:116-186) ran its data and
+ * filter passes on NCHW tensors and staged nothing. */
+PVB2_API size_t pvb2_conv2d_staged_grad_bytes(const pvb2_conv2d_desc* d);
+PVB2_API int pvb2_conv2d_bwd_data_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const float* w,
+                                         const pvb2_tensor* dx, void* workspace, size_t workspace_bytes,
+                                         float* staged_dy, size_t staged_dy_bytes, int* staged_written,
+                                         pvb2_stream stream);
+PVB2_API int pvb2_conv2d_bwd_filter_staged_grad(const pvb2_conv2d_desc* d, const pvb2_tensor* x,
+                                                const pvb2_tensor* dy, float* dw, float* db, void* workspace,
+                                                size_t workspace_bytes, const float* staged, size_t staged_bytes,
+                                                const float* staged_dy, size_t staged_dy_bytes,
+                                                pvb2_stream stream);
 /* convolution_overrideable, vision_ops.cpp:61-113: y = conv(x, w) + b
  * x [N,C,H,W], w [K,C/g,R,S] contiguous, y [N,K,P,Q]; x/y NCHW-contiguous
  * or channels-last.  b may be NULL. */

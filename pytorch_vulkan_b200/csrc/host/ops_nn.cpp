@@ -262,10 +262,15 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward(
       gx = empty(x.sizes(), at::kFloat, dev);
       dgrad_later = conv_dgrad_deferrable(d, gy, w, gx);
     }
+    // the input gradient's channels-last copy of dy, kept for the weight gradient
+    const size_t gsb = output_mask[0] && !dgrad_later && output_mask[1] ? pvb2_conv2d_staged_grad_bytes(&d) : 0;
+    Workspace staged_gy(gsb, dev);
+    int gy_staged = 0;
     if (output_mask[0] && !dgrad_later) {
       Workspace ws(pvb2_conv2d_workspace_size(&d, 1), dev);
       pvb2_tensor gxd = desc(gx);
-      OCL_CHECK(pvb2_conv2d_bwd_data(&d, &gyd, w.data_ptr<float>(), &gxd, ws.get(), ws.bytes, st));
+      OCL_CHECK(pvb2_conv2d_bwd_data_staged(&d, &gyd, w.data_ptr<float>(), &gxd, ws.get(), ws.bytes,
+                                            (float*)staged_gy.get(), gsb, &gy_staged, st));
     }
     if (output_mask[1] || output_mask[2]) {
       if (output_mask[1]) gw = empty(w.sizes(), at::kFloat, dev);
@@ -273,9 +278,10 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward(
       Workspace ws(output_mask[1] ? pvb2_conv2d_workspace_size(&d, 2) : 0, dev);
       size_t sb = 0;
       c10::DataPtr staged = output_mask[1] ? take_staged_input(x, d, &sb) : c10::DataPtr();
-      OCL_CHECK(pvb2_conv2d_bwd_filter_staged(&d, &xd, &gyd, output_mask[1] ? gw.data_ptr<float>() : nullptr,
-                                              output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes,
-                                              (const float*)staged.get(), sb, st));
+      OCL_CHECK(pvb2_conv2d_bwd_filter_staged_grad(
+          &d, &xd, &gyd, output_mask[1] ? gw.data_ptr<float>() : nullptr,
+          output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, (const float*)staged.get(), sb,
+          gy_staged ? (const float*)staged_gy.get() : nullptr, gsb, st));
     }
     if (dgrad_later) defer_conv_dgrad(d, gy, w, gx);
     return {gx, gw, gb};

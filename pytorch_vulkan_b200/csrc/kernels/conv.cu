@@ -18,9 +18,11 @@ namespace pvb2 {
 int conv_tc_fwd(const pvb2_conv2d_desc* d, const float* x, const float* w, const float* b, float* y, void* ws,
                 size_t ws_bytes, cudaStream_t s, bool* handled, float* staged, bool* staged_written);
 int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, void* ws,
-                     size_t ws_bytes, cudaStream_t s, bool* handled);
+                     size_t ws_bytes, cudaStream_t s, bool* handled, float* staged_dy, bool* staged_written);
 int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* dy, float* dw, void* ws,
-                       size_t ws_bytes, cudaStream_t s, bool* handled, const float* staged);
+                       size_t ws_bytes, cudaStream_t s, bool* handled, const float* staged,
+                       const float* staged_dy);
+size_t conv_tc_staged_grad_bytes(const pvb2_conv2d_desc* d);
 size_t conv_tc_workspace(const pvb2_conv2d_desc* d, int which);
 size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d);
 bool conv_tc_path(const pvb2_conv2d_desc* d, int which);
@@ -377,6 +379,11 @@ size_t pvb2_conv2d_staged_input_bytes(const pvb2_conv2d_desc* d) {
   return conv_tc_staged_bytes(d);
 }
 
+size_t pvb2_conv2d_staged_grad_bytes(const pvb2_conv2d_desc* d) {
+  if (check_desc(d) != PVB2_OK || d->math != PVB2_MATH_TF32 || is_depthwise(geom(d))) return 0;
+  return conv_tc_staged_grad_bytes(d);
+}
+
 int pvb2_conv2d_fwd(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const float* w, const float* b,
                     const pvb2_tensor* y, void* workspace, size_t workspace_bytes, pvb2_stream stream) {
   return pvb2_conv2d_fwd_staged(d, x, w, b, y, workspace, workspace_bytes, nullptr, 0, nullptr, stream);
@@ -427,6 +434,13 @@ int pvb2_conv2d_fwd_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x, cons
 
 int pvb2_conv2d_bwd_data(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const float* w, const pvb2_tensor* dx,
                          void* workspace, size_t workspace_bytes, pvb2_stream stream) {
+  return pvb2_conv2d_bwd_data_staged(d, dy, w, dx, workspace, workspace_bytes, nullptr, 0, nullptr, stream);
+}
+
+int pvb2_conv2d_bwd_data_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const float* w,
+                                const pvb2_tensor* dx, void* workspace, size_t workspace_bytes, float* staged_dy,
+                                size_t staged_dy_bytes, int* staged_written, pvb2_stream stream) {
+  if (staged_written) *staged_written = 0;
   PVB2_TRY(check_desc(d));
   PVB2_TRY(check_t(dy, d->N, d->K, d->P, d->Q, "grad_output"));
   PVB2_TRY(check_t(dx, d->N, d->C, d->H, d->W, "grad_input"));
@@ -444,9 +458,14 @@ int pvb2_conv2d_bwd_data(const pvb2_conv2d_desc* d, const pvb2_tensor* dy, const
     return PVB2_OK;
   }
   if (d->math == PVB2_MATH_TF32) {
-    bool handled = false;
+    bool handled = false, written = false;
+    if (staged_dy) {
+      PVB2_CHECK_ARG(staged_dy_bytes >= conv_tc_staged_grad_bytes(d) && ((uintptr_t)staged_dy & 15) == 0,
+                     "conv2d_bwd_data_staged: staged buffer too small or not 16-byte aligned");
+    }
     PVB2_TRY(conv_tc_bwd_data(d, (const float*)dy->data, w, (float*)dx->data, workspace, workspace_bytes, s,
-                              &handled));
+                              &handled, staged_dy, &written));
+    if (staged_written) *staged_written = written ? 1 : 0;
     if (handled) return PVB2_OK;
   }
   ConvBwdDataProb pb;
@@ -487,6 +506,14 @@ int pvb2_conv2d_bwd_filter(const pvb2_conv2d_desc* d, const pvb2_tensor* x, cons
 int pvb2_conv2d_bwd_filter_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* dy,
                                   float* dw, float* db, void* workspace, size_t workspace_bytes,
                                   const float* staged, size_t staged_bytes, pvb2_stream stream) {
+  return pvb2_conv2d_bwd_filter_staged_grad(d, x, dy, dw, db, workspace, workspace_bytes, staged, staged_bytes,
+                                            nullptr, 0, stream);
+}
+
+int pvb2_conv2d_bwd_filter_staged_grad(const pvb2_conv2d_desc* d, const pvb2_tensor* x, const pvb2_tensor* dy,
+                                       float* dw, float* db, void* workspace, size_t workspace_bytes,
+                                       const float* staged, size_t staged_bytes, const float* staged_dy,
+                                       size_t staged_dy_bytes, pvb2_stream stream) {
   PVB2_TRY(check_desc(d));
   PVB2_TRY(check_t(x, d->N, d->C, d->H, d->W, "input"));
   PVB2_TRY(check_t(dy, d->N, d->K, d->P, d->Q, "grad_output"));
@@ -522,8 +549,13 @@ int pvb2_conv2d_bwd_filter_staged(const pvb2_conv2d_desc* d, const pvb2_tensor* 
                          ((uintptr_t)staged & 15) == 0,
                      "conv2d_bwd_filter_staged: staged input does not match this convolution");
     }
+    if (staged_dy) {
+      PVB2_CHECK_ARG(conv_tc_staged_grad_bytes(d) > 0 && staged_dy_bytes >= conv_tc_staged_grad_bytes(d) &&
+                         ((uintptr_t)staged_dy & 15) == 0,
+                     "conv2d_bwd_filter_staged_grad: staged grad_output does not match this convolution");
+    }
     PVB2_TRY(conv_tc_bwd_filter(d, (const float*)x->data, (const float*)dy->data, dw, workspace, workspace_bytes, s,
-                                &handled, staged));
+                                &handled, staged, staged_dy));
     if (handled) return PVB2_OK;
   }
   const int splits = wgrad_splits(g);

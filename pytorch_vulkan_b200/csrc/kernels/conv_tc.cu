@@ -1765,6 +1765,16 @@ size_t conv_tc_staged_bytes(const pvb2_conv2d_desc* d) {
   return (size_t)d->N * d->H * d->W * round4(d->C) * 4;
 }
 
+// The output gradient as the input- and weight-gradient launches of the
+// tap-box path both read it (channels-last, K padded to 4): its size when
+// both passes take that path, else 0.  A caller may keep the input
+// gradient's copy for the weight gradient.
+size_t conv_tc_staged_grad_bytes(const pvb2_conv2d_desc* d) {
+  if (!tc_conv_shape_ok(d) || pointwise(d) || strided_pointwise(d) || use_window(d) || use_im2col(d)) return 0;
+  if (!stride_ok_for_boxes(d)) return 0;
+  return (size_t)d->N * d->P * d->Q * round4(d->K) * 4;
+}
+
 // whether conv_tc_fwd (which 0), conv_tc_bwd_data (1) or conv_tc_bwd_filter
 // (2) take the tensor-core path, given 16-byte aligned tensors and the
 // workspace that conv_tc_workspace reports; mirrors their conditions
@@ -1860,9 +1870,13 @@ static int pos_mod(int a, int m) { return ((a % m) + m) % m; }
 // i + (ph_a + pad_h - r*dil_h)/sh; likewise for columns.  Each phase is a
 // stride-1 correlation over dY with its own tap list, written to dX with
 // strides (sh, sw).  Phases without taps are zero.
+// `staged_dy` (conv_tc_staged_grad_bytes long, or null): where the
+// channels-last dy goes instead of the workspace; *staged_written says
+// whether it was filled
 int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w, float* dx, void* ws, size_t ws_bytes,
-                     cudaStream_t s, bool* handled) {
+                     cudaStream_t s, bool* handled, float* staged_dy, bool* staged_written) {
   *handled = false;
+  if (staged_written) *staged_written = false;
   if (!tc_conv_shape_ok(d)) return PVB2_OK;
   if (pointwise(d)) {
     if (!aligned16(dy) || !aligned16(w) || !aligned16(dx)) return PVB2_OK;
@@ -1889,7 +1903,8 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
     return PVB2_OK;
   }
   const int Kp = round4(d->K);
-  float* dyn = (float*)((char*)ws + l.a);
+  const bool keep = staged_dy && conv_tc_staged_grad_bytes(d) > 0;
+  float* dyn = keep ? staged_dy : (float*)((char*)ws + l.a);
   float* wd = (float*)((char*)ws + l.b);
   bool empty_phase = false;
   Taps ph[16];
@@ -1950,13 +1965,16 @@ int conv_tc_bwd_data(const pvb2_conv2d_desc* d, const float* dy, const float* w,
                           (int64_t)a * d->W + b, (int64_t)d->C * hw, hw, (int64_t)d->stride_h * d->W, d->stride_w,
                           (float*)((char*)ws + l.part), l.part_bytes, s));
   }
+  if (staged_written) *staged_written = keep;
   *handled = true;
   return PVB2_OK;
 }
 
-// `staged`: the forward's staged copy of this x (conv_tc_fwd), or null
+// `staged`: the forward's staged copy of this x (conv_tc_fwd), or null;
+// `staged_dy`: the input gradient's channels-last dy (conv_tc_bwd_data), or null
 int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* dy, float* dw, void* ws,
-                       size_t ws_bytes, cudaStream_t s, bool* handled, const float* staged) {
+                       size_t ws_bytes, cudaStream_t s, bool* handled, const float* staged,
+                       const float* staged_dy) {
   *handled = false;
   if (!tc_conv_shape_ok(d)) return PVB2_OK;
   WgPlan p;
@@ -2022,9 +2040,9 @@ int conv_tc_bwd_filter(const pvb2_conv2d_desc* d, const float* x, const float* d
   if (!stride_ok_for_boxes(d)) return PVB2_OK;
   const int Kp = round4(d->K);
   float* xn = staged ? const_cast<float*>(staged) : (float*)((char*)ws + l.a);
-  float* dyn = (float*)((char*)ws + l.b);
+  float* dyn = staged_dy ? const_cast<float*>(staged_dy) : (float*)((char*)ws + l.b);
   float* part = (float*)((char*)ws + l.c);
-  PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
+  if (!staged_dy) PVB2_TRY(to_nhwc(dy, dyn, d->N, d->K, Kp, (int64_t)d->P * d->Q, s));
   const int Cp = round4(d->C);
   if (!staged) PVB2_TRY(to_nhwc(x, xn, d->N, d->C, Cp, (int64_t)d->H * d->W, s));
   if (use_wgrad_t(d)) {

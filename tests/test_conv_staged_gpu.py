@@ -23,6 +23,7 @@ def lib(ocl):
     L.pvb2_last_error.restype = ctypes.c_char_p
     L.pvb2_conv2d_workspace_size.restype = ctypes.c_size_t
     L.pvb2_conv2d_staged_input_bytes.restype = ctypes.c_size_t
+    L.pvb2_conv2d_staged_grad_bytes.restype = ctypes.c_size_t
     return L
 
 
@@ -95,6 +96,95 @@ def test_staged_wgrad_matches_plain(lib, shape):
     bound = 2.0 ** -9 * torch.nn.grad.conv2d_weight(x.cpu().double().abs(), w.shape,
                                                 gy.cpu().double().abs(), st, pd, dl) + 1e-4
     assert bool(((gw_plain.cpu().double() - ref).abs() <= bound).all())
+
+
+GRAD_SHAPES = [
+    # N, C, H, W, K, R, S, stride, pad, dil, staged
+    (2, 64, 56, 56, 64, 3, 3, 1, 1, 1, True),      # ResNet layer1 3x3
+    (2, 128, 28, 28, 128, 3, 3, 2, 1, 1, True),    # stride-2 3x3: four input-gradient phases read the copy
+    (3, 512, 7, 7, 512, 3, 3, 1, 1, 1, True),      # layer4 3x3: split-K input gradient
+    (2, 512, 7, 7, 256, 1, 1, 1, 0, 1, True),      # 1x1 on 49-pixel planes: tap-box path
+    (2, 20, 17, 17, 40, 7, 7, 1, 3, 1, True),      # 7x7, K padded to 40
+    (2, 3, 64, 64, 64, 7, 7, 2, 3, 1, False),      # stem: the weight gradient reads NCHW dy (window path)
+    (2, 64, 14, 14, 128, 1, 1, 1, 0, 1, False),    # pointwise: NCHW throughout
+]
+
+
+@pytest.mark.parametrize("shape", GRAD_SHAPES, ids=["x".join(map(str, s[:10])) for s in GRAD_SHAPES])
+def test_staged_grad_matches_plain(lib, shape):
+    """pvb2_conv2d_bwd_data_staged leaves its channels-last dy for
+    pvb2_conv2d_bwd_filter_staged_grad: input and weight gradients are bit
+    for bit those of the plain calls (each staging dy itself)"""
+    N, C, H, W, K, R, S, st, pd, dl, staged = shape
+    P = (H + 2 * pd - dl * (R - 1) - 1) // st + 1
+    Q = (W + 2 * pd - dl * (S - 1) - 1) // st + 1
+    d = Conv(N, C, H, W, K, R, S, P, Q, st, st, pd, pd, dl, dl, 1, 0)
+    nbytes = lib.pvb2_conv2d_staged_grad_bytes(ctypes.byref(d))
+    assert (nbytes > 0) == staged
+    exact = Conv(N, C, H, W, K, R, S, P, Q, st, st, pd, pd, dl, dl, 1, 1)
+    assert lib.pvb2_conv2d_staged_grad_bytes(ctypes.byref(exact)) == 0
+    g = torch.Generator().manual_seed(sum(shape[:10]) + 1)
+    x = torch.randn(N, C, H, W, generator=g).to(DEV)
+    w = (torch.randn(K, C, R, S, generator=g) * 0.1).to(DEV)
+    gy = torch.randn(N, K, P, Q, generator=g).to(DEV)
+    buf = torch.empty(max(nbytes, 16), dtype=torch.uint8).to(DEV)
+    ws1 = torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), 1), 4), dtype=torch.uint8).to(DEV)
+    ws2 = torch.empty(max(lib.pvb2_conv2d_workspace_size(ctypes.byref(d), 2), 4), dtype=torch.uint8).to(DEV)
+    gx_plain, gx_staged = torch.empty(x.shape).to(DEV), torch.empty(x.shape).to(DEV)
+    gw_plain, gw_staged = torch.empty(w.shape).to(DEV), torch.empty(w.shape).to(DEV)
+    wp = ctypes.c_void_p(w.data_ptr())
+    sync()
+    ok(lib, lib.pvb2_conv2d_bwd_data(ctypes.byref(d), ctypes.byref(td(gy)), wp, ctypes.byref(td(gx_plain)),
+                                     ctypes.c_void_p(ws1.data_ptr()), ctypes.c_size_t(ws1.numel()), stream()))
+    ok(lib, lib.pvb2_conv2d_bwd_filter(ctypes.byref(d), ctypes.byref(td(x)), ctypes.byref(td(gy)),
+                                       ctypes.c_void_p(gw_plain.data_ptr()), None, ctypes.c_void_p(ws2.data_ptr()),
+                                       ctypes.c_size_t(ws2.numel()), stream()))
+    written = ctypes.c_int(-1)
+    ok(lib, lib.pvb2_conv2d_bwd_data_staged(ctypes.byref(d), ctypes.byref(td(gy)), wp, ctypes.byref(td(gx_staged)),
+                                            ctypes.c_void_p(ws1.data_ptr()), ctypes.c_size_t(ws1.numel()),
+                                            ctypes.c_void_p(buf.data_ptr()), ctypes.c_size_t(nbytes),
+                                            ctypes.byref(written), stream()))
+    sync()
+    assert written.value == (1 if staged else 0)
+    assert torch.equal(gx_plain.cpu(), gx_staged.cpu())
+    st_ = lib.pvb2_conv2d_bwd_filter_staged_grad(
+        ctypes.byref(d), ctypes.byref(td(x)), ctypes.byref(td(gy)), ctypes.c_void_p(gw_staged.data_ptr()), None,
+        ctypes.c_void_p(ws2.data_ptr()), ctypes.c_size_t(ws2.numel()), None, ctypes.c_size_t(0),
+        ctypes.c_void_p(buf.data_ptr()), ctypes.c_size_t(max(nbytes, 16)), stream())
+    sync()
+    if staged:
+        ok(lib, st_)
+        assert torch.equal(gw_plain.cpu(), gw_staged.cpu())
+    else:
+        assert st_ != 0  # a staged dy that this convolution never makes is refused
+    ref = torch.nn.grad.conv2d_input(x.shape, w.cpu().double(), gy.cpu().double(), st, pd, dl)
+    bound = 2.0 ** -9 * torch.nn.grad.conv2d_input(x.shape, w.cpu().double().abs(), gy.cpu().double().abs(), st,
+                                                   pd, dl) + 1e-4
+    assert bool(((gx_plain.cpu().double() - ref).abs() <= bound).all())
+
+
+def test_autograd_backward_keeps_staged_grad(ocl):
+    """through autograd (convolution_backward passing the staged dy from the
+    input gradient to the weight gradient) the gradients equal those of the
+    exact path within the TF32 bound, for a 3x3 and a 7x7-plane 1x1 layer"""
+    old = torch.ocl.get_math_mode()
+    try:
+        for (C, K, R, hw) in [(32, 48, 3, 20), (64, 96, 1, 7)]:
+            torch.manual_seed(11)
+            conv = nn.Conv2d(C, K, R, padding=R // 2, bias=False).to(DEV)
+            x0 = torch.randn(4, C, hw, hw)
+            g0 = torch.randn(4, K, hw, hw)
+            grads = []
+            for mode in (0, 1):
+                torch.ocl.set_math_mode(mode)
+                conv.zero_grad()
+                x = x0.to(DEV).requires_grad_()
+                conv(x).backward(g0.to(DEV))
+                grads.append((x.grad.cpu().double(), conv.weight.grad.cpu().double()))
+            for a, b in zip(*grads):
+                assert (a - b).abs().max().item() <= 2e-3 * max(1.0, b.abs().max().item())
+    finally:
+        torch.ocl.set_math_mode(old)
 
 
 def _grads(conv, xs, clear_between):
