@@ -179,7 +179,8 @@ def bn_roofline(rows, bn_numel, hbm_gbs, measured):
     with their fused ReLU gradient).  Algorithmic bytes per element of a
     layer's input: forward 8 (read x, write y) + 4 when the residual add is
     fused (read the other summand); backward 12 (read dy and x, write dx) + 4
-    when the ReLU gradient is fused (read the ReLU output).  The normalising
+    when the ReLU / ReLU6 gradient is fused and read from the activation's
+    output (not when its mask is formed from x).  The normalising
     passes run in forward call order and the backward passes in reverse, so
     row i of each kind belongs to batch norm i (resp. n-1-i)."""
     ms = sum(d for k, d in rows if "batch_norm" in k)
@@ -195,7 +196,7 @@ def bn_roofline(rows, bn_numel, hbm_gbs, measured):
         fwd_b += sum(4 * e for e, k in zip(bn_numel, applies) if "+add_" in k)
     bwd_b = sum(12 * e for e in bn_numel)
     if len(bwd) == n:
-        bwd_b += sum(4 * e for e, k in zip(reversed(bn_numel), bwd) if "threshold_backward" in k)
+        bwd_b += sum(4 * e for e, k in zip(reversed(bn_numel), bwd) if _reads_act_out(k))
     total = fwd_b + bwd_b
     achieved = total / (ms / 1000.0) / 1e9
     return {"bound": "hbm", "kernel": "batch norm fwd+bwd (all batch-norm launches of one step)",
@@ -204,7 +205,19 @@ def bn_roofline(rows, bn_numel, hbm_gbs, measured):
             "peak_note": "measured HBM copy (MEASURED_PEAKS.json)" if measured else "fallback 6650 GB/s",
             "traffic": None, "bn_ms_per_step": round(ms, 3), "bn_layers": n,
             "algorithmic_gb_per_step": round(total / 1e9, 3), "fused_adds": sum("+add_" in k for k in applies),
-            "fused_relu_grads": sum("threshold_backward" in k for k in bwd)}
+            "fused_relu_grads": sum(_act_grad_fused(k) for k in bwd),
+            "act_masks_from_x": sum("@x+" in k for k in bwd)}
+
+
+def _act_grad_fused(name):
+    """a batch-norm backward row that also formed the ReLU / ReLU6 gradient"""
+    return "threshold_backward" in name or "hardtanh_backward" in name
+
+
+def _reads_act_out(name):
+    """such a row that read the activation's output for the mask (rather than
+    forming it from x and the forward's (a, b): the "@x" rows)"""
+    return _act_grad_fused(name) and "@x+" not in name
 
 
 def _watchdog(comm, seconds):

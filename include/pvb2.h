@@ -257,6 +257,28 @@ PVB2_API int pvb2_batch_norm_bwd_act(int act, const pvb2_tensor* grad_above, con
                                      const float* invstd, const pvb2_tensor* dy, const pvb2_tensor* dx,
                                      float* dgamma, float* dbeta, void* workspace, size_t workspace_bytes,
                                      pvb2_stream stream);
+/* The activation's mask formed from x instead of read from its output.
+ * pvb2_batch_norm_fwd_apply_ab is pvb2_batch_norm_fwd_apply that also writes
+ * each channel's (a, b) of the normalising pass, y = fmaf(x, a, b), to
+ * ab_out (2*C floats: a at [c], b at [C + c]).  When that pass applied the
+ * activation act with no residual, its output is act(fmaf(x, a, b)) bit for
+ * bit, and pvb2_batch_norm_bwd_act_ab forms the same gradient as
+ * pvb2_batch_norm_bwd_act from x and ab without reading that output:
+ * grad_above is the gradient above the activation, dy (may be NULL) receives
+ * the gradient below it, dx the input gradient.  The reference ran
+ * threshold_backward (pointwise_ops.cpp) before its batch-norm backward
+ * (norm_ops.cpp:87-164), each as its own pass. */
+PVB2_API int pvb2_batch_norm_fwd_apply_ab(const pvb2_tensor* x, const float* gamma, const float* beta,
+                                          float* running_mean, float* running_var, double momentum, double eps,
+                                          const pvb2_tensor* y, float* save_mean, float* save_invstd,
+                                          const pvb2_tensor* residual, int act, const pvb2_tensor* sum_out,
+                                          const void* workspace, size_t workspace_bytes, float* ab_out,
+                                          pvb2_stream stream);
+PVB2_API int pvb2_batch_norm_bwd_act_ab(int act, const pvb2_tensor* grad_above, const pvb2_tensor* x,
+                                        const float* ab, const float* gamma, const float* mean,
+                                        const float* invstd, const pvb2_tensor* dy, const pvb2_tensor* dx,
+                                        float* dgamma, float* dbeta, void* workspace, size_t workspace_bytes,
+                                        pvb2_stream stream);
 /* Training forward in two calls, so that a host can fuse what follows the
  * normalisation into the second pass: pvb2_batch_norm_fwd_stats writes the
  * per-CTA partial sums of x into the workspace; pvb2_batch_norm_fwd_apply

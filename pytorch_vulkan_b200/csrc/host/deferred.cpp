@@ -23,6 +23,17 @@
 // forms the gradient from the activation's output on the fly
 // (pvb2_batch_norm_bwd_act), still storing it to the op's output tensor.
 //
+// When the activation joined a pass with no residual, its output is
+// act(fmaf(x, a, b)) with that pass's per-channel (a, b): the pass writes
+// them to a small tensor and a record remembers which output they belong to
+// (holding its storage and x's only weakly).  The batch-norm backward that
+// takes the activation gradient then forms the mask from x
+// (pvb2_batch_norm_bwd_act_ab) instead of reading the activation's output,
+// and does not store the gradient below the activation either: that tensor
+// is left as an unwritten record, written by the next flush only if
+// something still holds its storage (the engine drops it after the batch
+// norm's backward, the usual case).
+//
 // Input gradients of 1x1 stride-1 convolutions (a residual block's first
 // convolution) are left pending as well: when the next op adds that gradient
 // to another (the autograd engine summing the identity branch's gradient
@@ -37,8 +48,10 @@
 // instead of a launch of its own; any other op launches it as the add it is.
 // B200_DEFER_BN=0 turns all four deferrals off.
 #include <cstdlib>
+#include <deque>
 #include <mutex>
 #include <optional>
+#include <vector>
 
 #include "ocl.h"
 
@@ -65,7 +78,28 @@ struct PendingThr {  // act 1: out = self <= 0 ? 0 : grad; act 2: (self <= 0 || 
   int act = 1;
   pvb2_stream stream = nullptr;
   int device = 0;
+  // after a batch-norm backward that formed the gradient without storing
+  // it: out is not held, only its storage weakly, with its descriptor;
+  // written at the next flush if that storage is still alive
+  std::optional<c10::weak_intrusive_ptr<c10::StorageImpl>> unwritten;
+  pvb2_tensor out_desc;
 };
+
+// an activation output y = act(fmaf(x, a, b)) of a normalising pass, with
+// the pass's (a, b) (ab: a at [c], b at [C + c])
+struct ActRecord {
+  ActRecord(c10::weak_intrusive_ptr<c10::StorageImpl> y, c10::weak_intrusive_ptr<c10::StorageImpl> x)
+      : y_storage(std::move(y)), x_storage(std::move(x)) {}
+  c10::weak_intrusive_ptr<c10::StorageImpl> y_storage, x_storage;
+  const void* y_data = nullptr;
+  const void* x_data = nullptr;
+  std::vector<int64_t> sizes;
+  at::Tensor ab;
+  int act = 0;
+};
+constexpr size_t kMaxActRecords = 1024;
+std::mutex g_rec_mutex;
+std::deque<ActRecord> g_act_records;
 
 struct PendingDgrad {  // gx = conv2d_bwd_data(gy, w)
   pvb2_conv2d_desc d;
@@ -119,16 +153,37 @@ void launch(PendingBn& p) {
   pvb2_tensor rd, od;
   if (p.residual.defined()) rd = desc(p.residual);
   if (epi.defined()) od = desc(epi);
-  OCL_CHECK(pvb2_batch_norm_fwd_apply(&xd, fptr(p.weight), fptr(p.bias), fptr(p.running_mean), fptr(p.running_var),
-                                      p.momentum, p.eps, &yd, fptr(p.save_mean), fptr(p.save_invstd),
-                                      p.residual.defined() ? &rd : nullptr, p.act, epi.defined() ? &od : nullptr,
-                                      p.ws.get(), p.ws_bytes, p.stream));
+  // y = act(fmaf(x, a, b)) exactly: keep (a, b) for the backward
+  const bool record = p.act != 0 && !p.residual.defined() && !p.copy.defined() && !p.out.defined();
+  at::Tensor ab = record ? empty({2 * p.x.size(1)}, at::kFloat, p.device) : at::Tensor();
+  OCL_CHECK(pvb2_batch_norm_fwd_apply_ab(&xd, fptr(p.weight), fptr(p.bias), fptr(p.running_mean),
+                                         fptr(p.running_var), p.momentum, p.eps, &yd, fptr(p.save_mean),
+                                         fptr(p.save_invstd), p.residual.defined() ? &rd : nullptr, p.act,
+                                         epi.defined() ? &od : nullptr, p.ws.get(), p.ws_bytes, fptr(ab),
+                                         p.stream));
+  if (!record) return;
+  ActRecord r(p.y.storage().getWeakStorageImpl(), p.x.storage().getWeakStorageImpl());
+  r.y_data = p.y.data_ptr();
+  r.x_data = p.x.data_ptr();
+  r.sizes = p.y.sizes().vec();
+  r.ab = std::move(ab);
+  r.act = p.act;
+  std::lock_guard<std::mutex> g(g_rec_mutex);
+  // forget records whose tensors are gone (a forward without a backward)
+  for (auto it = g_act_records.begin(); it != g_act_records.end();)
+    it = it->y_storage.expired() || it->x_storage.expired() ? g_act_records.erase(it) : it + 1;
+  if (g_act_records.size() >= kMaxActRecords) g_act_records.pop_front();
+  g_act_records.push_back(std::move(r));
 }
 
 void launch_thr(PendingThr& t) {
+  if (t.unwritten) {
+    const c10::intrusive_ptr<c10::StorageImpl> st = t.unwritten->lock();
+    if (!st || st->data() != t.out_desc.data) return;  // nobody kept it
+  }
   DeviceScope scope(t.device);
   OCL_OP(t.act == 2 ? "hardtanh_backward" : "threshold_backward", t.device);
-  const pvb2_tensor od = desc(t.out), gd = desc(t.grad), sd = desc(t.self);
+  const pvb2_tensor od = t.unwritten ? t.out_desc : desc(t.out), gd = desc(t.grad), sd = desc(t.self);
   if (t.act == 2)
     OCL_CHECK(pvb2_binary(PVB2_BIN_HARDTANH_BWD, &od, &gd, &sd, 0.0, 6.0, PVB2_F32, t.stream));
   else
@@ -394,6 +449,43 @@ bool fuse_deferred_dgrad_add(const at::Tensor& self, const at::Tensor& other, co
     g_dgrad = std::move(p);
     g_any.store(true, std::memory_order_release);
     return true;
+  }
+}
+
+at::Tensor take_act_record(const at::Tensor& act_out, const at::Tensor& x, int act) {
+  if (!act_out.defined() || !x.defined()) return at::Tensor();
+  std::lock_guard<std::mutex> g(g_rec_mutex);
+  for (auto it = g_act_records.begin(); it != g_act_records.end(); ++it) {
+    if (it->y_data != act_out.data_ptr()) continue;
+    const c10::intrusive_ptr<c10::StorageImpl> ys = it->y_storage.lock(), xs = it->x_storage.lock();
+    const bool match = ys && xs && ys.get() == act_out.storage().unsafeGetStorageImpl() &&
+                       xs.get() == x.storage().unsafeGetStorageImpl() && it->x_data == x.data_ptr() &&
+                       it->act == act && act_out.sizes().equals(it->sizes) && x.sizes().equals(it->sizes) &&
+                       act_out.is_contiguous() && x.is_contiguous();
+    if (!match) continue;
+    at::Tensor ab = std::move(it->ab);
+    g_act_records.erase(it);
+    return ab;
+  }
+  return at::Tensor();
+}
+
+void defer_unwritten_act_grad(const at::Tensor& out, const at::Tensor& grad, const at::Tensor& act_out, int act) {
+  PendingThr t;
+  t.grad = grad;
+  t.self = act_out;
+  t.act = act;
+  t.device = (int)out.device().index();
+  t.stream = stream_for(t.device);
+  t.out_desc = desc(out);
+  t.unwritten = out.storage().getWeakStorageImpl();
+  for (;;) {
+    flush_deferred();  // one pending record at a time
+    std::lock_guard<std::mutex> g(g_mutex);
+    if (anything_pending()) continue;
+    g_thr = std::move(t);
+    g_any.store(true, std::memory_order_release);
+    return;
   }
 }
 

@@ -113,6 +113,12 @@ bool defer_threshold_bwd(const at::Tensor& grad, const at::Tensor& self, const a
 // when the pending activation gradient wrote grad_out: hand over its inputs
 // and kind (the batch-norm backward then stores grad_out itself) and clear it
 bool take_deferred_threshold(const at::Tensor& grad_out, at::Tensor* grad_above, at::Tensor* relu_out, int* act);
+// the forward's (a, b) when act_out = act(fmaf(x, a, b)) came from a
+// normalising pass of x (the record is consumed), else an undefined tensor
+at::Tensor take_act_record(const at::Tensor& act_out, const at::Tensor& x, int act);
+// `out` = the activation gradient of (grad, act_out), formed by a batch-norm
+// backward but not stored: written at the next flush if still held
+void defer_unwritten_act_grad(const at::Tensor& out, const at::Tensor& grad, const at::Tensor& act_out, int act);
 // input gradient of a convolution whose dgrad can also form a sum
 // (pvb2_conv2d_bwd_data_acc_ok), left pending so that a following add of it
 // joins the dgrad's epilogue

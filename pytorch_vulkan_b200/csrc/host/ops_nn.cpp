@@ -488,11 +488,16 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward
     const pvb2_tensor xd0 = desc(input);
     below_relu = pvb2_batch_norm_fwd_split_ok(&xd0) && take_deferred_threshold(grad_out, &relu_grad, &relu_out, &act);
   }
+  // the forward's (a, b) when the activation's output came from this input's
+  // normalising pass: the mask is then formed from x ("@x" in the op name)
+  const at::Tensor ab = below_relu ? take_act_record(relu_out, input, act) : at::Tensor();
+  static const char* const names[2][3] = {
+      {"native_batch_norm_backward", "threshold_backward+native_batch_norm_backward",
+       "hardtanh_backward+native_batch_norm_backward"},
+      {"native_batch_norm_backward", "threshold_backward@x+native_batch_norm_backward",
+       "hardtanh_backward@x+native_batch_norm_backward"}};
   DeviceScope scope(dev);
-  OCL_OP(!below_relu ? "native_batch_norm_backward"
-                     : (act == 2 ? "hardtanh_backward+native_batch_norm_backward"
-                                 : "threshold_backward+native_batch_norm_backward"),
-         dev);
+  OCL_OP(names[ab.defined()][below_relu ? act : 0], dev);
   at::Tensor x = contiguous(input), gy = below_relu ? grad_out : contiguous(grad_out);
   const int64_t C = x.size(1);
   const float* g = weight.has_value() && weight->defined() ? weight->data_ptr<float>() : nullptr;
@@ -509,6 +514,17 @@ static std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward
     Workspace ws(pvb2_batch_norm_workspace_size(&xd), dev);
     if (below_relu) {
       const pvb2_tensor rgd = desc(relu_grad), rod = desc(relu_out);
+      // the activation's mask from x with the forward's (a, b); its gradient
+      // (grad_out) is stored only if someone still holds it at the next flush
+      if (ab.defined()) {
+        OCL_CHECK(pvb2_batch_norm_bwd_act_ab(act, &rgd, &xd, ab.data_ptr<float>(), g, save_mean->data_ptr<float>(),
+                                             save_invstd->data_ptr<float>(), nullptr,
+                                             output_mask[0] ? &gxd : nullptr,
+                                             output_mask[1] ? gw.data_ptr<float>() : nullptr,
+                                             output_mask[2] ? gb.data_ptr<float>() : nullptr, ws.get(), ws.bytes, st));
+        defer_unwritten_act_grad(gy, relu_grad, relu_out, act);
+        return {gx, gw, gb};
+      }
       OCL_CHECK(pvb2_batch_norm_bwd_act(act, &rgd, &rod, &xd, g, save_mean->data_ptr<float>(),
                                         save_invstd->data_ptr<float>(), &gyd, output_mask[0] ? &gxd : nullptr,
                                         output_mask[1] ? gw.data_ptr<float>() : nullptr,

@@ -443,7 +443,9 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
     const float* __restrict__ part, const float* __restrict__ gamma, const float* __restrict__ beta,
     float* __restrict__ running_mean, float* __restrict__ running_var, float momentum, float eps,
     float* __restrict__ save_mean, float* __restrict__ save_invstd, const float* __restrict__ residual, int act,
-    float* __restrict__ sum_out) {
+    float* __restrict__ sum_out, float* __restrict__ ab_out) {
+  // ab_out (or null): the channel's (a, b) of y = fmaf(x, a, b), a at [c],
+  // b at [C + c], for a backward that forms the activation's mask from x
   __shared__ float s_ab[2];
   const int s = blockIdx.x, c = C - 1 - blockIdx.y;
   const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
@@ -468,6 +470,10 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
     s_ab[0] = a;
     s_ab[1] = b - meanf * a;
     if (s == 0) {
+      if (ab_out) {
+        ab_out[c] = a;
+        ab_out[C + c] = s_ab[1];
+      }
       if (save_mean) save_mean[c] = meanf;
       if (save_invstd) save_invstd[c] = invstd;
       if (running_mean) running_mean[c] = (1.f - momentum) * running_mean[c] + momentum * meanf;
@@ -544,64 +550,88 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_apply_kernel(
   }
 }
 
+// How the backward forms the gradient below an activation (GATE):
+// 0 none (dy is the batch norm's output gradient); 1 / 2 ReLU / ReLU6 whose
+// output relu_y is read; 3 / 4 ReLU / ReLU6 whose output act(fmaf(x, a, b))
+// is formed from x with the forward's (a, b), bit for bit as the forward
+// formed it.  A compile-time mode keeps each form's loop to its own math
+// (these loops are latency-bound: every instruction between a load and the
+// next one counts).
+template <int GATE>
+struct BnGate {
+  static constexpr bool on = GATE != 0;
+  static constexpr bool from_x = GATE >= 3;
+  static constexpr int act = (GATE == 1 || GATE == 3) ? 1 : 2;
+  __device__ __forceinline__ static float grad(float g, float v, float r, float fa, float fb) {
+    if (!on) return g;
+    return act_grad(from_x ? bn_epi(fmaf(v, fa, fb), nullptr, 0, act) : r, g, act);
+  }
+};
+
+// VEC: 128-bit accesses (HW % 4 == 0, aligned pointers).  dy_out (or null):
+// where the gradient below the activation is stored.
+template <bool VEC, int GATE>
 __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
     const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean, int N, int C, int HW,
-    int chunk, int splits, int vec, float* __restrict__ part, const float* __restrict__ relu_y,
-    float* __restrict__ dy_out, int act) {
-  // with relu_y: `dy` is the gradient above an activation (act 1 ReLU, 2
-  // ReLU6) whose output is relu_y; the gradient below it, as
-  // threshold_backward or hardtanh_backward computes it (act_grad), is
-  // formed here, stored to dy_out and used for the sums
+    int chunk, int splits, float* __restrict__ part, const float* __restrict__ relu_y, float* __restrict__ dy_out,
+    const float* __restrict__ ab) {
+  using G = BnGate<GATE>;
+  constexpr bool read_y = G::on && !G::from_x;
   __shared__ float red[64];
   const int s = blockIdx.x, c = blockIdx.y;
   const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
   const int64_t nstride = (int64_t)C * HW;
   const float* gc = dy + (int64_t)c * HW;
   const float* xc = x + (int64_t)c * HW;
-  const float* yc = relu_y ? relu_y + (int64_t)c * HW : nullptr;
-  float* oc = relu_y ? dy_out + (int64_t)c * HW : nullptr;
+  const float* yc = read_y ? relu_y + (int64_t)c * HW : nullptr;
+  float* oc = G::on && dy_out ? dy_out + (int64_t)c * HW : nullptr;
+  const float fa = G::from_x ? ab[c] : 0.f, fb = G::from_x ? ab[C + c] : 0.f;
   const float m = mean[c];
   float sg = 0.f, sd = 0.f;
-  const int vw = vec ? 4 : 1, step = vw * blockDim.x;
+  const int vw = VEC ? 4 : 1, step = vw * blockDim.x;
   int e = start + vw * threadIdx.x;
   if (e < end) {
     ChanWalk w(e, step, HW);
-    if (vec) {
+    if (VEC) {
       for (; e < end; e += step, w.next()) {
         const int64_t o = w.n * nstride + w.i;
         float4 g = __ldg(reinterpret_cast<const float4*>(gc + o));
         const float4 v = __ldg(reinterpret_cast<const float4*>(xc + o));
-        if (yc) {
-          const float4 r = __ldg(reinterpret_cast<const float4*>(yc + o));
-          g.x = act_grad(r.x, g.x, act);
-          g.y = act_grad(r.y, g.y, act);
-          g.z = act_grad(r.z, g.z, act);
-          g.w = act_grad(r.w, g.w, act);
-          *reinterpret_cast<float4*>(oc + o) = g;
+        if (G::on) {
+          float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (read_y) r = __ldg(reinterpret_cast<const float4*>(yc + o));
+          g.x = G::grad(g.x, v.x, r.x, fa, fb);
+          g.y = G::grad(g.y, v.y, r.y, fa, fb);
+          g.z = G::grad(g.z, v.z, r.z, fa, fb);
+          g.w = G::grad(g.w, v.w, r.w, fa, fb);
+          if (oc) *reinterpret_cast<float4*>(oc + o) = g;
         }
         sg += (g.x + g.y) + (g.z + g.w);
         sd += (g.x * (v.x - m) + g.y * (v.y - m)) + (g.z * (v.z - m) + g.w * (v.w - m));
       }
     } else {
       for (; e < end; e += 4 * step) {
-        float g[4], v[4];
+        float g[4], v[4], r[4];
+        int64_t o[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int64_t o = w.n * nstride + w.i;
+        for (int u = 0; u < 4; ++u) {  // every load first
+          o[u] = w.n * nstride + w.i;
           g[u] = 0.f;
           v[u] = m;
+          r[u] = 0.f;
           if (e + u * step < end) {
-            g[u] = __ldg(gc + o);
-            v[u] = __ldg(xc + o);
-            if (yc) {
-              g[u] = act_grad(__ldg(yc + o), g[u], act);
-              oc[o] = g[u];
-            }
+            g[u] = __ldg(gc + o[u]);
+            v[u] = __ldg(xc + o[u]);
+            if (read_y) r[u] = __ldg(yc + o[u]);
           }
           w.next();
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
+          if (G::on && e + u * step < end) {
+            g[u] = G::grad(g[u], v[u], r[u], fa, fb);
+            if (oc) oc[o[u]] = g[u];
+          }
           sg += g[u];
           sd += g[u] * (v[u] - m);
         }
@@ -615,11 +645,15 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_reduce_kernel(
   }
 }
 
+// GATE 0, 3 or 4 (the reading forms hand this pass the stored gradient)
+template <bool VEC, int GATE>
 __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_apply_kernel(
     const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean,
     const float* __restrict__ invstd, const float* __restrict__ gamma, int N, int C, int HW, int chunk, int splits,
-    int vec, const float* __restrict__ part, float* __restrict__ dx, float* __restrict__ dgamma,
-    float* __restrict__ dbeta) {
+    const float* __restrict__ part, float* __restrict__ dx, float* __restrict__ dgamma, float* __restrict__ dbeta,
+    const float* __restrict__ ab) {
+  using G = BnGate<GATE>;
+  static_assert(GATE == 0 || G::from_x, "the apply pass forms the gradient from x or takes it formed");
   __shared__ float s_k[3];
   const int s = blockIdx.x, c = C - 1 - blockIdx.y;
   const int M = N * HW, start = s * chunk, end = min(M, start + chunk);
@@ -643,31 +677,51 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_apply_kernel(
   __syncthreads();
   if (!dx) return;
   const float gm = s_k[0], kk = s_k[1], mul = s_k[2], m = mean[c];
+  const float fa = G::from_x ? ab[c] : 0.f, fb = G::from_x ? ab[C + c] : 0.f;
   const float* gc = dy + (int64_t)c * HW;
   const float* xc = x + (int64_t)c * HW;
   float* dc = dx + (int64_t)c * HW;
-  const int vw = vec ? 4 : 1, step = vw * blockDim.x;
+  const int vw = VEC ? 4 : 1, step = vw * blockDim.x;
   int e = start + vw * threadIdx.x;
   if (e >= end) return;
   ChanWalk w(e, step, HW);
-  if (vec) {
-    for (; e < end; e += step, w.next()) {
-      const int64_t o = w.n * nstride + w.i;
-      const float4 g = __ldg(reinterpret_cast<const float4*>(gc + o));
-      const float4 v = __ldg(reinterpret_cast<const float4*>(xc + o));
-      float4 r;
-      r.x = (g.x - gm - (v.x - m) * kk) * mul;
-      r.y = (g.y - gm - (v.y - m) * kk) * mul;
-      r.z = (g.z - gm - (v.z - m) * kk) * mul;
-      r.w = (g.w - gm - (v.w - m) * kk) * mul;
-      *reinterpret_cast<float4*>(dc + o) = r;
+  if (VEC) {
+    // two float4 steps per iteration, both loads issued before the math
+    for (; e < end; e += 2 * step) {
+      float4 g[2], v[2];
+      int64_t o[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        o[u] = w.n * nstride + w.i;
+        if (e + u * step < end) {
+          g[u] = __ldg(reinterpret_cast<const float4*>(gc + o[u]));
+          v[u] = __ldg(reinterpret_cast<const float4*>(xc + o[u]));
+        }
+        w.next();
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (e + u * step >= end) continue;
+        float4 gg = g[u];
+        const float4 vv = v[u];
+        gg.x = G::grad(gg.x, vv.x, 0.f, fa, fb);
+        gg.y = G::grad(gg.y, vv.y, 0.f, fa, fb);
+        gg.z = G::grad(gg.z, vv.z, 0.f, fa, fb);
+        gg.w = G::grad(gg.w, vv.w, 0.f, fa, fb);
+        float4 r;
+        r.x = (gg.x - gm - (vv.x - m) * kk) * mul;
+        r.y = (gg.y - gm - (vv.y - m) * kk) * mul;
+        r.z = (gg.z - gm - (vv.z - m) * kk) * mul;
+        r.w = (gg.w - gm - (vv.w - m) * kk) * mul;
+        *reinterpret_cast<float4*>(dc + o[u]) = r;
+      }
     }
   } else {
     for (; e < end; e += 4 * step) {
       float g[4], v[4];
       int64_t o[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 4; ++u) {  // every load first
         o[u] = w.n * nstride + w.i;
         if (e + u * step < end) {
           g[u] = __ldg(gc + o[u]);
@@ -677,9 +731,37 @@ __global__ void __launch_bounds__(kBnStThreads) bn_st_bwd_apply_kernel(
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u)
-        if (e + u * step < end) dc[o[u]] = (g[u] - gm - (v[u] - m) * kk) * mul;
+        if (e + u * step < end) dc[o[u]] = (G::grad(g[u], v[u], 0.f, fa, fb) - gm - (v[u] - m) * kk) * mul;
     }
   }
+}
+
+template <bool VEC>
+static int launch_bn_bwd(const BnGeom& g, const BnStream& p, int gate, const float* dy, const float* x,
+                          const float* mean, const float* invstd, const float* gamma, float* dx, float* dgamma,
+                          float* dbeta, float* part, const float* relu_y, float* dy_out, const float* ab,
+                          cudaStream_t s) {
+  using R = void (*)(const float*, const float*, const float*, int, int, int, int, int, float*, const float*, float*,
+                     const float*);
+  using A = void (*)(const float*, const float*, const float*, const float*, const float*, int, int, int, int, int,
+                     const float*, float*, float*, float*, const float*);
+  static const R reduce[5] = {bn_st_bwd_reduce_kernel<VEC, 0>, bn_st_bwd_reduce_kernel<VEC, 1>,
+                              bn_st_bwd_reduce_kernel<VEC, 2>, bn_st_bwd_reduce_kernel<VEC, 3>,
+                              bn_st_bwd_reduce_kernel<VEC, 4>};
+  static const A apply[3] = {bn_st_bwd_apply_kernel<VEC, 0>, bn_st_bwd_apply_kernel<VEC, 3>,
+                             bn_st_bwd_apply_kernel<VEC, 4>};
+  const dim3 grid((unsigned)p.splits, (unsigned)g.C);
+  reduce[gate]<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits, part,
+                                            relu_y, dy_out, ab);
+  PVB2_LAUNCH_CHECK();
+  // the apply pass reads the stored gradient below a read activation, or
+  // forms it again from x
+  if (gate == 1 || gate == 2) dy = dy_out;
+  apply[gate >= 3 ? gate - 2 : 0]<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, invstd, gamma, (int)g.N, (int)g.C,
+                                                                (int)g.HW, p.chunk, p.splits, part, dx, dgamma,
+                                                                dbeta, ab);
+  PVB2_LAUNCH_CHECK();
+  return PVB2_OK;
 }
 
 static int bn_fwd_stream(const BnGeom& g, const BnStream& p, const float* x, float* y, const float* gamma,
@@ -692,23 +774,22 @@ static int bn_fwd_stream(const BnGeom& g, const BnStream& p, const float* x, flo
   bn_st_apply_kernel<<<grid, kBnStThreads, 0, s>>>(x, y, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits,
                                                     p.vec ? 1 : 0, part, gamma, beta, running_mean, running_var,
                                                     (float)momentum, (float)eps, save_mean, save_invstd, nullptr, 0,
-                                                    nullptr);
+                                                    nullptr, nullptr);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
 
 static int bn_bwd_stream(const BnGeom& g, const BnStream& p, const float* dy, const float* x, const float* mean,
                          const float* invstd, const float* gamma, float* dx, float* dgamma, float* dbeta, float* part,
-                         cudaStream_t s, const float* relu_y = nullptr, float* dy_out = nullptr, int act = 0) {
-  const dim3 grid((unsigned)p.splits, (unsigned)g.C);
-  bn_st_bwd_reduce_kernel<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, (int)g.N, (int)g.C, (int)g.HW, p.chunk,
-                                                         p.splits, p.vec ? 1 : 0, part, relu_y, dy_out, act);
-  PVB2_LAUNCH_CHECK();
-  if (relu_y) dy = dy_out;  // the apply pass reads the gradient below the activation
-  bn_st_bwd_apply_kernel<<<grid, kBnStThreads, 0, s>>>(dy, x, mean, invstd, gamma, (int)g.N, (int)g.C, (int)g.HW,
-                                                        p.chunk, p.splits, p.vec ? 1 : 0, part, dx, dgamma, dbeta);
-  PVB2_LAUNCH_CHECK();
-  return PVB2_OK;
+                         cudaStream_t s, const float* relu_y = nullptr, float* dy_out = nullptr, int act = 0,
+                         const float* ab = nullptr) {
+  // gate: 0 none, 1 / 2 ReLU / ReLU6 read from relu_y, 3 / 4 formed from x
+  const int gate = ab ? (act == 1 ? 3 : 4) : (relu_y ? act : 0);
+  if (p.vec)
+    return launch_bn_bwd<true>(g, p, gate, dy, x, mean, invstd, gamma, dx, dgamma, dbeta, part, relu_y, dy_out, ab,
+                               s);
+  return launch_bn_bwd<false>(g, p, gate, dy, x, mean, invstd, gamma, dx, dgamma, dbeta, part, relu_y, dy_out, ab,
+                              s);
 }
 
 // ------------------------------------------------------------- layer norm
@@ -1115,6 +1196,16 @@ int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const fl
                               float* save_mean, float* save_invstd, const pvb2_tensor* residual, int act,
                               const pvb2_tensor* sum_out, const void* workspace, size_t workspace_bytes,
                               pvb2_stream stream) {
+  return pvb2_batch_norm_fwd_apply_ab(x, gamma, beta, running_mean, running_var, momentum, eps, y, save_mean,
+                                      save_invstd, residual, act, sum_out, workspace, workspace_bytes, nullptr,
+                                      stream);
+}
+
+int pvb2_batch_norm_fwd_apply_ab(const pvb2_tensor* x, const float* gamma, const float* beta, float* running_mean,
+                                 float* running_var, double momentum, double eps, const pvb2_tensor* y,
+                                 float* save_mean, float* save_invstd, const pvb2_tensor* residual, int act,
+                                 const pvb2_tensor* sum_out, const void* workspace, size_t workspace_bytes,
+                                 float* ab_out, pvb2_stream stream) {
   PVB2_TRY(check_bn_x(x));
   PVB2_CHECK_ARG(act >= 0 && act <= 2, "batch_norm: activation %d is not 0 (none), 1 (ReLU) or 2 (ReLU6)", act);
   PVB2_CHECK_ARG(pvb2_batch_norm_fwd_split_ok(x), "batch_norm: input not supported by the split forward");
@@ -1141,7 +1232,7 @@ int pvb2_batch_norm_fwd_apply(const pvb2_tensor* x, const float* gamma, const fl
       (const float*)x->data, (float*)y->data, (int)g.N, (int)g.C, (int)g.HW, p.chunk, p.splits, p.vec ? 1 : 0,
       (const float*)workspace, gamma, beta, running_mean, running_var, (float)momentum, (float)eps, save_mean,
       save_invstd, residual ? (const float*)residual->data : nullptr, act,
-      sum_out ? (float*)sum_out->data : nullptr);
+      sum_out ? (float*)sum_out->data : nullptr, ab_out);
   PVB2_LAUNCH_CHECK();
   return PVB2_OK;
 }
@@ -1274,6 +1365,29 @@ int pvb2_batch_norm_bwd_act(int act, const pvb2_tensor* grad_above, const pvb2_t
   return bn_bwd_stream(g, p, (const float*)grad_above->data, (const float*)x->data, mean, invstd, gamma,
                        dx ? (float*)dx->data : nullptr, dgamma, dbeta, (float*)workspace, as_stream(stream),
                        (const float*)relu_out->data, (float*)dy->data, act);
+}
+
+int pvb2_batch_norm_bwd_act_ab(int act, const pvb2_tensor* grad_above, const pvb2_tensor* x, const float* ab,
+                               const float* gamma, const float* mean, const float* invstd, const pvb2_tensor* dy,
+                               const pvb2_tensor* dx, float* dgamma, float* dbeta, void* workspace,
+                               size_t workspace_bytes, pvb2_stream stream) {
+  PVB2_CHECK_ARG(act == 1 || act == 2, "batch_norm_backward: activation %d is not 1 (ReLU) or 2 (ReLU6)", act);
+  PVB2_CHECK_ARG(ab != nullptr, "batch_norm_backward_act_ab: the forward's (a, b) are required");
+  PVB2_TRY(check_bn_x(x));
+  for (const pvb2_tensor* t : {grad_above, dy}) {
+    PVB2_CHECK_ARG(!t || (is_contiguous(t) && t->dtype == PVB2_F32 && numel(t) == numel(x)),
+                   "batch_norm_backward_act_ab: gradients must be contiguous float32 like x");
+  }
+  PVB2_CHECK_ARG(grad_above != nullptr, "batch_norm_backward_act_ab: grad_above is required");
+  PVB2_CHECK_ARG(pvb2_batch_norm_fwd_split_ok(x), "batch_norm_backward_act_ab: input not supported");
+  const BnGeom g = bn_geom(x);
+  const void* ptrs[4] = {grad_above->data, x->data, dy ? dy->data : nullptr, dx ? dx->data : nullptr};
+  const BnStream p = bn_stream_plan(g, ptrs, 4);
+  const size_t need = (size_t)g.C * p.splits * 2 * sizeof(float);
+  PVB2_CHECK_ARG(workspace && workspace_bytes >= need, "batch_norm_backward: workspace too small");
+  return bn_bwd_stream(g, p, (const float*)grad_above->data, (const float*)x->data, mean, invstd, gamma,
+                       dx ? (float*)dx->data : nullptr, dgamma, dbeta, (float*)workspace, as_stream(stream), nullptr,
+                       dy ? (float*)dy->data : nullptr, act, ab);
 }
 
 int pvb2_batch_norm_bwd_eval(const pvb2_tensor* dy, const float* gamma, const float* running_var, double eps,

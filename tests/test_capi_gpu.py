@@ -533,3 +533,67 @@ def test_batch_norm_relu6_capi(lib):
     assert np.abs(dxd.cpu().numpy() - dx).max() < 1e-4 * scale
     assert np.abs(dgam.cpu().numpy() - dgr).max() < 1e-3 * np.abs(dgr).max()
     assert np.abs(dbet.cpu().numpy() - dbr).max() < 1e-3 * np.abs(dbr).max()
+
+
+@pytest.mark.parametrize("act", [1, 2])
+@pytest.mark.parametrize("shape", [(4, 16, 12, 10), (8, 32, 14, 14), (3, 5, 7, 7)], ids=["odd_hw", "vec", "tiny"])
+def test_batch_norm_act_from_x_capi(lib, act, shape):
+    """pvb2_batch_norm_fwd_apply_ab hands out the pass's (a, b): its
+    activated output is act(fmaf(x, a, b)) bit for bit, and
+    pvb2_batch_norm_bwd_act_ab, which forms the mask from x and ab, gives
+    exactly what pvb2_batch_norm_bwd_act (reading that output) gives: the
+    gradient below the activation, dx, dgamma, dbeta; dy may be omitted."""
+    rng = np.random.default_rng(29 + act)
+    x = (rng.standard_normal(shape) * 2 + 1).astype(np.float32)
+    C = shape[1]
+    gam = rng.uniform(1.5, 4.0, C).astype(np.float32)
+    bet = rng.standard_normal(C).astype(np.float32)
+    xd, gd, bd = dev(x), dev(gam), dev(bet)
+    rmd, rvd = dev(np.zeros(C, np.float32)), dev(np.ones(C, np.float32))
+    yd, abd = torch.empty(shape).to(DEV), torch.empty(2 * C).to(DEV)
+    md, isd = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    wsz = lib.pvb2_batch_norm_workspace_size(ctypes.byref(td(xd)))
+    ws = torch.empty(max(wsz, 4), dtype=torch.uint8).to(DEV)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    sync()
+    ok(lib, lib.pvb2_batch_norm_fwd_stats(ctypes.byref(td(xd)), ptr(ws), ctypes.c_size_t(ws.numel()), stream()))
+    ok(lib, lib.pvb2_batch_norm_fwd_apply_ab(
+        ctypes.byref(td(xd)), ptr(gd), ptr(bd), ptr(rmd), ptr(rvd), ctypes.c_double(0.1), ctypes.c_double(1e-5),
+        ctypes.byref(td(yd)), ptr(md), ptr(isd), None, act, None, ptr(ws), ctypes.c_size_t(ws.numel()),
+        ptr(abd), stream()))
+    sync()
+    a, b = abd.cpu()[:C].view(1, C, 1, 1).double(), abd.cpu()[C:].view(1, C, 1, 1).double()
+    v = (torch.from_numpy(x).double() * a + b).float()  # x * a exact in float64, then rounded: fmaf
+    ref = v.clamp(min=0.0) if act == 1 else v.clamp(0.0, 6.0)
+    assert torch.equal(yd.cpu(), ref)
+    g = dev(rng.standard_normal(shape).astype(np.float32))
+    outs = []
+    for use_ab in (False, True):
+        dyd, dxd = torch.full(shape, 7.0).to(DEV), torch.empty(shape).to(DEV)
+        dgam, dbet = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+        if use_ab:
+            ok(lib, lib.pvb2_batch_norm_bwd_act_ab(
+                act, ctypes.byref(td(g)), ctypes.byref(td(xd)), ptr(abd), ptr(gd), ptr(md), ptr(isd),
+                ctypes.byref(td(dyd)), ctypes.byref(td(dxd)), ptr(dgam), ptr(dbet), ptr(ws),
+                ctypes.c_size_t(ws.numel()), stream()))
+        else:
+            ok(lib, lib.pvb2_batch_norm_bwd_act(
+                act, ctypes.byref(td(g)), ctypes.byref(td(yd)), ctypes.byref(td(xd)), ptr(gd), ptr(md), ptr(isd),
+                ctypes.byref(td(dyd)), ctypes.byref(td(dxd)), ptr(dgam), ptr(dbet), ptr(ws),
+                ctypes.c_size_t(ws.numel()), stream()))
+        sync()
+        outs.append([t.cpu() for t in (dyd, dxd, dgam, dbet)])
+    for p_, q_ in zip(*outs):
+        assert torch.equal(p_, q_)
+    # without dy: the same dx, dgamma, dbeta, and dy left untouched
+    dyd, dxd = torch.full(shape, 7.0).to(DEV), torch.empty(shape).to(DEV)
+    dgam, dbet = torch.empty(C).to(DEV), torch.empty(C).to(DEV)
+    ok(lib, lib.pvb2_batch_norm_bwd_act_ab(
+        act, ctypes.byref(td(g)), ctypes.byref(td(xd)), ptr(abd), ptr(gd), ptr(md), ptr(isd), None,
+        ctypes.byref(td(dxd)), ptr(dgam), ptr(dbet), ptr(ws), ctypes.c_size_t(ws.numel()), stream()))
+    sync()
+    assert torch.equal(dxd.cpu(), outs[0][1]) and torch.equal(dgam.cpu(), outs[0][2])
+    assert torch.equal(dbet.cpu(), outs[0][3]) and bool((dyd.cpu() == 7.0).all())
+    assert lib.pvb2_batch_norm_bwd_act_ab(
+        act, ctypes.byref(td(g)), ctypes.byref(td(xd)), None, ptr(gd), ptr(md), ptr(isd), None,
+        ctypes.byref(td(dxd)), ptr(dgam), ptr(dbet), ptr(ws), ctypes.c_size_t(ws.numel()), stream()) != 0

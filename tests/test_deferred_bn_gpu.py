@@ -421,3 +421,39 @@ def test_pending_count_read_or_followed_by_other_ops(ocl):
     c.add_(1)  # another counter: the first one is launched first
     dev(x.to(DEV))
     assert (dev.num_batches_tracked.item(), c.item()) == (11, 10)
+
+
+@pytest.mark.parametrize("act", ["relu", "relu6"])
+def test_act_grad_kept_by_hook_is_written(ocl, act):
+    """the batch-norm backward forms the activation gradient from x and does
+    not store it; a hook that keeps that gradient (the batch norm's output
+    gradient) still sees the right values, written by the next flush"""
+    cpu, dev = _bn_pair_wide(16, 105) if act == "relu6" else _bn_pair(16, 105)
+    f = (lambda t: nn.functional.relu6(t, inplace=True)) if act == "relu6" else (lambda t: torch.relu_(t))
+    x = _x((4, 16, 10, 10), 106)
+    g = _x((4, 16, 10, 10), 107)
+    res = []
+    for m, d in ((cpu, "cpu"), (dev, DEV)):
+        xi = x.detach().to(d).requires_grad_()
+        kept = []
+        y = m(xi)
+        y.register_hook(lambda t: kept.append(t))
+        z = f(y)
+        z.backward(g.to(d))
+        res.append((kept[0].cpu(), xi.grad.cpu()))
+    assert _close(res[0][0], res[1][0], 1e-6) and _close(res[0][1], res[1][1], 1e-4)
+
+
+@pytest.mark.parametrize("act", ["relu", "relu6"])
+def test_act_grad_from_x_twice_with_retained_graph(ocl, act):
+    """a second backward through a retained graph (the (a, b) record is
+    consumed by the first) reads the activation output instead, with the
+    same result, bit for bit"""
+    _, dev = _bn_pair_wide(8, 108) if act == "relu6" else _bn_pair(8, 108)
+    f = (lambda t: nn.functional.relu6(t, inplace=True)) if act == "relu6" else (lambda t: torch.relu_(t))
+    x = _x((4, 8, 12, 12), 109).to(DEV).requires_grad_()
+    z = f(dev(x))
+    g = _x((4, 8, 12, 12), 110).to(DEV)
+    (g1,) = torch.autograd.grad(z, x, g, retain_graph=True)
+    (g2,) = torch.autograd.grad(z, x, g)
+    assert torch.equal(g1.cpu(), g2.cpu())
