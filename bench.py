@@ -18,6 +18,14 @@ roofline object, `roofline_bn`, covers the batch-norm class (forward with its
 fused residual add / ReLU, backward with its fused ReLU gradient) against the
 measured HBM copy bandwidth.
 
+On one GPU the step is captured once as a CUDA graph (`torch.ocl.Graph`,
+`--graph auto`, the default) and every timed step, in both measurements,
+replays it: the same kernels as the eager step, issued with one launch
+instead of by Python, the autograd engine and the backend op by op (the
+eager step's host time is within a millisecond of its device time).  If the
+capture fails the bench times eager steps and says so (`config.step`);
+`--graph off` forces eager steps.  Data-parallel runs step eagerly.
+
 `--impl reference` times the reference's CPU path (torch-CPU ATen, as its
 tests/validate_network.py runs it) for the same workload on all host cores;
 under torchrun only rank 0 runs it.
@@ -66,6 +74,8 @@ def parse():
                     help="scaled_dot_product_attention backend for vit_b_16 (math = bmm + softmax + bmm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--graph", default="auto", choices=["auto", "off"],
+                    help="auto: one-GPU runs capture the step as a CUDA graph and replay it (eager if capture fails)")
     ap.add_argument("--deadline-s", type=float, default=600.0,
                     help="multi-GPU runs abort the NCCL communicator and exit 3 after this many seconds")
     return ap.parse_args()
@@ -292,6 +302,39 @@ def run_ours(a):
     for _ in range(a.warmup):
         step(x, y)
     barrier()
+
+    # one-GPU runs: the step captured once, replayed as one launch
+    graph = None
+    l_graph = None
+    graph_note = "eager"
+    if world == 1 and a.graph == "auto":
+        try:
+            from pytorch_vulkan_b200.graphs import Graph
+
+            graph = Graph(local)
+            with graph.capture():
+                l_graph = step(x, y)
+            for _ in range(a.warmup):
+                graph.replay()
+            if not bool(torch.isfinite(l_graph).item()):
+                raise RuntimeError("non-finite loss from the replayed step")
+            graph_note = f"cuda_graph ({graph.kernels} kernels per replay)"
+        except Exception as e:  # the eager step is the same work, issued op by op
+            sys.stderr.write(f"bench: graph capture unavailable ({e}); timing eager steps\n")
+            if graph is not None:
+                graph.reset()
+            graph = None
+            graph_note = "eager (graph capture failed)"
+
+    def run_step(xb=None, yb=None):
+        if graph is None:
+            return step(x if xb is None else xb, y if yb is None else yb)
+        if xb is not None:  # the captured step reads x and y: the batch goes there
+            x.copy_(xb)
+            y.copy_(yb)
+        graph.replay()
+        return l_graph
+
     # ---------------------------------------------------------- timed region
     e0, e1 = _C.impl_event_create(True), _C.impl_event_create(True)
     l0 = _C.impl_launch_count()
@@ -299,7 +342,7 @@ def run_ours(a):
         barrier()
         _C.impl_event_record(e0, local)
         for _ in range(a.steps):
-            step(x, y)
+            run_step()
         _C.impl_event_record(e1, local)
         barrier()
     launches = _C.impl_launch_count() - l0
@@ -341,7 +384,7 @@ def run_ours(a):
             load(0)
             for i in range(n):
                 ready[i % 2].wait()
-                l = step(*bufs[i % 2])
+                l = run_step(*bufs[i % 2])
                 free[i % 2].record()
                 loss_h[i % 2].copy_(l.detach(), non_blocking=True)
                 loss_ev[i % 2].record()
@@ -452,7 +495,7 @@ def run_ours(a):
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"{a.model} fp32 train step (fwd+bwd+SGD m0.9), batch {a.batch}/GPU, 3x224x224",
-                       "global_batch": a.batch * world, "parallelism": f"dp{world}",
+                       "global_batch": a.batch * world, "parallelism": f"dp{world}", "step": graph_note,
                        "math": ["tf32", "fp32", "3xtf32"][torch.ocl.get_math_mode()],
                        **({"attention": a.attention} if "vit" in a.model else {}),
                        "l2": "inputs/activations larger than L2 (126 MB) every step",
@@ -462,6 +505,8 @@ def run_ours(a):
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
+    if graph is not None:
+        graph.reset()
     if comm is not None:
         comm.close()
     if world > 1:

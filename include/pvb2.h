@@ -73,6 +73,7 @@ typedef struct pvb2_tensor {
 
 typedef void* pvb2_stream;          /* cudaStream_t */
 typedef void* pvb2_event;           /* cudaEvent_t  */
+typedef void* pvb2_graph;           /* a captured, instantiated CUDA graph */
 
 /* ------------------------------------------------------------------ */
 /* runtime: devices, memory, streams, events                           */
@@ -108,6 +109,23 @@ PVB2_API int pvb2_memcpy_async(void* dst, const void* src, size_t bytes, int kin
 PVB2_API int pvb2_memset_async(void* dst, int value, size_t bytes, pvb2_stream stream);
 /* number of kernels this library has launched in this process (all devices) */
 PVB2_API int64_t pvb2_launch_count(void);
+/* CUDA graphs: the work this library issues to `stream` between
+ * pvb2_graph_capture_begin and pvb2_graph_capture_end (relaxed capture mode;
+ * the stream must be one of pvb2_stream_create's) becomes one graph that
+ * pvb2_graph_launch replays on a stream with a single launch, the pointers
+ * and arguments of the capture baked in.  Nothing may synchronise with the
+ * stream while it is captured (a read back to the host, a stream or device
+ * synchronisation), and memory the captured work uses must stay allocated,
+ * unchanged in address, for as long as the graph is replayed.  Each replay
+ * adds the number of kernels captured to pvb2_launch_count.  The reference
+ * has no counterpart: it issued every kernel from the host, one by one
+ * (dlprimitives through its OpenCL queue). */
+PVB2_API int pvb2_graph_capture_begin(pvb2_stream stream);
+PVB2_API int pvb2_graph_capture_end(pvb2_stream stream, pvb2_graph* graph);
+PVB2_API int pvb2_graph_launch(pvb2_graph graph, pvb2_stream stream);
+PVB2_API int pvb2_graph_kernel_count(pvb2_graph graph, int64_t* kernels);
+PVB2_API int pvb2_graph_destroy(pvb2_graph graph);
+PVB2_API int pvb2_stream_is_capturing(pvb2_stream stream, int* capturing);
 
 /* ------------------------------------------------------------------ */
 /* tensor plumbing (src/tensor_ops.cpp)                                 */

@@ -180,6 +180,11 @@ class _OCL:
         return _C.impl_launch_count()
 
 
+from .graphs import Graph  # noqa: E402
+
+_OCL.Graph = Graph
+
+
 def synchronize(dev=None):
     """Module-level synchronize (the reference's referenced an undefined name, __init__.py:73-74)."""
     _OCL.synchronize(dev)

@@ -19,6 +19,7 @@
 #include <cstdlib>
 #include <fstream>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <random>
 #include <unordered_map>
@@ -166,11 +167,22 @@ DeviceScope::~DeviceScope() {
 // in stream order.  A block that was also used on another stream
 // (record_stream) is held back until an event recorded on that stream at
 // free time has completed.
+// Blocks allocated while a graph is being captured on a device come from a
+// pool of their own and go back to it when freed: the graph's replays write
+// them, so they stay reserved for it (never handed to other tensors, never
+// released) until the graph is destroyed, when the pool is retired and its
+// free blocks join the device's ordinary free lists.
+struct CapturePool {
+  std::unordered_map<size_t, std::vector<void*>> free_blocks;
+  bool retired = false;
+};
+
 struct BlockCtx {
   void* ptr;
   size_t size;
   int device;
   std::vector<pvb2_stream> extra_streams;
+  std::shared_ptr<CapturePool> cpool;  // set for blocks allocated during a capture
 };
 
 struct PendingFree {
@@ -182,6 +194,7 @@ struct Pool {
   std::mutex m;
   std::unordered_map<size_t, std::vector<void*>> free_blocks;
   std::vector<PendingFree> pending;
+  std::shared_ptr<CapturePool> capturing;  // the pool of the graph being captured, if any
   size_t reserved = 0, allocated = 0, peak_allocated = 0, peak_reserved = 0;
   uint64_t n_malloc = 0, n_hits = 0;
 };
@@ -249,6 +262,7 @@ class OclAllocator final : public c10::Allocator {
     void* p = nullptr;
     {
       std::lock_guard<std::mutex> g(pool.m);
+      if (pool.capturing) return allocate_captured(pool, d, nbytes, sz);
       if (!pool.pending.empty()) process_pending(pool);
       auto it = pool.free_blocks.find(sz);
       if (it != pool.free_blocks.end() && !it->second.empty()) {
@@ -293,6 +307,31 @@ class OclAllocator final : public c10::Allocator {
 
   c10::DeleterFnPtr raw_deleter() const override { return nullptr; }
 
+ private:
+  // caller holds pool.m: a block of the capture pool (no event polling and
+  // no release of cached blocks while capturing: neither may run then)
+  c10::DataPtr allocate_captured(Pool& pool, int d, size_t nbytes, size_t sz) {
+    const c10::Device dev(kOcl, d);
+    void* p = nullptr;
+    auto it = pool.capturing->free_blocks.find(sz);
+    if (it != pool.capturing->free_blocks.end() && !it->second.empty()) {
+      p = it->second.back();
+      it->second.pop_back();
+      pool.n_hits++;
+    } else {
+      const int s = pvb2_malloc(&p, sz);
+      TORCH_CHECK(s == PVB2_OK, "ocl: out of memory allocating ", nbytes, " bytes on device ", d,
+                  " while capturing a graph: ", pvb2_last_error());
+      pool.reserved += sz;
+      pool.n_malloc++;
+      pool.peak_reserved = std::max(pool.peak_reserved, pool.reserved);
+    }
+    pool.allocated += sz;
+    pool.peak_allocated = std::max(pool.peak_allocated, pool.allocated);
+    return c10::DataPtr(p, new BlockCtx{p, sz, d, {}, pool.capturing}, &free_block, dev);
+  }
+
+ public:
   void copy_data(void* dest, const void* src, std::size_t count) const override {
     flush_deferred();
     OCL_CHECK(pvb2_memcpy_async(dest, src, count, 2, current_stream()));
@@ -307,6 +346,11 @@ static void free_block(void* raw_ctx) {
   Pool& pool = pools()[b->device];
   std::lock_guard<std::mutex> g(pool.m);
   pool.allocated -= b->size;
+  if (b->cpool) {  // a graph's block: back to its pool while the graph lives
+    (b->cpool->retired ? pool.free_blocks : b->cpool->free_blocks)[b->size].push_back(b->ptr);
+    delete b;
+    return;
+  }
   if (g_no_cache) {
     DeviceScope scope(b->device);
     pvb2_stream_synchronize(stream_for(b->device));
@@ -347,6 +391,12 @@ c10::Allocator* allocator() { return &g_allocator; }
 REGISTER_ALLOCATOR(c10::DeviceType::PrivateUse1, &g_allocator);
 
 static void empty_cache_all() {
+  for (int d = 0; d < device_count(); ++d) {
+    if (!states()[d].ready) continue;
+    Pool& pool = pools()[d];
+    std::lock_guard<std::mutex> g(pool.m);
+    TORCH_CHECK(!pool.capturing, "ocl: empty_cache() while a graph is being captured on device ", d);
+  }
   clear_staged_inputs();
   for (int d = 0; d < device_count(); ++d) {
     if (!states()[d].ready) continue;
@@ -794,6 +844,119 @@ static double event_elapsed(uintptr_t a, uintptr_t b) {
 }
 static void event_destroy(uintptr_t e) { pvb2_event_destroy((pvb2_event)e); }
 
+// ================================================================== graphs
+// A training step (or any other sequence of this backend's ops on one
+// stream) captured once and replayed with one launch: the host-side work of
+// every op -- Python, the autograd engine, dispatch, planning, deferred
+// fusion decisions -- runs once, at capture.  Memory allocated during the
+// capture comes from the graph's own pool (CapturePool above).
+struct HostGraph {
+  pvb2_graph graph = nullptr;
+  std::shared_ptr<CapturePool> pool;
+  int device = 0;
+};
+
+// the pool's free blocks join the device's ordinary free lists; blocks still
+// held by tensors follow when those are freed
+static void retire_capture_pool(HostGraph* h) {
+  Pool& pool = pools()[h->device];
+  std::lock_guard<std::mutex> g(pool.m);
+  for (auto& kv : h->pool->free_blocks)
+    for (void* p : kv.second) pool.free_blocks[kv.first].push_back(p);
+  h->pool->free_blocks.clear();
+  h->pool->retired = true;
+  if (pool.capturing == h->pool) pool.capturing.reset();
+}
+
+static uintptr_t graph_capture_begin(int d) {
+  check_index(d);
+  TORCH_CHECK(!g_no_cache, "ocl graphs: not available with the memory cache off (B200_NO_MEM_CACHE=1)");
+  DeviceScope scope(d);  // launches any deferred work first: it precedes the capture
+  dev_state(d);
+  OCL_CHECK(pvb2_stream_synchronize(stream_for(d)));
+  auto h = std::make_unique<HostGraph>();
+  h->device = d;
+  h->pool = std::make_shared<CapturePool>();
+  Pool& pool = pools()[d];
+  {
+    std::lock_guard<std::mutex> g(pool.m);
+    TORCH_CHECK(!pool.capturing, "ocl graphs: a capture is already in progress on device ", d);
+    process_pending(pool);  // event queries may not run once the capture has begun
+    pool.capturing = h->pool;
+  }
+  const int s = pvb2_graph_capture_begin(stream_for(d));
+  if (s != PVB2_OK) {
+    const std::string msg = pvb2_last_error();
+    retire_capture_pool(h.get());
+    TORCH_CHECK(false, "ocl graphs: ", msg);
+  }
+  return reinterpret_cast<uintptr_t>(h.release());
+}
+
+static void graph_capture_end(uintptr_t handle) {
+  HostGraph* h = reinterpret_cast<HostGraph*>(handle);
+  TORCH_CHECK(h && !h->graph, "ocl graphs: no capture in progress for this handle");
+  pvb2_graph g = nullptr;
+  int s;
+  std::string msg;
+  {
+    DeviceScope scope(h->device, /*flush=*/false);
+    // deferred work belongs to the capture; if launching it fails (a capture
+    // already invalidated), the capture is still ended and the pool cleared
+    try {
+      flush_deferred();
+    } catch (const std::exception& e) {
+      msg = e.what();
+    }
+    s = pvb2_graph_capture_end(stream_for(h->device), &g);
+  }
+  if (s != PVB2_OK) msg = std::string(pvb2_last_error()) + (msg.empty() ? "" : "; " + msg);
+  if (s == PVB2_OK && !msg.empty()) {  // captured, but without the deferred work
+    pvb2_graph_destroy(g);
+    s = PVB2_ERR_CUDA;
+  }
+  {
+    Pool& pool = pools()[h->device];
+    std::lock_guard<std::mutex> lk(pool.m);
+    pool.capturing.reset();
+  }
+  if (s != PVB2_OK) {
+    retire_capture_pool(h);  // a failed capture ran nothing on the device
+    TORCH_CHECK(false, "ocl graphs: ", msg);
+  }
+  h->graph = g;
+}
+
+static void graph_replay(uintptr_t handle) {
+  HostGraph* h = reinterpret_cast<HostGraph*>(handle);
+  TORCH_CHECK(h && h->graph, "ocl graphs: replay of a graph that was not captured");
+  DeviceScope scope(h->device);
+  OCL_CHECK(pvb2_graph_launch(h->graph, stream_for(h->device)));
+}
+
+static int64_t graph_kernels(uintptr_t handle) {
+  HostGraph* h = reinterpret_cast<HostGraph*>(handle);
+  TORCH_CHECK(h && h->graph, "ocl graphs: not a captured graph");
+  int64_t n = 0;
+  OCL_CHECK(pvb2_graph_kernel_count(h->graph, &n));
+  return n;
+}
+
+// after every replay has finished (device synchronisation), the graph and
+// its pool are released
+static void graph_destroy(uintptr_t handle) {
+  HostGraph* h = reinterpret_cast<HostGraph*>(handle);
+  if (!h) return;
+  {
+    DeviceScope scope(h->device);
+    OCL_CHECK(pvb2_device_synchronize());
+    if (h->graph) OCL_CHECK(pvb2_graph_destroy(h->graph));
+    h->graph = nullptr;
+  }
+  retire_capture_pool(h);
+  delete h;
+}
+
 }  // namespace ocl
 
 // defined in ops_dist.cpp
@@ -829,5 +992,10 @@ PYBIND11_MODULE(_C, m) {
   m.def("impl_event_record", &event_record);
   m.def("impl_event_elapsed_ms", &event_elapsed);
   m.def("impl_event_destroy", &event_destroy);
+  m.def("impl_graph_capture_begin", &graph_capture_begin, "begin capturing device d's current stream");
+  m.def("impl_graph_capture_end", &graph_capture_end, "end the capture and instantiate the graph");
+  m.def("impl_graph_replay", &graph_replay, "replay a captured graph on its device's current stream");
+  m.def("impl_graph_kernels", &graph_kernels, "kernels launched by one replay");
+  m.def("impl_graph_destroy", &graph_destroy, "release a graph and its memory pool");
   register_dist_bindings(m);
 }

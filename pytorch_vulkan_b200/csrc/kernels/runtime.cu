@@ -288,6 +288,84 @@ int pvb2_stream_create(pvb2_stream* stream, int priority) {
   return PVB2_OK;
 }
 
+// ---------------------------------------------------------------- graphs
+// A captured sequence of this library's work on one stream, replayed with
+// one launch.  The number of kernels captured is kept so that each replay
+// adds it to the launch counter, as launching them one by one would.
+namespace {
+struct Graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int64_t kernels = 0;
+};
+thread_local int64_t t_capture_start = -1;
+}  // namespace
+
+int pvb2_graph_capture_begin(pvb2_stream stream) {
+  PVB2_CHECK_ARG(stream != nullptr, "graph capture needs a created stream, not the default stream");
+  PVB2_CUDA_TRY(cudaStreamBeginCapture(as_stream(stream), cudaStreamCaptureModeRelaxed));
+  t_capture_start = g_launches.load();
+  return PVB2_OK;
+}
+
+int pvb2_graph_capture_end(pvb2_stream stream, pvb2_graph* graph) {
+  PVB2_CHECK_ARG(graph != nullptr, "graph_capture_end: graph is NULL");
+  *graph = nullptr;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(as_stream(stream), &g);
+  const int64_t kernels = t_capture_start >= 0 ? g_launches.load() - t_capture_start : 0;
+  t_capture_start = -1;
+  if (e != cudaSuccess || !g) {
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    return fail(PVB2_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(e));
+  }
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, g, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(g);
+    cudaGetLastError();
+    return fail(PVB2_ERR_CUDA, "graph instantiation failed: %s", cudaGetErrorString(e));
+  }
+  Graph* h = new Graph;
+  h->graph = g;
+  h->exec = exec;
+  h->kernels = kernels;
+  *graph = h;
+  return PVB2_OK;
+}
+
+int pvb2_graph_launch(pvb2_graph graph, pvb2_stream stream) {
+  PVB2_CHECK_ARG(graph != nullptr, "graph_launch: graph is NULL");
+  Graph* h = static_cast<Graph*>(graph);
+  PVB2_CUDA_TRY(cudaGraphLaunch(h->exec, as_stream(stream)));
+  g_launches.fetch_add(h->kernels, std::memory_order_relaxed);
+  return PVB2_OK;
+}
+
+int pvb2_graph_kernel_count(pvb2_graph graph, int64_t* kernels) {
+  PVB2_CHECK_ARG(graph != nullptr && kernels != nullptr, "graph_kernel_count: NULL argument");
+  *kernels = static_cast<Graph*>(graph)->kernels;
+  return PVB2_OK;
+}
+
+int pvb2_graph_destroy(pvb2_graph graph) {
+  if (!graph) return PVB2_OK;
+  Graph* h = static_cast<Graph*>(graph);
+  if (h->exec) cudaGraphExecDestroy(h->exec);
+  if (h->graph) cudaGraphDestroy(h->graph);
+  delete h;
+  return PVB2_OK;
+}
+
+int pvb2_stream_is_capturing(pvb2_stream stream, int* capturing) {
+  PVB2_CHECK_ARG(capturing != nullptr, "stream_is_capturing: NULL argument");
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  PVB2_CUDA_TRY(cudaStreamIsCapturing(as_stream(stream), &st));
+  *capturing = st == cudaStreamCaptureStatusActive ? 1 : 0;
+  return PVB2_OK;
+}
+
 int pvb2_stream_destroy(pvb2_stream stream) {
   PVB2_CUDA_TRY(cudaStreamDestroy(as_stream(stream)));
   return PVB2_OK;
