@@ -22,9 +22,12 @@ On one GPU the step is captured once as a CUDA graph (`torch.ocl.Graph`,
 `--graph auto`, the default) and every timed step, in both measurements,
 replays it: the same kernels as the eager step, issued with one launch
 instead of by Python, the autograd engine and the backend op by op (the
-eager step's host time is within a millisecond of its device time).  If the
-capture fails the bench times eager steps and says so (`config.step`);
-`--graph off` forces eager steps.  Data-parallel runs step eagerly.
+eager step's host time is within a millisecond of its device time).  Before
+timing, one eager step and the first replay run from the same saved state
+and must give the same loss bit for bit.  If the capture fails or the
+losses differ, the bench times eager steps and says so (`config.step`), as
+it does for steps that draw random numbers (dropout), which a replay would
+repeat; `--graph off` forces eager steps.  Data-parallel runs step eagerly.
 
 `--impl reference` times the reference's CPU path (torch-CPU ATen, as its
 tests/validate_network.py runs it) for the same workload on all host cores;
@@ -307,18 +310,42 @@ def run_ours(a):
     graph = None
     l_graph = None
     graph_note = "eager"
-    if world == 1 and a.graph == "auto":
+    # a replay repeats the random numbers drawn at capture: steps that draw
+    # some (dropout) stay eager
+    draws = any(isinstance(m_, torch.nn.Dropout) and m_.p > 0 for m_ in model.modules())
+    if world == 1 and a.graph == "auto" and draws:
+        graph_note = "eager (the step draws random numbers)"
+    elif world == 1 and a.graph == "auto":
         try:
             from pytorch_vulkan_b200.graphs import Graph
 
+            # checked on this workload: from one saved state, the first
+            # replay's loss must equal an eager step's bit for bit
+            with torch.no_grad():
+                saved = [t.detach().clone() for t in model.state_dict().values()]
+                saved_m = [(st_["momentum_buffer"], st_["momentum_buffer"].clone()) for st_ in opt.state.values()
+                           if st_.get("momentum_buffer") is not None]
+
+            def restore():
+                with torch.no_grad():
+                    for t, v in zip(model.state_dict().values(), saved):
+                        t.copy_(v)
+                    for t, v in saved_m:
+                        t.copy_(v)
+
+            eager_loss = step(x, y).item()
+            restore()
             graph = Graph(local)
             with graph.capture():
                 l_graph = step(x, y)
+            graph.replay()
+            replay_loss = l_graph.item()
+            del saved, saved_m
+            if replay_loss != eager_loss:
+                raise RuntimeError(f"replayed step's loss {replay_loss!r} differs from the eager step's {eager_loss!r}")
             for _ in range(a.warmup):
                 graph.replay()
-            if not bool(torch.isfinite(l_graph).item()):
-                raise RuntimeError("non-finite loss from the replayed step")
-            graph_note = f"cuda_graph ({graph.kernels} kernels per replay)"
+            graph_note = f"cuda_graph ({graph.kernels} kernels per replay, first replay's loss equal to eager)"
         except Exception as e:  # the eager step is the same work, issued op by op
             sys.stderr.write(f"bench: graph capture unavailable ({e}); timing eager steps\n")
             if graph is not None:
