@@ -162,3 +162,24 @@ def test_unimplemented_math_mode_is_rejected():
     assert lib.pvb2_conv2d_fwd(ctypes.byref(d), ctypes.byref(x), None, None, ctypes.byref(y), None,
                                ctypes.c_size_t(0), None) == 2
     assert b"math mode 2" in lib.pvb2_last_error()
+
+
+def test_graph_api_host_side():
+    """torch.ocl.Graph refuses replay() before a capture and reports no
+    kernels; the C-ABI graph calls check their arguments before touching a
+    device (a NULL graph is refused, destroying NULL is a no-op)."""
+    import pytorch_vulkan_b200  # noqa: F401
+
+    g = torch.ocl.Graph(0)
+    assert g.kernels == 0 and g.device == 0
+    with pytest.raises(RuntimeError):
+        g.replay()
+    g.reset()
+    lib = ctypes.CDLL(LIB)
+    lib.pvb2_last_error.restype = ctypes.c_char_p
+    assert lib.pvb2_graph_launch(None, None) != 0
+    assert b"graph" in lib.pvb2_last_error()
+    n = ctypes.c_int64(-1)
+    assert lib.pvb2_graph_kernel_count(None, ctypes.byref(n)) != 0
+    assert lib.pvb2_graph_destroy(None) == 0
+    assert lib.pvb2_graph_capture_begin(None) != 0
